@@ -1,0 +1,393 @@
+#!/usr/bin/env python
+"""Decode throughput of the B200 build of chat-wgpu's batch-1 decode loop.
+
+Workload (the one its metric is quoted on): Qwen3-0.6B
+shape, random-init GGUF Q4_0 weights (seeded; there are no real checkpoints
+on this machine), a 128-token uniform-random prompt, then greedy decode at
+batch 1 with an f32 KV cache.  One "step" is one decode token: embed ->
+28 layers -> lm_head -> argmax -> next input, as one CUDA-graph replay.
+
+  value     decode tok/s (all ranks), device-timed with CUDA events around K
+            back-to-back steps whose inputs live in HBM (weights 335 MB > L2)
+  e2e       the same through Session.step(): per token a 4-byte H2D copy of
+            the input token from pinned memory and a 4-byte D2H read of the
+            produced token (the reference's ctx.read per token, mod.rs:103)
+  roofline  the dominant kernel from a per-kernel CUDA-event profile pass
+  cpu_baseline  the oracle port on the host cores (bounded sample)
+
+Multi-GPU: one process per GPU, one independent model replica and session
+per rank (sessions shard with no collective; weak scaling).  torch.distributed
+is used only for the barrier and the max-over-ranks of the timings.
+
+`--impl reference` times the reference's CPU implementation of this path
+(the oracle port: the Rust/wgpu reference cannot be built here) on the same
+config, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s/GPU, Qwen3 Q4_0 bs=1; Q4 GEMV HBM GB/s vs 8 TB/s peak"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--model", default="qwen3-0.6b")
+    ap.add_argument("--prompt-len", type=int, default=128)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=8)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- plumbing
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+def physical_gpu(local: int) -> str:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids):
+            return ids[local]
+    return str(local)
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (clocks + throttle reasons)."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: str):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.gpu],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax.append(float(p[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+# ---------------------------------------------------------------- bytes model
+def kernel_bytes(info: dict, pos: float) -> dict:
+    """Algorithmic HBM bytes per launch of each decode kernel at position pos:
+    Q4_0 weights 18 B per 32 weights, f32 activations in/out, f32 KV cache
+    reads of pos+1 rows per layer plus the new row's write."""
+    dim, L, nh, nkv, hd, hid, V = (info[k] for k in ("dim", "n_layers", "n_heads", "n_kv",
+                                                     "head_dim", "hidden", "vocab"))
+    qd, kvd = nh * hd, nkv * hd
+    q4 = lambda rows, k: rows * (k // 32) * 18  # noqa: E731
+    return {
+        "attn_in": q4(qd + 2 * kvd, dim) + 4 * dim * 2 + 4 * (qd + 2 * kvd),
+        "attention": 4 * (2 * (pos + 1) * kvd + qd + 2 * kvd + qd),
+        "attn_out": q4(dim, qd) + 4 * qd + 8 * dim,
+        "ffn_in": q4(2 * hid, dim) + 4 * dim * 2 + 4 * hid,
+        "ffn_out": q4(dim, hid) + 4 * hid + 8 * dim,
+        "lm_head": q4(V, dim) + 4 * dim * 2 + 4 * V,
+        "embed": 18 * (dim // 32) + 4 * dim,
+        "finalize": 64,
+    }
+
+
+def step_bytes(info: dict, pos: float) -> float:
+    kb = kernel_bytes(info, pos)
+    L = info["n_layers"]
+    return (L * (kb["attn_in"] + kb["attention"] + kb["attn_out"] + kb["ffn_in"] + kb["ffn_out"])
+            + kb["lm_head"] + kb["embed"] + kb["finalize"])
+
+
+# ---------------------------------------------------------------- CPU legs
+def oracle_decode_rate(path: str, prompt, n_decode: int, threads: int | None = None):
+    """Oracle port: tokens/s of n_decode decode steps after the prompt."""
+    from oracle import oracle as orc
+    if threads:
+        orc.set_threads(threads)
+    m = orc.Model(path)
+    m.reset(len(prompt) + n_decode + 1)
+    tok = int(prompt[0])
+    for pos in range(len(prompt) - 1):
+        m.step(tok, pos, want_logits=False)
+        tok = int(prompt[pos + 1])
+    t0 = time.perf_counter()
+    pos = len(prompt) - 1
+    for _ in range(n_decode):
+        _, logits = m.step(tok, pos, want_logits=True)
+        tok = orc.argmax(logits)
+        pos += 1
+    dt = time.perf_counter() - t0
+    cores = orc.get_threads()
+    m.close()
+    return n_decode / dt, dt, cores
+
+
+def run_reference(args, dist):
+    """--impl reference: the oracle port on the host cores, same config."""
+    if dist.rank != 0:
+        return
+    from chat_wgpu_b200 import gguf
+    path = gguf.cached_model(args.model, seed=args.seed)
+    cfg = gguf.CONFIGS[args.model]
+    rng = np.random.default_rng(args.seed + 1)
+    prompt = rng.integers(0, cfg["vocab"], args.prompt_len).astype(np.uint32)
+    from oracle import oracle as orc
+    m = orc.Model(path)
+    m.reset(args.prompt_len + args.warmup + args.steps + 1)
+    tok = int(prompt[0])
+    for pos in range(args.prompt_len - 1):
+        m.step(tok, pos, want_logits=False)
+        tok = int(prompt[pos + 1])
+    pos = args.prompt_len - 1
+    for _ in range(args.warmup):
+        _, lg = m.step(tok, pos)
+        tok = orc.argmax(lg)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, lg = m.step(tok, pos)
+        tok = orc.argmax(lg)
+        pos += 1
+    dt = time.perf_counter() - t0
+    cores = orc.get_threads()
+    m.close()
+    value = args.steps / dt
+    sample = (f"{args.steps} decode steps at positions {args.prompt_len - 1 + args.warmup}.."
+              f"{pos - 1} of {args.model} (prompt {args.prompt_len}), oracle port, {cores} threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init Q4_0 GGUF, uniform-random prompt)",
+        "config": {"workload": f"{args.model} greedy decode, bs=1, prompt {args.prompt_len}",
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the Rust/wgpu reference cannot be built or run here (no cargo, no graphics "
+                "stack); this arm is the C restatement of its CPU path",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- main arm
+def run_cuda(args, dist):
+    from chat_wgpu_b200 import gguf
+    from chat_wgpu_b200.context import GpuContext
+    from chat_wgpu_b200.model import Model, Session
+
+    cfg = gguf.CONFIGS[args.model]
+    if dist.rank == 0:
+        path = gguf.cached_model(args.model, seed=args.seed)
+    dist.barrier()
+    path = gguf.cached_model(args.model, seed=args.seed)
+    ctx = GpuContext(dist.local)
+    model = Model(ctx, path)
+    info = model.info
+    rng = np.random.default_rng(args.seed + 1)
+    prompt = rng.integers(0, cfg["vocab"], args.prompt_len).astype(np.uint32)
+    P, W, K = args.prompt_len, args.warmup, args.steps
+    max_seq = P + W + K + args.profile_steps + 4
+
+    # ---- device-timed decode: K graph replays, inputs resident in HBM
+    s = Session(model, max_seq)
+    s.begin(prompt)
+    s.run(P - 1)                     # prompt positions (no lm_head)
+    s.run(W)                         # warm-up decode steps
+    ctx.sync()
+    dist.barrier()
+    clk = Clocks(physical_gpu(dist.local))
+    clk.start()
+    time.sleep(0.3)
+    ms = s.run_timed(K)
+    clocks = clk.stop()
+    ms_max = dist.max(ms)
+    toks = s.tokens()
+    assert toks.size == W + K, (toks.size, W + K)
+    value = K * dist.world / (ms_max / 1000.0)
+    pos_lo, pos_hi = P - 1 + W, P - 1 + W + K - 1
+    mean_pos = 0.5 * (pos_lo + pos_hi)
+    _, launches_decode = s.launches()
+
+    # ---- per-kernel profile pass (direct launches, CUDA events per kernel)
+    s.set_graph(False)
+    ctx.begin_profile()
+    s.run(args.profile_steps)
+    ctx.sync()
+    prof = ctx.report_profile()
+    s.close()
+
+    # ---- e2e: public per-token API with host round trips
+    s2 = Session(model, max_seq)
+    s2.begin(prompt)
+    s2.run(P - 1)
+    tok = Session.TOKEN_DEVICE
+    for _ in range(W):
+        tok = s2.step(tok)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        tok = s2.step(tok)
+    e2e_s = time.perf_counter() - t0
+    e2e_max = dist.max(e2e_s)
+    toks2 = s2.tokens()
+    s2.close()
+    e2e_value = K * dist.world / e2e_max
+    same_stream = bool(np.array_equal(toks, toks2))
+
+    # ---- roofline of the dominant kernel
+    peaks = measured_peaks()
+    kb = kernel_bytes(info, mean_pos + args.profile_steps / 2)
+    rows = {name: (n, t) for name, n, t in prof}
+    dom = max(((n, c, t) for n, (c, t) in rows.items() if n in kb), key=lambda r: r[2])
+    dom_name, dom_count, dom_ms = dom
+    dom_bytes = kb[dom_name]
+    achieved = dom_bytes / (dom_ms / dom_count / 1000.0) / 1e9
+    per_kernel = {n: {"launches": c, "ms": round(t, 4),
+                      "gbs": round(kb[n] / (t / c / 1000.0) / 1e9, 1) if n in kb else None}
+                  for n, (c, t) in rows.items()}
+    sb = step_bytes(info, mean_pos)
+    step_gbs = sb / (ms_max / K / 1000.0) / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": dist.world, "steps": K,
+        "warmup": W, "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (Q4_0 weights, f32 accumulation)",
+        "data": "synthetic (seeded random-init Q4_0 GGUF, uniform-random prompt)",
+        "config": {"workload": f"{args.model} greedy decode, bs=1, prompt {P}, timed decode "
+                               f"positions {pos_lo}..{pos_hi}",
+                   "parallelism": f"replicas x{dist.world} (one session per GPU)",
+                   "l2": "inputs larger than L2 (335 MB of weights per step)",
+                   "weight_bytes": int(info["weight_bytes"])},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4, "same_tokens_as_device_loop": same_stream},
+        "gpu_launches": int(K * launches_decode),
+        "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "traffic": None, "peak_src": peaks["src"],
+                     "bytes_per_launch": int(dom_bytes)},
+        "step_roofline": {"bytes_per_step": int(sb), "achieved_gbs": step_gbs,
+                          "frac": step_gbs / peaks["hbm_gbs"],
+                          "roofline_tok_s": peaks["hbm_gbs"] * 1e9 / sb},
+        "kernels": per_kernel,
+        "clocks": clocks,
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        rate, dt, cores = oracle_decode_rate(path, prompt[:4], 6)
+        line["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": cores, "kind": "port",
+                                "sample": f"6 decode steps after a 4-token prompt of {args.model} "
+                                          f"({dt:.1f} s), oracle port on {cores} host threads"}
+    model.close()
+    ctx.close()
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    dist = Dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, dist)
+        else:
+            run_cuda(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

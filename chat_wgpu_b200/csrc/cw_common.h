@@ -1,0 +1,126 @@
+// cw_common.h -- internal declarations shared by the libchatcuda.so sources.
+//
+// The context mirrors chat-wgpu's GpuContext (src/context.rs): a device and a
+// stream, a buffer table, the per-frame arena (empty()/reset_frame()), and a
+// per-op timing profiler (src/profile.rs) built on CUDA events.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <map>
+#include <string>
+#include <unordered_map>
+#include <utility>
+#include <vector>
+
+#include "../../include/chatcuda.h"
+
+namespace cw {
+
+// ---- errors ---------------------------------------------------------------
+// Thread-local message for cw_last_error(); set_error returns the status so
+// call sites can `return set_error(...)`.
+int set_error(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+void clear_error();
+
+#define CW_CUDA(call)                                                              \
+    do {                                                                           \
+        cudaError_t e_ = (call);                                                   \
+        if (e_ != cudaSuccess)                                                     \
+            return ::cw::set_error(e_ == cudaErrorMemoryAllocation ? CW_ERR_OOM    \
+                                                                   : CW_ERR_CUDA,  \
+                                   "%s: %s (%s:%d)", #call, cudaGetErrorString(e_),\
+                                   __FILE__, __LINE__);                            \
+    } while (0)
+
+#define CW_CHECK(cond, status, ...)                                                \
+    do {                                                                           \
+        if (!(cond)) return ::cw::set_error((status), __VA_ARGS__);                \
+    } while (0)
+
+#define CW_TRY(expr)                                                               \
+    do {                                                                           \
+        int s_ = (expr);                                                           \
+        if (s_ != CW_OK) return s_;                                                \
+    } while (0)
+
+// Device-side status word written by bounded waits (never a trap).
+enum DeviceStatus : int { DEV_OK = 0, DEV_TIMEOUT = 1, DEV_BAD_INPUT = 2 };
+
+enum BufKind : int { BUF_STORAGE = 0, BUF_PERSISTENT = 1, BUF_ARENA = 2 };
+
+struct BufEntry {
+    void* ptr = nullptr;
+    size_t nbytes = 0;
+    int kind = BUF_STORAGE;
+    // Set for packed Q4_0 weights: rows x in_f and the byte offset of the f16
+    // scale plane (the nibble plane starts at 0).
+    size_t rows = 0, in_f = 0, scale_off = 0;
+    bool q4_0 = false;
+};
+
+struct ProfRec {
+    const char* name;
+    cudaEvent_t start, stop;
+};
+
+}  // namespace cw
+
+struct cw_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int sm_count = 0;
+    int max_smem_optin = 0;
+    size_t l2_bytes = 0;
+    std::string backend;
+
+    std::unordered_map<uint64_t, cw::BufEntry> bufs;
+    uint64_t next_id = 1;
+    // arena[slot] = (len in f32 elements, buffer id) -- context.rs:42-47
+    std::vector<std::pair<size_t, uint64_t>> arena;
+    size_t cursor = 0;
+
+    // profiler (context.rs:53-56, profile.rs)
+    bool profiling = false;
+    std::vector<cw::ProfRec> prof;
+    std::vector<cudaEvent_t> event_pool;
+
+    // device status word (DeviceStatus) and zero-initialised per-head
+    // completion counters used by the split-KV attention combine.
+    int* d_status = nullptr;
+    unsigned* d_counters = nullptr;
+    size_t n_counters = 0;
+
+    // RoPE inverse-frequency tables keyed by (head_dim, theta bits).
+    std::map<std::pair<uint32_t, uint32_t>, float*> rope_tables;
+};
+
+namespace cw {
+
+// buffer helpers (cw_context.cu)
+int buf_get(cw_ctx* ctx, cw_buf b, BufEntry** out, size_t min_bytes, const char* what);
+int buf_new(cw_ctx* ctx, size_t nbytes, int kind, cw_buf* out, BufEntry** entry = nullptr);
+int arena_get(cw_ctx* ctx, size_t len_f32, cw_buf* out, BufEntry** entry = nullptr);
+int check_launch(const char* what);
+int check_device_status(cw_ctx* ctx);
+
+// A profiler scope: records a start/stop event pair around the launches made
+// while it is alive, labelled with the op name (context.rs:302-328).
+struct OpScope {
+    cw_ctx* ctx;
+    const char* name;
+    cudaEvent_t start = nullptr, stop = nullptr;
+    OpScope(cw_ctx* c, const char* n);
+    ~OpScope();
+};
+
+// RoPE table for (head_dim, theta): inv_freq[i] = theta^(-2i/head_dim)
+// computed on the host in f32 exactly as rope.wgsl:26-27 writes it.
+int rope_table(cw_ctx* ctx, uint32_t head_dim, float theta, const float** out);
+
+// zeroed counters for the attention combine; grows on demand (syncs).
+int ensure_counters(cw_ctx* ctx, size_t n);
+
+}  // namespace cw

@@ -1,0 +1,1128 @@
+// cw_model.cu -- the model layer of chat-wgpu (src/model/{mod,qwen3,layers,
+// cache}.rs) on B200: GGUF load with Q4_0 weights kept Q4_0 in HBM, a decode
+// session (KV cache + per-token device state), and one decode step built from
+// five fused kernels per layer, replayed as a CUDA graph.
+//
+// Per token (src/model/qwen3.rs:139-191 composition):
+//   embed        hidden = dequant(token_embd[token])            (qwen3.rs:128-133)
+//   per layer
+//     attn_in    x = rmsnorm(hidden); qkv = [Wq;Wk;Wv] x (+bias)  (:149-152)
+//     attn       q/k = rmsnorm per head (QK-norm), RoPE, K/V row written at
+//                pos, split-KV attention over pos+1 keys        (:154-177)
+//     attn_out   hidden += Wo attn                              (:178-179)
+//     ffn_in     x = rmsnorm(hidden); act = swiglu(Wg x, Wu x)  (:182-185)
+//     ffn_out    hidden += Wd act                               (:186-187)
+//   head         x = rmsnorm(hidden); logits = Wlm x; argmax    (:190, mod.rs:95-103)
+//   finalize     next input = prompt[pos+1] or the argmax; pos += 1  (mod.rs:114-122)
+// Families with post-norms (gemma2) defer each residual add into the next
+// kernel's prologue so that no kernel reads the vector another CTA writes.
+// Position, input token and the argmax live in device memory, so the same
+// graph replays for every token.
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "cw_attn.cuh"
+#include "cw_common.h"
+#include "cw_device.cuh"
+#include "cw_gguf.h"
+#include "cw_ops.h"
+#include "cw_q4.h"
+
+namespace cw {
+
+struct DevState {
+    int pos;          // position of the next step
+    unsigned token;   // input token of the next step
+    int n_prompt;
+    int n_produced;
+    unsigned long long key;  // argmax accumulator of the current step
+};
+
+struct QW {  // packed Q4_0 weight
+    const uint8_t* payload = nullptr;
+    const __half* scales = nullptr;
+    int rows = 0, in_f = 0;
+    cw_buf buf = 0;
+};
+
+struct Layer {
+    float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
+    float *post_attn = nullptr, *post_ffw = nullptr, *qkv_bias = nullptr;
+    QW qkv, wo, gate_up, down;
+};
+
+}  // namespace cw
+
+struct cw_model {
+    cw_ctx* ctx = nullptr;
+    cw_model_info info{};
+    std::vector<cw::Layer> L;
+    float* final_norm = nullptr;
+    cw::QW embed, head;
+    std::vector<cw_buf> owned;
+    const float* inv_freq = nullptr;
+};
+
+namespace cw {
+
+// ===========================================================================
+// fused kernels
+// ===========================================================================
+enum { PRO_X = 0, PRO_NORM = 1 };
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_GLU = 2, EPI_HEAD = 3 };
+
+struct FArgs {
+    const uint8_t* payload;
+    const __half* scales;
+    int K, N;
+    // PRO_X
+    const float* x;
+    // PRO_NORM: h = base (+ delta, post-normed if post_w); x = rmsnorm(h) * gain
+    const float* base;
+    const float* delta;
+    const float* post_w;
+    float* h_out;   // CTA 0 stores h here when non-null
+    const float* norm_w;
+    float* xn_out;  // CTA 0 stores the normalised x here when non-null
+    float eps;
+    int unit;       // UnitShift gain (1 + w) for norm_w and post_w
+    // epilogue
+    float* y;
+    const float* bias;
+    int geglu;
+    float softcap;
+    DevState* st;
+};
+
+__device__ __forceinline__ float cta_sum(float v, float* red) {
+    v = warp_sum(v);
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; i++) t += red[i];
+    return t;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }  // glu.wgsl:25
+__device__ __forceinline__ float gelu_f(float x) {                                 // glu.wgsl:27-30
+    const float c = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+}
+
+__host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ constexpr size_t fgemv_smem(int pro, int K) {
+    return align_up(q24_bytes(K / 32), 16) + (pro == PRO_NORM ? (size_t)K * 4 : 0);
+}
+
+template <int PRO, int EPI, int R>
+__global__ void __launch_bounds__(256) k_fgemv(FArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ float red[8];
+    __shared__ unsigned long long red_key[8];
+    const int nb = a.K / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    Q24 s = q24_carve(smem, nb);
+    if (PRO == PRO_X) {
+        q24_prepare<LAYOUT_GGUF>(s, a.x);
+    } else {
+        float* hbuf = reinterpret_cast<float*>(smem + align_up(q24_bytes(nb), 16));
+        const int K = a.K;
+        float inv_d = 0.f;
+        if (a.delta && a.post_w) {
+            float ss = 0.f;
+            for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(a.delta[i], a.delta[i], ss);
+            ss = cta_sum(ss, red);
+            inv_d = 1.0f / sqrtf(ss / (float)K + a.eps);
+        }
+        float ssh = 0.f;
+        const bool wr = a.h_out && blockIdx.x == 0;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            float h = a.base[i];
+            if (a.delta) {
+                float dv = a.delta[i];
+                if (a.post_w) {
+                    float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
+                    dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
+                }
+                h = h + dv;
+            }
+            hbuf[i] = h;
+            if (wr) a.h_out[i] = h;
+            ssh = fmaf(h, h, ssh);
+        }
+        ssh = cta_sum(ssh, red);
+        const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
+        const bool wx = a.xn_out && blockIdx.x == 0;
+        for (int b = warp; b < nb; b += (blockDim.x >> 5)) {
+            int i = b * 32 + lane;
+            float gw = a.unit ? 1.0f + a.norm_w[i] : a.norm_w[i];
+            float v = __fmul_rn(__fmul_rn(hbuf[i], inv), gw);
+            if (wx) a.xn_out[i] = v;
+            q24_block<LAYOUT_GGUF>(s, b, v, lane);
+        }
+    }
+    __syncthreads();
+
+    unsigned long long best = argmax_key_init();
+    const long groups = ((long)a.N + 8 * R - 1) / (8 * R);
+    for (long g = blockIdx.x; g < groups; g += gridDim.x) {
+        long row0 = (g * 8 + warp) * R;
+        if (row0 >= a.N) continue;
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = 0.f;
+        q4_rows_dot<LAYOUT_GGUF, R>(s, a.payload, a.scales, row0, a.N, lane, acc);
+#pragma unroll
+        for (int r = 0; r < R; r++) acc[r] = warp_sum(acc[r]);
+        if (EPI == EPI_GLU) {
+            // interleaved rows: 2i = gate_i, 2i+1 = up_i
+#pragma unroll
+            for (int p = 0; p < R / 2; p++) {
+                long row = row0 + 2 * p;
+                if (lane == p && row < a.N) {
+                    float gv = acc[2 * p], uv = acc[2 * p + 1];
+                    float act = a.geglu ? gelu_f(gv) : silu_f(gv);
+                    a.y[row / 2] = act * uv;
+                }
+            }
+        } else if (EPI == EPI_HEAD) {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                long row = row0 + r;
+                if (row < a.N) {
+                    float v = acc[r];
+                    if (a.softcap > 0.f) v = a.softcap * tanhf(v / a.softcap);
+                    if (lane == r) a.y[row] = v;
+                    unsigned long long k = argmax_key(v, (unsigned)row);
+                    best = k > best ? k : best;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                long row = row0 + r;
+                if (lane == r && row < a.N) {
+                    if (EPI == EPI_RESID)
+                        a.y[row] = a.y[row] + acc[r];
+                    else
+                        a.y[row] = a.bias ? acc[r] + a.bias[row] : acc[r];
+                }
+            }
+        }
+    }
+    if (EPI == EPI_HEAD) {
+        if (lane == 0) red_key[warp] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = red_key[w] > best ? red_key[w] : best;
+            atomicMax(&a.st->key, best);
+        }
+    }
+}
+
+// ---- attention with QK-norm + RoPE + KV write fused in front -------------
+struct AArgs {
+    const float* qkv;      // [qd | kvd | kvd] raw projections
+    const float* q_norm;   // QK-norm gains (qwen3.rs:154-155) or null
+    const float* k_norm;
+    float eps;
+    const float* inv_freq; // RoPE table
+    float* kc;             // this layer's cache [n_kv][max_seq][hd]
+    float* vc;
+    int max_seq;
+    float* out;            // [n_heads * hd]
+    float* part;
+    unsigned* counters;
+    int n_heads, n_kv, hd, n_splits, window;
+    float scale, softcap;
+    const DevState* st;
+};
+
+template <int EPL, int GMAX>
+__global__ void __launch_bounds__(128) k_fattn(AArgs a) {
+    extern __shared__ float sm[];
+    const int G = a.n_heads / a.n_kv, hd = a.hd;
+    const int g = blockIdx.y, split = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = a.st->pos, seq = pos + 1;
+    int jlo, jhi;
+    attn_range(seq, a.window, split, a.n_splits, &jlo, &jhi);
+    const bool holds = pos >= jlo && pos < jhi;
+    float* qs = sm + attn_smem_floats(G, hd);  // [G][hd]
+    float* ks = qs + (size_t)G * hd;           // [hd]
+    const int qd = a.n_heads * hd, kvd = a.n_kv * hd;
+    const int nrows = G + (holds ? 1 : 0);
+    for (int r = warp; r < nrows; r += 4) {
+        const bool isq = r < G;
+        const float* src = isq ? a.qkv + (size_t)(g * G + r) * hd : a.qkv + qd + (size_t)g * hd;
+        const float* nw = isq ? a.q_norm : a.k_norm;
+        float* dst = isq ? qs + (size_t)r * hd : ks;
+        float v[EPL];
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; e++) {
+            int d = lane + 32 * e;
+            v[e] = d < hd ? src[d] : 0.f;
+            ss = fmaf(v[e], v[e], ss);
+        }
+        if (nw) {  // norm.wgsl:20-37 over one head row
+            ss = warp_sum(ss);
+            float inv = 1.0f / sqrtf(ss / (float)hd + a.eps);
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                int d = lane + 32 * e;
+                if (d < hd) v[e] = __fmul_rn(__fmul_rn(v[e], inv), nw[d]);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < EPL; e++) {
+            int d = lane + 32 * e;
+            if (d < hd) dst[d] = v[e];
+        }
+    }
+    __syncthreads();
+    // RoPE (rope.wgsl:25-34) in place, one thread per rotated pair
+    const int half = hd / 2;
+    for (int i = threadIdx.x; i < nrows * half; i += blockDim.x) {
+        int r = i / half, k = i - r * half;
+        float* row = r < G ? qs + (size_t)r * hd : ks;
+        float freq = __fmul_rn((float)pos, a.inv_freq[k]);
+        float sn, cs;
+        sincosf(freq, &sn, &cs);
+        float lo = row[k], hi = row[k + half];
+        row[k] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
+        row[k + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+    }
+    __syncthreads();
+    float* kbase = a.kc + (size_t)g * a.max_seq * hd;
+    float* vbase = a.vc + (size_t)g * a.max_seq * hd;
+    if (holds) {  // cache.rs:21-24: this token's K (normed, roped) and V at pos
+        const float* vsrc = a.qkv + qd + kvd + (size_t)g * hd;
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+            kbase[(size_t)pos * hd + d] = ks[d];
+            vbase[(size_t)pos * hd + d] = vsrc[d];
+        }
+    }
+    __syncthreads();
+    float* res = sm + 4 * G * (hd + 2);
+    attn_core<EPL, GMAX, false>(qs, G, hd, kbase, vbase, hd, jlo, jhi, a.scale, a.softcap, sm, res);
+    attn_finish(res, G, hd, g, split, a.n_splits, a.part, a.counters, a.out);
+}
+
+// ---- embed / finalize ------------------------------------------------------
+// qwen3.rs:128-133: row `token` of token_embd, exact Q4_0 dequantisation.
+__global__ void k_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
+                        int dim, float scale, const DevState* __restrict__ st,
+                        float* __restrict__ hidden) {
+    const int nb = dim / 32;
+    const unsigned tok = st->token;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        int b = i >> 5, j = i & 31;
+        size_t blk = (size_t)tok * nb + b;
+        float d = __half2float(scales[blk]);
+        uint8_t byte = payload[blk * 16 + (j & 15)];
+        int q = (j < 16) ? (byte & 0xf) : (byte >> 4);
+        float v = __fmul_rn(d, (float)(q - 8));
+        hidden[i] = scale > 0.f ? __fmul_rn(v, scale) : v;
+    }
+}
+
+// mod.rs:114-122: the next input is the next prompt token while the prompt
+// lasts, else the argmax, which is also appended to the output.
+__global__ void k_finalize(DevState* st, const unsigned* __restrict__ prompt,
+                           unsigned* __restrict__ toks, int decode) {
+    int pos = st->pos;
+    unsigned next;
+    if (pos + 1 < st->n_prompt) {
+        next = prompt[pos + 1];
+    } else {
+        unsigned tok = decode ? argmax_key_index(st->key) : 0u;
+        toks[st->n_produced] = tok;
+        st->n_produced = st->n_produced + 1;
+        next = tok;
+    }
+    st->key = argmax_key_init();
+    st->token = next;
+    st->pos = pos + 1;
+}
+
+__global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n_prompt) {
+    st->pos = 0;
+    st->token = prompt[0];
+    st->n_prompt = n_prompt;
+    st->n_produced = 0;
+    st->key = argmax_key_init();
+}
+
+// ===========================================================================
+// host side
+// ===========================================================================
+template <int PRO, int EPI, int R>
+static int launch_fgemv(cw_ctx* ctx, const FArgs& a) {
+    size_t smem = fgemv_smem(PRO, a.K);
+    auto kern = k_fgemv<PRO, EPI, R>;
+    if (smem > 48 * 1024) {
+        CW_CHECK((int)smem <= ctx->max_smem_optin, CW_ERR_UNSUPPORTED,
+                 "fused gemv: K=%d needs %zu bytes of shared memory", a.K, smem);
+        CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    int per_sm = 0;
+    CW_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem));
+    per_sm = std::max(per_sm, 1);
+    long groups = ((long)a.N + 8 * R - 1) / (8 * R);
+    long grid = std::min<long>(groups, (long)ctx->sm_count * per_sm);
+    kern<<<(unsigned)grid, 256, smem, ctx->stream>>>(a);
+    return check_launch("fused gemv");
+}
+
+// Rows per warp for a GEMV of N rows: enough warps to cover every SM twice.
+static int pick_r(cw_ctx* ctx, long N) {
+    long sm2 = 2L * ctx->sm_count * 8;
+    if (N >= sm2 * 4) return 4;
+    if (N >= sm2 * 2) return 2;
+    return 1;
+}
+
+template <int PRO, int EPI>
+static int fgemv(cw_ctx* ctx, const FArgs& a) {
+    int r = pick_r(ctx, a.N);
+    if (r == 4) return launch_fgemv<PRO, EPI, 4>(ctx, a);
+    if constexpr (EPI == EPI_GLU) {
+        return launch_fgemv<PRO, EPI, 2>(ctx, a);  // gate/up rows come in pairs
+    } else {
+        if (r == 2) return launch_fgemv<PRO, EPI, 2>(ctx, a);
+        return launch_fgemv<PRO, EPI, 1>(ctx, a);
+    }
+}
+
+template <int EPL, int GM>
+static int fattn_go(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
+    if (smem > 48 * 1024)
+        CW_CUDA(cudaFuncSetAttribute(k_fattn<EPL, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+    k_fattn<EPL, GM><<<grid, 128, smem, ctx->stream>>>(a);
+    return CW_OK;
+}
+
+template <int EPL>
+static int launch_fattn_e(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
+    int G = a.n_heads / a.n_kv;
+#define CW_FATTN(GM) CW_TRY((fattn_go<EPL, GM>(ctx, a, grid, smem)))
+    if (G <= 1) CW_FATTN(1);
+    else if (G <= 2) CW_FATTN(2);
+    else if (G <= 4) CW_FATTN(4);
+    else CW_FATTN(8);
+#undef CW_FATTN
+    return check_launch("fused attention");
+}
+
+static size_t fattn_smem(int G, int hd) {
+    return (attn_smem_floats(G, hd) + (size_t)G * hd + hd) * sizeof(float);
+}
+
+static int launch_fattn(cw_ctx* ctx, const AArgs& a) {
+    dim3 grid(a.n_splits, a.n_kv);
+    int G = a.n_heads / a.n_kv;
+    size_t smem = fattn_smem(G, a.hd);
+    int epl = (a.hd + 31) / 32;
+    if (epl <= 1) return launch_fattn_e<1>(ctx, a, grid, smem);
+    if (epl <= 2) return launch_fattn_e<2>(ctx, a, grid, smem);
+    if (epl <= 4) return launch_fattn_e<4>(ctx, a, grid, smem);
+    return launch_fattn_e<8>(ctx, a, grid, smem);
+}
+
+// ---- loading ----------------------------------------------------------------
+static int dev_alloc(cw_model* m, size_t nbytes, void** p) {
+    cw_buf b;
+    BufEntry* e;
+    CW_TRY(buf_new(m->ctx, nbytes, BUF_PERSISTENT, &b, &e));
+    m->owned.push_back(b);
+    *p = e->ptr;
+    return CW_OK;
+}
+
+static float f16_bits_to_f32(uint16_t h) {
+    // exact decode incl. subnormals / inf / nan (dequant.rs:9-21)
+    int sign = (h >> 15) & 1, e = (h >> 10) & 0x1f;
+    float mant = (float)(h & 0x3ff), mag;
+    if (e == 0) mag = mant * ldexpf(1.0f, -24);
+    else if (e == 0x1f) mag = mant == 0.f ? INFINITY : NAN;
+    else mag = (1.0f + mant / 1024.0f) * ldexpf(1.0f, e - 15);
+    return sign ? -mag : mag;
+}
+
+static int load_vec(cw_model* m, const GgufFile& f, const std::string& name, size_t len,
+                    float** out) {
+    const GgufTensor* t = f.tensor(name);
+    CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", name.c_str());
+    CW_CHECK(t->n_elems == len, CW_ERR_FORMAT, "tensor %s has %llu elements, expected %zu",
+             name.c_str(), (unsigned long long)t->n_elems, len);
+    std::vector<float> h(len);
+    if (t->type == GGML_F32) {
+        memcpy(h.data(), t->data, len * 4);
+    } else if (t->type == GGML_F16) {
+        const uint16_t* s = (const uint16_t*)t->data;
+        for (size_t i = 0; i < len; i++) h[i] = f16_bits_to_f32(s[i]);
+    } else if (t->type == GGML_BF16) {
+        const uint16_t* s = (const uint16_t*)t->data;
+        for (size_t i = 0; i < len; i++) {
+            uint32_t u = (uint32_t)s[i] << 16;
+            memcpy(&h[i], &u, 4);
+        }
+    } else {
+        return set_error(CW_ERR_UNSUPPORTED, "vector %s has type %s (F32/F16/BF16 expected)",
+                         name.c_str(), ggml_type_name(t->type));
+    }
+    void* p;
+    CW_TRY(dev_alloc(m, len * 4, &p));
+    CW_CUDA(cudaMemcpy(p, h.data(), len * 4, cudaMemcpyHostToDevice));
+    *out = (float*)p;
+    return CW_OK;
+}
+
+// Load one or more Q4_0 [rows_i, in_f] tensors as a single packed weight.
+// interleave: two parts with equal rows become rows p0[0], p1[0], p0[1], ...
+static int load_q4(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
+                   size_t in_f, bool interleave, QW* out) {
+    std::vector<const GgufTensor*> parts;
+    size_t rows = 0;
+    const size_t rb = in_f / 32 * 18;
+    for (auto& n : names) {
+        const GgufTensor* t = f.tensor(n);
+        CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", n.c_str());
+        CW_CHECK(t->type == GGML_Q4_0, CW_ERR_UNSUPPORTED,
+                 "tensor %s is %s; the decode path takes Q4_0 matrices", n.c_str(),
+                 ggml_type_name(t->type));
+        CW_CHECK(!t->dims.empty() && t->dims[0] == in_f && t->n_elems % in_f == 0, CW_ERR_FORMAT,
+                 "tensor %s: inner dimension %llu, expected %zu", n.c_str(),
+                 (unsigned long long)(t->dims.empty() ? 0 : t->dims[0]), in_f);
+        parts.push_back(t);
+        rows += t->n_elems / in_f;
+    }
+    CW_CHECK(!interleave || (parts.size() == 2 && parts[0]->n_elems == parts[1]->n_elems),
+             CW_ERR_FORMAT, "interleaved weights need two equal parts");
+    size_t nbytes = rows * rb;
+    void* tmp = nullptr;
+    CW_CUDA(cudaMalloc(&tmp, nbytes));
+    cudaError_t ce = cudaSuccess;
+    if (!interleave) {
+        size_t off = 0;
+        for (auto* t : parts) {
+            ce = cudaMemcpy((char*)tmp + off, t->data, t->nbytes, cudaMemcpyHostToDevice);
+            if (ce != cudaSuccess) break;
+            off += t->nbytes;
+        }
+    } else {
+        size_t r1 = parts[0]->n_elems / in_f;
+        std::vector<uint8_t> stage(nbytes);
+        for (size_t r = 0; r < r1; r++) {
+            memcpy(stage.data() + (2 * r) * rb, parts[0]->data + r * rb, rb);
+            memcpy(stage.data() + (2 * r + 1) * rb, parts[1]->data + r * rb, rb);
+        }
+        ce = cudaMemcpy(tmp, stage.data(), nbytes, cudaMemcpyHostToDevice);
+    }
+    if (ce != cudaSuccess) {
+        cudaFree(tmp);
+        return set_error(CW_ERR_CUDA, "weight upload: %s", cudaGetErrorString(ce));
+    }
+    cw_buf b;
+    int rc = pack_q4_0(m->ctx, tmp, rows, in_f, &b);
+    cudaStreamSynchronize(m->ctx->stream);
+    cudaFree(tmp);
+    CW_TRY(rc);
+    m->owned.push_back(b);
+    BufEntry& e = m->ctx->bufs[b];
+    out->payload = (const uint8_t*)e.ptr;
+    out->scales = (const __half*)((const char*)e.ptr + e.scale_off);
+    out->rows = (int)rows;
+    out->in_f = (int)in_f;
+    out->buf = b;
+    m->info.weight_bytes += rows * rb;
+    return CW_OK;
+}
+
+static int model_load(cw_model* m, const std::string& path) {
+    GgufFile f;
+    std::string err;
+    int rc = f.open(path, err);
+    if (rc != CW_OK) return set_error(rc, "%s", err.c_str());
+    std::string arch = f.meta_str("general.architecture");
+    if (arch.empty()) arch = "qwen3";
+    cw_model_info& I = m->info;
+    snprintf(I.arch, sizeof I.arch, "%s", arch.c_str());
+    int family;
+    if (arch == "qwen3") family = 0;
+    else if (arch == "qwen2" || arch == "llama") family = 1;
+    else if (arch == "gemma2") family = 2;
+    else return set_error(CW_ERR_UNSUPPORTED, "unsupported architecture '%s'", arch.c_str());
+    auto K = [&](const char* s) { return arch + "." + s; };
+    // qwen3.rs:45-53
+    I.n_layers = f.meta_u32(K("block_count"));
+    I.dim = f.meta_u32(K("embedding_length"));
+    I.n_heads = f.meta_u32(K("attention.head_count"));
+    I.n_kv = f.meta_u32(K("attention.head_count_kv"), I.n_heads);
+    I.head_dim = f.meta_u32(K("attention.key_length"), I.n_heads ? I.dim / I.n_heads : 0);
+    I.hidden = f.meta_u32(K("feed_forward_length"));
+    I.eps = f.meta_f32(K("attention.layer_norm_rms_epsilon"), 1e-6f);
+    I.rope_theta = f.meta_f32(K("rope.freq_base"), family == 2 ? 10000.f : 1000000.f);
+    I.vocab = f.meta_u32(K("vocab_size"));
+    if (!I.vocab) {  // gguf.rs:171-177
+        if (const GgufTensor* te = f.tensor("token_embd.weight"))
+            for (auto d : te->dims) I.vocab = std::max<uint32_t>(I.vocab, (uint32_t)d);
+    }
+    I.norm_kind = family == 2 ? 1 : 0;
+    I.activation = family == 2 ? 1 : 0;
+    I.qk_norm = family == 0 ? 1 : 0;
+    I.post_norms = family == 2 ? 1 : 0;
+    if (family == 2) {
+        I.sliding_window = f.meta_u32(K("attention.sliding_window"));
+        I.attn_softcap = f.meta_f32(K("attn_logit_softcapping"));
+        I.final_softcap = f.meta_f32(K("final_logit_softcapping"));
+        I.embed_scale = sqrtf((float)I.dim);
+    }
+    CW_CHECK(I.n_layers && I.dim && I.n_heads && I.n_kv && I.head_dim && I.hidden && I.vocab,
+             CW_ERR_FORMAT, "model metadata incomplete");
+    CW_CHECK(I.n_heads % I.n_kv == 0 && I.n_heads / I.n_kv <= 8, CW_ERR_UNSUPPORTED,
+             "GQA group %u/%u not supported (n_kv | n_heads, group <= 8)", I.n_heads, I.n_kv);
+    CW_CHECK(I.head_dim <= 256 && I.head_dim % 2 == 0, CW_ERR_UNSUPPORTED,
+             "head_dim %u not supported (even, <= 256)", I.head_dim);
+    CW_CHECK(I.dim % 32 == 0 && I.hidden % 32 == 0 && (I.n_heads * I.head_dim) % 32 == 0,
+             CW_ERR_UNSUPPORTED, "dimensions must be multiples of 32");
+    const size_t qd = (size_t)I.n_heads * I.head_dim, kvd = (size_t)I.n_kv * I.head_dim;
+    m->L.resize(I.n_layers);
+    for (uint32_t i = 0; i < I.n_layers; i++) {
+        Layer& l = m->L[i];
+        std::string p = "blk." + std::to_string(i) + ".";
+        CW_TRY(load_vec(m, f, p + "attn_norm.weight", I.dim, &l.attn_norm));
+        CW_TRY(load_q4(m, f, {p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"},
+                       I.dim, false, &l.qkv));
+        CW_CHECK((size_t)l.qkv.rows == qd + 2 * kvd, CW_ERR_FORMAT, "layer %u: q/k/v rows %d",
+                 i, l.qkv.rows);
+        if (f.has(p + "attn_q.bias")) {  // Linear bias (layers.rs:20-21,59-61)
+            I.qkv_bias = 1;
+            float *bq, *bk, *bv;
+            CW_TRY(load_vec(m, f, p + "attn_q.bias", qd, &bq));
+            CW_TRY(load_vec(m, f, p + "attn_k.bias", kvd, &bk));
+            CW_TRY(load_vec(m, f, p + "attn_v.bias", kvd, &bv));
+            void* pb;
+            CW_TRY(dev_alloc(m, (qd + 2 * kvd) * 4, &pb));
+            CW_CUDA(cudaMemcpy(pb, bq, qd * 4, cudaMemcpyDeviceToDevice));
+            CW_CUDA(cudaMemcpy((float*)pb + qd, bk, kvd * 4, cudaMemcpyDeviceToDevice));
+            CW_CUDA(cudaMemcpy((float*)pb + qd + kvd, bv, kvd * 4, cudaMemcpyDeviceToDevice));
+            l.qkv_bias = (float*)pb;
+        }
+        CW_TRY(load_q4(m, f, {p + "attn_output.weight"}, qd, false, &l.wo));
+        if (I.qk_norm) {
+            CW_TRY(load_vec(m, f, p + "attn_q_norm.weight", I.head_dim, &l.q_norm));
+            CW_TRY(load_vec(m, f, p + "attn_k_norm.weight", I.head_dim, &l.k_norm));
+        }
+        CW_TRY(load_vec(m, f, p + "ffn_norm.weight", I.dim, &l.ffn_norm));
+        CW_TRY(load_q4(m, f, {p + "ffn_gate.weight", p + "ffn_up.weight"}, I.dim, true,
+                       &l.gate_up));
+        CW_TRY(load_q4(m, f, {p + "ffn_down.weight"}, I.hidden, false, &l.down));
+        if (I.post_norms) {
+            CW_TRY(load_vec(m, f, p + "post_attention_norm.weight", I.dim, &l.post_attn));
+            CW_TRY(load_vec(m, f, p + "post_ffw_norm.weight", I.dim, &l.post_ffw));
+        }
+    }
+    CW_TRY(load_vec(m, f, "output_norm.weight", I.dim, &m->final_norm));
+    CW_TRY(load_q4(m, f, {"token_embd.weight"}, I.dim, false, &m->embed));
+    CW_CHECK(m->embed.rows == (int)I.vocab, CW_ERR_FORMAT, "token_embd has %d rows, vocab %u",
+             m->embed.rows, I.vocab);
+    if (f.has("output.weight")) {  // untied head; tied otherwise (qwen3.rs:93-98)
+        CW_TRY(load_q4(m, f, {"output.weight"}, I.dim, false, &m->head));
+    } else {
+        m->head = m->embed;
+    }
+    CW_TRY(rope_table(m->ctx, I.head_dim, I.rope_theta, &m->inv_freq));
+    return CW_OK;
+}
+
+}  // namespace cw
+
+// ===========================================================================
+// session
+// ===========================================================================
+struct cw_session {
+    cw_model* m = nullptr;
+    cw_ctx* ctx = nullptr;
+    size_t max_seq = 0;
+    std::vector<cw_buf> owned;
+    float *kc = nullptr, *vc = nullptr;
+    float *hidden = nullptr, *hidden_b = nullptr, *tmp = nullptr, *qkv = nullptr, *attn = nullptr;
+    float *act = nullptr, *logits = nullptr, *xnorm = nullptr, *part = nullptr;
+    unsigned *prompt = nullptr, *toks = nullptr, *counters = nullptr;
+    cw::DevState* st = nullptr;
+    int n_splits = 1;
+    bool use_graph = true;
+    cudaGraphExec_t g_prompt = nullptr, g_decode = nullptr;
+    size_t host_pos = 0, n_prompt = 0, n_produced = 0;
+    unsigned* h_tok = nullptr;     // pinned, one token for per-step reads
+    unsigned* h_tok_in = nullptr;  // pinned, one token for per-step writes
+};
+
+namespace cw {
+
+static int sess_alloc(cw_session* s, size_t nbytes, void** p) {
+    cw_buf b;
+    BufEntry* e;
+    CW_TRY(buf_new(s->ctx, nbytes, BUF_PERSISTENT, &b, &e));
+    s->owned.push_back(b);
+    CW_CUDA(cudaMemsetAsync(e->ptr, 0, nbytes, s->ctx->stream));
+    *p = e->ptr;
+    return CW_OK;
+}
+
+// Enqueue one generate step (decode: with lm_head + argmax).
+static int enqueue_step(cw_session* s, bool decode) {
+    cw_model* m = s->m;
+    cw_ctx* ctx = s->ctx;
+    const cw_model_info& I = m->info;
+    const int qd = I.n_heads * I.head_dim, kvd = I.n_kv * I.head_dim;
+    const bool post = I.post_norms != 0;
+    const int unit = I.norm_kind == 1;
+    // With the context profiler on (direct launches only), every kernel is
+    // bracketed by CUDA events under its stage name.
+    std::unique_ptr<OpScope> sc;
+    auto stage = [&](const char* name) {
+        sc.reset();
+        if (ctx->profiling) sc.reset(new OpScope(ctx, name));
+    };
+    stage("embed");
+    k_embed<<<1, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, I.dim, I.embed_scale,
+                                        s->st, s->hidden);
+    CW_TRY(check_launch("embed"));
+    for (uint32_t li = 0; li < I.n_layers; li++) {
+        stage("attn_in");
+        const Layer& l = m->L[li];
+        FArgs a{};
+        // attn_in: x = rmsnorm(h) with h = hidden, or (post-norm families,
+        // li > 0) h = hidden_b + postnorm(tmp) written back to hidden.
+        a.payload = l.qkv.payload;
+        a.scales = l.qkv.scales;
+        a.K = I.dim;
+        a.N = l.qkv.rows;
+        if (post && li > 0) {
+            a.base = s->hidden_b;
+            a.delta = s->tmp;
+            a.post_w = m->L[li - 1].post_ffw;
+            a.h_out = s->hidden;
+        } else {
+            a.base = s->hidden;
+        }
+        a.norm_w = l.attn_norm;
+        a.eps = I.eps;
+        a.unit = unit;
+        a.y = s->qkv;
+        a.bias = l.qkv_bias;
+        CW_TRY((fgemv<PRO_NORM, EPI_STORE>(ctx, a)));
+
+        stage("attention");
+        AArgs t{};
+        t.qkv = s->qkv;
+        t.q_norm = l.q_norm;
+        t.k_norm = l.k_norm;
+        t.eps = I.eps;
+        t.inv_freq = m->inv_freq;
+        t.kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
+        t.vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
+        t.max_seq = (int)s->max_seq;
+        t.out = s->attn;
+        t.part = s->part;
+        t.counters = s->counters;
+        t.n_heads = I.n_heads;
+        t.n_kv = I.n_kv;
+        t.hd = I.head_dim;
+        t.n_splits = s->n_splits;
+        t.window = (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
+        t.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
+        t.softcap = I.attn_softcap;
+        t.st = s->st;
+        CW_TRY(launch_fattn(ctx, t));
+
+        stage("attn_out");
+        FArgs o{};
+        o.payload = l.wo.payload;
+        o.scales = l.wo.scales;
+        o.K = qd;
+        o.N = I.dim;
+        o.x = s->attn;
+        o.y = post ? s->tmp : s->hidden;
+        CW_TRY(post ? (fgemv<PRO_X, EPI_STORE>(ctx, o)) : (fgemv<PRO_X, EPI_RESID>(ctx, o)));
+
+        stage("ffn_in");
+        FArgs f{};
+        f.payload = l.gate_up.payload;
+        f.scales = l.gate_up.scales;
+        f.K = I.dim;
+        f.N = l.gate_up.rows;
+        f.base = s->hidden;
+        if (post) {
+            f.delta = s->tmp;
+            f.post_w = l.post_attn;
+            f.h_out = s->hidden_b;
+        }
+        f.norm_w = l.ffn_norm;
+        f.eps = I.eps;
+        f.unit = unit;
+        f.y = s->act;
+        f.geglu = I.activation == 1;
+        CW_TRY((fgemv<PRO_NORM, EPI_GLU>(ctx, f)));
+
+        stage("ffn_out");
+        FArgs d{};
+        d.payload = l.down.payload;
+        d.scales = l.down.scales;
+        d.K = I.hidden;
+        d.N = I.dim;
+        d.x = s->act;
+        d.y = post ? s->tmp : s->hidden;
+        CW_TRY(post ? (fgemv<PRO_X, EPI_STORE>(ctx, d)) : (fgemv<PRO_X, EPI_RESID>(ctx, d)));
+    }
+    if (decode) {
+        stage("lm_head");
+        FArgs h{};
+        h.payload = m->head.payload;
+        h.scales = m->head.scales;
+        h.K = I.dim;
+        h.N = (int)I.vocab;
+        if (post) {
+            h.base = s->hidden_b;
+            h.delta = s->tmp;
+            h.post_w = m->L[I.n_layers - 1].post_ffw;
+        } else {
+            h.base = s->hidden;
+        }
+        h.norm_w = m->final_norm;
+        h.xn_out = s->xnorm;
+        h.eps = I.eps;
+        h.unit = unit;
+        h.y = s->logits;
+        h.softcap = I.final_softcap;
+        h.st = s->st;
+        CW_TRY((fgemv<PRO_NORM, EPI_HEAD>(ctx, h)));
+    }
+    stage("finalize");
+    k_finalize<<<1, 1, 0, ctx->stream>>>(s->st, s->prompt, s->toks, decode ? 1 : 0);
+    sc.reset();
+    return check_launch("finalize");
+}
+
+static int build_graph(cw_session* s, bool decode, cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    CW_CUDA(cudaStreamBeginCapture(s->ctx->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(s, decode);
+    cudaError_t e = cudaStreamEndCapture(s->ctx->stream, &g);
+    if (rc != CW_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return set_error(CW_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess)
+        return set_error(CW_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    return CW_OK;
+}
+
+static int run_step(cw_session* s) {
+    bool decode = !(s->host_pos + 1 < s->n_prompt);
+    CW_CHECK(s->host_pos < s->max_seq, CW_ERR_INVALID_ARG,
+             "session is full: position %zu, max_seq %zu", s->host_pos, s->max_seq);
+    if (s->use_graph) {
+        cudaGraphExec_t* g = decode ? &s->g_decode : &s->g_prompt;
+        if (!*g) CW_TRY(build_graph(s, decode, g));
+        CW_CUDA(cudaGraphLaunch(*g, s->ctx->stream));
+    } else {
+        CW_TRY(enqueue_step(s, decode));
+    }
+    s->host_pos++;
+    if (decode) s->n_produced++;
+    return CW_OK;
+}
+
+}  // namespace cw
+
+using namespace cw;
+
+extern "C" {
+
+int cw_model_load_gguf(cw_ctx* ctx, const char* path, cw_model** out) {
+    clear_error();
+    CW_CHECK(ctx && path && out, CW_ERR_INVALID_ARG, "cw_model_load_gguf: bad arguments");
+    cudaSetDevice(ctx->device);
+    cw_model* m = new cw_model();
+    m->ctx = ctx;
+    int rc = model_load(m, path);
+    if (rc != CW_OK) {
+        std::string msg = cw_last_error();
+        cw_model_free(m);
+        return set_error(rc, "%s", msg.c_str());
+    }
+    *out = m;
+    return CW_OK;
+}
+
+int cw_model_free(cw_model* m) {
+    if (!m) return CW_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    for (cw_buf b : m->owned) {
+        auto it = m->ctx->bufs.find(b);
+        if (it != m->ctx->bufs.end()) {
+            cudaFree(it->second.ptr);
+            m->ctx->bufs.erase(it);
+        }
+    }
+    delete m;
+    return CW_OK;
+}
+
+int cw_model_get_info(cw_model* m, cw_model_info* info) {
+    clear_error();
+    CW_CHECK(m && info, CW_ERR_INVALID_ARG, "cw_model_get_info: bad arguments");
+    *info = m->info;
+    return CW_OK;
+}
+
+int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
+    clear_error();
+    CW_CHECK(m && out && max_seq > 0 && max_seq < (1u << 24), CW_ERR_INVALID_ARG,
+             "cw_session_create: bad arguments");
+    cw_ctx* ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    const cw_model_info& I = m->info;
+    cw_session* s = new cw_session();
+    s->m = m;
+    s->ctx = ctx;
+    s->max_seq = max_seq;
+    int rc = CW_OK;
+    auto A = [&](size_t n, void** p) {
+        if (rc == CW_OK) rc = sess_alloc(s, n, p);
+    };
+    size_t kv = (size_t)I.n_layers * I.n_kv * max_seq * I.head_dim * 4;
+    size_t qd = (size_t)I.n_heads * I.head_dim, kvd = (size_t)I.n_kv * I.head_dim;
+    A(kv, (void**)&s->kc);
+    A(kv, (void**)&s->vc);
+    A(I.dim * 4, (void**)&s->hidden);
+    A(I.dim * 4, (void**)&s->hidden_b);
+    A(I.dim * 4, (void**)&s->tmp);
+    A((qd + 2 * kvd) * 4, (void**)&s->qkv);
+    A(qd * 4, (void**)&s->attn);
+    A((size_t)I.hidden * 4, (void**)&s->act);
+    A((size_t)I.vocab * 4, (void**)&s->logits);
+    A(I.dim * 4, (void**)&s->xnorm);
+    // split-KV: about two CTAs per SM, at most one split per 8 keys
+    s->n_splits = std::max(1, std::min<int>((int)((max_seq + 7) / 8),
+                                            2 * ctx->sm_count / (int)I.n_kv));
+    A((size_t)I.n_heads * s->n_splits * (I.head_dim + 2) * 4, (void**)&s->part);
+    A(max_seq * 4, (void**)&s->prompt);
+    A(max_seq * 4, (void**)&s->toks);
+    A((size_t)I.n_kv * 4, (void**)&s->counters);
+    A(sizeof(DevState), (void**)&s->st);
+    if (rc == CW_OK && (cudaMallocHost(&s->h_tok, sizeof(unsigned)) != cudaSuccess ||
+                        cudaMallocHost(&s->h_tok_in, sizeof(unsigned)) != cudaSuccess))
+        rc = set_error(CW_ERR_OOM, "pinned host allocation failed");
+    if (rc == CW_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+        rc = set_error(CW_ERR_CUDA, "session setup failed");
+    if (rc != CW_OK) {
+        std::string msg = cw_last_error();
+        cw_session_free(s);
+        return set_error(rc, "%s", msg.c_str());
+    }
+    *out = s;
+    return CW_OK;
+}
+
+int cw_session_free(cw_session* s) {
+    if (!s) return CW_OK;
+    cudaSetDevice(s->ctx->device);
+    cudaStreamSynchronize(s->ctx->stream);
+    if (s->g_prompt) cudaGraphExecDestroy(s->g_prompt);
+    if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
+    for (cw_buf b : s->owned) {
+        auto it = s->ctx->bufs.find(b);
+        if (it != s->ctx->bufs.end()) {
+            cudaFree(it->second.ptr);
+            s->ctx->bufs.erase(it);
+        }
+    }
+    if (s->h_tok) cudaFreeHost(s->h_tok);
+    if (s->h_tok_in) cudaFreeHost(s->h_tok_in);
+    delete s;
+    return CW_OK;
+}
+
+int cw_session_set_graph(cw_session* s, int use_graph) {
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_set_graph: session is NULL");
+    s->use_graph = use_graph != 0;
+    return CW_OK;
+}
+
+int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
+    clear_error();
+    CW_CHECK(s && prompt && n_prompt > 0, CW_ERR_INVALID_ARG,
+             "cw_session_begin: the prompt must hold at least one token");
+    CW_CHECK(n_prompt <= s->max_seq, CW_ERR_INVALID_ARG, "prompt of %zu tokens exceeds max_seq %zu",
+             n_prompt, s->max_seq);
+    for (size_t i = 0; i < n_prompt; i++)
+        CW_CHECK(prompt[i] < s->m->info.vocab, CW_ERR_INVALID_ARG,
+                 "prompt token %u at %zu is outside the vocabulary (%u)", prompt[i], i,
+                 s->m->info.vocab);
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaMemcpyAsync(s->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, s->ctx->stream));
+    k_begin<<<1, 1, 0, s->ctx->stream>>>(s->st, s->prompt, (int)n_prompt);
+    CW_TRY(check_launch("session begin"));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    s->host_pos = 0;
+    s->n_prompt = n_prompt;
+    s->n_produced = 0;
+    return CW_OK;
+}
+
+int cw_session_run(cw_session* s, size_t n_steps, size_t* n_produced) {
+    clear_error();
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_run: session is NULL");
+    CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_session_run: call cw_session_begin first");
+    cudaSetDevice(s->ctx->device);
+    size_t before = s->n_produced;
+    for (size_t i = 0; i < n_steps; i++) CW_TRY(run_step(s));
+    if (n_produced) *n_produced = s->n_produced - before;
+    return check_launch("session run");
+}
+
+int cw_session_tokens(cw_session* s, uint32_t* out, size_t cap, size_t* n) {
+    clear_error();
+    CW_CHECK(s && n, CW_ERR_INVALID_ARG, "cw_session_tokens: bad arguments");
+    cudaSetDevice(s->ctx->device);
+    size_t k = std::min(cap, s->n_produced);
+    if (k && out)
+        CW_CUDA(cudaMemcpyAsync(out, s->toks, k * 4, cudaMemcpyDeviceToHost, s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    *n = s->n_produced;
+    return check_device_status(s->ctx);
+}
+
+int cw_session_logits(cw_session* s, float* out, size_t vocab) {
+    clear_error();
+    CW_CHECK(s && out && vocab == s->m->info.vocab, CW_ERR_INVALID_ARG,
+             "cw_session_logits: bad arguments (vocab is %u)", s ? s->m->info.vocab : 0);
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaMemcpyAsync(out, s->logits, vocab * 4, cudaMemcpyDeviceToHost, s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    return CW_OK;
+}
+
+int cw_session_hidden(cw_session* s, float* out, size_t dim) {
+    clear_error();
+    CW_CHECK(s && out && dim == s->m->info.dim, CW_ERR_INVALID_ARG,
+             "cw_session_hidden: bad arguments");
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaMemcpyAsync(out, s->xnorm, dim * 4, cudaMemcpyDeviceToHost, s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    return CW_OK;
+}
+
+int cw_session_pos(cw_session* s, size_t* pos) {
+    CW_CHECK(s && pos, CW_ERR_INVALID_ARG, "cw_session_pos: bad arguments");
+    *pos = s->host_pos;
+    return CW_OK;
+}
+
+int cw_session_step(cw_session* s, uint32_t token_in, uint32_t* token_out) {
+    clear_error();
+    CW_CHECK(s && token_out, CW_ERR_INVALID_ARG, "cw_session_step: bad arguments");
+    CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_session_step: call cw_session_begin first");
+    CW_CHECK(token_in == CW_TOKEN_DEVICE || token_in < s->m->info.vocab, CW_ERR_INVALID_ARG,
+             "cw_session_step: token %u outside the vocabulary", token_in);
+    cudaSetDevice(s->ctx->device);
+    if (token_in != CW_TOKEN_DEVICE) {
+        *s->h_tok_in = token_in;
+        CW_CUDA(cudaMemcpyAsync(&s->st->token, s->h_tok_in, 4, cudaMemcpyHostToDevice,
+                                s->ctx->stream));
+    }
+    bool decode = !(s->host_pos + 1 < s->n_prompt);
+    size_t slot = s->n_produced;
+    CW_TRY(run_step(s));
+    if (decode) {
+        CW_CUDA(cudaMemcpyAsync(s->h_tok, s->toks + slot, 4, cudaMemcpyDeviceToHost,
+                                s->ctx->stream));
+        CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+        *token_out = *s->h_tok;
+    } else {
+        CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+        *token_out = 0xffffffffu;
+    }
+    return CW_OK;
+}
+
+int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms) {
+    clear_error();
+    CW_CHECK(s && ms, CW_ERR_INVALID_ARG, "cw_session_run_timed: bad arguments");
+    CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_session_run_timed: call cw_session_begin first");
+    cudaSetDevice(s->ctx->device);
+    // build graphs outside the timed region
+    if (s->use_graph) {
+        if (!s->g_prompt && s->host_pos + 1 < s->n_prompt) CW_TRY(build_graph(s, false, &s->g_prompt));
+        if (!s->g_decode) CW_TRY(build_graph(s, true, &s->g_decode));
+    }
+    cudaEvent_t e0, e1;
+    CW_CUDA(cudaEventCreate(&e0));
+    CW_CUDA(cudaEventCreate(&e1));
+    CW_CUDA(cudaEventRecord(e0, s->ctx->stream));
+    int rc = CW_OK;
+    for (size_t i = 0; i < n_steps && rc == CW_OK; i++) rc = run_step(s);
+    cudaEventRecord(e1, s->ctx->stream);
+    cudaEventSynchronize(e1);
+    float f = 0.f;
+    cudaEventElapsedTime(&f, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    CW_TRY(rc);
+    *ms = f;
+    return check_device_status(s->ctx);
+}
+
+int cw_session_launches(cw_session* s, size_t* prompt_step, size_t* decode_step) {
+    CW_CHECK(s && prompt_step && decode_step, CW_ERR_INVALID_ARG, "cw_session_launches: bad arguments");
+    // embed + 5 per layer + finalize (+ lm_head/argmax on decode steps)
+    size_t per = 2 + 5 * (size_t)s->m->info.n_layers;
+    *prompt_step = per;
+    *decode_step = per + 1;
+    return CW_OK;
+}
+
+int cw_generate(cw_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new,
+                uint32_t* out_tokens) {
+    clear_error();
+    CW_CHECK(m && prompt && out_tokens && n_prompt > 0, CW_ERR_INVALID_ARG,
+             "cw_generate: bad arguments (the prompt must hold at least one token)");
+    size_t want = std::max<size_t>(max_new, 1);
+    cw_session* s = nullptr;
+    CW_TRY(cw_session_create(m, n_prompt + want, &s));
+    std::unique_ptr<cw_session, int (*)(cw_session*)> guard(s, cw_session_free);
+    CW_TRY(cw_session_begin(s, prompt, n_prompt));
+    size_t produced = 0;
+    while (produced < want) {
+        bool decode = !(s->host_pos + 1 < s->n_prompt);
+        CW_TRY(run_step(s));
+        if (decode) {
+            // mod.rs:103: the produced token is read back every step
+            CW_CUDA(cudaMemcpyAsync(s->h_tok, s->toks + produced, 4, cudaMemcpyDeviceToHost,
+                                    s->ctx->stream));
+            CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+            out_tokens[produced++] = *s->h_tok;
+        }
+    }
+    return check_device_status(s->ctx);
+}
+
+}  // extern "C"

@@ -1,0 +1,305 @@
+"""GGUF v3 writing and seeded random-init checkpoints.
+
+The writer produces the container that chat-wgpu's loader parses
+(src/loader/gguf.rs:68-106): magic, version 3, tensor/metadata counts,
+typed metadata, tensor infos, a data section aligned to `general.alignment`.
+
+`synth_model` writes a random-init checkpoint of a model shape: every matrix
+(projections and token_embd) as GGUF Q4_0 blocks with 4-bit codes uniform in
+0..15 and per-block scales d ~ U(0.002, 0.02) rounded to f16; norm gains f32
+~ N(1, 0.02) (UnitShift families: N(0, 0.02), so the applied gain 1 + w is
+again near 1).  There are no real checkpoints on this machine; these files
+stand in for them with the same tensor names, shapes and dtypes.
+"""
+from __future__ import annotations
+
+import os
+import struct
+from dataclasses import dataclass, field
+
+import numpy as np
+
+GGML_F32, GGML_F16, GGML_Q4_0 = 0, 1, 2
+
+# metadata value type ids (gguf.rs:125-151)
+_T_U8, _T_I8, _T_U16, _T_I16, _T_U32, _T_I32, _T_F32, _T_BOOL, _T_STR, _T_ARR, _T_U64, _T_I64, _T_F64 = range(13)
+
+
+def _str(s: str) -> bytes:
+    b = s.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def _meta_value(v) -> bytes:
+    if isinstance(v, bool):
+        return struct.pack("<IB", _T_BOOL, int(v))
+    if isinstance(v, int):
+        return struct.pack("<II", _T_U32, v) if 0 <= v < 2**32 else struct.pack("<Iq", _T_I64, v)
+    if isinstance(v, float):
+        return struct.pack("<If", _T_F32, v)
+    if isinstance(v, str):
+        return struct.pack("<I", _T_STR) + _str(v)
+    if isinstance(v, (list, tuple)):
+        body = b"".join(_str(x) if isinstance(x, str) else struct.pack("<I", x) for x in v)
+        et = _T_STR if v and isinstance(v[0], str) else _T_U32
+        return struct.pack("<IIQ", _T_ARR, et, len(v)) + body
+    raise TypeError(f"unsupported metadata value {v!r}")
+
+
+@dataclass
+class Tensor:
+    name: str
+    ggml_type: int
+    dims: tuple          # ne[0] = innermost (row length)
+    data: object         # bytes-like, or a callable returning bytes (lazy)
+
+
+@dataclass
+class GgufWriter:
+    meta: dict = field(default_factory=dict)
+    tensors: list = field(default_factory=list)
+    alignment: int = 32
+
+    def add(self, name, ggml_type, dims, data):
+        self.tensors.append(Tensor(name, ggml_type, tuple(int(d) for d in dims), data))
+
+    @staticmethod
+    def nbytes(t: Tensor) -> int:
+        n = int(np.prod(t.dims))
+        return {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18}[t.ggml_type]
+
+    def write(self, path: str) -> None:
+        meta = dict(self.meta)
+        meta.setdefault("general.alignment", self.alignment)
+        head = bytearray(b"GGUF" + struct.pack("<IQQ", 3, len(self.tensors), len(meta)))
+        for k, v in meta.items():
+            head += _str(k) + _meta_value(v)
+        off = 0
+        offsets = []
+        for t in self.tensors:
+            offsets.append(off)
+            off += self.nbytes(t)
+            off = (off + self.alignment - 1) // self.alignment * self.alignment
+        for t, o in zip(self.tensors, offsets):
+            head += _str(t.name) + struct.pack("<I", len(t.dims))
+            head += b"".join(struct.pack("<Q", d) for d in t.dims)
+            head += struct.pack("<IQ", t.ggml_type, o)
+        pad = (-len(head)) % self.alignment
+        tmp = path + ".tmp"
+        with open(tmp, "wb") as f:
+            f.write(head + b"\0" * pad)
+            pos = 0
+            for t, o in zip(self.tensors, offsets):
+                if o > pos:
+                    f.write(b"\0" * (o - pos))
+                    pos = o
+                data = t.data() if callable(t.data) else t.data
+                mv = memoryview(np.ascontiguousarray(data) if isinstance(data, np.ndarray) else data).cast("B")
+                if len(mv) != self.nbytes(t):
+                    raise ValueError(f"{t.name}: {len(mv)} bytes, expected {self.nbytes(t)}")
+                f.write(mv)
+                pos += len(mv)
+        os.replace(tmp, path)
+
+
+def random_q4_0_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.ndarray:
+    """[rows * in_f/32, 18] uint8 GGUF Q4_0 blocks: f16 d ~ U(0.002, 0.02), codes uniform."""
+    nb = rows * (in_f // 32)
+    blocks = np.empty((nb, 18), dtype=np.uint8)
+    d = rng.uniform(0.002, 0.02, size=nb).astype(np.float16)
+    blocks[:, 0:2] = d.view(np.uint8).reshape(nb, 2)
+    blocks[:, 2:] = rng.integers(0, 256, size=(nb, 16), dtype=np.uint8)
+    return blocks
+
+
+# Model shapes named by BASELINE.json's configs (random-init), plus the tiny
+# shape of the reference's RandomWeights verify model (src/main.rs:166-174).
+CONFIGS = {
+    "qwen3-0.6b": dict(arch="qwen3", dim=1024, n_layers=28, n_heads=16, n_kv=8, head_dim=128,
+                       hidden=3072, vocab=151936, eps=1e-6, theta=1e6, tied=True),
+    "qwen3-8b": dict(arch="qwen3", dim=4096, n_layers=36, n_heads=32, n_kv=8, head_dim=128,
+                     hidden=12288, vocab=151936, eps=1e-6, theta=1e6, tied=False),
+    "gemma2-2b": dict(arch="gemma2", dim=2304, n_layers=26, n_heads=8, n_kv=4, head_dim=256,
+                      hidden=9216, vocab=256000, eps=1e-6, theta=1e4, tied=True, window=4096,
+                      attn_softcap=50.0, final_softcap=30.0),
+    "tiny-qwen3": dict(arch="qwen3", dim=64, n_layers=2, n_heads=4, n_kv=2, head_dim=16,
+                       hidden=128, vocab=256, eps=1e-6, theta=1e6, tied=True),
+    # small shapes that exercise the family switches in tests
+    "tiny-gemma2": dict(arch="gemma2", dim=128, n_layers=3, n_heads=4, n_kv=2, head_dim=32,
+                        hidden=256, vocab=512, eps=1e-6, theta=1e4, tied=True, window=6,
+                        attn_softcap=2.0, final_softcap=3.0),
+    "tiny-qwen2": dict(arch="qwen2", dim=128, n_layers=2, n_heads=8, n_kv=2, head_dim=16,
+                       hidden=256, vocab=300, eps=1e-6, theta=1e6, tied=False, bias=True),
+}
+
+
+def synth_model(path: str, cfg: dict, seed: int = 0) -> str:
+    """Write a seeded random-init GGUF of shape `cfg` (see CONFIGS)."""
+    arch = cfg["arch"]
+    dim, L, nh, nkv, hd = cfg["dim"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv"], cfg["head_dim"]
+    hid, vocab = cfg["hidden"], cfg["vocab"]
+    qd, kvd = nh * hd, nkv * hd
+    unit = arch == "gemma2"
+    w = GgufWriter()
+    w.meta["general.architecture"] = arch
+    w.meta["general.name"] = f"synthetic-{arch}"
+    p = arch + "."
+    w.meta[p + "block_count"] = L
+    w.meta[p + "context_length"] = 40960
+    w.meta[p + "embedding_length"] = dim
+    w.meta[p + "feed_forward_length"] = hid
+    w.meta[p + "attention.head_count"] = nh
+    w.meta[p + "attention.head_count_kv"] = nkv
+    w.meta[p + "attention.key_length"] = hd
+    w.meta[p + "attention.value_length"] = hd
+    w.meta[p + "attention.layer_norm_rms_epsilon"] = float(cfg["eps"])
+    w.meta[p + "rope.freq_base"] = float(cfg["theta"])
+    w.meta[p + "vocab_size"] = vocab
+    if arch == "gemma2":
+        w.meta[p + "attention.sliding_window"] = int(cfg.get("window", 4096))
+        w.meta[p + "attn_logit_softcapping"] = float(cfg.get("attn_softcap", 50.0))
+        w.meta[p + "final_logit_softcapping"] = float(cfg.get("final_softcap", 30.0))
+    idx = [0]
+
+    def rng():  # one independent stream per tensor, in file order
+        idx[0] += 1
+        return np.random.default_rng(np.random.SeedSequence([seed, idx[0]]))
+
+    def mat(name, rows, in_f):
+        r = rng()
+        w.add(name, GGML_Q4_0, (in_f, rows), lambda r=r: random_q4_0_blocks(r, rows, in_f))
+
+    def vec(name, n, mean=None):
+        r = rng()
+        mean = (0.0 if unit else 1.0) if mean is None else mean
+        w.add(name, GGML_F32, (n,), lambda r=r: r.normal(mean, 0.02, size=n).astype(np.float32))
+
+    mat("token_embd.weight", vocab, dim)
+    for i in range(L):
+        b = f"blk.{i}."
+        vec(b + "attn_norm.weight", dim)
+        mat(b + "attn_q.weight", qd, dim)
+        mat(b + "attn_k.weight", kvd, dim)
+        mat(b + "attn_v.weight", kvd, dim)
+        if cfg.get("bias"):
+            vec(b + "attn_q.bias", qd, mean=0.0)
+            vec(b + "attn_k.bias", kvd, mean=0.0)
+            vec(b + "attn_v.bias", kvd, mean=0.0)
+        mat(b + "attn_output.weight", dim, qd)
+        if arch == "qwen3":
+            vec(b + "attn_q_norm.weight", hd)
+            vec(b + "attn_k_norm.weight", hd)
+        vec(b + "ffn_norm.weight", dim)
+        mat(b + "ffn_gate.weight", hid, dim)
+        mat(b + "ffn_up.weight", hid, dim)
+        mat(b + "ffn_down.weight", dim, hid)
+        if arch == "gemma2":
+            vec(b + "post_attention_norm.weight", dim)
+            vec(b + "post_ffw_norm.weight", dim)
+    vec("output_norm.weight", dim)
+    if not cfg.get("tied", True):
+        mat("output.weight", vocab, dim)
+    w.write(path)
+    return path
+
+
+def cached_model(name: str, seed: int = 0, cfg: dict | None = None, directory: str | None = None) -> str:
+    """Path of the synthetic GGUF for config `name`, written once per seed."""
+    cfg = cfg or CONFIGS[name]
+    directory = directory or os.environ.get("CW_MODEL_DIR", "/tmp/chat_wgpu_b200_models")
+    os.makedirs(directory, exist_ok=True)
+    path = os.path.join(directory, f"{name}-seed{seed}.gguf")
+    if not os.path.exists(path):
+        synth_model(path, cfg, seed)
+    return path
+
+
+class GgufReader:
+    """Minimal GGUF v3 reader (src/loader/gguf.rs:68-106) for host-side tools:
+    metadata values and raw tensor bytes, memory-mapped."""
+
+    _SIZES = {_T_U8: 1, _T_I8: 1, _T_U16: 2, _T_I16: 2, _T_U32: 4, _T_I32: 4, _T_F32: 4,
+              _T_BOOL: 1, _T_U64: 8, _T_I64: 8, _T_F64: 8}
+    _FMT = {_T_U8: "<B", _T_I8: "<b", _T_U16: "<H", _T_I16: "<h", _T_U32: "<I", _T_I32: "<i",
+            _T_F32: "<f", _T_BOOL: "<B", _T_U64: "<Q", _T_I64: "<q", _T_F64: "<d"}
+
+    def __init__(self, path: str):
+        import mmap
+        self._f = open(path, "rb")
+        self.buf = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
+        buf = self.buf
+        if buf[:4] != b"GGUF":
+            raise ValueError("not a GGUF file")
+        _ver, n_t, n_kv = struct.unpack_from("<IQQ", buf, 4)
+        o = 24
+        self.meta = {}
+        for _ in range(n_kv):
+            k, o = self._str(o)
+            t = struct.unpack_from("<I", buf, o)[0]
+            o += 4
+            if t == _T_STR:
+                v, o = self._str(o)
+            elif t == _T_ARR:
+                et, cnt = struct.unpack_from("<IQ", buf, o)
+                o += 12
+                v = []
+                for _ in range(cnt):
+                    if et == _T_STR:
+                        x, o = self._str(o)
+                    else:
+                        x = struct.unpack_from(self._FMT[et], buf, o)[0]
+                        o += self._SIZES[et]
+                    v.append(x)
+            else:
+                v = struct.unpack_from(self._FMT[t], buf, o)[0]
+                o += self._SIZES[t]
+            self.meta[k] = v
+        self.infos = {}
+        for _ in range(n_t):
+            nm, o = self._str(o)
+            nd = struct.unpack_from("<I", buf, o)[0]
+            o += 4
+            dims = struct.unpack_from("<" + "Q" * nd, buf, o)
+            o += 8 * nd
+            tt, off = struct.unpack_from("<IQ", buf, o)
+            o += 12
+            self.infos[nm] = (tt, tuple(int(d) for d in dims), off)
+        align = int(self.meta.get("general.alignment", 32)) or 32
+        self.data_start = (o + align - 1) // align * align
+
+    def _str(self, o):
+        n = struct.unpack_from("<Q", self.buf, o)[0]
+        return bytes(self.buf[o + 8:o + 8 + n]).decode(), o + 8 + n
+
+    def has(self, name: str) -> bool:
+        return name in self.infos
+
+    def tensor(self, name: str):
+        """(ggml_type, dims, bytes) of a tensor."""
+        tt, dims, off = self.infos[name]
+        n = int(np.prod(dims))
+        nbytes = {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18}[tt]
+        s = self.data_start + off
+        return tt, dims, self.buf[s:s + nbytes]
+
+    def vector_f32(self, name: str) -> np.ndarray:
+        tt, dims, raw = self.tensor(name)
+        if tt == GGML_F32:
+            return np.frombuffer(raw, dtype=np.float32).copy()
+        if tt == GGML_F16:
+            return np.frombuffer(raw, dtype=np.float16).astype(np.float32)
+        raise ValueError(f"{name}: type {tt} is not a float vector")
+
+    def close(self):
+        self.buf.close()
+        self._f.close()
+
+
+def read_tensor_bytes(path: str, name: str) -> tuple[int, tuple, bytes]:
+    """(ggml_type, dims, raw bytes) of one tensor of a GGUF file."""
+    r = GgufReader(path)
+    try:
+        tt, dims, raw = r.tensor(name)
+        return tt, dims, bytes(raw)
+    finally:
+        r.close()

@@ -1,0 +1,238 @@
+/*
+ * chatcuda.h -- C ABI of libchatcuda.so, the B200 (sm_100a) replacement for
+ * chat-wgpu's GPU layer.
+ *
+ * The reference reaches the GPU through a Rust `GpuContext` (src/context.rs)
+ * and one host wrapper per op (src/kernels/{op}.rs); the model layer
+ * (src/model/{mod,qwen3,layers,cache}.rs) only ever calls those.  This header exports the same
+ * surface as plain C: an opaque context, buffer handles, one entry point per
+ * op wrapper, and the model-level calls.  Each declaration names the
+ * reference interface it replaces (path:line in the chat-wgpu tree).
+ *
+ * Conventions
+ *  - Every call returns a cw_status (0 == CW_OK).  On failure a message is
+ *    available from cw_last_error() on the calling thread.  Nothing aborts,
+ *    traps or throws across the ABI.
+ *  - Lengths named `len`/`n` count f32 (or u32) ELEMENTS, as in the reference
+ *    (GpuContext::empty(len), copy offsets in f32 elements, context.rs:207,252).
+ *    Lengths named `nbytes` count bytes.
+ *  - A context is bound to one CUDA device and one stream and, like the
+ *    reference's GpuContext (RefCell/Cell, !Sync), must be used from one
+ *    thread at a time.
+ *  - Ops are enqueued asynchronously on the context's stream, the analogue of
+ *    the reference recording into its shared encoder (context.rs:30-33).
+ *    cw_read()/cw_read_u32() synchronise, like GpuContext::read.
+ *  - Op wrappers return their result in a fresh ARENA buffer (*out), valid
+ *    until the next cw_reset_frame()/cw_clear_cache(), exactly as the
+ *    reference's ctx.empty() arena slots (context.rs:207-227).
+ */
+#ifndef CHATCUDA_H
+#define CHATCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CW_ABI_VERSION 1
+
+typedef struct cw_ctx cw_ctx;
+typedef struct cw_model cw_model;
+typedef struct cw_session cw_session;
+/* Buffer handle; 0 is "no buffer".  Replaces wgpu::Buffer. */
+typedef uint64_t cw_buf;
+
+typedef enum {
+    CW_OK = 0,
+    CW_ERR_INVALID_ARG = 1,  /* bad handle, size or shape                  */
+    CW_ERR_CUDA = 2,         /* a CUDA runtime call failed                 */
+    CW_ERR_OOM = 3,          /* device or host allocation failed           */
+    CW_ERR_NOT_FOUND = 4,    /* missing file / tensor / metadata           */
+    CW_ERR_UNSUPPORTED = 5,  /* dtype, architecture or shape not handled   */
+    CW_ERR_TIMEOUT = 6,      /* a bounded device-side wait gave up         */
+    CW_ERR_FORMAT = 7,       /* malformed GGUF                             */
+    CW_ERR_NO_DEVICE = 8     /* no CUDA device / wrong architecture        */
+} cw_status;
+
+/* ---- errors / version --------------------------------------------------- */
+/* Message of the last failing call on this thread ("" if none). */
+const char* cw_last_error(void);
+int cw_abi_version(void);
+
+/* ---- context: src/context.rs ------------------------------------------- */
+/* GpuContext::new (context.rs:60-104).  Picks CUDA device `device`, creates a
+ * non-blocking stream.  Fails with CW_ERR_NO_DEVICE if the device is not an
+ * sm_100 part. */
+int cw_ctx_create(int device, cw_ctx** out);
+int cw_ctx_destroy(cw_ctx* ctx);
+/* GpuContext.backend (context.rs:28,70): e.g. "CUDA sm_100a (NVIDIA B200)". */
+int cw_ctx_backend(cw_ctx* ctx, char* buf, size_t cap);
+/* Device index and the cudaStream_t (as void*) the context enqueues on. */
+int cw_ctx_device(cw_ctx* ctx, int* device);
+int cw_ctx_stream(cw_ctx* ctx, void** stream);
+
+/* ---- buffers ------------------------------------------------------------- */
+/* GpuContext::storage (context.rs:177-184): upload f32s to a new buffer. */
+int cw_storage(cw_ctx* ctx, const float* data, size_t len, cw_buf* out);
+/* GpuContext::storage_u32 (context.rs:187-194). */
+int cw_storage_u32(cw_ctx* ctx, const uint32_t* data, size_t len, cw_buf* out);
+/* Raw bytes (e.g. GGUF blocks); no reference counterpart beyond storage_u32. */
+int cw_storage_bytes(cw_ctx* ctx, const void* data, size_t nbytes, cw_buf* out);
+/* GpuContext::empty (context.rs:207-227): arena slot `cursor++`, reused at
+ * the same slot index every frame while its size is unchanged.  Contents are
+ * undefined.  Valid until the next reset_frame / clear_cache. */
+int cw_empty(cw_ctx* ctx, size_t len, cw_buf* out);
+/* GpuContext::empty_persistent (context.rs:229-232): never recycled. */
+int cw_empty_persistent(cw_ctx* ctx, size_t len, cw_buf* out);
+/* Drop a storage / persistent buffer (wgpu frees on Drop).  Arena buffers
+ * are owned by the context and are rejected here. */
+int cw_buf_release(cw_ctx* ctx, cw_buf buf);
+/* Size in bytes and device address of a buffer (interop, tests). */
+int cw_buf_nbytes(cw_ctx* ctx, cw_buf buf, size_t* nbytes);
+int cw_buf_device_ptr(cw_ctx* ctx, cw_buf buf, void** dptr);
+/* GpuContext::copy (context.rs:252-269): len f32s from src[src_off..] to
+ * dst[dst_off..]; offsets in f32 elements. */
+int cw_copy(cw_ctx* ctx, cw_buf src, size_t src_off, cw_buf dst, size_t dst_off, size_t len);
+/* queue.write_buffer equivalent: host f32s into dst[dst_off..]. */
+int cw_write(cw_ctx* ctx, cw_buf dst, size_t dst_off, const float* data, size_t len);
+/* GpuContext::read (context.rs:359-389): flush, wait for the stream, copy
+ * len f32s back.  cw_read_u32 is the `.to_bits()` reading of mod.rs:103. */
+int cw_read(cw_ctx* ctx, cw_buf src, float* out, size_t len);
+int cw_read_u32(cw_ctx* ctx, cw_buf src, uint32_t* out, size_t len);
+/* GpuContext::flush (context.rs:139-151): ops are already enqueued, so this
+ * only checks for launch errors; it does not wait. */
+int cw_flush(cw_ctx* ctx);
+/* Wait for all enqueued work; reports device-side errors (CW_ERR_TIMEOUT). */
+int cw_sync(cw_ctx* ctx);
+/* GpuContext::reset_frame (context.rs:234-240) / clear_cache (:242-250). */
+int cw_reset_frame(cw_ctx* ctx);
+int cw_clear_cache(cw_ctx* ctx);
+
+/* ---- profiler: src/context.rs:106-126, src/profile.rs ------------------- */
+typedef struct {
+    char kernel[32];    /* op label, as the reference's pass labels        */
+    uint32_t passes;    /* launches                                        */
+    double total_ms;    /* summed device time (CUDA events)                */
+} cw_profile_row;
+/* GpuContext::begin_profile: time every op launched until report. */
+int cw_begin_profile(cw_ctx* ctx);
+/* GpuContext::report_profile: rows sorted by total descending (profile.rs:114-115). */
+int cw_report_profile(cw_ctx* ctx, cw_profile_row* rows, size_t cap, size_t* n_rows);
+
+/* ---- op wrappers: src/kernels/{op}.rs ------------------------------------- */
+/* q4::gemv (q4.rs:9-30): y[out_f] = W x with W in the crate's re-quantised
+ * layout -- f32 scales[out_f*in_f/32], u32 quants[out_f*in_f/8], sequential
+ * nibbles (q4.rs:32-36).  in_f % 32 == 0. */
+int cw_q4_gemv(cw_ctx* ctx, cw_buf x, cw_buf scales, cw_buf quants,
+               size_t in_f, size_t out_f, cw_buf* out);
+/* q4::quantize_q4_0 (q4.rs:37-60) run on the device: f32 w[out_f, in_f] ->
+ * new persistent (scales, quants) buffers, bit-identical to the host routine. */
+int cw_q4_quantize(cw_ctx* ctx, cw_buf w, size_t out_f, size_t in_f,
+                   cw_buf* scales, cw_buf* quants);
+/* attention::attention (attention.rs:7-38): single-query GQA attention,
+ * q[n_heads*head_dim], k/v [seq, n_kv*head_dim], scale head_dim^-0.5. */
+int cw_attention(cw_ctx* ctx, cw_buf q, cw_buf k, cw_buf v, size_t n_heads,
+                 size_t n_kv, size_t seq, size_t head_dim, cw_buf* out);
+/* The same with the family extensions (no reference code): tanh soft-cap of
+ * the scaled scores (softcap > 0) and a sliding window of the last `window`
+ * keys (window > 0). */
+int cw_attention_ext(cw_ctx* ctx, cw_buf q, cw_buf k, cw_buf v, size_t n_heads,
+                     size_t n_kv, size_t seq, size_t head_dim, float softcap,
+                     uint32_t window, cw_buf* out);
+/* attention::add (attention.rs:40-51): c = a + b. */
+int cw_add(cw_ctx* ctx, cw_buf a, cw_buf b, size_t n, cw_buf* out);
+/* norm::rmsnorm / norm::rmsnorm_unit (norm.rs:185-195). */
+int cw_rmsnorm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t dim, float eps, cw_buf* out);
+int cw_rmsnorm_unit(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t dim, float eps, cw_buf* out);
+/* rope::rope (rope.rs:8-27): rotate-half at position pos. */
+int cw_rope(cw_ctx* ctx, cw_buf x, size_t rows, size_t head_dim, size_t pos, float theta, cw_buf* out);
+/* activation::swiglu / activation::geglu (activation.rs:103-110). */
+int cw_swiglu(cw_ctx* ctx, cw_buf gate, cw_buf up, size_t n, cw_buf* out);
+int cw_geglu(cw_ctx* ctx, cw_buf gate, cw_buf up, size_t n, cw_buf* out);
+/* argmax::argmax (argmax.rs:11-18): 1-element u32 buffer, ties -> lowest. */
+int cw_argmax(cw_ctx* ctx, cw_buf logits, size_t n, cw_buf* out);
+
+/* ---- GGUF-native Q4_0 (the B200 weight format) --------------------------
+ * GGUF Q4_0 blocks (f16 d + 16 nibble bytes, dequant.rs:60-78) are kept in
+ * HBM as two planes: the 16-byte nibble payloads and the f16 scales.  The
+ * repack is a lossless byte shuffle, so dequantised weights are bit-exact. */
+/* Upload host GGUF Q4_0 blocks of a [rows, in_f] tensor to a new persistent
+ * packed weight.  Replaces Q4Linear::from_f32 (layers.rs:82-90) without the
+ * lossy re-quantisation. */
+int cw_q4_0_upload(cw_ctx* ctx, const void* gguf_blocks, size_t rows, size_t in_f, cw_buf* w);
+/* Same from GGUF blocks already on the device (cw_storage_bytes). */
+int cw_q4_0_pack(cw_ctx* ctx, cw_buf gguf_blocks, size_t rows, size_t in_f, cw_buf* w);
+/* y[out_f] = W x over a packed Q4_0 weight (the decode GEMV). */
+int cw_q4_0_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out);
+/* Exact f32 dequantisation of a packed weight (dequant.rs:62-78). */
+int cw_q4_0_dequant(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out);
+
+/* ---- model: src/model/{mod,qwen3,layers,cache}.rs --------------------------------------------- */
+typedef struct {
+    uint32_t dim, n_layers, n_heads, n_kv, head_dim, hidden, vocab;
+    float eps, rope_theta;
+    /* FamilySpec (described by the reference's docs, not implemented there):
+     * norm 0 Plain / 1 UnitShift; act 0 SwiGlu / 1 GeGlu. */
+    uint32_t norm_kind, activation, qk_norm, qkv_bias, post_norms;
+    uint32_t sliding_window;            /* 0 = none; applies to even layers */
+    float attn_softcap, final_softcap;  /* 0 = off                          */
+    float embed_scale;                  /* 0 = none                         */
+    uint64_t weight_bytes;              /* bytes of packed weights in HBM   */
+    char arch[16];
+} cw_model_info;
+
+/* Model::load (mod.rs:26, qwen3.rs:44-99) from a GGUF file: architectures
+ * qwen3 / qwen2 / llama / gemma2; Q4_0 projections and embeddings, F32/F16
+ * norms and biases.  Weights stay Q4_0 in HBM (no re-quantisation). */
+int cw_model_load_gguf(cw_ctx* ctx, const char* path, cw_model** out);
+int cw_model_free(cw_model* model);
+int cw_model_get_info(cw_model* model, cw_model_info* info);
+
+/* A decode session = Model::new_cache (qwen3.rs:115) + the per-token state of
+ * generate (mod.rs:57-125).  max_seq bounds prompt + generated tokens. */
+int cw_session_create(cw_model* model, size_t max_seq, cw_session** out);
+int cw_session_free(cw_session* s);
+/* Start a sequence: upload the prompt and rewind to position 0. */
+int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt);
+/* Run `n_steps` steps of the generate loop (embed -> forward -> lm_head ->
+ * argmax -> next input) on the device without host round trips.  Prompt
+ * positions skip the lm_head, whose logits the reference discards
+ * (mod.rs:78-81).  Returns the number of tokens produced by these steps. */
+int cw_session_run(cw_session* s, size_t n_steps, size_t* n_produced);
+/* Tokens produced so far (<= cap). */
+int cw_session_tokens(cw_session* s, uint32_t* out, size_t cap, size_t* n);
+/* Logits of the last produced token (vocab floats) and the position count. */
+int cw_session_logits(cw_session* s, float* out, size_t vocab);
+int cw_session_pos(cw_session* s, size_t* pos);
+/* Hidden state after the final norm of the last step (dim floats): the
+ * analogue of tapping the forward's output (mod.rs:155-165). */
+int cw_session_hidden(cw_session* s, float* out, size_t dim);
+/* Per-step path selection: 1 = one CUDA graph per token (default),
+ * 0 = direct launches (debug). */
+int cw_session_set_graph(cw_session* s, int use_graph);
+/* One step with a host round trip, the shape of the reference's loop body
+ * (mod.rs:93-103): the input token is copied from the host (token_in, or
+ * CW_TOKEN_DEVICE to keep the device-side feedback), the step runs, and the
+ * token it produced (UINT32_MAX for a prompt position) is read back. */
+#define CW_TOKEN_DEVICE 0xffffffffu
+int cw_session_step(cw_session* s, uint32_t token_in, uint32_t* token_out);
+/* cw_session_run timed with CUDA events on the context stream: *ms is the
+ * device time of the n_steps steps. */
+int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms);
+/* Kernel launches one step makes (prompt and decode steps). */
+int cw_session_launches(cw_session* s, size_t* prompt_step, size_t* decode_step);
+
+/* model::generate (mod.rs:57-125): greedy, the prompt one token per step,
+ * exactly max_new tokens (and one token when max_new == 0, as the reference's
+ * post-push check does).  out_tokens holds max(max_new, 1) entries.  Like the
+ * reference (ctx.read per token, mod.rs:103) each produced token is read
+ * back to the host before the next step is launched. */
+int cw_generate(cw_model* model, const uint32_t* prompt, size_t n_prompt,
+                size_t max_new, uint32_t* out_tokens);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHATCUDA_H */
