@@ -59,6 +59,7 @@ SIGNATURES = {
     "cw_ctx_backend": [_vp, C.c_char_p, _sz],
     "cw_ctx_device": [_vp, C.POINTER(C.c_int)],
     "cw_ctx_stream": [_vp, C.POINTER(_vp)],
+    "cw_ctx_set_pdl": [_vp, C.c_int],
     "cw_storage": [_vp, _vp, _sz, _pbuf],
     "cw_storage_u32": [_vp, _vp, _sz, _pbuf],
     "cw_storage_bytes": [_vp, _vp, _sz, _pbuf],
@@ -92,6 +93,8 @@ SIGNATURES = {
     "cw_q4_0_pack": [_vp, _buf, _sz, _sz, _pbuf],
     "cw_q4_0_gemv": [_vp, _buf, _buf, _sz, _sz, _pbuf],
     "cw_q4_0_dequant": [_vp, _buf, _sz, _sz, _pbuf],
+    "cw_q4_0_gemv_bench": [_vp, _buf, C.POINTER(C.c_uint64), _sz, _sz, _sz, _sz,
+                           C.POINTER(C.c_double)],
     "cw_model_load_gguf": [_vp, C.c_char_p, C.POINTER(_vp)],
     "cw_model_free": [_vp],
     "cw_model_get_info": [_vp, C.POINTER(ModelInfo)],

@@ -4,11 +4,12 @@
 // Semantics follow chat-wgpu src/kernels/attention.wgsl:23-96: scores
 // s = scale * (q . k_j), an online softmax (running max m, denominator l,
 // rescaled accumulator), GQA head h -> kv head h / (n_heads / n_kv).
-// Work split: one CTA per (key range, kv head); the CTA's 4 warps take keys
-// j = lo + w, lo + w + 4, ... and each warp keeps an online-softmax state for
-// every query head of the group (GQA: K/V rows are read once per group).
-// Lane l holds head dims l, l+32, ... so each key row is one coalesced
-// 128-byte read per 32 dims.
+// Work split: one CTA per (key range, kv head); the CTA's 4 warps take
+// groups of 4 consecutive keys (warp w: keys lo + 4w .. lo + 4w + 3, then
+// +16, ...), issue all 8 K/V row loads of a group before using any, and keep
+// one online-softmax state per query head of the GQA group, so K/V rows are
+// read once per group.  Lane l holds head dims l, l+32, ..., so a key row is
+// one coalesced 128-byte read per 32 dims.
 #pragma once
 
 #include "cw_device.cuh"
@@ -16,17 +17,43 @@
 namespace cw {
 
 constexpr float REF_NEG_INF = -3.402823e38f;  // attention.wgsl:27
+constexpr int ATTN_MIN_KEYS = 32;             // keys per split before splitting further
+constexpr int ATTN_U = 4;                     // keys per warp iteration
 
-// Shared memory floats needed by attn_core for G heads of dim hd.
-__host__ __device__ constexpr size_t attn_smem_floats(int G, int hd) {
-    return (size_t)5 * G * (hd + 2);
+// Shared memory floats needed by attn_core + attn_finish for G heads of dim
+// hd and up to n_splits splits.
+__host__ __device__ constexpr size_t attn_smem_floats(int G, int hd, int n_splits) {
+    return (size_t)5 * G * (hd + 2) + (size_t)G * (n_splits + 1);
+}
+
+// Splits that hold keys for a (windowed) span: at most n_splits, at least
+// ATTN_MIN_KEYS keys each.
+__host__ __device__ __forceinline__ int attn_active_splits(int span, int n_splits) {
+    int by_len = (span + ATTN_MIN_KEYS - 1) / ATTN_MIN_KEYS;
+    by_len = by_len < 1 ? 1 : by_len;
+    return by_len < n_splits ? by_len : n_splits;
+}
+
+// Key range of split `split` of n_active over the prefix [j0, seq), with
+// j0 = seq - window for a sliding-window layer.
+__device__ __forceinline__ void attn_range(int seq, int window, int split, int n_active, int* jlo,
+                                           int* jhi) {
+    int j0 = (window > 0 && seq > window) ? seq - window : 0;
+    int span = seq - j0;
+    int per = (span + n_active - 1) / n_active;
+    *jlo = min(seq, j0 + split * per);
+    *jhi = min(seq, *jlo + per);
+}
+
+__device__ __forceinline__ int attn_span(int seq, int window) {
+    return (window > 0 && seq > window) ? window : seq;
 }
 
 // Computes, for the G query heads in qg[G][hd] (global or shared memory),
 // the un-normalised attention state over keys [jlo, jhi) of one kv head
 // (rows kb + j*rs, vb + j*rs).  On return res[gi*(hd+2) + d] holds the
-// accumulator A, res[.. + hd] the max M, res[.. + hd + 1] the denominator L
-// (all threads of the 128-thread CTA call it; it ends with __syncthreads()).
+// accumulator A, res[.. + hd] the max M, res[.. + hd + 1] the denominator L.
+// All threads of the 128-thread CTA call it; it ends with __syncthreads().
 // NC selects the read-only (non-coherent) load path; it must be false when
 // the calling kernel itself wrote K/V rows it then reads.
 template <int EPL, int GMAX, bool NC = true>
@@ -48,35 +75,56 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
             acc[gi][e] = 0.f;
         }
     }
-    for (int j = jlo + warp; j < jhi; j += 4) {
-        const float* kr = kb + (size_t)j * rs;
-        const float* vr = vb + (size_t)j * rs;
-        float kk[EPL], vv[EPL];
+    for (int base = jlo + warp * ATTN_U; base < jhi; base += 4 * ATTN_U) {
+        float kk[ATTN_U][EPL], vv[ATTN_U][EPL];
 #pragma unroll
-        for (int e = 0; e < EPL; e++) {
-            int d = lane + 32 * e;
-            if (NC) {
-                kk[e] = d < hd ? __ldg(kr + d) : 0.f;
-                vv[e] = d < hd ? __ldg(vr + d) : 0.f;
-            } else {
-                kk[e] = d < hd ? kr[d] : 0.f;
-                vv[e] = d < hd ? vr[d] : 0.f;
+        for (int u = 0; u < ATTN_U; u++) {
+            const int j = base + u;
+            const bool ok = j < jhi;
+            const float* kr = kb + (size_t)(ok ? j : jlo) * rs;
+            const float* vr = vb + (size_t)(ok ? j : jlo) * rs;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                int d = lane + 32 * e;
+                bool in = ok && d < hd;
+                if (NC) {
+                    kk[u][e] = in ? __ldg(kr + d) : 0.f;
+                    vv[u][e] = in ? __ldg(vr + d) : 0.f;
+                } else {
+                    kk[u][e] = in ? kr[d] : 0.f;
+                    vv[u][e] = in ? vr[d] : 0.f;
+                }
             }
         }
 #pragma unroll
         for (int gi = 0; gi < GMAX; gi++) {
             if (gi < G) {
-                float p = 0.f;
+                float s[ATTN_U];
+                float mn = m[gi];
 #pragma unroll
-                for (int e = 0; e < EPL; e++) p = fmaf(qr[gi][e], kk[e], p);
-                float s = warp_sum(p) * scale;
-                if (softcap > 0.f) s = softcap * tanhf(s / softcap);
-                float mn = fmaxf(m[gi], s);
-                float corr = expf(m[gi] - mn);
-                float pe = expf(s - mn);
-                l[gi] = l[gi] * corr + pe;
+                for (int u = 0; u < ATTN_U; u++) {
+                    float p = 0.f;
 #pragma unroll
-                for (int e = 0; e < EPL; e++) acc[gi][e] = acc[gi][e] * corr + vv[e] * pe;
+                    for (int e = 0; e < EPL; e++) p = fmaf(qr[gi][e], kk[u][e], p);
+                    s[u] = warp_sum(p) * scale;
+                    if (softcap > 0.f) s[u] = softcap * tanhf(s[u] / softcap);
+                    if (base + u < jhi) mn = fmaxf(mn, s[u]);
+                }
+                const float corr = expf(m[gi] - mn);
+                float pe[ATTN_U], psum = 0.f;
+#pragma unroll
+                for (int u = 0; u < ATTN_U; u++) {
+                    pe[u] = (base + u < jhi) ? expf(s[u] - mn) : 0.f;
+                    psum += pe[u];
+                }
+                l[gi] = l[gi] * corr + psum;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    float a = acc[gi][e] * corr;
+#pragma unroll
+                    for (int u = 0; u < ATTN_U; u++) a = fmaf(vv[u][e], pe[u], a);
+                    acc[gi][e] = a;
+                }
                 m[gi] = mn;
             }
         }
@@ -97,7 +145,7 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
         }
     }
     __syncthreads();
-    // merge the 4 warp states (attention.wgsl:88-95 merge rule)
+    // merge the 4 warp states (the merge rule of attention.wgsl:88-95)
     for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
         int gi = i / hd, d = i - gi * hd;
         float M = REF_NEG_INF;
@@ -120,15 +168,17 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
     __syncthreads();
 }
 
-// After attn_core: either write the normalised output (one split), or
-// publish this split's state to part[head][split][hd+2] and let the last CTA
-// of the kv head merge all splits (counter self-resets to 0).
+// After attn_core: with one active split, write the normalised output;
+// otherwise publish this split's state to part[head][split][hd+2] and let the
+// last CTA of the kv head merge the n_active splits (the counter resets itself
+// to 0).  cwt is shared scratch of G*(n_active+1) floats for the merge weights.
 __device__ __forceinline__ void attn_finish(const float* res, int G, int hd, int g, int split,
-                                            int n_splits, float* __restrict__ part,
+                                            int n_active, int n_splits_alloc,
+                                            float* __restrict__ part,
                                             unsigned* __restrict__ counters,
-                                            float* __restrict__ out) {
+                                            float* __restrict__ out, float* cwt) {
     const int W = hd + 2;
-    if (n_splits == 1) {
+    if (n_active == 1) {
         for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
             int gi = i / hd, d = i - gi * hd;
             out[(size_t)(g * G + gi) * hd + d] = res[gi * W + d] * (1.0f / res[gi * W + hd + 1]);
@@ -137,41 +187,49 @@ __device__ __forceinline__ void attn_finish(const float* res, int G, int hd, int
     }
     for (int i = threadIdx.x; i < G * W; i += blockDim.x) {
         int gi = i / W, d = i - gi * W;
-        part[((size_t)(g * G + gi) * n_splits + split) * W + d] = res[i];
+        part[((size_t)(g * G + gi) * n_splits_alloc + split) * W + d] = res[i];
     }
     __threadfence();
     __syncthreads();
     __shared__ int s_last;
-    if (threadIdx.x == 0) s_last = (atomicAdd(&counters[g], 1u) == (unsigned)n_splits - 1);
+    if (threadIdx.x == 0) s_last = (atomicAdd(&counters[g], 1u) == (unsigned)n_active - 1);
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // merge weights c_s = exp(M_s - M) and 1/L per head, one warp per head
+    for (int gi = warp; gi < G; gi += (blockDim.x >> 5)) {
+        const float* ph = part + (size_t)(g * G + gi) * n_splits_alloc * W;
+        float M = REF_NEG_INF;
+        for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(ph + (size_t)s * W + hd));
+        M = warp_max(M);
+        float L = 0.f;
+        for (int s = lane; s < n_active; s += 32) {
+            float c = expf(__ldcg(ph + (size_t)s * W + hd) - M);
+            cwt[gi * (n_active + 1) + s] = c;
+            L += __ldcg(ph + (size_t)s * W + hd + 1) * c;
+        }
+        L = warp_sum(L);
+        if (lane == 0) cwt[gi * (n_active + 1) + n_active] = 1.0f / L;
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
         int gi = i / hd, d = i - gi * hd;
-        const float* ph = part + (size_t)(g * G + gi) * n_splits * W;
-        float M = REF_NEG_INF;
-        for (int s = 0; s < n_splits; s++) M = fmaxf(M, __ldcg(ph + (size_t)s * W + hd));
-        float L = 0.f, A = 0.f;
-        for (int s = 0; s < n_splits; s++) {
-            float c = expf(__ldcg(ph + (size_t)s * W + hd) - M);
-            L += __ldcg(ph + (size_t)s * W + hd + 1) * c;
-            A += __ldcg(ph + (size_t)s * W + d) * c;
+        const float* ph = part + (size_t)(g * G + gi) * n_splits_alloc * W + d;
+        const float* c = cwt + gi * (n_active + 1);
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int s = 0;
+        for (; s + 3 < n_active; s += 4) {
+            a0 = fmaf(__ldcg(ph + (size_t)(s + 0) * W), c[s + 0], a0);
+            a1 = fmaf(__ldcg(ph + (size_t)(s + 1) * W), c[s + 1], a1);
+            a2 = fmaf(__ldcg(ph + (size_t)(s + 2) * W), c[s + 2], a2);
+            a3 = fmaf(__ldcg(ph + (size_t)(s + 3) * W), c[s + 3], a3);
         }
-        out[(size_t)(g * G + gi) * hd + d] = A * (1.0f / L);
+        for (; s < n_active; s++) a0 = fmaf(__ldcg(ph + (size_t)s * W), c[s], a0);
+        out[(size_t)(g * G + gi) * hd + d] = ((a0 + a1) + (a2 + a3)) * c[n_active];
     }
     __syncthreads();
     if (threadIdx.x == 0) counters[g] = 0;
-}
-
-// Key range of split `split` out of n_splits over the (windowed) prefix
-// [j0, seq): j0 = seq - window for a sliding-window layer.
-__device__ __forceinline__ void attn_range(int seq, int window, int split, int n_splits, int* jlo,
-                                           int* jhi) {
-    int j0 = (window > 0 && seq > window) ? seq - window : 0;
-    int span = seq - j0;
-    int per = (span + n_splits - 1) / n_splits;
-    *jlo = min(seq, j0 + split * per);
-    *jhi = min(seq, *jlo + per);
 }
 
 }  // namespace cw

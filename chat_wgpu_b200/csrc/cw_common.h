@@ -82,6 +82,9 @@ struct cw_ctx {
     std::vector<std::pair<size_t, uint64_t>> arena;
     size_t cursor = 0;
 
+    // launch model kernels with programmatic dependent launch (PDL)
+    bool pdl = true;
+
     // profiler (context.rs:53-56, profile.rs)
     bool profiling = false;
     std::vector<cw::ProfRec> prof;

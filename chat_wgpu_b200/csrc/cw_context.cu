@@ -249,6 +249,12 @@ int cw_ctx_device(cw_ctx* ctx, int* device) {
     return CW_OK;
 }
 
+int cw_ctx_set_pdl(cw_ctx* ctx, int on) {
+    CW_CHECK(ctx, CW_ERR_INVALID_ARG, "cw_ctx_set_pdl: ctx is NULL");
+    ctx->pdl = on != 0;
+    return CW_OK;
+}
+
 int cw_ctx_stream(cw_ctx* ctx, void** stream) {
     CW_CHECK(ctx && stream, CW_ERR_INVALID_ARG, "cw_ctx_stream: bad arguments");
     *stream = (void*)ctx->stream;

@@ -68,6 +68,30 @@ __device__ __forceinline__ unsigned short ldg_u16(const void* p) {
     return r;
 }
 
+// ---- programmatic dependent launch (PDL) -----------------------------------
+// A kernel launched with programmatic stream serialisation may start before
+// its predecessor finishes; pdl_wait() blocks until the predecessor grid has
+// completed and its writes are visible, pdl_trigger() lets the successor
+// start launching.  Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Hint the bytes [lo, hi) of a read-only buffer into L2 with bulk prefetches
+// issued by the calling thread.  lo is rounded down and hi up to 16 bytes;
+// callers pass ranges inside allocations that are 256-byte aligned and
+// padded, so the rounded range stays inside the allocation.
+__device__ __forceinline__ void prefetch_l2(const void* lo, const void* hi) {
+    uintptr_t a = reinterpret_cast<uintptr_t>(lo) & ~uintptr_t(15);
+    uintptr_t b = (reinterpret_cast<uintptr_t>(hi) + 15) & ~uintptr_t(15);
+    while (a < b) {
+        uint32_t n = (b - a) > (1u << 20) ? (1u << 20) : (uint32_t)(b - a);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
+        a += n;
+    }
+}
+
 // Weight layouts understood by the GEMV core.
 enum Q4Layout : int {
     // GGUF Q4_0 repacked into planes: nibble payload [rows][nb][16] (byte j:

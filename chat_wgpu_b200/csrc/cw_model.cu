@@ -24,6 +24,7 @@
 #include <cmath>
 #include <memory>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "cw_attn.cuh"
@@ -130,6 +131,16 @@ __global__ void __launch_bounds__(256) k_fgemv(FArgs a) {
     const int nb = a.K / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     Q24 s = q24_carve(smem, nb);
+    const long groups = ((long)a.N + 8 * R - 1) / (8 * R);
+    pdl_trigger();
+    if (threadIdx.x == 0) {  // this CTA's weight rows do not depend on the predecessor
+        for (long g = blockIdx.x; g < groups; g += gridDim.x) {
+            long r0 = g * 8 * R, r1 = min((long)a.N, r0 + 8 * R);
+            prefetch_l2(a.payload + (size_t)r0 * nb * 16, a.payload + (size_t)r1 * nb * 16);
+            prefetch_l2(a.scales + (size_t)r0 * nb, a.scales + (size_t)r1 * nb);
+        }
+    }
+    pdl_wait();
     if (PRO == PRO_X) {
         q24_prepare<LAYOUT_GGUF>(s, a.x);
     } else {
@@ -172,7 +183,6 @@ __global__ void __launch_bounds__(256) k_fgemv(FArgs a) {
     __syncthreads();
 
     unsigned long long best = argmax_key_init();
-    const long groups = ((long)a.N + 8 * R - 1) / (8 * R);
     for (long g = blockIdx.x; g < groups; g += gridDim.x) {
         long row0 = (g * 8 + warp) * R;
         if (row0 >= a.N) continue;
@@ -252,11 +262,27 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
     const int G = a.n_heads / a.n_kv, hd = a.hd;
     const int g = blockIdx.y, split = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = a.st->pos, seq = pos + 1;
+    pdl_trigger();
+    const int pos = a.st->pos, seq = pos + 1;  // written only by the previous step
+    const int n_active = attn_active_splits(attn_span(seq, a.window), a.n_splits);
+    if (split >= n_active) {
+        pdl_wait();
+        return;
+    }
     int jlo, jhi;
-    attn_range(seq, a.window, split, a.n_splits, &jlo, &jhi);
+    attn_range(seq, a.window, split, n_active, &jlo, &jhi);
     const bool holds = pos >= jlo && pos < jhi;
-    float* qs = sm + attn_smem_floats(G, hd);  // [G][hd]
+    if (threadIdx.x == 0) {  // cached rows [jlo, min(jhi, pos)) were written by earlier steps
+        int j1 = min(jhi, pos);
+        if (j1 > jlo) {
+            const float* kb0 = a.kc + ((size_t)g * a.max_seq) * hd;
+            const float* vb0 = a.vc + ((size_t)g * a.max_seq) * hd;
+            prefetch_l2(kb0 + (size_t)jlo * hd, kb0 + (size_t)j1 * hd);
+            prefetch_l2(vb0 + (size_t)jlo * hd, vb0 + (size_t)j1 * hd);
+        }
+    }
+    pdl_wait();
+    float* qs = sm + attn_smem_floats(G, hd, a.n_splits);  // [G][hd]
     float* ks = qs + (size_t)G * hd;           // [hd]
     const int qd = a.n_heads * hd, kvd = a.n_kv * hd;
     const int nrows = G + (holds ? 1 : 0);
@@ -313,8 +339,9 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
     }
     __syncthreads();
     float* res = sm + 4 * G * (hd + 2);
+    float* cwt = sm + 5 * G * (hd + 2);
     attn_core<EPL, GMAX, false>(qs, G, hd, kbase, vbase, hd, jlo, jhi, a.scale, a.softcap, sm, res);
-    attn_finish(res, G, hd, g, split, a.n_splits, a.part, a.counters, a.out);
+    attn_finish(res, G, hd, g, split, n_active, a.n_splits, a.part, a.counters, a.out, cwt);
 }
 
 // ---- embed / finalize ------------------------------------------------------
@@ -322,6 +349,8 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
 __global__ void k_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
                         int dim, float scale, const DevState* __restrict__ st,
                         float* __restrict__ hidden) {
+    pdl_trigger();
+    pdl_wait();
     const int nb = dim / 32;
     const unsigned tok = st->token;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -339,6 +368,8 @@ __global__ void k_embed(const uint8_t* __restrict__ payload, const __half* __res
 // lasts, else the argmax, which is also appended to the output.
 __global__ void k_finalize(DevState* st, const unsigned* __restrict__ prompt,
                            unsigned* __restrict__ toks, int decode) {
+    pdl_trigger();
+    pdl_wait();
     int pos = st->pos;
     unsigned next;
     if (pos + 1 < st->n_prompt) {
@@ -365,6 +396,26 @@ __global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n
 // ===========================================================================
 // host side
 // ===========================================================================
+// Kernel launch on the context stream; with ctx->pdl the launch carries
+// programmatic stream serialisation so it may overlap its predecessor up to
+// the kernel's pdl_wait().
+template <typename... KArgs, typename... Args>
+static int launch_k(cw_ctx* ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                    Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ctx->pdl ? 1 : 0;
+    CW_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+    return CW_OK;
+}
+
 template <int PRO, int EPI, int R>
 static int launch_fgemv(cw_ctx* ctx, const FArgs& a) {
     size_t smem = fgemv_smem(PRO, a.K);
@@ -379,7 +430,7 @@ static int launch_fgemv(cw_ctx* ctx, const FArgs& a) {
     per_sm = std::max(per_sm, 1);
     long groups = ((long)a.N + 8 * R - 1) / (8 * R);
     long grid = std::min<long>(groups, (long)ctx->sm_count * per_sm);
-    kern<<<(unsigned)grid, 256, smem, ctx->stream>>>(a);
+    CW_TRY(launch_k(ctx, kern, dim3((unsigned)grid), dim3(256), smem, a));
     return check_launch("fused gemv");
 }
 
@@ -408,7 +459,7 @@ static int fattn_go(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
     if (smem > 48 * 1024)
         CW_CUDA(cudaFuncSetAttribute(k_fattn<EPL, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem));
-    k_fattn<EPL, GM><<<grid, 128, smem, ctx->stream>>>(a);
+    CW_TRY(launch_k(ctx, k_fattn<EPL, GM>, grid, dim3(128), smem, a));
     return CW_OK;
 }
 
@@ -424,14 +475,14 @@ static int launch_fattn_e(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
     return check_launch("fused attention");
 }
 
-static size_t fattn_smem(int G, int hd) {
-    return (attn_smem_floats(G, hd) + (size_t)G * hd + hd) * sizeof(float);
+static size_t fattn_smem(int G, int hd, int n_splits) {
+    return (attn_smem_floats(G, hd, n_splits) + (size_t)G * hd + hd) * sizeof(float);
 }
 
 static int launch_fattn(cw_ctx* ctx, const AArgs& a) {
     dim3 grid(a.n_splits, a.n_kv);
     int G = a.n_heads / a.n_kv;
-    size_t smem = fattn_smem(G, a.hd);
+    size_t smem = fattn_smem(G, a.hd, a.n_splits);
     int epl = (a.hd + 31) / 32;
     if (epl <= 1) return launch_fattn_e<1>(ctx, a, grid, smem);
     if (epl <= 2) return launch_fattn_e<2>(ctx, a, grid, smem);
@@ -697,8 +748,8 @@ static int enqueue_step(cw_session* s, bool decode) {
         if (ctx->profiling) sc.reset(new OpScope(ctx, name));
     };
     stage("embed");
-    k_embed<<<1, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, I.dim, I.embed_scale,
-                                        s->st, s->hidden);
+    CW_TRY(launch_k(ctx, k_embed, dim3(1), dim3(256), 0, m->embed.payload, m->embed.scales,
+                    (int)I.dim, I.embed_scale, (const DevState*)s->st, s->hidden));
     CW_TRY(check_launch("embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         stage("attn_in");
@@ -811,7 +862,8 @@ static int enqueue_step(cw_session* s, bool decode) {
         CW_TRY((fgemv<PRO_NORM, EPI_HEAD>(ctx, h)));
     }
     stage("finalize");
-    k_finalize<<<1, 1, 0, ctx->stream>>>(s->st, s->prompt, s->toks, decode ? 1 : 0);
+    CW_TRY(launch_k(ctx, k_finalize, dim3(1), dim3(1), 0, s->st, (const unsigned*)s->prompt,
+                    s->toks, decode ? 1 : 0));
     sc.reset();
     return check_launch("finalize");
 }

@@ -90,12 +90,15 @@ __global__ void __launch_bounds__(128) k_attention(
     extern __shared__ float sm[];
     const int G = n_heads / n_kv;
     const int g = blockIdx.y, split = blockIdx.x;
+    const int n_active = attn_active_splits(attn_span(seq, window), n_splits);
+    if (split >= n_active) return;
     int jlo, jhi;
-    attn_range(seq, window, split, n_splits, &jlo, &jhi);
+    attn_range(seq, window, split, n_active, &jlo, &jhi);
     float* res = sm + 4 * G * (hd + 2);
+    float* cwt = sm + 5 * G * (hd + 2);
     attn_core<EPL, GMAX>(q + (size_t)g * G * hd, G, hd, k + g * head_stride, v + g * head_stride,
                          row_stride, jlo, jhi, scale, softcap, sm, res);
-    attn_finish(res, G, hd, g, split, n_splits, part, counters, out);
+    attn_finish(res, G, hd, g, split, n_active, n_splits, part, counters, out, cwt);
 }
 
 template <int EPL>
@@ -104,9 +107,15 @@ static int attn_dispatch_g(int G, dim3 grid, size_t smem, cudaStream_t st, const
                            int seq, int hd, float scale, float softcap, int window, long hs, long rs,
                            int n_splits, float* part, unsigned* counters) {
 #define CW_ATTN_LAUNCH(GM)                                                                     \
-    k_attention<EPL, GM><<<grid, 128, smem, st>>>(q, k, v, out, n_heads, n_kv, seq, hd, scale, \
-                                                  softcap, window, hs, rs, n_splits, part,     \
-                                                  counters)
+    do {                                                                                       \
+        if (smem > 48 * 1024)                                                                  \
+            CW_CUDA(cudaFuncSetAttribute(k_attention<EPL, GM>,                                 \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,          \
+                                         (int)smem));                                          \
+        k_attention<EPL, GM><<<grid, 128, smem, st>>>(q, k, v, out, n_heads, n_kv, seq, hd,    \
+                                                      scale, softcap, window, hs, rs,          \
+                                                      n_splits, part, counters);               \
+    } while (0)
     if (G <= 1) CW_ATTN_LAUNCH(1);
     else if (G <= 2) CW_ATTN_LAUNCH(2);
     else if (G <= 4) CW_ATTN_LAUNCH(4);
@@ -116,9 +125,8 @@ static int attn_dispatch_g(int G, dim3 grid, size_t smem, cudaStream_t st, const
 }
 
 int attention_splits(cw_ctx* ctx, int span, int n_kv) {
-    int by_len = std::max(1, (span + 31) / 32);
     int by_sm = std::max(1, 2 * ctx->sm_count / std::max(1, n_kv));
-    return std::max(1, std::min(by_len, by_sm));
+    return attn_active_splits(span, by_sm);
 }
 
 int launch_attention(cw_ctx* ctx, const float* q, const float* k, const float* v, float* out,
@@ -126,7 +134,7 @@ int launch_attention(cw_ctx* ctx, const float* q, const float* k, const float* v
                      long head_stride, long row_stride, int n_splits, float* part) {
     const int G = n_heads / n_kv;
     const float scale = powf((float)hd, -0.5f);  // attention.rs:18
-    size_t smem = attn_smem_floats(G, hd) * sizeof(float);
+    size_t smem = attn_smem_floats(G, hd, n_splits) * sizeof(float);
     CW_TRY(ensure_counters(ctx, (size_t)n_kv));
     dim3 grid(n_splits, n_kv);
     int epl = (hd + 31) / 32;

@@ -1,6 +1,8 @@
 // cw_q4.cu -- Q4 GEMV entry points (chat-wgpu src/kernels/q4.rs), the GGUF
 // Q4_0 pack/dequant kernels and the on-device re-quantiser.
 #include <algorithm>
+#include <map>
+#include <vector>
 
 #include "cw_common.h"
 #include "cw_device.cuh"
@@ -46,14 +48,24 @@ static int launch_gemv_r(cw_ctx* ctx, const float* x, const void* payload, const
                          int K, long N, float* y) {
     size_t smem = q24_bytes(K / 32);
     auto kern = k_q4_gemv<LAYOUT, R>;
-    if (smem > 48 * 1024) {
-        CW_CHECK((int)smem <= ctx->max_smem_optin, CW_ERR_UNSUPPORTED,
-                 "q4 gemv: in_f=%d needs %zu bytes of shared memory", K, smem);
-        CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    }
+    // occupancy per (device, smem size) of this instantiation, queried once
+    static thread_local std::map<std::pair<int, size_t>, int> occ;
+    auto key = std::make_pair(ctx->device, smem);
+    auto it = occ.find(key);
     int per_sm = 0;
-    CW_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem));
-    per_sm = std::max(per_sm, 1);
+    if (it == occ.end()) {
+        if (smem > 48 * 1024) {
+            CW_CHECK((int)smem <= ctx->max_smem_optin, CW_ERR_UNSUPPORTED,
+                     "q4 gemv: in_f=%d needs %zu bytes of shared memory", K, smem);
+            CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+        }
+        CW_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem));
+        per_sm = std::max(per_sm, 1);
+        occ[key] = per_sm;
+    } else {
+        per_sm = it->second;
+    }
     long groups = (N + 8 * R - 1) / (8 * R);
     long grid = std::min<long>(groups, (long)ctx->sm_count * per_sm);
     kern<<<(unsigned)grid, 256, smem, ctx->stream>>>(x, (const uint8_t*)payload, scales, K, N, y);
@@ -258,6 +270,66 @@ int cw_q4_0_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_
     return launch_q4_gemv<LAYOUT_GGUF>(ctx, (const float*)ex->ptr, ew->ptr,
                                        (const char*)ew->ptr + ew->scale_off, (int)in_f,
                                        (long)out_f, (float*)ey->ptr);
+}
+
+int cw_q4_0_gemv_bench(cw_ctx* ctx, cw_buf x, const cw_buf* ws, size_t n_w, size_t in_f,
+                       size_t out_f, size_t iters, double* us_per_launch) {
+    clear_error();
+    CW_CHECK(ctx && ws && n_w > 0 && iters > 0 && us_per_launch, CW_ERR_INVALID_ARG,
+             "cw_q4_0_gemv_bench: bad arguments");
+    CW_CHECK(in_f % 32 == 0 && in_f > 0 && out_f > 0 && out_f < (1ull << 31), CW_ERR_INVALID_ARG,
+             "cw_q4_0_gemv_bench: bad shape [%zu, %zu]", out_f, in_f);
+    BufEntry *ex, *ey;
+    CW_TRY(buf_get(ctx, x, &ex, in_f * 4, "cw_q4_0_gemv_bench(x)"));
+    std::vector<BufEntry*> we(n_w);
+    for (size_t i = 0; i < n_w; i++)
+        CW_TRY(q4_0_weight(ctx, ws[i], out_f, in_f, &we[i], "cw_q4_0_gemv_bench(w)"));
+    cudaSetDevice(ctx->device);
+    cw_buf y;
+    CW_TRY(arena_get(ctx, out_f, &y, &ey));
+    // one untimed pass over every weight (attributes, first-touch)
+    for (size_t i = 0; i < n_w; i++)
+        CW_TRY(launch_q4_gemv<LAYOUT_GGUF>(ctx, (const float*)ex->ptr, we[i]->ptr,
+                                           (const char*)we[i]->ptr + we[i]->scale_off, (int)in_f,
+                                           (long)out_f, (float*)ey->ptr));
+    // the launches are replayed as one CUDA graph so host launch overhead
+    // does not starve the device between short kernels
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    CW_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = CW_OK;
+    for (size_t it = 0; it < iters && rc == CW_OK; it++) {
+        BufEntry* w = we[it % n_w];
+        rc = launch_q4_gemv<LAYOUT_GGUF>(ctx, (const float*)ex->ptr, w->ptr,
+                                         (const char*)w->ptr + w->scale_off, (int)in_f,
+                                         (long)out_f, (float*)ey->ptr);
+    }
+    cudaError_t ce = cudaStreamEndCapture(ctx->stream, &graph);
+    if (rc != CW_OK) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (ce != cudaSuccess) return set_error(CW_ERR_CUDA, "bench capture: %s", cudaGetErrorString(ce));
+    ce = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ce != cudaSuccess)
+        return set_error(CW_ERR_CUDA, "bench instantiate: %s", cudaGetErrorString(ce));
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaGraphLaunch(exec, ctx->stream);  // warm
+    cudaEventRecord(e0, ctx->stream);
+    cudaGraphLaunch(exec, ctx->stream);
+    cudaEventRecord(e1, ctx->stream);
+    ce = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaGraphExecDestroy(exec);
+    if (ce != cudaSuccess) return set_error(CW_ERR_CUDA, "bench: %s", cudaGetErrorString(ce));
+    *us_per_launch = (double)ms * 1000.0 / (double)iters;
+    return CW_OK;
 }
 
 int cw_q4_0_dequant(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out) {

@@ -1,0 +1,72 @@
+"""Q4_0 GEMV microbenchmark -- the B200 counterpart of chat-wgpu's
+examples/q4bench.rs: µs per launch and achieved HBM GB/s per projection
+shape, kernel only (no model).
+
+Each shape cycles through enough distinct weight copies (> 4x the L2 size)
+that every launch streams its weight from HBM; the launches are replayed as
+one CUDA graph and timed with CUDA events (cw_q4_0_gemv_bench).
+
+    python -m chat_wgpu_b200.q4bench            # BASELINE shape sweep
+    python -m chat_wgpu_b200.q4bench --json
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+
+import numpy as np
+
+from . import _lib
+from .context import GpuContext
+from .gguf import random_q4_0_blocks
+from .kernels import q4
+
+# (in_f, out_f): Qwen3 0.6B/1.7B/4B/8B projections and LM heads
+SHAPES = [(1024, 2048), (1024, 3072), (3072, 1024), (2048, 6144), (6144, 2048), (2560, 9728),
+          (9728, 2560), (4096, 12288), (12288, 4096), (1024, 151936), (2048, 151936),
+          (2560, 151936), (4096, 151936)]
+
+
+def algorithmic_bytes(in_f: int, out_f: int) -> int:
+    """N*K/32*18 (Q4_0 blocks) + 4K (x) + 4N (y)."""
+    return out_f * (in_f // 32) * 18 + 4 * in_f + 4 * out_f
+
+
+def bench_shape(ctx: GpuContext, in_f: int, out_f: int, iters: int = 200, seed: int = 0,
+                l2_bytes: int = 126 << 20) -> dict:
+    rng = np.random.default_rng(seed)
+    wbytes = out_f * (in_f // 32) * 18
+    n_w = max(2, min(64, -(-4 * l2_bytes // wbytes)))
+    blocks = random_q4_0_blocks(rng, out_f, in_f)
+    ws = [q4.q4_0_upload(ctx, blocks, out_f, in_f) for _ in range(n_w)]
+    x = ctx.storage(rng.normal(0, 1, in_f).astype(np.float32))
+    arr = (C.c_uint64 * n_w)(*[w.handle for w in ws])
+    us = C.c_double()
+    iters = max(iters, n_w)
+    _lib.call("cw_q4_0_gemv_bench", ctx.handle, x.handle, arr, n_w, in_f, out_f, iters, C.byref(us))
+    for w in ws:
+        w.release()
+    nbytes = algorithmic_bytes(in_f, out_f)
+    return {"in_f": in_f, "out_f": out_f, "us": us.value, "bytes": nbytes,
+            "gbs": nbytes / (us.value * 1e-6) / 1e9, "copies": n_w}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--json", action="store_true")
+    ap.add_argument("--iters", type=int, default=200)
+    args = ap.parse_args()
+    ctx = GpuContext(0)
+    rows = [bench_shape(ctx, k, n, args.iters) for k, n in SHAPES]
+    if args.json:
+        print(json.dumps(rows))
+    else:
+        print(f"{'shape (in->out)':<18} {'us/pass':>9} {'GB/s':>9} {'bytes':>11}")
+        for r in rows:
+            print(f"{r['in_f']:>6}->{r['out_f']:<10} {r['us']:>9.2f} {r['gbs']:>9.1f} {r['bytes']:>11}")
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -72,6 +72,9 @@ int cw_ctx_backend(cw_ctx* ctx, char* buf, size_t cap);
 /* Device index and the cudaStream_t (as void*) the context enqueues on. */
 int cw_ctx_device(cw_ctx* ctx, int* device);
 int cw_ctx_stream(cw_ctx* ctx, void** stream);
+/* Launch the decode kernels with programmatic dependent launch (default 1);
+ * takes effect for CUDA graphs built afterwards.  No reference counterpart. */
+int cw_ctx_set_pdl(cw_ctx* ctx, int on);
 
 /* ---- buffers ------------------------------------------------------------- */
 /* GpuContext::storage (context.rs:177-184): upload f32s to a new buffer. */
@@ -168,6 +171,13 @@ int cw_q4_0_pack(cw_ctx* ctx, cw_buf gguf_blocks, size_t rows, size_t in_f, cw_b
 int cw_q4_0_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out);
 /* Exact f32 dequantisation of a packed weight (dequant.rs:62-78). */
 int cw_q4_0_dequant(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out);
+/* The microbenchmark of examples/q4bench.rs for the packed GEMV: `iters`
+ * back-to-back launches cycling through the n_w distinct weights ws[] (all
+ * [out_f, in_f]; pass enough copies that a weight is evicted from L2 before
+ * it comes round again), timed with CUDA events on the context stream.
+ * *us_per_launch = device time / iters. */
+int cw_q4_0_gemv_bench(cw_ctx* ctx, cw_buf x, const cw_buf* ws, size_t n_w, size_t in_f,
+                       size_t out_f, size_t iters, double* us_per_launch);
 
 /* ---- model: src/model/{mod,qwen3,layers,cache}.rs --------------------------------------------- */
 typedef struct {

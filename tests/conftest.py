@@ -40,10 +40,17 @@ def tiny_gguf(tmp_path_factory):
 
 
 def rel_err(got, ref):
-    """Max |got-ref| / max(|ref|, 1e-3*rms(ref)) -- the north-star's 1e-3
-    relative gate with a floor for near-zero references."""
+    """Max |got-ref| / max(|ref|, 0.1*rms(ref)).
+
+    The north-star gate is 1e-3 relative.  Outputs that sit near zero (a dot
+    product whose terms cancel) cannot be held to a pure relative bound by
+    any two f32 implementations that sum in different orders: the rounding
+    noise of a K-term f32 sum is ~sqrt(K)*2^-24 of the typical output, i.e.
+    ~5e-6*rms at K = 6144.  The floor 0.1*rms(ref) therefore allows near-zero
+    outputs an absolute error of 1e-4*rms -- twenty times that noise, and
+    two orders of magnitude below what a wrong row, block or scale produces."""
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     rms = float(np.sqrt(np.mean(ref * ref))) if ref.size else 0.0
-    den = np.maximum(np.abs(ref), max(1e-3 * rms, 1e-30))
+    den = np.maximum(np.abs(ref), max(0.1 * rms, 1e-30))
     return float(np.max(np.abs(got - ref) / den)) if ref.size else 0.0
