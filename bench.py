@@ -52,7 +52,8 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-steps", type=int, default=8)
+    ap.add_argument("--profile-steps", type=int, default=8,
+                    help="decode steps of the per-kernel profile pass (at least 1)")
     return ap.parse_args()
 
 
@@ -303,12 +304,8 @@ def run_cuda(args, dist):
     mean_pos = 0.5 * (pos_lo + pos_hi)
     _, launches_decode = s.launches()
 
-    # ---- per-kernel profile pass (direct launches, CUDA events per kernel)
-    s.set_graph(False)
-    ctx.begin_profile()
-    s.run(args.profile_steps)
-    ctx.sync()
-    prof = ctx.report_profile()
+    # ---- per-kernel profile: the step as a graph with an event pair per kernel
+    prof = s.profile(max(1, args.profile_steps))
     s.close()
 
     # ---- e2e: public per-token API with host round trips

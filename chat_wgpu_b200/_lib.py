@@ -110,6 +110,7 @@ SIGNATURES = {
     "cw_session_step": [_vp, C.c_uint32, C.POINTER(C.c_uint32)],
     "cw_session_run_timed": [_vp, _sz, C.POINTER(C.c_double)],
     "cw_session_launches": [_vp, C.POINTER(_sz), C.POINTER(_sz)],
+    "cw_session_profile": [_vp, _sz, C.POINTER(ProfileRow), _sz, C.POINTER(_sz)],
     "cw_generate": [_vp, _vp, _sz, _sz, _vp],
 }
 _RESTYPE = {"cw_last_error": C.c_char_p}

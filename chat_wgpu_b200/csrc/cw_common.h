@@ -73,6 +73,7 @@ struct cw_ctx {
     cudaStream_t stream = nullptr;
     int sm_count = 0;
     int max_smem_optin = 0;
+    int smem_per_sm = 0;
     size_t l2_bytes = 0;
     std::string backend;
 

@@ -199,6 +199,7 @@ int cw_ctx_create(int device, cw_ctx** out) {
     c->sm_count = prop.multiProcessorCount;
     c->l2_bytes = prop.l2CacheSize;
     c->max_smem_optin = (int)prop.sharedMemPerBlockOptin;
+    c->smem_per_sm = (int)prop.sharedMemPerMultiprocessor;
     char b[320];
     snprintf(b, sizeof b, "CUDA sm_%d%da (%s)", prop.major, prop.minor, prop.name);
     c->backend = b;

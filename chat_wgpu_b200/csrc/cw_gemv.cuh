@@ -1,0 +1,398 @@
+// cw_gemv.cuh -- the streaming Q4 GEMV: y[N] = W[N,K] x for Q4 weights,
+// shared by the stand-alone op entry points and the fused decode kernels.
+//
+// Data movement (B200): weight rows are contiguous in both planes (16-byte
+// nibble payloads, then f16/f32 scales), so a CTA streams "chunks" of RC
+// consecutive rows with two cp.async.bulk copies per chunk into a ring of S
+// shared-memory stages, completion tracked by one mbarrier per stage.  One
+// elected thread issues the copies; the first S chunks are issued before
+// griddepcontrol.wait, i.e. while the previous kernel of the decode step is
+// still running.  A chunk is 8-16 KB, so each SM keeps up to ~140 KB of
+// weights in flight with two CTAs resident.
+//
+// Arithmetic: x is converted once per CTA to q24 block-floating-point planes
+// (cw_device.cuh) and each lane keeps the planes of its BPL blocks in
+// registers for the whole kernel; a weight block then costs one shared-memory
+// load, 12 bit ops, 24 dp4a and a few flops.
+//
+// Work mapping: 8 warps; WPR warps share a row (lanes over its blocks,
+// block b = (warp % WPR)*32 + lane + k*32*WPR, k < BPL), 8/WPR row slots per
+// chunk, RPW rows per slot: RC = (8/WPR)*RPW rows per chunk.  Per-row sums go
+// through shared memory and are added in a fixed order, so results are
+// bit-reproducible run to run.
+//
+// Waits are bounded by %globaltimer: a wait that exceeds the limit records
+// DEV_TIMEOUT in the status word, waits (bounded) for the copies in flight
+// and ends the kernel; the host reports CW_ERR_TIMEOUT.
+#pragma once
+
+#include <stdint.h>
+
+#include "cw_common.h"
+#include "cw_device.cuh"
+
+namespace cw {
+
+enum { PRO_X = 0, PRO_NORM = 1 };
+enum { EPI_STORE = 0, EPI_RESID = 1, EPI_GLU = 2, EPI_HEAD = 3 };
+
+struct GemvArgs {
+    const uint8_t* payload;  // [N][K/32][16]
+    const void* scales;      // [N][K/32] f16 (GGUF) or f32 (crate layout)
+    int K, N;
+    // PRO_X: x [K] from global memory
+    const float* x;
+    // PRO_NORM: h = base (+ delta, post-normed with post_w when non-null);
+    // x = rmsnorm(h) * gain(norm_w); h written to h_out and x to xn_out by CTA 0
+    const float* base;
+    const float* delta;
+    const float* post_w;
+    float* h_out;
+    const float* norm_w;
+    float* xn_out;
+    float eps;
+    int unit;  // UnitShift gain (1 + w)
+    // epilogue
+    float* y;
+    const float* bias;              // EPI_STORE: optional per-row bias
+    int geglu;                      // EPI_GLU: 0 SwiGLU, 1 GeGLU (rows 2i = gate_i, 2i+1 = up_i)
+    float softcap;                  // EPI_HEAD: tanh soft-cap of the logits (0 = off)
+    unsigned long long* key;        // EPI_HEAD: argmax accumulator (atomicMax)
+    int* status;                    // device status word
+};
+
+template <int WPR_, int BPL_, int RPW_>
+struct GemvCfg {
+    static constexpr int WPR = WPR_, BPL = BPL_, RPW = RPW_;
+    static constexpr int SLOTS = 8 / WPR;
+    static constexpr int RC = SLOTS * RPW;
+    static constexpr int NB_MAX = 32 * WPR * BPL;
+};
+using GemvC32 = GemvCfg<1, 1, 4>;   // K <= 1024:  32 rows per chunk
+using GemvC64 = GemvCfg<1, 2, 2>;   // K <= 2048:  16 rows
+using GemvC96 = GemvCfg<1, 3, 1>;   // K <= 3072:   8 rows
+using GemvC192 = GemvCfg<2, 3, 1>;  // K <= 6144:   4 rows
+using GemvC384 = GemvCfg<4, 3, 1>;  // K <= 12288:  2 rows
+using GemvC768 = GemvCfg<8, 3, 1>;  // K <= 24576:  1 row
+
+constexpr uint64_t GEMV_WAIT_NS = 2000000000ull;  // 2 s
+
+// ---- mbarrier / bulk-copy helpers ----------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait for the phase with `parity` to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_ns() - t0 > limit_ns) return false;
+    return true;
+}
+// Global -> this CTA's shared memory, completion counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__host__ __device__ constexpr size_t al128(size_t v) { return (v + 127) / 128 * 128; }
+__host__ __device__ constexpr size_t al16(size_t v) { return (v + 15) / 16 * 16; }
+
+// Shared-memory layout sizes (bytes).
+struct GemvSmem {
+    size_t pay, sc, stage, q24, hbuf, red, total;
+    __host__ __device__ GemvSmem(int RC, int WPR, int nb, int sw, int S, int K, bool norm) {
+        pay = al128((size_t)RC * nb * 16);
+        sc = al128((size_t)RC * nb * sw);
+        stage = pay + sc;
+        q24 = al16(q24_bytes(nb));
+        hbuf = norm ? al16((size_t)K * 4) : 0;
+        red = al16((size_t)2 * RC * WPR * 4);
+        total = 128 + (size_t)S * stage + q24 + hbuf + red;
+    }
+};
+
+__device__ __forceinline__ float gemv_cta_sum(float v, float* red8) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red8[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) t += red8[i];
+    return t;
+}
+
+__device__ __forceinline__ float silu_ref_f(float x) { return x / (1.0f + expf(-x)); }  // glu.wgsl:25
+__device__ __forceinline__ float gelu_ref_f(float x) {                                 // glu.wgsl:27-30
+    const float c = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+}
+
+// x -> q24 planes in shared memory (PRO_X: x from global; PRO_NORM: the
+// rmsnorm prologue of the decode kernels, norm.wgsl:20-56).
+template <int LAYOUT, int PRO>
+__device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, float* hbuf,
+                                              float* red8) {
+    const int nb = a.K / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (PRO == PRO_X) {
+        q24_prepare<LAYOUT>(q, a.x);
+        return;
+    }
+    const int K = a.K;
+    float inv_d = 0.f;
+    if (a.delta && a.post_w) {
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(a.delta[i], a.delta[i], ss);
+        ss = gemv_cta_sum(ss, red8);
+        inv_d = 1.0f / sqrtf(ss / (float)K + a.eps);
+    }
+    float ssh = 0.f;
+    const bool wr = a.h_out && blockIdx.x == 0;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        float h = a.base[i];
+        if (a.delta) {
+            float dv = a.delta[i];
+            if (a.post_w) {
+                float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
+                dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
+            }
+            h = h + dv;
+        }
+        hbuf[i] = h;
+        if (wr) a.h_out[i] = h;
+        ssh = fmaf(h, h, ssh);
+    }
+    ssh = gemv_cta_sum(ssh, red8);
+    const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
+    const bool wx = a.xn_out && blockIdx.x == 0;
+    for (int b = warp; b < nb; b += (blockDim.x >> 5)) {
+        const int i = b * 32 + lane;
+        const float gw = a.unit ? 1.0f + a.norm_w[i] : a.norm_w[i];
+        const float v = __fmul_rn(__fmul_rn(hbuf[i], inv), gw);
+        if (wx) a.xn_out[i] = v;
+        q24_block<LAYOUT>(q, b, v, lane);
+    }
+}
+
+template <int LAYOUT, int PRO, int EPI, class CF>
+__global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ float red8[8];
+    constexpr int WPR = CF::WPR, BPL = CF::BPL, RPW = CF::RPW, RC = CF::RC;
+    constexpr int SW = LAYOUT == LAYOUT_GGUF ? 2 : 4;
+    const int nb = a.K / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const long nchunks = ((long)a.N + RC - 1) / RC;
+    const int mycount =
+        blockIdx.x < nchunks ? (int)((nchunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    const GemvSmem L(RC, WPR, nb, SW, S, a.K, PRO == PRO_NORM);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    unsigned char* stages = smem + 128;
+    const Q24 q = q24_carve(stages + (size_t)S * L.stage, nb);
+    float* hbuf = reinterpret_cast<float*>(stages + (size_t)S * L.stage + L.q24);
+    float* red = reinterpret_cast<float*>(stages + (size_t)S * L.stage + L.q24 + L.hbuf);
+
+    auto issue = [&](int i) {  // chunk i of this CTA into stage i % S (thread 0 only)
+        const long c = blockIdx.x + (long)i * gridDim.x;
+        const int s = i % S;
+        const long row0 = c * RC;
+        const int rows = (int)min((long)RC, (long)a.N - row0);
+        const unsigned pb = (unsigned)rows * nb * 16, sb = (unsigned)rows * nb * SW;
+        fence_proxy_async();
+        mbar_expect_tx(&bars[s], pb + sb);
+        bulk_g2s(stages + (size_t)s * L.stage, a.payload + (size_t)row0 * nb * 16, pb, &bars[s]);
+        bulk_g2s(stages + (size_t)s * L.stage + L.pay,
+                 reinterpret_cast<const char*>(a.scales) + (size_t)row0 * nb * SW, sb, &bars[s]);
+    };
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    // weight streaming starts before the dependency on the previous kernel
+    if (tid == 0)
+        for (int i = 0; i < S && i < mycount; i++) issue(i);
+    pdl_trigger();
+    pdl_wait();
+
+    gemv_prologue<LAYOUT, PRO>(a, q, hbuf, red8);
+    __syncthreads();
+    // this lane's activation planes, kept in registers
+    uint4 xa[BPL][3], xb[BPL][3];
+    int cbr[BPL];
+    float sbr[BPL];
+    const int wsub = warp % WPR, slot = warp / WPR;
+#pragma unroll
+    for (int k = 0; k < BPL; k++) {
+        const int b = wsub * 32 + lane + k * 32 * WPR;
+        const bool in = b < nb;
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            xa[k][p] = in ? q.pl[(p * 2 + 0) * nb + b] : make_uint4(0, 0, 0, 0);
+            xb[k][p] = in ? q.pl[(p * 2 + 1) * nb + b] : make_uint4(0, 0, 0, 0);
+        }
+        cbr[k] = in ? q.cb[b] : 0;
+        sbr[k] = in ? q.sb[b] : 0.f;
+    }
+
+    unsigned long long best = argmax_key_init();
+    int failed = 0;
+    for (int i = 0; i < mycount; i++) {
+        const int s = i % S;
+        const unsigned par = (unsigned)((i / S) & 1);
+        const bool ok = mbar_wait(&bars[s], par, GEMV_WAIT_NS);
+        if (__syncthreads_or(!ok)) {
+            failed = i + 1;
+            break;
+        }
+        const unsigned char* pay = stages + (size_t)s * L.stage;
+        const unsigned char* scs = pay + L.pay;
+        const long row0 = (blockIdx.x + (long)i * gridDim.x) * RC;
+        const int rows = (int)min((long)RC, (long)a.N - row0);
+        float* rb = red + (size_t)(i & 1) * RC * WPR;
+#pragma unroll
+        for (int j = 0; j < RPW; j++) {
+            const int r = slot * RPW + j;
+            float acc = 0.f;
+            if (r < rows) {
+#pragma unroll
+                for (int k = 0; k < BPL; k++) {
+                    const int b = wsub * 32 + lane + k * 32 * WPR;
+                    if (b < nb) {
+                        const size_t blk = (size_t)r * nb + b;
+                        const uint4 w4 = reinterpret_cast<const uint4*>(pay)[blk];
+                        const float d =
+                            SW == 2 ? __half2float(reinterpret_cast<const __half*>(scs)[blk])
+                                    : reinterpret_cast<const float*>(scs)[blk];
+                        const unsigned w[4] = {w4.x, w4.y, w4.z, w4.w};
+                        const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
+                        const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
+                        const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
+                        const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
+                        const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
+                        const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
+                        int s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+                        for (int t = 0; t < 4; t++) {
+                            const unsigned lo = w[t] & 0x0f0f0f0fu;
+                            const unsigned hi = (w[t] >> 4) & 0x0f0f0f0fu;
+                            s0 = dp4a_uu(lo, a0[t], s0);
+                            s0 = dp4a_uu(hi, b0[t], s0);
+                            s1 = dp4a_uu(lo, a1[t], s1);
+                            s1 = dp4a_uu(hi, b1[t], s1);
+                            s2 = dp4a_us(lo, a2[t], s2);
+                            s2 = dp4a_us(hi, b2[t], s2);
+                        }
+                        const float T = fmaf((float)s2, 65536.0f, (float)(s0 + (s1 << 8) - cbr[k]));
+                        acc = fmaf(d * sbr[k], T, acc);
+                    }
+                }
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) rb[r * WPR + wsub] = acc;
+        }
+        __syncthreads();  // stage s consumed, row partials complete
+        if (tid == 0 && i + S < mycount) issue(i + S);
+        // epilogue: fixed-order sum of the WPR partials of each row
+        if (EPI == EPI_GLU) {
+            if (tid < RC / 2) {
+                const int r0 = 2 * tid;
+                if (r0 + 1 < rows) {
+                    float gv = 0.f, uv = 0.f;
+#pragma unroll
+                    for (int w = 0; w < WPR; w++) {
+                        gv += rb[r0 * WPR + w];
+                        uv += rb[(r0 + 1) * WPR + w];
+                    }
+                    const float act = a.geglu ? gelu_ref_f(gv) : silu_ref_f(gv);
+                    a.y[(row0 + r0) / 2] = act * uv;
+                }
+            }
+        } else if (tid < RC && tid < rows) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < WPR; w++) v += rb[tid * WPR + w];
+            const long row = row0 + tid;
+            if (EPI == EPI_RESID) {
+                a.y[row] = a.y[row] + v;
+            } else if (EPI == EPI_HEAD) {
+                if (a.softcap > 0.f) v = a.softcap * tanhf(v / a.softcap);
+                a.y[row] = v;
+                const unsigned long long kk = argmax_key(v, (unsigned)row);
+                best = kk > best ? kk : best;
+            } else {
+                a.y[row] = a.bias ? v + a.bias[row] : v;
+            }
+        }
+    }
+    if (failed) {
+        // record the timeout and let every issued copy land before exiting
+        if (tid == 0) {
+            atomicExch(a.status, (int)DEV_TIMEOUT);
+            const int issued = min(mycount, failed - 1 + S);
+            for (int i = failed - 1; i < issued; i++)
+                mbar_wait(&bars[i % S], (unsigned)((i / S) & 1), GEMV_WAIT_NS);
+        }
+        return;
+    }
+    if (EPI == EPI_HEAD && warp == 0) {  // RC <= 32: the epilogue rows live in warp 0
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(FULL, best, o);
+            best = t > best ? t : best;
+        }
+        if (lane == 0 && mycount > 0) atomicMax(a.key, best);
+    }
+}
+
+// ---- host side ----------------------------------------------------------------
+// The streaming kernel handles K with K/32 a multiple of 8 (GGUF f16 scales)
+// or 4 (crate f32 scales), so every chunk copy is a multiple of 16 bytes, and
+// K <= 24576.
+inline bool sgemv_supported(int layout, int K) {
+    const int nb = K / 32;
+    if (K % 32 || nb > GemvC768::NB_MAX) return false;
+    return layout == LAYOUT_GGUF ? nb % 8 == 0 : nb % 4 == 0;
+}
+
+int launch_sgemv(cw_ctx* ctx, int layout, int pro, int epi, const GemvArgs& a, bool pdl);
+
+}  // namespace cw

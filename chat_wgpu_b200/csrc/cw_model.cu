@@ -30,6 +30,7 @@
 #include "cw_attn.cuh"
 #include "cw_common.h"
 #include "cw_device.cuh"
+#include "cw_gemv.cuh"
 #include "cw_gguf.h"
 #include "cw_ops.h"
 #include "cw_q4.h"
@@ -74,31 +75,10 @@ namespace cw {
 // ===========================================================================
 // fused kernels
 // ===========================================================================
-enum { PRO_X = 0, PRO_NORM = 1 };
-enum { EPI_STORE = 0, EPI_RESID = 1, EPI_GLU = 2, EPI_HEAD = 3 };
-
-struct FArgs {
-    const uint8_t* payload;
-    const __half* scales;
-    int K, N;
-    // PRO_X
-    const float* x;
-    // PRO_NORM: h = base (+ delta, post-normed if post_w); x = rmsnorm(h) * gain
-    const float* base;
-    const float* delta;
-    const float* post_w;
-    float* h_out;   // CTA 0 stores h here when non-null
-    const float* norm_w;
-    float* xn_out;  // CTA 0 stores the normalised x here when non-null
-    float eps;
-    int unit;       // UnitShift gain (1 + w) for norm_w and post_w
-    // epilogue
-    float* y;
-    const float* bias;
-    int geglu;
-    float softcap;
-    DevState* st;
-};
+// The prologue/epilogue vocabulary and argument block are shared with the
+// streaming GEMV (cw_gemv.cuh); k_fgemv below is the fallback for K that the
+// streaming kernel does not take (K/32 not a multiple of 8).
+using FArgs = GemvArgs;
 
 __device__ __forceinline__ float cta_sum(float v, float* red) {
     v = warp_sum(v);
@@ -125,7 +105,7 @@ __host__ __device__ constexpr size_t fgemv_smem(int pro, int K) {
 
 template <int PRO, int EPI, int R>
 __global__ void __launch_bounds__(256) k_fgemv(FArgs a) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     __shared__ float red[8];
     __shared__ unsigned long long red_key[8];
     const int nb = a.K / 32;
@@ -137,7 +117,8 @@ __global__ void __launch_bounds__(256) k_fgemv(FArgs a) {
         for (long g = blockIdx.x; g < groups; g += gridDim.x) {
             long r0 = g * 8 * R, r1 = min((long)a.N, r0 + 8 * R);
             prefetch_l2(a.payload + (size_t)r0 * nb * 16, a.payload + (size_t)r1 * nb * 16);
-            prefetch_l2(a.scales + (size_t)r0 * nb, a.scales + (size_t)r1 * nb);
+            const __half* sc = reinterpret_cast<const __half*>(a.scales);
+            prefetch_l2(sc + (size_t)r0 * nb, sc + (size_t)r1 * nb);
         }
     }
     pdl_wait();
@@ -233,7 +214,7 @@ __global__ void __launch_bounds__(256) k_fgemv(FArgs a) {
         __syncthreads();
         if (threadIdx.x == 0) {
             for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = red_key[w] > best ? red_key[w] : best;
-            atomicMax(&a.st->key, best);
+            atomicMax(a.key, best);
         }
     }
 }
@@ -444,6 +425,7 @@ static int pick_r(cw_ctx* ctx, long N) {
 
 template <int PRO, int EPI>
 static int fgemv(cw_ctx* ctx, const FArgs& a) {
+    if (sgemv_supported(LAYOUT_GGUF, a.K)) return launch_sgemv(ctx, LAYOUT_GGUF, PRO, EPI, a, ctx->pdl);
     int r = pick_r(ctx, a.N);
     if (r == 4) return launch_fgemv<PRO, EPI, 4>(ctx, a);
     if constexpr (EPI == EPI_GLU) {
@@ -858,7 +840,7 @@ static int enqueue_step(cw_session* s, bool decode) {
         h.unit = unit;
         h.y = s->logits;
         h.softcap = I.final_softcap;
-        h.st = s->st;
+        h.key = &s->st->key;
         CW_TRY((fgemv<PRO_NORM, EPI_HEAD>(ctx, h)));
     }
     stage("finalize");
@@ -1150,6 +1132,84 @@ int cw_session_launches(cw_session* s, size_t* prompt_step, size_t* decode_step)
     *prompt_step = per;
     *decode_step = per + 1;
     return CW_OK;
+}
+
+int cw_session_profile(cw_session* s, size_t n_steps, cw_profile_row* rows, size_t cap,
+                       size_t* n_rows) {
+    clear_error();
+    CW_CHECK(s && n_rows, CW_ERR_INVALID_ARG, "cw_session_profile: bad arguments");
+    CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_session_profile: call cw_session_begin first");
+    CW_CHECK(s->host_pos + 1 >= s->n_prompt, CW_ERR_INVALID_ARG,
+             "cw_session_profile: run the prompt positions first");
+    cw_ctx* ctx = s->ctx;
+    cudaSetDevice(ctx->device);
+    CW_CUDA(cudaStreamSynchronize(ctx->stream));
+    // capture one decode step with an event pair around each kernel
+    const bool pdl = ctx->pdl, prof = ctx->profiling;
+    std::vector<ProfRec> saved;
+    saved.swap(ctx->prof);
+    ctx->pdl = false;
+    ctx->profiling = true;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int rc = CW_OK;
+    cudaError_t ce = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+    if (ce == cudaSuccess) {
+        rc = enqueue_step(s, true);
+        ce = cudaStreamEndCapture(ctx->stream, &g);
+    }
+    std::vector<ProfRec> recs;
+    recs.swap(ctx->prof);
+    ctx->prof.swap(saved);
+    ctx->pdl = pdl;
+    ctx->profiling = prof;
+    if (rc == CW_OK && ce == cudaSuccess) ce = cudaGraphInstantiate(&exec, g, 0);
+    if (g) cudaGraphDestroy(g);
+    auto release = [&]() {
+        if (exec) cudaGraphExecDestroy(exec);
+        for (auto& p : recs) {
+            ctx->event_pool.push_back(p.start);
+            ctx->event_pool.push_back(p.stop);
+        }
+    };
+    if (rc != CW_OK || ce != cudaSuccess) {
+        release();
+        if (rc != CW_OK) return rc;
+        return set_error(CW_ERR_CUDA, "profile graph: %s", cudaGetErrorString(ce));
+    }
+    std::map<std::string, std::pair<uint32_t, double>> agg;
+    for (size_t it = 0; it < n_steps; it++) {
+        if (s->host_pos >= s->max_seq) {
+            release();
+            return set_error(CW_ERR_INVALID_ARG, "session is full: position %zu", s->host_pos);
+        }
+        ce = cudaGraphLaunch(exec, ctx->stream);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(ctx->stream);
+        if (ce != cudaSuccess) {
+            release();
+            return set_error(CW_ERR_CUDA, "profile step: %s", cudaGetErrorString(ce));
+        }
+        s->host_pos++;
+        s->n_produced++;
+        for (auto& p : recs) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, p.start, p.stop);
+            auto& a = agg[p.name];
+            a.first += 1;
+            a.second += ms;
+        }
+    }
+    release();
+    std::vector<std::pair<std::string, std::pair<uint32_t, double>>> v(agg.begin(), agg.end());
+    std::sort(v.begin(), v.end(),
+              [](const auto& a, const auto& b) { return a.second.second > b.second.second; });
+    *n_rows = v.size();
+    for (size_t i = 0; i < v.size() && i < cap && rows; i++) {
+        snprintf(rows[i].kernel, sizeof rows[i].kernel, "%s", v[i].first.c_str());
+        rows[i].passes = v[i].second.first;
+        rows[i].total_ms = v[i].second.second;
+    }
+    return check_device_status(ctx);
 }
 
 int cw_generate(cw_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new,

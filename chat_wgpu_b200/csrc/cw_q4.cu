@@ -6,6 +6,7 @@
 
 #include "cw_common.h"
 #include "cw_device.cuh"
+#include "cw_gemv.cuh"
 #include "cw_q4.h"
 
 namespace cw {
@@ -21,7 +22,7 @@ __global__ void __launch_bounds__(256) k_q4_gemv(const float* __restrict__ x,
                                                  const uint8_t* __restrict__ payload,
                                                  const void* __restrict__ scales, int K, long N,
                                                  float* __restrict__ y) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     const int nb = K / 32;
     Q24 s = q24_carve(smem, nb);
     q24_prepare<LAYOUT>(s, x);
@@ -75,6 +76,16 @@ static int launch_gemv_r(cw_ctx* ctx, const float* x, const void* payload, const
 template <int LAYOUT>
 int launch_q4_gemv(cw_ctx* ctx, const float* x, const void* payload, const void* scales, int K,
                    long N, float* y) {
+    if (sgemv_supported(LAYOUT, K)) {
+        GemvArgs a = {};
+        a.payload = (const uint8_t*)payload;
+        a.scales = scales;
+        a.K = K;
+        a.N = (int)N;
+        a.x = x;
+        a.y = y;
+        return launch_sgemv(ctx, LAYOUT, PRO_X, EPI_STORE, a, false);
+    }
     // R rows per warp: 4 when there are enough rows to fill every SM twice
     // over, else fewer rows per warp and more warps.
     long sm2 = 2L * ctx->sm_count * 8;

@@ -125,11 +125,13 @@ CONFIGS = {
     "tiny-qwen3": dict(arch="qwen3", dim=64, n_layers=2, n_heads=4, n_kv=2, head_dim=16,
                        hidden=128, vocab=256, eps=1e-6, theta=1e6, tied=True),
     # small shapes that exercise the family switches in tests
-    "tiny-gemma2": dict(arch="gemma2", dim=128, n_layers=3, n_heads=4, n_kv=2, head_dim=32,
-                        hidden=256, vocab=512, eps=1e-6, theta=1e4, tied=True, window=6,
+    "small-qwen3": dict(arch="qwen3", dim=512, n_layers=4, n_heads=8, n_kv=4, head_dim=64,
+                        hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True),
+    "tiny-gemma2": dict(arch="gemma2", dim=256, n_layers=3, n_heads=4, n_kv=2, head_dim=64,
+                        hidden=512, vocab=512, eps=1e-6, theta=1e4, tied=True, window=6,
                         attn_softcap=2.0, final_softcap=3.0),
-    "tiny-qwen2": dict(arch="qwen2", dim=128, n_layers=2, n_heads=8, n_kv=2, head_dim=16,
-                       hidden=256, vocab=300, eps=1e-6, theta=1e6, tied=False, bias=True),
+    "tiny-qwen2": dict(arch="qwen2", dim=256, n_layers=2, n_heads=8, n_kv=2, head_dim=32,
+                       hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=False, bias=True),
 }
 
 

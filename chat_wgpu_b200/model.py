@@ -129,6 +129,15 @@ class Session:
         _lib.call("cw_session_launches", self._h, C.byref(a), C.byref(b))
         return int(a.value), int(b.value)
 
+    def profile(self, n_steps: int) -> list[tuple[str, int, float]]:
+        """Per-kernel device time of n_steps decode steps (kernel, launches, ms),
+        sorted by total descending (cw_session_profile)."""
+        rows = (_lib.ProfileRow * 64)()
+        n = C.c_size_t()
+        _lib.call("cw_session_profile", self._h, int(n_steps), rows, 64, C.byref(n))
+        return [(rows[i].kernel.decode(), int(rows[i].passes), float(rows[i].total_ms))
+                for i in range(min(n.value, 64))]
+
     @property
     def pos(self) -> int:
         n = C.c_size_t()

@@ -233,6 +233,13 @@ int cw_session_step(cw_session* s, uint32_t token_in, uint32_t* token_out);
 int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms);
 /* Kernel launches one step makes (prompt and decode steps). */
 int cw_session_launches(cw_session* s, size_t* prompt_step, size_t* decode_step);
+/* Per-kernel device time of n_steps decode steps: the step is captured once
+ * as a CUDA graph with a CUDA-event pair around every kernel (kernels run
+ * back to back without overlap in this graph) and replayed n_steps times;
+ * rows aggregate by kernel stage name (the reference's WGPU_PROFILE
+ * breakdown, mod.rs:74-88, profile.rs:86-117). */
+int cw_session_profile(cw_session* s, size_t n_steps, cw_profile_row* rows, size_t cap,
+                       size_t* n_rows);
 
 /* model::generate (mod.rs:57-125): greedy, the prompt one token per step,
  * exactly max_new tokens (and one token when max_new == 0, as the reference's

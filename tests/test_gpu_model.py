@@ -59,12 +59,12 @@ def models(tmp_path_factory):
     from chat_wgpu_b200 import gguf
     d = tmp_path_factory.mktemp("gpu_models")
     out = {}
-    for name, seed in [("tiny-qwen3", 7), ("tiny-gemma2", 3), ("tiny-qwen2", 5)]:
+    for name, seed in [("tiny-qwen3", 7), ("small-qwen3", 2), ("tiny-gemma2", 3), ("tiny-qwen2", 5)]:
         out[name] = gguf.synth_model(str(d / f"{name}.gguf"), gguf.CONFIGS[name], seed=seed)
     return out
 
 
-@pytest.mark.parametrize("name", ["tiny-qwen3", "tiny-gemma2", "tiny-qwen2"])
+@pytest.mark.parametrize("name", ["tiny-qwen3", "small-qwen3", "tiny-gemma2", "tiny-qwen2"])
 def test_fused_session_vs_oracle(ctx, orc, models, name):
     from chat_wgpu_b200.model import Model
     path = models[name]
@@ -83,7 +83,7 @@ def test_fused_session_vs_oracle(ctx, orc, models, name):
 
 def test_graph_equals_direct_launch(ctx, models):
     from chat_wgpu_b200.model import Model
-    m = Model(ctx, models["tiny-qwen3"])
+    m = Model(ctx, models["small-qwen3"])
     prompt = np.array([3, 1, 4, 1, 5], np.uint32)
     t1, l1 = session_stream(m, prompt, 12, use_graph=True)
     t2, l2 = session_stream(m, prompt, 12, use_graph=False)
