@@ -116,6 +116,7 @@ struct OpScope {
     cw_ctx* ctx;
     const char* name;
     cudaEvent_t start = nullptr, stop = nullptr;
+    unsigned flags = 0;
     OpScope(cw_ctx* c, const char* n);
     ~OpScope();
 };

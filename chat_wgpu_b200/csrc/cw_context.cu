@@ -24,7 +24,12 @@ int set_error(int status, const char* fmt, ...) {
     return status;
 }
 
-void clear_error() { g_err.clear(); }
+// Clears this thread's message and any non-sticky CUDA error left by an
+// earlier call, so a later launch check reports only its own failure.
+void clear_error() {
+    g_err.clear();
+    (void)cudaGetLastError();
+}
 
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
@@ -121,12 +126,17 @@ OpScope::OpScope(cw_ctx* c, const char* n) : ctx(c), name(n) {
     };
     start = take();
     stop = take();
-    cudaEventRecord(start, ctx->stream);
+    // Inside stream capture a plain record only tracks dependencies; the
+    // External flag makes it an event-record node that timestamps on replay.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(ctx->stream, &cs);
+    flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : 0;
+    cudaEventRecordWithFlags(start, ctx->stream, flags);
 }
 
 OpScope::~OpScope() {
     if (!start) return;
-    cudaEventRecord(stop, ctx->stream);
+    cudaEventRecordWithFlags(stop, ctx->stream, flags);
     ctx->prof.push_back({name, start, stop});
 }
 

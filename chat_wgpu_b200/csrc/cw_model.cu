@@ -244,16 +244,18 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
     const int g = blockIdx.y, split = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_trigger();
-    const int pos = a.st->pos, seq = pos + 1;  // written only by the previous step
+    // The position is written by the previous step's finalize kernel, which an
+    // early-launched chain of dependents can overtake: read it only after the
+    // dependency wait (no global data read before pdl_wait may come from an
+    // earlier kernel).
+    pdl_wait();
+    const int pos = a.st->pos, seq = pos + 1;
     const int n_active = attn_active_splits(attn_span(seq, a.window), a.n_splits);
-    if (split >= n_active) {
-        pdl_wait();
-        return;
-    }
+    if (split >= n_active) return;
     int jlo, jhi;
     attn_range(seq, a.window, split, n_active, &jlo, &jhi);
     const bool holds = pos >= jlo && pos < jhi;
-    if (threadIdx.x == 0) {  // cached rows [jlo, min(jhi, pos)) were written by earlier steps
+    if (threadIdx.x == 0) {  // cached rows [jlo, min(jhi, pos)) into L2 in one go
         int j1 = min(jhi, pos);
         if (j1 > jlo) {
             const float* kb0 = a.kc + ((size_t)g * a.max_seq) * hd;
@@ -262,7 +264,6 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
             prefetch_l2(vb0 + (size_t)jlo * hd, vb0 + (size_t)j1 * hd);
         }
     }
-    pdl_wait();
     float* qs = sm + attn_smem_floats(G, hd, a.n_splits);  // [G][hd]
     float* ks = qs + (size_t)G * hd;           // [hd]
     const int qd = a.n_heads * hd, kvd = a.n_kv * hd;

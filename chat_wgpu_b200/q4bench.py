@@ -56,9 +56,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--iters", type=int, default=200)
+    ap.add_argument("--shape", default=None, help="one shape as IN_FxOUT_F, e.g. 1024x151936")
     args = ap.parse_args()
+    shapes = SHAPES
+    if args.shape:
+        k, n = (int(v) for v in args.shape.lower().split("x"))
+        shapes = [(k, n)]
     ctx = GpuContext(0)
-    rows = [bench_shape(ctx, k, n, args.iters) for k, n in SHAPES]
+    rows = [bench_shape(ctx, k, n, args.iters) for k, n in shapes]
     if args.json:
         print(json.dumps(rows))
     else:
