@@ -13,32 +13,29 @@ static int sgemv_go(cw_ctx* ctx, const GemvArgs& a, bool pdl) {
     const int nb = a.K / 32;
     const long nchunks = ((long)a.N + CF::RC - 1) / CF::RC;
     // Small GEMVs (the per-layer decode projections): one chunk per CTA, all
-    // weight traffic in flight at once.  Large ones (LM heads): two
-    // persistent CTAs per SM with a ring of up to 4 stages.
-    long grid;
-    int S;
-    if (nchunks <= 2L * ctx->sm_count) {
-        grid = nchunks;
-        S = 1;
-    } else {
-        grid = 2L * ctx->sm_count;
-        S = (int)std::min<long>(4, (nchunks + grid - 1) / grid);
-    }
-    GemvSmem L(CF::RC, CF::WPR, nb, SW, S, a.K, PRO == PRO_NORM);
-    while (S > 1 && 2 * (L.total + 1024) > (size_t)ctx->smem_per_sm) {
-        S--;
-        L = GemvSmem(CF::RC, CF::WPR, nb, SW, S, a.K, PRO == PRO_NORM);
-    }
+    // weight traffic in flight at once.  Large ones (LM heads): persistent
+    // CTAs, as many per SM as registers and shared memory allow, each with a
+    // two-stage ring (one chunk landing while the other is consumed).
+    auto kern = k_sgemv<LAYOUT, PRO, EPI, CF>;
+    const int S = nchunks <= (long)ctx->sm_count * 2 ? 1 : 2;
+    const GemvSmem L(CF::RC, CF::WPR, nb, SW, S, a.K, PRO == PRO_NORM);
     CW_CHECK((int)L.total <= ctx->max_smem_optin, CW_ERR_UNSUPPORTED,
              "gemv: K=%d needs %zu bytes of shared memory", a.K, L.total);
-    auto kern = k_sgemv<LAYOUT, PRO, EPI, CF>;
-    static thread_local std::map<std::pair<int, const void*>, size_t> attr_set;
-    auto key = std::make_pair(ctx->device, (const void*)kern);
-    if (L.total > 48 * 1024 && attr_set[key] < L.total) {
-        CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)L.total));
-        attr_set[key] = L.total;
+    static thread_local std::map<std::tuple<int, const void*, size_t>, int> occ;
+    const auto key = std::make_tuple(ctx->device, (const void*)kern, L.total);
+    auto it = occ.find(key);
+    int per_sm;
+    if (it == occ.end()) {
+        if (L.total > 48 * 1024)
+            CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)L.total));
+        CW_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, L.total));
+        per_sm = std::max(per_sm, 1);
+        occ[key] = per_sm;
+    } else {
+        per_sm = it->second;
     }
+    const long grid = std::min<long>(nchunks, (long)ctx->sm_count * per_sm);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(256);

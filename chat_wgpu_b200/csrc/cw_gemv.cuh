@@ -159,6 +159,39 @@ __device__ __forceinline__ float gemv_cta_sum(float v, float* red8) {
     return t;
 }
 
+// Reduce RPW (1, 2 or 4) per-lane partials across the warp in 5 shuffles:
+// the first log2(RPW) butterfly steps exchange whole rows instead of summing
+// them, so afterwards lanes [j*32/RPW, (j+1)*32/RPW) hold row j's total.
+// The order of additions is fixed, so the result is reproducible.
+template <int RPW>
+__device__ __forceinline__ float warp_reduce_rows(const float (&v)[RPW], int lane) {
+    if constexpr (RPW == 1) {
+        return warp_sum(v[0]);
+    } else if constexpr (RPW == 2) {
+        const bool up = lane & 16;
+        float keep = up ? v[1] : v[0];
+        const float send = up ? v[0] : v[1];
+        keep += __shfl_xor_sync(FULL, send, 16);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(FULL, keep, o);
+        return keep;
+    } else {
+        static_assert(RPW == 4, "rows per warp must be 1, 2 or 4");
+        const bool up = lane & 16;
+        float k0 = up ? v[2] : v[0], k1 = up ? v[3] : v[1];
+        const float s0 = up ? v[0] : v[2], s1 = up ? v[1] : v[3];
+        k0 += __shfl_xor_sync(FULL, s0, 16);
+        k1 += __shfl_xor_sync(FULL, s1, 16);
+        const bool up2 = lane & 8;
+        float k = up2 ? k1 : k0;
+        const float s = up2 ? k0 : k1;
+        k += __shfl_xor_sync(FULL, s, 8);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) k += __shfl_xor_sync(FULL, k, o);
+        return k;
+    }
+}
+
 __device__ __forceinline__ float silu_ref_f(float x) { return x / (1.0f + expf(-x)); }  // glu.wgsl:25
 __device__ __forceinline__ float gelu_ref_f(float x) {                                 // glu.wgsl:27-30
     const float c = 0.7978845608028654f;
@@ -288,47 +321,58 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
         const long row0 = (blockIdx.x + (long)i * gridDim.x) * RC;
         const int rows = (int)min((long)RC, (long)a.N - row0);
         float* rb = red + (size_t)(i & 1) * RC * WPR;
+        // all of this warp's loads first (RPW rows x BPL blocks), then the math
+        uint4 w4[RPW][BPL];
+        float dd[RPW][BPL];
 #pragma unroll
         for (int j = 0; j < RPW; j++) {
             const int r = slot * RPW + j;
-            float acc = 0.f;
-            if (r < rows) {
 #pragma unroll
-                for (int k = 0; k < BPL; k++) {
-                    const int b = wsub * 32 + lane + k * 32 * WPR;
-                    if (b < nb) {
-                        const size_t blk = (size_t)r * nb + b;
-                        const uint4 w4 = reinterpret_cast<const uint4*>(pay)[blk];
-                        const float d =
-                            SW == 2 ? __half2float(reinterpret_cast<const __half*>(scs)[blk])
-                                    : reinterpret_cast<const float*>(scs)[blk];
-                        const unsigned w[4] = {w4.x, w4.y, w4.z, w4.w};
-                        const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
-                        const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
-                        const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
-                        const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
-                        const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
-                        const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
-                        int s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-                        for (int t = 0; t < 4; t++) {
-                            const unsigned lo = w[t] & 0x0f0f0f0fu;
-                            const unsigned hi = (w[t] >> 4) & 0x0f0f0f0fu;
-                            s0 = dp4a_uu(lo, a0[t], s0);
-                            s0 = dp4a_uu(hi, b0[t], s0);
-                            s1 = dp4a_uu(lo, a1[t], s1);
-                            s1 = dp4a_uu(hi, b1[t], s1);
-                            s2 = dp4a_us(lo, a2[t], s2);
-                            s2 = dp4a_us(hi, b2[t], s2);
-                        }
-                        const float T = fmaf((float)s2, 65536.0f, (float)(s0 + (s1 << 8) - cbr[k]));
-                        acc = fmaf(d * sbr[k], T, acc);
-                    }
-                }
+            for (int k = 0; k < BPL; k++) {
+                const int b = wsub * 32 + lane + k * 32 * WPR;
+                const bool in = r < rows && b < nb;
+                const size_t blk = in ? (size_t)r * nb + b : 0;
+                w4[j][k] = in ? reinterpret_cast<const uint4*>(pay)[blk] : make_uint4(0, 0, 0, 0);
+                dd[j][k] = !in ? 0.f
+                               : (SW == 2 ? __half2float(reinterpret_cast<const __half*>(scs)[blk])
+                                          : reinterpret_cast<const float*>(scs)[blk]);
             }
-            acc = warp_sum(acc);
-            if (lane == 0) rb[r * WPR + wsub] = acc;
         }
+        float acc[RPW];
+#pragma unroll
+        for (int j = 0; j < RPW; j++) {
+            acc[j] = 0.f;
+#pragma unroll
+            for (int k = 0; k < BPL; k++) {
+                const unsigned w[4] = {w4[j][k].x, w4[j][k].y, w4[j][k].z, w4[j][k].w};
+                const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
+                const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
+                const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
+                const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
+                const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
+                const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
+                // six independent dp4a chains of four (low / high nibbles apart)
+                int s0l = 0, s0h = 0, s1l = 0, s1h = 0, s2l = 0, s2h = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const unsigned lo = w[t] & 0x0f0f0f0fu;
+                    const unsigned hi = (w[t] >> 4) & 0x0f0f0f0fu;
+                    s0l = dp4a_uu(lo, a0[t], s0l);
+                    s0h = dp4a_uu(hi, b0[t], s0h);
+                    s1l = dp4a_uu(lo, a1[t], s1l);
+                    s1h = dp4a_uu(hi, b1[t], s1h);
+                    s2l = dp4a_us(lo, a2[t], s2l);
+                    s2h = dp4a_us(hi, b2[t], s2h);
+                }
+                const int s01 = (s0l + s0h) + ((s1l + s1h) << 8) - cbr[k];
+                const float T = fmaf((float)(s2l + s2h), 65536.0f, (float)s01);
+                acc[j] = fmaf(dd[j][k] * sbr[k], T, acc[j]);
+            }
+        }
+        // transposed butterfly: the RPW row sums in 5 shuffles; afterwards lane
+        // (32/RPW)*j holds the warp's partial of row slot*RPW + j
+        float v = warp_reduce_rows<RPW>(acc, lane);
+        if ((lane & (32 / RPW - 1)) == 0) rb[(slot * RPW + lane / (32 / RPW)) * WPR + wsub] = v;
         __syncthreads();  // stage s consumed, row partials complete
         if (tid == 0 && i + S < mycount) issue(i + S);
         // epilogue: fixed-order sum of the WPR partials of each row
