@@ -89,6 +89,7 @@ SIGNATURES = {
     "cw_swiglu": [_vp, _buf, _buf, _sz, _pbuf],
     "cw_geglu": [_vp, _buf, _buf, _sz, _pbuf],
     "cw_argmax": [_vp, _buf, _sz, _pbuf],
+    "cw_attention_noalloc": [C.c_int, _vp, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _sz],
     "cw_q4_0_upload": [_vp, _vp, _sz, _sz, _pbuf],
     "cw_q4_0_pack": [_vp, _buf, _sz, _sz, _pbuf],
     "cw_q4_0_gemv": [_vp, _buf, _buf, _sz, _sz, _pbuf],

@@ -124,30 +124,44 @@ static int attn_dispatch_g(int G, dim3 grid, size_t smem, cudaStream_t st, const
     return check_launch("attention");
 }
 
+int attention_splits_for(int sm_count, int span, int n_kv);
+
 int attention_splits(cw_ctx* ctx, int span, int n_kv) {
-    int by_sm = std::max(1, 2 * ctx->sm_count / std::max(1, n_kv));
+    return attention_splits_for(ctx->sm_count, span, n_kv);
+}
+
+int attention_splits_for(int sm_count, int span, int n_kv) {
+    int by_sm = std::max(1, 2 * sm_count / std::max(1, n_kv));
     return attn_active_splits(span, by_sm);
 }
 
-int launch_attention(cw_ctx* ctx, const float* q, const float* k, const float* v, float* out,
-                     int n_heads, int n_kv, int seq, int hd, float softcap, int window,
-                     long head_stride, long row_stride, int n_splits, float* part) {
+int launch_attention_raw(cudaStream_t st, const float* q, const float* k, const float* v,
+                         float* out, int n_heads, int n_kv, int seq, int hd, float softcap,
+                         int window, long head_stride, long row_stride, int n_splits, float* part,
+                         unsigned* counters) {
     const int G = n_heads / n_kv;
     const float scale = powf((float)hd, -0.5f);  // attention.rs:18
     size_t smem = attn_smem_floats(G, hd, n_splits) * sizeof(float);
-    CW_TRY(ensure_counters(ctx, (size_t)n_kv));
     dim3 grid(n_splits, n_kv);
     int epl = (hd + 31) / 32;
     auto go = [&](auto tag) -> int {
         constexpr int E = decltype(tag)::value;
-        return attn_dispatch_g<E>(G, grid, smem, ctx->stream, q, k, v, out, n_heads, n_kv, seq, hd,
-                                  scale, softcap, window, head_stride, row_stride, n_splits, part,
-                                  ctx->d_counters);
+        return attn_dispatch_g<E>(G, grid, smem, st, q, k, v, out, n_heads, n_kv, seq, hd, scale,
+                                  softcap, window, head_stride, row_stride, n_splits, part,
+                                  counters);
     };
     if (epl <= 1) return go(std::integral_constant<int, 1>());
     if (epl <= 2) return go(std::integral_constant<int, 2>());
     if (epl <= 4) return go(std::integral_constant<int, 4>());
     return go(std::integral_constant<int, 8>());
+}
+
+int launch_attention(cw_ctx* ctx, const float* q, const float* k, const float* v, float* out,
+                     int n_heads, int n_kv, int seq, int hd, float softcap, int window,
+                     long head_stride, long row_stride, int n_splits, float* part) {
+    CW_TRY(ensure_counters(ctx, (size_t)n_kv));
+    return launch_attention_raw(ctx->stream, q, k, v, out, n_heads, n_kv, seq, hd, softcap, window,
+                                head_stride, row_stride, n_splits, part, ctx->d_counters);
 }
 
 // ---- elementwise: ewise.wgsl:9-13, glu.wgsl:22-32 ----------------------------

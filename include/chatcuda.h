@@ -157,6 +157,29 @@ int cw_geglu(cw_ctx* ctx, cw_buf gate, cw_buf up, size_t n, cw_buf* out);
 /* argmax::argmax (argmax.rs:11-18): 1-element u32 buffer, ties -> lowest. */
 int cw_argmax(cw_ctx* ctx, cw_buf logits, size_t n, cw_buf* out);
 
+/* ---- attention without allocation ----------------------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory -- a host whose own pool owns every device allocation, code running
+ * while a CUDA graph is captured, a plugin whose process allocator must not
+ * see new blocks: the single-query GQA attention of cw_attention, with q
+ * [n_heads*head_dim], k/v [seq, n_kv*head_dim] and out [n_heads*head_dim]
+ * passed as device pointers, and the split scratch (partial results and merge
+ * counters) kept in one static device array of CW_NOALLOC_SCRATCH_BYTES per
+ * GPU that loads the library (held until the process exits).  It calls no
+ * cudaMalloc, cudaFree or other allocating routine.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture.  Every call
+ * shares the array and it keeps the last call's contents: each call clears
+ * the counters it uses before its kernel, and calls whose kernels can overlap
+ * on the GPU (e.g. on unordered streams) race.  Shapes whose partials exceed
+ * the array are rejected with CW_ERR_INVALID_ARG.  The work is enqueued on
+ * `stream` (a cudaStream_t; NULL = the legacy default stream); synchronise it
+ * before reading `out`.  Results equal cw_attention's for the same inputs. */
+#define CW_NOALLOC_SCRATCH_BYTES (1 << 20)
+int cw_attention_noalloc(int device, void* stream, const float* q, const float* k,
+                         const float* v, float* out, size_t n_heads, size_t n_kv, size_t seq,
+                         size_t head_dim);
+
 /* ---- GGUF-native Q4_0 (the B200 weight format) --------------------------
  * GGUF Q4_0 blocks (f16 d + 16 nibble bytes, dequant.rs:60-78) are kept in
  * HBM as two planes: the 16-byte nibble payloads and the f16 scales.  The
