@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--per-stage", action="store_true",
+                    help="time the one-kernel-per-stage step instead of the persistent one")
     ap.add_argument("--profile-steps", type=int, default=8,
                     help="decode steps of the per-kernel profile pass (at least 1)")
     return ap.parse_args()
@@ -193,6 +195,13 @@ def step_bytes(info: dict, pos: float) -> float:
             + kb["lm_head"] + kb["embed"] + kb["finalize"])
 
 
+def launch_bytes(info: dict, pos: float) -> dict:
+    """kernel_bytes plus the persistent kernel, whose one launch is the step."""
+    kb = kernel_bytes(info, pos)
+    kb["decode_step"] = step_bytes(info, pos)
+    return kb
+
+
 # ---------------------------------------------------------------- CPU legs
 def oracle_decode_rate(path: str, prompt, n_decode: int, threads: int | None = None):
     """Oracle port: tokens/s of n_decode decode steps after the prompt."""
@@ -286,6 +295,9 @@ def run_cuda(args, dist):
 
     # ---- device-timed decode: K graph replays, inputs resident in HBM
     s = Session(model, max_seq)
+    if args.per_stage:
+        s.set_persistent(False)
+    persistent = s.persistent
     s.begin(prompt)
     s.run(P - 1)                     # prompt positions (no lm_head)
     s.run(W)                         # warm-up decode steps
@@ -308,6 +320,18 @@ def run_cuda(args, dist):
     prof = s.profile(max(1, args.profile_steps))
     s.close()
 
+    # ---- the other step path on the same positions, for the record
+    other = None
+    if persistent:
+        so = Session(model, max_seq)
+        so.set_persistent(False)
+        so.begin(prompt)
+        so.run(P - 1 + W)
+        ms_o = dist.max(so.run_timed(K))
+        other = {"path": "per-stage kernels", "ms_per_step": ms_o / K,
+                 "launches_per_step": so.launches()[1]}
+        so.close()
+
     # ---- e2e: public per-token API with host round trips
     s2 = Session(model, max_seq)
     s2.begin(prompt)
@@ -328,7 +352,7 @@ def run_cuda(args, dist):
 
     # ---- roofline of the dominant kernel
     peaks = measured_peaks()
-    kb = kernel_bytes(info, mean_pos + args.profile_steps / 2)
+    kb = launch_bytes(info, mean_pos + args.profile_steps / 2)
     rows = {name: (n, t) for name, n, t in prof}
     dom = max(((n, c, t) for n, (c, t) in rows.items() if n in kb), key=lambda r: r[2])
     dom_name, dom_count, dom_ms = dom
@@ -353,6 +377,9 @@ def run_cuda(args, dist):
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4, "same_tokens_as_device_loop": same_stream},
         "gpu_launches": int(K * launches_decode),
+        "step_path": "persistent (one cooperative launch per token)" if persistent
+                     else "per-stage kernels in a CUDA graph",
+        "other_path": other,
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "traffic": None, "peak_src": peaks["src"],

@@ -21,15 +21,20 @@ constexpr int ATTN_MIN_KEYS = 32;             // keys per split before splitting
 constexpr int ATTN_U = 4;                     // keys per warp iteration
 
 // Shared memory floats needed by attn_core + attn_finish for G heads of dim
-// hd and up to n_splits splits.
-__host__ __device__ constexpr size_t attn_smem_floats(int G, int hd, int n_splits) {
-    return (size_t)5 * G * (hd + 2) + (size_t)G * (n_splits + 1);
+// hd, up to n_splits splits and NW warps.
+__host__ __device__ constexpr size_t attn_smem_floats(int G, int hd, int n_splits, int NW = 4) {
+    return (size_t)(NW + 1) * G * (hd + 2) + (size_t)G * (n_splits + 1);
 }
 
+// K/V load paths: read-only cache (rows written by earlier launches), plain,
+// or L2-only (rows written by other CTAs of the same persistent kernel).
+enum { KV_NC = 0, KV_PLAIN = 1, KV_CG = 2 };
+
 // Splits that hold keys for a (windowed) span: at most n_splits, at least
-// ATTN_MIN_KEYS keys each.
-__host__ __device__ __forceinline__ int attn_active_splits(int span, int n_splits) {
-    int by_len = (span + ATTN_MIN_KEYS - 1) / ATTN_MIN_KEYS;
+// min_keys keys each.
+__host__ __device__ __forceinline__ int attn_active_splits(int span, int n_splits,
+                                                          int min_keys = ATTN_MIN_KEYS) {
+    int by_len = (span + min_keys - 1) / min_keys;
     by_len = by_len < 1 ? 1 : by_len;
     return by_len < n_splits ? by_len : n_splits;
 }
@@ -54,9 +59,10 @@ __device__ __forceinline__ int attn_span(int seq, int window) {
 // (rows kb + j*rs, vb + j*rs).  On return res[gi*(hd+2) + d] holds the
 // accumulator A, res[.. + hd] the max M, res[.. + hd + 1] the denominator L.
 // All threads of the 128-thread CTA call it; it ends with __syncthreads().
-// NC selects the read-only (non-coherent) load path; it must be false when
-// the calling kernel itself wrote K/V rows it then reads.
-template <int EPL, int GMAX, bool NC = true>
+// LD selects the K/V load path (KV_NC must not be used for rows the calling
+// kernel wrote).  NW warps (the CTA has NW*32 threads) take groups of four
+// keys in turn.
+template <int EPL, int GMAX, int LD = KV_NC, int NW = 4>
 __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
                                           const float* __restrict__ kb,
                                           const float* __restrict__ vb, long rs, int jlo, int jhi,
@@ -75,7 +81,7 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
             acc[gi][e] = 0.f;
         }
     }
-    for (int base = jlo + warp * ATTN_U; base < jhi; base += 4 * ATTN_U) {
+    for (int base = jlo + warp * ATTN_U; base < jhi; base += NW * ATTN_U) {
         float kk[ATTN_U][EPL], vv[ATTN_U][EPL];
 #pragma unroll
         for (int u = 0; u < ATTN_U; u++) {
@@ -87,9 +93,12 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
             for (int e = 0; e < EPL; e++) {
                 int d = lane + 32 * e;
                 bool in = ok && d < hd;
-                if (NC) {
+                if (LD == KV_NC) {
                     kk[u][e] = in ? __ldg(kr + d) : 0.f;
                     vv[u][e] = in ? __ldg(vr + d) : 0.f;
+                } else if (LD == KV_CG) {
+                    kk[u][e] = in ? __ldcg(kr + d) : 0.f;
+                    vv[u][e] = in ? __ldcg(vr + d) : 0.f;
                 } else {
                     kk[u][e] = in ? kr[d] : 0.f;
                     vv[u][e] = in ? vr[d] : 0.f;
@@ -145,15 +154,15 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
         }
     }
     __syncthreads();
-    // merge the 4 warp states (the merge rule of attention.wgsl:88-95)
+    // merge the NW warp states (the merge rule of attention.wgsl:88-95)
     for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
         int gi = i / hd, d = i - gi * hd;
         float M = REF_NEG_INF;
 #pragma unroll
-        for (int w = 0; w < 4; w++) M = fmaxf(M, sm[(size_t)(w * G + gi) * W + hd]);
+        for (int w = 0; w < NW; w++) M = fmaxf(M, sm[(size_t)(w * G + gi) * W + hd]);
         float L = 0.f, A = 0.f;
 #pragma unroll
-        for (int w = 0; w < 4; w++) {
+        for (int w = 0; w < NW; w++) {
             const float* src = sm + (size_t)(w * G + gi) * W;
             float c = expf(src[hd] - M);
             L += src[hd + 1] * c;

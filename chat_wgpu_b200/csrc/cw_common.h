@@ -72,6 +72,7 @@ struct cw_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
     int sm_count = 0;
+    int clock_khz = 1;  // max SM clock (profile cycle conversion)
     int max_smem_optin = 0;
     int smem_per_sm = 0;
     size_t l2_bytes = 0;

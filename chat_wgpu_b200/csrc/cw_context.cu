@@ -207,6 +207,8 @@ int cw_ctx_create(int device, cw_ctx** out) {
     cw_ctx* c = new cw_ctx();
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
+    cudaDeviceGetAttribute(&c->clock_khz, cudaDevAttrClockRate, c->device);
+    if (c->clock_khz <= 0) c->clock_khz = 1;
     c->l2_bytes = prop.l2CacheSize;
     c->max_smem_optin = (int)prop.sharedMemPerBlockOptin;
     c->smem_per_sm = (int)prop.sharedMemPerMultiprocessor;

@@ -136,24 +136,42 @@ __device__ __forceinline__ Q24 q24_carve(void* smem, int nb) {
     return q;
 }
 
-// Convert one 32-element block held one element per lane (v) into the planes.
-template <int LAYOUT>
-__device__ __forceinline__ void q24_block(const Q24& s, int b, float v, int lane) {
-    bool bad = !isfinite(v);
-    bad = __any_sync(FULL, bad);
-    float m = warp_max(fabsf(v));
-    int X = 0;
-    float sb;
-    if (bad) {
+// Block exponent and this lane's 24-bit integer from the block's max |v|
+// given as IEEE bits (mbits >= 0x7f800000: the block holds Inf/NaN).  For a
+// normal max with exponent field e >= 22, frexp's E is e - 126 and both
+// 2^(22-E) and 2^(E-22) are normal floats built from their exponent fields,
+// so v * 2^(22-E) is exact and equals ldexpf(v, 22 - E); smaller maxima take
+// the frexpf/ldexpf path.
+__device__ __forceinline__ void q24_scale(unsigned mbits, float v, int& X, float& sb) {
+    X = 0;
+    if (mbits >= 0x7f800000u) {
         sb = __int_as_float(0x7fc00000);
-    } else if (m == 0.0f) {
+    } else if (mbits == 0u) {
         sb = 0.0f;
     } else {
-        int E;
-        frexpf(m, &E);  // m = f * 2^E, f in [0.5, 1)  =>  m < 2^E
-        X = __float2int_rn(ldexpf(v, 22 - E));
-        sb = ldexpf(1.0f, E - 22);
+        const unsigned e = mbits >> 23;
+        if (e >= 22u) {
+            X = __float2int_rn(v * __uint_as_float((275u - e) << 23));
+            sb = __uint_as_float((e - 21u) << 23);
+        } else {
+            int E;
+            frexpf(__uint_as_float(mbits), &E);  // m = f * 2^E, f in [0.5, 1)
+            X = __float2int_rn(ldexpf(v, 22 - E));
+            sb = ldexpf(1.0f, E - 22);
+        }
     }
+}
+
+// Convert one 32-element block held one element per lane (v) into the planes.
+// The block max and the sum of the integers are single-instruction warp
+// reductions (redux.sync): for non-negative floats the IEEE bit patterns
+// order like the values, and Inf/NaN compare above every finite value.
+template <int LAYOUT>
+__device__ __forceinline__ void q24_block(const Q24& s, int b, float v, int lane) {
+    const unsigned mbits = __reduce_max_sync(FULL, __float_as_uint(fabsf(v)));
+    int X;
+    float sb;
+    q24_scale(mbits, v, X, sb);
     int pos = q24_pos<LAYOUT>(lane);
     uint8_t* base = reinterpret_cast<uint8_t*>(s.pl);
     int half = pos >> 4, off = pos & 15;
@@ -162,7 +180,7 @@ __device__ __forceinline__ void q24_block(const Q24& s, int b, float v, int lane
         int byte = (p == 2) ? ((X >> 16) & 0xff) : ((X >> (8 * p)) & 0xff);
         base[((size_t)(p * 2 + half) * s.nb + b) * 16 + off] = (uint8_t)byte;
     }
-    int sx = warp_sum_i(X);
+    const int sx = __reduce_add_sync(FULL, X);
     if (lane == 0) {
         s.cb[b] = 8 * sx;
         s.sb[b] = sb;

@@ -45,6 +45,7 @@ struct GemvArgs {
     // PRO_NORM: h = base (+ delta, post-normed with post_w when non-null);
     // x = rmsnorm(h) * gain(norm_w); h written to h_out and x to xn_out by CTA 0
     const float* base;
+    int base_smem;  // base points to this CTA's shared memory
     const float* delta;
     const float* post_w;
     float* h_out;
@@ -123,6 +124,23 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
+// Same copy with an L2 cache-policy hint (see l2_evict_first).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, unsigned bytes,
+                                              uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+// L2 policy for data read once per step (the weight stream): its lines are
+// the first to go, so the KV cache, activations and small parameters stay
+// resident in L2 while hundreds of MB of weights pass through.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -147,15 +165,15 @@ struct GemvSmem {
     }
 };
 
-__device__ __forceinline__ float gemv_cta_sum(float v, float* red8) {
+// Sum over the CTA (up to 32 warps); red holds one float per warp.
+__device__ __forceinline__ float gemv_cta_sum(float v, float* red) {
     v = warp_sum(v);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     __syncthreads();
-    if (lane == 0) red8[warp] = v;
+    if (lane == 0) red[warp] = v;
     __syncthreads();
     float t = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) t += red8[i];
+    for (int i = 0; i < nw; i++) t += red[i];
     return t;
 }
 
@@ -206,23 +224,29 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
     const int nb = a.K / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (PRO == PRO_X) {
-        q24_prepare<LAYOUT>(q, a.x);
+        for (int b = warp; b < nb; b += (blockDim.x >> 5))
+            q24_block<LAYOUT>(q, b, __ldcg(a.x + b * 32 + lane), lane);
         return;
     }
+    // base/delta may have been written by other CTAs of a persistent kernel:
+    // read them through L2 (ld.global.cg), never from a stale L1 line
     const int K = a.K;
     float inv_d = 0.f;
     if (a.delta && a.post_w) {
         float ss = 0.f;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(a.delta[i], a.delta[i], ss);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            const float dv = __ldcg(a.delta + i);
+            ss = fmaf(dv, dv, ss);
+        }
         ss = gemv_cta_sum(ss, red8);
         inv_d = 1.0f / sqrtf(ss / (float)K + a.eps);
     }
     float ssh = 0.f;
     const bool wr = a.h_out && blockIdx.x == 0;
     for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        float h = a.base[i];
+        float h = a.base_smem ? a.base[i] : __ldcg(a.base + i);
         if (a.delta) {
-            float dv = a.delta[i];
+            float dv = __ldcg(a.delta + i);
             if (a.post_w) {
                 float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
                 dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
@@ -248,7 +272,7 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
 template <int LAYOUT, int PRO, int EPI, class CF>
 __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ float red8[8];
+    __shared__ float red8[32];
     constexpr int WPR = CF::WPR, BPL = CF::BPL, RPW = CF::RPW, RC = CF::RC;
     constexpr int SW = LAYOUT == LAYOUT_GGUF ? 2 : 4;
     const int nb = a.K / 32;
@@ -269,11 +293,14 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
         const long row0 = c * RC;
         const int rows = (int)min((long)RC, (long)a.N - row0);
         const unsigned pb = (unsigned)rows * nb * 16, sb = (unsigned)rows * nb * SW;
+        const uint64_t pol = l2_evict_first();
         fence_proxy_async();
         mbar_expect_tx(&bars[s], pb + sb);
-        bulk_g2s(stages + (size_t)s * L.stage, a.payload + (size_t)row0 * nb * 16, pb, &bars[s]);
-        bulk_g2s(stages + (size_t)s * L.stage + L.pay,
-                 reinterpret_cast<const char*>(a.scales) + (size_t)row0 * nb * SW, sb, &bars[s]);
+        bulk_g2s_hint(stages + (size_t)s * L.stage, a.payload + (size_t)row0 * nb * 16, pb,
+                      &bars[s], pol);
+        bulk_g2s_hint(stages + (size_t)s * L.stage + L.pay,
+                      reinterpret_cast<const char*>(a.scales) + (size_t)row0 * nb * SW, sb,
+                      &bars[s], pol);
     };
     if (tid == 0) {
         for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);

@@ -33,42 +33,8 @@
 #include "cw_gemv.cuh"
 #include "cw_gguf.h"
 #include "cw_ops.h"
+#include "cw_model.h"
 #include "cw_q4.h"
-
-namespace cw {
-
-struct DevState {
-    int pos;          // position of the next step
-    unsigned token;   // input token of the next step
-    int n_prompt;
-    int n_produced;
-    unsigned long long key;  // argmax accumulator of the current step
-};
-
-struct QW {  // packed Q4_0 weight
-    const uint8_t* payload = nullptr;
-    const __half* scales = nullptr;
-    int rows = 0, in_f = 0;
-    cw_buf buf = 0;
-};
-
-struct Layer {
-    float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
-    float *post_attn = nullptr, *post_ffw = nullptr, *qkv_bias = nullptr;
-    QW qkv, wo, gate_up, down;
-};
-
-}  // namespace cw
-
-struct cw_model {
-    cw_ctx* ctx = nullptr;
-    cw_model_info info{};
-    std::vector<cw::Layer> L;
-    float* final_norm = nullptr;
-    cw::QW embed, head;
-    std::vector<cw_buf> owned;
-    const float* inv_freq = nullptr;
-};
 
 namespace cw {
 
@@ -322,7 +288,8 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
     __syncthreads();
     float* res = sm + 4 * G * (hd + 2);
     float* cwt = sm + 5 * G * (hd + 2);
-    attn_core<EPL, GMAX, false>(qs, G, hd, kbase, vbase, hd, jlo, jhi, a.scale, a.softcap, sm, res);
+    attn_core<EPL, GMAX, KV_PLAIN>(qs, G, hd, kbase, vbase, hd, jlo, jhi, a.scale, a.softcap, sm,
+                                   res);
     attn_finish(res, G, hd, g, split, n_active, a.n_splits, a.part, a.counters, a.out, cwt);
 }
 
@@ -367,12 +334,15 @@ __global__ void k_finalize(DevState* st, const unsigned* __restrict__ prompt,
     st->pos = pos + 1;
 }
 
-__global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n_prompt) {
+__global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n_prompt,
+                        const unsigned long long* __restrict__ bar) {
     st->pos = 0;
     st->token = prompt[0];
     st->n_prompt = n_prompt;
     st->n_produced = 0;
     st->key = argmax_key_init();
+    st->bar_base = *bar;  // the persistent step's grid barrier continues from here
+    st->done = 0;
 }
 
 // ===========================================================================
@@ -685,24 +655,6 @@ static int model_load(cw_model* m, const std::string& path) {
 // ===========================================================================
 // session
 // ===========================================================================
-struct cw_session {
-    cw_model* m = nullptr;
-    cw_ctx* ctx = nullptr;
-    size_t max_seq = 0;
-    std::vector<cw_buf> owned;
-    float *kc = nullptr, *vc = nullptr;
-    float *hidden = nullptr, *hidden_b = nullptr, *tmp = nullptr, *qkv = nullptr, *attn = nullptr;
-    float *act = nullptr, *logits = nullptr, *xnorm = nullptr, *part = nullptr;
-    unsigned *prompt = nullptr, *toks = nullptr, *counters = nullptr;
-    cw::DevState* st = nullptr;
-    int n_splits = 1;
-    bool use_graph = true;
-    cudaGraphExec_t g_prompt = nullptr, g_decode = nullptr;
-    size_t host_pos = 0, n_prompt = 0, n_produced = 0;
-    unsigned* h_tok = nullptr;     // pinned, one token for per-step reads
-    unsigned* h_tok_in = nullptr;  // pinned, one token for per-step writes
-};
-
 namespace cw {
 
 static int sess_alloc(cw_session* s, size_t nbytes, void** p) {
@@ -717,10 +669,11 @@ static int sess_alloc(cw_session* s, size_t nbytes, void** p) {
 
 // Enqueue one generate step (decode: with lm_head + argmax).
 static int enqueue_step(cw_session* s, bool decode) {
+    if (s->plan) return step_enqueue(s, decode);  // one persistent launch
     cw_model* m = s->m;
     cw_ctx* ctx = s->ctx;
     const cw_model_info& I = m->info;
-    const int qd = I.n_heads * I.head_dim, kvd = I.n_kv * I.head_dim;
+    const int qd = I.n_heads * I.head_dim;
     const bool post = I.post_norms != 0;
     const int unit = I.norm_kind == 1;
     // With the context profiler on (direct launches only), every kernel is
@@ -963,11 +916,13 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     A(max_seq * 4, (void**)&s->toks);
     A((size_t)I.n_kv * 4, (void**)&s->counters);
     A(sizeof(DevState), (void**)&s->st);
+    A(sizeof(unsigned long long), (void**)&s->bar);
     if (rc == CW_OK && (cudaMallocHost(&s->h_tok, sizeof(unsigned)) != cudaSuccess ||
                         cudaMallocHost(&s->h_tok_in, sizeof(unsigned)) != cudaSuccess))
         rc = set_error(CW_ERR_OOM, "pinned host allocation failed");
     if (rc == CW_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess)
         rc = set_error(CW_ERR_CUDA, "session setup failed");
+    if (rc == CW_OK && s->use_persistent && step_supported(m, s)) rc = step_plan_create(s);
     if (rc != CW_OK) {
         std::string msg = cw_last_error();
         cw_session_free(s);
@@ -983,6 +938,7 @@ int cw_session_free(cw_session* s) {
     cudaStreamSynchronize(s->ctx->stream);
     if (s->g_prompt) cudaGraphExecDestroy(s->g_prompt);
     if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
+    step_plan_free(s);
     for (cw_buf b : s->owned) {
         auto it = s->ctx->bufs.find(b);
         if (it != s->ctx->bufs.end()) {
@@ -1002,6 +958,32 @@ int cw_session_set_graph(cw_session* s, int use_graph) {
     return CW_OK;
 }
 
+int cw_session_set_persistent(cw_session* s, int on) {
+    clear_error();
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_set_persistent: session is NULL");
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    // captured graphs hold one path or the other
+    if (s->g_prompt) cudaGraphExecDestroy(s->g_prompt);
+    if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
+    s->g_prompt = s->g_decode = nullptr;
+    s->use_persistent = on != 0;
+    if (!on) {
+        step_plan_free(s);
+        return CW_OK;
+    }
+    if (s->plan) return CW_OK;
+    CW_CHECK(step_supported(s->m, s), CW_ERR_UNSUPPORTED,
+             "the persistent step does not cover this model family");
+    return step_plan_create(s);
+}
+
+int cw_session_persistent(cw_session* s, int* on) {
+    CW_CHECK(s && on, CW_ERR_INVALID_ARG, "cw_session_persistent: bad arguments");
+    *on = s->plan != nullptr;
+    return CW_OK;
+}
+
 int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     clear_error();
     CW_CHECK(s && prompt && n_prompt > 0, CW_ERR_INVALID_ARG,
@@ -1014,7 +996,7 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
                  s->m->info.vocab);
     cudaSetDevice(s->ctx->device);
     CW_CUDA(cudaMemcpyAsync(s->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, s->ctx->stream));
-    k_begin<<<1, 1, 0, s->ctx->stream>>>(s->st, s->prompt, (int)n_prompt);
+    k_begin<<<1, 1, 0, s->ctx->stream>>>(s->st, s->prompt, (int)n_prompt, s->bar);
     CW_TRY(check_launch("session begin"));
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     s->host_pos = 0;
@@ -1128,10 +1110,29 @@ int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms) {
 
 int cw_session_launches(cw_session* s, size_t* prompt_step, size_t* decode_step) {
     CW_CHECK(s && prompt_step && decode_step, CW_ERR_INVALID_ARG, "cw_session_launches: bad arguments");
+    if (s->plan) {  // the whole step is one persistent launch
+        *prompt_step = 1;
+        *decode_step = 1;
+        return CW_OK;
+    }
     // embed + 5 per layer + finalize (+ lm_head/argmax on decode steps)
     size_t per = 2 + 5 * (size_t)s->m->info.n_layers;
     *prompt_step = per;
     *decode_step = per + 1;
+    return CW_OK;
+}
+
+static int profile_rows(const std::map<std::string, std::pair<uint32_t, double>>& agg,
+                        cw_profile_row* rows, size_t cap, size_t* n_rows) {
+    std::vector<std::pair<std::string, std::pair<uint32_t, double>>> v(agg.begin(), agg.end());
+    std::sort(v.begin(), v.end(),
+              [](const auto& a, const auto& b) { return a.second.second > b.second.second; });
+    *n_rows = v.size();
+    for (size_t i = 0; i < v.size() && i < cap && rows; i++) {
+        snprintf(rows[i].kernel, sizeof rows[i].kernel, "%s", v[i].first.c_str());
+        rows[i].passes = v[i].second.first;
+        rows[i].total_ms = v[i].second.second;
+    }
     return CW_OK;
 }
 
@@ -1145,6 +1146,11 @@ int cw_session_profile(cw_session* s, size_t n_steps, cw_profile_row* rows, size
     cw_ctx* ctx = s->ctx;
     cudaSetDevice(ctx->device);
     CW_CUDA(cudaStreamSynchronize(ctx->stream));
+    std::map<std::string, std::pair<uint32_t, double>> agg;
+    if (s->plan) {  // persistent step: stage spans from in-kernel timestamps
+        CW_TRY(step_profile(s, n_steps, &agg));
+        return profile_rows(agg, rows, cap, n_rows);
+    }
     // capture one decode step with an event pair around each kernel
     const bool pdl = ctx->pdl, prof = ctx->profiling;
     std::vector<ProfRec> saved;
@@ -1178,7 +1184,6 @@ int cw_session_profile(cw_session* s, size_t n_steps, cw_profile_row* rows, size
         if (rc != CW_OK) return rc;
         return set_error(CW_ERR_CUDA, "profile graph: %s", cudaGetErrorString(ce));
     }
-    std::map<std::string, std::pair<uint32_t, double>> agg;
     for (size_t it = 0; it < n_steps; it++) {
         if (s->host_pos >= s->max_seq) {
             release();
@@ -1201,15 +1206,7 @@ int cw_session_profile(cw_session* s, size_t n_steps, cw_profile_row* rows, size
         }
     }
     release();
-    std::vector<std::pair<std::string, std::pair<uint32_t, double>>> v(agg.begin(), agg.end());
-    std::sort(v.begin(), v.end(),
-              [](const auto& a, const auto& b) { return a.second.second > b.second.second; });
-    *n_rows = v.size();
-    for (size_t i = 0; i < v.size() && i < cap && rows; i++) {
-        snprintf(rows[i].kernel, sizeof rows[i].kernel, "%s", v[i].first.c_str());
-        rows[i].passes = v[i].second.first;
-        rows[i].total_ms = v[i].second.second;
-    }
+    CW_TRY(profile_rows(agg, rows, cap, n_rows));
     return check_device_status(ctx);
 }
 

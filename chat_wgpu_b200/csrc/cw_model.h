@@ -1,0 +1,88 @@
+// cw_model.h -- model and session state shared by the decode paths
+// (cw_model.cu: per-stage kernels; cw_step.cu: the persistent step kernel).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "cw_common.h"
+
+namespace cw {
+
+// Per-session device state of the generate loop (src/model/mod.rs:57-125):
+// everything a step needs to know lives here, so one captured launch
+// replays for every token.
+struct DevState {
+    int pos;                 // position of the next step
+    unsigned token;          // input token of the next step
+    int n_prompt;
+    int n_produced;
+    unsigned long long key;  // argmax accumulator of the current step
+    unsigned long long bar_base;  // grid-barrier count at the start of the step
+    unsigned done;           // CTAs that finished the current step
+    unsigned pad;
+};
+
+struct QW {  // packed Q4_0 weight
+    const uint8_t* payload = nullptr;
+    const __half* scales = nullptr;
+    int rows = 0, in_f = 0;
+    cw_buf buf = 0;
+};
+
+struct Layer {
+    float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
+    float *post_attn = nullptr, *post_ffw = nullptr, *qkv_bias = nullptr;
+    QW qkv, wo, gate_up, down;
+};
+
+struct StepPlan;  // cw_step.cu
+
+}  // namespace cw
+
+struct cw_model {
+    cw_ctx* ctx = nullptr;
+    cw_model_info info{};
+    std::vector<cw::Layer> L;
+    float* final_norm = nullptr;
+    cw::QW embed, head;
+    std::vector<cw_buf> owned;
+    const float* inv_freq = nullptr;
+};
+
+struct cw_session {
+    cw_model* m = nullptr;
+    cw_ctx* ctx = nullptr;
+    size_t max_seq = 0;
+    std::vector<cw_buf> owned;
+    float *kc = nullptr, *vc = nullptr;
+    float *hidden = nullptr, *hidden_b = nullptr, *tmp = nullptr, *qkv = nullptr, *attn = nullptr;
+    float *act = nullptr, *logits = nullptr, *xnorm = nullptr, *part = nullptr;
+    unsigned *prompt = nullptr, *toks = nullptr, *counters = nullptr;
+    cw::DevState* st = nullptr;
+    int n_splits = 1;
+    bool use_graph = true;
+    cudaGraphExec_t g_prompt = nullptr, g_decode = nullptr;
+    size_t host_pos = 0, n_prompt = 0, n_produced = 0;
+    unsigned* h_tok = nullptr;     // pinned, one token for per-step reads
+    unsigned* h_tok_in = nullptr;  // pinned, one token for per-step writes
+    // persistent step kernel (cw_step.cu); null when the model is not eligible
+    cw::StepPlan* plan = nullptr;
+    bool use_persistent = true;
+    unsigned long long* bar = nullptr;  // grid-barrier counter (monotonic)
+};
+
+namespace cw {
+
+// cw_step.cu: persistent one-launch-per-step decode.
+bool step_supported(const cw_model* m, const cw_session* s);
+int step_plan_create(cw_session* s);
+void step_plan_free(cw_session* s);
+int step_enqueue(cw_session* s, bool decode);
+int step_profile(cw_session* s, size_t n_steps,
+                 std::map<std::string, std::pair<uint32_t, double>>* agg);
+
+}  // namespace cw

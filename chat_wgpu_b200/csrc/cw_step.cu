@@ -1,0 +1,1129 @@
+// cw_step.cu -- the persistent decode step: one cooperative launch per token.
+//
+// The step of src/model/qwen3.rs:128-191 + mod.rs:93-122 (embed, per layer
+// norm+QKV, QK-norm+RoPE+attention, o-proj+residual, norm+gate/up+SwiGLU,
+// down+residual, then norm+LM head+argmax and the next-input bookkeeping) runs
+// as a list of stages inside ONE kernel with one CTA per SM (16 warps).
+// Consecutive stages are separated by a grid-wide barrier (a monotonic 64-bit
+// counter, bounded wait); no kernel boundary, launch latency or grid drain
+// sits between stages.
+//
+// Weight streaming is decoupled from that dependency chain: every CTA knows
+// which weight chunks (16 KB of consecutive rows) it will consume in all the
+// GEMV stages of the step, in order.  Its thread 0 keeps an 8-slot ring of
+// shared memory filled with cp.async.bulk copies of the NEXT chunks in that
+// sequence, refilling a slot as soon as it is consumed, so copies for the
+// following stages (about two layers ahead) are in flight while the CTA waits
+// at a barrier.  The GEMV arithmetic is the q24 dp4a scheme of cw_gemv.cuh.
+//
+// Cross-CTA data (hidden, q/k/v, attention output, activations, partials) is
+// read with ld.global.cg so a stale L1 line can never be used.  All waits are
+// bounded by %globaltimer; a timeout sets the status word, every CTA drains
+// its copies and leaves, and the host reports CW_ERR_TIMEOUT.
+#include <algorithm>
+#include <cstdlib>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "cw_attn.cuh"
+#include "cw_gemv.cuh"
+#include "cw_model.h"
+#include "cw_ops.h"
+
+namespace cw {
+
+constexpr int MK_THREADS = 512;
+constexpr int MK_WARPS = MK_THREADS / 32;
+constexpr int MK_SLOTS = 8;
+constexpr int MK_SLOT_PAY = 16384;  // nibble payload of one chunk
+constexpr int MK_SLOT_SC = 2048;    // its f16 scales
+constexpr int MK_SLOT_BYTES = MK_SLOT_PAY + MK_SLOT_SC;
+constexpr uint64_t MK_WAIT_NS = 2000000000ull;  // 2 s
+// profile stamps per stage and CTA: [0..3] %globaltimer (stage start, end of
+// prologue, end of main loop, end of work), [4..11] clock64 at the MK_CLK
+// points of the GEMV stages
+constexpr int MK_STAMPS = 16;
+enum {
+    CLK_START = 0,    // stage start (after the barrier)
+    CLK_AHEAD = 1,    // descriptor two stages ahead requested, K/V prefetch issued
+    CLK_LOADED = 2,   // prologue: global inputs arrived (NORM) / converted (X)
+    CLK_NORMED = 3,   // prologue: CTA-wide sum of squares done
+    CLK_Q24 = 4,      // prologue: q24 planes written
+    CLK_REGS = 5,     // planes in registers (after __syncthreads)
+    CLK_MAIN = 6,     // chunk loop done
+    CLK_END = 7,      // stage end
+    CLK_N = 8,
+    // first chunk of the main loop (extra points, reported separately)
+    CLK_WAITED = 8,   // its weights are in shared memory
+    CLK_SUMMED = 9,   // row partials complete (after __syncthreads)
+    CLK_ISSUED = 10,  // next copy issued
+};
+
+// GEMV work mapping for 16 warps (see cw_gemv.cuh): WPR warps per row, BPL
+// blocks per lane, RPW rows per warp; RC rows per chunk, RC*K/2 <= 16 KB.
+template <int WPR_, int BPL_, int RPW_>
+struct MCfg {
+    static constexpr int WPR = WPR_, BPL = BPL_, RPW = RPW_;
+    static constexpr int SLOTS = MK_WARPS / WPR;
+    static constexpr int RC = SLOTS * RPW;
+    static constexpr int NB_MAX = 32 * WPR * BPL;
+};
+using MC0 = MCfg<1, 1, 2>;  // K <= 1024:  32 rows per chunk
+using MC1 = MCfg<1, 2, 1>;  // K <= 2048:  16 rows
+using MC2 = MCfg<2, 2, 1>;  // K <= 4096:   8 rows
+using MC3 = MCfg<4, 2, 1>;  // K <= 8192:   4 rows
+using MC4 = MCfg<8, 2, 1>;  // K <= 16384:  2 rows
+
+inline int mk_cfg_for(int K) {
+    const int nb = K / 32;
+    if (nb <= MC0::NB_MAX) return 0;
+    if (nb <= MC1::NB_MAX) return 1;
+    if (nb <= MC2::NB_MAX) return 2;
+    if (nb <= MC3::NB_MAX) return 3;
+    if (nb <= MC4::NB_MAX) return 4;
+    return -1;
+}
+inline int mk_rc(int cfg) {
+    switch (cfg) {
+        case 0: return MC0::RC;
+        case 1: return MC1::RC;
+        case 2: return MC2::RC;
+        case 3: return MC3::RC;
+        default: return MC4::RC;
+    }
+}
+
+enum { SK_GEMV = 0, SK_ATTN = 1 };
+
+struct MStage {
+    int kind, cfg, pro, epi;
+    int K, N, RC, nchunks;
+    const uint8_t* payload;
+    const __half* scales;
+    const float* x;        // PRO_X input
+    const float* base;     // PRO_NORM input (null: this CTA's embedding row)
+    const float* norm_w;
+    float* xn_out;         // CTA 0 stores the normalised input here
+    float* y;
+    const float* bias;
+    // attention stage of one layer
+    const float* q_norm;
+    const float* k_norm;
+    float* kc;             // this layer's K cache [n_kv][max_seq][hd]
+    float* vc;
+};
+static_assert(sizeof(MStage) % 8 == 0, "stage descriptors are copied as u64 words");
+
+// The weight-copy schedule of one stage (nchunks 0: no weights), kept in
+// shared memory so the copy issuer never waits on a global read.
+struct MIssue {
+    const uint8_t* payload;
+    const __half* scales;
+    int nchunks, rc, nb, n;
+};
+static_assert(sizeof(MIssue) == 32, "issue entries are copied as two int4");
+
+struct MParams {
+    const MStage* stages;
+    const MIssue* issues;
+    int n_stages;
+    DevState* st;
+    int* status;
+    unsigned long long* bar;
+    const uint8_t* emb_payload;
+    const __half* emb_scales;
+    float embed_scale;
+    float* hidden;
+    const float* qkv;
+    float* attn;
+    const unsigned* prompt;
+    unsigned* toks;
+    float* part;
+    unsigned* counters;
+    const float* inv_freq;
+    int dim, n_heads, n_kv, hd, max_seq, n_splits, part_stride, decode;
+    int attn_min;  // keys per attention split before splitting further
+    float eps, scale;
+    size_t work_bytes;  // shared-memory work region (q24 + hbuf + wbuf, or attention scratch)
+    // profiling only: per stage and CTA, %globaltimer at the stage's start
+    // (after its barrier), after its input prologue, after its main loop and
+    // at the end of its work ([stage][cta][MK_STAMPS]; 0 = no work here)
+    unsigned long long* stamps;
+};
+
+// keys per attention split in the persistent step: one iteration of all
+// 16 warps (4 keys each) before a split is worth its combine
+constexpr int MK_ATTN_MIN = MK_WARPS * ATTN_U;
+constexpr int MK_PRE = 2;  // epilogue addends preloaded per stage (chunks)
+
+// per-CTA state shared by all threads
+struct MShared {
+    uint64_t full[MK_SLOTS];
+    uint64_t pol;  // L2 evict-first policy of the weight stream
+    int it_stage, it_t, issued, abort;
+    float red[32];
+    unsigned long long keys[MK_WARPS];
+};
+
+struct MCtx {
+    unsigned char* ring;
+    unsigned char* work;
+    float* emb;
+    const MIssue* iss;  // shared-memory copy of the issue table
+    float* rowred;      // 2 x 32 row partials
+    MShared* sh;
+    int seq;            // chunks consumed by this CTA so far (same in every thread)
+    int pos;
+    unsigned long long* stamp;  // this stage's stamps (profiling) or null
+};
+
+__device__ __forceinline__ void mk_clk(const MCtx& c, int k) {
+    if (c.stamp && threadIdx.x == 0) c.stamp[4 + k] = clock64();
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_volatile_i32(const int* p) {
+    int v;
+    asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Thread 0: issue the copy of this CTA's next weight chunk (in the stage
+// order) into the next ring slot.  Returns false when the step has no more.
+__device__ bool mk_issue_next(const MParams& p, MCtx& c) {
+    MShared* sh = c.sh;
+    while (sh->it_stage < p.n_stages) {
+        const MIssue& I = c.iss[sh->it_stage];
+        const long chunk = blockIdx.x + (long)sh->it_t * gridDim.x;
+        if (chunk < I.nchunks) {
+            const int slot = sh->issued % MK_SLOTS;
+            const long row0 = chunk * I.rc;
+            const int rows = (int)min((long)I.rc, (long)I.n - row0);
+            const unsigned pb = (unsigned)rows * I.nb * 16, sb = (unsigned)rows * I.nb * 2;
+            unsigned char* dst = c.ring + (size_t)slot * MK_SLOT_BYTES;
+            // the slot's previous contents were read before the __syncthreads
+            // that precedes this call (a generic-proxy read followed by an
+            // async-proxy write: ordered by that barrier, no proxy fence)
+            mbar_expect_tx(&sh->full[slot], pb + sb);
+            const uint64_t pol = sh->pol;
+            bulk_g2s_hint(dst, I.payload + (size_t)row0 * I.nb * 16, pb, &sh->full[slot], pol);
+            bulk_g2s_hint(dst + MK_SLOT_PAY, I.scales + (size_t)row0 * I.nb, sb, &sh->full[slot],
+                          pol);
+            sh->issued++;
+            sh->it_t++;
+            return true;
+        }
+        sh->it_stage++;
+        sh->it_t = 0;
+    }
+    return false;
+}
+
+// Wait (bounded) for every copy issued and not yet consumed, so no bulk copy
+// writes shared memory after the CTA has left.
+__device__ void mk_drain(MCtx& c) {
+    if (threadIdx.x == 0) {
+        for (int q = c.seq; q < c.sh->issued; q++)
+            mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS);
+    }
+    __syncthreads();
+}
+
+__device__ void mk_fail(const MParams& p, MCtx& c) {
+    if (threadIdx.x == 0) {
+        atomicExch(p.status, (int)DEV_TIMEOUT);
+        c.sh->abort = 1;
+    }
+    __syncthreads();
+}
+
+// Grid-wide barrier: arrive (release), then poll (acquire) until the counter
+// reaches `target`; the status word and the time limit are checked every 64
+// polls.
+__device__ bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long long target) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        red_release_add(p.bar, 1ull);
+        uint64_t t0 = 0;
+        int ok = 1;
+        for (unsigned it = 1; ld_acquire_u64(p.bar) < target; it++) {
+            if ((it & 63) == 0) {
+                const uint64_t now = global_ns();
+                if (t0 == 0) t0 = now;
+                if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (!ok) {
+            atomicExch(p.status, (int)DEV_TIMEOUT);
+            c.sh->abort = 1;
+        }
+    }
+    __syncthreads();
+    return c.sh->abort == 0;
+}
+
+// Stage descriptors travel global -> shared by cp.async (16 bytes per thread
+// of the loader lanes, no register staging), requested two stages ahead and
+// waited for at the end of the current stage, so no thread ever stalls on
+// the descriptor table.
+constexpr int MK_LOADER = MK_THREADS - 32;  // first thread of the loader lanes (last warp)
+static_assert(sizeof(MStage) / 16 <= 32, "one 16-byte piece per loader lane");
+__device__ __forceinline__ void mk_load_stage(const MParams& p, int si, MStage* dst) {
+    const int l = threadIdx.x - MK_LOADER;
+    if (si < p.n_stages && l >= 0 && l < (int)(sizeof(MStage) / 16)) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         smem_addr(reinterpret_cast<char*>(dst) + 16 * l)),
+                     "l"(reinterpret_cast<const char*>(p.stages + si) + 16 * l)
+                     : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+}
+__device__ __forceinline__ void mk_load_stage_wait() {
+    if (threadIdx.x >= MK_LOADER) asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// q24 conversion of the valid blocks among b0 + k*stride (k < B; a
+// warp-uniform bound, valid ones first), one element per lane each: the
+// q24_block arithmetic, two blocks at a time so their reductions overlap.
+template <int B>
+__device__ __forceinline__ void mk_q24_blocks(const Q24& s, int b0, int stride, int nb,
+                                              const float (&v)[B], int lane) {
+    const int pos = q24_pos<LAYOUT_GGUF>(lane);
+    const int half = pos >> 4, off = pos & 15;
+    uint8_t* base = reinterpret_cast<uint8_t*>(s.pl);
+#pragma unroll
+    for (int k = 0; k < B; k += 2) {
+        const int ba = b0 + k * stride, bb = ba + stride;
+        if (ba >= nb) break;
+        const bool two = (k + 1 < B) && bb < nb;
+        const unsigned ma = __reduce_max_sync(FULL, __float_as_uint(fabsf(v[k])));
+        const unsigned mb =
+            two ? __reduce_max_sync(FULL, __float_as_uint(fabsf(v[k + 1 < B ? k + 1 : k]))) : 0u;
+        int Xa, Xb = 0;
+        float sa, sbb = 0.f;
+        q24_scale(ma, v[k], Xa, sa);
+        if (two) q24_scale(mb, v[k + 1 < B ? k + 1 : k], Xb, sbb);
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            const int sh = 8 * pl;
+            base[((size_t)(pl * 2 + half) * s.nb + ba) * 16 + off] = (uint8_t)((Xa >> sh) & 0xff);
+            if (two)
+                base[((size_t)(pl * 2 + half) * s.nb + bb) * 16 + off] =
+                    (uint8_t)((Xb >> sh) & 0xff);
+        }
+        const int xa = __reduce_add_sync(FULL, Xa);
+        const int xb = two ? __reduce_add_sync(FULL, Xb) : 0;
+        if (lane == 0) {
+            s.cb[ba] = 8 * xa;
+            s.sb[ba] = sa;
+            if (two) {
+                s.cb[bb] = 8 * xb;
+                s.sb[bb] = sbb;
+            }
+        }
+    }
+}
+
+constexpr int MK_PB = 8;  // prologue blocks per warp per batch
+
+// The stage input as q24 planes.  PRO_X: x from global.  PRO_NORM: rmsnorm
+// of `base` (norm.wgsl:20-56; thread t sums elements t, t+512, ... in that
+// order, as the per-stage prologue does) with the gains.  Each batch issues
+// all of its global loads before using any.
+template <int PRO>
+__device__ void mk_prologue(const MParams& p, const MStage& S, const Q24& q, float* hbuf,
+                            float* wbuf, MCtx& c) {
+    const int nb = S.K / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (PRO == PRO_X) {
+        for (int b0 = warp; b0 < nb; b0 += MK_WARPS * MK_PB) {
+            float v[MK_PB];
+#pragma unroll
+            for (int k = 0; k < MK_PB; k++) {
+                const int b = b0 + k * MK_WARPS;
+                v[k] = b < nb ? __ldcg(S.x + b * 32 + lane) : 0.f;
+            }
+            mk_q24_blocks<MK_PB>(q, b0, MK_WARPS, nb, v, lane);
+        }
+        mk_clk(c, CLK_LOADED);
+        mk_clk(c, CLK_NORMED);
+        return;
+    }
+    const float* src = S.base ? S.base : c.emb;
+    const bool gsrc = S.base != nullptr;
+    const bool wx = S.xn_out && blockIdx.x == 0;
+    float ss = 0.f;
+    if (nb <= MK_WARPS * MK_PB) {  // one batch: everything stays in registers
+        float v[MK_PB], w[MK_PB];
+#pragma unroll
+        for (int k = 0; k < MK_PB; k++) {
+            const int b = warp + k * MK_WARPS, i = b * 32 + lane;
+            v[k] = b < nb ? (gsrc ? __ldcg(src + i) : src[i]) : 0.f;
+            w[k] = b < nb ? __ldg(S.norm_w + i) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < MK_PB; k++) ss = fmaf(v[k], v[k], ss);  // padding adds +0
+        mk_clk(c, CLK_LOADED);
+        ss = gemv_cta_sum(ss, c.sh->red);
+        mk_clk(c, CLK_NORMED);
+        const float inv = 1.0f / sqrtf(ss / (float)S.K + p.eps);
+#pragma unroll
+        for (int k = 0; k < MK_PB; k++) {
+            const int b = warp + k * MK_WARPS;
+            v[k] = __fmul_rn(__fmul_rn(v[k], inv), w[k]);
+            if (wx && b < nb) S.xn_out[b * 32 + lane] = v[k];
+        }
+        mk_q24_blocks<MK_PB>(q, warp, MK_WARPS, nb, v, lane);
+        return;
+    }
+    for (int b0 = warp; b0 < nb; b0 += MK_WARPS * MK_PB) {
+        float v[MK_PB], w[MK_PB];
+#pragma unroll
+        for (int k = 0; k < MK_PB; k++) {
+            const int b = b0 + k * MK_WARPS, i = b * 32 + lane;
+            v[k] = b < nb ? (gsrc ? __ldcg(src + i) : src[i]) : 0.f;
+            w[k] = b < nb ? __ldg(S.norm_w + i) : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < MK_PB; k++) {
+            const int b = b0 + k * MK_WARPS, i = b * 32 + lane;
+            if (b < nb) {
+                hbuf[i] = v[k];
+                wbuf[i] = w[k];
+                ss = fmaf(v[k], v[k], ss);
+            }
+        }
+    }
+    mk_clk(c, CLK_LOADED);
+    ss = gemv_cta_sum(ss, c.sh->red);
+    mk_clk(c, CLK_NORMED);
+    const float inv = 1.0f / sqrtf(ss / (float)S.K + p.eps);
+    for (int b0 = warp; b0 < nb; b0 += MK_WARPS * MK_PB) {
+        float v[MK_PB];
+#pragma unroll
+        for (int k = 0; k < MK_PB; k++) {
+            const int b = b0 + k * MK_WARPS, i = b * 32 + lane;
+            v[k] = b < nb ? __fmul_rn(__fmul_rn(hbuf[i], inv), wbuf[i]) : 0.f;
+            if (wx && b < nb) S.xn_out[i] = v[k];
+        }
+        mk_q24_blocks<MK_PB>(q, b0, MK_WARPS, nb, v, lane);
+    }
+}
+
+// ---- GEMV stage ------------------------------------------------------------------
+template <class CF>
+__device__ bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
+    constexpr int WPR = CF::WPR, BPL = CF::BPL, RPW = CF::RPW, RC = CF::RC;
+    const int nb = S.K / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if ((int)blockIdx.x >= S.nchunks) return true;  // no rows of this stage here
+    // epilogue addends (old residual or bias) of the first chunks, requested
+    // now so they arrive while the prologue runs
+    const bool has_pre = S.epi == EPI_RESID || (S.epi == EPI_STORE && S.bias);
+    float pre[MK_PRE];
+#pragma unroll
+    for (int t = 0; t < MK_PRE; t++) {
+        const long row = (blockIdx.x + (long)t * gridDim.x) * RC + tid;
+        pre[t] = 0.f;
+        if (has_pre && tid < RC && row < S.N)
+            pre[t] = S.epi == EPI_RESID ? __ldcg(S.y + row) : __ldg(S.bias + row);
+    }
+    const Q24 q = q24_carve(c.work, nb);
+    float* hbuf = reinterpret_cast<float*>(c.work + al16(q24_bytes(nb)));
+    float* wbuf = hbuf + S.K;
+    if (S.pro == PRO_NORM)
+        mk_prologue<PRO_NORM>(p, S, q, hbuf, wbuf, c);
+    else
+        mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
+    mk_clk(c, CLK_Q24);
+    __syncthreads();
+    uint4 xa[BPL][3], xb[BPL][3];
+    int cbr[BPL];
+    float sbr[BPL];
+    const int wsub = warp % WPR, slot = warp / WPR;
+#pragma unroll
+    for (int k = 0; k < BPL; k++) {
+        const int b = wsub * 32 + lane + k * 32 * WPR;
+        const bool in = b < nb;
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            xa[k][pl] = in ? q.pl[(pl * 2 + 0) * nb + b] : make_uint4(0, 0, 0, 0);
+            xb[k][pl] = in ? q.pl[(pl * 2 + 1) * nb + b] : make_uint4(0, 0, 0, 0);
+        }
+        cbr[k] = in ? q.cb[b] : 0;
+        sbr[k] = in ? q.sb[b] : 0.f;
+    }
+    if (c.stamp && tid == 0) c.stamp[1] = global_ns();
+    mk_clk(c, CLK_REGS);
+    unsigned long long best = argmax_key_init();
+    int t = 0;
+    for (long chunk = blockIdx.x; chunk < S.nchunks; chunk += gridDim.x, t++) {
+        const long row0 = chunk * RC;
+        const int rows = (int)min((long)RC, (long)S.N - row0);
+        float add = 0.f;
+#pragma unroll
+        for (int u = 0; u < MK_PRE; u++)
+            if (u == t) add = pre[u];
+        if (t >= MK_PRE && has_pre && tid < rows)  // later chunks: requested before the wait
+            add = S.epi == EPI_RESID ? __ldcg(S.y + row0 + tid) : __ldg(S.bias + row0 + tid);
+        const int rs = c.seq % MK_SLOTS;
+        const unsigned par = (unsigned)((c.seq / MK_SLOTS) & 1);
+        const bool ok = mbar_wait(&c.sh->full[rs], par, MK_WAIT_NS);
+        if (__syncthreads_or(!ok)) {
+            mk_fail(p, c);
+            return false;
+        }
+        if (t == 0) mk_clk(c, CLK_WAITED);
+        const unsigned char* pay = c.ring + (size_t)rs * MK_SLOT_BYTES;
+        const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+        float* rb = c.rowred + (size_t)(c.seq & 1) * 32;
+        uint4 w4[RPW][BPL];
+        float dd[RPW][BPL];
+#pragma unroll
+        for (int j = 0; j < RPW; j++) {
+            const int r = slot * RPW + j;
+#pragma unroll
+            for (int k = 0; k < BPL; k++) {
+                const int b = wsub * 32 + lane + k * 32 * WPR;
+                const bool in = r < rows && b < nb;
+                const size_t blk = in ? (size_t)r * nb + b : 0;
+                w4[j][k] = in ? reinterpret_cast<const uint4*>(pay)[blk] : make_uint4(0, 0, 0, 0);
+                dd[j][k] = in ? __half2float(scs[blk]) : 0.f;
+            }
+        }
+        float acc[RPW];
+#pragma unroll
+        for (int j = 0; j < RPW; j++) {
+            acc[j] = 0.f;
+#pragma unroll
+            for (int k = 0; k < BPL; k++) {
+                const unsigned w[4] = {w4[j][k].x, w4[j][k].y, w4[j][k].z, w4[j][k].w};
+                const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
+                const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
+                const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
+                const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
+                const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
+                const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
+                int s0l = 0, s0h = 0, s1l = 0, s1h = 0, s2l = 0, s2h = 0;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const unsigned lo = w[e] & 0x0f0f0f0fu;
+                    const unsigned hi = (w[e] >> 4) & 0x0f0f0f0fu;
+                    s0l = dp4a_uu(lo, a0[e], s0l);
+                    s0h = dp4a_uu(hi, b0[e], s0h);
+                    s1l = dp4a_uu(lo, a1[e], s1l);
+                    s1h = dp4a_uu(hi, b1[e], s1h);
+                    s2l = dp4a_us(lo, a2[e], s2l);
+                    s2h = dp4a_us(hi, b2[e], s2h);
+                }
+                const int s01 = (s0l + s0h) + ((s1l + s1h) << 8) - cbr[k];
+                const float T = fmaf((float)(s2l + s2h), 65536.0f, (float)s01);
+                acc[j] = fmaf(dd[j][k] * sbr[k], T, acc[j]);
+            }
+        }
+        const float v = warp_reduce_rows<RPW>(acc, lane);
+        if ((lane & (32 / RPW - 1)) == 0) rb[(slot * RPW + lane / (32 / RPW)) * WPR + wsub] = v;
+        __syncthreads();  // slot consumed, row partials complete
+        if (t == 0) mk_clk(c, CLK_SUMMED);
+        if (tid == 0) mk_issue_next(p, c);
+        if (t == 0) mk_clk(c, CLK_ISSUED);
+        c.seq++;
+        // epilogue: fixed-order sum of the WPR partials of each row
+        if (S.epi == EPI_GLU) {
+            if (tid < RC / 2 && 2 * tid + 1 < rows) {
+                const int r0 = 2 * tid;
+                float gv = 0.f, uv = 0.f;
+#pragma unroll
+                for (int w = 0; w < WPR; w++) {
+                    gv += rb[r0 * WPR + w];
+                    uv += rb[(r0 + 1) * WPR + w];
+                }
+                S.y[(row0 + r0) / 2] = silu_ref_f(gv) * uv;
+            }
+        } else if (tid < rows) {
+            float vv = 0.f;
+#pragma unroll
+            for (int w = 0; w < WPR; w++) vv += rb[tid * WPR + w];
+            const long row = row0 + tid;
+            if (S.epi == EPI_HEAD) {
+                S.y[row] = vv;
+                const unsigned long long kk = argmax_key(vv, (unsigned)row);
+                best = kk > best ? kk : best;
+            } else {
+                S.y[row] = has_pre ? (S.epi == EPI_RESID ? add + vv : vv + add) : vv;
+            }
+        }
+    }
+    if (c.stamp && tid == 0) c.stamp[2] = global_ns();
+    mk_clk(c, CLK_MAIN);
+    if (S.epi == EPI_HEAD) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long tt = __shfl_xor_sync(FULL, best, o);
+            best = tt > best ? tt : best;
+        }
+        if (lane == 0) c.sh->keys[warp] = best;
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < MK_WARPS; w++) best = c.sh->keys[w] > best ? c.sh->keys[w] : best;
+            atomicMax(&p.st->key, best);
+        }
+    }
+    return true;
+}
+
+// ---- attention stage: QK-norm + RoPE + K/V write + split-KV attention -----------
+// Thread 0 of the CTA that will run attention unit blockIdx.x: pull the cached
+// K/V rows of that unit into L2 while the stage before it runs.
+__device__ void mk_kv_prefetch(const MParams& p, const MStage& A, const MCtx& c) {
+    const int seq = c.pos + 1;
+    const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
+    const int u = blockIdx.x;
+    if (u >= p.n_kv * n_active) return;
+    const int g = u % p.n_kv, split = u / p.n_kv;
+    int jlo, jhi;
+    attn_range(seq, 0, split, n_active, &jlo, &jhi);
+    const int j1 = min(jhi, c.pos);
+    if (j1 <= jlo) return;
+    const float* kb = A.kc + (size_t)g * p.max_seq * p.hd;
+    const float* vb = A.vc + (size_t)g * p.max_seq * p.hd;
+    prefetch_l2(kb + (size_t)jlo * p.hd, kb + (size_t)j1 * p.hd);
+    prefetch_l2(vb + (size_t)jlo * p.hd, vb + (size_t)j1 * p.hd);
+}
+
+template <int EPL, int GMAX>
+__device__ bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
+    const int G = p.n_heads / p.n_kv, hd = p.hd, half = hd / 2;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pos = c.pos, seq = pos + 1;
+    const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
+    const int units = p.n_kv * n_active;
+    const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
+    float* sm = reinterpret_cast<float*>(c.work);
+    float* res = sm + (size_t)MK_WARPS * G * (hd + 2);
+    float* cwt = sm + (size_t)(MK_WARPS + 1) * G * (hd + 2);
+    float* qs = cwt + (size_t)G * (p.n_splits + 1);
+    float* ks = qs + (size_t)G * hd;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int g = u % p.n_kv, split = u / p.n_kv;
+        int jlo, jhi;
+        attn_range(seq, 0, split, n_active, &jlo, &jhi);
+        const bool holds = pos >= jlo && pos < jhi;
+        const int nrows = G + (holds ? 1 : 0);  // <= 5 rows, one per warp
+        // every global input of the prologue is requested before any is used:
+        // this warp's q/k row and its norm gains, the new V row, the RoPE
+        // frequency of this thread's first rotated pair
+        const int r = warp;
+        const bool isq = r < G, has_row = r < nrows;
+        const float* nw = isq ? S.q_norm : S.k_norm;
+        float vv[EPL], wv[EPL];
+        {
+            const float* src = isq ? p.qkv + (size_t)(g * G + r) * hd : p.qkv + qd + (size_t)g * hd;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const int d = lane + 32 * e;
+                const bool in = has_row && d < hd;
+                vv[e] = in ? __ldcg(src + d) : 0.f;
+                wv[e] = (in && nw) ? __ldg(nw + d) : 0.f;
+            }
+        }
+        const float vnew = (holds && tid < hd) ? __ldcg(p.qkv + qd + kvd + (size_t)g * hd + tid) : 0.f;
+        float sn0 = 0.f, cs0 = 1.f;
+        if (tid < nrows * half) sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid % half)), &sn0, &cs0);
+        if (has_row) {  // QK-norm (qwen3.rs:154-155)
+            float* dst = isq ? qs + (size_t)r * hd : ks;
+            if (nw) {
+                float ss = 0.f;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) ss = fmaf(vv[e], vv[e], ss);
+                ss = warp_sum(ss);
+                const float inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
+#pragma unroll
+                for (int e = 0; e < EPL; e++) vv[e] = __fmul_rn(__fmul_rn(vv[e], inv), wv[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const int d = lane + 32 * e;
+                if (d < hd) dst[d] = vv[e];
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < nrows * half; i += blockDim.x) {  // RoPE (rope.wgsl:25-34)
+            const int rr = i / half, kq = i - rr * half;
+            float* row = rr < G ? qs + (size_t)rr * hd : ks;
+            float sn = sn0, cs = cs0;
+            if (i != tid) sincosf(__fmul_rn((float)pos, p.inv_freq[kq]), &sn, &cs);
+            const float lo = row[kq], hi = row[kq + half];
+            row[kq] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
+            row[kq + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+        }
+        __syncthreads();
+        float* kbase = S.kc + (size_t)g * p.max_seq * hd;
+        float* vbase = S.vc + (size_t)g * p.max_seq * hd;
+        if (holds && tid < hd) {  // cache.rs:21-24
+            kbase[(size_t)pos * hd + tid] = ks[tid];
+            vbase[(size_t)pos * hd + tid] = vnew;
+        }
+        __syncthreads();
+        if (c.stamp && tid == 0) c.stamp[1] = global_ns();
+        attn_core<EPL, GMAX, KV_CG, MK_WARPS>(qs, G, hd, kbase, vbase, hd, jlo, jhi, p.scale, 0.f,
+                                              sm, res);
+        if (c.stamp && tid == 0) c.stamp[2] = global_ns();
+        attn_finish(res, G, hd, g, split, n_active, p.part_stride, p.part, p.counters, p.attn, cwt);
+        __syncthreads();
+    }
+    return true;
+}
+
+template <int EPL, int GMAX>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ MShared sh;
+    __shared__ float rowred[64];
+    __shared__ __align__(16) MStage sst[3];  // stage si in sst[si % 3], two fetched ahead
+    MCtx c;
+    c.sh = &sh;
+    c.ring = smem;
+    c.work = smem + (size_t)MK_SLOTS * MK_SLOT_BYTES;
+    c.emb = reinterpret_cast<float*>(c.work + p.work_bytes);
+    MIssue* iss = reinterpret_cast<MIssue*>(c.work + p.work_bytes + al16((size_t)p.dim * 4));
+    c.iss = iss;
+    c.rowred = rowred;
+    c.seq = 0;
+    c.stamp = nullptr;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < MK_SLOTS; s++) mbar_init(&sh.full[s], 1);
+        fence_mbar_init();
+        sh.it_stage = 0;
+        sh.it_t = 0;
+        sh.issued = 0;
+        sh.abort = 0;
+        sh.pol = l2_evict_first();
+    }
+    for (int i = tid; i < p.n_stages * 2; i += blockDim.x)
+        reinterpret_cast<int4*>(iss)[i] = reinterpret_cast<const int4*>(p.issues)[i];
+    mk_load_stage(p, 0, &sst[0]);
+    mk_load_stage(p, 1, &sst[1]);
+    mk_load_stage_wait();
+    const int pos = p.st->pos;
+    const unsigned tok = p.st->token;
+    const unsigned long long base = p.st->bar_base;
+    c.pos = pos;
+    __syncthreads();
+    if (tid == 0)  // the first ring-full of weights
+        for (int s = 0; s < MK_SLOTS; s++)
+            if (!mk_issue_next(p, c)) break;
+    // embedding row (qwen3.rs:128-133), every CTA its own copy
+    {
+        const int nb = p.dim / 32;
+        for (int i = tid; i < p.dim; i += blockDim.x) {
+            const int b = i >> 5, j = i & 31;
+            const size_t blk = (size_t)tok * nb + b;
+            const float d = __half2float(p.emb_scales[blk]);
+            const uint8_t byte = p.emb_payload[blk * 16 + (j & 15)];
+            const int qv = (j < 16) ? (byte & 0xf) : (byte >> 4);
+            float v = __fmul_rn(d, (float)(qv - 8));
+            if (p.embed_scale > 0.f) v = __fmul_rn(v, p.embed_scale);
+            c.emb[i] = v;
+            if (blockIdx.x == 0) p.hidden[i] = v;
+        }
+        __syncthreads();
+    }
+    bool ok = true;
+    for (int si = 0; si < p.n_stages && ok; si++) {
+        if (si > 0) ok = mk_grid_sync(p, c, base + (unsigned long long)si * gridDim.x);
+        if (!ok) break;
+        unsigned long long* stamp =
+            p.stamps ? p.stamps + ((size_t)si * gridDim.x + blockIdx.x) * MK_STAMPS : nullptr;
+        c.stamp = stamp;
+        if (stamp && tid == 0) stamp[0] = global_ns();
+        mk_clk(c, CLK_START);
+        mk_load_stage(p, si + 2, &sst[(si + 2) % 3]);  // waited for at the stage end
+        const MStage& S = sst[si % 3];
+        const MStage& S1 = sst[(si + 1) % 3];
+        if (tid == 0 && si + 1 < p.n_stages && S1.kind == SK_ATTN) mk_kv_prefetch(p, S1, c);
+        mk_clk(c, CLK_AHEAD);
+        if (S.kind == SK_ATTN) {
+            ok = mk_attn<EPL, GMAX>(p, S, c);
+        } else {
+            switch (S.cfg) {
+                case 0: ok = mk_gemv<MC0>(p, S, c); break;
+                case 1: ok = mk_gemv<MC1>(p, S, c); break;
+                case 2: ok = mk_gemv<MC2>(p, S, c); break;
+                case 3: ok = mk_gemv<MC3>(p, S, c); break;
+                default: ok = mk_gemv<MC4>(p, S, c); break;
+            }
+        }
+        mk_load_stage_wait();  // made visible by the barrier's __syncthreads
+        if (stamp) {
+            __syncthreads();
+            if (tid == 0) stamp[3] = global_ns();
+            mk_clk(c, CLK_END);
+        }
+    }
+    mk_load_stage_wait();
+    mk_drain(c);
+    if (!ok || sh.abort) return;
+    // the last CTA to finish does the generate-loop bookkeeping (mod.rs:114-122)
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(&p.st->done, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence();
+            DevState* st = p.st;
+            unsigned next;
+            if (pos + 1 < st->n_prompt) {
+                next = p.prompt[pos + 1];
+            } else {
+                const unsigned long long k = atomicMax(&st->key, 0ull);
+                const unsigned t = p.decode ? argmax_key_index(k) : 0u;
+                p.toks[st->n_produced] = t;
+                st->n_produced = st->n_produced + 1;
+                next = t;
+            }
+            st->key = argmax_key_init();
+            st->token = next;
+            st->pos = pos + 1;
+            st->done = 0;
+            st->bar_base = base + (unsigned long long)(p.n_stages - 1) * gridDim.x;
+            __threadfence();
+        }
+    }
+}
+
+// ---- host ---------------------------------------------------------------------------
+struct StepPlan {
+    std::vector<const char*> names;  // stage names, for the profile
+    MStage* d_stages = nullptr;
+    int n_stages = 0;  // decode step (prompt steps drop the final LM-head stage)
+    MParams params{};
+    size_t smem = 0;
+    int grid = 0;
+    int epl = 0, gmax = 0;
+    void (*kern)(MParams) = nullptr;
+};
+
+static void (*pick_kernel(int epl, int gmax))(MParams) {
+#define CW_MK(E, G) \
+    if (epl == E && gmax == G) return k_step<E, G>;
+    CW_MK(1, 1) CW_MK(1, 2) CW_MK(1, 4)
+    CW_MK(2, 1) CW_MK(2, 2) CW_MK(2, 4)
+    CW_MK(4, 1) CW_MK(4, 2) CW_MK(4, 4)
+    CW_MK(8, 1) CW_MK(8, 2) CW_MK(8, 4)
+#undef CW_MK
+    return nullptr;
+}
+
+static size_t work_bytes_for(const cw_model_info& I, int n_splits) {
+    const int G = I.n_heads / I.n_kv, hd = I.head_dim;
+    const int kmax = std::max<int>(I.dim, std::max<int>(I.n_heads * I.head_dim, I.hidden));
+    // PRO_X: q24 planes of K <= kmax; PRO_NORM (K = dim): planes + hbuf + wbuf
+    const size_t gemv = std::max(al16(q24_bytes(kmax / 32)),
+                                 al16(q24_bytes((int)I.dim / 32)) + (size_t)I.dim * 8);
+    const size_t attn = (attn_smem_floats(G, hd, n_splits, MK_WARPS) + (size_t)G * hd + hd) * 4;
+    return al16(std::max(gemv, attn));
+}
+
+bool step_supported(const cw_model* m, const cw_session* s) {
+    const cw_model_info& I = m->info;
+    if (I.post_norms || I.sliding_window || I.attn_softcap > 0.f || I.final_softcap > 0.f ||
+        I.activation != 0 || I.norm_kind != 0)
+        return false;
+    const int G = I.n_heads / I.n_kv;
+    const int epl = (I.head_dim + 31) / 32;
+    const int gmax = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+    if (!pick_kernel(epl, gmax) || I.head_dim % 32) return false;
+    const int ks[3] = {(int)I.dim, (int)(I.n_heads * I.head_dim), (int)I.hidden};
+    for (int K : ks)
+        if (K % 256 || mk_cfg_for(K) < 0) return false;
+    (void)s;
+    return true;
+}
+
+int step_plan_create(cw_session* s) {
+    cw_model* m = s->m;
+    cw_ctx* ctx = s->ctx;
+    const cw_model_info& I = m->info;
+    if (!step_supported(m, s)) return CW_ERR_UNSUPPORTED;
+    std::unique_ptr<StepPlan> P(new StepPlan());
+    const int G = I.n_heads / I.n_kv;
+    P->epl = (I.head_dim + 31) / 32;
+    P->gmax = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+    P->kern = pick_kernel(P->epl, P->gmax);
+    const int grid = ctx->sm_count;
+    const int n_splits = std::max(1, std::min(s->n_splits, grid / (int)I.n_kv));
+    // ---- stage list and its weight-copy schedule
+    std::vector<MStage> st;
+    std::vector<MIssue> is;
+    auto gemv = [&](const char* name, const QW& w, int pro, int epi, const float* x,
+                    const float* base, const float* norm_w, float* y, const float* bias,
+                    float* xn_out) {
+        P->names.push_back(name);
+        MStage S = {};
+        S.kind = SK_GEMV;
+        S.cfg = mk_cfg_for(w.in_f);
+        S.pro = pro;
+        S.epi = epi;
+        S.K = w.in_f;
+        S.N = w.rows;
+        S.RC = mk_rc(S.cfg);
+        S.nchunks = (S.N + S.RC - 1) / S.RC;
+        S.payload = w.payload;
+        S.scales = w.scales;
+        S.x = x;
+        S.base = base;
+        S.norm_w = norm_w;
+        S.y = y;
+        S.bias = bias;
+        S.xn_out = xn_out;
+        st.push_back(S);
+        is.push_back(MIssue{S.payload, S.scales, S.nchunks, S.RC, S.K / 32, S.N});
+    };
+    for (uint32_t li = 0; li < I.n_layers; li++) {
+        const Layer& l = m->L[li];
+        gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, nullptr, li == 0 ? nullptr : s->hidden,
+             l.attn_norm, s->qkv, l.qkv_bias, nullptr);
+        P->names.push_back("attention");
+        MStage A = {};
+        A.kind = SK_ATTN;
+        A.q_norm = l.q_norm;
+        A.k_norm = l.k_norm;
+        A.kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
+        A.vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
+        st.push_back(A);
+        is.push_back(MIssue{nullptr, nullptr, 0, 0, 0, 0});
+        gemv("attn_out", l.wo, PRO_X, EPI_RESID, s->attn, nullptr, nullptr, s->hidden, nullptr,
+             nullptr);
+        gemv("ffn_in", l.gate_up, PRO_NORM, EPI_GLU, nullptr, s->hidden, l.ffn_norm, s->act,
+             nullptr, nullptr);
+        gemv("ffn_out", l.down, PRO_X, EPI_RESID, s->act, nullptr, nullptr, s->hidden, nullptr,
+             nullptr);
+    }
+    gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, s->hidden, m->final_norm, s->logits,
+         nullptr, s->xnorm);
+    P->n_stages = (int)st.size();
+    // ---- shared memory: ring | work | embedding row | issue table
+    const size_t work = work_bytes_for(I, n_splits);
+    P->smem = (size_t)MK_SLOTS * MK_SLOT_BYTES + work + al16((size_t)I.dim * 4) +
+              is.size() * sizeof(MIssue);
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, P->kern);
+    if (e == cudaSuccess && (long)(P->smem + fa.sharedSizeBytes) > (long)ctx->max_smem_optin)
+        return set_error(CW_ERR_UNSUPPORTED,
+                         "persistent step needs %zu + %zu bytes of shared memory (max %d)", P->smem,
+                         (size_t)fa.sharedSizeBytes, ctx->max_smem_optin);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(P->kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)P->smem);
+    int per_sm = 0;
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, P->kern, MK_THREADS, P->smem);
+    if (e != cudaSuccess || per_sm < 1)
+        return set_error(CW_ERR_UNSUPPORTED, "persistent step cannot be resident: %s",
+                         cudaGetErrorString(e));
+    P->grid = grid;
+    const size_t sb = st.size() * sizeof(MStage), ib = is.size() * sizeof(MIssue);
+    e = cudaMalloc(&P->d_stages, sb + ib);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(P->d_stages, st.data(), sb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(reinterpret_cast<char*>(P->d_stages) + sb, is.data(), ib,
+                       cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        if (P->d_stages) cudaFree(P->d_stages);
+        return set_error(CW_ERR_CUDA, "persistent step plan: %s", cudaGetErrorString(e));
+    }
+    MParams& pp = P->params;
+    pp.stages = P->d_stages;
+    pp.issues = reinterpret_cast<const MIssue*>(reinterpret_cast<char*>(P->d_stages) + sb);
+    pp.st = s->st;
+    pp.status = ctx->d_status;
+    pp.bar = s->bar;
+    pp.emb_payload = m->embed.payload;
+    pp.emb_scales = m->embed.scales;
+    pp.embed_scale = I.embed_scale;
+    pp.hidden = s->hidden;
+    pp.qkv = s->qkv;
+    pp.attn = s->attn;
+    pp.prompt = s->prompt;
+    pp.toks = s->toks;
+    pp.part = s->part;
+    pp.counters = s->counters;
+    pp.inv_freq = m->inv_freq;
+    pp.dim = (int)I.dim;
+    pp.n_heads = (int)I.n_heads;
+    pp.n_kv = (int)I.n_kv;
+    pp.hd = (int)I.head_dim;
+    pp.max_seq = (int)s->max_seq;
+    pp.n_splits = n_splits;
+    pp.part_stride = s->n_splits;
+    pp.attn_min = MK_ATTN_MIN;
+    if (const char* ev = getenv("CW_ATTN_MIN_KEYS")) {  // tuning knob
+        const int v = atoi(ev);
+        if (v >= 1) pp.attn_min = v;
+    }
+    pp.eps = I.eps;
+    pp.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
+    pp.work_bytes = work;
+    s->plan = P.release();
+    return CW_OK;
+}
+
+void step_plan_free(cw_session* s) {
+    if (!s->plan) return;
+    if (s->plan->d_stages) cudaFree(s->plan->d_stages);
+    delete s->plan;
+    s->plan = nullptr;
+}
+
+static int step_launch(cw_session* s, bool decode, unsigned long long* stamps) {
+    StepPlan* P = s->plan;
+    MParams pp = P->params;
+    pp.stamps = stamps;
+    pp.decode = decode ? 1 : 0;
+    pp.n_stages = decode ? P->n_stages : P->n_stages - 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)P->grid);
+    cfg.blockDim = dim3(MK_THREADS);
+    cfg.dynamicSmemBytes = P->smem;
+    cfg.stream = s->ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    std::unique_ptr<OpScope> sc;
+    if (s->ctx->profiling) sc.reset(new OpScope(s->ctx, "decode_step"));
+    CW_CUDA(cudaLaunchKernelEx(&cfg, P->kern, pp));
+    return CW_OK;
+}
+
+int step_enqueue(cw_session* s, bool decode) { return step_launch(s, decode, nullptr); }
+
+// Stage breakdown of n_steps decode steps from the in-kernel stamps: per
+// stage, the span from its first CTA's start to its last CTA's end ("work",
+// under the stage name) and from there to the next stage's first start
+// ("grid_barrier"); "decode_step" is the CUDA-event time of the launch.
+int step_profile(cw_session* s, size_t n_steps,
+                 std::map<std::string, std::pair<uint32_t, double>>* agg) {
+    StepPlan* P = s->plan;
+    cw_ctx* ctx = s->ctx;
+    const size_t n = (size_t)P->n_stages * P->grid * MK_STAMPS;
+    unsigned long long* d = nullptr;
+    CW_CUDA(cudaMalloc(&d, n * 8));
+    std::vector<unsigned long long> h(n);
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = CW_OK;
+    if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess)
+        rc = set_error(CW_ERR_CUDA, "profile events");
+    for (size_t it = 0; it < n_steps && rc == CW_OK; it++) {
+        if (s->host_pos >= s->max_seq) {
+            rc = set_error(CW_ERR_INVALID_ARG, "session is full: position %zu", s->host_pos);
+            break;
+        }
+        cudaMemsetAsync(d, 0, n * 8, ctx->stream);
+        cudaEventRecord(e0, ctx->stream);
+        rc = step_launch(s, true, d);
+        if (rc != CW_OK) break;
+        cudaEventRecord(e1, ctx->stream);
+        cudaError_t e = cudaMemcpyAsync(h.data(), d, n * 8, cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) {
+            rc = set_error(CW_ERR_CUDA, "profile step: %s", cudaGetErrorString(e));
+            break;
+        }
+        rc = check_device_status(ctx);
+        if (rc != CW_OK) break;
+        s->host_pos++;
+        s->n_produced++;
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        auto& a = (*agg)["decode_step"];
+        a.first += 1;
+        a.second += ms;
+        unsigned long long prev_end = 0;
+        for (int si = 0; si < P->n_stages; si++) {
+            unsigned long long t0 = ~0ull, t1 = 0;
+            double ph[3] = {0, 0, 0};
+            int nw = 0;
+            for (int b = 0; b < P->grid; b++) {
+                const unsigned long long* q = &h[((size_t)si * P->grid + b) * MK_STAMPS];
+                t0 = std::min(t0, q[0]);
+                t1 = std::max(t1, q[3]);
+                if (q[1] && q[2]) {  // a CTA with work in this stage: its phases
+                    ph[0] += (double)(q[1] - q[0]);
+                    ph[1] += (double)(q[2] - q[1]);
+                    ph[2] += (double)(q[3] - q[2]);
+                    nw++;
+                }
+            }
+            auto& w = (*agg)[P->names[si]];
+            w.first += 1;
+            w.second += (double)(t1 - t0) * 1e-6;
+            static const char* phase[3] = {"prologue", "main", "epilogue"};
+            for (int k = 0; k < 3 && nw; k++) {
+                auto& r = (*agg)[std::string(P->names[si]) + "." + phase[k]];
+                r.first += 1;
+                r.second += ph[k] / nw * 1e-6;
+            }
+            // GEMV stages: SM-clock intervals between the CLK points
+            static const char* clk[CLK_N - 1] = {"ahead", "loaded", "normed", "q24",
+                                                 "regs", "main", "end"};
+            double cl[CLK_N - 1] = {0};
+            int nc = 0;
+            for (int b = 0; b < P->grid; b++) {
+                const unsigned long long* q = &h[((size_t)si * P->grid + b) * MK_STAMPS + 4];
+                if (!q[CLK_REGS] || !q[CLK_START]) continue;
+                for (int k = 0; k < CLK_N - 1; k++) cl[k] += (double)(q[k + 1] - q[k]);
+                nc++;
+            }
+            for (int k = 0; k < CLK_N - 1 && nc; k++) {
+                auto& r = (*agg)[std::string(P->names[si]) + ":" + clk[k]];
+                r.first += 1;
+                r.second += cl[k] / nc / (double)ctx->clock_khz;  // cycles -> ms
+            }
+            // first chunk: regs -> waited -> summed -> issued
+            static const char* ck[3] = {"1st_wait", "1st_math", "1st_issue"};
+            double c3[3] = {0, 0, 0};
+            int n3 = 0;
+            for (int b = 0; b < P->grid; b++) {
+                const unsigned long long* q = &h[((size_t)si * P->grid + b) * MK_STAMPS + 4];
+                if (!q[CLK_REGS] || !q[CLK_ISSUED]) continue;
+                c3[0] += (double)(q[CLK_WAITED] - q[CLK_REGS]);
+                c3[1] += (double)(q[CLK_SUMMED] - q[CLK_WAITED]);
+                c3[2] += (double)(q[CLK_ISSUED] - q[CLK_SUMMED]);
+                n3++;
+            }
+            for (int k = 0; k < 3 && n3; k++) {
+                auto& r = (*agg)[std::string(P->names[si]) + ":" + ck[k]];
+                r.first += 1;
+                r.second += c3[k] / n3 / (double)ctx->clock_khz;
+            }
+            if (si > 0) {
+                auto& g = (*agg)["grid_barrier"];
+                g.first += 1;
+                g.second += (double)(t0 - prev_end) * 1e-6;
+            }
+            prev_end = t1;
+        }
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaFree(d);
+    return rc;
+}
+
+}  // namespace cw

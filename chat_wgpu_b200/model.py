@@ -81,6 +81,17 @@ class Session:
     def set_graph(self, use_graph: bool) -> None:
         _lib.call("cw_session_set_graph", self._h, 1 if use_graph else 0)
 
+    def set_persistent(self, on: bool) -> None:
+        """Select the step kernel: one persistent cooperative launch per token
+        (default where the family is covered) or one kernel per stage."""
+        _lib.call("cw_session_set_persistent", self._h, 1 if on else 0)
+
+    @property
+    def persistent(self) -> bool:
+        v = C.c_int()
+        _lib.call("cw_session_persistent", self._h, C.byref(v))
+        return bool(v.value)
+
     def begin(self, prompt) -> None:
         p = np.ascontiguousarray(prompt, dtype=np.uint32)
         _lib.call("cw_session_begin", self._h, p.ctypes.data, p.size)

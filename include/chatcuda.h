@@ -245,6 +245,15 @@ int cw_session_hidden(cw_session* s, float* out, size_t dim);
 /* Per-step path selection: 1 = one CUDA graph per token (default),
  * 0 = direct launches (debug). */
 int cw_session_set_graph(cw_session* s, int use_graph);
+/* Step kernel selection (no reference counterpart: the reference always
+ * dispatches one compute pass per op).  1 = the whole step as ONE persistent
+ * cooperative launch (default for families it covers: no post-norms, no
+ * sliding window, no soft-caps, RMSNorm, SwiGLU, dim/q-dim/hidden multiples
+ * of 256); 0 = one kernel per stage.  Returns CW_ERR_UNSUPPORTED when 1 is
+ * asked for a family it does not cover.  cw_session_persistent reports the
+ * path in use. */
+int cw_session_set_persistent(cw_session* s, int on);
+int cw_session_persistent(cw_session* s, int* on);
 /* One step with a host round trip, the shape of the reference's loop body
  * (mod.rs:93-103): the input token is copied from the host (token_in, or
  * CW_TOKEN_DEVICE to keep the device-side feedback), the step runs, and the

@@ -39,10 +39,12 @@ def compare_streams(got_toks, ref_toks, ref_logits, got_logits=None):
     return n
 
 
-def session_stream(model, prompt, max_new, use_graph=True):
+def session_stream(model, prompt, max_new, use_graph=True, persistent=None):
     from chat_wgpu_b200.model import Session
     s = Session(model, len(prompt) + max_new)
     s.set_graph(use_graph)
+    if persistent is not None:
+        s.set_persistent(persistent)
     s.begin(prompt)
     s.run(len(prompt) - 1)  # prompt positions (no lm_head)
     logits = []
@@ -64,9 +66,17 @@ def models(tmp_path_factory):
     return out
 
 
+# families the persistent one-launch step covers (the others always use the
+# per-stage kernels)
+PERSISTENT = {"tiny-qwen3": False, "small-qwen3": True, "tiny-gemma2": False, "tiny-qwen2": True}
+
+
+@pytest.mark.parametrize("persistent", [False, True], ids=["per-stage", "persistent"])
 @pytest.mark.parametrize("name", ["tiny-qwen3", "small-qwen3", "tiny-gemma2", "tiny-qwen2"])
-def test_fused_session_vs_oracle(ctx, orc, models, name):
+def test_fused_session_vs_oracle(ctx, orc, models, name, persistent):
     from chat_wgpu_b200.model import Model
+    if persistent and not PERSISTENT[name]:
+        pytest.skip("family not covered by the persistent step")
     path = models[name]
     om = orc.Model(path)
     prompt = np.array([1, 5, 9, 2, 77, 3, 41, 8, 100, 6][: 4 if name == "tiny-qwen3" else 10],
@@ -74,7 +84,7 @@ def test_fused_session_vs_oracle(ctx, orc, models, name):
     max_new = 24
     ref_toks, ref_logits = om.generate(prompt, max_new, want_logits=True)
     m = Model(ctx, path)
-    toks, logits = session_stream(m, prompt, max_new)
+    toks, logits = session_stream(m, prompt, max_new, persistent=persistent)
     n = compare_streams(toks, ref_toks, ref_logits, logits)
     assert n >= 4, f"only {n} steps compared"
     m.close()
@@ -90,6 +100,51 @@ def test_graph_equals_direct_launch(ctx, models):
     assert np.array_equal(t1, t2)
     assert np.array_equal(l1.view(np.uint32), l2.view(np.uint32))
     m.close()
+
+
+@pytest.mark.parametrize("name", ["tiny-qwen3", "small-qwen3", "tiny-gemma2", "tiny-qwen2"])
+def test_persistent_default_and_coverage(ctx, models, name):
+    """The persistent step is the default where the family is covered; asking
+    for it elsewhere fails loudly; one launch per step when it is used."""
+    from chat_wgpu_b200 import CwError
+    from chat_wgpu_b200.model import Model, Session
+    m = Model(ctx, models[name])
+    s = Session(m, 16)
+    assert s.persistent == PERSISTENT[name]
+    if PERSISTENT[name]:
+        assert s.launches() == (1, 1)
+        s.set_persistent(False)
+        assert not s.persistent and s.launches()[1] > 1
+        s.set_persistent(True)
+        assert s.persistent
+    else:
+        with pytest.raises(CwError):
+            s.set_persistent(True)
+        assert not s.persistent
+    s.close()
+    m.close()
+
+
+def test_persistent_equals_per_stage_long(ctx, orc, models):
+    """A 200-token prompt and 40 generated tokens on small-qwen3: the attention
+    stage runs with many active key splits.  Persistent and per-stage paths
+    both within tolerance of the oracle; persistent graph == direct, bit-exact."""
+    from chat_wgpu_b200.model import Model
+    path = models["small-qwen3"]
+    om = orc.Model(path)
+    rng = np.random.default_rng(11)
+    prompt = rng.integers(0, om.vocab, 200).astype(np.uint32)
+    ref_toks, ref_logits = om.generate(prompt, 40, want_logits=True)
+    m = Model(ctx, path)
+    tp, lp = session_stream(m, prompt, 40, persistent=True)
+    ts, ls = session_stream(m, prompt, 40, persistent=False)
+    assert compare_streams(tp, ref_toks, ref_logits, lp) >= 4
+    assert compare_streams(ts, ref_toks, ref_logits, ls) >= 4
+    td, ld = session_stream(m, prompt, 40, use_graph=False, persistent=True)
+    assert np.array_equal(tp, td)
+    assert np.array_equal(lp.view(np.uint32), ld.view(np.uint32))
+    m.close()
+    om.close()
 
 
 def test_generate_api_matches_session(ctx, orc, models):
@@ -155,5 +210,8 @@ def test_full_size_qwen3_0_6b(ctx, orc):
     toks2, logits2 = session_stream(m, prompt, 4)
     assert np.array_equal(toks, toks2)
     assert np.array_equal(logits.view(np.uint32), logits2.view(np.uint32))
+    # the per-stage kernels on the same checkpoint
+    toks3, logits3 = session_stream(m, prompt, 4, persistent=False)
+    assert compare_streams(toks3, ref_toks, ref_logits, logits3) >= 1
     m.close()
     om.close()
