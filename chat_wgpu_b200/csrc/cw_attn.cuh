@@ -23,7 +23,7 @@ constexpr int ATTN_U = 4;                     // keys per warp iteration
 // Shared memory floats needed by attn_core + attn_finish for G heads of dim
 // hd, up to n_splits splits and NW warps.
 __host__ __device__ constexpr size_t attn_smem_floats(int G, int hd, int n_splits, int NW = 4) {
-    return (size_t)(NW + 1) * G * (hd + 2) + (size_t)G * (n_splits + 1);
+    return (size_t)(NW + 1) * G * (hd + 2) + (size_t)G * NW + (size_t)G * (n_splits + 1);
 }
 
 // K/V load paths: read-only cache (rows written by earlier launches), plain,
@@ -154,25 +154,31 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
         }
     }
     __syncthreads();
-    // merge the NW warp states (the merge rule of attention.wgsl:88-95)
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-        int gi = i / hd, d = i - gi * hd;
-        float M = REF_NEG_INF;
-#pragma unroll
-        for (int w = 0; w < NW; w++) M = fmaxf(M, sm[(size_t)(w * G + gi) * W + hd]);
-        float L = 0.f, A = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; w++) {
-            const float* src = sm + (size_t)(w * G + gi) * W;
-            float c = expf(src[hd] - M);
-            L += src[hd + 1] * c;
-            A += src[d] * c;
-        }
-        res[gi * W + d] = A;
-        if (d == 0) {
+    // merge the NW warp states (the merge rule of attention.wgsl:88-95): per
+    // head, warp gi finds M = max_w m_w, the weights c_w = exp(m_w - M) and
+    // L = sum_w l_w c_w (lane w holds warp w's state), so each output element
+    // is a plain weighted sum of the NW accumulators
+    float* cw = res + (size_t)G * W;  // [G][NW] merge weights
+    for (int gi = warp; gi < G; gi += NW) {
+        const float* st = sm + (size_t)gi * W;
+        const float mw = lane < NW ? st[(size_t)lane * G * W + hd] : REF_NEG_INF;
+        const float lw = lane < NW ? st[(size_t)lane * G * W + hd + 1] : 0.f;
+        const float M = warp_max(mw);
+        const float c = lane < NW ? expf(mw - M) : 0.f;
+        const float L = warp_sum(lw * c);
+        if (lane < NW) cw[gi * NW + lane] = c;
+        if (lane == 0) {
             res[gi * W + hd] = M;
             res[gi * W + hd + 1] = L;
         }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        int gi = i / hd, d = i - gi * hd;
+        float A = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) A = fmaf(sm[(size_t)(w * G + gi) * W + d], cw[gi * NW + w], A);
+        res[gi * W + d] = A;
     }
     __syncthreads();
 }

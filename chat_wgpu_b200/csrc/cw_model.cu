@@ -917,6 +917,7 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     A((size_t)I.n_kv * 4, (void**)&s->counters);
     A(sizeof(DevState), (void**)&s->st);
     A(sizeof(unsigned long long), (void**)&s->bar);
+    A((size_t)I.dim * sizeof(long long), (void**)&s->racc);
     if (rc == CW_OK && (cudaMallocHost(&s->h_tok, sizeof(unsigned)) != cudaSuccess ||
                         cudaMallocHost(&s->h_tok_in, sizeof(unsigned)) != cudaSuccess))
         rc = set_error(CW_ERR_OOM, "pinned host allocation failed");

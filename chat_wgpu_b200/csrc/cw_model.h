@@ -49,6 +49,7 @@ struct cw_model {
     std::vector<cw::Layer> L;
     float* final_norm = nullptr;
     cw::QW embed, head;
+    std::vector<cw::QW> down_cm;  // down projections, column-block-major (persistent step)
     std::vector<cw_buf> owned;
     const float* inv_freq = nullptr;
 };
@@ -62,6 +63,7 @@ struct cw_session {
     float *hidden = nullptr, *hidden_b = nullptr, *tmp = nullptr, *qkv = nullptr, *attn = nullptr;
     float *act = nullptr, *logits = nullptr, *xnorm = nullptr, *part = nullptr;
     unsigned *prompt = nullptr, *toks = nullptr, *counters = nullptr;
+    long long* racc = nullptr;  // fixed-point residual accumulator (persistent step)
     cw::DevState* st = nullptr;
     int n_splits = 1;
     bool use_graph = true;

@@ -95,11 +95,28 @@ inline int mk_rc(int cfg) {
     }
 }
 
-enum { SK_GEMV = 0, SK_ATTN = 1 };
+enum { SK_GEMV = 0, SK_ATTN = 1, SK_FFN = 2 };
+
+// Fixed-point residual accumulator: the FFN stage adds its down-projection
+// partial sums into int64 words scaled by 2^32 with integer atomics, so the
+// total does not depend on the order in which CTAs arrive.
+constexpr float MK_FIX = 4294967296.0f;      // 2^32
+constexpr float MK_UNFIX = 2.3283064365386963e-10f;  // 2^-32
+constexpr int MK_DOWN_ROWS = MK_SLOT_PAY / 16;  // rows of one down-projection slot (1024)
 
 struct MStage {
     int kind, cfg, pro, epi;
     int K, N, RC, nchunks;
+    // FFN stage: act blocks (units), gate/up chunks and down slots per unit
+    int nunits, per0, per1, N2;
+    // residual accumulator: add it to the residual read here (acc_in), zero
+    // the rows written here (acc_zero)
+    int acc_in, acc_zero;
+    int pad0, pad1;
+    long long* racc;
+    const uint8_t* payload2;  // FFN: down projection, column-block-major [K/32 of down][dim][16]
+    const __half* scales2;    //      and its scales [K/32 of down][dim]
+    const void* pad_ptr;
     const uint8_t* payload;
     const __half* scales;
     const float* x;        // PRO_X input
@@ -114,16 +131,22 @@ struct MStage {
     float* kc;             // this layer's K cache [n_kv][max_seq][hd]
     float* vc;
 };
-static_assert(sizeof(MStage) % 8 == 0, "stage descriptors are copied as u64 words");
+static_assert(sizeof(MStage) % 16 == 0, "stage descriptors are copied in 16-byte pieces");
 
 // The weight-copy schedule of one stage (nchunks 0: no weights), kept in
 // shared memory so the copy issuer never waits on a global read.
 struct MIssue {
-    const uint8_t* payload;
-    const __half* scales;
-    int nchunks, rc, nb, n;
+    const uint8_t* pay0;  // GEMV weight, or the FFN gate/up matrix
+    const __half* sc0;
+    const uint8_t* pay1;  // FFN: down projection, column-block-major
+    const __half* sc1;
+    int n0;               // GEMV: chunks; FFN: units (act blocks)
+    int rc, nb, n;        // rows per chunk, blocks per row, rows of pay0
+    int per0, per1;       // FFN: gate/up chunks and down slots per unit
+    int dim;              // FFN: rows of the down projection
+    int kind;
 };
-static_assert(sizeof(MIssue) == 32, "issue entries are copied as two int4");
+static_assert(sizeof(MIssue) == 64, "issue entries are copied as four int4");
 
 struct MParams {
     const MStage* stages;
@@ -146,6 +169,7 @@ struct MParams {
     int dim, n_heads, n_kv, hd, max_seq, n_splits, part_stride, decode;
     int attn_min;  // keys per attention split before splitting further
     float eps, scale;
+    float inv_dim;      // 1/dim: the mean of squares as a product (exact for power-of-two dims)
     size_t work_bytes;  // shared-memory work region (q24 + hbuf + wbuf, or attention scratch)
     // profiling only: per stage and CTA, %globaltimer at the stage's start
     // (after its barrier), after its input prologue, after its main loop and
@@ -157,13 +181,23 @@ struct MParams {
 // 16 warps (4 keys each) before a split is worth its combine
 constexpr int MK_ATTN_MIN = MK_WARPS * ATTN_U;
 constexpr int MK_PRE = 2;  // epilogue addends preloaded per stage (chunks)
+// With 2..MK_DEFER active key splits, the attention stage only publishes each
+// split's (accumulator, max, denominator) and the O-projection stage merges
+// the splits while it builds its input (no combine step, fence or counter
+// inside the attention stage); with more splits the attention stage combines.
+constexpr int MK_DEFER = 4;
+enum { PRO_ATTN = 2 };  // prologue: merged attention splits (see MK_DEFER)
 
 // per-CTA state shared by all threads
 struct MShared {
     uint64_t full[MK_SLOTS];
     uint64_t pol;  // L2 evict-first policy of the weight stream
-    int it_stage, it_t, issued, abort;
-    float red[32];
+    int it_stage, it_t, it_j, issued, abort;
+    __align__(16) float act[32];  // FFN: the act block of the current unit
+    __align__(16) uint4 aq[6];    // FFN: its q24 planes
+    int acb;
+    float asb;
+    __align__(16) float red[2][MK_WARPS];  // CTA-sum partials, alternating per call
     unsigned long long keys[MK_WARPS];
 };
 
@@ -175,9 +209,31 @@ struct MCtx {
     float* rowred;      // 2 x 32 row partials
     MShared* sh;
     int seq;            // chunks consumed by this CTA so far (same in every thread)
+    int redsel;         // CTA-sum buffer of the next call
     int pos;
     unsigned long long* stamp;  // this stage's stamps (profiling) or null
 };
+
+// CTA-wide sum with one __syncthreads: the warps' partials go to one of two
+// alternating buffers, so a call never overwrites the buffer the previous
+// call is still reading (every thread passed that call's barrier first).
+// Fixed summation order.
+__device__ __forceinline__ float mk_cta_sum(float v, MCtx& c) {
+    static_assert(MK_WARPS == 16, "four float4 partial loads");
+    v = warp_sum(v);
+    float* r = c.sh->red[c.redsel];
+    c.redsel ^= 1;
+    if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = v;
+    __syncthreads();
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+    const float4 a = r4[0], b = r4[1], d = r4[2], e = r4[3];
+    return (((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w))) +
+           (((d.x + d.y) + (d.z + d.w)) + ((e.x + e.y) + (e.z + e.w)));
+}
+
+// One lane of the last warp issues the weight copies, so the copy issue
+// never delays warp 0 (epilogue rows, barrier arrival).
+constexpr int MK_ISSUER = MK_THREADS - 32;
 
 __device__ __forceinline__ void mk_clk(const MCtx& c, int k) {
     if (c.stamp && threadIdx.x == 0) c.stamp[4 + k] = clock64();
@@ -199,31 +255,55 @@ __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned 
 
 // Thread 0: issue the copy of this CTA's next weight chunk (in the stage
 // order) into the next ring slot.  Returns false when the step has no more.
+__device__ __forceinline__ void mk_issue_copy(MCtx& c, const uint8_t* pay, const __half* sc,
+                                              unsigned pb, unsigned sb) {
+    MShared* sh = c.sh;
+    const int slot = sh->issued % MK_SLOTS;
+    unsigned char* dst = c.ring + (size_t)slot * MK_SLOT_BYTES;
+    // the slot's previous contents were read before the __syncthreads that
+    // precedes this call (a generic-proxy read followed by an async-proxy
+    // write: ordered by that barrier, no proxy fence)
+    mbar_expect_tx(&sh->full[slot], pb + sb);
+    bulk_g2s_hint(dst, pay, pb, &sh->full[slot], sh->pol);
+    bulk_g2s_hint(dst + MK_SLOT_PAY, sc, sb, &sh->full[slot], sh->pol);
+    sh->issued++;
+}
+
 __device__ bool mk_issue_next(const MParams& p, MCtx& c) {
     MShared* sh = c.sh;
     while (sh->it_stage < p.n_stages) {
         const MIssue& I = c.iss[sh->it_stage];
-        const long chunk = blockIdx.x + (long)sh->it_t * gridDim.x;
-        if (chunk < I.nchunks) {
-            const int slot = sh->issued % MK_SLOTS;
-            const long row0 = chunk * I.rc;
+        const long u = blockIdx.x + (long)sh->it_t * gridDim.x;
+        if (I.kind == SK_GEMV && u < I.n0) {
+            const long row0 = u * I.rc;
             const int rows = (int)min((long)I.rc, (long)I.n - row0);
-            const unsigned pb = (unsigned)rows * I.nb * 16, sb = (unsigned)rows * I.nb * 2;
-            unsigned char* dst = c.ring + (size_t)slot * MK_SLOT_BYTES;
-            // the slot's previous contents were read before the __syncthreads
-            // that precedes this call (a generic-proxy read followed by an
-            // async-proxy write: ordered by that barrier, no proxy fence)
-            mbar_expect_tx(&sh->full[slot], pb + sb);
-            const uint64_t pol = sh->pol;
-            bulk_g2s_hint(dst, I.payload + (size_t)row0 * I.nb * 16, pb, &sh->full[slot], pol);
-            bulk_g2s_hint(dst + MK_SLOT_PAY, I.scales + (size_t)row0 * I.nb, sb, &sh->full[slot],
-                          pol);
-            sh->issued++;
+            mk_issue_copy(c, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
+                          (unsigned)rows * I.nb * 16, (unsigned)rows * I.nb * 2);
             sh->it_t++;
+            return true;
+        }
+        if (I.kind == SK_FFN && u < I.n0) {
+            const int j = sh->it_j;
+            if (j < I.per0) {  // gate/up rows [64u + j*rc, +rc)
+                const long row0 = u * 64 + (long)j * I.rc;
+                mk_issue_copy(c, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
+                              (unsigned)I.rc * I.nb * 16, (unsigned)I.rc * I.nb * 2);
+            } else {  // down rows [k*1024, ...) of column block u
+                const int k = j - I.per0, r0 = k * MK_DOWN_ROWS;
+                const int rows = min(MK_DOWN_ROWS, I.dim - r0);
+                const size_t off = (size_t)u * I.dim + r0;
+                mk_issue_copy(c, I.pay1 + off * 16, I.sc1 + off, (unsigned)rows * 16,
+                              (unsigned)rows * 2);
+            }
+            if (++sh->it_j == I.per0 + I.per1) {
+                sh->it_j = 0;
+                sh->it_t++;
+            }
             return true;
         }
         sh->it_stage++;
         sh->it_t = 0;
+        sh->it_j = 0;
     }
     return false;
 }
@@ -231,7 +311,7 @@ __device__ bool mk_issue_next(const MParams& p, MCtx& c) {
 // Wait (bounded) for every copy issued and not yet consumed, so no bulk copy
 // writes shared memory after the CTA has left.
 __device__ void mk_drain(MCtx& c) {
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == MK_ISSUER) {
         for (int q = c.seq; q < c.sh->issued; q++)
             mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS);
     }
@@ -294,68 +374,136 @@ __device__ __forceinline__ void mk_load_stage_wait() {
     if (threadIdx.x >= MK_LOADER) asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
-// q24 conversion of the valid blocks among b0 + k*stride (k < B; a
-// warp-uniform bound, valid ones first), one element per lane each: the
-// q24_block arithmetic, two blocks at a time so their reductions overlap.
-template <int B>
-__device__ __forceinline__ void mk_q24_blocks(const Q24& s, int b0, int stride, int nb,
-                                              const float (&v)[B], int lane) {
-    const int pos = q24_pos<LAYOUT_GGUF>(lane);
-    const int half = pos >> 4, off = pos & 15;
-    uint8_t* base = reinterpret_cast<uint8_t*>(s.pl);
-#pragma unroll
-    for (int k = 0; k < B; k += 2) {
-        const int ba = b0 + k * stride, bb = ba + stride;
-        if (ba >= nb) break;
-        const bool two = (k + 1 < B) && bb < nb;
-        const unsigned ma = __reduce_max_sync(FULL, __float_as_uint(fabsf(v[k])));
-        const unsigned mb =
-            two ? __reduce_max_sync(FULL, __float_as_uint(fabsf(v[k + 1 < B ? k + 1 : k]))) : 0u;
-        int Xa, Xb = 0;
-        float sa, sbb = 0.f;
-        q24_scale(ma, v[k], Xa, sa);
-        if (two) q24_scale(mb, v[k + 1 < B ? k + 1 : k], Xb, sbb);
+// ---- stage input -> q24 planes ---------------------------------------------------
+// Four consecutive elements per lane: lane L of a warp covers block
+// 4t + L/8 (t: the warp's quad group), elements 4*(L%8) .. 4*(L%8)+3, loaded
+// as one float4.  The block max and the integer sum are 3-step shuffles
+// within the 8 lanes of a block, and each lane writes one 32-bit word per
+// byte plane (its 4 elements' bytes, packed with __byte_perm) -- the planes
+// q24_block writes, in a quarter of the instructions.
+constexpr int MK_QB = 2;  // quad groups per warp per batch
+
+__device__ __forceinline__ void mk_q24_quad(const Q24& s, int b, bool valid, const float4& v,
+                                            int lane) {
+    unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                     max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+    m = max(m, __shfl_xor_sync(FULL, m, 1));
+    m = max(m, __shfl_xor_sync(FULL, m, 2));
+    m = max(m, __shfl_xor_sync(FULL, m, 4));
+    int X0, X1, X2, X3;
+    float sb;
+    q24_scale(m, v.x, X0, sb);
+    q24_scale(m, v.y, X1, sb);
+    q24_scale(m, v.z, X2, sb);
+    q24_scale(m, v.w, X3, sb);
+    const int g8 = lane & 7, half = g8 >> 2, w = g8 & 3;
+    if (valid) {
+        uint32_t* pw = reinterpret_cast<uint32_t*>(s.pl);
 #pragma unroll
         for (int pl = 0; pl < 3; pl++) {
-            const int sh = 8 * pl;
-            base[((size_t)(pl * 2 + half) * s.nb + ba) * 16 + off] = (uint8_t)((Xa >> sh) & 0xff);
-            if (two)
-                base[((size_t)(pl * 2 + half) * s.nb + bb) * 16 + off] =
-                    (uint8_t)((Xb >> sh) & 0xff);
+            const unsigned sel = (unsigned)pl | ((4u + pl) << 4);
+            const unsigned lo = __byte_perm((unsigned)X0, (unsigned)X1, sel);
+            const unsigned hi = __byte_perm((unsigned)X2, (unsigned)X3, sel);
+            pw[((size_t)(pl * 2 + half) * s.nb + b) * 4 + w] = __byte_perm(lo, hi, 0x5410);
         }
-        const int xa = __reduce_add_sync(FULL, Xa);
-        const int xb = two ? __reduce_add_sync(FULL, Xb) : 0;
-        if (lane == 0) {
-            s.cb[ba] = 8 * xa;
-            s.sb[ba] = sa;
-            if (two) {
-                s.cb[bb] = 8 * xb;
-                s.sb[bb] = sbb;
-            }
-        }
+    }
+    int sx = (X0 + X1) + (X2 + X3);
+    sx += __shfl_xor_sync(FULL, sx, 1);
+    sx += __shfl_xor_sync(FULL, sx, 2);
+    sx += __shfl_xor_sync(FULL, sx, 4);
+    if (valid && g8 == 0) {
+        s.cb[b] = 8 * sx;
+        s.sb[b] = sb;
     }
 }
 
-constexpr int MK_PB = 8;  // prologue blocks per warp per batch
+__device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+__device__ __forceinline__ float4 f4_norm(const float4& h, float inv, const float4& g) {
+    return make_float4(__fmul_rn(__fmul_rn(h.x, inv), g.x), __fmul_rn(__fmul_rn(h.y, inv), g.y),
+                       __fmul_rn(__fmul_rn(h.z, inv), g.z), __fmul_rn(__fmul_rn(h.w, inv), g.w));
+}
 
 // The stage input as q24 planes.  PRO_X: x from global.  PRO_NORM: rmsnorm
-// of `base` (norm.wgsl:20-56; thread t sums elements t, t+512, ... in that
-// order, as the per-stage prologue does) with the gains.  Each batch issues
-// all of its global loads before using any.
+// of `base` with the gains (norm.wgsl:20-56).  PRO_ATTN: merged attention
+// splits.  Each batch issues all of its global loads before using any.
 template <int PRO>
 __device__ void mk_prologue(const MParams& p, const MStage& S, const Q24& q, float* hbuf,
                             float* wbuf, MCtx& c) {
-    const int nb = S.K / 32;
+    const int nb = S.K / 32, nq = nb / 4;  // quad groups (nb is a multiple of 8)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (PRO == PRO_X) {
-        for (int b0 = warp; b0 < nb; b0 += MK_WARPS * MK_PB) {
-            float v[MK_PB];
+    const int sub = lane >> 3, e0 = 4 * (lane & 7);
+    if (PRO == PRO_ATTN) {
+        // the attention output of 2..MK_DEFER splits per head, merged here
+        // (attention.wgsl:88-95 across splits): per head M = max_s m_s,
+        // c_s = exp(m_s - M), 1/L with L = sum_s l_s c_s; then
+        // x = (sum_s acc_s c_s) / L per element
+        const int hd = p.hd, W = hd + 2, na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
+        float* cw = hbuf;  // [n_heads][na + 1]
+        for (int h = warp; h < p.n_heads; h += MK_WARPS) {
+            const float* ph = p.part + (size_t)h * p.part_stride * W;
+            const float m = lane < na ? __ldcg(ph + (size_t)lane * W + hd) : REF_NEG_INF;
+            const float l = lane < na ? __ldcg(ph + (size_t)lane * W + hd + 1) : 0.f;
+            const float M = warp_max(m);
+            const float cc = lane < na ? expf(m - M) : 0.f;
+            const float L = warp_sum(l * cc);
+            if (lane < na) cw[h * (na + 1) + lane] = cc;
+            if (lane == 0) cw[h * (na + 1) + na] = 1.0f / L;
+        }
+        __syncthreads();
+        for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
+            float4 v[MK_QB];
 #pragma unroll
-            for (int k = 0; k < MK_PB; k++) {
-                const int b = b0 + k * MK_WARPS;
-                v[k] = b < nb ? __ldcg(S.x + b * 32 + lane) : 0.f;
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                v[k] = f4_zero();
+                if (b < nb) {
+                    const int i0 = b * 32 + e0, h = i0 / hd, d0 = i0 - h * hd;
+                    const float* ph = p.part + (size_t)h * p.part_stride * W + d0;
+                    const float* cc = cw + h * (na + 1);
+                    float2 lo[MK_DEFER], hi[MK_DEFER];  // (W even, d0 % 4 == 0: 8-byte aligned)
+#pragma unroll
+                    for (int s = 0; s < MK_DEFER; s++) {
+                        const float2* q2 = reinterpret_cast<const float2*>(ph + (size_t)s * W);
+                        lo[s] = s < na ? __ldcg(q2) : make_float2(0.f, 0.f);
+                        hi[s] = s < na ? __ldcg(q2 + 1) : make_float2(0.f, 0.f);
+                    }
+                    float r[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        float a[MK_DEFER];
+#pragma unroll
+                        for (int s = 0; s < MK_DEFER; s++) {
+                            const float2 t2 = e < 2 ? lo[s] : hi[s];
+                            a[s] = (s < na ? ((e & 1) ? t2.y : t2.x) : 0.f) * cc[s < na ? s : 0];
+                        }
+                        r[e] = ((a[0] + a[1]) + (a[2] + a[3])) * cc[na];
+                    }
+                    v[k] = make_float4(r[0], r[1], r[2], r[3]);
+                }
             }
-            mk_q24_blocks<MK_PB>(q, b0, MK_WARPS, nb, v, lane);
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                if (t0 + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
+            }
+        }
+        mk_clk(c, CLK_LOADED);
+        mk_clk(c, CLK_NORMED);
+        return;
+    }
+    if (PRO == PRO_X) {
+        for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
+            float4 v[MK_QB];
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                v[k] = b < nb ? __ldcg(reinterpret_cast<const float4*>(S.x + b * 32 + e0)) : f4_zero();
+            }
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                if (t0 + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
+            }
         }
         mk_clk(c, CLK_LOADED);
         mk_clk(c, CLK_NORMED);
@@ -364,68 +512,219 @@ __device__ void mk_prologue(const MParams& p, const MStage& S, const Q24& q, flo
     const float* src = S.base ? S.base : c.emb;
     const bool gsrc = S.base != nullptr;
     const bool wx = S.xn_out && blockIdx.x == 0;
+    // the residual: base (+ the fixed-point FFN accumulator when acc_in)
+    auto ld_src = [&](int i) {
+        float4 h = gsrc ? __ldcg(reinterpret_cast<const float4*>(src + i))
+                        : *reinterpret_cast<const float4*>(src + i);
+        if (S.acc_in) {
+            const longlong2 a0 = __ldcg(reinterpret_cast<const longlong2*>(S.racc + i));
+            const longlong2 a1 = __ldcg(reinterpret_cast<const longlong2*>(S.racc + i + 2));
+            h.x = h.x + __ll2float_rn(a0.x) * MK_UNFIX;
+            h.y = h.y + __ll2float_rn(a0.y) * MK_UNFIX;
+            h.z = h.z + __ll2float_rn(a1.x) * MK_UNFIX;
+            h.w = h.w + __ll2float_rn(a1.y) * MK_UNFIX;
+        }
+        return h;
+    };
     float ss = 0.f;
-    if (nb <= MK_WARPS * MK_PB) {  // one batch: everything stays in registers
-        float v[MK_PB], w[MK_PB];
+    if (nq <= MK_WARPS * MK_QB) {  // one batch: everything stays in registers
+        float4 v[MK_QB], w[MK_QB];
 #pragma unroll
-        for (int k = 0; k < MK_PB; k++) {
-            const int b = warp + k * MK_WARPS, i = b * 32 + lane;
-            v[k] = b < nb ? (gsrc ? __ldcg(src + i) : src[i]) : 0.f;
-            w[k] = b < nb ? __ldg(S.norm_w + i) : 0.f;
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub, i = b * 32 + e0;
+            v[k] = b < nb ? ld_src(i) : f4_zero();
+            w[k] = b < nb ? __ldg(reinterpret_cast<const float4*>(S.norm_w + i)) : f4_zero();
         }
 #pragma unroll
-        for (int k = 0; k < MK_PB; k++) ss = fmaf(v[k], v[k], ss);  // padding adds +0
+        for (int k = 0; k < MK_QB; k++) {  // padding adds +0
+            ss = fmaf(v[k].x, v[k].x, ss);
+            ss = fmaf(v[k].y, v[k].y, ss);
+            ss = fmaf(v[k].z, v[k].z, ss);
+            ss = fmaf(v[k].w, v[k].w, ss);
+        }
         mk_clk(c, CLK_LOADED);
-        ss = gemv_cta_sum(ss, c.sh->red);
+        ss = mk_cta_sum(ss, c);
         mk_clk(c, CLK_NORMED);
-        const float inv = 1.0f / sqrtf(ss / (float)S.K + p.eps);
+        const float inv = 1.0f / sqrtf(ss * p.inv_dim + p.eps);
 #pragma unroll
-        for (int k = 0; k < MK_PB; k++) {
-            const int b = warp + k * MK_WARPS;
-            v[k] = __fmul_rn(__fmul_rn(v[k], inv), w[k]);
-            if (wx && b < nb) S.xn_out[b * 32 + lane] = v[k];
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub;
+            v[k] = f4_norm(v[k], inv, w[k]);
+            if (wx && b < nb) *reinterpret_cast<float4*>(S.xn_out + b * 32 + e0) = v[k];
         }
-        mk_q24_blocks<MK_PB>(q, warp, MK_WARPS, nb, v, lane);
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub;
+            if (warp + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
+        }
         return;
     }
-    for (int b0 = warp; b0 < nb; b0 += MK_WARPS * MK_PB) {
-        float v[MK_PB], w[MK_PB];
+    for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
+        float4 v[MK_QB], w[MK_QB];
 #pragma unroll
-        for (int k = 0; k < MK_PB; k++) {
-            const int b = b0 + k * MK_WARPS, i = b * 32 + lane;
-            v[k] = b < nb ? (gsrc ? __ldcg(src + i) : src[i]) : 0.f;
-            w[k] = b < nb ? __ldg(S.norm_w + i) : 0.f;
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (t0 + k * MK_WARPS) + sub, i = b * 32 + e0;
+            v[k] = b < nb ? ld_src(i) : f4_zero();
+            w[k] = b < nb ? __ldg(reinterpret_cast<const float4*>(S.norm_w + i)) : f4_zero();
         }
 #pragma unroll
-        for (int k = 0; k < MK_PB; k++) {
-            const int b = b0 + k * MK_WARPS, i = b * 32 + lane;
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (t0 + k * MK_WARPS) + sub, i = b * 32 + e0;
             if (b < nb) {
-                hbuf[i] = v[k];
-                wbuf[i] = w[k];
-                ss = fmaf(v[k], v[k], ss);
+                *reinterpret_cast<float4*>(hbuf + i) = v[k];
+                *reinterpret_cast<float4*>(wbuf + i) = w[k];
             }
+            ss = fmaf(v[k].x, v[k].x, ss);
+            ss = fmaf(v[k].y, v[k].y, ss);
+            ss = fmaf(v[k].z, v[k].z, ss);
+            ss = fmaf(v[k].w, v[k].w, ss);
         }
     }
     mk_clk(c, CLK_LOADED);
-    ss = gemv_cta_sum(ss, c.sh->red);
+    ss = mk_cta_sum(ss, c);
     mk_clk(c, CLK_NORMED);
-    const float inv = 1.0f / sqrtf(ss / (float)S.K + p.eps);
-    for (int b0 = warp; b0 < nb; b0 += MK_WARPS * MK_PB) {
-        float v[MK_PB];
-#pragma unroll
-        for (int k = 0; k < MK_PB; k++) {
-            const int b = b0 + k * MK_WARPS, i = b * 32 + lane;
-            v[k] = b < nb ? __fmul_rn(__fmul_rn(hbuf[i], inv), wbuf[i]) : 0.f;
-            if (wx && b < nb) S.xn_out[i] = v[k];
+    const float inv = 1.0f / sqrtf(ss * p.inv_dim + p.eps);
+    for (int t = warp; t < nq; t += MK_WARPS) {
+        const int b = 4 * t + sub, i = b * 32 + e0;
+        float4 v = f4_zero();
+        if (b < nb) {
+            v = f4_norm(*reinterpret_cast<const float4*>(hbuf + i), inv,
+                        *reinterpret_cast<const float4*>(wbuf + i));
+            if (wx) *reinterpret_cast<float4*>(S.xn_out + i) = v;
         }
-        mk_q24_blocks<MK_PB>(q, b0, MK_WARPS, nb, v, lane);
+        mk_q24_quad(q, b, b < nb, v, lane);
     }
 }
 
 // ---- GEMV stage ------------------------------------------------------------------
+// T = sum_j (q_j - 8) X_j of one Q4_0 block (16 payload bytes w) against one
+// q24 block (planes xa: elements 0-15, xb: 16-31; cb = 8 * sum X): six
+// independent dp4a chains of four, low and high nibbles apart.
+__device__ __forceinline__ float mk_block_dot(const uint4& w4, const uint4 (&xa)[3],
+                                              const uint4 (&xb)[3], int cb) {
+    const unsigned w[4] = {w4.x, w4.y, w4.z, w4.w};
+    const unsigned a0[4] = {xa[0].x, xa[0].y, xa[0].z, xa[0].w};
+    const unsigned b0[4] = {xb[0].x, xb[0].y, xb[0].z, xb[0].w};
+    const unsigned a1[4] = {xa[1].x, xa[1].y, xa[1].z, xa[1].w};
+    const unsigned b1[4] = {xb[1].x, xb[1].y, xb[1].z, xb[1].w};
+    const unsigned a2[4] = {xa[2].x, xa[2].y, xa[2].z, xa[2].w};
+    const unsigned b2[4] = {xb[2].x, xb[2].y, xb[2].z, xb[2].w};
+    int s0l = 0, s0h = 0, s1l = 0, s1h = 0, s2l = 0, s2h = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const unsigned lo = w[e] & 0x0f0f0f0fu;
+        const unsigned hi = (w[e] >> 4) & 0x0f0f0f0fu;
+        s0l = dp4a_uu(lo, a0[e], s0l);
+        s0h = dp4a_uu(hi, b0[e], s0h);
+        s1l = dp4a_uu(lo, a1[e], s1l);
+        s1h = dp4a_uu(hi, b1[e], s1h);
+        s2l = dp4a_us(lo, a2[e], s2l);
+        s2h = dp4a_us(hi, b2[e], s2h);
+    }
+    const int s01 = (s0l + s0h) + ((s1l + s1h) << 8) - cb;
+    return fmaf((float)(s2l + s2h), 65536.0f, (float)s01);
+}
+
+// The input vector of a GEMV stage as q24 planes in the work region.
+__device__ __forceinline__ void mk_input(const MParams& p, const MStage& S, const Q24& q,
+                                         MCtx& c) {
+    float* hbuf = reinterpret_cast<float*>(c.work + al16(q24_bytes(q.nb)));
+    float* wbuf = hbuf + S.K;
+    if (S.pro == PRO_NORM) {
+        mk_prologue<PRO_NORM>(p, S, q, hbuf, wbuf, c);
+    } else if (S.pro == PRO_ATTN) {
+        const int na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
+        if (na >= 2 && na <= MK_DEFER)
+            mk_prologue<PRO_ATTN>(p, S, q, hbuf, wbuf, c);
+        else
+            mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
+    } else {
+        mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
+    }
+}
+
+// This lane's blocks of the q24 planes, kept in registers for the chunk loop.
+template <class CF>
+struct MRegs {
+    uint4 xa[CF::BPL][3], xb[CF::BPL][3];
+    int cb[CF::BPL];
+    float sb[CF::BPL];
+};
+template <class CF>
+__device__ __forceinline__ void mk_load_regs(const Q24& q, MRegs<CF>& R) {
+    constexpr int WPR = CF::WPR, BPL = CF::BPL;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wsub = warp % WPR;
+#pragma unroll
+    for (int k = 0; k < BPL; k++) {
+        const int b = wsub * 32 + lane + k * 32 * WPR;
+        const bool in = b < q.nb;
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            R.xa[k][pl] = in ? q.pl[(pl * 2 + 0) * q.nb + b] : make_uint4(0, 0, 0, 0);
+            R.xb[k][pl] = in ? q.pl[(pl * 2 + 1) * q.nb + b] : make_uint4(0, 0, 0, 0);
+        }
+        R.cb[k] = in ? q.cb[b] : 0;
+        R.sb[k] = in ? q.sb[b] : 0.f;
+    }
+}
+
+// One chunk of RC rows: wait for ring slot c.seq, dot each row with the
+// planes in R, reduce the per-warp partials into rb[row * WPR + sub], then
+// (after __syncthreads) issue the next copy into the freed slot.  Returns
+// rb, or null after a timed-out wait (the failure is recorded).
+template <class CF>
+__device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int nb, int rows,
+                                                 const MRegs<CF>& R, bool first) {
+    constexpr int WPR = CF::WPR, BPL = CF::BPL, RPW = CF::RPW;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wsub = warp % WPR, slot = warp / WPR;
+    const int rs = c.seq % MK_SLOTS;
+    const unsigned par = (unsigned)((c.seq / MK_SLOTS) & 1);
+    const bool ok = mbar_wait(&c.sh->full[rs], par, MK_WAIT_NS);
+    if (__syncthreads_or(!ok)) {
+        mk_fail(p, c);
+        return nullptr;
+    }
+    if (first) mk_clk(c, CLK_WAITED);
+    const unsigned char* pay = c.ring + (size_t)rs * MK_SLOT_BYTES;
+    const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+    float* rb = c.rowred + (size_t)(c.seq & 1) * 32;
+    uint4 w4[RPW][BPL];
+    float dd[RPW][BPL];
+#pragma unroll
+    for (int j = 0; j < RPW; j++) {
+        const int r = slot * RPW + j;
+#pragma unroll
+        for (int k = 0; k < BPL; k++) {
+            const int b = wsub * 32 + lane + k * 32 * WPR;
+            const bool in = r < rows && b < nb;
+            const size_t blk = in ? (size_t)r * nb + b : 0;
+            w4[j][k] = in ? reinterpret_cast<const uint4*>(pay)[blk] : make_uint4(0, 0, 0, 0);
+            dd[j][k] = in ? __half2float(scs[blk]) : 0.f;
+        }
+    }
+    float acc[RPW];
+#pragma unroll
+    for (int j = 0; j < RPW; j++) {
+        acc[j] = 0.f;
+#pragma unroll
+        for (int k = 0; k < BPL; k++)
+            acc[j] = fmaf(dd[j][k] * R.sb[k], mk_block_dot(w4[j][k], R.xa[k], R.xb[k], R.cb[k]),
+                          acc[j]);
+    }
+    const float v = warp_reduce_rows<RPW>(acc, lane);
+    if ((lane & (32 / RPW - 1)) == 0) rb[(slot * RPW + lane / (32 / RPW)) * WPR + wsub] = v;
+    __syncthreads();  // slot consumed, row partials complete
+    if (first) mk_clk(c, CLK_SUMMED);
+    if (threadIdx.x == MK_ISSUER) mk_issue_next(p, c);
+    if (first) mk_clk(c, CLK_ISSUED);
+    c.seq++;
+    return rb;
+}
+
 template <class CF>
 __device__ bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
-    constexpr int WPR = CF::WPR, BPL = CF::BPL, RPW = CF::RPW, RC = CF::RC;
+    constexpr int WPR = CF::WPR, RC = CF::RC;
     const int nb = S.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if ((int)blockIdx.x >= S.nchunks) return true;  // no rows of this stage here
@@ -437,34 +736,18 @@ __device__ bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     for (int t = 0; t < MK_PRE; t++) {
         const long row = (blockIdx.x + (long)t * gridDim.x) * RC + tid;
         pre[t] = 0.f;
-        if (has_pre && tid < RC && row < S.N)
+        if (has_pre && tid < RC && row < S.N) {
             pre[t] = S.epi == EPI_RESID ? __ldcg(S.y + row) : __ldg(S.bias + row);
+            if (S.epi == EPI_RESID && S.acc_in)
+                pre[t] = pre[t] + __ll2float_rn(__ldcg(S.racc + row)) * MK_UNFIX;
+        }
     }
     const Q24 q = q24_carve(c.work, nb);
-    float* hbuf = reinterpret_cast<float*>(c.work + al16(q24_bytes(nb)));
-    float* wbuf = hbuf + S.K;
-    if (S.pro == PRO_NORM)
-        mk_prologue<PRO_NORM>(p, S, q, hbuf, wbuf, c);
-    else
-        mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
+    mk_input(p, S, q, c);
     mk_clk(c, CLK_Q24);
     __syncthreads();
-    uint4 xa[BPL][3], xb[BPL][3];
-    int cbr[BPL];
-    float sbr[BPL];
-    const int wsub = warp % WPR, slot = warp / WPR;
-#pragma unroll
-    for (int k = 0; k < BPL; k++) {
-        const int b = wsub * 32 + lane + k * 32 * WPR;
-        const bool in = b < nb;
-#pragma unroll
-        for (int pl = 0; pl < 3; pl++) {
-            xa[k][pl] = in ? q.pl[(pl * 2 + 0) * nb + b] : make_uint4(0, 0, 0, 0);
-            xb[k][pl] = in ? q.pl[(pl * 2 + 1) * nb + b] : make_uint4(0, 0, 0, 0);
-        }
-        cbr[k] = in ? q.cb[b] : 0;
-        sbr[k] = in ? q.sb[b] : 0.f;
-    }
+    MRegs<CF> R;
+    mk_load_regs<CF>(q, R);
     if (c.stamp && tid == 0) c.stamp[1] = global_ns();
     mk_clk(c, CLK_REGS);
     unsigned long long best = argmax_key_init();
@@ -476,70 +759,13 @@ __device__ bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
 #pragma unroll
         for (int u = 0; u < MK_PRE; u++)
             if (u == t) add = pre[u];
-        if (t >= MK_PRE && has_pre && tid < rows)  // later chunks: requested before the wait
+        if (t >= MK_PRE && has_pre && tid < rows) {  // later chunks: requested before the wait
             add = S.epi == EPI_RESID ? __ldcg(S.y + row0 + tid) : __ldg(S.bias + row0 + tid);
-        const int rs = c.seq % MK_SLOTS;
-        const unsigned par = (unsigned)((c.seq / MK_SLOTS) & 1);
-        const bool ok = mbar_wait(&c.sh->full[rs], par, MK_WAIT_NS);
-        if (__syncthreads_or(!ok)) {
-            mk_fail(p, c);
-            return false;
+            if (S.epi == EPI_RESID && S.acc_in)
+                add = add + __ll2float_rn(__ldcg(S.racc + row0 + tid)) * MK_UNFIX;
         }
-        if (t == 0) mk_clk(c, CLK_WAITED);
-        const unsigned char* pay = c.ring + (size_t)rs * MK_SLOT_BYTES;
-        const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
-        float* rb = c.rowred + (size_t)(c.seq & 1) * 32;
-        uint4 w4[RPW][BPL];
-        float dd[RPW][BPL];
-#pragma unroll
-        for (int j = 0; j < RPW; j++) {
-            const int r = slot * RPW + j;
-#pragma unroll
-            for (int k = 0; k < BPL; k++) {
-                const int b = wsub * 32 + lane + k * 32 * WPR;
-                const bool in = r < rows && b < nb;
-                const size_t blk = in ? (size_t)r * nb + b : 0;
-                w4[j][k] = in ? reinterpret_cast<const uint4*>(pay)[blk] : make_uint4(0, 0, 0, 0);
-                dd[j][k] = in ? __half2float(scs[blk]) : 0.f;
-            }
-        }
-        float acc[RPW];
-#pragma unroll
-        for (int j = 0; j < RPW; j++) {
-            acc[j] = 0.f;
-#pragma unroll
-            for (int k = 0; k < BPL; k++) {
-                const unsigned w[4] = {w4[j][k].x, w4[j][k].y, w4[j][k].z, w4[j][k].w};
-                const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
-                const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
-                const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
-                const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
-                const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
-                const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
-                int s0l = 0, s0h = 0, s1l = 0, s1h = 0, s2l = 0, s2h = 0;
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const unsigned lo = w[e] & 0x0f0f0f0fu;
-                    const unsigned hi = (w[e] >> 4) & 0x0f0f0f0fu;
-                    s0l = dp4a_uu(lo, a0[e], s0l);
-                    s0h = dp4a_uu(hi, b0[e], s0h);
-                    s1l = dp4a_uu(lo, a1[e], s1l);
-                    s1h = dp4a_uu(hi, b1[e], s1h);
-                    s2l = dp4a_us(lo, a2[e], s2l);
-                    s2h = dp4a_us(hi, b2[e], s2h);
-                }
-                const int s01 = (s0l + s0h) + ((s1l + s1h) << 8) - cbr[k];
-                const float T = fmaf((float)(s2l + s2h), 65536.0f, (float)s01);
-                acc[j] = fmaf(dd[j][k] * sbr[k], T, acc[j]);
-            }
-        }
-        const float v = warp_reduce_rows<RPW>(acc, lane);
-        if ((lane & (32 / RPW - 1)) == 0) rb[(slot * RPW + lane / (32 / RPW)) * WPR + wsub] = v;
-        __syncthreads();  // slot consumed, row partials complete
-        if (t == 0) mk_clk(c, CLK_SUMMED);
-        if (tid == 0) mk_issue_next(p, c);
-        if (t == 0) mk_clk(c, CLK_ISSUED);
-        c.seq++;
+        const float* rb = mk_chunk<CF>(p, c, nb, rows, R, t == 0);
+        if (!rb) return false;
         // epilogue: fixed-order sum of the WPR partials of each row
         if (S.epi == EPI_GLU) {
             if (tid < RC / 2 && 2 * tid + 1 < rows) {
@@ -563,6 +789,7 @@ __device__ bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
                 best = kk > best ? kk : best;
             } else {
                 S.y[row] = has_pre ? (S.epi == EPI_RESID ? add + vv : vv + add) : vv;
+                if (S.acc_zero) S.racc[row] = 0;
             }
         }
     }
@@ -581,6 +808,94 @@ __device__ bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
             atomicMax(&p.st->key, best);
         }
     }
+    return true;
+}
+
+// ---- FFN stage: gate/up + SwiGLU + down projection, one act block per unit --------
+// Unit u owns act block u (act rows 32u .. 32u+31 = gate/up rows 64u ..
+// 64u+63, glu.wgsl:25): its gate/up chunks give the 32 act values, which are
+// converted to one q24 block, and the down projection's column block u
+// (MK_DOWN_ROWS rows per ring slot, one Q4_0 block per row) turns them into a
+// partial sum for every output row, added into the fixed-point residual
+// accumulator (the next stage that reads the residual adds it).
+template <class CF>
+__device__ bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
+    constexpr int WPR = CF::WPR, RC = CF::RC;
+    const int nb = S.K / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if ((int)blockIdx.x >= S.nunits) return true;
+    const Q24 q = q24_carve(c.work, nb);
+    mk_input(p, S, q, c);
+    mk_clk(c, CLK_Q24);
+    __syncthreads();
+    MRegs<CF> R;
+    mk_load_regs<CF>(q, R);
+    if (c.stamp && tid == 0) c.stamp[1] = global_ns();
+    mk_clk(c, CLK_REGS);
+    MShared* sh = c.sh;
+    bool first = true;
+    for (int u = blockIdx.x; u < S.nunits; u += gridDim.x) {
+        for (int j = 0; j < S.per0; j++) {  // gate/up rows 64u + j*RC ..
+            const float* rb = mk_chunk<CF>(p, c, nb, RC, R, first);
+            first = false;
+            if (!rb) return false;
+            if (tid < RC / 2) {
+                const int r0 = 2 * tid;
+                float gv = 0.f, uv = 0.f;
+#pragma unroll
+                for (int w = 0; w < WPR; w++) {
+                    gv += rb[r0 * WPR + w];
+                    uv += rb[(r0 + 1) * WPR + w];
+                }
+                sh->act[(j * RC + r0) / 2] = silu_ref_f(gv) * uv;
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {  // the act block as q24 (lanes 0-7: four elements each)
+            Q24 aq;
+            aq.pl = sh->aq;
+            aq.cb = &sh->acb;
+            aq.sb = &sh->asb;
+            aq.nb = 1;
+            const float4 v = lane < 8 ? reinterpret_cast<const float4*>(sh->act)[lane]
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            mk_q24_quad(aq, 0, lane < 8, v, lane);
+        }
+        __syncthreads();
+        uint4 xa[3], xb[3];
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            xa[pl] = sh->aq[pl * 2 + 0];
+            xb[pl] = sh->aq[pl * 2 + 1];
+        }
+        const int acb = sh->acb;
+        const float asb = sh->asb;
+        for (int k = 0; k < S.per1; k++) {  // down rows k*MK_DOWN_ROWS ..
+            const int r0 = k * MK_DOWN_ROWS, rows = min(MK_DOWN_ROWS, S.N2 - r0);
+            const int rs = c.seq % MK_SLOTS;
+            const unsigned par = (unsigned)((c.seq / MK_SLOTS) & 1);
+            const bool ok = mbar_wait(&sh->full[rs], par, MK_WAIT_NS);
+            if (__syncthreads_or(!ok)) {
+                mk_fail(p, c);
+                return false;
+            }
+            const unsigned char* pay = c.ring + (size_t)rs * MK_SLOT_BYTES;
+            const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+            for (int r = tid; r < rows; r += MK_THREADS) {
+                const uint4 w4 = reinterpret_cast<const uint4*>(pay)[r];
+                const float d = __half2float(scs[r]);
+                const float part = fmaf(d * asb, mk_block_dot(w4, xa, xb, acb), 0.f);
+                const long long fx = __float2ll_rn(part * MK_FIX);
+                atomicAdd(reinterpret_cast<unsigned long long*>(S.racc + r0 + r),
+                          (unsigned long long)fx);
+            }
+            __syncthreads();  // slot consumed
+            if (tid == MK_ISSUER) mk_issue_next(p, c);
+            c.seq++;
+        }
+    }
+    if (c.stamp && tid == 0) c.stamp[2] = global_ns();
+    mk_clk(c, CLK_MAIN);
     return true;
 }
 
@@ -659,6 +974,7 @@ __device__ bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
                 if (d < hd) dst[d] = vv[e];
             }
         }
+        mk_clk(c, CLK_LOADED);  // attention: inputs arrived, QK-norm done
         __syncthreads();
         for (int i = tid; i < nrows * half; i += blockDim.x) {  // RoPE (rope.wgsl:25-34)
             const int rr = i / half, kq = i - rr * half;
@@ -670,6 +986,7 @@ __device__ bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
             row[kq + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
         }
         __syncthreads();
+        mk_clk(c, CLK_NORMED);  // attention: RoPE done
         float* kbase = S.kc + (size_t)g * p.max_seq * hd;
         float* vbase = S.vc + (size_t)g * p.max_seq * hd;
         if (holds && tid < hd) {  // cache.rs:21-24
@@ -677,12 +994,24 @@ __device__ bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
             vbase[(size_t)pos * hd + tid] = vnew;
         }
         __syncthreads();
+        mk_clk(c, CLK_Q24);  // attention: new K/V row stored
         if (c.stamp && tid == 0) c.stamp[1] = global_ns();
         attn_core<EPL, GMAX, KV_CG, MK_WARPS>(qs, G, hd, kbase, vbase, hd, jlo, jhi, p.scale, 0.f,
                                               sm, res);
+        mk_clk(c, CLK_REGS);  // attention: this split's state merged
         if (c.stamp && tid == 0) c.stamp[2] = global_ns();
-        attn_finish(res, G, hd, g, split, n_active, p.part_stride, p.part, p.counters, p.attn, cwt);
+        if (n_active >= 2 && n_active <= MK_DEFER) {
+            const int W = hd + 2;
+            for (int i = tid; i < G * W; i += blockDim.x) {
+                const int gi = i / W, d = i - gi * W;
+                p.part[((size_t)(g * G + gi) * p.part_stride + split) * W + d] = res[i];
+            }
+        } else {
+            attn_finish(res, G, hd, g, split, n_active, p.part_stride, p.part, p.counters, p.attn,
+                        cwt);
+        }
         __syncthreads();
+        mk_clk(c, CLK_MAIN);  // attention: output (or partial) published
     }
     return true;
 }
@@ -702,6 +1031,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     c.iss = iss;
     c.rowred = rowred;
     c.seq = 0;
+    c.redsel = 0;
     c.stamp = nullptr;
     const int tid = threadIdx.x;
     if (tid == 0) {
@@ -709,11 +1039,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
         fence_mbar_init();
         sh.it_stage = 0;
         sh.it_t = 0;
+        sh.it_j = 0;
         sh.issued = 0;
         sh.abort = 0;
         sh.pol = l2_evict_first();
     }
-    for (int i = tid; i < p.n_stages * 2; i += blockDim.x)
+    for (int i = tid; i < p.n_stages * 4; i += blockDim.x)
         reinterpret_cast<int4*>(iss)[i] = reinterpret_cast<const int4*>(p.issues)[i];
     mk_load_stage(p, 0, &sst[0]);
     mk_load_stage(p, 1, &sst[1]);
@@ -723,7 +1054,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     const unsigned long long base = p.st->bar_base;
     c.pos = pos;
     __syncthreads();
-    if (tid == 0)  // the first ring-full of weights
+    if (tid == MK_ISSUER)  // the first ring-full of weights
         for (int s = 0; s < MK_SLOTS; s++)
             if (!mk_issue_next(p, c)) break;
     // embedding row (qwen3.rs:128-133), every CTA its own copy
@@ -758,6 +1089,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
         mk_clk(c, CLK_AHEAD);
         if (S.kind == SK_ATTN) {
             ok = mk_attn<EPL, GMAX>(p, S, c);
+        } else if (S.kind == SK_FFN) {
+            switch (S.cfg) {
+                case 0: ok = mk_ffn<MC0>(p, S, c); break;
+                case 1: ok = mk_ffn<MC1>(p, S, c); break;
+                case 2: ok = mk_ffn<MC2>(p, S, c); break;
+                case 3: ok = mk_ffn<MC3>(p, S, c); break;
+                default: ok = mk_ffn<MC4>(p, S, c); break;
+            }
         } else {
             switch (S.cfg) {
                 case 0: ok = mk_gemv<MC0>(p, S, c); break;
@@ -805,6 +1144,46 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
 }
 
 // ---- host ---------------------------------------------------------------------------
+// Column-block-major copy of a packed Q4_0 matrix: block b of row r moves to
+// [b][r], so the column block an FFN unit needs is one contiguous range.
+__global__ void k_colmajor(const uint8_t* __restrict__ pay, const __half* __restrict__ sc, int rows,
+                           int nb, uint8_t* __restrict__ opay, __half* __restrict__ osc) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)rows * nb) return;
+    const int r = (int)(i / nb), b = (int)(i - (long)r * nb);
+    reinterpret_cast<uint4*>(opay)[(size_t)b * rows + r] = reinterpret_cast<const uint4*>(pay)[i];
+    osc[(size_t)b * rows + r] = sc[i];
+}
+
+static int build_down_colmajor(cw_model* m) {
+    if (!m->down_cm.empty()) return CW_OK;
+    cw_ctx* ctx = m->ctx;
+    std::vector<QW> out;
+    for (const Layer& l : m->L) {
+        const int rows = l.down.rows, nb = l.down.in_f / 32;
+        const size_t pb = (size_t)rows * nb * 16, sb = (size_t)rows * nb * 2;
+        const size_t soff = (pb + 255) / 256 * 256;
+        cw_buf b;
+        BufEntry* e;
+        CW_TRY(buf_new(ctx, soff + sb, BUF_PERSISTENT, &b, &e));
+        m->owned.push_back(b);
+        QW q;
+        q.payload = reinterpret_cast<const uint8_t*>(e->ptr);
+        q.scales = reinterpret_cast<const __half*>(reinterpret_cast<char*>(e->ptr) + soff);
+        q.rows = rows;
+        q.in_f = l.down.in_f;
+        q.buf = b;
+        const long n = (long)rows * nb;
+        k_colmajor<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
+            l.down.payload, l.down.scales, rows, nb, const_cast<uint8_t*>(q.payload),
+            const_cast<__half*>(q.scales));
+        CW_CUDA(cudaGetLastError());
+        out.push_back(q);
+    }
+    CW_CUDA(cudaStreamSynchronize(ctx->stream));
+    m->down_cm.swap(out);
+    return CW_OK;
+}
 struct StepPlan {
     std::vector<const char*> names;  // stage names, for the profile
     MStage* d_stages = nullptr;
@@ -831,8 +1210,10 @@ static size_t work_bytes_for(const cw_model_info& I, int n_splits) {
     const int G = I.n_heads / I.n_kv, hd = I.head_dim;
     const int kmax = std::max<int>(I.dim, std::max<int>(I.n_heads * I.head_dim, I.hidden));
     // PRO_X: q24 planes of K <= kmax; PRO_NORM (K = dim): planes + hbuf + wbuf
-    const size_t gemv = std::max(al16(q24_bytes(kmax / 32)),
-                                 al16(q24_bytes((int)I.dim / 32)) + (size_t)I.dim * 8);
+    const int qd = I.n_heads * I.head_dim;
+    const size_t gemv = std::max({al16(q24_bytes(kmax / 32)),
+                                  al16(q24_bytes((int)I.dim / 32)) + (size_t)I.dim * 8,
+                                  al16(q24_bytes(qd / 32)) + (size_t)I.n_heads * (MK_DEFER + 1) * 4});
     const size_t attn = (attn_smem_floats(G, hd, n_splits, MK_WARPS) + (size_t)G * hd + hd) * 4;
     return al16(std::max(gemv, attn));
 }
@@ -865,14 +1246,18 @@ int step_plan_create(cw_session* s) {
     P->kern = pick_kernel(P->epl, P->gmax);
     const int grid = ctx->sm_count;
     const int n_splits = std::max(1, std::min(s->n_splits, grid / (int)I.n_kv));
+    CW_TRY(build_down_colmajor(m));
     // ---- stage list and its weight-copy schedule
     std::vector<MStage> st;
     std::vector<MIssue> is;
     auto gemv = [&](const char* name, const QW& w, int pro, int epi, const float* x,
                     const float* base, const float* norm_w, float* y, const float* bias,
-                    float* xn_out) {
+                    float* xn_out, int acc_in, int acc_zero) {
         P->names.push_back(name);
         MStage S = {};
+        S.acc_in = acc_in;
+        S.acc_zero = acc_zero;
+        S.racc = s->racc;
         S.kind = SK_GEMV;
         S.cfg = mk_cfg_for(w.in_f);
         S.pro = pro;
@@ -890,12 +1275,20 @@ int step_plan_create(cw_session* s) {
         S.bias = bias;
         S.xn_out = xn_out;
         st.push_back(S);
-        is.push_back(MIssue{S.payload, S.scales, S.nchunks, S.RC, S.K / 32, S.N});
+        MIssue I = {};
+        I.kind = SK_GEMV;
+        I.pay0 = S.payload;
+        I.sc0 = S.scales;
+        I.n0 = S.nchunks;
+        I.rc = S.RC;
+        I.nb = S.K / 32;
+        I.n = S.N;
+        is.push_back(I);
     };
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
         gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, nullptr, li == 0 ? nullptr : s->hidden,
-             l.attn_norm, s->qkv, l.qkv_bias, nullptr);
+             l.attn_norm, s->qkv, l.qkv_bias, nullptr, li > 0, 0);
         P->names.push_back("attention");
         MStage A = {};
         A.kind = SK_ATTN;
@@ -904,16 +1297,51 @@ int step_plan_create(cw_session* s) {
         A.kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
         A.vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
         st.push_back(A);
-        is.push_back(MIssue{nullptr, nullptr, 0, 0, 0, 0});
-        gemv("attn_out", l.wo, PRO_X, EPI_RESID, s->attn, nullptr, nullptr, s->hidden, nullptr,
-             nullptr);
-        gemv("ffn_in", l.gate_up, PRO_NORM, EPI_GLU, nullptr, s->hidden, l.ffn_norm, s->act,
-             nullptr, nullptr);
-        gemv("ffn_out", l.down, PRO_X, EPI_RESID, s->act, nullptr, nullptr, s->hidden, nullptr,
-             nullptr);
+        MIssue IA = {};
+        IA.kind = SK_ATTN;
+        is.push_back(IA);
+        // the residual read here includes the previous layer's FFN output
+        // (fixed-point accumulator), which is folded in and cleared
+        gemv("attn_out", l.wo, PRO_ATTN, EPI_RESID, s->attn, nullptr, nullptr, s->hidden, nullptr,
+             nullptr, li > 0, 1);
+        P->names.push_back("ffn");
+        const QW& dcm = m->down_cm[li];
+        MStage F = {};
+        F.kind = SK_FFN;
+        F.cfg = mk_cfg_for(l.gate_up.in_f);
+        F.pro = PRO_NORM;
+        F.K = l.gate_up.in_f;
+        F.N = l.gate_up.rows;
+        F.RC = mk_rc(F.cfg);
+        F.nunits = (int)I.hidden / 32;
+        F.per0 = 64 / F.RC;
+        F.per1 = ((int)I.dim + MK_DOWN_ROWS - 1) / MK_DOWN_ROWS;
+        F.N2 = (int)I.dim;
+        F.racc = s->racc;
+        F.payload = l.gate_up.payload;
+        F.scales = l.gate_up.scales;
+        F.payload2 = dcm.payload;
+        F.scales2 = dcm.scales;
+        F.base = s->hidden;
+        F.norm_w = l.ffn_norm;
+        st.push_back(F);
+        MIssue IF = {};
+        IF.kind = SK_FFN;
+        IF.pay0 = F.payload;
+        IF.sc0 = F.scales;
+        IF.pay1 = F.payload2;
+        IF.sc1 = F.scales2;
+        IF.n0 = F.nunits;
+        IF.rc = F.RC;
+        IF.nb = F.K / 32;
+        IF.n = F.N;
+        IF.per0 = F.per0;
+        IF.per1 = F.per1;
+        IF.dim = F.N2;
+        is.push_back(IF);
     }
     gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, s->hidden, m->final_norm, s->logits,
-         nullptr, s->xnorm);
+         nullptr, s->xnorm, I.n_layers > 0, 0);
     P->n_stages = (int)st.size();
     // ---- shared memory: ring | work | embedding row | issue table
     const size_t work = work_bytes_for(I, n_splits);
@@ -976,6 +1404,7 @@ int step_plan_create(cw_session* s) {
         if (v >= 1) pp.attn_min = v;
     }
     pp.eps = I.eps;
+    pp.inv_dim = 1.0f / (float)I.dim;
     pp.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
     pp.work_bytes = work;
     s->plan = P.release();
@@ -1073,6 +1502,14 @@ int step_profile(cw_session* s, size_t n_steps,
             auto& w = (*agg)[P->names[si]];
             w.first += 1;
             w.second += (double)(t1 - t0) * 1e-6;
+            double dmax = 0;  // the slowest CTA's own duration (span minus start skew)
+            for (int b = 0; b < P->grid; b++) {
+                const unsigned long long* q = &h[((size_t)si * P->grid + b) * MK_STAMPS];
+                if (q[1]) dmax = std::max(dmax, (double)(q[3] - q[0]));
+            }
+            auto& wm = (*agg)[std::string(P->names[si]) + ".cta_max"];
+            wm.first += 1;
+            wm.second += dmax * 1e-6;
             static const char* phase[3] = {"prologue", "main", "epilogue"};
             for (int k = 0; k < 3 && nw; k++) {
                 auto& r = (*agg)[std::string(P->names[si]) + "." + phase[k]];

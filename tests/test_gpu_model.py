@@ -125,15 +125,18 @@ def test_persistent_default_and_coverage(ctx, models, name):
     m.close()
 
 
-def test_persistent_equals_per_stage_long(ctx, orc, models):
-    """A 200-token prompt and 40 generated tokens on small-qwen3: the attention
-    stage runs with many active key splits.  Persistent and per-stage paths
-    both within tolerance of the oracle; persistent graph == direct, bit-exact."""
+@pytest.mark.parametrize("n_prompt", [200, 300])
+def test_persistent_equals_per_stage_long(ctx, orc, models, n_prompt):
+    """Long prompts and 40 generated tokens on small-qwen3: the attention stage
+    runs with several active key splits (200: 4 splits, merged by the
+    O-projection stage; 300: 5-6 splits, combined inside the attention stage).
+    Persistent and per-stage paths both within tolerance of the oracle;
+    persistent graph == direct, bit-exact."""
     from chat_wgpu_b200.model import Model
     path = models["small-qwen3"]
     om = orc.Model(path)
     rng = np.random.default_rng(11)
-    prompt = rng.integers(0, om.vocab, 200).astype(np.uint32)
+    prompt = rng.integers(0, om.vocab, n_prompt).astype(np.uint32)
     ref_toks, ref_logits = om.generate(prompt, 40, want_logits=True)
     m = Model(ctx, path)
     tp, lp = session_stream(m, prompt, 40, persistent=True)
