@@ -1,0 +1,1179 @@
+// cw_step.cuh -- device side of the persistent decode step (cw_step.cu).
+//
+// The step of src/model/qwen3.rs:128-191 + mod.rs:93-122 (embed, per layer
+// norm+QKV, QK-norm+RoPE+attention, o-proj+residual, norm+gate/up+SwiGLU,
+// down+residual, then norm+LM head+argmax and the next-input bookkeeping) runs
+// as a list of stages inside ONE kernel with one CTA per SM (16 warps).
+// Consecutive stages are separated by a grid-wide barrier (a monotonic 64-bit
+// counter, bounded wait); no kernel boundary, launch latency or grid drain
+// sits between stages.
+//
+// Weight streaming is decoupled from that dependency chain: every CTA knows
+// which weight chunks (16 KB of consecutive rows) it will consume in all the
+// GEMV stages of the step, in order.  Its thread 0 keeps an 8-slot ring of
+// shared memory filled with cp.async.bulk copies of the NEXT chunks in that
+// sequence, refilling a slot as soon as it is consumed, so copies for the
+// following stages (about two layers ahead) are in flight while the CTA waits
+// at a barrier.  The GEMV arithmetic is the q24 dp4a scheme of cw_gemv.cuh.
+//
+// Cross-CTA data (hidden, q/k/v, attention output, activations, partials) is
+// read with ld.global.cg so a stale L1 line can never be used.  All waits are
+// bounded by %globaltimer; a timeout sets the status word, every CTA drains
+// its copies and leaves, and the host reports CW_ERR_TIMEOUT.
+#pragma once
+
+#include "cw_attn.cuh"
+#include "cw_gemv.cuh"
+#include "cw_model.h"
+#include "cw_ops.h"
+
+namespace cw {
+
+constexpr int MK_THREADS = 512;
+constexpr int MK_WARPS = MK_THREADS / 32;
+constexpr int MK_SLOTS = 8;
+constexpr int MK_SLOT_PAY = 16384;  // nibble payload of one chunk
+constexpr int MK_SLOT_SC = 2048;    // its f16 scales
+constexpr int MK_SLOT_BYTES = MK_SLOT_PAY + MK_SLOT_SC;
+constexpr uint64_t MK_WAIT_NS = 2000000000ull;  // 2 s
+// profile stamps per stage and CTA: [0..3] %globaltimer (stage start, end of
+// prologue, end of main loop, end of work), [4..11] clock64 at the MK_CLK
+// points of the GEMV stages
+constexpr int MK_STAMPS = 16;
+enum {
+    CLK_START = 0,    // stage start (after the barrier)
+    CLK_AHEAD = 1,    // descriptor two stages ahead requested, K/V prefetch issued
+    CLK_LOADED = 2,   // prologue: global inputs arrived (NORM) / converted (X)
+    CLK_NORMED = 3,   // prologue: CTA-wide sum of squares done
+    CLK_Q24 = 4,      // prologue: q24 planes written
+    CLK_REGS = 5,     // planes in registers (after __syncthreads)
+    CLK_MAIN = 6,     // chunk loop done
+    CLK_END = 7,      // stage end
+    CLK_N = 8,
+    // first chunk of the main loop (extra points, reported separately)
+    CLK_WAITED = 8,   // its weights are in shared memory
+    CLK_SUMMED = 9,   // row partials complete (after __syncthreads)
+    CLK_ISSUED = 10,  // next copy issued
+};
+
+// GEMV work mapping for 16 warps (see cw_gemv.cuh): WPR warps per row, BPL
+// blocks per lane, RPW rows per warp; RC rows per chunk spread over NS ring
+// slots of RS = RC / NS rows each (RS * K/2 <= 16 KB).  Two-slot chunks halve
+// the per-chunk wait / reduce / barrier overhead of stages where a CTA has
+// several chunks (the LM head, the FFN's 64 gate/up rows).
+template <int WPR_, int BPL_, int RPW_, int NS_ = 1>
+struct MCfg {
+    static constexpr int WPR = WPR_, BPL = BPL_, RPW = RPW_, NS = NS_;
+    static constexpr int SLOTS = MK_WARPS / WPR;
+    static constexpr int RC = SLOTS * RPW;
+    static constexpr int RS = RC / NS;
+    static constexpr int NB_MAX = 32 * WPR * BPL;
+    static_assert(RC * WPR <= 64, "row partials fit rowred");
+};
+using MC0 = MCfg<1, 1, 2>;  // K <= 1024:  32 rows per chunk
+using MC1 = MCfg<1, 2, 1>;  // K <= 2048:  16 rows
+using MC2 = MCfg<2, 2, 1>;  // K <= 4096:   8 rows
+using MC3 = MCfg<4, 2, 1>;  // K <= 8192:   4 rows
+using MC4 = MCfg<8, 2, 1>;  // K <= 16384:  2 rows
+using MD0 = MCfg<1, 1, 4, 2>;  // the same K ranges, two slots per chunk: 64 rows
+using MD1 = MCfg<1, 2, 2, 2>;  // 32 rows
+using MD2 = MCfg<2, 2, 2, 2>;  // 16 rows
+using MD3 = MCfg<4, 2, 2, 2>;  //  8 rows
+using MD4 = MCfg<8, 2, 2, 2>;  //  4 rows
+constexpr int MK_NCFG = 5;     // configs 0-4 one slot per chunk, 5-9 two
+
+inline int mk_cfg_for(int K) {
+    const int nb = K / 32;
+    if (nb <= MC0::NB_MAX) return 0;
+    if (nb <= MC1::NB_MAX) return 1;
+    if (nb <= MC2::NB_MAX) return 2;
+    if (nb <= MC3::NB_MAX) return 3;
+    if (nb <= MC4::NB_MAX) return 4;
+    return -1;
+}
+inline int mk_rc(int cfg) {  // rows per chunk
+    static const int rc[2 * MK_NCFG] = {MC0::RC, MC1::RC, MC2::RC, MC3::RC, MC4::RC,
+                                        MD0::RC, MD1::RC, MD2::RC, MD3::RC, MD4::RC};
+    return rc[cfg];
+}
+inline int mk_ns(int cfg) { return cfg >= MK_NCFG ? 2 : 1; }  // ring slots per chunk
+
+enum { SK_GEMV = 0, SK_ATTN = 1, SK_FFN = 2 };
+
+// Fixed-point residual accumulator: the FFN stage adds its down-projection
+// partial sums into int64 words scaled by 2^32 with integer atomics, so the
+// total does not depend on the order in which CTAs arrive.
+constexpr float MK_FIX = 4294967296.0f;      // 2^32
+constexpr float MK_UNFIX = 2.3283064365386963e-10f;  // 2^-32
+constexpr int MK_DOWN_ROWS = MK_SLOT_PAY / 16;  // rows of one down-projection slot (1024)
+
+struct MStage {
+    int kind, cfg, pro, epi;
+    int K, N, RC, nchunks;
+    // FFN stage: act blocks (units), gate/up chunks and down slots per unit
+    int nunits, per0, per1, N2;
+    // residual accumulator: add it to the residual read here (acc_in), zero
+    // the rows written here (acc_zero)
+    int acc_in, acc_zero;
+    int pad0, pad1;
+    long long* racc;
+    const uint8_t* payload2;  // FFN: down projection, column-block-major [K/32 of down][dim][16]
+    const __half* scales2;    //      and its scales [K/32 of down][dim]
+    const void* pad_ptr;
+    const uint8_t* payload;
+    const __half* scales;
+    const float* x;        // PRO_X input
+    const float* base;     // PRO_NORM input (null: this CTA's embedding row)
+    const float* norm_w;
+    float* xn_out;         // CTA 0 stores the normalised input here
+    float* y;
+    const float* bias;
+    // attention stage of one layer
+    const float* q_norm;
+    const float* k_norm;
+    float* kc;             // this layer's K cache [n_kv][max_seq][hd]
+    float* vc;
+};
+static_assert(sizeof(MStage) % 16 == 0, "stage descriptors are copied in 16-byte pieces");
+
+// The weight-copy schedule of one stage (nchunks 0: no weights), kept in
+// shared memory so the copy issuer never waits on a global read.
+struct MIssue {
+    const uint8_t* pay0;  // GEMV weight, or the FFN gate/up matrix
+    const __half* sc0;
+    const uint8_t* pay1;  // FFN: down projection, column-block-major
+    const __half* sc1;
+    int n0;               // GEMV: chunks; FFN: units (act blocks)
+    int rc, nb, n;        // rows per copy (ring slot), blocks per row, rows of pay0
+    int per0, per1;       // GEMV: slots per chunk; FFN: gate/up copies and down slots per unit
+    int dim;              // FFN: rows of the down projection
+    int kind;
+};
+static_assert(sizeof(MIssue) == 64, "issue entries are copied as four int4");
+
+struct MParams {
+    const MStage* stages;
+    const MIssue* issues;
+    int n_stages;
+    DevState* st;
+    int* status;
+    unsigned long long* bar;
+    const uint8_t* emb_payload;
+    const __half* emb_scales;
+    float embed_scale;
+    float* hidden;
+    const float* qkv;
+    float* attn;
+    const unsigned* prompt;
+    unsigned* toks;
+    float* part;
+    unsigned* counters;
+    const float* inv_freq;
+    int dim, n_heads, n_kv, hd, max_seq, n_splits, part_stride, decode;
+    int attn_min;  // keys per attention split before splitting further
+    float eps, scale;
+    float inv_dim;      // 1/dim: the mean of squares as a product (exact for power-of-two dims)
+    size_t work_bytes;  // shared-memory work region (q24 + hbuf + wbuf, or attention scratch)
+    // profiling only: per stage and CTA, %globaltimer at the stage's start
+    // (after its barrier), after its input prologue, after its main loop and
+    // at the end of its work ([stage][cta][MK_STAMPS]; 0 = no work here)
+    unsigned long long* stamps;
+};
+
+// keys per attention split in the persistent step: one iteration of all
+// 16 warps (4 keys each) before a split is worth its combine
+constexpr int MK_ATTN_MIN = MK_WARPS * ATTN_U;
+constexpr int MK_PRE = 2;  // epilogue addends preloaded per stage (chunks)
+// With 2..MK_DEFER active key splits, the attention stage only publishes each
+// split's (accumulator, max, denominator) and the O-projection stage merges
+// the splits while it builds its input (no combine step, fence or counter
+// inside the attention stage); with more splits the attention stage combines.
+constexpr int MK_DEFER = 4;
+enum { PRO_ATTN = 2 };  // prologue: merged attention splits (see MK_DEFER)
+
+// per-CTA state shared by all threads
+struct MShared {
+    uint64_t full[MK_SLOTS];
+    uint64_t pol;  // L2 evict-first policy of the weight stream
+    int it_stage, it_t, it_j, issued, abort;
+    __align__(16) float act[32];  // FFN: the act block of the current unit
+    __align__(16) uint4 aq[6];    // FFN: its q24 planes
+    int acb;
+    float asb;
+    __align__(16) float red[2][MK_WARPS];  // CTA-sum partials, alternating per call
+    unsigned long long keys[MK_WARPS];
+};
+
+struct MCtx {
+    unsigned char* ring;
+    unsigned char* work;
+    float* emb;
+    const MIssue* iss;  // shared-memory copy of the issue table
+    float* rowred;      // 2 x 64 row partials
+    MShared* sh;
+    int seq;            // chunks consumed by this CTA so far (same in every thread)
+    int redsel;         // CTA-sum buffer of the next call
+    int nch;            // chunks consumed (row-partial buffer parity)
+    int pos;
+    unsigned long long* stamp;  // this stage's stamps (profiling) or null
+};
+
+// CTA-wide sum with one __syncthreads: the warps' partials go to one of two
+// alternating buffers, so a call never overwrites the buffer the previous
+// call is still reading (every thread passed that call's barrier first).
+// Fixed summation order.
+__device__ __forceinline__ float mk_cta_sum(float v, MCtx& c) {
+    static_assert(MK_WARPS == 16, "four float4 partial loads");
+    v = warp_sum(v);
+    float* r = c.sh->red[c.redsel];
+    c.redsel ^= 1;
+    if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = v;
+    __syncthreads();
+    const float4* r4 = reinterpret_cast<const float4*>(r);
+    const float4 a = r4[0], b = r4[1], d = r4[2], e = r4[3];
+    return (((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w))) +
+           (((d.x + d.y) + (d.z + d.w)) + ((e.x + e.y) + (e.z + e.w)));
+}
+
+// One lane of the last warp issues the weight copies, so the copy issue
+// never delays warp 0 (epilogue rows, barrier arrival).
+constexpr int MK_ISSUER = MK_THREADS - 32;
+
+__device__ __forceinline__ void mk_clk(const MCtx& c, int k) {
+    if (c.stamp && threadIdx.x == 0) c.stamp[4 + k] = clock64();
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_volatile_i32(const int* p) {
+    int v;
+    asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Thread 0: issue the copy of this CTA's next weight chunk (in the stage
+// order) into the next ring slot.  Returns false when the step has no more.
+__device__ __forceinline__ void mk_issue_copy(MCtx& c, const uint8_t* pay, const __half* sc,
+                                              unsigned pb, unsigned sb) {
+    MShared* sh = c.sh;
+    const int slot = sh->issued % MK_SLOTS;
+    unsigned char* dst = c.ring + (size_t)slot * MK_SLOT_BYTES;
+    // the slot's previous contents were read before the __syncthreads that
+    // precedes this call (a generic-proxy read followed by an async-proxy
+    // write: ordered by that barrier, no proxy fence)
+    mbar_expect_tx(&sh->full[slot], pb + sb);  // pb == 0: a plain arrive (rows past the end)
+    if (pb) {
+        bulk_g2s_hint(dst, pay, pb, &sh->full[slot], sh->pol);
+        bulk_g2s_hint(dst + MK_SLOT_PAY, sc, sb, &sh->full[slot], sh->pol);
+    }
+    sh->issued++;
+}
+
+__device__ inline bool mk_issue_next(const MParams& p, MCtx& c) {
+    MShared* sh = c.sh;
+    while (sh->it_stage < p.n_stages) {
+        const MIssue& I = c.iss[sh->it_stage];
+        const long u = blockIdx.x + (long)sh->it_t * gridDim.x;
+        if (I.kind == SK_GEMV) {  // copy it_t: part it_t % per0 of this CTA's chunk it_t / per0
+            const long ch = blockIdx.x + (long)(sh->it_t / I.per0) * gridDim.x;
+            if (ch < I.n0) {
+                const long row0 = (ch * I.per0 + sh->it_t % I.per0) * I.rc;
+                const int rows = (int)max(0L, min((long)I.rc, (long)I.n - row0));
+                mk_issue_copy(c, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
+                              (unsigned)rows * I.nb * 16, (unsigned)rows * I.nb * 2);
+                sh->it_t++;
+                return true;
+            }
+        }
+        if (I.kind == SK_FFN && u < I.n0) {
+            const int j = sh->it_j;
+            if (j < I.per0) {  // gate/up rows [64u + j*rc, +rc)
+                const long row0 = u * 64 + (long)j * I.rc;
+                mk_issue_copy(c, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
+                              (unsigned)I.rc * I.nb * 16, (unsigned)I.rc * I.nb * 2);
+            } else {  // down rows [k*1024, ...) of column block u
+                const int k = j - I.per0, r0 = k * MK_DOWN_ROWS;
+                const int rows = min(MK_DOWN_ROWS, I.dim - r0);
+                const size_t off = (size_t)u * I.dim + r0;
+                mk_issue_copy(c, I.pay1 + off * 16, I.sc1 + off, (unsigned)rows * 16,
+                              (unsigned)rows * 2);
+            }
+            if (++sh->it_j == I.per0 + I.per1) {
+                sh->it_j = 0;
+                sh->it_t++;
+            }
+            return true;
+        }
+        sh->it_stage++;
+        sh->it_t = 0;
+        sh->it_j = 0;
+    }
+    return false;
+}
+
+// Wait (bounded) for every copy issued and not yet consumed, so no bulk copy
+// writes shared memory after the CTA has left.
+__device__ inline void mk_drain(MCtx& c) {
+    if (threadIdx.x == MK_ISSUER) {
+        for (int q = c.seq; q < c.sh->issued; q++)
+            mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS);
+    }
+    __syncthreads();
+}
+
+__device__ inline void mk_fail(const MParams& p, MCtx& c) {
+    if (threadIdx.x == 0) {
+        atomicExch(p.status, (int)DEV_TIMEOUT);
+        c.sh->abort = 1;
+    }
+    __syncthreads();
+}
+
+// Grid-wide barrier: arrive (release), then poll (acquire) until the counter
+// reaches `target`; the status word and the time limit are checked every 64
+// polls.
+__device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long long target) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        red_release_add(p.bar, 1ull);
+        uint64_t t0 = 0;
+        int ok = 1;
+        for (unsigned it = 1; ld_acquire_u64(p.bar) < target; it++) {
+            if ((it & 63) == 0) {
+                const uint64_t now = global_ns();
+                if (t0 == 0) t0 = now;
+                if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (!ok) {
+            atomicExch(p.status, (int)DEV_TIMEOUT);
+            c.sh->abort = 1;
+        }
+    }
+    __syncthreads();
+    return c.sh->abort == 0;
+}
+
+// Stage descriptors travel global -> shared by cp.async (16 bytes per thread
+// of the loader lanes, no register staging), requested two stages ahead and
+// waited for at the end of the current stage, so no thread ever stalls on
+// the descriptor table.
+constexpr int MK_LOADER = MK_THREADS - 32;  // first thread of the loader lanes (last warp)
+static_assert(sizeof(MStage) / 16 <= 32, "one 16-byte piece per loader lane");
+__device__ __forceinline__ void mk_load_stage(const MParams& p, int si, MStage* dst) {
+    const int l = threadIdx.x - MK_LOADER;
+    if (si < p.n_stages && l >= 0 && l < (int)(sizeof(MStage) / 16)) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         smem_addr(reinterpret_cast<char*>(dst) + 16 * l)),
+                     "l"(reinterpret_cast<const char*>(p.stages + si) + 16 * l)
+                     : "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+}
+__device__ __forceinline__ void mk_load_stage_wait() {
+    if (threadIdx.x >= MK_LOADER) asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// ---- stage input -> q24 planes ---------------------------------------------------
+// Four consecutive elements per lane: lane L of a warp covers block
+// 4t + L/8 (t: the warp's quad group), elements 4*(L%8) .. 4*(L%8)+3, loaded
+// as one float4.  The block max and the integer sum are 3-step shuffles
+// within the 8 lanes of a block, and each lane writes one 32-bit word per
+// byte plane (its 4 elements' bytes, packed with __byte_perm) -- the planes
+// q24_block writes, in a quarter of the instructions.
+constexpr int MK_QB = 2;  // quad groups per warp per batch
+
+__device__ __forceinline__ void mk_q24_quad(const Q24& s, int b, bool valid, const float4& v,
+                                            int lane) {
+    unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                     max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+    m = max(m, __shfl_xor_sync(FULL, m, 1));
+    m = max(m, __shfl_xor_sync(FULL, m, 2));
+    m = max(m, __shfl_xor_sync(FULL, m, 4));
+    int X0, X1, X2, X3;
+    float sb;
+    q24_scale(m, v.x, X0, sb);
+    q24_scale(m, v.y, X1, sb);
+    q24_scale(m, v.z, X2, sb);
+    q24_scale(m, v.w, X3, sb);
+    const int g8 = lane & 7, half = g8 >> 2, w = g8 & 3;
+    if (valid) {
+        uint32_t* pw = reinterpret_cast<uint32_t*>(s.pl);
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            const unsigned sel = (unsigned)pl | ((4u + pl) << 4);
+            const unsigned lo = __byte_perm((unsigned)X0, (unsigned)X1, sel);
+            const unsigned hi = __byte_perm((unsigned)X2, (unsigned)X3, sel);
+            pw[((size_t)(pl * 2 + half) * s.nb + b) * 4 + w] = __byte_perm(lo, hi, 0x5410);
+        }
+    }
+    int sx = (X0 + X1) + (X2 + X3);
+    sx += __shfl_xor_sync(FULL, sx, 1);
+    sx += __shfl_xor_sync(FULL, sx, 2);
+    sx += __shfl_xor_sync(FULL, sx, 4);
+    if (valid && g8 == 0) {
+        s.cb[b] = 8 * sx;
+        s.sb[b] = sb;
+    }
+}
+
+__device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+__device__ __forceinline__ float4 f4_norm(const float4& h, float inv, const float4& g) {
+    return make_float4(__fmul_rn(__fmul_rn(h.x, inv), g.x), __fmul_rn(__fmul_rn(h.y, inv), g.y),
+                       __fmul_rn(__fmul_rn(h.z, inv), g.z), __fmul_rn(__fmul_rn(h.w, inv), g.w));
+}
+
+// The stage input as q24 planes.  PRO_X: x from global.  PRO_NORM: rmsnorm
+// of `base` with the gains (norm.wgsl:20-56).  PRO_ATTN: merged attention
+// splits.  Each batch issues all of its global loads before using any.
+template <int PRO>
+__device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24& q, float* hbuf,
+                            float* wbuf, MCtx& c) {
+    const int nb = S.K / 32, nq = nb / 4;  // quad groups (nb is a multiple of 8)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane >> 3, e0 = 4 * (lane & 7);
+    if (PRO == PRO_ATTN) {
+        // the attention output of 2..MK_DEFER splits per head, merged here
+        // (attention.wgsl:88-95 across splits): per head M = max_s m_s,
+        // c_s = exp(m_s - M), 1/L with L = sum_s l_s c_s; then
+        // x = (sum_s acc_s c_s) / L per element
+        const int hd = p.hd, W = hd + 2, na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
+        float* cw = hbuf;  // [n_heads][na + 1]
+        for (int h = warp; h < p.n_heads; h += MK_WARPS) {
+            const float* ph = p.part + (size_t)h * p.part_stride * W;
+            const float m = lane < na ? __ldcg(ph + (size_t)lane * W + hd) : REF_NEG_INF;
+            const float l = lane < na ? __ldcg(ph + (size_t)lane * W + hd + 1) : 0.f;
+            const float M = warp_max(m);
+            const float cc = lane < na ? expf(m - M) : 0.f;
+            const float L = warp_sum(l * cc);
+            if (lane < na) cw[h * (na + 1) + lane] = cc;
+            if (lane == 0) cw[h * (na + 1) + na] = 1.0f / L;
+        }
+        __syncthreads();
+        for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
+            float4 v[MK_QB];
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                v[k] = f4_zero();
+                if (b < nb) {
+                    const int i0 = b * 32 + e0, h = i0 / hd, d0 = i0 - h * hd;
+                    const float* ph = p.part + (size_t)h * p.part_stride * W + d0;
+                    const float* cc = cw + h * (na + 1);
+                    float2 lo[MK_DEFER], hi[MK_DEFER];  // (W even, d0 % 4 == 0: 8-byte aligned)
+#pragma unroll
+                    for (int s = 0; s < MK_DEFER; s++) {
+                        const float2* q2 = reinterpret_cast<const float2*>(ph + (size_t)s * W);
+                        lo[s] = s < na ? __ldcg(q2) : make_float2(0.f, 0.f);
+                        hi[s] = s < na ? __ldcg(q2 + 1) : make_float2(0.f, 0.f);
+                    }
+                    float r[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        float a[MK_DEFER];
+#pragma unroll
+                        for (int s = 0; s < MK_DEFER; s++) {
+                            const float2 t2 = e < 2 ? lo[s] : hi[s];
+                            a[s] = (s < na ? ((e & 1) ? t2.y : t2.x) : 0.f) * cc[s < na ? s : 0];
+                        }
+                        r[e] = ((a[0] + a[1]) + (a[2] + a[3])) * cc[na];
+                    }
+                    v[k] = make_float4(r[0], r[1], r[2], r[3]);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                if (t0 + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
+            }
+        }
+        mk_clk(c, CLK_LOADED);
+        mk_clk(c, CLK_NORMED);
+        return;
+    }
+    if (PRO == PRO_X) {
+        for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
+            float4 v[MK_QB];
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                v[k] = b < nb ? __ldcg(reinterpret_cast<const float4*>(S.x + b * 32 + e0)) : f4_zero();
+            }
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (t0 + k * MK_WARPS) + sub;
+                if (t0 + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
+            }
+        }
+        mk_clk(c, CLK_LOADED);
+        mk_clk(c, CLK_NORMED);
+        return;
+    }
+    const float* src = S.base ? S.base : c.emb;
+    const bool gsrc = S.base != nullptr;
+    const bool wx = S.xn_out && blockIdx.x == 0;
+    // the residual: base (+ the fixed-point FFN accumulator when acc_in)
+    auto ld_src = [&](int i) {
+        float4 h = gsrc ? __ldcg(reinterpret_cast<const float4*>(src + i))
+                        : *reinterpret_cast<const float4*>(src + i);
+        if (S.acc_in) {
+            const longlong2 a0 = __ldcg(reinterpret_cast<const longlong2*>(S.racc + i));
+            const longlong2 a1 = __ldcg(reinterpret_cast<const longlong2*>(S.racc + i + 2));
+            h.x = h.x + __ll2float_rn(a0.x) * MK_UNFIX;
+            h.y = h.y + __ll2float_rn(a0.y) * MK_UNFIX;
+            h.z = h.z + __ll2float_rn(a1.x) * MK_UNFIX;
+            h.w = h.w + __ll2float_rn(a1.y) * MK_UNFIX;
+        }
+        return h;
+    };
+    float ss = 0.f;
+    if (nq <= MK_WARPS * MK_QB) {  // one batch: everything stays in registers
+        float4 v[MK_QB], w[MK_QB];
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub, i = b * 32 + e0;
+            v[k] = b < nb ? ld_src(i) : f4_zero();
+            w[k] = b < nb ? __ldg(reinterpret_cast<const float4*>(S.norm_w + i)) : f4_zero();
+        }
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {  // padding adds +0
+            ss = fmaf(v[k].x, v[k].x, ss);
+            ss = fmaf(v[k].y, v[k].y, ss);
+            ss = fmaf(v[k].z, v[k].z, ss);
+            ss = fmaf(v[k].w, v[k].w, ss);
+        }
+        mk_clk(c, CLK_LOADED);
+        ss = mk_cta_sum(ss, c);
+        mk_clk(c, CLK_NORMED);
+        const float inv = 1.0f / sqrtf(ss * p.inv_dim + p.eps);
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub;
+            v[k] = f4_norm(v[k], inv, w[k]);
+            if (wx && b < nb) *reinterpret_cast<float4*>(S.xn_out + b * 32 + e0) = v[k];
+        }
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub;
+            if (warp + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
+        }
+        return;
+    }
+    for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
+        float4 v[MK_QB], w[MK_QB];
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (t0 + k * MK_WARPS) + sub, i = b * 32 + e0;
+            v[k] = b < nb ? ld_src(i) : f4_zero();
+            w[k] = b < nb ? __ldg(reinterpret_cast<const float4*>(S.norm_w + i)) : f4_zero();
+        }
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (t0 + k * MK_WARPS) + sub, i = b * 32 + e0;
+            if (b < nb) {
+                *reinterpret_cast<float4*>(hbuf + i) = v[k];
+                *reinterpret_cast<float4*>(wbuf + i) = w[k];
+            }
+            ss = fmaf(v[k].x, v[k].x, ss);
+            ss = fmaf(v[k].y, v[k].y, ss);
+            ss = fmaf(v[k].z, v[k].z, ss);
+            ss = fmaf(v[k].w, v[k].w, ss);
+        }
+    }
+    mk_clk(c, CLK_LOADED);
+    ss = mk_cta_sum(ss, c);
+    mk_clk(c, CLK_NORMED);
+    const float inv = 1.0f / sqrtf(ss * p.inv_dim + p.eps);
+    for (int t = warp; t < nq; t += MK_WARPS) {
+        const int b = 4 * t + sub, i = b * 32 + e0;
+        float4 v = f4_zero();
+        if (b < nb) {
+            v = f4_norm(*reinterpret_cast<const float4*>(hbuf + i), inv,
+                        *reinterpret_cast<const float4*>(wbuf + i));
+            if (wx) *reinterpret_cast<float4*>(S.xn_out + i) = v;
+        }
+        mk_q24_quad(q, b, b < nb, v, lane);
+    }
+}
+
+// ---- GEMV stage ------------------------------------------------------------------
+// T = sum_j (q_j - 8) X_j of one Q4_0 block (16 payload bytes w) against one
+// q24 block (planes xa: elements 0-15, xb: 16-31; cb = 8 * sum X): six
+// independent dp4a chains of four, low and high nibbles apart.
+__device__ __forceinline__ float mk_block_dot(const uint4& w4, const uint4 (&xa)[3],
+                                              const uint4 (&xb)[3], int cb) {
+    const unsigned w[4] = {w4.x, w4.y, w4.z, w4.w};
+    const unsigned a0[4] = {xa[0].x, xa[0].y, xa[0].z, xa[0].w};
+    const unsigned b0[4] = {xb[0].x, xb[0].y, xb[0].z, xb[0].w};
+    const unsigned a1[4] = {xa[1].x, xa[1].y, xa[1].z, xa[1].w};
+    const unsigned b1[4] = {xb[1].x, xb[1].y, xb[1].z, xb[1].w};
+    const unsigned a2[4] = {xa[2].x, xa[2].y, xa[2].z, xa[2].w};
+    const unsigned b2[4] = {xb[2].x, xb[2].y, xb[2].z, xb[2].w};
+    int s0l = 0, s0h = 0, s1l = 0, s1h = 0, s2l = 0, s2h = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const unsigned lo = w[e] & 0x0f0f0f0fu;
+        const unsigned hi = (w[e] >> 4) & 0x0f0f0f0fu;
+        s0l = dp4a_uu(lo, a0[e], s0l);
+        s0h = dp4a_uu(hi, b0[e], s0h);
+        s1l = dp4a_uu(lo, a1[e], s1l);
+        s1h = dp4a_uu(hi, b1[e], s1h);
+        s2l = dp4a_us(lo, a2[e], s2l);
+        s2h = dp4a_us(hi, b2[e], s2h);
+    }
+    const int s01 = (s0l + s0h) + ((s1l + s1h) << 8) - cb;
+    return fmaf((float)(s2l + s2h), 65536.0f, (float)s01);
+}
+
+// The input vector of a GEMV stage as q24 planes in the work region.
+__device__ __forceinline__ void mk_input(const MParams& p, const MStage& S, const Q24& q,
+                                         MCtx& c) {
+    float* hbuf = reinterpret_cast<float*>(c.work + al16(q24_bytes(q.nb)));
+    float* wbuf = hbuf + S.K;
+    if (S.pro == PRO_NORM) {
+        mk_prologue<PRO_NORM>(p, S, q, hbuf, wbuf, c);
+    } else if (S.pro == PRO_ATTN) {
+        const int na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
+        if (na >= 2 && na <= MK_DEFER)
+            mk_prologue<PRO_ATTN>(p, S, q, hbuf, wbuf, c);
+        else
+            mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
+    } else {
+        mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
+    }
+}
+
+// This lane's blocks of the q24 planes, kept in registers for the chunk loop.
+template <class CF>
+struct MRegs {
+    uint4 xa[CF::BPL][3], xb[CF::BPL][3];
+    int cb[CF::BPL];
+    float sb[CF::BPL];
+};
+template <class CF>
+__device__ __forceinline__ void mk_load_regs(const Q24& q, MRegs<CF>& R) {
+    constexpr int WPR = CF::WPR, BPL = CF::BPL;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wsub = warp % WPR;
+#pragma unroll
+    for (int k = 0; k < BPL; k++) {
+        const int b = wsub * 32 + lane + k * 32 * WPR;
+        const bool in = b < q.nb;
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            R.xa[k][pl] = in ? q.pl[(pl * 2 + 0) * q.nb + b] : make_uint4(0, 0, 0, 0);
+            R.xb[k][pl] = in ? q.pl[(pl * 2 + 1) * q.nb + b] : make_uint4(0, 0, 0, 0);
+        }
+        R.cb[k] = in ? q.cb[b] : 0;
+        R.sb[k] = in ? q.sb[b] : 0.f;
+    }
+}
+
+// One chunk of RC rows: wait for ring slot c.seq, dot each row with the
+// planes in R, reduce the per-warp partials into rb[row * WPR + sub], then
+// (after __syncthreads) issue the next copy into the freed slot.  Returns
+// rb, or null after a timed-out wait (the failure is recorded).
+template <class CF>
+__device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int nb, int rows,
+                                                 const MRegs<CF>& R, bool first) {
+    constexpr int WPR = CF::WPR, BPL = CF::BPL, RPW = CF::RPW, NS = CF::NS, RS = CF::RS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wsub = warp % WPR, slot = warp / WPR;
+    bool ok = true;
+#pragma unroll
+    for (int h = 0; h < NS; h++) {
+        const int q = c.seq + h;
+        ok = mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS) && ok;
+    }
+    if (__syncthreads_or(!ok)) {
+        mk_fail(p, c);
+        return nullptr;
+    }
+    if (first) mk_clk(c, CLK_WAITED);
+    // this warp's rows lie in one slot (RS is a multiple of RPW)
+    const int h = (slot * RPW) / RS;
+    const unsigned char* pay = c.ring + (size_t)((c.seq + h) % MK_SLOTS) * MK_SLOT_BYTES;
+    const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+    float* rb = c.rowred + (size_t)(c.nch & 1) * 64;
+    uint4 w4[RPW][BPL];
+    float dd[RPW][BPL];
+#pragma unroll
+    for (int j = 0; j < RPW; j++) {
+        const int r = slot * RPW + j, rr = r - h * RS;
+#pragma unroll
+        for (int k = 0; k < BPL; k++) {
+            const int b = wsub * 32 + lane + k * 32 * WPR;
+            const bool in = r < rows && b < nb;
+            const size_t blk = in ? (size_t)rr * nb + b : 0;
+            w4[j][k] = in ? reinterpret_cast<const uint4*>(pay)[blk] : make_uint4(0, 0, 0, 0);
+            dd[j][k] = in ? __half2float(scs[blk]) : 0.f;
+        }
+    }
+    float acc[RPW];
+#pragma unroll
+    for (int j = 0; j < RPW; j++) {
+        acc[j] = 0.f;
+#pragma unroll
+        for (int k = 0; k < BPL; k++)
+            acc[j] = fmaf(dd[j][k] * R.sb[k], mk_block_dot(w4[j][k], R.xa[k], R.xb[k], R.cb[k]),
+                          acc[j]);
+    }
+    const float v = warp_reduce_rows<RPW>(acc, lane);
+    if ((lane & (32 / RPW - 1)) == 0) rb[(slot * RPW + lane / (32 / RPW)) * WPR + wsub] = v;
+    __syncthreads();  // slots consumed, row partials complete
+    if (first) mk_clk(c, CLK_SUMMED);
+    if (threadIdx.x == MK_ISSUER)
+        for (int k = 0; k < NS; k++) mk_issue_next(p, c);
+    if (first) mk_clk(c, CLK_ISSUED);
+    c.seq += NS;
+    c.nch++;
+    return rb;
+}
+
+template <class CF>
+__device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
+    constexpr int WPR = CF::WPR, RC = CF::RC;
+    const int nb = S.K / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if ((int)blockIdx.x >= S.nchunks) return true;  // no rows of this stage here
+    // epilogue addends (old residual or bias) of the first chunks, requested
+    // now so they arrive while the prologue runs
+    const bool has_pre = S.epi == EPI_RESID || (S.epi == EPI_STORE && S.bias);
+    float pre[MK_PRE];
+#pragma unroll
+    for (int t = 0; t < MK_PRE; t++) {
+        const long row = (blockIdx.x + (long)t * gridDim.x) * RC + tid;
+        pre[t] = 0.f;
+        if (has_pre && tid < RC && row < S.N) {
+            pre[t] = S.epi == EPI_RESID ? __ldcg(S.y + row) : __ldg(S.bias + row);
+            if (S.epi == EPI_RESID && S.acc_in)
+                pre[t] = pre[t] + __ll2float_rn(__ldcg(S.racc + row)) * MK_UNFIX;
+        }
+    }
+    const Q24 q = q24_carve(c.work, nb);
+    mk_input(p, S, q, c);
+    mk_clk(c, CLK_Q24);
+    __syncthreads();
+    MRegs<CF> R;
+    mk_load_regs<CF>(q, R);
+    if (c.stamp && tid == 0) c.stamp[1] = global_ns();
+    mk_clk(c, CLK_REGS);
+    unsigned long long best = argmax_key_init();
+    int t = 0;
+    for (long chunk = blockIdx.x; chunk < S.nchunks; chunk += gridDim.x, t++) {
+        const long row0 = chunk * RC;
+        const int rows = (int)min((long)RC, (long)S.N - row0);
+        float add = 0.f;
+#pragma unroll
+        for (int u = 0; u < MK_PRE; u++)
+            if (u == t) add = pre[u];
+        if (t >= MK_PRE && has_pre && tid < rows) {  // later chunks: requested before the wait
+            add = S.epi == EPI_RESID ? __ldcg(S.y + row0 + tid) : __ldg(S.bias + row0 + tid);
+            if (S.epi == EPI_RESID && S.acc_in)
+                add = add + __ll2float_rn(__ldcg(S.racc + row0 + tid)) * MK_UNFIX;
+        }
+        const float* rb = mk_chunk<CF>(p, c, nb, rows, R, t == 0);
+        if (!rb) return false;
+        // epilogue: fixed-order sum of the WPR partials of each row
+        if (S.epi == EPI_GLU) {
+            if (tid < RC / 2 && 2 * tid + 1 < rows) {
+                const int r0 = 2 * tid;
+                float gv = 0.f, uv = 0.f;
+#pragma unroll
+                for (int w = 0; w < WPR; w++) {
+                    gv += rb[r0 * WPR + w];
+                    uv += rb[(r0 + 1) * WPR + w];
+                }
+                S.y[(row0 + r0) / 2] = silu_ref_f(gv) * uv;
+            }
+        } else if (tid < rows) {
+            float vv = 0.f;
+#pragma unroll
+            for (int w = 0; w < WPR; w++) vv += rb[tid * WPR + w];
+            const long row = row0 + tid;
+            if (S.epi == EPI_HEAD) {
+                S.y[row] = vv;
+                const unsigned long long kk = argmax_key(vv, (unsigned)row);
+                best = kk > best ? kk : best;
+            } else {
+                S.y[row] = has_pre ? (S.epi == EPI_RESID ? add + vv : vv + add) : vv;
+                if (S.acc_zero) S.racc[row] = 0;
+            }
+        }
+    }
+    if (c.stamp && tid == 0) c.stamp[2] = global_ns();
+    mk_clk(c, CLK_MAIN);
+    if (S.epi == EPI_HEAD) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long tt = __shfl_xor_sync(FULL, best, o);
+            best = tt > best ? tt : best;
+        }
+        if (lane == 0) c.sh->keys[warp] = best;
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < MK_WARPS; w++) best = c.sh->keys[w] > best ? c.sh->keys[w] : best;
+            atomicMax(&p.st->key, best);
+        }
+    }
+    return true;
+}
+
+// ---- FFN stage: gate/up + SwiGLU + down projection, one act block per unit --------
+// Unit u owns act block u (act rows 32u .. 32u+31 = gate/up rows 64u ..
+// 64u+63, glu.wgsl:25): its gate/up chunks give the 32 act values, which are
+// converted to one q24 block, and the down projection's column block u
+// (MK_DOWN_ROWS rows per ring slot, one Q4_0 block per row) turns them into a
+// partial sum for every output row, added into the fixed-point residual
+// accumulator (the next stage that reads the residual adds it).
+template <class CF>
+__device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
+    constexpr int WPR = CF::WPR, RC = CF::RC;
+    const int nb = S.K / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if ((int)blockIdx.x >= S.nunits) return true;
+    const Q24 q = q24_carve(c.work, nb);
+    mk_input(p, S, q, c);
+    mk_clk(c, CLK_Q24);
+    __syncthreads();
+    MRegs<CF> R;
+    mk_load_regs<CF>(q, R);
+    if (c.stamp && tid == 0) c.stamp[1] = global_ns();
+    mk_clk(c, CLK_REGS);
+    MShared* sh = c.sh;
+    bool first = true;
+    for (int u = blockIdx.x; u < S.nunits; u += gridDim.x) {
+        for (int j = 0; j < S.per0; j++) {  // gate/up rows 64u + j*RC ..
+            const float* rb = mk_chunk<CF>(p, c, nb, RC, R, first);
+            first = false;
+            if (!rb) return false;
+            if (tid < RC / 2) {
+                const int r0 = 2 * tid;
+                float gv = 0.f, uv = 0.f;
+#pragma unroll
+                for (int w = 0; w < WPR; w++) {
+                    gv += rb[r0 * WPR + w];
+                    uv += rb[(r0 + 1) * WPR + w];
+                }
+                sh->act[(j * RC + r0) / 2] = silu_ref_f(gv) * uv;
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {  // the act block as q24 (lanes 0-7: four elements each)
+            Q24 aq;
+            aq.pl = sh->aq;
+            aq.cb = &sh->acb;
+            aq.sb = &sh->asb;
+            aq.nb = 1;
+            const float4 v = lane < 8 ? reinterpret_cast<const float4*>(sh->act)[lane]
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            mk_q24_quad(aq, 0, lane < 8, v, lane);
+        }
+        __syncthreads();
+        uint4 xa[3], xb[3];
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            xa[pl] = sh->aq[pl * 2 + 0];
+            xb[pl] = sh->aq[pl * 2 + 1];
+        }
+        const int acb = sh->acb;
+        const float asb = sh->asb;
+        for (int k = 0; k < S.per1; k++) {  // down rows k*MK_DOWN_ROWS ..
+            const int r0 = k * MK_DOWN_ROWS, rows = min(MK_DOWN_ROWS, S.N2 - r0);
+            const int rs = c.seq % MK_SLOTS;
+            const unsigned par = (unsigned)((c.seq / MK_SLOTS) & 1);
+            const bool ok = mbar_wait(&sh->full[rs], par, MK_WAIT_NS);
+            if (__syncthreads_or(!ok)) {
+                mk_fail(p, c);
+                return false;
+            }
+            const unsigned char* pay = c.ring + (size_t)rs * MK_SLOT_BYTES;
+            const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+            for (int r = tid; r < rows; r += MK_THREADS) {
+                const uint4 w4 = reinterpret_cast<const uint4*>(pay)[r];
+                const float d = __half2float(scs[r]);
+                const float part = fmaf(d * asb, mk_block_dot(w4, xa, xb, acb), 0.f);
+                const long long fx = __float2ll_rn(part * MK_FIX);
+                atomicAdd(reinterpret_cast<unsigned long long*>(S.racc + r0 + r),
+                          (unsigned long long)fx);
+            }
+            __syncthreads();  // slot consumed
+            if (tid == MK_ISSUER) mk_issue_next(p, c);
+            c.seq++;
+        }
+    }
+    if (c.stamp && tid == 0) c.stamp[2] = global_ns();
+    mk_clk(c, CLK_MAIN);
+    return true;
+}
+
+// ---- attention stage: QK-norm + RoPE + K/V write + split-KV attention -----------
+// Thread 0 of the CTA that will run attention unit blockIdx.x: pull the cached
+// K/V rows of that unit into L2 while the stage before it runs.
+__device__ inline void mk_kv_prefetch(const MParams& p, const MStage& A, const MCtx& c) {
+    const int seq = c.pos + 1;
+    const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
+    const int u = blockIdx.x;
+    if (u >= p.n_kv * n_active) return;
+    const int g = u % p.n_kv, split = u / p.n_kv;
+    int jlo, jhi;
+    attn_range(seq, 0, split, n_active, &jlo, &jhi);
+    const int j1 = min(jhi, c.pos);
+    if (j1 <= jlo) return;
+    const float* kb = A.kc + (size_t)g * p.max_seq * p.hd;
+    const float* vb = A.vc + (size_t)g * p.max_seq * p.hd;
+    prefetch_l2(kb + (size_t)jlo * p.hd, kb + (size_t)j1 * p.hd);
+    prefetch_l2(vb + (size_t)jlo * p.hd, vb + (size_t)j1 * p.hd);
+}
+
+template <int EPL, int GMAX>
+__device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
+    const int G = p.n_heads / p.n_kv, hd = p.hd, half = hd / 2;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pos = c.pos, seq = pos + 1;
+    const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
+    const int units = p.n_kv * n_active;
+    const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
+    float* sm = reinterpret_cast<float*>(c.work);
+    float* res = sm + (size_t)MK_WARPS * G * (hd + 2);
+    float* cwt = sm + (size_t)(MK_WARPS + 1) * G * (hd + 2);
+    float* qs = cwt + (size_t)G * (p.n_splits + 1);
+    float* ks = qs + (size_t)G * hd;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int g = u % p.n_kv, split = u / p.n_kv;
+        int jlo, jhi;
+        attn_range(seq, 0, split, n_active, &jlo, &jhi);
+        const bool holds = pos >= jlo && pos < jhi;
+        const int nrows = G + (holds ? 1 : 0);  // <= 5 rows, one per warp
+        // every global input of the prologue is requested before any is used:
+        // this warp's q/k row and its norm gains, the new V row, the RoPE
+        // frequency of this thread's first rotated pair
+        const int r = warp;
+        const bool isq = r < G, has_row = r < nrows;
+        const float* nw = isq ? S.q_norm : S.k_norm;
+        float vv[EPL], wv[EPL];
+        {
+            const float* src = isq ? p.qkv + (size_t)(g * G + r) * hd : p.qkv + qd + (size_t)g * hd;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const int d = lane + 32 * e;
+                const bool in = has_row && d < hd;
+                vv[e] = in ? __ldcg(src + d) : 0.f;
+                wv[e] = (in && nw) ? __ldg(nw + d) : 0.f;
+            }
+        }
+        const float vnew = (holds && tid < hd) ? __ldcg(p.qkv + qd + kvd + (size_t)g * hd + tid) : 0.f;
+        float sn0 = 0.f, cs0 = 1.f;
+        if (tid < nrows * half) sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid % half)), &sn0, &cs0);
+        if (has_row) {  // QK-norm (qwen3.rs:154-155)
+            float* dst = isq ? qs + (size_t)r * hd : ks;
+            if (nw) {
+                float ss = 0.f;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) ss = fmaf(vv[e], vv[e], ss);
+                ss = warp_sum(ss);
+                const float inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
+#pragma unroll
+                for (int e = 0; e < EPL; e++) vv[e] = __fmul_rn(__fmul_rn(vv[e], inv), wv[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const int d = lane + 32 * e;
+                if (d < hd) dst[d] = vv[e];
+            }
+        }
+        mk_clk(c, CLK_LOADED);  // attention: inputs arrived, QK-norm done
+        __syncthreads();
+        for (int i = tid; i < nrows * half; i += blockDim.x) {  // RoPE (rope.wgsl:25-34)
+            const int rr = i / half, kq = i - rr * half;
+            float* row = rr < G ? qs + (size_t)rr * hd : ks;
+            float sn = sn0, cs = cs0;
+            if (i != tid) sincosf(__fmul_rn((float)pos, p.inv_freq[kq]), &sn, &cs);
+            const float lo = row[kq], hi = row[kq + half];
+            row[kq] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
+            row[kq + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+        }
+        __syncthreads();
+        mk_clk(c, CLK_NORMED);  // attention: RoPE done
+        float* kbase = S.kc + (size_t)g * p.max_seq * hd;
+        float* vbase = S.vc + (size_t)g * p.max_seq * hd;
+        if (holds && tid < hd) {  // cache.rs:21-24
+            kbase[(size_t)pos * hd + tid] = ks[tid];
+            vbase[(size_t)pos * hd + tid] = vnew;
+        }
+        __syncthreads();
+        mk_clk(c, CLK_Q24);  // attention: new K/V row stored
+        if (c.stamp && tid == 0) c.stamp[1] = global_ns();
+        attn_core<EPL, GMAX, KV_CG, MK_WARPS>(qs, G, hd, kbase, vbase, hd, jlo, jhi, p.scale, 0.f,
+                                              sm, res);
+        mk_clk(c, CLK_REGS);  // attention: this split's state merged
+        if (c.stamp && tid == 0) c.stamp[2] = global_ns();
+        if (n_active >= 2 && n_active <= MK_DEFER) {
+            const int W = hd + 2;
+            for (int i = tid; i < G * W; i += blockDim.x) {
+                const int gi = i / W, d = i - gi * W;
+                p.part[((size_t)(g * G + gi) * p.part_stride + split) * W + d] = res[i];
+            }
+        } else {
+            attn_finish(res, G, hd, g, split, n_active, p.part_stride, p.part, p.counters, p.attn,
+                        cwt);
+        }
+        __syncthreads();
+        mk_clk(c, CLK_MAIN);  // attention: output (or partial) published
+    }
+    return true;
+}
+
+// GEMV work mapping by config index and slots per chunk.
+template <int I, int NS> struct CfgOfT;
+template <> struct CfgOfT<0, 1> { using T = MC0; };
+template <> struct CfgOfT<1, 1> { using T = MC1; };
+template <> struct CfgOfT<2, 1> { using T = MC2; };
+template <> struct CfgOfT<3, 1> { using T = MC3; };
+template <> struct CfgOfT<4, 1> { using T = MC4; };
+template <> struct CfgOfT<0, 2> { using T = MD0; };
+template <> struct CfgOfT<1, 2> { using T = MD1; };
+template <> struct CfgOfT<2, 2> { using T = MD2; };
+template <> struct CfgOfT<3, 2> { using T = MD3; };
+template <> struct CfgOfT<4, 2> { using T = MD4; };
+template <int I, int NS> using CfgOf = typename CfgOfT<I, NS>::T;
+
+// The step kernel, specialised for one model shape: EPL = head_dim / 32
+// registers per lane and GMAX >= n_heads / n_kv for the attention stage,
+// CD / CQ the GEMV configs of K = dim (QKV, FFN gate/up, LM head) and
+// K = n_heads * head_dim (O projection).  Only the code one model runs is
+// compiled into its kernel, which keeps the instruction footprint small.
+template <int EPL, int GMAX, int CD, int CQ>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ MShared sh;
+    __shared__ float rowred[128];
+    __shared__ __align__(16) MStage sst[3];  // stage si in sst[si % 3], two fetched ahead
+    MCtx c;
+    c.sh = &sh;
+    c.ring = smem;
+    c.work = smem + (size_t)MK_SLOTS * MK_SLOT_BYTES;
+    c.emb = reinterpret_cast<float*>(c.work + p.work_bytes);
+    MIssue* iss = reinterpret_cast<MIssue*>(c.work + p.work_bytes + al16((size_t)p.dim * 4));
+    c.iss = iss;
+    c.rowred = rowred;
+    c.seq = 0;
+    c.redsel = 0;
+    c.nch = 0;
+    c.stamp = nullptr;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < MK_SLOTS; s++) mbar_init(&sh.full[s], 1);
+        fence_mbar_init();
+        sh.it_stage = 0;
+        sh.it_t = 0;
+        sh.it_j = 0;
+        sh.issued = 0;
+        sh.abort = 0;
+        sh.pol = l2_evict_first();
+    }
+    for (int i = tid; i < p.n_stages * 4; i += blockDim.x)
+        reinterpret_cast<int4*>(iss)[i] = reinterpret_cast<const int4*>(p.issues)[i];
+    mk_load_stage(p, 0, &sst[0]);
+    mk_load_stage(p, 1, &sst[1]);
+    mk_load_stage_wait();
+    const int pos = p.st->pos;
+    const unsigned tok = p.st->token;
+    const unsigned long long base = p.st->bar_base;
+    c.pos = pos;
+    __syncthreads();
+    if (tid == MK_ISSUER)  // the first ring-full of weights
+        for (int s = 0; s < MK_SLOTS; s++)
+            if (!mk_issue_next(p, c)) break;
+    // embedding row (qwen3.rs:128-133), every CTA its own copy
+    {
+        const int nb = p.dim / 32;
+        for (int i = tid; i < p.dim; i += blockDim.x) {
+            const int b = i >> 5, j = i & 31;
+            const size_t blk = (size_t)tok * nb + b;
+            const float d = __half2float(p.emb_scales[blk]);
+            const uint8_t byte = p.emb_payload[blk * 16 + (j & 15)];
+            const int qv = (j < 16) ? (byte & 0xf) : (byte >> 4);
+            float v = __fmul_rn(d, (float)(qv - 8));
+            if (p.embed_scale > 0.f) v = __fmul_rn(v, p.embed_scale);
+            c.emb[i] = v;
+            if (blockIdx.x == 0) p.hidden[i] = v;
+        }
+        __syncthreads();
+    }
+    bool ok = true;
+    for (int si = 0; si < p.n_stages && ok; si++) {
+        if (si > 0) ok = mk_grid_sync(p, c, base + (unsigned long long)si * gridDim.x);
+        if (!ok) break;
+        unsigned long long* stamp =
+            p.stamps ? p.stamps + ((size_t)si * gridDim.x + blockIdx.x) * MK_STAMPS : nullptr;
+        c.stamp = stamp;
+        if (stamp && tid == 0) stamp[0] = global_ns();
+        mk_clk(c, CLK_START);
+        mk_load_stage(p, si + 2, &sst[(si + 2) % 3]);  // waited for at the stage end
+        const MStage& S = sst[si % 3];
+        const MStage& S1 = sst[(si + 1) % 3];
+        if (tid == 0 && si + 1 < p.n_stages && S1.kind == SK_ATTN) mk_kv_prefetch(p, S1, c);
+        mk_clk(c, CLK_AHEAD);
+        if (S.kind == SK_ATTN) {
+            ok = mk_attn<EPL, GMAX>(p, S, c);
+        } else if (S.kind == SK_FFN) {
+            ok = mk_ffn<CfgOf<CD, 2>>(p, S, c);
+        } else if (S.cfg == CD) {
+            ok = mk_gemv<CfgOf<CD, 1>>(p, S, c);
+        } else if (S.cfg == CD + MK_NCFG) {
+            ok = mk_gemv<CfgOf<CD, 2>>(p, S, c);
+        } else if (S.cfg == CQ) {
+            ok = mk_gemv<CfgOf<CQ, 1>>(p, S, c);
+        } else {
+            ok = mk_gemv<CfgOf<CQ, 2>>(p, S, c);
+        }
+        mk_load_stage_wait();  // made visible by the barrier's __syncthreads
+        if (stamp) {
+            __syncthreads();
+            if (tid == 0) stamp[3] = global_ns();
+            mk_clk(c, CLK_END);
+        }
+    }
+    mk_load_stage_wait();
+    mk_drain(c);
+    if (!ok || sh.abort) return;
+    // the last CTA to finish does the generate-loop bookkeeping (mod.rs:114-122)
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(&p.st->done, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence();
+            DevState* st = p.st;
+            unsigned next;
+            if (pos + 1 < st->n_prompt) {
+                next = p.prompt[pos + 1];
+            } else {
+                const unsigned long long k = atomicMax(&st->key, 0ull);
+                const unsigned t = p.decode ? argmax_key_index(k) : 0u;
+                p.toks[st->n_produced] = t;
+                st->n_produced = st->n_produced + 1;
+                next = t;
+            }
+            st->key = argmax_key_init();
+            st->token = next;
+            st->pos = pos + 1;
+            st->done = 0;
+            st->bar_base = base + (unsigned long long)(p.n_stages - 1) * gridDim.x;
+            __threadfence();
+        }
+    }
+}
+
+
+using StepKernel = void (*)(MParams);
+
+}  // namespace cw
