@@ -196,9 +196,12 @@ def step_bytes(info: dict, pos: float) -> float:
 
 
 def launch_bytes(info: dict, pos: float) -> dict:
-    """kernel_bytes plus the persistent kernel, whose one launch is the step."""
+    """kernel_bytes plus the persistent kernel, whose one launch is the step,
+    and its fused stages (the same algorithmic bytes, regrouped)."""
     kb = kernel_bytes(info, pos)
     kb["decode_step"] = step_bytes(info, pos)
+    kb["ffn"] = kb["ffn_in"] + kb["ffn_out"]                # gate/up + SwiGLU + down
+    kb["attention_o"] = kb["attention"] + kb["attn_out"]  # attention + O projection
     return kb
 
 

@@ -10,6 +10,7 @@ copy back, context.rs:359-389), `flush`, `reset_frame`, `clear_cache`,
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -56,14 +57,22 @@ class GpuContext:
         h = C.c_void_p()
         _lib.call("cw_ctx_create", int(device), C.byref(h))
         self._h = h
+        # models (and through them sessions) made on this context: released
+        # before the context itself, whatever order Python drops them in
+        self._dependents = weakref.WeakSet()
         buf = C.create_string_buffer(256)
         _lib.call("cw_ctx_backend", self._h, buf, 256)
         self.backend = buf.value.decode()
         self.device = int(device)
 
     # -- lifetime -------------------------------------------------------------
+    def _adopt(self, obj) -> None:
+        self._dependents.add(obj)
+
     def close(self) -> None:
         if getattr(self, "_h", None):
+            for obj in list(getattr(self, "_dependents", ())):
+                obj.close()
             _lib.load().cw_ctx_destroy(self._h)
             self._h = None
 

@@ -148,7 +148,9 @@ int ensure_counters(cw_ctx* ctx, size_t n) {
     ctx->d_counters = nullptr;
     ctx->n_counters = 0;
     CW_CUDA(cudaMalloc(&ctx->d_counters, m * sizeof(unsigned)));
-    CW_CUDA(cudaMemset(ctx->d_counters, 0, m * sizeof(unsigned)));
+    // on the context stream: kernels there do not wait for the legacy stream
+    CW_CUDA(cudaMemsetAsync(ctx->d_counters, 0, m * sizeof(unsigned), ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(ctx->stream));
     ctx->n_counters = m;
     return CW_OK;
 }
@@ -171,7 +173,11 @@ int rope_table(cw_ctx* ctx, uint32_t head_dim, float theta, const float** out) {
     }
     float* d = nullptr;
     CW_CUDA(cudaMalloc(&d, t.size() * sizeof(float)));
-    CW_CUDA(cudaMemcpy(d, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice));
+    // on the context stream (the non-blocking stream does not wait for the
+    // legacy default stream a plain cudaMemcpy uses), complete before t dies
+    CW_CUDA(cudaMemcpyAsync(d, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice,
+                            ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(ctx->stream));
     ctx->rope_tables[key] = d;
     *out = d;
     return CW_OK;
@@ -222,7 +228,7 @@ int cw_ctx_create(int device, cw_ctx** out) {
         return set_error(CW_ERR_CUDA, "context setup failed: %s",
                          cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
     }
-    cudaMemset(c->d_status, 0, sizeof(int));
+    cudaMemsetAsync(c->d_status, 0, sizeof(int), c->stream);  // ordered with c's kernels
     int rc = ensure_counters(c, 1024);
     if (rc != CW_OK) {
         cw_ctx_destroy(c);

@@ -341,7 +341,8 @@ __global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n
     st->n_prompt = n_prompt;
     st->n_produced = 0;
     st->key = argmax_key_init();
-    st->bar_base = *bar;  // the persistent step's grid barrier continues from here
+    st->bar_base = bar[0];  // the persistent step's counters continue from here
+    st->ctr_base = bar[1];
     st->done = 0;
 }
 
@@ -487,7 +488,10 @@ static int load_vec(cw_model* m, const GgufFile& f, const std::string& name, siz
     }
     void* p;
     CW_TRY(dev_alloc(m, len * 4, &p));
-    CW_CUDA(cudaMemcpy(p, h.data(), len * 4, cudaMemcpyHostToDevice));
+    // stream-ordered with the kernels that read it (the context stream does
+    // not wait for the legacy default stream) and complete before h dies
+    CW_CUDA(cudaMemcpyAsync(p, h.data(), len * 4, cudaMemcpyHostToDevice, m->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
     *out = (float*)p;
     return CW_OK;
 }
@@ -520,7 +524,8 @@ static int load_q4(cw_model* m, const GgufFile& f, const std::vector<std::string
     if (!interleave) {
         size_t off = 0;
         for (auto* t : parts) {
-            ce = cudaMemcpy((char*)tmp + off, t->data, t->nbytes, cudaMemcpyHostToDevice);
+            ce = cudaMemcpyAsync((char*)tmp + off, t->data, t->nbytes, cudaMemcpyHostToDevice,
+                                 m->ctx->stream);
             if (ce != cudaSuccess) break;
             off += t->nbytes;
         }
@@ -531,12 +536,17 @@ static int load_q4(cw_model* m, const GgufFile& f, const std::vector<std::string
             memcpy(stage.data() + (2 * r) * rb, parts[0]->data + r * rb, rb);
             memcpy(stage.data() + (2 * r + 1) * rb, parts[1]->data + r * rb, rb);
         }
-        ce = cudaMemcpy(tmp, stage.data(), nbytes, cudaMemcpyHostToDevice);
+        ce = cudaMemcpyAsync(tmp, stage.data(), nbytes, cudaMemcpyHostToDevice, m->ctx->stream);
+        if (ce == cudaSuccess) ce = cudaStreamSynchronize(m->ctx->stream);  // before stage dies
     }
     if (ce != cudaSuccess) {
+        cudaStreamSynchronize(m->ctx->stream);
         cudaFree(tmp);
         return set_error(CW_ERR_CUDA, "weight upload: %s", cudaGetErrorString(ce));
     }
+    // the upload and the repack are ordered on the context stream: a plain
+    // cudaMemcpy from pageable memory can return before its DMA lands, and
+    // the non-blocking context stream would not wait for it
     cw_buf b;
     int rc = pack_q4_0(m->ctx, tmp, rows, in_f, &b);
     cudaStreamSynchronize(m->ctx->stream);
@@ -618,9 +628,12 @@ static int model_load(cw_model* m, const std::string& path) {
             CW_TRY(load_vec(m, f, p + "attn_v.bias", kvd, &bv));
             void* pb;
             CW_TRY(dev_alloc(m, (qd + 2 * kvd) * 4, &pb));
-            CW_CUDA(cudaMemcpy(pb, bq, qd * 4, cudaMemcpyDeviceToDevice));
-            CW_CUDA(cudaMemcpy((float*)pb + qd, bk, kvd * 4, cudaMemcpyDeviceToDevice));
-            CW_CUDA(cudaMemcpy((float*)pb + qd + kvd, bv, kvd * 4, cudaMemcpyDeviceToDevice));
+            cudaStream_t st = m->ctx->stream;
+            CW_CUDA(cudaMemcpyAsync(pb, bq, qd * 4, cudaMemcpyDeviceToDevice, st));
+            CW_CUDA(cudaMemcpyAsync((float*)pb + qd, bk, kvd * 4, cudaMemcpyDeviceToDevice, st));
+            CW_CUDA(cudaMemcpyAsync((float*)pb + qd + kvd, bv, kvd * 4, cudaMemcpyDeviceToDevice,
+                                    st));
+            CW_CUDA(cudaStreamSynchronize(st));
             l.qkv_bias = (float*)pb;
         }
         CW_TRY(load_q4(m, f, {p + "attn_output.weight"}, qd, false, &l.wo));
@@ -821,12 +834,21 @@ static int build_graph(cw_session* s, bool decode, cudaGraphExec_t* out) {
     return CW_OK;
 }
 
+static void destroy_graphs(cw_session* s) {
+    for (auto& row : s->graphs)
+        for (auto& g : row)
+            if (g) {
+                cudaGraphExecDestroy(g);
+                g = nullptr;
+            }
+}
+
 static int run_step(cw_session* s) {
     bool decode = !(s->host_pos + 1 < s->n_prompt);
     CW_CHECK(s->host_pos < s->max_seq, CW_ERR_INVALID_ARG,
              "session is full: position %zu, max_seq %zu", s->host_pos, s->max_seq);
     if (s->use_graph) {
-        cudaGraphExec_t* g = decode ? &s->g_decode : &s->g_prompt;
+        cudaGraphExec_t* g = &s->graphs[step_variant(s)][decode ? 1 : 0];
         if (!*g) CW_TRY(build_graph(s, decode, g));
         CW_CUDA(cudaGraphLaunch(*g, s->ctx->stream));
     } else {
@@ -916,8 +938,10 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     A(max_seq * 4, (void**)&s->toks);
     A((size_t)I.n_kv * 4, (void**)&s->counters);
     A(sizeof(DevState), (void**)&s->st);
-    A(sizeof(unsigned long long), (void**)&s->bar);
+    A(2 * sizeof(unsigned long long), (void**)&s->bar);
+    // fixed-point residual accumulator (persistent step: FFN partial sums)
     A((size_t)I.dim * sizeof(long long), (void**)&s->racc);
+    A((size_t)I.n_heads * I.dim * sizeof(float), (void**)&s->opart);
     if (rc == CW_OK && (cudaMallocHost(&s->h_tok, sizeof(unsigned)) != cudaSuccess ||
                         cudaMallocHost(&s->h_tok_in, sizeof(unsigned)) != cudaSuccess))
         rc = set_error(CW_ERR_OOM, "pinned host allocation failed");
@@ -937,8 +961,7 @@ int cw_session_free(cw_session* s) {
     if (!s) return CW_OK;
     cudaSetDevice(s->ctx->device);
     cudaStreamSynchronize(s->ctx->stream);
-    if (s->g_prompt) cudaGraphExecDestroy(s->g_prompt);
-    if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
+    destroy_graphs(s);
     step_plan_free(s);
     for (cw_buf b : s->owned) {
         auto it = s->ctx->bufs.find(b);
@@ -965,18 +988,20 @@ int cw_session_set_persistent(cw_session* s, int on) {
     cudaSetDevice(s->ctx->device);
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     // captured graphs hold one path or the other
-    if (s->g_prompt) cudaGraphExecDestroy(s->g_prompt);
-    if (s->g_decode) cudaGraphExecDestroy(s->g_decode);
-    s->g_prompt = s->g_decode = nullptr;
+    destroy_graphs(s);
+    CW_CHECK(on >= 0 && on <= 3, CW_ERR_INVALID_ARG, "cw_session_set_persistent: mode %d", on);
     s->use_persistent = on != 0;
     if (!on) {
         step_plan_free(s);
         return CW_OK;
     }
-    if (s->plan) return CW_OK;
-    CW_CHECK(step_supported(s->m, s), CW_ERR_UNSUPPORTED,
-             "the persistent step does not cover this model family");
-    return step_plan_create(s);
+    if (!s->plan) {
+        CW_CHECK(step_supported(s->m, s), CW_ERR_UNSUPPORTED,
+                 "the persistent step does not cover this model family");
+        CW_TRY(step_plan_create(s));
+    }
+    step_set_mode(s, on);
+    return CW_OK;
 }
 
 int cw_session_persistent(cw_session* s, int* on) {
@@ -1089,8 +1114,10 @@ int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms) {
     cudaSetDevice(s->ctx->device);
     // build graphs outside the timed region
     if (s->use_graph) {
-        if (!s->g_prompt && s->host_pos + 1 < s->n_prompt) CW_TRY(build_graph(s, false, &s->g_prompt));
-        if (!s->g_decode) CW_TRY(build_graph(s, true, &s->g_decode));
+        cudaGraphExec_t* gp = &s->graphs[step_variant(s)][0];
+        cudaGraphExec_t* gd = &s->graphs[step_variant(s)][1];
+        if (!*gp && s->host_pos + 1 < s->n_prompt) CW_TRY(build_graph(s, false, gp));
+        if (!*gd) CW_TRY(build_graph(s, true, gd));
     }
     cudaEvent_t e0, e1;
     CW_CUDA(cudaEventCreate(&e0));

@@ -24,6 +24,7 @@ struct DevState {
     unsigned long long bar_base;  // grid-barrier count at the start of the step
     unsigned done;           // CTAs that finished the current step
     unsigned pad;
+    unsigned long long ctr_base;  // persistent step's head counter at the start of the step
 };
 
 struct QW {  // packed Q4_0 weight
@@ -50,6 +51,7 @@ struct cw_model {
     float* final_norm = nullptr;
     cw::QW embed, head;
     std::vector<cw::QW> down_cm;  // down projections, column-block-major (persistent step)
+    std::vector<cw::QW> wo_cm;    // O projections, column-block-major (persistent step)
     std::vector<cw_buf> owned;
     const float* inv_freq = nullptr;
 };
@@ -63,18 +65,21 @@ struct cw_session {
     float *hidden = nullptr, *hidden_b = nullptr, *tmp = nullptr, *qkv = nullptr, *attn = nullptr;
     float *act = nullptr, *logits = nullptr, *xnorm = nullptr, *part = nullptr;
     unsigned *prompt = nullptr, *toks = nullptr, *counters = nullptr;
-    long long* racc = nullptr;  // fixed-point residual accumulator (persistent step)
+    long long* racc = nullptr;  // fixed-point residual accumulator, dim words (persistent step)
     cw::DevState* st = nullptr;
     int n_splits = 1;
     bool use_graph = true;
-    cudaGraphExec_t g_prompt = nullptr, g_decode = nullptr;
+    // captured steps, [step variant][decode]: variant 1 is the persistent
+    // step's fused short-context plan, 0 everything else
+    cudaGraphExec_t graphs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
     size_t host_pos = 0, n_prompt = 0, n_produced = 0;
     unsigned* h_tok = nullptr;     // pinned, one token for per-step reads
     unsigned* h_tok_in = nullptr;  // pinned, one token for per-step writes
     // persistent step kernel (cw_step.cu); null when the model is not eligible
     cw::StepPlan* plan = nullptr;
     bool use_persistent = true;
-    unsigned long long* bar = nullptr;  // grid-barrier counter (monotonic)
+    unsigned long long* bar = nullptr;  // [0] grid-barrier counter, [1] head counter (monotonic)
+    float* opart = nullptr;             // per-head O-projection row sums (persistent step)
 };
 
 namespace cw {
@@ -84,6 +89,8 @@ bool step_supported(const cw_model* m, const cw_session* s);
 int step_plan_create(cw_session* s);
 void step_plan_free(cw_session* s);
 int step_enqueue(cw_session* s, bool decode);
+int step_variant(const cw_session* s);  // 0 or 1: which plan the next step uses
+void step_set_mode(cw_session* s, int mode);  // 1 auto, 2 split plan only, 3 fused plan only
 int step_profile(cw_session* s, size_t n_steps,
                  std::map<std::string, std::pair<uint32_t, double>>* agg);
 

@@ -25,40 +25,60 @@ __global__ void k_colmajor(const uint8_t* __restrict__ pay, const __half* __rest
     osc[(size_t)b * rows + r] = sc[i];
 }
 
-static int build_down_colmajor(cw_model* m) {
-    if (!m->down_cm.empty()) return CW_OK;
+// Column-block-major copy of a packed Q4_0 matrix (k_colmajor), owned by the model.
+static int colmajor_copy(cw_model* m, const QW& w, QW* out) {
     cw_ctx* ctx = m->ctx;
-    std::vector<QW> out;
-    for (const Layer& l : m->L) {
-        const int rows = l.down.rows, nb = l.down.in_f / 32;
-        const size_t pb = (size_t)rows * nb * 16, sb = (size_t)rows * nb * 2;
-        const size_t soff = (pb + 255) / 256 * 256;
-        cw_buf b;
-        BufEntry* e;
-        CW_TRY(buf_new(ctx, soff + sb, BUF_PERSISTENT, &b, &e));
-        m->owned.push_back(b);
-        QW q;
-        q.payload = reinterpret_cast<const uint8_t*>(e->ptr);
-        q.scales = reinterpret_cast<const __half*>(reinterpret_cast<char*>(e->ptr) + soff);
-        q.rows = rows;
-        q.in_f = l.down.in_f;
-        q.buf = b;
-        const long n = (long)rows * nb;
-        k_colmajor<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
-            l.down.payload, l.down.scales, rows, nb, const_cast<uint8_t*>(q.payload),
-            const_cast<__half*>(q.scales));
-        CW_CUDA(cudaGetLastError());
-        out.push_back(q);
-    }
-    CW_CUDA(cudaStreamSynchronize(ctx->stream));
-    m->down_cm.swap(out);
+    const int rows = w.rows, nb = w.in_f / 32;
+    const size_t pb = (size_t)rows * nb * 16, sb = (size_t)rows * nb * 2;
+    const size_t soff = (pb + 255) / 256 * 256;
+    cw_buf b;
+    BufEntry* e;
+    CW_TRY(buf_new(ctx, soff + sb, BUF_PERSISTENT, &b, &e));
+    m->owned.push_back(b);
+    out->payload = reinterpret_cast<const uint8_t*>(e->ptr);
+    out->scales = reinterpret_cast<const __half*>(reinterpret_cast<char*>(e->ptr) + soff);
+    out->rows = rows;
+    out->in_f = w.in_f;
+    out->buf = b;
+    const long n = (long)rows * nb;
+    k_colmajor<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
+        w.payload, w.scales, rows, nb, const_cast<uint8_t*>(out->payload),
+        const_cast<__half*>(out->scales));
+    CW_CUDA(cudaGetLastError());
     return CW_OK;
 }
-struct StepPlan {
+
+// Down projections (FFN stage) and O projections (fused attention stage) in
+// column-block-major order, built once per model.
+static int build_colmajor(cw_model* m) {
+    if (!m->down_cm.empty()) return CW_OK;
+    std::vector<QW> down, wo;
+    for (const Layer& l : m->L) {
+        QW d, o;
+        CW_TRY(colmajor_copy(m, l.down, &d));
+        CW_TRY(colmajor_copy(m, l.wo, &o));
+        down.push_back(d);
+        wo.push_back(o);
+    }
+    CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    m->down_cm.swap(down);
+    m->wo_cm.swap(wo);
+    return CW_OK;
+}
+
+// One stage list: 0 = split attention + O-projection stage (any context
+// length), 1 = fused attention + O projection (contexts up to fuse_max keys).
+struct StepVariant {
     std::vector<const char*> names;  // stage names, for the profile
-    MStage* d_stages = nullptr;
-    int n_stages = 0;  // decode step (prompt steps drop the final LM-head stage)
+    MStage* d_stages = nullptr;      // stage table + issue table, one allocation
+    int n_stages = 0;                // decode step (prompt steps drop the LM-head stage)
     MParams params{};
+};
+
+struct StepPlan {
+    StepVariant v[2];
+    bool has_fused = false;
+    int fuse_max = 0;  // keys (position + 1) up to which variant 1 runs
     size_t smem = 0;
     int grid = 0;
     void (*kern)(MParams) = nullptr;
@@ -87,16 +107,22 @@ static StepKernel find_kernel(const cw_model_info& I) {
     return nullptr;
 }
 
+
+
 static size_t work_bytes_for(const cw_model_info& I, int n_splits) {
     const int G = I.n_heads / I.n_kv, hd = I.head_dim;
     const int kmax = std::max<int>(I.dim, std::max<int>(I.n_heads * I.head_dim, I.hidden));
-    // PRO_X: q24 planes of K <= kmax; PRO_NORM (K = dim): planes + hbuf + wbuf
     const int qd = I.n_heads * I.head_dim;
+    // PRO_X: q24 planes of K <= kmax; PRO_NORM (K = dim): planes + hbuf + wbuf;
+    // PRO_ATTN: planes of K = qd + the merge weights
     const size_t gemv = std::max({al16(q24_bytes(kmax / 32)),
                                   al16(q24_bytes((int)I.dim / 32)) + (size_t)I.dim * 8,
                                   al16(q24_bytes(qd / 32)) + (size_t)I.n_heads * (MK_DEFER + 1) * 4});
     const size_t attn = (attn_smem_floats(G, hd, n_splits, MK_WARPS) + (size_t)G * hd + hd) * 4;
-    return al16(std::max(gemv, attn));
+    // fused stage: attn_core scratch for one head, q, k, output, its q24 blocks
+    const size_t attno = al16(((size_t)(MK_WARPS + 1) * (hd + 2) + MK_WARPS) * 4) +
+                         (size_t)3 * hd * 4 + q24_bytes(hd / 32);
+    return al16(std::max({gemv, attn, attno}));
 }
 
 bool step_supported(const cw_model* m, const cw_session* s) {
@@ -112,27 +138,26 @@ bool step_supported(const cw_model* m, const cw_session* s) {
     return true;
 }
 
-int step_plan_create(cw_session* s) {
+// Stage list of one variant, uploaded to the device.
+static int build_variant(cw_session* s, bool fused, int grid, int n_splits, size_t work,
+                         StepVariant* V, size_t* smem_need) {
     cw_model* m = s->m;
     cw_ctx* ctx = s->ctx;
     const cw_model_info& I = m->info;
-    if (!step_supported(m, s)) return CW_ERR_UNSUPPORTED;
-    std::unique_ptr<StepPlan> P(new StepPlan());
-    P->kern = find_kernel(I);
-    const int grid = ctx->sm_count;
-    const int n_splits = std::max(1, std::min(s->n_splits, grid / (int)I.n_kv));
-    CW_TRY(build_down_colmajor(m));
-    // ---- stage list and its weight-copy schedule
+    const int dim = (int)I.dim;
+    long long* A = s->racc;  // FFN down-projection partial sums (fixed point)
     std::vector<MStage> st;
     std::vector<MIssue> is;
     auto gemv = [&](const char* name, const QW& w, int pro, int epi, const float* x,
                     const float* base, const float* norm_w, float* y, const float* bias,
-                    float* xn_out, int acc_in, int acc_zero) {
-        P->names.push_back(name);
+                    float* xn_out, int acc_in, long long* r1, long long* r2, int acc_zero) {
+        V->names.push_back(name);
         MStage S = {};
         S.acc_in = acc_in;
         S.acc_zero = acc_zero;
-        S.racc = s->racc;
+        S.racc = r1;
+        S.racc2 = r2;
+        S.acc_clear = s->racc;
         S.kind = SK_GEMV;
         S.cfg = mk_cfg_for(w.in_f);
         // two slots per chunk where a CTA would otherwise take several chunks
@@ -152,37 +177,68 @@ int step_plan_create(cw_session* s) {
         S.bias = bias;
         S.xn_out = xn_out;
         st.push_back(S);
-        MIssue I = {};
-        I.kind = SK_GEMV;
-        I.pay0 = S.payload;
-        I.sc0 = S.scales;
-        I.n0 = S.nchunks;
-        I.rc = S.RC / mk_ns(S.cfg);
-        I.per0 = mk_ns(S.cfg);
-        I.nb = S.K / 32;
-        I.n = S.N;
-        is.push_back(I);
+        MIssue Is = {};
+        Is.kind = SK_GEMV;
+        Is.pay0 = S.payload;
+        Is.sc0 = S.scales;
+        Is.n0 = S.nchunks;
+        Is.rc = S.RC / mk_ns(S.cfg);
+        Is.per0 = mk_ns(S.cfg);
+        Is.nb = S.K / 32;
+        Is.n = S.N;
+        is.push_back(Is);
+        return (int)st.size() - 1;
     };
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
-        gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, nullptr, li == 0 ? nullptr : s->hidden,
-             l.attn_norm, s->qkv, l.qkv_bias, nullptr, li > 0, 0);
-        P->names.push_back("attention");
-        MStage A = {};
-        A.kind = SK_ATTN;
-        A.q_norm = l.q_norm;
-        A.k_norm = l.k_norm;
-        A.kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
-        A.vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
-        st.push_back(A);
-        MIssue IA = {};
-        IA.kind = SK_ATTN;
-        is.push_back(IA);
-        // the residual read here includes the previous layer's FFN output
-        // (fixed-point accumulator), which is folded in and cleared
-        gemv("attn_out", l.wo, PRO_ATTN, EPI_RESID, s->attn, nullptr, nullptr, s->hidden, nullptr,
-             nullptr, li > 0, 1);
-        P->names.push_back("ffn");
+        float* kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
+        float* vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
+        // QKV: residual = hidden + A (the previous layer's FFN output)
+        const int qi = gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, nullptr,
+                            li == 0 ? nullptr : s->hidden, l.attn_norm, s->qkv, l.qkv_bias,
+                            nullptr, li == 0 ? 0 : 1, A, nullptr, 0);
+        if (li == 0 && fused) st[qi].zero_acc = 1;
+        if (fused) {
+            V->names.push_back("attention_o");
+            MStage T = {};
+            T.kind = SK_ATTNO;
+            T.q_norm = l.q_norm;
+            T.k_norm = l.k_norm;
+            T.kc = kc;
+            T.vc = vc;
+            T.per1 = (dim + MK_DOWN_ROWS - 1) / MK_DOWN_ROWS;
+            T.layer = (int)li;
+            T.y = s->hidden;  // hidden = (hidden + A) + O projection, A = 0
+            T.fold_a = A;
+            st.push_back(T);
+            const QW& ocm = m->wo_cm[li];
+            MIssue It = {};
+            It.kind = SK_ATTNO;
+            It.pay1 = ocm.payload;
+            It.sc1 = ocm.scales;
+            It.n0 = (int)I.n_heads;
+            It.per0 = (int)I.head_dim / 32;
+            It.per1 = T.per1;
+            It.dim = dim;
+            is.push_back(It);
+        } else {
+            V->names.push_back("attention");
+            MStage T = {};
+            T.kind = SK_ATTN;
+            T.q_norm = l.q_norm;
+            T.k_norm = l.k_norm;
+            T.kc = kc;
+            T.vc = vc;
+            st.push_back(T);
+            MIssue It = {};
+            It.kind = SK_ATTN;
+            is.push_back(It);
+            // the residual read here includes the previous layer's FFN output
+            // (accumulator A), which is folded in and cleared
+            gemv("attn_out", l.wo, PRO_ATTN, EPI_RESID, s->attn, nullptr, nullptr, s->hidden,
+                 nullptr, nullptr, li > 0 ? 1 : 0, A, nullptr, 1);
+        }
+        V->names.push_back("ffn");
         const QW& dcm = m->down_cm[li];
         MStage F = {};
         F.kind = SK_FFN;
@@ -193,38 +249,114 @@ int step_plan_create(cw_session* s) {
         F.RC = mk_rc(F.cfg);
         F.nunits = (int)I.hidden / 32;
         F.per0 = 64 / F.RC;
-        F.per1 = ((int)I.dim + MK_DOWN_ROWS - 1) / MK_DOWN_ROWS;
-        F.N2 = (int)I.dim;
-        F.racc = s->racc;
+        F.per1 = (dim + MK_DOWN_ROWS - 1) / MK_DOWN_ROWS;
+        F.N2 = dim;
+        F.racc = A;
+        F.acc_in = 0;  // the residual is hidden alone here (A folded in before)
         F.payload = l.gate_up.payload;
         F.scales = l.gate_up.scales;
         F.payload2 = dcm.payload;
         F.scales2 = dcm.scales;
         F.base = s->hidden;
         F.norm_w = l.ffn_norm;
+        F.fold_a = A;  // the accumulator the down projection adds into
         st.push_back(F);
-        MIssue IF = {};
-        IF.kind = SK_FFN;
-        IF.pay0 = F.payload;
-        IF.sc0 = F.scales;
-        IF.pay1 = F.payload2;
-        IF.sc1 = F.scales2;
-        IF.n0 = F.nunits;
-        IF.rc = F.RC / mk_ns(F.cfg);
-        IF.nb = F.K / 32;
-        IF.n = F.N;
-        IF.per0 = 64 / IF.rc;
-        IF.per1 = F.per1;
-        IF.dim = F.N2;
-        is.push_back(IF);
+        MIssue If = {};
+        If.kind = SK_FFN;
+        If.pay0 = F.payload;
+        If.sc0 = F.scales;
+        If.pay1 = F.payload2;
+        If.sc1 = F.scales2;
+        If.n0 = F.nunits;
+        If.rc = F.RC / mk_ns(F.cfg);
+        If.nb = F.K / 32;
+        If.n = F.N;
+        If.per0 = 64 / If.rc;
+        If.per1 = F.per1;
+        If.dim = F.N2;
+        is.push_back(If);
     }
     gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, s->hidden, m->final_norm, s->logits,
-         nullptr, s->xnorm, I.n_layers > 0, 0);
-    P->n_stages = (int)st.size();
-    // ---- shared memory: ring | work | embedding row | issue table
+         nullptr, s->xnorm, I.n_layers == 0 ? 0 : 1, A, nullptr, 0);
+    V->n_stages = (int)st.size();
+    *smem_need = (size_t)MK_SLOTS * MK_SLOT_BYTES + work + al16((size_t)dim * 4) +
+                 is.size() * sizeof(MIssue);
+    const size_t sb = st.size() * sizeof(MStage), ib = is.size() * sizeof(MIssue);
+    cudaError_t e = cudaMalloc(&V->d_stages, sb + ib);
+    // stream-ordered with the step launches (the context stream does not wait
+    // for the legacy default stream) and complete before st / is die
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(V->d_stages, st.data(), sb, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(reinterpret_cast<char*>(V->d_stages) + sb, is.data(), ib,
+                            cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess)
+        return set_error(CW_ERR_CUDA, "persistent step plan: %s", cudaGetErrorString(e));
+    MParams& pp = V->params;
+    pp.stages = V->d_stages;
+    pp.issues = reinterpret_cast<const MIssue*>(reinterpret_cast<char*>(V->d_stages) + sb);
+    pp.st = s->st;
+    pp.status = ctx->d_status;
+    pp.bar = s->bar;
+    pp.emb_payload = m->embed.payload;
+    pp.emb_scales = m->embed.scales;
+    pp.embed_scale = I.embed_scale;
+    pp.hidden = s->hidden;
+    pp.qkv = s->qkv;
+    pp.attn = s->attn;
+    pp.prompt = s->prompt;
+    pp.toks = s->toks;
+    pp.part = s->part;
+    pp.counters = s->counters;
+    pp.inv_freq = m->inv_freq;
+    pp.dim = dim;
+    pp.n_heads = (int)I.n_heads;
+    pp.n_kv = (int)I.n_kv;
+    pp.hd = (int)I.head_dim;
+    pp.max_seq = (int)s->max_seq;
+    pp.n_splits = n_splits;
+    pp.part_stride = s->n_splits;
+    pp.attn_min = MK_ATTN_MIN;
+    if (const char* ev = getenv("CW_ATTN_MIN_KEYS")) {  // tuning knob
+        const int v = atoi(ev);
+        if (v >= 1) pp.attn_min = v;
+    }
+    pp.eps = I.eps;
+    pp.inv_dim = 1.0f / (float)dim;
+    pp.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
+    pp.work_bytes = work;
+    pp.opart = s->opart;
+    pp.hctr = s->bar + 1;
+    pp.hctr_per_step = fused ? (int)(I.n_layers * I.n_heads) : 0;
+    return CW_OK;
+}
+
+static void plan_release(StepPlan* P) {
+    for (StepVariant& V : P->v)
+        if (V.d_stages) cudaFree(V.d_stages);
+    delete P;
+}
+
+int step_plan_create(cw_session* s) {
+    cw_model* m = s->m;
+    cw_ctx* ctx = s->ctx;
+    const cw_model_info& I = m->info;
+    if (!step_supported(m, s)) return CW_ERR_UNSUPPORTED;
+    std::unique_ptr<StepPlan, void (*)(StepPlan*)> P(new StepPlan(), plan_release);
+    P->kern = find_kernel(I);
+    const int grid = ctx->sm_count;
+    const int n_splits = std::max(1, std::min(s->n_splits, grid / (int)I.n_kv));
+    CW_TRY(build_colmajor(m));
     const size_t work = work_bytes_for(I, n_splits);
-    P->smem = (size_t)MK_SLOTS * MK_SLOT_BYTES + work + al16((size_t)I.dim * 4) +
-              is.size() * sizeof(MIssue);
+    // the fused attention stage needs a CTA per query head and spare CTAs to fold
+    P->has_fused = (int)I.n_heads < grid && I.n_layers > 0;
+    P->fuse_max = MK_FUSE_MAX;
+    if (const char* ev = getenv("CW_FUSE_MAX_KEYS")) P->fuse_max = atoi(ev);  // tuning knob
+    size_t need0 = 0, need1 = 0;
+    CW_TRY(build_variant(s, false, grid, n_splits, work, &P->v[0], &need0));
+    if (P->has_fused) CW_TRY(build_variant(s, true, grid, n_splits, work, &P->v[1], &need1));
+    P->smem = std::max(need0, need1);
     cudaFuncAttributes fa{};
     cudaError_t e = cudaFuncGetAttributes(&fa, P->kern);
     if (e == cudaSuccess && (long)(P->smem + fa.sharedSizeBytes) > (long)ctx->max_smem_optin)
@@ -241,67 +373,37 @@ int step_plan_create(cw_session* s) {
         return set_error(CW_ERR_UNSUPPORTED, "persistent step cannot be resident: %s",
                          cudaGetErrorString(e));
     P->grid = grid;
-    const size_t sb = st.size() * sizeof(MStage), ib = is.size() * sizeof(MIssue);
-    e = cudaMalloc(&P->d_stages, sb + ib);
-    if (e == cudaSuccess)
-        e = cudaMemcpy(P->d_stages, st.data(), sb, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess)
-        e = cudaMemcpy(reinterpret_cast<char*>(P->d_stages) + sb, is.data(), ib,
-                       cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-        if (P->d_stages) cudaFree(P->d_stages);
-        return set_error(CW_ERR_CUDA, "persistent step plan: %s", cudaGetErrorString(e));
-    }
-    MParams& pp = P->params;
-    pp.stages = P->d_stages;
-    pp.issues = reinterpret_cast<const MIssue*>(reinterpret_cast<char*>(P->d_stages) + sb);
-    pp.st = s->st;
-    pp.status = ctx->d_status;
-    pp.bar = s->bar;
-    pp.emb_payload = m->embed.payload;
-    pp.emb_scales = m->embed.scales;
-    pp.embed_scale = I.embed_scale;
-    pp.hidden = s->hidden;
-    pp.qkv = s->qkv;
-    pp.attn = s->attn;
-    pp.prompt = s->prompt;
-    pp.toks = s->toks;
-    pp.part = s->part;
-    pp.counters = s->counters;
-    pp.inv_freq = m->inv_freq;
-    pp.dim = (int)I.dim;
-    pp.n_heads = (int)I.n_heads;
-    pp.n_kv = (int)I.n_kv;
-    pp.hd = (int)I.head_dim;
-    pp.max_seq = (int)s->max_seq;
-    pp.n_splits = n_splits;
-    pp.part_stride = s->n_splits;
-    pp.attn_min = MK_ATTN_MIN;
-    if (const char* ev = getenv("CW_ATTN_MIN_KEYS")) {  // tuning knob
-        const int v = atoi(ev);
-        if (v >= 1) pp.attn_min = v;
-    }
-    pp.eps = I.eps;
-    pp.inv_dim = 1.0f / (float)I.dim;
-    pp.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
-    pp.work_bytes = work;
     s->plan = P.release();
     return CW_OK;
 }
 
 void step_plan_free(cw_session* s) {
     if (!s->plan) return;
-    if (s->plan->d_stages) cudaFree(s->plan->d_stages);
-    delete s->plan;
+    plan_release(s->plan);
     s->plan = nullptr;
+}
+
+void step_set_mode(cw_session* s, int mode) {
+    StepPlan* P = s->plan;
+    if (!P) return;
+    P->fuse_max = mode == 2 ? 0 : mode == 3 ? (1 << 30) : MK_FUSE_MAX;
+    if (mode == 1)
+        if (const char* ev = getenv("CW_FUSE_MAX_KEYS")) P->fuse_max = atoi(ev);  // tuning knob
+}
+
+int step_variant(const cw_session* s) {
+    const StepPlan* P = s->plan;
+    if (!P || !P->has_fused) return 0;
+    return (int)(s->host_pos + 1) <= P->fuse_max ? 1 : 0;
 }
 
 static int step_launch(cw_session* s, bool decode, unsigned long long* stamps) {
     StepPlan* P = s->plan;
-    MParams pp = P->params;
+    const StepVariant& V = P->v[step_variant(s)];
+    MParams pp = V.params;
     pp.stamps = stamps;
     pp.decode = decode ? 1 : 0;
-    pp.n_stages = decode ? P->n_stages : P->n_stages - 1;
+    pp.n_stages = decode ? V.n_stages : V.n_stages - 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)P->grid);
     cfg.blockDim = dim3(MK_THREADS);
@@ -328,7 +430,9 @@ int step_profile(cw_session* s, size_t n_steps,
                  std::map<std::string, std::pair<uint32_t, double>>* agg) {
     StepPlan* P = s->plan;
     cw_ctx* ctx = s->ctx;
-    const size_t n = (size_t)P->n_stages * P->grid * MK_STAMPS;
+    int max_stages = 0;
+    for (const StepVariant& V : P->v) max_stages = std::max(max_stages, V.n_stages);
+    const size_t n = (size_t)max_stages * P->grid * MK_STAMPS;
     unsigned long long* d = nullptr;
     CW_CUDA(cudaMalloc(&d, n * 8));
     std::vector<unsigned long long> h(n);
@@ -341,6 +445,7 @@ int step_profile(cw_session* s, size_t n_steps,
             rc = set_error(CW_ERR_INVALID_ARG, "session is full: position %zu", s->host_pos);
             break;
         }
+        const int vsel = step_variant(s);  // before the position advances
         cudaMemsetAsync(d, 0, n * 8, ctx->stream);
         cudaEventRecord(e0, ctx->stream);
         rc = step_launch(s, true, d);
@@ -362,7 +467,8 @@ int step_profile(cw_session* s, size_t n_steps,
         a.first += 1;
         a.second += ms;
         unsigned long long prev_end = 0;
-        for (int si = 0; si < P->n_stages; si++) {
+        const StepVariant& V = P->v[vsel];
+        for (int si = 0; si < V.n_stages; si++) {
             unsigned long long t0 = ~0ull, t1 = 0;
             double ph[3] = {0, 0, 0};
             int nw = 0;
@@ -377,7 +483,7 @@ int step_profile(cw_session* s, size_t n_steps,
                     nw++;
                 }
             }
-            auto& w = (*agg)[P->names[si]];
+            auto& w = (*agg)[V.names[si]];
             w.first += 1;
             w.second += (double)(t1 - t0) * 1e-6;
             double dmax = 0;  // the slowest CTA's own duration (span minus start skew)
@@ -385,12 +491,12 @@ int step_profile(cw_session* s, size_t n_steps,
                 const unsigned long long* q = &h[((size_t)si * P->grid + b) * MK_STAMPS];
                 if (q[1]) dmax = std::max(dmax, (double)(q[3] - q[0]));
             }
-            auto& wm = (*agg)[std::string(P->names[si]) + ".cta_max"];
+            auto& wm = (*agg)[std::string(V.names[si]) + ".cta_max"];
             wm.first += 1;
             wm.second += dmax * 1e-6;
             static const char* phase[3] = {"prologue", "main", "epilogue"};
             for (int k = 0; k < 3 && nw; k++) {
-                auto& r = (*agg)[std::string(P->names[si]) + "." + phase[k]];
+                auto& r = (*agg)[std::string(V.names[si]) + "." + phase[k]];
                 r.first += 1;
                 r.second += ph[k] / nw * 1e-6;
             }
@@ -406,7 +512,7 @@ int step_profile(cw_session* s, size_t n_steps,
                 nc++;
             }
             for (int k = 0; k < CLK_N - 1 && nc; k++) {
-                auto& r = (*agg)[std::string(P->names[si]) + ":" + clk[k]];
+                auto& r = (*agg)[std::string(V.names[si]) + ":" + clk[k]];
                 r.first += 1;
                 r.second += cl[k] / nc / (double)ctx->clock_khz;  // cycles -> ms
             }
@@ -423,7 +529,7 @@ int step_profile(cw_session* s, size_t n_steps,
                 n3++;
             }
             for (int k = 0; k < 3 && n3; k++) {
-                auto& r = (*agg)[std::string(P->names[si]) + ":" + ck[k]];
+                auto& r = (*agg)[std::string(V.names[si]) + ":" + ck[k]];
                 r.first += 1;
                 r.second += c3[k] / n3 / (double)ctx->clock_khz;
             }
@@ -431,6 +537,9 @@ int step_profile(cw_session* s, size_t n_steps,
                 auto& g = (*agg)["grid_barrier"];
                 g.first += 1;
                 g.second += (double)(t0 - prev_end) * 1e-6;
+                auto& gs = (*agg)[std::string("barrier>") + V.names[si]];  // by the stage it opens
+                gs.first += 1;
+                gs.second += (double)(t0 - prev_end) * 1e-6;
             }
             prev_end = t1;
         }

@@ -98,7 +98,7 @@ inline int mk_rc(int cfg) {  // rows per chunk
 }
 inline int mk_ns(int cfg) { return cfg >= MK_NCFG ? 2 : 1; }  // ring slots per chunk
 
-enum { SK_GEMV = 0, SK_ATTN = 1, SK_FFN = 2 };
+enum { SK_GEMV = 0, SK_ATTN = 1, SK_FFN = 2, SK_ATTNO = 3 };
 
 // Fixed-point residual accumulator: the FFN stage adds its down-projection
 // partial sums into int64 words scaled by 2^32 with integer atomics, so the
@@ -106,20 +106,28 @@ enum { SK_GEMV = 0, SK_ATTN = 1, SK_FFN = 2 };
 constexpr float MK_FIX = 4294967296.0f;      // 2^32
 constexpr float MK_UNFIX = 2.3283064365386963e-10f;  // 2^-32
 constexpr int MK_DOWN_ROWS = MK_SLOT_PAY / 16;  // rows of one down-projection slot (1024)
+__host__ __device__ __forceinline__ long long* acc_at(long long* a, int r) { return a + r; }
 
 struct MStage {
     int kind, cfg, pro, epi;
     int K, N, RC, nchunks;
     // FFN stage: act blocks (units), gate/up chunks and down slots per unit
     int nunits, per0, per1, N2;
-    // residual accumulator: add it to the residual read here (acc_in), zero
-    // the rows written here (acc_zero)
-    int acc_in, acc_zero;
-    int pad0, pad1;
+    // residual accumulators (fixed point): acc_in = 0, 1 (racc) or 2 (racc,
+    // racc2) of them added, in that order, to the residual read here;
+    // acc_zero: zero racc at the rows this stage writes; zero_acc: clear the
+    // accumulator acc_clear (dim rows) at the start of a step
+    int acc_in, acc_zero, zero_acc;
+    int layer;                // ATTNO: layer index (head-counter target)
     long long* racc;
+    long long* racc2;
+    long long* acc_clear;     // the accumulator cleared by zero_acc
+    long long* fold_a;        // ATTNO: accumulator folded into y (the residual) by the
+                              // CTAs without a head; FFN: the accumulator it adds into
+    long long* fold_b;        // (unused)
     const uint8_t* payload2;  // FFN: down projection, column-block-major [K/32 of down][dim][16]
     const __half* scales2;    //      and its scales [K/32 of down][dim]
-    const void* pad_ptr;
+    const void* pad_ptr0;
     const uint8_t* payload;
     const __half* scales;
     const float* x;        // PRO_X input
@@ -135,6 +143,8 @@ struct MStage {
     float* vc;
 };
 static_assert(sizeof(MStage) % 16 == 0, "stage descriptors are copied in 16-byte pieces");
+static_assert(MK_DOWN_ROWS % MK_THREADS == 0, "whole rows per thread in one-block-per-row slots");
+static_assert(MK_SLOTS >= 4, "a head's O-projection column blocks (head_dim <= 128) fit the ring");
 
 // The weight-copy schedule of one stage (nchunks 0: no weights), kept in
 // shared memory so the copy issuer never waits on a global read.
@@ -171,6 +181,12 @@ struct MParams {
     const float* inv_freq;
     int dim, n_heads, n_kv, hd, max_seq, n_splits, part_stride, decode;
     int attn_min;  // keys per attention split before splitting further
+    // fused attention stage: per-head O-projection row sums [n_heads][dim],
+    // and the counter the head CTAs bump when theirs are stored (monotonic;
+    // DevState.ctr_base is its value at the start of the step)
+    float* opart;
+    unsigned long long* hctr;
+    int hctr_per_step;
     float eps, scale;
     float inv_dim;      // 1/dim: the mean of squares as a product (exact for power-of-two dims)
     size_t work_bytes;  // shared-memory work region (q24 + hbuf + wbuf, or attention scratch)
@@ -184,6 +200,10 @@ struct MParams {
 // 16 warps (4 keys each) before a split is worth its combine
 constexpr int MK_ATTN_MIN = MK_WARPS * ATTN_U;
 constexpr int MK_PRE = 2;  // epilogue addends preloaded per stage (chunks)
+// Contexts (position + 1) up to which a step uses the fused attention + O
+// projection stage (one CTA per query head over all keys); longer contexts
+// use split-KV attention and a separate O-projection stage.
+constexpr int MK_FUSE_MAX = 768;
 // With 2..MK_DEFER active key splits, the attention stage only publishes each
 // split's (accumulator, max, denominator) and the O-projection stage merges
 // the splits while it builds its input (no combine step, fence or counter
@@ -215,6 +235,7 @@ struct MCtx {
     int redsel;         // CTA-sum buffer of the next call
     int nch;            // chunks consumed (row-partial buffer parity)
     int pos;
+    unsigned long long hbase;   // head counter at the start of the step
     unsigned long long* stamp;  // this stage's stamps (profiling) or null
 };
 
@@ -291,6 +312,17 @@ __device__ inline bool mk_issue_next(const MParams& p, MCtx& c) {
                 return true;
             }
         }
+        if (I.kind == SK_ATTNO && u < I.n0) {  // head u: row chunk j / per0, column block j % per0
+            const int j = sh->it_j, rc = j / I.per0, k = j % I.per0;
+            const int r0 = rc * MK_DOWN_ROWS, rows = min(MK_DOWN_ROWS, I.dim - r0);
+            const size_t off = ((size_t)u * I.per0 + k) * I.dim + r0;
+            mk_issue_copy(c, I.pay1 + off * 16, I.sc1 + off, (unsigned)rows * 16, (unsigned)rows * 2);
+            if (++sh->it_j == I.per0 * I.per1) {
+                sh->it_j = 0;
+                sh->it_t++;
+            }
+            return true;
+        }
         if (I.kind == SK_FFN && u < I.n0) {
             const int j = sh->it_j;
             if (j < I.per0) {  // gate/up rows [64u + j*rc, +rc)
@@ -335,9 +367,10 @@ __device__ inline void mk_fail(const MParams& p, MCtx& c) {
     __syncthreads();
 }
 
-// Grid-wide barrier: arrive (release), then poll (acquire) until the counter
-// reaches `target`; the status word and the time limit are checked every 64
-// polls.
+// Grid-wide barrier: __syncthreads orders the CTA's writes before thread 0's
+// gpu-scope release arrive; thread 0 polls (acquire) until the counter
+// reaches `target`, and __syncthreads passes that on to the CTA.  The status
+// word and the time limit are checked every 64 polls.
 __device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long long target) {
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -427,6 +460,16 @@ __device__ __forceinline__ void mk_q24_quad(const Q24& s, int b, bool valid, con
 }
 
 __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+// h + 2^-32 * (accumulator rows i .. i+3; i % 4 == 0)
+__device__ __forceinline__ float4 mk_add_fixed4(float4 h, const long long* acc, int i) {
+    const longlong2 a0 = __ldcg(reinterpret_cast<const longlong2*>(acc + i));
+    const longlong2 a1 = __ldcg(reinterpret_cast<const longlong2*>(acc + i + 2));
+    h.x = h.x + __ll2float_rn(a0.x) * MK_UNFIX;
+    h.y = h.y + __ll2float_rn(a0.y) * MK_UNFIX;
+    h.z = h.z + __ll2float_rn(a1.x) * MK_UNFIX;
+    h.w = h.w + __ll2float_rn(a1.y) * MK_UNFIX;
+    return h;
+}
 __device__ __forceinline__ float4 f4_norm(const float4& h, float inv, const float4& g) {
     return make_float4(__fmul_rn(__fmul_rn(h.x, inv), g.x), __fmul_rn(__fmul_rn(h.y, inv), g.y),
                        __fmul_rn(__fmul_rn(h.z, inv), g.z), __fmul_rn(__fmul_rn(h.w, inv), g.w));
@@ -525,14 +568,8 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
     auto ld_src = [&](int i) {
         float4 h = gsrc ? __ldcg(reinterpret_cast<const float4*>(src + i))
                         : *reinterpret_cast<const float4*>(src + i);
-        if (S.acc_in) {
-            const longlong2 a0 = __ldcg(reinterpret_cast<const longlong2*>(S.racc + i));
-            const longlong2 a1 = __ldcg(reinterpret_cast<const longlong2*>(S.racc + i + 2));
-            h.x = h.x + __ll2float_rn(a0.x) * MK_UNFIX;
-            h.y = h.y + __ll2float_rn(a0.y) * MK_UNFIX;
-            h.z = h.z + __ll2float_rn(a1.x) * MK_UNFIX;
-            h.w = h.w + __ll2float_rn(a1.y) * MK_UNFIX;
-        }
+        if (S.acc_in >= 1) h = mk_add_fixed4(h, S.racc, i);
+        if (S.acc_in >= 2) h = mk_add_fixed4(h, S.racc2, i);
         return h;
     };
     float ss = 0.f;
@@ -743,6 +780,9 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     constexpr int WPR = CF::WPR, RC = CF::RC;
     const int nb = S.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (S.zero_acc)  // start of a step: the residual accumulators from zero
+        for (int r = blockIdx.x * MK_THREADS + tid; r < p.dim; r += gridDim.x * MK_THREADS)
+            *acc_at(S.acc_clear, r) = 0;
     if ((int)blockIdx.x >= S.nchunks) return true;  // no rows of this stage here
     // epilogue addends (old residual or bias) of the first chunks, requested
     // now so they arrive while the prologue runs
@@ -755,7 +795,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
         if (has_pre && tid < RC && row < S.N) {
             pre[t] = S.epi == EPI_RESID ? __ldcg(S.y + row) : __ldg(S.bias + row);
             if (S.epi == EPI_RESID && S.acc_in)
-                pre[t] = pre[t] + __ll2float_rn(__ldcg(S.racc + row)) * MK_UNFIX;
+                pre[t] = pre[t] + __ll2float_rn(__ldcg(acc_at(S.racc, (int)row))) * MK_UNFIX;
         }
     }
     const Q24 q = q24_carve(c.work, nb);
@@ -778,7 +818,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
         if (t >= MK_PRE && has_pre && tid < rows) {  // later chunks: requested before the wait
             add = S.epi == EPI_RESID ? __ldcg(S.y + row0 + tid) : __ldg(S.bias + row0 + tid);
             if (S.epi == EPI_RESID && S.acc_in)
-                add = add + __ll2float_rn(__ldcg(S.racc + row0 + tid)) * MK_UNFIX;
+                add = add + __ll2float_rn(__ldcg(acc_at(S.racc, (int)row0 + tid))) * MK_UNFIX;
         }
         const float* rb = mk_chunk<CF>(p, c, nb, rows, R, t == 0);
         if (!rb) return false;
@@ -805,7 +845,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
                 best = kk > best ? kk : best;
             } else {
                 S.y[row] = has_pre ? (S.epi == EPI_RESID ? add + vv : vv + add) : vv;
-                if (S.acc_zero) S.racc[row] = 0;
+                if (S.acc_zero) *acc_at(S.racc, (int)row) = 0;
             }
         }
     }
@@ -833,7 +873,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
 // converted to one q24 block, and the down projection's column block u
 // (MK_DOWN_ROWS rows per ring slot, one Q4_0 block per row) turns them into a
 // partial sum for every output row, added into the fixed-point residual
-// accumulator (the next stage that reads the residual adds it).
+// accumulator S.fold_a (the next stage that reads the residual adds it).
 template <class CF>
 __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
     constexpr int WPR = CF::WPR, RC = CF::RC;
@@ -902,7 +942,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
                 const float d = __half2float(scs[r]);
                 const float part = fmaf(d * asb, mk_block_dot(w4, xa, xb, acb), 0.f);
                 const long long fx = __float2ll_rn(part * MK_FIX);
-                atomicAdd(reinterpret_cast<unsigned long long*>(S.racc + r0 + r),
+                atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.fold_a, r0 + r)),
                           (unsigned long long)fx);
             }
             __syncthreads();  // slot consumed
@@ -920,6 +960,15 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
 // K/V rows of that unit into L2 while the stage before it runs.
 __device__ inline void mk_kv_prefetch(const MParams& p, const MStage& A, const MCtx& c) {
     const int seq = c.pos + 1;
+    if (A.kind == SK_ATTNO) {  // unit = query head: all cached rows of its group
+        if ((int)blockIdx.x >= p.n_heads || c.pos == 0) return;
+        const int g = blockIdx.x / (p.n_heads / p.n_kv);
+        const float* kb = A.kc + (size_t)g * p.max_seq * p.hd;
+        const float* vb = A.vc + (size_t)g * p.max_seq * p.hd;
+        prefetch_l2(kb, kb + (size_t)c.pos * p.hd);
+        prefetch_l2(vb, vb + (size_t)c.pos * p.hd);
+        return;
+    }
     const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
     const int u = blockIdx.x;
     if (u >= p.n_kv * n_active) return;
@@ -1032,6 +1081,192 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
     return true;
 }
 
+// ---- fused attention + O projection (short contexts) ---------------------------------
+// Unit = query head h (CTA h): QK-norm + RoPE of q_h and of its group's k,
+// the group's new K/V row written to the cache (the G CTAs of a group write
+// the same values), attention over all keys in one split, the normalised
+// output (hd values) as q24 blocks, then its slice of the O projection --
+// column blocks h*hd/32 .. of W_o, MK_DOWN_ROWS rows per ring slot -- whose
+// row sums are stored to p.opart[h].  The CTAs without a head then add the
+// heads' sums, in head order, to the residual (nothing else reads or writes
+// the residual during this stage), folding in the FFN accumulator too.
+template <int EPL>
+__device__ inline bool mk_attno(const MParams& p, const MStage& S, MCtx& c) {
+    const int G = p.n_heads / p.n_kv, hd = p.hd, half = hd / 2, nbh = hd / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pos = c.pos, seq = pos + 1;
+    const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
+    if ((int)blockIdx.x >= p.n_heads) {
+        // CTAs without a head: rows [f*rpc, ...) of the residual.  The old
+        // residual (y + A) is read while the heads compute; once every head
+        // has stored its O-projection row sums (the head counter reaches this
+        // layer's target), y = (y + A) + sum_h part[h] in head order, A = 0.
+        const int nf = gridDim.x - p.n_heads, f = blockIdx.x - p.n_heads;
+        const int rpc = (p.dim + nf - 1) / nf, r = f * rpc + tid;
+        const bool mine = tid < rpc && r < p.dim;
+        const float h0 = mine ? __ldcg(S.y + r) + __ll2float_rn(__ldcg(acc_at(S.fold_a, r))) * MK_UNFIX
+                              : 0.f;
+        if (tid == 0) {
+            const unsigned long long target = c.hbase + (unsigned long long)(S.layer + 1) * p.n_heads;
+            uint64_t t0 = 0;
+            int ok = 1;
+            for (unsigned it = 1; ld_acquire_u64(p.hctr) < target; it++) {
+                if ((it & 63) == 0) {
+                    const uint64_t now = global_ns();
+                    if (t0 == 0) t0 = now;
+                    if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
+                        ok = 0;
+                        break;
+                    }
+                }
+            }
+            if (!ok) {
+                atomicExch(p.status, (int)DEV_TIMEOUT);
+                c.sh->abort = 1;
+            }
+        }
+        __syncthreads();
+        if (c.sh->abort) return false;
+        if (mine) {
+            float o = 0.f;
+            for (int hh = 0; hh < p.n_heads; hh++) o += __ldcg(p.opart + (size_t)hh * p.dim + r);
+            S.y[r] = h0 + o;
+            *acc_at(S.fold_a, r) = 0;
+        }
+        return true;
+    }
+    const int h = blockIdx.x, g = h / G;
+    const int W = hd + 2;
+    float* sm = reinterpret_cast<float*>(c.work);                   // attn_core scratch (G = 1)
+    float* res = sm + (size_t)MK_WARPS * W;
+    float* qs = sm + al16(((size_t)(MK_WARPS + 1) * W + MK_WARPS) * 4) / 4;
+    float* ks = qs + hd;
+    float* os = ks + hd;
+    const Q24 aq = q24_carve(os + hd, nbh);
+    // prologue: every global input requested first (q row h by warp 0, k row g
+    // by warp 1, with their gains; the new V row; this thread's RoPE angle)
+    {
+        const bool isq = warp == 0, has_row = warp < 2;
+        const float* src = isq ? p.qkv + (size_t)h * hd : p.qkv + qd + (size_t)g * hd;
+        const float* nw = isq ? S.q_norm : S.k_norm;
+        float vv[EPL], wv[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; e++) {
+            const int d = lane + 32 * e;
+            const bool in = has_row && d < hd;
+            vv[e] = in ? __ldcg(src + d) : 0.f;
+            wv[e] = (in && nw) ? __ldg(nw + d) : 0.f;
+        }
+        const float vnew = tid < hd ? __ldcg(p.qkv + qd + kvd + (size_t)g * hd + tid) : 0.f;
+        float sn = 0.f, cs = 1.f;
+        if (tid < 2 * half) sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid % half)), &sn, &cs);
+        if (has_row) {  // QK-norm (qwen3.rs:154-155)
+            if (nw) {
+                float ss = 0.f;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) ss = fmaf(vv[e], vv[e], ss);
+                ss = warp_sum(ss);
+                const float inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
+#pragma unroll
+                for (int e = 0; e < EPL; e++) vv[e] = __fmul_rn(__fmul_rn(vv[e], inv), wv[e]);
+            }
+            float* dst = isq ? qs : ks;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const int d = lane + 32 * e;
+                if (d < hd) dst[d] = vv[e];
+            }
+        }
+        __syncthreads();
+        if (tid < 2 * half) {  // RoPE (rope.wgsl:25-34): one rotated pair per thread
+            float* row = tid < half ? qs : ks;
+            const int kq = tid % half;
+            const float lo = row[kq], hi = row[kq + half];
+            row[kq] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
+            row[kq + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+        }
+        __syncthreads();
+        float* kbase = S.kc + (size_t)g * p.max_seq * hd;
+        float* vbase = S.vc + (size_t)g * p.max_seq * hd;
+        if (tid < hd) {  // cache.rs:21-24
+            kbase[(size_t)pos * hd + tid] = ks[tid];
+            vbase[(size_t)pos * hd + tid] = vnew;
+        }
+        __syncthreads();
+        mk_clk(c, CLK_LOADED);
+        if (c.stamp && tid == 0) c.stamp[1] = global_ns();
+        attn_core<EPL, 1, KV_CG, MK_WARPS>(qs, 1, hd, kbase, vbase, hd, 0, seq, p.scale, 0.f, sm,
+                                           res);
+    }
+    mk_clk(c, CLK_NORMED);
+    if (tid < hd) os[tid] = res[tid] * (1.0f / res[hd + 1]);  // attention.wgsl:96
+    __syncthreads();
+    if (warp == 0) {  // the head's output as nbh q24 blocks (lane: block lane/8)
+        const int b = lane >> 3;
+        const float4 v = b < nbh ? *reinterpret_cast<const float4*>(os + b * 32 + 4 * (lane & 7))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        mk_q24_quad(aq, b, b < nbh, v, lane);
+    }
+    __syncthreads();
+    mk_clk(c, CLK_Q24);
+    if (c.stamp && tid == 0) c.stamp[2] = global_ns();
+    // O projection slice: per row chunk, the nbh column blocks (consecutive
+    // ring slots) waited for together and consumed in one pass
+    for (int rc = 0; rc < S.per1; rc++) {
+        const int r0 = rc * MK_DOWN_ROWS, rows = min(MK_DOWN_ROWS, p.dim - r0);
+        bool ok = true;
+        for (int k = 0; k < nbh; k++) {
+            const int q = c.seq + k;
+            ok = mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS) && ok;
+        }
+        if (__syncthreads_or(!ok)) {
+            mk_fail(p, c);
+            return false;
+        }
+        float acc[MK_DOWN_ROWS / MK_THREADS];
+#pragma unroll
+        for (int i = 0; i < MK_DOWN_ROWS / MK_THREADS; i++) acc[i] = 0.f;
+        for (int k = 0; k < nbh; k++) {
+            uint4 xa[3], xb[3];
+#pragma unroll
+            for (int pl = 0; pl < 3; pl++) {
+                xa[pl] = aq.pl[(pl * 2 + 0) * nbh + k];
+                xb[pl] = aq.pl[(pl * 2 + 1) * nbh + k];
+            }
+            const int acb = aq.cb[k];
+            const float asb = aq.sb[k];
+            const unsigned char* pay = c.ring + (size_t)((c.seq + k) % MK_SLOTS) * MK_SLOT_BYTES;
+            const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+#pragma unroll
+            for (int i = 0; i < MK_DOWN_ROWS / MK_THREADS; i++) {
+                const int r = tid + i * MK_THREADS;
+                if (r < rows) {
+                    const uint4 w4 = reinterpret_cast<const uint4*>(pay)[r];
+                    const float d = __half2float(scs[r]);
+                    acc[i] = fmaf(d * asb, mk_block_dot(w4, xa, xb, acb), acc[i]);
+                }
+            }
+        }
+        __syncthreads();  // slots consumed
+        if (tid == MK_ISSUER)
+            for (int k = 0; k < nbh; k++) mk_issue_next(p, c);
+        c.seq += nbh;
+#pragma unroll
+        for (int i = 0; i < MK_DOWN_ROWS / MK_THREADS; i++) {
+            const int r = tid + i * MK_THREADS;
+            if (r < rows) p.opart[(size_t)h * p.dim + r0 + r] = acc[i];
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {  // this head's row sums are stored: release them to the fold CTAs
+        __threadfence();
+        atomicAdd(p.hctr, 1ull);
+    }
+    mk_clk(c, CLK_REGS);
+    mk_clk(c, CLK_MAIN);
+    return true;
+}
+
 // GEMV work mapping by config index and slots per chunk.
 template <int I, int NS> struct CfgOfT;
 template <> struct CfgOfT<0, 1> { using T = MC0; };
@@ -1088,6 +1323,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     const int pos = p.st->pos;
     const unsigned tok = p.st->token;
     const unsigned long long base = p.st->bar_base;
+    c.hbase = p.st->ctr_base;
     c.pos = pos;
     __syncthreads();
     if (tid == MK_ISSUER)  // the first ring-full of weights
@@ -1121,10 +1357,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
         mk_load_stage(p, si + 2, &sst[(si + 2) % 3]);  // waited for at the stage end
         const MStage& S = sst[si % 3];
         const MStage& S1 = sst[(si + 1) % 3];
-        if (tid == 0 && si + 1 < p.n_stages && S1.kind == SK_ATTN) mk_kv_prefetch(p, S1, c);
+        if (tid == 0 && si + 1 < p.n_stages && (S1.kind == SK_ATTN || S1.kind == SK_ATTNO))
+            mk_kv_prefetch(p, S1, c);
         mk_clk(c, CLK_AHEAD);
         if (S.kind == SK_ATTN) {
             ok = mk_attn<EPL, GMAX>(p, S, c);
+        } else if (S.kind == SK_ATTNO) {
+            ok = mk_attno<EPL>(p, S, c);
         } else if (S.kind == SK_FFN) {
             ok = mk_ffn<CfgOf<CD, 2>>(p, S, c);
         } else if (S.cfg == CD) {
@@ -1168,6 +1407,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
             st->pos = pos + 1;
             st->done = 0;
             st->bar_base = base + (unsigned long long)(p.n_stages - 1) * gridDim.x;
+            st->ctr_base = c.hbase + (unsigned long long)p.hctr_per_step;
             __threadfence();
         }
     }

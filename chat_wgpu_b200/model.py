@@ -13,6 +13,7 @@ composes a model and to cross-check the fused path.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -30,6 +31,8 @@ class Model:
         h = C.c_void_p()
         _lib.call("cw_model_load_gguf", ctx.handle, path.encode(), C.byref(h))
         self._h = h
+        self._sessions = weakref.WeakSet()  # released before the model
+        ctx._adopt(self)
         info = _lib.ModelInfo()
         _lib.call("cw_model_get_info", self._h, C.byref(info))
         self.info = {k: (getattr(info, k).decode() if k == "arch" else getattr(info, k))
@@ -45,6 +48,8 @@ class Model:
 
     def close(self):
         if getattr(self, "_h", None):
+            for sess in list(getattr(self, "_sessions", ())):
+                sess.close()
             _lib.load().cw_model_free(self._h)
             self._h = None
 
@@ -66,6 +71,7 @@ class Session:
         _lib.call("cw_session_create", model.handle, int(max_seq), C.byref(h))
         self._h = h
         self.max_seq = int(max_seq)
+        model._sessions.add(self)
 
     def close(self):
         if getattr(self, "_h", None):
@@ -81,10 +87,15 @@ class Session:
     def set_graph(self, use_graph: bool) -> None:
         _lib.call("cw_session_set_graph", self._h, 1 if use_graph else 0)
 
-    def set_persistent(self, on: bool) -> None:
-        """Select the step kernel: one persistent cooperative launch per token
-        (default where the family is covered) or one kernel per stage."""
-        _lib.call("cw_session_set_persistent", self._h, 1 if on else 0)
+    def set_persistent(self, on) -> None:
+        """Select the step kernel: True/1 one persistent cooperative launch per
+        token (default where the family is covered), "split"/2 or "fused"/3
+        that launch with one of its two plans only, False/0 one kernel per
+        stage."""
+        mode = {"split": 2, "fused": 3}.get(on, None) if isinstance(on, str) else (1 if on else 0)
+        if mode is None:
+            raise ValueError(f"unknown persistent mode {on!r}")
+        _lib.call("cw_session_set_persistent", self._h, int(mode))
 
     @property
     def persistent(self) -> bool:

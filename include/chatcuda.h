@@ -247,11 +247,14 @@ int cw_session_hidden(cw_session* s, float* out, size_t dim);
 int cw_session_set_graph(cw_session* s, int use_graph);
 /* Step kernel selection (no reference counterpart: the reference always
  * dispatches one compute pass per op).  1 = the whole step as ONE persistent
- * cooperative launch (default for families it covers: no post-norms, no
+ * cooperative launch (default for the shapes it covers: no post-norms, no
  * sliding window, no soft-caps, RMSNorm, SwiGLU, dim/q-dim/hidden multiples
- * of 256); 0 = one kernel per stage.  Returns CW_ERR_UNSUPPORTED when 1 is
- * asked for a family it does not cover.  cw_session_persistent reports the
- * path in use. */
+ * of 256, a compiled kernel variant for the head shape), choosing per step
+ * between its fused short-context plan and its split-attention plan;
+ * 2 / 3 = persistent with the split / fused plan only (testing); 0 = one
+ * kernel per stage.  Returns CW_ERR_UNSUPPORTED when a persistent mode is
+ * asked for a family it does not cover.  cw_session_persistent reports
+ * whether the persistent step is in use. */
 int cw_session_set_persistent(cw_session* s, int on);
 int cw_session_persistent(cw_session* s, int* on);
 /* One step with a host round trip, the shape of the reference's loop body

@@ -71,7 +71,8 @@ def models(tmp_path_factory):
 PERSISTENT = {"tiny-qwen3": False, "small-qwen3": True, "tiny-gemma2": False, "tiny-qwen2": True}
 
 
-@pytest.mark.parametrize("persistent", [False, True], ids=["per-stage", "persistent"])
+@pytest.mark.parametrize("persistent", [False, True, "split", "fused"],
+                         ids=["per-stage", "persistent", "persistent-split", "persistent-fused"])
 @pytest.mark.parametrize("name", ["tiny-qwen3", "small-qwen3", "tiny-gemma2", "tiny-qwen2"])
 def test_fused_session_vs_oracle(ctx, orc, models, name, persistent):
     from chat_wgpu_b200.model import Model
@@ -125,13 +126,15 @@ def test_persistent_default_and_coverage(ctx, models, name):
     m.close()
 
 
+@pytest.mark.parametrize("mode", ["split", "fused"])
 @pytest.mark.parametrize("n_prompt", [200, 300])
-def test_persistent_equals_per_stage_long(ctx, orc, models, n_prompt):
-    """Long prompts and 40 generated tokens on small-qwen3: the attention stage
-    runs with several active key splits (200: 4 splits, merged by the
-    O-projection stage; 300: 5-6 splits, combined inside the attention stage).
-    Persistent and per-stage paths both within tolerance of the oracle;
-    persistent graph == direct, bit-exact."""
+def test_persistent_equals_per_stage_long(ctx, orc, models, n_prompt, mode):
+    """Long prompts and 40 generated tokens on small-qwen3.  Split plan: the
+    attention stage runs with several active key splits (200: 4 splits,
+    merged by the O-projection stage; 300: 5-6 splits, combined inside the
+    attention stage).  Fused plan: one CTA per query head over all keys with
+    the O projection in the same stage.  Persistent and per-stage paths both
+    within tolerance of the oracle; persistent graph == direct, bit-exact."""
     from chat_wgpu_b200.model import Model
     path = models["small-qwen3"]
     om = orc.Model(path)
@@ -139,11 +142,11 @@ def test_persistent_equals_per_stage_long(ctx, orc, models, n_prompt):
     prompt = rng.integers(0, om.vocab, n_prompt).astype(np.uint32)
     ref_toks, ref_logits = om.generate(prompt, 40, want_logits=True)
     m = Model(ctx, path)
-    tp, lp = session_stream(m, prompt, 40, persistent=True)
+    tp, lp = session_stream(m, prompt, 40, persistent=mode)
     ts, ls = session_stream(m, prompt, 40, persistent=False)
     assert compare_streams(tp, ref_toks, ref_logits, lp) >= 4
     assert compare_streams(ts, ref_toks, ref_logits, ls) >= 4
-    td, ld = session_stream(m, prompt, 40, use_graph=False, persistent=True)
+    td, ld = session_stream(m, prompt, 40, use_graph=False, persistent=mode)
     assert np.array_equal(tp, td)
     assert np.array_equal(lp.view(np.uint32), ld.view(np.uint32))
     m.close()
@@ -213,8 +216,9 @@ def test_full_size_qwen3_0_6b(ctx, orc):
     toks2, logits2 = session_stream(m, prompt, 4)
     assert np.array_equal(toks, toks2)
     assert np.array_equal(logits.view(np.uint32), logits2.view(np.uint32))
-    # the per-stage kernels on the same checkpoint
-    toks3, logits3 = session_stream(m, prompt, 4, persistent=False)
-    assert compare_streams(toks3, ref_toks, ref_logits, logits3) >= 1
+    # the per-stage kernels and both persistent plans on the same checkpoint
+    for mode in (False, "split", "fused"):
+        toks3, logits3 = session_stream(m, prompt, 4, persistent=mode)
+        assert compare_streams(toks3, ref_toks, ref_logits, logits3) >= 1, mode
     m.close()
     om.close()
