@@ -61,19 +61,32 @@ def parse():
 
 # ---------------------------------------------------------------- plumbing
 class Dist:
-    def __init__(self):
+    """One process per GPU (torchrun env).  The process group carries only the
+    barrier and the max-over-ranks of the timings: sessions are independent
+    replicas (no data-path collective).  Backend: NCCL on the GPU box; gloo
+    (CW_DIST_BACKEND=gloo or no CUDA) for the CPU tests of this plumbing."""
+
+    def __init__(self, backend: str | None = None):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = False
+        self.device = "cpu"
         if self.world > 1:
             import datetime
 
             import torch
             import torch.distributed as dist
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
+            backend = backend or os.environ.get("CW_DIST_BACKEND") or (
+                "nccl" if torch.cuda.is_available() else "gloo")
+            timeout = datetime.timedelta(seconds=600)
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+                self.device = f"cuda:{self.local}"
+                dist.init_process_group("nccl", timeout=timeout,
+                                        device_id=torch.device("cuda", self.local))
+            else:
+                dist.init_process_group(backend, timeout=timeout)
             self.pg = True
 
     def barrier(self):
@@ -86,7 +99,7 @@ class Dist:
             return v
         import torch
         import torch.distributed as dist
-        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        t = torch.tensor([v], dtype=torch.float64, device=self.device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
@@ -94,6 +107,13 @@ class Dist:
         if self.pg:
             import torch.distributed as dist
             dist.destroy_process_group()
+            self.pg = False
+
+
+def replica_rate(steps: int, world: int, seconds_max: float) -> float:
+    """Whole-job tokens/s of `world` replicas that each ran `steps` tokens, the
+    slowest in seconds_max (weak scaling: per-GPU work fixed as N grows)."""
+    return steps * world / seconds_max
 
 
 def physical_gpu(local: int) -> str:
@@ -314,7 +334,7 @@ def run_cuda(args, dist):
     ms_max = dist.max(ms)
     toks = s.tokens()
     assert toks.size == W + K, (toks.size, W + K)
-    value = K * dist.world / (ms_max / 1000.0)
+    value = replica_rate(K, dist.world, ms_max / 1000.0)
     pos_lo, pos_hi = P - 1 + W, P - 1 + W + K - 1
     mean_pos = 0.5 * (pos_lo + pos_hi)
     _, launches_decode = s.launches()
@@ -350,7 +370,7 @@ def run_cuda(args, dist):
     e2e_max = dist.max(e2e_s)
     toks2 = s2.tokens()
     s2.close()
-    e2e_value = K * dist.world / e2e_max
+    e2e_value = replica_rate(K, dist.world, e2e_max)
     same_stream = bool(np.array_equal(toks, toks2))
 
     # ---- roofline of the dominant kernel
