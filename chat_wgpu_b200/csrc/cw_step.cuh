@@ -119,6 +119,7 @@ struct MStage {
     // accumulator acc_clear (dim rows) at the start of a step
     int acc_in, acc_zero, zero_acc;
     int layer;                // ATTNO: layer index (head-counter target)
+    int pad1, pad2, pad3, pad4;
     long long* racc;
     long long* racc2;
     long long* acc_clear;     // the accumulator cleared by zero_acc
@@ -128,6 +129,8 @@ struct MStage {
     const uint8_t* payload2;  // FFN: down projection, column-block-major [K/32 of down][dim][16]
     const __half* scales2;    //      and its scales [K/32 of down][dim]
     const void* pad_ptr0;
+    const void* pad_ptr1;
+    const void* pad_ptr2;
     const uint8_t* payload;
     const __half* scales;
     const float* x;        // PRO_X input
@@ -203,12 +206,15 @@ constexpr int MK_PRE = 2;  // epilogue addends preloaded per stage (chunks)
 // Contexts (position + 1) up to which a step uses the fused attention + O
 // projection stage (one CTA per query head over all keys); longer contexts
 // use split-KV attention and a separate O-projection stage.
-constexpr int MK_FUSE_MAX = 768;
+// The fused plan is measured slower than the split plan on Qwen3-0.6B at
+// every context length (its single-CTA attention and the cross-head fold sit
+// on the critical path), so by default no step uses it (mode 3 selects it).
+constexpr int MK_FUSE_MAX = 0;
 // With 2..MK_DEFER active key splits, the attention stage only publishes each
 // split's (accumulator, max, denominator) and the O-projection stage merges
 // the splits while it builds its input (no combine step, fence or counter
 // inside the attention stage); with more splits the attention stage combines.
-constexpr int MK_DEFER = 4;
+constexpr int MK_DEFER = 8;
 enum { PRO_ATTN = 2 };  // prologue: merged attention splits (see MK_DEFER)
 
 // per-CTA state shared by all threads
@@ -512,25 +518,32 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
                     const int i0 = b * 32 + e0, h = i0 / hd, d0 = i0 - h * hd;
                     const float* ph = p.part + (size_t)h * p.part_stride * W + d0;
                     const float* cc = cw + h * (na + 1);
-                    float2 lo[MK_DEFER], hi[MK_DEFER];  // (W even, d0 % 4 == 0: 8-byte aligned)
+                    // splits in groups of four (W even, d0 % 4 == 0: 8-byte
+                    // aligned float2 pairs); fixed summation tree
+                    float r[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int s = 0; s < MK_DEFER; s++) {
-                        const float2* q2 = reinterpret_cast<const float2*>(ph + (size_t)s * W);
-                        lo[s] = s < na ? __ldcg(q2) : make_float2(0.f, 0.f);
-                        hi[s] = s < na ? __ldcg(q2 + 1) : make_float2(0.f, 0.f);
-                    }
-                    float r[4];
+                    for (int s0 = 0; s0 < MK_DEFER; s0 += 4) {
+                        if (s0 >= na) break;
+                        float2 lo[4], hi[4];
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        float a[MK_DEFER];
-#pragma unroll
-                        for (int s = 0; s < MK_DEFER; s++) {
-                            const float2 t2 = e < 2 ? lo[s] : hi[s];
-                            a[s] = (s < na ? ((e & 1) ? t2.y : t2.x) : 0.f) * cc[s < na ? s : 0];
+                        for (int j = 0; j < 4; j++) {
+                            const float2* q2 = reinterpret_cast<const float2*>(ph + (size_t)(s0 + j) * W);
+                            lo[j] = s0 + j < na ? __ldcg(q2) : make_float2(0.f, 0.f);
+                            hi[j] = s0 + j < na ? __ldcg(q2 + 1) : make_float2(0.f, 0.f);
                         }
-                        r[e] = ((a[0] + a[1]) + (a[2] + a[3])) * cc[na];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            float a[4];
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const float2 t2 = e < 2 ? lo[j] : hi[j];
+                                a[j] = (s0 + j < na ? ((e & 1) ? t2.y : t2.x) : 0.f) *
+                                       cc[s0 + j < na ? s0 + j : 0];
+                            }
+                            r[e] = r[e] + ((a[0] + a[1]) + (a[2] + a[3]));
+                        }
                     }
-                    v[k] = make_float4(r[0], r[1], r[2], r[3]);
+                    v[k] = make_float4(r[0] * cc[na], r[1] * cc[na], r[2] * cc[na], r[3] * cc[na]);
                 }
             }
 #pragma unroll

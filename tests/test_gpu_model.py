@@ -127,14 +127,15 @@ def test_persistent_default_and_coverage(ctx, models, name):
 
 
 @pytest.mark.parametrize("mode", ["split", "fused"])
-@pytest.mark.parametrize("n_prompt", [200, 300])
+@pytest.mark.parametrize("n_prompt", [200, 300, 600])
 def test_persistent_equals_per_stage_long(ctx, orc, models, n_prompt, mode):
     """Long prompts and 40 generated tokens on small-qwen3.  Split plan: the
-    attention stage runs with several active key splits (200: 4 splits,
-    merged by the O-projection stage; 300: 5-6 splits, combined inside the
-    attention stage).  Fused plan: one CTA per query head over all keys with
-    the O projection in the same stage.  Persistent and per-stage paths both
-    within tolerance of the oracle; persistent graph == direct, bit-exact."""
+    attention stage runs with several active key splits (200: 4 and 300: 5-6
+    splits, merged by the O-projection stage; 600: 10 splits, combined inside
+    the attention stage).  Fused plan: one CTA per query head over all keys
+    with the O projection in the same stage.  Persistent and per-stage paths
+    both within tolerance of the oracle; persistent graph == direct,
+    bit-exact."""
     from chat_wgpu_b200.model import Model
     path = models["small-qwen3"]
     om = orc.Model(path)
