@@ -187,6 +187,48 @@ __device__ __forceinline__ void q24_block(const Q24& s, int b, float v, int lane
     }
 }
 
+// The same planes from four consecutive elements per lane (GGUF layout only):
+// lane L of a warp covers block b = (quad group) * 4 + L/8, elements
+// 4*(L%8) .. 4*(L%8)+3, given as one float4.  The block max and the integer
+// sum are 3-step shuffles within the 8 lanes of a block, and each lane
+// writes one 32-bit word per byte plane (its 4 elements' bytes, packed with
+// __byte_perm): the bytes q24_block<LAYOUT_GGUF> writes, in a quarter of
+// the instructions.  `valid` (b < nb) may differ between the warp's four
+// groups; every lane takes part in the shuffles.
+__device__ __forceinline__ void q24_quad(const Q24& s, int b, bool valid, const float4& v,
+                                         int lane) {
+    unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                     max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+    m = max(m, __shfl_xor_sync(FULL, m, 1));
+    m = max(m, __shfl_xor_sync(FULL, m, 2));
+    m = max(m, __shfl_xor_sync(FULL, m, 4));
+    int X0, X1, X2, X3;
+    float sb;
+    q24_scale(m, v.x, X0, sb);
+    q24_scale(m, v.y, X1, sb);
+    q24_scale(m, v.z, X2, sb);
+    q24_scale(m, v.w, X3, sb);
+    const int g8 = lane & 7, half = g8 >> 2, w = g8 & 3;
+    if (valid) {
+        uint32_t* pw = reinterpret_cast<uint32_t*>(s.pl);
+#pragma unroll
+        for (int pl = 0; pl < 3; pl++) {
+            const unsigned sel = (unsigned)pl | ((4u + pl) << 4);
+            const unsigned lo = __byte_perm((unsigned)X0, (unsigned)X1, sel);
+            const unsigned hi = __byte_perm((unsigned)X2, (unsigned)X3, sel);
+            pw[((size_t)(pl * 2 + half) * s.nb + b) * 4 + w] = __byte_perm(lo, hi, 0x5410);
+        }
+    }
+    int sx = (X0 + X1) + (X2 + X3);
+    sx += __shfl_xor_sync(FULL, sx, 1);
+    sx += __shfl_xor_sync(FULL, sx, 2);
+    sx += __shfl_xor_sync(FULL, sx, 4);
+    if (valid && g8 == 0) {
+        s.cb[b] = 8 * sx;
+        s.sb[b] = sb;
+    }
+}
+
 // Whole vector from global/shared f32 x[K]; all threads of the CTA call it,
 // a __syncthreads() must follow before the planes are read.
 template <int LAYOUT>

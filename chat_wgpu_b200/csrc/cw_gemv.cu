@@ -1,5 +1,6 @@
 // cw_gemv.cu -- host launcher of the streaming Q4 GEMV (cw_gemv.cuh).
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <tuple>
 
@@ -17,6 +18,8 @@ static int sgemv_go(cw_ctx* ctx, const GemvArgs& a, bool pdl) {
     // CTAs, as many per SM as registers and shared memory allow, each with a
     // two-stage ring (one chunk landing while the other is consumed).
     auto kern = k_sgemv<LAYOUT, PRO, EPI, CF>;
+    // (deeper rings measured slower: they cost CTAs per SM, and the large
+    // GEMVs are bound by their consumers, not by bytes in flight)
     const int S = nchunks <= (long)ctx->sm_count * 2 ? 1 : 2;
     const GemvSmem L(CF::RC, CF::WPR, nb, SW, S, a.K, PRO == PRO_NORM);
     CW_CHECK((int)L.total <= ctx->max_smem_optin, CW_ERR_UNSUPPORTED,
@@ -58,7 +61,9 @@ static int sgemv_cfg(cw_ctx* ctx, const GemvArgs& a, bool pdl) {
     if (nb <= GemvC32::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC32>(ctx, a, pdl);
     if (nb <= GemvC64::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC64>(ctx, a, pdl);
     if (nb <= GemvC96::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC96>(ctx, a, pdl);
+    if (nb <= GemvC128::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC128>(ctx, a, pdl);
     if (nb <= GemvC192::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC192>(ctx, a, pdl);
+    if (nb <= GemvC256::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC256>(ctx, a, pdl);
     if (nb <= GemvC384::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC384>(ctx, a, pdl);
     if constexpr (EPI != EPI_GLU) {  // gate/up pairs need at least two rows per chunk
         if (nb <= GemvC768::NB_MAX) return sgemv_go<LAYOUT, PRO, EPI, GemvC768>(ctx, a, pdl);

@@ -72,7 +72,9 @@ struct GemvCfg {
 using GemvC32 = GemvCfg<1, 1, 4>;   // K <= 1024:  32 rows per chunk
 using GemvC64 = GemvCfg<1, 2, 2>;   // K <= 2048:  16 rows
 using GemvC96 = GemvCfg<1, 3, 1>;   // K <= 3072:   8 rows
+using GemvC128 = GemvCfg<2, 2, 2>;  // K <= 4096:   8 rows (18 KB chunks at 4096, no idle lanes)
 using GemvC192 = GemvCfg<2, 3, 1>;  // K <= 6144:   4 rows
+using GemvC256 = GemvCfg<4, 2, 2>;  // K <= 8192:   4 rows
 using GemvC384 = GemvCfg<4, 3, 1>;  // K <= 12288:  2 rows
 using GemvC768 = GemvCfg<8, 3, 1>;  // K <= 24576:  1 row
 
@@ -223,9 +225,16 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
                                               float* red8) {
     const int nb = a.K / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nw = blockDim.x >> 5, sub = lane >> 3, e0 = 4 * (lane & 7);
     if (PRO == PRO_X) {
-        for (int b = warp; b < nb; b += (blockDim.x >> 5))
-            q24_block<LAYOUT>(q, b, __ldcg(a.x + b * 32 + lane), lane);
+        if constexpr (LAYOUT == LAYOUT_GGUF) {  // four elements per lane (q24_quad); nb % 8 == 0
+            for (int t = warp; t < nb / 4; t += nw) {
+                const int b = 4 * t + sub;
+                q24_quad(q, b, true, __ldcg(reinterpret_cast<const float4*>(a.x + b * 32 + e0)), lane);
+            }
+        } else {
+            for (int b = warp; b < nb; b += nw) q24_block<LAYOUT>(q, b, __ldcg(a.x + b * 32 + lane), lane);
+        }
         return;
     }
     // base/delta may have been written by other CTAs of a persistent kernel:
@@ -260,12 +269,27 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
     ssh = gemv_cta_sum(ssh, red8);
     const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
     const bool wx = a.xn_out && blockIdx.x == 0;
-    for (int b = warp; b < nb; b += (blockDim.x >> 5)) {
+    if constexpr (LAYOUT == LAYOUT_GGUF) {  // four elements per lane (q24_quad); nb % 8 == 0
+        for (int t = warp; t < nb / 4; t += nw) {
+            const int b = 4 * t + sub, i = b * 32 + e0;
+            const float4 h = *reinterpret_cast<const float4*>(hbuf + i);
+            float4 g = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
+            if (a.unit) g = make_float4(1.0f + g.x, 1.0f + g.y, 1.0f + g.z, 1.0f + g.w);
+            const float4 v = make_float4(__fmul_rn(__fmul_rn(h.x, inv), g.x),
+                                         __fmul_rn(__fmul_rn(h.y, inv), g.y),
+                                         __fmul_rn(__fmul_rn(h.z, inv), g.z),
+                                         __fmul_rn(__fmul_rn(h.w, inv), g.w));
+            if (wx) *reinterpret_cast<float4*>(a.xn_out + i) = v;
+            q24_quad(q, b, true, v, lane);
+        }
+    } else {
+    for (int b = warp; b < nb; b += nw) {
         const int i = b * 32 + lane;
         const float gw = a.unit ? 1.0f + a.norm_w[i] : a.norm_w[i];
         const float v = __fmul_rn(__fmul_rn(hbuf[i], inv), gw);
         if (wx) a.xn_out[i] = v;
         q24_block<LAYOUT>(q, b, v, lane);
+    }
     }
 }
 

@@ -433,36 +433,7 @@ constexpr int MK_QB = 2;  // quad groups per warp per batch
 
 __device__ __forceinline__ void mk_q24_quad(const Q24& s, int b, bool valid, const float4& v,
                                             int lane) {
-    unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
-                     max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
-    m = max(m, __shfl_xor_sync(FULL, m, 1));
-    m = max(m, __shfl_xor_sync(FULL, m, 2));
-    m = max(m, __shfl_xor_sync(FULL, m, 4));
-    int X0, X1, X2, X3;
-    float sb;
-    q24_scale(m, v.x, X0, sb);
-    q24_scale(m, v.y, X1, sb);
-    q24_scale(m, v.z, X2, sb);
-    q24_scale(m, v.w, X3, sb);
-    const int g8 = lane & 7, half = g8 >> 2, w = g8 & 3;
-    if (valid) {
-        uint32_t* pw = reinterpret_cast<uint32_t*>(s.pl);
-#pragma unroll
-        for (int pl = 0; pl < 3; pl++) {
-            const unsigned sel = (unsigned)pl | ((4u + pl) << 4);
-            const unsigned lo = __byte_perm((unsigned)X0, (unsigned)X1, sel);
-            const unsigned hi = __byte_perm((unsigned)X2, (unsigned)X3, sel);
-            pw[((size_t)(pl * 2 + half) * s.nb + b) * 4 + w] = __byte_perm(lo, hi, 0x5410);
-        }
-    }
-    int sx = (X0 + X1) + (X2 + X3);
-    sx += __shfl_xor_sync(FULL, sx, 1);
-    sx += __shfl_xor_sync(FULL, sx, 2);
-    sx += __shfl_xor_sync(FULL, sx, 4);
-    if (valid && g8 == 0) {
-        s.cb[b] = 8 * sx;
-        s.sb[b] = sb;
-    }
+    q24_quad(s, b, valid, v, lane);
 }
 
 __device__ __forceinline__ float4 f4_zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
