@@ -100,6 +100,10 @@ struct cw_ctx {
 
     // RoPE inverse-frequency tables keyed by (head_dim, theta bits).
     std::map<std::pair<uint32_t, uint32_t>, float*> rope_tables;
+
+    // grow-only scratch of the prefill GEMM op (split f16 operands)
+    void* gemm_scratch = nullptr;
+    size_t gemm_scratch_bytes = 0;
 };
 
 namespace cw {
@@ -128,5 +132,14 @@ int rope_table(cw_ctx* ctx, uint32_t head_dim, float theta, const float** out);
 
 // zeroed counters for the attention combine; grows on demand (syncs).
 int ensure_counters(cw_ctx* ctx, size_t n);
+
+// cw_gemm.cu: the tcgen05 prefill GEMM, Y[M,N] (=|+=) X[M,K] W[N,K]^T (+bias)
+// over split f16 operands (xh/xl [M,K], wh/wl [N,K]; see cw_gemm.cuh).
+int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const void* wl, int M,
+            int N, int K, float* y, int ldy, const float* bias, int epi);
+// Packed Q4_0 [rows, K] -> wh, wl; X f32 [M, K] (row stride ldx) -> xh, xl.
+int q4_split(cw_ctx* ctx, const void* payload, const void* scales, long rows, int K, void* wh,
+             void* wl);
+int x_split(cw_ctx* ctx, const float* x, long M, int K, int ldx, void* xh, void* xl);
 
 }  // namespace cw

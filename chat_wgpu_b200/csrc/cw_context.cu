@@ -251,6 +251,7 @@ int cw_ctx_destroy(cw_ctx* ctx) {
     for (auto e : ctx->event_pool) cudaEventDestroy(e);
     if (ctx->d_status) cudaFree(ctx->d_status);
     if (ctx->d_counters) cudaFree(ctx->d_counters);
+    if (ctx->gemm_scratch) cudaFree(ctx->gemm_scratch);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
     return CW_OK;

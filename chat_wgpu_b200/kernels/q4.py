@@ -40,6 +40,12 @@ def q4_0_gemv(ctx, x: Buffer, w: Buffer, in_f: int, out_f: int) -> Buffer:
     return op(ctx, "cw_q4_0_gemv", x.handle, w.handle, int(in_f), int(out_f))
 
 
+def q4_0_gemm(ctx, x: Buffer, w: Buffer, rows: int, in_f: int, out_f: int) -> Buffer:
+    """Y[rows, out_f] = X[rows, in_f] W^T over a packed Q4_0 weight on the
+    tcgen05 tensor cores (the batched prefill form of q4_0_gemv)."""
+    return op(ctx, "cw_q4_0_gemm", x.handle, w.handle, int(rows), int(in_f), int(out_f))
+
+
 def q4_0_dequant(ctx, w: Buffer, rows: int, in_f: int) -> Buffer:
     """Exact f32 dequantisation of a packed weight (dequant.rs:62-78)."""
     return op(ctx, "cw_q4_0_dequant", w.handle, int(rows), int(in_f))

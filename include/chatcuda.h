@@ -192,6 +192,16 @@ int cw_q4_0_upload(cw_ctx* ctx, const void* gguf_blocks, size_t rows, size_t in_
 int cw_q4_0_pack(cw_ctx* ctx, cw_buf gguf_blocks, size_t rows, size_t in_f, cw_buf* w);
 /* y[out_f] = W x over a packed Q4_0 weight (the decode GEMV). */
 int cw_q4_0_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out);
+/* Y[rows, out_f] = X[rows, in_f] W^T over a packed Q4_0 weight: the prefill
+ * GEMM on the tcgen05 tensor cores (TMA-staged tiles, TMEM accumulators).
+ * No counterpart in the reference, whose prompt runs one token at a time
+ * through q4::gemv (q4.rs:9-30, mod.rs:78-83); each output row equals that
+ * GEMV of the same x row within 1e-3 relative (f16 hi/lo operand split,
+ * three MMAs per K step, f32 accumulation).  X f32 row-major; the result is
+ * an arena buffer of rows*out_f f32.  Uses a context-owned scratch of
+ * 4*(rows + out_f)*in_f bytes (grown on demand, which synchronises). */
+int cw_q4_0_gemm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t in_f, size_t out_f,
+                 cw_buf* out);
 /* Exact f32 dequantisation of a packed weight (dequant.rs:62-78). */
 int cw_q4_0_dequant(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out);
 /* The microbenchmark of examples/q4bench.rs for the packed GEMV: `iters`
