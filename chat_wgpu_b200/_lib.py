@@ -104,6 +104,8 @@ SIGNATURES = {
     "cw_session_free": [_vp],
     "cw_session_begin": [_vp, _vp, _sz],
     "cw_session_run": [_vp, _sz, C.POINTER(_sz)],
+    "cw_session_prefill": [_vp, C.POINTER(_sz)],
+    "cw_session_read_kv": [_vp, C.c_uint32, _sz, _vp, _vp],
     "cw_session_tokens": [_vp, _vp, _sz, C.POINTER(_sz)],
     "cw_session_logits": [_vp, _vp, _sz],
     "cw_session_pos": [_vp, C.POINTER(_sz)],

@@ -1,6 +1,6 @@
-// cw_gemm.cu -- host side of the tcgen05 prefill GEMM (kernels in
-// cw_gemm.cuh): TMA tensor maps, operand splitting, launch, and the
-// cw_q4_0_gemm op.
+// cw_gemm.cu -- the tcgen05 prefill GEMM kernel (design notes and device
+// primitives in cw_gemm.cuh), the operand-split kernels, TMA tensor maps,
+// launch, and the cw_q4_0_gemm op.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -9,6 +9,199 @@
 #include "cw_gemm.cuh"
 
 namespace cw {
+
+__global__ void __launch_bounds__(192, 1)
+    k_gemm_x3(const __grid_constant__ CUtensorMap tXh, const __grid_constant__ CUtensorMap tXl,
+              const __grid_constant__ CUtensorMap tWh, const __grid_constant__ CUtensorMap tWl,
+              GemmArgs a) {
+    extern __shared__ uint8_t gm_raw[];
+    uint8_t* sm = (uint8_t*)(((uintptr_t)gm_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = (uint64_t*)(sm + (size_t)GM_ST * GM_STAGE);
+    uint64_t* empty = full + GM_ST;
+    uint64_t* done = empty + GM_ST;
+    uint32_t* tslot = (uint32_t*)(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tiles = (a.M + GM_BM - 1) / GM_BM, n_tiles = (a.N + GM_BN - 1) / GM_BN;
+    int mt, nt;
+    gm_tile(blockIdx.x, m_tiles, n_tiles, a.group_m, &mt, &nt);
+    const int m0 = mt * GM_BM, n0 = nt * GM_BN;
+    const int KB = (a.K + GM_BK - 1) / GM_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < GM_ST; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+        tma_prefetch_desc(&tXh);
+        tma_prefetch_desc(&tXl);
+        tma_prefetch_desc(&tWh);
+        tma_prefetch_desc(&tWl);
+    }
+    if (warp == 1) tmem_alloc(tslot, GM_TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            int kb = 0;
+            for (; kb < KB; kb++) {
+                const int s = kb % GM_ST;
+                if (kb >= GM_ST && !mbar_wait(&empty[s], ((kb / GM_ST) - 1) & 1, GM_WAIT_NS)) {
+                    gm_fail(a.status);
+                    break;
+                }
+                uint8_t* st = sm + (size_t)s * GM_STAGE;
+                mbar_expect_tx(&full[s], GM_STAGE);
+                const int kx = kb * GM_BK;
+                tma_load_2d(st, &tXh, kx, m0, &full[s]);
+                tma_load_2d(st + GM_TILE, &tXl, kx, m0, &full[s]);
+                tma_load_2d(st + 2 * GM_TILE, &tWh, kx, n0, &full[s]);
+                tma_load_2d(st + 3 * GM_TILE, &tWl, kx, n0, &full[s]);
+            }
+            // copies still in flight land before the CTA may exit
+            for (int j = max(0, kb - GM_ST); j < kb; j++)
+                if (!mbar_wait(&full[j % GM_ST], (j / GM_ST) & 1, GM_WAIT_NS)) gm_fail(a.status);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer
+            constexpr uint32_t idesc = umma_idesc_f16(GM_BM, GM_BN);
+            const uint32_t acc_hi = tmem, acc_lo = tmem + GM_BN;
+            for (int kb = 0; kb < KB; kb++) {
+                const int s = kb % GM_ST;
+                if (!mbar_wait(&full[s], (kb / GM_ST) & 1, GM_WAIT_NS)) {
+                    gm_fail(a.status);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t st = smem_addr(sm + (size_t)s * GM_STAGE);
+                const uint64_t dxh = umma_desc_sw128(st), dxl = umma_desc_sw128(st + GM_TILE);
+                const uint64_t dwh = umma_desc_sw128(st + 2 * GM_TILE),
+                               dwl = umma_desc_sw128(st + 3 * GM_TILE);
+#pragma unroll
+                for (int k = 0; k < GM_BK / 16; k++) {
+                    const uint64_t adv = (uint64_t)(k * 32) >> 4;  // 16 f16 = 32 bytes along K
+                    const uint32_t first = (kb > 0 || k > 0) ? 1u : 0u;
+                    umma_f16(acc_hi, dxh + adv, dwh + adv, idesc, first);
+                    umma_f16(acc_lo, dxh + adv, dwl + adv, idesc, first);
+                    umma_f16(acc_lo, dxl + adv, dwh + adv, idesc, 1u);
+                }
+                tc_commit(&empty[s]);  // stage reusable once these MMAs have read it
+            }
+            tc_commit(done);  // also on the error path: the drain waits for in-flight MMAs
+        }
+    } else {  // ---- epilogue: warps 2..5
+        const bool ok = mbar_wait(done, 0, GM_WAIT_NS);
+        if (!ok) gm_fail(a.status);
+        tc_fence_after();
+        const int q = warp & 3;
+        const int row = m0 + q * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+        for (int c = 0; c < GM_BN; c += 16) {
+            uint32_t h[16], l[16];
+            tmem_ld16(lane_base + c, h);
+            tmem_ld16(lane_base + GM_BN + c, l);
+            tmem_wait_ld();
+            if (!ok || row >= a.M) continue;
+            float* yr = a.y + (size_t)row * a.ldy;
+            const int nb = n0 + c;
+            if (nb + 16 <= a.N && (a.ldy & 3) == 0) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4) {
+                    float r[4];
+#pragma unroll
+                    for (int t = 0; t < 4; t++) {
+                        r[t] = __uint_as_float(h[j + t]) +
+                               __uint_as_float(l[j + t]) * (1.0f / GM_LO);
+                        if (a.bias) r[t] += a.bias[nb + j + t];
+                    }
+                    float4* dst = (float4*)(yr + nb + j);
+                    if (a.epi == GE_ADD) {
+                        const float4 o = *dst;
+                        r[0] += o.x;
+                        r[1] += o.y;
+                        r[2] += o.z;
+                        r[3] += o.w;
+                    }
+                    *dst = make_float4(r[0], r[1], r[2], r[3]);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    if (nb + j >= a.N) continue;
+                    float acc =
+                        __uint_as_float(h[j]) + __uint_as_float(l[j]) * (1.0f / GM_LO);
+                    if (a.bias) acc += a.bias[nb + j];
+                    if (a.epi == GE_ADD) acc += yr[nb + j];
+                    yr[nb + j] = acc;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, GM_TMEM_COLS);
+    }
+}
+
+// Packed Q4_0 [rows, K] -> Wh, Wl f16 [rows, K] (row-major, K contiguous).
+// One thread per 8 consecutive weights (one 16-byte chunk of each output).
+// GGUF block layout (dequant.rs:62-78): byte j holds weight j (low nibble)
+// and weight j+16 (high nibble); w = (q - 8) * d is exact in f32.
+__global__ void k_q4_split(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
+                           long rows, int K, __half* __restrict__ wh, __half* __restrict__ wl) {
+    const int nb = K / 32;
+    const long chunks = rows * (long)(K / 8);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < chunks;
+         i += (long)gridDim.x * blockDim.x) {
+        const long r = i / (K / 8);
+        const int c = (int)(i - r * (K / 8));
+        const int b = c >> 2, sub = c & 3;
+        const long blk = r * nb + b;
+        const float d = __half2float(scales[blk]);
+        const uint2 raw = *(const uint2*)(payload + blk * 16 + (sub & 1) * 8);
+        const uint32_t w2[2] = {raw.x, raw.y};
+        __align__(16) __half hv[8], lv[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            uint32_t byte = (w2[j >> 2] >> ((j & 3) * 8)) & 0xff;
+            int q = (sub < 2) ? (int)(byte & 0xf) : (int)(byte >> 4);
+            float w = __fmul_rn(d, (float)(q - 8));
+            __half h = __float2half_rn(w);
+            hv[j] = h;
+            lv[j] = __float2half_rn((w - __half2float(h)) * GM_LO);
+        }
+        const long o = r * (long)K + (long)c * 8;
+        *(uint4*)(wh + o) = *(const uint4*)hv;
+        *(uint4*)(wl + o) = *(const uint4*)lv;
+    }
+}
+
+// X f32 [M, K] (row stride ldx) -> Xh, Xl f16 [M, K].
+__global__ void k_x_split(const float* __restrict__ x, long M, int K, int ldx,
+                          __half* __restrict__ xh, __half* __restrict__ xl) {
+    const long n = M * (long)(K / 4);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        const long r = i / (K / 4);
+        const int c = (int)(i - r * (K / 4)) * 4;
+        const float4 v = *(const float4*)(x + r * ldx + c);
+        __align__(8) __half hv[4], lv[4];
+        split_f16(v.x, &hv[0], &lv[0]);
+        split_f16(v.y, &hv[1], &lv[1]);
+        split_f16(v.z, &hv[2], &lv[2]);
+        split_f16(v.w, &hv[3], &lv[3]);
+        *(uint2*)(xh + r * K + c) = *(const uint2*)hv;
+        *(uint2*)(xl + r * K + c) = *(const uint2*)lv;
+    }
+}
 
 static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -131,9 +324,16 @@ int cw_q4_0_gemm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t in_f, size
     CW_TRY(gemm_scratch(ctx, 2 * xbytes + 2 * wbytes, &sc));
     uint8_t *xh = sc, *xl = sc + xbytes, *wh = sc + 2 * xbytes, *wl = wh + wbytes;
     OpScope scope(ctx, "q4_gemm");
-    CW_TRY(x_split(ctx, (const float*)ex->ptr, (long)rows, (int)in_f, (int)in_f, xh, xl));
-    CW_TRY(q4_split(ctx, ew->ptr, (const char*)ew->ptr + ew->scale_off, (long)out_f, (int)in_f,
-                    wh, wl));
+    {
+        OpScope s1(ctx, "q4_gemm.split_x");
+        CW_TRY(x_split(ctx, (const float*)ex->ptr, (long)rows, (int)in_f, (int)in_f, xh, xl));
+    }
+    {
+        OpScope s2(ctx, "q4_gemm.split_w");
+        CW_TRY(q4_split(ctx, ew->ptr, (const char*)ew->ptr + ew->scale_off, (long)out_f,
+                        (int)in_f, wh, wl));
+    }
+    OpScope s3(ctx, "q4_gemm.mma");
     return gemm_x3(ctx, xh, xl, wh, wl, (int)rows, (int)out_f, (int)in_f, (float*)ey->ptr,
                    (int)out_f, nullptr, GE_STORE);
 }

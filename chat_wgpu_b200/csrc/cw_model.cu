@@ -972,6 +972,7 @@ int cw_session_free(cw_session* s) {
     }
     if (s->h_tok) cudaFreeHost(s->h_tok);
     if (s->h_tok_in) cudaFreeHost(s->h_tok_in);
+    if (s->pf_mem) cudaFree(s->pf_mem);
     delete s;
     return CW_OK;
 }
@@ -1029,6 +1030,33 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     s->n_prompt = n_prompt;
     s->n_produced = 0;
     return CW_OK;
+}
+
+int cw_session_prefill(cw_session* s, size_t* n_done) {
+    clear_error();
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_prefill: session is NULL");
+    CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_session_prefill: call cw_session_begin first");
+    cudaSetDevice(s->ctx->device);
+    CW_TRY(session_prefill(s, n_done));
+    return check_launch("session prefill");
+}
+
+int cw_session_read_kv(cw_session* s, uint32_t layer, size_t n_pos, float* k, float* v) {
+    clear_error();
+    CW_CHECK(s && k && v && layer < s->m->info.n_layers && n_pos <= s->max_seq,
+             CW_ERR_INVALID_ARG, "cw_session_read_kv: bad arguments");
+    cudaSetDevice(s->ctx->device);
+    const cw_model_info& I = s->m->info;
+    const size_t row = (size_t)I.head_dim * 4, per_head = s->max_seq * I.head_dim;
+    const size_t base = (size_t)layer * I.n_kv * per_head;
+    for (uint32_t g = 0; g < I.n_kv; g++) {
+        CW_CUDA(cudaMemcpyAsync(k + (size_t)g * n_pos * I.head_dim, s->kc + base + g * per_head,
+                                n_pos * row, cudaMemcpyDeviceToHost, s->ctx->stream));
+        CW_CUDA(cudaMemcpyAsync(v + (size_t)g * n_pos * I.head_dim, s->vc + base + g * per_head,
+                                n_pos * row, cudaMemcpyDeviceToHost, s->ctx->stream));
+    }
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    return check_device_status(s->ctx);
 }
 
 int cw_session_run(cw_session* s, size_t n_steps, size_t* n_produced) {

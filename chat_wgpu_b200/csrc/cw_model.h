@@ -80,6 +80,8 @@ struct cw_session {
     bool use_persistent = true;
     unsigned long long* bar = nullptr;  // [0] grid-barrier counter, [1] head counter (monotonic)
     float* opart = nullptr;             // per-head O-projection row sums (persistent step)
+    void* pf_mem = nullptr;             // batched-prefill scratch (cw_prefill.cu), grown on demand
+    size_t pf_bytes = 0;
 };
 
 namespace cw {
@@ -93,5 +95,9 @@ int step_variant(const cw_session* s);  // 0 or 1: which plan the next step uses
 void step_set_mode(cw_session* s, int mode);  // 1 auto, 2 split plan only, 3 fused plan only
 int step_profile(cw_session* s, size_t n_steps,
                  std::map<std::string, std::pair<uint32_t, double>>* agg);
+
+// cw_prefill.cu: prompt positions [host_pos, n_prompt - 1) in batched chunks
+// on the tensor cores; advances host_pos and the device state.
+int session_prefill(cw_session* s, size_t* n_done);
 
 }  // namespace cw

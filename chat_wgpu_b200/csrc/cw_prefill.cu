@@ -1,0 +1,389 @@
+// cw_prefill.cu -- batched prompt prefill: the prompt's rows go through each
+// layer together, with every projection on the tcgen05 tensor cores
+// (cw_gemm.cuh) instead of one Q4 GEMV per token.
+//
+// The reference runs the prompt one token at a time (src/model/mod.rs:78-83)
+// through the same layer composition as decode (src/model/qwen3.rs:139-191).
+// Prefill reproduces that composition over C rows at positions p0 .. p0+C-1:
+//
+//   embed      H[r]   = dequant(token_embd[prompt[p0+r]])          (qwen3.rs:128-133)
+//   per layer
+//     norm     X      = rmsnorm(H) (+ post-norm residual, gemma2)  (norm.wgsl:20-56)
+//     qkv      QKV    = X Wqkv^T (+bias)                            tcgen05 GEMM
+//     qk       QK-norm, RoPE at the row's position; K, V rows into the cache
+//     attn     causal attention of each row over cache positions <= its own
+//     o        H     += O Wo^T            (gemma2: T = O Wo^T, added post-normed)
+//     norm, gate/up GEMM, SwiGLU/GeGLU, down GEMM the same way
+//
+// The last layer stops after writing K and V: no later computation reads the
+// prefill rows' hidden states, because the final prompt token runs through
+// the decode step, which produces the first token's logits exactly as the
+// token-by-token loop does.  Activations feed the GEMMs as f16 hi/lo pairs
+// (cw_gemm.cuh); each weight matrix is split into its f16 pair once per
+// chunk, into a session scratch reused across layers.
+#include <stdlib.h>
+
+#include <algorithm>
+#include <cmath>
+#include <memory>
+
+#include "cw_attn.cuh"
+#include "cw_common.h"
+#include "cw_device.cuh"
+#include "cw_gemm.cuh"
+#include "cw_model.h"
+
+namespace cw {
+
+constexpr int PF_CHUNK = 4096;  // rows per prefill chunk (bounds the scratch)
+
+__device__ __forceinline__ float pf_block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; i++) t += red[i];
+    return t;
+}
+
+// Rows of token_embd for prompt[0 .. C), exact Q4_0 dequantisation.
+__global__ void k_pf_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
+                           int dim, float scale, const unsigned* __restrict__ toks,
+                           float* __restrict__ H) {
+    const int r = blockIdx.x, nb = dim / 32;
+    const unsigned tok = toks[r];
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const int b = i >> 5, j = i & 31;
+        const size_t blk = (size_t)tok * nb + b;
+        const float d = __half2float(scales[blk]);
+        const uint8_t byte = payload[blk * 16 + (j & 15)];
+        const int q = (j < 16) ? (byte & 0xf) : (byte >> 4);
+        const float v = __fmul_rn(d, (float)(q - 8));
+        H[(size_t)r * dim + i] = scale > 0.f ? __fmul_rn(v, scale) : v;
+    }
+}
+
+// Row r: h = H[r] (+ rmsnorm(T[r]) * gain(post_w), written back to H), then
+// X = rmsnorm(h) * gain(norm_w) as an f16 hi/lo pair.
+__global__ void __launch_bounds__(256) k_pf_norm(float* __restrict__ H, const float* __restrict__ T,
+                                                 const float* __restrict__ post_w,
+                                                 const float* __restrict__ norm_w, int unit,
+                                                 float eps, int dim, __half* __restrict__ xh,
+                                                 __half* __restrict__ xl) {
+    extern __shared__ float hb[];
+    __shared__ float red[32];
+    const size_t r0 = (size_t)blockIdx.x * dim;
+    float inv_d = 0.f;
+    if (T && post_w) {
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(T[r0 + i], T[r0 + i], ss);
+        ss = pf_block_sum(ss, red);
+        inv_d = 1.0f / sqrtf(ss / (float)dim + eps);
+    }
+    float ssh = 0.f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        float h = H[r0 + i];
+        if (T) {
+            float dv = T[r0 + i];
+            if (post_w) {
+                const float gw = unit ? 1.0f + post_w[i] : post_w[i];
+                dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
+            }
+            h = h + dv;
+            H[r0 + i] = h;
+        }
+        hb[i] = h;
+        ssh = fmaf(h, h, ssh);
+    }
+    ssh = pf_block_sum(ssh, red);
+    const float inv = 1.0f / sqrtf(ssh / (float)dim + eps);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float g = unit ? 1.0f + norm_w[i] : norm_w[i];
+        split_f16(__fmul_rn(__fmul_rn(hb[i], inv), g), xh + r0 + i, xl + r0 + i);
+    }
+}
+
+// Row r, one warp per head: QK-norm (qwen3.rs:154-155), RoPE at position
+// p0 + r (rope.wgsl:25-34); q back in place, k and v into the cache
+// (cache.rs:21-24, layout [n_kv][max_seq][hd]).
+__global__ void __launch_bounds__(256) k_pf_qk(float* __restrict__ QKV, int ld,
+                                               const float* __restrict__ q_norm,
+                                               const float* __restrict__ k_norm, float eps,
+                                               const float* __restrict__ inv_freq,
+                                               float* __restrict__ kc, float* __restrict__ vc,
+                                               int max_seq, int p0, int nh, int nkv, int hd) {
+    extern __shared__ float rb[];
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nw = blockDim.x >> 5, pos = p0 + r, half = hd / 2;
+    const int qd = nh * hd, kvd = nkv * hd;
+    float* row = QKV + (size_t)r * ld;
+    float* sb = rb + (size_t)warp * hd;
+    for (int h = warp; h < nh + nkv; h += nw) {
+        const bool isq = h < nh;
+        float* src = isq ? row + (size_t)h * hd : row + qd + (size_t)(h - nh) * hd;
+        const float* nwt = isq ? q_norm : k_norm;
+        float ss = 0.f;
+        for (int d = lane; d < hd; d += 32) {
+            const float v = src[d];
+            sb[d] = v;
+            ss = fmaf(v, v, ss);
+        }
+        __syncwarp();
+        if (nwt) {
+            ss = warp_sum(ss);
+            const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+            for (int d = lane; d < hd; d += 32) sb[d] = __fmul_rn(__fmul_rn(sb[d], inv), nwt[d]);
+            __syncwarp();
+        }
+        float* dst = isq ? src : kc + ((size_t)(h - nh) * max_seq + pos) * hd;
+        for (int k = lane; k < half; k += 32) {
+            const float freq = __fmul_rn((float)pos, inv_freq[k]);
+            float sn, cs;
+            sincosf(freq, &sn, &cs);
+            const float lo = sb[k], hi = sb[k + half];
+            dst[k] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
+            dst[k + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+        }
+        __syncwarp();
+    }
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
+        const int g = i / hd, d = i - g * hd;
+        vc[((size_t)g * max_seq + pos) * hd + d] = row[qd + kvd + i];
+    }
+}
+
+// Row r, kv head g: the G query heads of the group attend over cache
+// positions [j0, p0 + r] (attention.wgsl:33-95 via attn_core; sliding window
+// and soft-cap as in decode); the output goes out as an f16 hi/lo pair.
+template <int EPL, int GMAX>
+__global__ void __launch_bounds__(128) k_pf_attn(const float* __restrict__ QKV, int ld,
+                                                 const float* __restrict__ kc,
+                                                 const float* __restrict__ vc, int max_seq, int p0,
+                                                 int nh, int nkv, int hd, int window, float scale,
+                                                 float softcap, __half* __restrict__ xh,
+                                                 __half* __restrict__ xl) {
+    extern __shared__ float sm[];
+    const int r = blockIdx.x, g = blockIdx.y, G = nh / nkv, W = hd + 2;
+    const int seq = p0 + r + 1;
+    float* qs = sm + attn_smem_floats(G, hd, 1);
+    const float* qsrc = QKV + (size_t)r * ld + (size_t)g * G * hd;
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = qsrc[i];
+    __syncthreads();
+    int jlo, jhi;
+    attn_range(seq, window, 0, 1, &jlo, &jhi);
+    float* res = sm + 4 * G * W;
+    attn_core<EPL, GMAX, KV_NC>(qs, G, hd, kc + (size_t)g * max_seq * hd,
+                                vc + (size_t)g * max_seq * hd, hd, jlo, jhi, scale, softcap, sm,
+                                res);
+    const size_t o0 = (size_t)r * nh * hd + (size_t)g * G * hd;
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int gi = i / hd, d = i - gi * hd;
+        const float o = res[gi * W + d] * (1.0f / res[gi * W + hd + 1]);
+        split_f16(o, xh + o0 + i, xl + o0 + i);
+    }
+}
+
+// act = silu(gate) * up or gelu(gate) * up (glu.wgsl:15-32) over the
+// interleaved gate/up GEMM output (column 2i gate_i, 2i+1 up_i).
+__global__ void k_pf_glu(const float* __restrict__ Gm, int I, int geglu, long rows,
+                         __half* __restrict__ xh, __half* __restrict__ xl) {
+    const long n = rows * (long)I;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        const long r = i / I, c = i - r * I;
+        const float2 gu = *reinterpret_cast<const float2*>(Gm + r * 2 * I + 2 * c);
+        const float act = geglu ? gelu_ref_f(gu.x) : silu_ref_f(gu.x);
+        split_f16(act * gu.y, xh + i, xl + i);
+    }
+}
+
+// After the chunk: the next step reads prompt[p_next] at p_next.
+__global__ void k_pf_done(DevState* st, const unsigned* __restrict__ prompt, int p_next) {
+    st->pos = p_next;
+    st->token = prompt[p_next];
+}
+
+// ===========================================================================
+// host
+// ===========================================================================
+namespace {
+
+struct PfLayout {
+    size_t H, T, QKV, G, xh, xl, wh, wl, total;
+};
+
+size_t al256(size_t v) { return (v + 255) / 256 * 256; }
+
+PfLayout pf_layout(const cw_model* m, size_t C) {
+    const cw_model_info& I = m->info;
+    const size_t qd = (size_t)I.n_heads * I.head_dim, kvd = (size_t)I.n_kv * I.head_dim;
+    const size_t qkv = qd + 2 * kvd;
+    const size_t xk = std::max({(size_t)I.dim, qd, (size_t)I.hidden});
+    const size_t wmax =
+        std::max({qkv * I.dim, (size_t)I.dim * qd, 2 * (size_t)I.hidden * I.dim,
+                  (size_t)I.dim * I.hidden});
+    PfLayout L{};
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        size_t at = o;
+        o += al256(bytes);
+        return at;
+    };
+    L.H = take(C * I.dim * 4);
+    L.T = take(I.post_norms ? C * I.dim * 4 : 0);
+    L.QKV = take(C * qkv * 4);
+    L.G = take(C * 2 * (size_t)I.hidden * 4);
+    L.xh = take(C * xk * 2);
+    L.xl = take(C * xk * 2);
+    L.wh = take(wmax * 2);
+    L.wl = take(wmax * 2);
+    L.total = o;
+    return L;
+}
+
+template <int EPL, int GM>
+int pf_attn_go(cw_ctx* ctx, dim3 grid, size_t smem, const float* QKV, int ld, const float* kc,
+               const float* vc, int max_seq, int p0, int nh, int nkv, int hd, int window,
+               float scale, float softcap, void* xh, void* xl) {
+    if (smem > 48 * 1024)
+        CW_CUDA(cudaFuncSetAttribute(k_pf_attn<EPL, GM>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    k_pf_attn<EPL, GM><<<grid, 128, smem, ctx->stream>>>(QKV, ld, kc, vc, max_seq, p0, nh, nkv, hd,
+                                                          window, scale, softcap, (__half*)xh,
+                                                          (__half*)xl);
+    return check_launch("prefill attention");
+}
+
+template <int EPL>
+int pf_attn_e(cw_ctx* ctx, int G, dim3 grid, size_t smem, const float* QKV, int ld,
+              const float* kc, const float* vc, int max_seq, int p0, int nh, int nkv, int hd,
+              int window, float scale, float softcap, void* xh, void* xl) {
+#define CW_PFA(GM)                                                                              \
+    return pf_attn_go<EPL, GM>(ctx, grid, smem, QKV, ld, kc, vc, max_seq, p0, nh, nkv, hd, window, \
+                               scale, softcap, xh, xl)
+    if (G <= 1) CW_PFA(1);
+    if (G <= 2) CW_PFA(2);
+    if (G <= 4) CW_PFA(4);
+    CW_PFA(8);
+#undef CW_PFA
+}
+
+int pf_chunk(cw_session* s, int p0, int C) {
+    cw_model* m = s->m;
+    cw_ctx* ctx = s->ctx;
+    const cw_model_info& I = m->info;
+    const int dim = (int)I.dim, nh = (int)I.n_heads, nkv = (int)I.n_kv, hd = (int)I.head_dim;
+    const int qd = nh * hd, kvd = nkv * hd, qkv_rows = qd + 2 * kvd, hid = (int)I.hidden;
+    const bool post = I.post_norms != 0;
+    const int unit = I.norm_kind == 1;
+    const PfLayout L = pf_layout(m, (size_t)C);
+    uint8_t* b = (uint8_t*)s->pf_mem;
+    float* H = (float*)(b + L.H);
+    float* T = (float*)(b + L.T);
+    float* QKV = (float*)(b + L.QKV);
+    float* Gm = (float*)(b + L.G);
+    void *xh = b + L.xh, *xl = b + L.xl, *wh = b + L.wh, *wl = b + L.wl;
+
+    std::unique_ptr<OpScope> sc;
+    auto stage = [&](const char* name) {
+        sc.reset();
+        if (ctx->profiling) sc.reset(new OpScope(ctx, name));
+    };
+    auto gemm = [&](const QW& w, int K, int N, float* y, const float* bias, int epi) {
+        stage("prefill.split_w");
+        CW_TRY(q4_split(ctx, w.payload, w.scales, N, K, wh, wl));
+        stage("prefill.gemm");
+        return gemm_x3(ctx, xh, xl, wh, wl, C, N, K, y, N, bias, epi);
+    };
+    const int ew_grid = std::max(1, std::min(C * 8, ctx->sm_count * 8));
+
+    stage("prefill.embed");
+    k_pf_embed<<<C, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, dim, I.embed_scale,
+                                           s->prompt + p0, H);
+    CW_TRY(check_launch("prefill embed"));
+    for (uint32_t li = 0; li < I.n_layers; li++) {
+        const Layer& l = m->L[li];
+        float* kc = s->kc + (size_t)li * nkv * s->max_seq * hd;
+        float* vc = s->vc + (size_t)li * nkv * s->max_seq * hd;
+        const bool pre_t = post && li > 0;  // previous layer's FFN output, post-normed in
+        stage("prefill.norm");
+        k_pf_norm<<<C, 256, dim * 4, ctx->stream>>>(H, pre_t ? T : nullptr,
+                                                    pre_t ? m->L[li - 1].post_ffw : nullptr,
+                                                    l.attn_norm, unit, I.eps, dim, (__half*)xh,
+                                                    (__half*)xl);
+        CW_TRY(check_launch("prefill norm"));
+        CW_TRY(gemm(l.qkv, dim, qkv_rows, QKV, l.qkv_bias, GE_STORE));
+        stage("prefill.qk");
+        k_pf_qk<<<C, 256, 8 * hd * 4, ctx->stream>>>(QKV, qkv_rows, l.q_norm, l.k_norm, I.eps,
+                                                      m->inv_freq, kc, vc, (int)s->max_seq, p0,
+                                                      nh, nkv, hd);
+        CW_TRY(check_launch("prefill qk"));
+        if (li + 1 == I.n_layers) break;  // only the K/V rows of the last layer are read later
+
+        stage("prefill.attn");
+        const int G = nh / nkv, epl = (hd + 31) / 32;
+        const size_t smem = (attn_smem_floats(G, hd, 1) + (size_t)G * hd) * sizeof(float);
+        const int window = (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
+        const float scale = powf((float)hd, -0.5f);  // attention.rs:18
+        dim3 grid(C, nkv);
+#define CW_PFE(E)                                                                              \
+    CW_TRY(pf_attn_e<E>(ctx, G, grid, smem, QKV, qkv_rows, kc, vc, (int)s->max_seq, p0, nh, nkv, \
+                        hd, window, scale, I.attn_softcap, xh, xl))
+        if (epl <= 1) CW_PFE(1);
+        else if (epl <= 2) CW_PFE(2);
+        else if (epl <= 4) CW_PFE(4);
+        else CW_PFE(8);
+#undef CW_PFE
+        CW_TRY(gemm(l.wo, qd, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
+
+        stage("prefill.norm");
+        k_pf_norm<<<C, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
+                                                    post ? l.post_attn : nullptr, l.ffn_norm, unit,
+                                                    I.eps, dim, (__half*)xh, (__half*)xl);
+        CW_TRY(check_launch("prefill norm"));
+        CW_TRY(gemm(l.gate_up, dim, 2 * hid, Gm, nullptr, GE_STORE));
+        stage("prefill.glu");
+        k_pf_glu<<<ew_grid, 256, 0, ctx->stream>>>(Gm, hid, I.activation == 1, C, (__half*)xh,
+                                                    (__half*)xl);
+        CW_TRY(check_launch("prefill glu"));
+        CW_TRY(gemm(l.down, hid, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
+    }
+    stage("prefill.done");
+    k_pf_done<<<1, 1, 0, ctx->stream>>>(s->st, s->prompt, p0 + C);
+    sc.reset();
+    return check_launch("prefill done");
+}
+
+}  // namespace
+
+int session_prefill(cw_session* s, size_t* n_done) {
+    const size_t end = s->n_prompt - 1;  // the last prompt token runs through the decode step
+    size_t done = 0;
+    if (s->host_pos < end) {
+        size_t chunk = PF_CHUNK;
+        if (const char* e = getenv("CW_PREFILL_CHUNK"))  // smaller chunks (tests of the chunk seams)
+            chunk = std::max(1, std::min(atoi(e), PF_CHUNK));
+        const size_t C = std::min<size_t>(end - s->host_pos, chunk);
+        const PfLayout L = pf_layout(s->m, C);
+        if (s->pf_bytes < L.total) {
+            CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+            if (s->pf_mem) cudaFree(s->pf_mem);
+            s->pf_mem = nullptr;
+            s->pf_bytes = 0;
+            CW_CUDA(cudaMalloc(&s->pf_mem, L.total));
+            s->pf_bytes = L.total;
+        }
+        while (s->host_pos < end) {
+            const int c = (int)std::min<size_t>(end - s->host_pos, C);
+            CW_TRY(pf_chunk(s, (int)s->host_pos, c));
+            s->host_pos += c;
+            done += c;
+        }
+    }
+    if (n_done) *n_done = done;
+    return CW_OK;
+}
+
+}  // namespace cw

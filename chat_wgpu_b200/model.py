@@ -112,6 +112,22 @@ class Session:
         _lib.call("cw_session_run", self._h, int(n_steps), C.byref(n))
         return int(n.value)
 
+    def prefill(self) -> int:
+        """Run the remaining prompt positions but the last as one batch on the
+        tensor cores (cw_session_prefill); returns the positions processed."""
+        n = C.c_size_t()
+        _lib.call("cw_session_prefill", self._h, C.byref(n))
+        return n.value
+
+    def read_kv(self, layer: int, n_pos: int) -> tuple[np.ndarray, np.ndarray]:
+        """K and V cache rows [0, n_pos) of `layer`, each [n_kv, n_pos, head_dim]."""
+        I = self.model.info
+        k = np.empty((I["n_kv"], n_pos, I["head_dim"]), np.float32)
+        v = np.empty_like(k)
+        _lib.call("cw_session_read_kv", self._h, int(layer), int(n_pos), k.ctypes.data,
+                  v.ctypes.data)
+        return k, v
+
     def tokens(self) -> np.ndarray:
         out = np.zeros(self.max_seq, dtype=np.uint32)
         n = C.c_size_t()

@@ -244,6 +244,18 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt);
  * positions skip the lm_head, whose logits the reference discards
  * (mod.rs:78-81).  Returns the number of tokens produced by these steps. */
 int cw_session_run(cw_session* s, size_t n_steps, size_t* n_produced);
+/* Batched prefill: run prompt positions [pos, n_prompt - 1) together, the
+ * projections as tcgen05 tensor-core GEMMs over the Q4_0 weights (chunks of
+ * up to 4096 rows), filling the KV cache exactly where the token-by-token
+ * steps would (within 1e-3 relative).  The last prompt token is left for the
+ * next cw_session_run/step, which produces the first token as before.  No
+ * counterpart in the reference (its prompt runs through forward() one token
+ * at a time, mod.rs:78-83).  Allocates a session scratch on first use.
+ * *n_done (may be NULL) = positions processed. */
+int cw_session_prefill(cw_session* s, size_t* n_done);
+/* Copy the K and V cache rows [0, n_pos) of `layer` to the host, each laid
+ * out [n_kv][n_pos][head_dim] f32 (cache.rs:7-31 holds the same values). */
+int cw_session_read_kv(cw_session* s, uint32_t layer, size_t n_pos, float* k, float* v);
 /* Tokens produced so far (<= cap). */
 int cw_session_tokens(cw_session* s, uint32_t* out, size_t cap, size_t* n);
 /* Logits of the last produced token (vocab floats) and the position count. */
