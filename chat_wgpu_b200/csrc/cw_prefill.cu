@@ -185,6 +185,184 @@ __global__ void __launch_bounds__(128) k_pf_attn(const float* __restrict__ QKV, 
     }
 }
 
+// Tiled causal attention for head_dim HD in {64, 128, 256}: a CTA takes 64
+// consecutive query rows of one head and streams the kv head's cache rows
+// through shared memory 32 keys at a time, so every K/V row read serves 64
+// queries (k_pf_attn above re-reads them per query).  Same f32 arithmetic
+// as the decode path (attention.wgsl:33-95): scores q.k * scale (soft-capped),
+// an online softmax per query row with running max and denominator, keys
+// limited to [pos - window + 1, pos] on windowed layers.
+// Thread (tr, tc) = (tid / 16, tid % 16) owns query rows tr + 16i (i < 4),
+// score columns tc + 16j (j < 2) and output dims 4tc + 64jj .. +3; the 16
+// threads of a row form a half-warp, which reduces the row max and sum.
+constexpr int PFA_BQ = 64, PFA_BK = 32;
+
+__host__ __device__ constexpr size_t pfa_smem(int hd) {
+    return ((size_t)PFA_BQ * (hd + 4) + (size_t)PFA_BK * (hd + 4) + (size_t)PFA_BK * hd +
+            (size_t)PFA_BQ * (PFA_BK + 1)) *
+           sizeof(float);
+}
+
+__device__ __forceinline__ float hw_max(float v) {  // over the 16 lanes of a half-warp
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+}
+__device__ __forceinline__ float hw_sum(float v) {
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    return v + __shfl_xor_sync(0xffffffffu, v, 1);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_pf_fattn(const float* __restrict__ QKV, int ld,
+                                                  const float* __restrict__ kc,
+                                                  const float* __restrict__ vc, int max_seq,
+                                                  int p0, int C, int nh, int nkv, int window,
+                                                  float scale, float softcap,
+                                                  __half* __restrict__ xh,
+                                                  __half* __restrict__ xl) {
+    constexpr int BQ = PFA_BQ, BK = PFA_BK, QS = HD + 4, NJ = HD / 64, PS = BK + 1;
+    extern __shared__ __align__(16) float pfa[];
+    float* Qs = pfa;             // [BQ][QS]
+    float* Ks = Qs + BQ * QS;    // [BK][QS]
+    float* Vs = Ks + BK * QS;    // [BK][HD]
+    float* Ps = Vs + BK * HD;    // [BQ][PS]
+    const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+    // longest rows (latest positions) first: the causal work grows with the row
+    const int r0 = (gridDim.x - 1 - blockIdx.x) * BQ;
+    const int h = blockIdx.y, g = h / (nh / nkv);
+    const int nrows = min(BQ, C - r0);
+    for (int i = tid; i < BQ * (HD / 4); i += blockDim.x) {
+        const int r = i / (HD / 4), c4 = i - r * (HD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nrows) v = *reinterpret_cast<const float4*>(QKV + (size_t)(r0 + r) * ld +
+                                                            (size_t)h * HD + 4 * c4);
+        *reinterpret_cast<float4*>(Qs + r * QS + 4 * c4) = v;
+    }
+    const int pos_first = p0 + r0, j_end = p0 + r0 + nrows;  // keys [j_begin, j_end)
+    const int j_begin = window > 0 ? max(0, pos_first - window + 1) : 0;
+    int pos[4];
+    float m[4], l[4];
+    float4 acc[4][NJ];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        pos[i] = pos_first + tr + 16 * i;
+        m[i] = REF_NEG_INF;
+        l[i] = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < NJ; jj++) acc[i][jj] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float* kb = kc + (size_t)g * max_seq * HD;
+    const float* vb = vc + (size_t)g * max_seq * HD;
+    for (int kt = j_begin; kt < j_end; kt += BK) {
+        __syncthreads();  // previous tile's K, V, P consumed (and Q stored, first time)
+        for (int i = tid; i < BK * (HD / 4); i += blockDim.x) {
+            const int r = i / (HD / 4), c4 = i - r * (HD / 4);
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (kt + r < j_end) {
+                kv = __ldg(reinterpret_cast<const float4*>(kb + (size_t)(kt + r) * HD) + c4);
+                vv = __ldg(reinterpret_cast<const float4*>(vb + (size_t)(kt + r) * HD) + c4);
+            }
+            *reinterpret_cast<float4*>(Ks + r * QS + 4 * c4) = kv;
+            *reinterpret_cast<float4*>(Vs + r * HD + 4 * c4) = vv;
+        }
+        __syncthreads();
+        float s[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) s[i][0] = s[i][1] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < HD; d += 4) {
+            float4 k4[2], q4[4];
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+                k4[j] = *reinterpret_cast<const float4*>(Ks + (tc + 16 * j) * QS + d);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                q4[i] = *reinterpret_cast<const float4*>(Qs + (tr + 16 * i) * QS + d);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    float t = s[i][j];
+                    t = fmaf(q4[i].x, k4[j].x, t);
+                    t = fmaf(q4[i].y, k4[j].y, t);
+                    t = fmaf(q4[i].z, k4[j].z, t);
+                    t = fmaf(q4[i].w, k4[j].w, t);
+                    s[i][j] = t;
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float mx = REF_NEG_INF;
+            bool ok[2];
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int key = kt + tc + 16 * j;
+                ok[j] = key <= pos[i] && key < j_end && (window <= 0 || key > pos[i] - window);
+                float v = s[i][j] * scale;
+                if (softcap > 0.f) v = softcap * tanhf(v / softcap);
+                s[i][j] = v;
+                if (ok[j]) mx = fmaxf(mx, v);
+            }
+            mx = hw_max(mx);
+            const float mn = fmaxf(m[i], mx);
+            const float corr = expf(m[i] - mn);
+            float ps = 0.f;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float p = ok[j] ? expf(s[i][j] - mn) : 0.f;
+                Ps[(tr + 16 * i) * PS + tc + 16 * j] = p;
+                ps += p;
+            }
+            l[i] = l[i] * corr + hw_sum(ps);
+            m[i] = mn;
+#pragma unroll
+            for (int jj = 0; jj < NJ; jj++) {
+                acc[i][jj].x *= corr;
+                acc[i][jj].y *= corr;
+                acc[i][jj].z *= corr;
+                acc[i][jj].w *= corr;
+            }
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int c = 0; c < BK; c++) {
+            float p[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) p[i] = Ps[(tr + 16 * i) * PS + c];
+#pragma unroll
+            for (int jj = 0; jj < NJ; jj++) {
+                const float4 v = *reinterpret_cast<const float4*>(Vs + c * HD + 4 * tc + 64 * jj);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    acc[i][jj].x = fmaf(v.x, p[i], acc[i][jj].x);
+                    acc[i][jj].y = fmaf(v.y, p[i], acc[i][jj].y);
+                    acc[i][jj].z = fmaf(v.z, p[i], acc[i][jj].z);
+                    acc[i][jj].w = fmaf(v.w, p[i], acc[i][jj].w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = tr + 16 * i;
+        if (r >= nrows) continue;
+        const float inv = 1.0f / l[i];
+        const size_t o = (size_t)(r0 + r) * nh * HD + (size_t)h * HD + 4 * tc;
+#pragma unroll
+        for (int jj = 0; jj < NJ; jj++) {
+            const size_t oj = o + 64 * jj;
+            split_f16(acc[i][jj].x * inv, xh + oj + 0, xl + oj + 0);
+            split_f16(acc[i][jj].y * inv, xh + oj + 1, xl + oj + 1);
+            split_f16(acc[i][jj].z * inv, xh + oj + 2, xl + oj + 2);
+            split_f16(acc[i][jj].w * inv, xh + oj + 3, xl + oj + 3);
+        }
+    }
+}
+
 // act = silu(gate) * up or gelu(gate) * up (glu.wgsl:15-32) over the
 // interleaved gate/up GEMM output (column 2i gate_i, 2i+1 up_i).
 __global__ void k_pf_glu(const float* __restrict__ Gm, int I, int geglu, long rows,
@@ -270,6 +448,34 @@ int pf_attn_e(cw_ctx* ctx, int G, dim3 grid, size_t smem, const float* QKV, int 
 #undef CW_PFA
 }
 
+template <int HD>
+int pf_fattn_go(cw_ctx* ctx, int C, const float* QKV, int ld, const float* kc, const float* vc,
+                int max_seq, int p0, int nh, int nkv, int window, float scale, float softcap,
+                void* xh, void* xl) {
+    const size_t smem = pfa_smem(HD);
+    if (smem > 48 * 1024)
+        CW_CUDA(cudaFuncSetAttribute(k_pf_fattn<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+    dim3 grid((C + PFA_BQ - 1) / PFA_BQ, nh);
+    k_pf_fattn<HD><<<grid, 256, smem, ctx->stream>>>(QKV, ld, kc, vc, max_seq, p0, C, nh, nkv,
+                                                     window, scale, softcap, (__half*)xh,
+                                                     (__half*)xl);
+    return check_launch("prefill tiled attention");
+}
+
+int pf_fattn(cw_ctx* ctx, int hd, int C, const float* QKV, int ld, const float* kc,
+             const float* vc, int max_seq, int p0, int nh, int nkv, int window, float scale,
+             float softcap, void* xh, void* xl) {
+    if (hd == 64)
+        return pf_fattn_go<64>(ctx, C, QKV, ld, kc, vc, max_seq, p0, nh, nkv, window, scale,
+                               softcap, xh, xl);
+    if (hd == 128)
+        return pf_fattn_go<128>(ctx, C, QKV, ld, kc, vc, max_seq, p0, nh, nkv, window, scale,
+                                softcap, xh, xl);
+    return pf_fattn_go<256>(ctx, C, QKV, ld, kc, vc, max_seq, p0, nh, nkv, window, scale, softcap,
+                            xh, xl);
+}
+
 int pf_chunk(cw_session* s, int p0, int C) {
     cw_model* m = s->m;
     cw_ctx* ctx = s->ctx;
@@ -323,19 +529,24 @@ int pf_chunk(cw_session* s, int p0, int C) {
         if (li + 1 == I.n_layers) break;  // only the K/V rows of the last layer are read later
 
         stage("prefill.attn");
-        const int G = nh / nkv, epl = (hd + 31) / 32;
-        const size_t smem = (attn_smem_floats(G, hd, 1) + (size_t)G * hd) * sizeof(float);
         const int window = (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
         const float scale = powf((float)hd, -0.5f);  // attention.rs:18
-        dim3 grid(C, nkv);
+        if (hd == 64 || hd == 128 || hd == 256) {
+            CW_TRY(pf_fattn(ctx, hd, C, QKV, qkv_rows, kc, vc, (int)s->max_seq, p0, nh, nkv,
+                            window, scale, I.attn_softcap, xh, xl));
+        } else {  // other head sizes: one CTA per (row, kv head)
+            const int G = nh / nkv, epl = (hd + 31) / 32;
+            const size_t smem = (attn_smem_floats(G, hd, 1) + (size_t)G * hd) * sizeof(float);
+            dim3 grid(C, nkv);
 #define CW_PFE(E)                                                                              \
     CW_TRY(pf_attn_e<E>(ctx, G, grid, smem, QKV, qkv_rows, kc, vc, (int)s->max_seq, p0, nh, nkv, \
                         hd, window, scale, I.attn_softcap, xh, xl))
-        if (epl <= 1) CW_PFE(1);
-        else if (epl <= 2) CW_PFE(2);
-        else if (epl <= 4) CW_PFE(4);
-        else CW_PFE(8);
+            if (epl <= 1) CW_PFE(1);
+            else if (epl <= 2) CW_PFE(2);
+            else if (epl <= 4) CW_PFE(4);
+            else CW_PFE(8);
 #undef CW_PFE
+        }
         CW_TRY(gemm(l.wo, qd, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
 
         stage("prefill.norm");
