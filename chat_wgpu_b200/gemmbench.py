@@ -8,6 +8,7 @@ token GEMVs would form); the kernel itself issues three f16 MMAs per K step
 
     python -m chat_wgpu_b200.gemmbench                # BASELINE prefill sweep, M = 128, 512
     python -m chat_wgpu_b200.gemmbench --rows 4096 --json
+    python -m chat_wgpu_b200.gemmbench --rows 4096 --shape 4096 12288 --iters 2
 """
 from __future__ import annotations
 
@@ -55,12 +56,15 @@ def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--rows", type=int, nargs="*", default=[128, 512])
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--shape", type=int, nargs=2, metavar=("K", "N"),
+                    help="one (in_f, out_f) shape instead of the sweep")
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args()
+    shapes = [tuple(a.shape)] if a.shape else SHAPES
     ctx = GpuContext(0)
     out = []
     for rows in a.rows:
-        for in_f, out_f in SHAPES:
+        for in_f, out_f in shapes:
             r = bench(ctx, rows, in_f, out_f, a.iters)
             out.append(r)
             if not a.json:
