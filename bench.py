@@ -179,12 +179,20 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# DRAM bytes (read + write) per launch of the dominant kernel from one ncu
+# capture of this bench's workload (profiles/decode_step_persistent_qwen3_0.6b.md:
+# dram throughput x duration of the decode launch at position 130).
+NCU_TRAFFIC = {("qwen3-0.6b", "decode_step"): 370.6e6}
+NCU_TRAFFIC_SRC = "ncu, one decode_step launch at position 130 (profiles/decode_step_persistent_qwen3_0.6b.md)"
+
+
 def measured_peaks() -> dict:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
 # ---------------------------------------------------------------- bytes model
@@ -226,8 +234,11 @@ def launch_bytes(info: dict, pos: float) -> dict:
 
 
 # ---------------------------------------------------------------- CPU legs
-def oracle_decode_rate(path: str, prompt, n_decode: int, threads: int | None = None):
-    """Oracle port: tokens/s of n_decode decode steps after the prompt."""
+def oracle_decode_rate(path: str, prompt, n_decode: int, threads: int | None = None,
+                       budget_s: float | None = None):
+    """Oracle port: tokens/s of n_decode decode steps after the prompt (at
+    most; with budget_s the timed loop also stops once that much time has
+    passed, after at least 4 steps)."""
     from oracle import oracle as orc
     if threads:
         orc.set_threads(threads)
@@ -239,14 +250,18 @@ def oracle_decode_rate(path: str, prompt, n_decode: int, threads: int | None = N
         tok = int(prompt[pos + 1])
     t0 = time.perf_counter()
     pos = len(prompt) - 1
+    done = 0
     for _ in range(n_decode):
         _, logits = m.step(tok, pos, want_logits=True)
         tok = orc.argmax(logits)
         pos += 1
+        done += 1
+        if budget_s is not None and done >= 4 and time.perf_counter() - t0 > budget_s:
+            break
     dt = time.perf_counter() - t0
     cores = orc.get_threads()
     m.close()
-    return n_decode / dt, dt, cores
+    return done / dt, dt, cores, done
 
 
 def run_reference(args, dist):
@@ -355,6 +370,37 @@ def run_cuda(args, dist):
                  "launches_per_step": so.launches()[1]}
         so.close()
 
+    # ---- batched prefill of the same prompt (tcgen05 GEMMs), device time from
+    # the context profiler's event pairs around each prefill launch
+    prefill = None
+    if P > 1:
+        from chat_wgpu_b200.prefillprof import gemm_flops_per_row
+        s3 = Session(model, max_seq)
+        s3.begin(prompt)
+        s3.prefill()                 # warm-up: scratch, tensor maps
+        ctx.sync()
+        reps = 3
+        ctx.begin_profile()
+        for _ in range(reps):
+            s3.begin(prompt)
+            s3.prefill()
+        agg = {}
+        for name, count, t in ctx.report_profile():
+            if name.startswith("prefill."):
+                agg[name] = agg.get(name, 0.0) + t
+        s3.close()
+        pf_ms = sum(agg.values()) / reps
+        gemm_ms = agg.get("prefill.gemm", float("nan")) / reps
+        fl = gemm_flops_per_row(info) * (P - 1)
+        pk = measured_peaks()
+        prefill = {"positions": P - 1, "ms": pf_ms, "tok_s": (P - 1) / pf_ms * 1e3,
+                   "gemm_ms": gemm_ms, "gemm_tflops": fl / gemm_ms / 1e9,
+                   "gemm_pipe_tflops": 3 * fl / gemm_ms / 1e9,
+                   "gemm_pipe_frac": 3 * fl / gemm_ms / 1e9 / pk["bf16_tflops"],
+                   "stage_ms": {k: round(v / reps, 4) for k, v in agg.items()},
+                   "note": "GEMMs issue three f16 MMAs per K step (hi/lo operand split); "
+                           "pipe_frac is against measured burst bf16 TFLOP/s"}
+
     # ---- e2e: public per-token API with host round trips
     s2 = Session(model, max_seq)
     s2.begin(prompt)
@@ -405,19 +451,25 @@ def run_cuda(args, dist):
         "other_path": other,
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                     "traffic": None, "peak_src": peaks["src"],
+                     "traffic": NCU_TRAFFIC.get((args.model, dom_name)),
+                     "traffic_src": NCU_TRAFFIC_SRC if (args.model, dom_name) in NCU_TRAFFIC
+                     else None,
+                     "peak_src": peaks["src"],
                      "bytes_per_launch": int(dom_bytes)},
         "step_roofline": {"bytes_per_step": int(sb), "achieved_gbs": step_gbs,
                           "frac": step_gbs / peaks["hbm_gbs"],
                           "roofline_tok_s": peaks["hbm_gbs"] * 1e9 / sb},
         "kernels": per_kernel,
+        "prefill": prefill,
         "clocks": clocks,
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        rate, dt, cores = oracle_decode_rate(path, prompt[:4], 6)
+        rate, dt, cores, n = oracle_decode_rate(path, prompt, 1024, budget_s=10.0)
         line["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": cores, "kind": "port",
-                                "sample": f"6 decode steps after a 4-token prompt of {args.model} "
-                                          f"({dt:.1f} s), oracle port on {cores} host threads"}
+                                "sample": f"{n} decode steps at positions {P - 1}..{P - 2 + n} "
+                                          f"after the same {P}-token prompt of {args.model} "
+                                          f"({dt:.1f} s timed), oracle port on {cores} host "
+                                          f"threads"}
     model.close()
     ctx.close()
     if dist.rank == 0:
