@@ -344,6 +344,7 @@ __global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n
     st->bar_base = bar[0];  // the persistent step's counters continue from here
     st->ctr_base = bar[1];
     st->done = 0;
+    st->stopped = 0;
 }
 
 // ===========================================================================
@@ -681,8 +682,16 @@ static int sess_alloc(cw_session* s, size_t nbytes, void** p) {
 }
 
 // Enqueue one generate step (decode: with lm_head + argmax).
+static int enqueue_step_core(cw_session* s, bool decode);
+
+// One step: the decode kernels, then (decode steps with sampling or stop
+// tokens configured) the sampling kernel that may replace the argmax.
 static int enqueue_step(cw_session* s, bool decode) {
-    if (s->plan) return step_enqueue(s, decode);  // one persistent launch
+    CW_TRY(s->plan ? step_enqueue(s, decode) : enqueue_step_core(s, decode));
+    return decode && sample_active(s) ? sample_enqueue(s) : CW_OK;
+}
+
+static int enqueue_step_core(cw_session* s, bool decode) {
     cw_model* m = s->m;
     cw_ctx* ctx = s->ctx;
     const cw_model_info& I = m->info;
@@ -942,6 +951,8 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     // fixed-point residual accumulator (persistent step: FFN partial sums)
     A((size_t)I.dim * sizeof(long long), (void**)&s->racc);
     A((size_t)I.n_heads * I.dim * sizeof(float), (void**)&s->opart);
+    A((size_t)sample_params_size(), &s->smp_dev);
+    if (rc == CW_OK) rc = sample_params_write(s);
     if (rc == CW_OK && (cudaMallocHost(&s->h_tok, sizeof(unsigned)) != cudaSuccess ||
                         cudaMallocHost(&s->h_tok_in, sizeof(unsigned)) != cudaSuccess))
         rc = set_error(CW_ERR_OOM, "pinned host allocation failed");
@@ -1029,6 +1040,57 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     s->host_pos = 0;
     s->n_prompt = n_prompt;
     s->n_produced = 0;
+    s->stopped = false;
+    return CW_OK;
+}
+
+// Host counters from the device state (EOS may have ended the sequence
+// inside a run of steps).
+static int sync_counts(cw_session* s) {
+    DevState h;
+    CW_CUDA(cudaMemcpyAsync(&h, s->st, sizeof h, cudaMemcpyDeviceToHost, s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    s->n_produced = (size_t)h.n_produced;
+    s->stopped = h.stopped != 0;
+    return CW_OK;
+}
+
+int cw_session_set_sampling(cw_session* s, float temperature, uint32_t top_k, float top_p,
+                            uint64_t seed) {
+    clear_error();
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_set_sampling: session is NULL");
+    CW_CHECK(temperature == temperature && top_p >= 0.f && top_p <= 1.f, CW_ERR_INVALID_ARG,
+             "cw_session_set_sampling: temperature must be a number and top_p in [0, 1]");
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    destroy_graphs(s);  // the decode graph holds the sampling launch or not
+    s->smp_temperature = temperature > 0.f ? temperature : 0.f;
+    s->smp_top_k = top_k;
+    s->smp_top_p = top_p;
+    s->smp_seed = seed;
+    return sample_params_write(s);
+}
+
+int cw_session_set_eos(cw_session* s, const uint32_t* ids, size_t n) {
+    clear_error();
+    CW_CHECK(s && (ids || n == 0) && n <= CW_MAX_EOS, CW_ERR_INVALID_ARG,
+             "cw_session_set_eos: at most %d stop tokens", CW_MAX_EOS);
+    for (size_t i = 0; i < n; i++)
+        CW_CHECK(ids[i] < s->m->info.vocab, CW_ERR_INVALID_ARG,
+                 "cw_session_set_eos: token %u outside the vocabulary", ids[i]);
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    destroy_graphs(s);
+    s->eos.assign(ids, ids + n);
+    return sample_params_write(s);
+}
+
+int cw_session_stopped(cw_session* s, int* stopped) {
+    clear_error();
+    CW_CHECK(s && stopped, CW_ERR_INVALID_ARG, "cw_session_stopped: bad arguments");
+    cudaSetDevice(s->ctx->device);
+    CW_TRY(sync_counts(s));
+    *stopped = s->stopped ? 1 : 0;
     return CW_OK;
 }
 
@@ -1066,6 +1128,7 @@ int cw_session_run(cw_session* s, size_t n_steps, size_t* n_produced) {
     cudaSetDevice(s->ctx->device);
     size_t before = s->n_produced;
     for (size_t i = 0; i < n_steps; i++) CW_TRY(run_step(s));
+    if (!s->eos.empty()) CW_TRY(sync_counts(s));  // an EOS may have stopped the run
     if (n_produced) *n_produced = s->n_produced - before;
     return check_launch("session run");
 }
@@ -1074,6 +1137,7 @@ int cw_session_tokens(cw_session* s, uint32_t* out, size_t cap, size_t* n) {
     clear_error();
     CW_CHECK(s && n, CW_ERR_INVALID_ARG, "cw_session_tokens: bad arguments");
     cudaSetDevice(s->ctx->device);
+    CW_TRY(sync_counts(s));
     size_t k = std::min(cap, s->n_produced);
     if (k && out)
         CW_CUDA(cudaMemcpyAsync(out, s->toks, k * 4, cudaMemcpyDeviceToHost, s->ctx->stream));
@@ -1115,6 +1179,10 @@ int cw_session_step(cw_session* s, uint32_t token_in, uint32_t* token_out) {
     CW_CHECK(token_in == CW_TOKEN_DEVICE || token_in < s->m->info.vocab, CW_ERR_INVALID_ARG,
              "cw_session_step: token %u outside the vocabulary", token_in);
     cudaSetDevice(s->ctx->device);
+    if (s->stopped) {  // an EOS token ended the sequence: nothing more to produce
+        *token_out = CW_TOKEN_DEVICE;
+        return CW_OK;
+    }
     if (token_in != CW_TOKEN_DEVICE) {
         *s->h_tok_in = token_in;
         CW_CUDA(cudaMemcpyAsync(&s->st->token, s->h_tok_in, 4, cudaMemcpyHostToDevice,
@@ -1128,6 +1196,11 @@ int cw_session_step(cw_session* s, uint32_t token_in, uint32_t* token_out) {
                                 s->ctx->stream));
         CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
         *token_out = *s->h_tok;
+        // an EOS token is returned but not counted (wasm.rs:99-101)
+        if (std::find(s->eos.begin(), s->eos.end(), *token_out) != s->eos.end()) {
+            s->stopped = true;
+            s->n_produced--;
+        }
     } else {
         CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
         *token_out = 0xffffffffu;
@@ -1166,15 +1239,15 @@ int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms) {
 
 int cw_session_launches(cw_session* s, size_t* prompt_step, size_t* decode_step) {
     CW_CHECK(s && prompt_step && decode_step, CW_ERR_INVALID_ARG, "cw_session_launches: bad arguments");
-    if (s->plan) {  // the whole step is one persistent launch
+    if (s->plan) {  // the whole step is one persistent launch (+ sampling)
         *prompt_step = 1;
-        *decode_step = 1;
+        *decode_step = 1 + (sample_active(s) ? 1 : 0);
         return CW_OK;
     }
     // embed + 5 per layer + finalize (+ lm_head/argmax on decode steps)
     size_t per = 2 + 5 * (size_t)s->m->info.n_layers;
     *prompt_step = per;
-    *decode_step = per + 1;
+    *decode_step = per + 1 + (sample_active(s) ? 1 : 0);
     return CW_OK;
 }
 

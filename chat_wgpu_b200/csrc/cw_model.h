@@ -25,6 +25,8 @@ struct DevState {
     unsigned done;           // CTAs that finished the current step
     unsigned pad;
     unsigned long long ctr_base;  // persistent step's head counter at the start of the step
+    unsigned stopped;             // an EOS token ended the sequence (cw_sample.cu)
+    unsigned pad2;
 };
 
 struct QW {  // packed Q4_0 weight
@@ -82,6 +84,13 @@ struct cw_session {
     float* opart = nullptr;             // per-head O-projection row sums (persistent step)
     void* pf_mem = nullptr;             // batched-prefill scratch (cw_prefill.cu), grown on demand
     size_t pf_bytes = 0;
+    // sampling and stop tokens (cw_sample.cu); temperature 0 = greedy
+    float smp_temperature = 0.f, smp_top_p = 1.f;
+    unsigned smp_top_k = 0;
+    unsigned long long smp_seed = 0;
+    std::vector<unsigned> eos;
+    void* smp_dev = nullptr;  // SampleParams on the device
+    bool stopped = false;     // host view of DevState::stopped
 };
 
 namespace cw {
@@ -99,5 +108,11 @@ int step_profile(cw_session* s, size_t n_steps,
 // cw_prefill.cu: prompt positions [host_pos, n_prompt - 1) in batched chunks
 // on the tensor cores; advances host_pos and the device state.
 int session_prefill(cw_session* s, size_t* n_done);
+
+// cw_sample.cu: device-side sampling / EOS after a decode step's finalize.
+int sample_params_size();
+int sample_params_write(cw_session* s);  // session settings -> device (syncs)
+bool sample_active(const cw_session* s);
+int sample_enqueue(cw_session* s);
 
 }  // namespace cw

@@ -112,6 +112,24 @@ class Session:
         _lib.call("cw_session_run", self._h, int(n_steps), C.byref(n))
         return int(n.value)
 
+    def set_sampling(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                     seed: int = 0) -> None:
+        """Device-side sampling after the LM head (cw_session_set_sampling);
+        temperature 0 = greedy."""
+        _lib.call("cw_session_set_sampling", self._h, float(temperature), int(top_k),
+                  float(top_p), int(seed) & (2**64 - 1))
+
+    def set_eos(self, ids) -> None:
+        """Stop tokens: the sequence ends, without emitting it, at the first one."""
+        a = np.ascontiguousarray(list(ids), dtype=np.uint32)
+        _lib.call("cw_session_set_eos", self._h, a.ctypes.data if a.size else None, a.size)
+
+    @property
+    def stopped(self) -> bool:
+        v = C.c_int()
+        _lib.call("cw_session_stopped", self._h, C.byref(v))
+        return bool(v.value)
+
     def prefill(self) -> int:
         """Run the remaining prompt positions but the last as one batch on the
         tensor cores (cw_session_prefill); returns the positions processed."""

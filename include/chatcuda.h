@@ -156,6 +156,10 @@ int cw_swiglu(cw_ctx* ctx, cw_buf gate, cw_buf up, size_t n, cw_buf* out);
 int cw_geglu(cw_ctx* ctx, cw_buf gate, cw_buf up, size_t n, cw_buf* out);
 /* argmax::argmax (argmax.rs:11-18): 1-element u32 buffer, ties -> lowest. */
 int cw_argmax(cw_ctx* ctx, cw_buf logits, size_t n, cw_buf* out);
+/* One sampling draw over logits[n] with the rules of cw_session_set_sampling
+ * (draw = the draw index i): 1-element u32 buffer. */
+int cw_sample(cw_ctx* ctx, cw_buf logits, size_t n, float temperature, uint32_t top_k,
+              float top_p, uint64_t seed, uint64_t draw, cw_buf* out);
 
 /* ---- attention without allocation ----------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device
@@ -285,6 +289,27 @@ int cw_session_persistent(cw_session* s, int* on);
  * token it produced (UINT32_MAX for a prompt position) is read back. */
 #define CW_TOKEN_DEVICE 0xffffffffu
 int cw_session_step(cw_session* s, uint32_t token_in, uint32_t* token_out);
+/* Sampling after the LM head (no reference code: its decode is greedy and
+ * its `temperature` argument is reserved, wasm.rs:57,63; ROADMAP.md:56-57).
+ * temperature <= 0: greedy argmax (the default).  Otherwise a token is drawn
+ * on the device from softmax(logits / temperature) restricted to the logits
+ * >= the top_k-th largest (top_k 0 = all) and then to the nucleus: the
+ * highest-probability tokens whose mass reaches top_p (1 = all).  Draw i of
+ * a sequence (i = tokens produced before it) uses the 53-bit uniform
+ * splitmix64(seed ^ (i+1) * 0x9E3779B97F4A7C15) >> 11; masses are fixed
+ * point (p * 2^40), so a draw is reproducible.  Takes effect from the next
+ * step; cw_session_begin does not reset it. */
+int cw_session_set_sampling(cw_session* s, float temperature, uint32_t top_k, float top_p,
+                            uint64_t seed);
+/* Stop tokens (at most CW_MAX_EOS; n = 0 clears): when a decode step
+ * produces one, it is not counted or appended and the sequence stops --
+ * later steps produce nothing -- as the reference's chat loop breaks on its
+ * EOS ids before emitting them (wasm.rs:48-51,99-101).  cw_session_step
+ * returns the stop token itself once, then CW_TOKEN_DEVICE.  A new
+ * cw_session_begin clears the stop. */
+#define CW_MAX_EOS 16
+int cw_session_set_eos(cw_session* s, const uint32_t* ids, size_t n);
+int cw_session_stopped(cw_session* s, int* stopped);
 /* cw_session_run timed with CUDA events on the context stream: *ms is the
  * device time of the n_steps steps. */
 int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms);

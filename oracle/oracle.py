@@ -219,6 +219,56 @@ def argmax(logits) -> int:
     return int(lib().orc_argmax(l, l.size))
 
 
+_MASK64 = (1 << 64) - 1
+
+
+def _splitmix64(x: int) -> int:
+    x = (x + 0x9E3779B97F4A7C15) & _MASK64
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & _MASK64
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & _MASK64
+    return x ^ (x >> 31)
+
+
+def sample(logits, temperature: float, top_k: int = 0, top_p: float = 1.0, seed: int = 0,
+           draw: int = 0):
+    """Temperature / top-k / top-p draw.  The reference has no sampler (its
+    decode is greedy, src/wasm.rs:57,63; sampling is on ROADMAP.md:56-57), so
+    this restates the rules the CUDA path documents (include/chatcuda.h,
+    cw_session_set_sampling) with numpy: w = exp((l - max) / T) in f32,
+    masses floor(w * 2^40), top-k by value threshold (ties kept), nucleus by
+    mass threshold (ties kept), draw target = floor(u53 * Z / 2^53) with
+    u53 = splitmix64(seed ^ (draw+1) * 0x9E3779B97F4A7C15) >> 11, token =
+    first index whose inclusive prefix mass exceeds the target.
+    Returns (token, detail) where detail holds the kept masses, Z and target
+    so a caller can judge draws that sit at a rounding boundary."""
+    l = np.asarray(logits, dtype=np.float32).ravel()
+    amax = argmax(l)
+    if not temperature > 0 or np.isnan(l[amax]):
+        return amax, None
+    ok = ~np.isnan(l)
+    if 0 < top_k < l.size:
+        kth = np.sort(l[ok])[::-1][min(top_k, int(ok.sum())) - 1]
+        ok &= l >= kth
+    w = np.zeros(l.size, np.float32)
+    w[ok] = np.exp((l[ok] - l[amax]) * np.float32(1.0 / np.float32(temperature)),
+                   dtype=np.float32)
+    m = np.floor(w.astype(np.float64) * 2.0 ** 40).astype(np.uint64)
+    if top_p < 1.0:
+        total = int(m.sum(dtype=np.uint64))
+        need = max(1, int(float(top_p) * float(total)))
+        order = np.argsort(-w, kind="stable")
+        cum = np.cumsum(m[order].astype(object))
+        j = int(np.searchsorted(np.array(cum, dtype=np.float64), need, side="left"))
+        tau = w[order[min(j, l.size - 1)]]
+        m[w < tau] = 0
+    Z = int(m.sum(dtype=np.uint64))
+    u53 = _splitmix64(seed ^ (((draw + 1) * 0x9E3779B97F4A7C15) & _MASK64)) >> 11
+    target = (u53 * Z) >> 53
+    incl = np.cumsum(m.astype(np.uint64))
+    tok = int(np.searchsorted(incl, target, side="right")) if Z else amax
+    return tok, {"mass": m, "Z": Z, "target": target, "incl": incl}
+
+
 # --- model -----------------------------------------------------------------
 class Model:
     """GGUF-backed model: src/model/qwen3.rs (+ restated gemma2 family)."""
