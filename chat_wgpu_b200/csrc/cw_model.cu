@@ -201,6 +201,7 @@ struct AArgs {
     int n_heads, n_kv, hd, n_splits, window;
     float scale, softcap;
     const DevState* st;
+    float* q_out;  // optional: the normed, rotated q rows (hook tap "q")
 };
 
 template <int EPL, int GMAX>
@@ -276,6 +277,8 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
         row[k + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
     }
     __syncthreads();
+    if (a.q_out && split == 0)
+        for (int i = threadIdx.x; i < G * hd; i += blockDim.x) a.q_out[(size_t)g * G * hd + i] = qs[i];
     float* kbase = a.kc + (size_t)g * a.max_seq * hd;
     float* vbase = a.vc + (size_t)g * a.max_seq * hd;
     if (holds) {  // cache.rs:21-24: this token's K (normed, roped) and V at pos
@@ -345,6 +348,30 @@ __global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n
     st->ctr_base = bar[1];
     st->done = 0;
     st->stopped = 0;
+}
+
+// ---- hook taps (src/model/mod.rs:155-165) -----------------------------------
+// Copy a tapped vector into slot pos % cap of its ring.
+__global__ void k_tap(const float* __restrict__ src, int len, float* __restrict__ ring, int cap,
+                      const DevState* __restrict__ st) {
+    float* dst = ring + (size_t)(st->pos % cap) * len;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < len; i += gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+// Post-norm families: the residual sum base + rmsnorm(delta) * gain(w) that
+// the next kernel's prologue forms, computed into the ring for a tap.
+__global__ void k_tap_postadd(const float* __restrict__ base, const float* __restrict__ delta,
+                              const float* __restrict__ w, int unit, float eps, int dim,
+                              float* __restrict__ ring, int cap, const DevState* __restrict__ st) {
+    __shared__ float red[32];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss = fmaf(delta[i], delta[i], ss);
+    const float inv = 1.0f / sqrtf(cta_sum(ss, red) / (float)dim + eps);
+    float* dst = ring + (size_t)(st->pos % cap) * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float gw = unit ? 1.0f + w[i] : w[i];
+        dst[i] = base[i] + __fmul_rn(__fmul_rn(delta[i], inv), gw);
+    }
 }
 
 // ===========================================================================
@@ -686,8 +713,24 @@ static int enqueue_step_core(cw_session* s, bool decode);
 
 // One step: the decode kernels, then (decode steps with sampling or stop
 // tokens configured) the sampling kernel that may replace the argmax.
+const Tap* find_tap(const cw_session* s, int kind, uint32_t layer) {
+    for (const Tap& t : s->taps)
+        if (t.kind == kind && t.layer == layer) return &t;
+    return nullptr;
+}
+
+static int tap_copy(cw_session* s, int kind, uint32_t li, const float* src) {
+    const Tap* t = find_tap(s, kind, li);
+    if (!t) return CW_OK;
+    k_tap<<<(unsigned)((t->len + 255) / 256), 256, 0, s->ctx->stream>>>(
+        src, (int)t->len, t->ring, (int)t->cap, s->st);
+    return check_launch("hook tap");
+}
+
 static int enqueue_step(cw_session* s, bool decode) {
-    CW_TRY(s->plan ? step_enqueue(s, decode) : enqueue_step_core(s, decode));
+    // taps read intermediates the persistent step never materialises
+    const bool persistent = s->plan && s->taps.empty();
+    CW_TRY(persistent ? step_enqueue(s, decode) : enqueue_step_core(s, decode));
     return decode && sample_active(s) ? sample_enqueue(s) : CW_OK;
 }
 
@@ -755,7 +798,9 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         t.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
         t.softcap = I.attn_softcap;
         t.st = s->st;
+        t.q_out = find_tap(s, TAP_Q, li) ? s->qtap : nullptr;
         CW_TRY(launch_fattn(ctx, t));
+        CW_TRY(tap_copy(s, TAP_Q, li, s->qtap));
 
         stage("attn_out");
         FArgs o{};
@@ -766,6 +811,7 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         o.x = s->attn;
         o.y = post ? s->tmp : s->hidden;
         CW_TRY(post ? (fgemv<PRO_X, EPI_STORE>(ctx, o)) : (fgemv<PRO_X, EPI_RESID>(ctx, o)));
+        if (!post) CW_TRY(tap_copy(s, TAP_POST_ATTN, li, s->hidden));
 
         stage("ffn_in");
         FArgs f{};
@@ -785,6 +831,7 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         f.y = s->act;
         f.geglu = I.activation == 1;
         CW_TRY((fgemv<PRO_NORM, EPI_GLU>(ctx, f)));
+        if (post) CW_TRY(tap_copy(s, TAP_POST_ATTN, li, s->hidden_b));  // h_out of this prologue
 
         stage("ffn_out");
         FArgs d{};
@@ -795,6 +842,14 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         d.x = s->act;
         d.y = post ? s->tmp : s->hidden;
         CW_TRY(post ? (fgemv<PRO_X, EPI_STORE>(ctx, d)) : (fgemv<PRO_X, EPI_RESID>(ctx, d)));
+        if (!post) {
+            CW_TRY(tap_copy(s, TAP_LAYER_OUT, li, s->hidden));
+        } else if (const Tap* tp = find_tap(s, TAP_LAYER_OUT, li)) {
+            // the next prologue forms hidden_b + postnorm(tmp); form it here for the tap
+            k_tap_postadd<<<1, 256, 0, ctx->stream>>>(s->hidden_b, s->tmp, l.post_ffw, unit, I.eps,
+                                                      (int)I.dim, tp->ring, (int)tp->cap, s->st);
+            CW_TRY(check_launch("hook tap"));
+        }
     }
     if (decode) {
         stage("lm_head");
@@ -952,6 +1007,7 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     A((size_t)I.dim * sizeof(long long), (void**)&s->racc);
     A((size_t)I.n_heads * I.dim * sizeof(float), (void**)&s->opart);
     A((size_t)sample_params_size(), &s->smp_dev);
+    A(qd * 4, (void**)&s->qtap);
     if (rc == CW_OK) rc = sample_params_write(s);
     if (rc == CW_OK && (cudaMallocHost(&s->h_tok, sizeof(unsigned)) != cudaSuccess ||
                         cudaMallocHost(&s->h_tok_in, sizeof(unsigned)) != cudaSuccess))
@@ -1083,6 +1139,76 @@ int cw_session_set_eos(cw_session* s, const uint32_t* ids, size_t n) {
     destroy_graphs(s);
     s->eos.assign(ids, ids + n);
     return sample_params_write(s);
+}
+
+static int tap_kind(const char* name) {
+    if (!name) return -1;
+    if (!strcmp(name, "q")) return TAP_Q;
+    if (!strcmp(name, "post_attn")) return TAP_POST_ATTN;
+    if (!strcmp(name, "layer_out")) return TAP_LAYER_OUT;
+    return -1;
+}
+
+int cw_session_add_tap(cw_session* s, const char* name, uint32_t layer, size_t cap) {
+    clear_error();
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_add_tap: session is NULL");
+    const int kind = tap_kind(name);
+    CW_CHECK(kind >= 0, CW_ERR_INVALID_ARG,
+             "cw_session_add_tap: unknown tap '%s' (q, post_attn, layer_out)", name ? name : "");
+    const cw_model_info& I = s->m->info;
+    CW_CHECK(layer < I.n_layers && cap > 0 && cap <= s->max_seq, CW_ERR_INVALID_ARG,
+             "cw_session_add_tap: layer %u of %u, cap %zu (1..max_seq)", layer, I.n_layers, cap);
+    CW_CHECK(!find_tap(s, kind, layer), CW_ERR_INVALID_ARG, "tap %s/%u already added", name, layer);
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    destroy_graphs(s);  // the captured step gains the tap's copy
+    Tap t;
+    t.kind = kind;
+    t.layer = layer;
+    t.cap = cap;
+    t.len = kind == TAP_Q ? (size_t)I.n_heads * I.head_dim : I.dim;
+    CW_TRY(sess_alloc(s, t.cap * t.len * 4, (void**)&t.ring));
+    t.buf = s->owned.back();
+    CW_CUDA(cudaMemsetAsync(t.ring, 0, t.cap * t.len * 4, s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    s->taps.push_back(t);
+    return CW_OK;
+}
+
+int cw_session_clear_taps(cw_session* s) {
+    clear_error();
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_clear_taps: session is NULL");
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    destroy_graphs(s);
+    for (const Tap& t : s->taps) {
+        auto it = s->ctx->bufs.find(t.buf);
+        if (it != s->ctx->bufs.end()) {
+            cudaFree(it->second.ptr);
+            s->ctx->bufs.erase(it);
+        }
+        s->owned.erase(std::remove(s->owned.begin(), s->owned.end(), t.buf), s->owned.end());
+    }
+    s->taps.clear();
+    return CW_OK;
+}
+
+int cw_session_read_tap(cw_session* s, const char* name, uint32_t layer, size_t pos, float* out,
+                        size_t len) {
+    clear_error();
+    CW_CHECK(s && out, CW_ERR_INVALID_ARG, "cw_session_read_tap: bad arguments");
+    const Tap* t = find_tap(s, tap_kind(name), layer);
+    CW_CHECK(t, CW_ERR_INVALID_ARG, "cw_session_read_tap: no tap %s/%u", name ? name : "", layer);
+    CW_CHECK(len == t->len, CW_ERR_INVALID_ARG, "cw_session_read_tap: the tap holds %zu floats",
+             t->len);
+    CW_CHECK(pos < s->host_pos && pos + t->cap >= s->host_pos, CW_ERR_INVALID_ARG,
+             "cw_session_read_tap: position %zu is not among the last %zu recorded (next %zu)",
+             pos, t->cap, s->host_pos);
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaMemcpyAsync(out, t->ring + (pos % t->cap) * t->len, t->len * 4,
+                            cudaMemcpyDeviceToHost, s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    return check_device_status(s->ctx);
 }
 
 int cw_session_stopped(cw_session* s, int* stopped) {
@@ -1239,13 +1365,15 @@ int cw_session_run_timed(cw_session* s, size_t n_steps, double* ms) {
 
 int cw_session_launches(cw_session* s, size_t* prompt_step, size_t* decode_step) {
     CW_CHECK(s && prompt_step && decode_step, CW_ERR_INVALID_ARG, "cw_session_launches: bad arguments");
-    if (s->plan) {  // the whole step is one persistent launch (+ sampling)
+    if (s->plan && s->taps.empty()) {  // the whole step is one persistent launch (+ sampling)
         *prompt_step = 1;
         *decode_step = 1 + (sample_active(s) ? 1 : 0);
         return CW_OK;
     }
     // embed + 5 per layer + finalize (+ lm_head/argmax on decode steps)
     size_t per = 2 + 5 * (size_t)s->m->info.n_layers;
+    *prompt_step = per;
+    per += s->taps.size();
     *prompt_step = per;
     *decode_step = per + 1 + (sample_active(s) ? 1 : 0);
     return CW_OK;

@@ -44,6 +44,18 @@ struct Layer {
 
 struct StepPlan;  // cw_step.cu
 
+// Hook taps (src/model/mod.rs:155-165, qwen3.rs:165,180,188): a named
+// intermediate of one layer copied every step into a device ring of `cap`
+// positions (slot pos % cap).
+enum TapKind : int { TAP_Q = 0, TAP_POST_ATTN = 1, TAP_LAYER_OUT = 2 };
+struct Tap {
+    int kind = TAP_Q;
+    uint32_t layer = 0;
+    size_t cap = 0, len = 0;
+    float* ring = nullptr;
+    cw_buf buf = 0;
+};
+
 }  // namespace cw
 
 struct cw_model {
@@ -91,6 +103,8 @@ struct cw_session {
     std::vector<unsigned> eos;
     void* smp_dev = nullptr;  // SampleParams on the device
     bool stopped = false;     // host view of DevState::stopped
+    std::vector<cw::Tap> taps;  // active hook taps (force the per-stage step kernels)
+    float* qtap = nullptr;      // the step's normed, rotated q (source of "q" taps)
 };
 
 namespace cw {
@@ -108,6 +122,8 @@ int step_profile(cw_session* s, size_t n_steps,
 // cw_prefill.cu: prompt positions [host_pos, n_prompt - 1) in batched chunks
 // on the tensor cores; advances host_pos and the device state.
 int session_prefill(cw_session* s, size_t* n_done);
+
+const Tap* find_tap(const cw_session* s, int kind, uint32_t layer);
 
 // cw_sample.cu: device-side sampling / EOS after a decode step's finalize.
 int sample_params_size();

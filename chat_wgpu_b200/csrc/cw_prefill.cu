@@ -97,6 +97,7 @@ __global__ void __launch_bounds__(256) k_pf_norm(float* __restrict__ H, const fl
         hb[i] = h;
         ssh = fmaf(h, h, ssh);
     }
+    if (!xh) return;  // residual update only
     ssh = pf_block_sum(ssh, red);
     const float inv = 1.0f / sqrtf(ssh / (float)dim + eps);
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -377,6 +378,17 @@ __global__ void k_pf_glu(const float* __restrict__ Gm, int I, int geglu, long ro
     }
 }
 
+// Hook taps of C prompt rows: row r (stride ld) into ring slot (p0 + r) % cap.
+__global__ void k_tap_rows(const float* __restrict__ src, int ld, int len, int rows,
+                           float* __restrict__ ring, int cap, int p0) {
+    const long n = (long)rows * len;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / len), c = (int)(i - (long)r * len);
+        ring[(size_t)((p0 + r) % cap) * len + c] = src[(size_t)r * ld + c];
+    }
+}
+
 // After the chunk: the next step reads prompt[p_next] at p_next.
 __global__ void k_pf_done(DevState* st, const unsigned* __restrict__ prompt, int p_next) {
     st->pos = p_next;
@@ -504,6 +516,15 @@ int pf_chunk(cw_session* s, int p0, int C) {
         return gemm_x3(ctx, xh, xl, wh, wl, C, N, K, y, N, bias, epi);
     };
     const int ew_grid = std::max(1, std::min(C * 8, ctx->sm_count * 8));
+    auto tap = [&](int kind, uint32_t li, const float* src, int ld) {
+        const Tap* t = find_tap(s, kind, li);
+        if (!t) return (int)CW_OK;
+        k_tap_rows<<<ew_grid, 256, 0, ctx->stream>>>(src, ld, (int)t->len, C, t->ring, (int)t->cap,
+                                                     p0);
+        return check_launch("prefill hook tap");
+    };
+    const uint32_t last = I.n_layers - 1;
+    const bool last_full = find_tap(s, TAP_POST_ATTN, last) || find_tap(s, TAP_LAYER_OUT, last);
 
     stage("prefill.embed");
     k_pf_embed<<<C, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, dim, I.embed_scale,
@@ -520,13 +541,16 @@ int pf_chunk(cw_session* s, int p0, int C) {
                                                     l.attn_norm, unit, I.eps, dim, (__half*)xh,
                                                     (__half*)xl);
         CW_TRY(check_launch("prefill norm"));
+        if (pre_t) CW_TRY(tap(TAP_LAYER_OUT, li - 1, H, dim));  // H now holds layer li-1's output
         CW_TRY(gemm(l.qkv, dim, qkv_rows, QKV, l.qkv_bias, GE_STORE));
         stage("prefill.qk");
         k_pf_qk<<<C, 256, 8 * hd * 4, ctx->stream>>>(QKV, qkv_rows, l.q_norm, l.k_norm, I.eps,
                                                       m->inv_freq, kc, vc, (int)s->max_seq, p0,
                                                       nh, nkv, hd);
         CW_TRY(check_launch("prefill qk"));
-        if (li + 1 == I.n_layers) break;  // only the K/V rows of the last layer are read later
+        CW_TRY(tap(TAP_Q, li, QKV, qkv_rows));
+        // only the K/V rows of the last layer are read later (unless tapped)
+        if (li == last && !last_full) break;
 
         stage("prefill.attn");
         const int window = (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
@@ -548,18 +572,29 @@ int pf_chunk(cw_session* s, int p0, int C) {
 #undef CW_PFE
         }
         CW_TRY(gemm(l.wo, qd, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
+        if (!post) CW_TRY(tap(TAP_POST_ATTN, li, H, dim));
 
         stage("prefill.norm");
         k_pf_norm<<<C, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
                                                     post ? l.post_attn : nullptr, l.ffn_norm, unit,
                                                     I.eps, dim, (__half*)xh, (__half*)xl);
         CW_TRY(check_launch("prefill norm"));
+        if (post) CW_TRY(tap(TAP_POST_ATTN, li, H, dim));
         CW_TRY(gemm(l.gate_up, dim, 2 * hid, Gm, nullptr, GE_STORE));
         stage("prefill.glu");
         k_pf_glu<<<ew_grid, 256, 0, ctx->stream>>>(Gm, hid, I.activation == 1, C, (__half*)xh,
                                                     (__half*)xl);
         CW_TRY(check_launch("prefill glu"));
         CW_TRY(gemm(l.down, hid, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
+        if (!post) {
+            CW_TRY(tap(TAP_LAYER_OUT, li, H, dim));
+        } else if (li == last && find_tap(s, TAP_LAYER_OUT, li)) {
+            // no next layer folds the post-normed FFN output in: do it for the tap
+            k_pf_norm<<<C, 256, dim * 4, ctx->stream>>>(H, T, l.post_ffw, l.ffn_norm, unit, I.eps,
+                                                        dim, nullptr, nullptr);
+            CW_TRY(check_launch("prefill norm"));
+            CW_TRY(tap(TAP_LAYER_OUT, li, H, dim));
+        }
     }
     stage("prefill.done");
     k_pf_done<<<1, 1, 0, ctx->stream>>>(s->st, s->prompt, p0 + C);

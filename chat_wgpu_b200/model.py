@@ -130,6 +130,25 @@ class Session:
         _lib.call("cw_session_stopped", self._h, C.byref(v))
         return bool(v.value)
 
+    # ---- hook taps (Hook::tap, src/model/mod.rs:155-165)
+    TAPS = ("q", "post_attn", "layer_out")
+
+    def add_tap(self, name: str, layer: int, cap: int) -> None:
+        """Record `name` of `layer` at every position into a device ring of
+        the last `cap` positions."""
+        _lib.call("cw_session_add_tap", self._h, name.encode(), int(layer), int(cap))
+
+    def clear_taps(self) -> None:
+        _lib.call("cw_session_clear_taps", self._h)
+
+    def read_tap(self, name: str, layer: int, pos: int) -> np.ndarray:
+        I = self.model.info
+        n = I["n_heads"] * I["head_dim"] if name == "q" else I["dim"]
+        out = np.empty(n, np.float32)
+        _lib.call("cw_session_read_tap", self._h, name.encode(), int(layer), int(pos),
+                  out.ctypes.data, n)
+        return out
+
     def prefill(self) -> int:
         """Run the remaining prompt positions but the last as one batch on the
         tensor cores (cw_session_prefill); returns the positions processed."""

@@ -308,6 +308,20 @@ int cw_session_set_sampling(cw_session* s, float temperature, uint32_t top_k, fl
  * returns the stop token itself once, then CW_TOKEN_DEVICE.  A new
  * cw_session_begin clears the stop. */
 #define CW_MAX_EOS 16
+/* Hook::tap (mod.rs:155-165): record the forward pass's named intermediate
+ * of `layer` at every position -- "q" (normed, rotated queries, n_heads *
+ * head_dim floats, qwen3.rs:165), "post_attn" (hidden after the attention
+ * residual, dim floats, :180) or "layer_out" (hidden after the FFN residual,
+ * :188) -- into a device ring of the last `cap` positions, with copies that
+ * are part of the captured step (no host work per token).  A session with
+ * taps runs the per-stage step kernels (the persistent step keeps these
+ * values in registers and shared memory); cw_session_prefill records them
+ * too.  cw_session_read_tap copies the vector of position `pos` (one of the
+ * last `cap` positions run) to the host; len must be the tap's length. */
+int cw_session_add_tap(cw_session* s, const char* name, uint32_t layer, size_t cap);
+int cw_session_clear_taps(cw_session* s);
+int cw_session_read_tap(cw_session* s, const char* name, uint32_t layer, size_t pos, float* out,
+                        size_t len);
 int cw_session_set_eos(cw_session* s, const uint32_t* ids, size_t n);
 int cw_session_stopped(cw_session* s, int* stopped);
 /* cw_session_run timed with CUDA events on the context stream: *ms is the

@@ -545,6 +545,9 @@ struct orc_model {
     /* state */
     size_t max_seq;
     float *kc, *vc; /* [n_layers][max_seq][kv_dim] */
+    /* Hook::tap values of layer tap_layer from the last step (mod.rs:155-165) */
+    long tap_layer;
+    float *tap_q, *tap_post_attn, *tap_layer_out;
 };
 
 static size_t row_bytes_for(uint32_t dtype, size_t in_f) {
@@ -622,6 +625,7 @@ void orc_model_close(orc_model* M) {
         free(M->L);
     }
     free(M->final_norm); free(M->kc); free(M->vc);
+    free(M->tap_q); free(M->tap_post_attn); free(M->tap_layer_out);
     gguf_free(&M->g);
     free(M);
 }
@@ -762,6 +766,8 @@ int orc_model_step(orc_model* M, uint32_t token, size_t pos, float* hidden_out, 
         }
         orc_rope(q, M->n_heads, M->hd, (uint32_t)pos, M->theta, tmpq);
         orc_rope(k, M->n_kv, M->hd, (uint32_t)pos, M->theta, tmpk);
+        const int tapped = M->tap_q && (long)li == M->tap_layer;
+        if (tapped) memcpy(M->tap_q, tmpq, qd * sizeof(float));   /* qwen3.rs:165 */
         float* kc = M->kc + li * M->max_seq * kvd;
         float* vc = M->vc + li * M->max_seq * kvd;
         memcpy(kc + pos * kvd, tmpk, kvd * sizeof(float));   /* src/model/cache.rs:21-24 */
@@ -772,6 +778,7 @@ int orc_model_step(orc_model* M, uint32_t token, size_t pos, float* hidden_out, 
         mat_vec(&l->wo, attn, ao);
         if (M->post_norms) { orc_rmsnorm(ao, l->post_attn_norm, 1, dim, M->eps, 1, normed); memcpy(ao, normed, dim * sizeof(float)); }
         orc_add(h, ao, dim, h);
+        if (tapped) memcpy(M->tap_post_attn, h, dim * sizeof(float));   /* qwen3.rs:180 */
         orc_rmsnorm(h, l->ffn_norm, 1, dim, M->eps, M->unit_norm, normed);
         mat_vec(&l->gate, normed, g);
         mat_vec(&l->up, normed, u);
@@ -779,6 +786,7 @@ int orc_model_step(orc_model* M, uint32_t token, size_t pos, float* hidden_out, 
         mat_vec(&l->down, act, ff);
         if (M->post_norms) { orc_rmsnorm(ff, l->post_ffw_norm, 1, dim, M->eps, 1, normed); memcpy(ff, normed, dim * sizeof(float)); }
         orc_add(h, ff, dim, h);
+        if (tapped) memcpy(M->tap_layer_out, h, dim * sizeof(float));   /* qwen3.rs:188 */
     }
     orc_rmsnorm(h, M->final_norm, 1, dim, M->eps, M->unit_norm, normed);
     if (hidden_out) memcpy(hidden_out, normed, dim * sizeof(float));
@@ -790,6 +798,26 @@ int orc_model_step(orc_model* M, uint32_t token, size_t pos, float* hidden_out, 
     }
     free(h); free(normed); free(q); free(k); free(v); free(tmpq); free(tmpk);
     free(attn); free(ao); free(g); free(u); free(act); free(ff);
+    return 0;
+}
+
+int orc_model_set_tap(orc_model* M, long layer) {
+    free(M->tap_q); free(M->tap_post_attn); free(M->tap_layer_out);
+    M->tap_q = M->tap_post_attn = M->tap_layer_out = NULL;
+    M->tap_layer = layer;
+    if (layer < 0) return 0;
+    if ((size_t)layer >= M->n_layers) return -1;
+    M->tap_q = (float*)calloc(M->n_heads * M->hd, sizeof(float));
+    M->tap_post_attn = (float*)calloc(M->dim, sizeof(float));
+    M->tap_layer_out = (float*)calloc(M->dim, sizeof(float));
+    return (M->tap_q && M->tap_post_attn && M->tap_layer_out) ? 0 : -1;
+}
+
+int orc_model_get_tap(const orc_model* M, float* q, float* post_attn, float* layer_out) {
+    if (!M->tap_q) return -1;
+    memcpy(q, M->tap_q, M->n_heads * M->hd * sizeof(float));
+    memcpy(post_attn, M->tap_post_attn, M->dim * sizeof(float));
+    memcpy(layer_out, M->tap_layer_out, M->dim * sizeof(float));
     return 0;
 }
 

@@ -99,6 +99,13 @@ int orc_model_reset(orc_model* m, size_t max_seq);
 int orc_model_step(orc_model* m, uint32_t token, size_t pos, float* hidden,
                    float* logits);
 
+/* Hook::tap (src/model/mod.rs:155-165): record, at every step, the values the
+ * reference's forward hands its hook for layer `layer` -- "q" after QK-norm
+ * and RoPE (qwen3.rs:165), "post_attn" (:180), "layer_out" (:188); -1 = off.
+ * orc_model_get_tap copies the last step's three vectors. */
+int orc_model_set_tap(orc_model* m, long layer);
+int orc_model_get_tap(const orc_model* m, float* q, float* post_attn, float* layer_out);
+
 /* OpenMP threads the oracle may use (0 = library default). */
 void orc_set_threads(int n);
 int orc_get_threads(void);

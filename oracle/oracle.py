@@ -68,6 +68,8 @@ def lib():
                 "orc_generate": (C.c_int, [C.c_void_p, _u32p, _sz, _sz, _u32p, C.c_void_p]),
                 "orc_model_reset": (C.c_int, [C.c_void_p, _sz]),
                 "orc_model_step": (C.c_int, [C.c_void_p, C.c_uint32, _sz, C.c_void_p, C.c_void_p]),
+                "orc_model_set_tap": (C.c_int, [C.c_void_p, C.c_long]),
+                "orc_model_get_tap": (C.c_int, [C.c_void_p, _f32p, _f32p, _f32p]),
                 "orc_set_threads": (None, [C.c_int]),
                 "orc_get_threads": (C.c_int, []),
             }
@@ -309,6 +311,20 @@ class Model:
     def reset(self, max_seq: int):
         if lib().orc_model_reset(self._h, int(max_seq)) != 0:
             raise RuntimeError("oracle reset failed")
+
+    def set_tap(self, layer: int) -> None:
+        """Hook::tap (src/model/mod.rs:155-165) for `layer` (-1 = off)."""
+        if lib().orc_model_set_tap(self._h, int(layer)) != 0:
+            raise RuntimeError("oracle set_tap failed")
+
+    def tap(self) -> dict:
+        """The last step's tapped vectors: q, post_attn, layer_out."""
+        q = np.zeros(self.n_heads * self.head_dim, np.float32)
+        pa = np.zeros(self.dim, np.float32)
+        lo = np.zeros(self.dim, np.float32)
+        if lib().orc_model_get_tap(self._h, q, pa, lo) != 0:
+            raise RuntimeError("no tap set")
+        return {"q": q, "post_attn": pa, "layer_out": lo}
 
     def step(self, token: int, pos: int, want_logits: bool = True):
         hidden = np.zeros(self.dim, dtype=np.float32)
