@@ -109,6 +109,10 @@ SIGNATURES = {
     "cw_session_set_eos": [_vp, _vp, _sz],
     "cw_session_stopped": [_vp, C.POINTER(C.c_int)],
     "cw_session_add_tap": [_vp, C.c_char_p, C.c_uint32, _sz],
+    "cw_group_create": [C.POINTER(_vp), _sz, C.POINTER(_vp)],
+    "cw_group_free": [_vp],
+    "cw_group_run": [_vp, _sz],
+    "cw_group_run_timed": [_vp, _sz, C.POINTER(C.c_double)],
     "cw_session_clear_taps": [_vp],
     "cw_session_read_tap": [_vp, C.c_char_p, C.c_uint32, _sz, _vp, _sz],
     "cw_sample": [_vp, _buf, _sz, C.c_float, C.c_uint32, C.c_float, C.c_uint64, C.c_uint64, _pbuf],

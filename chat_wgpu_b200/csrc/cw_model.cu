@@ -907,6 +907,17 @@ static void destroy_graphs(cw_session* s) {
             }
 }
 
+// Host counters from the device state (EOS may have ended the sequence
+// inside a run of steps).
+int sync_counts(cw_session* s) {
+    DevState h;
+    CW_CUDA(cudaMemcpyAsync(&h, s->st, sizeof h, cudaMemcpyDeviceToHost, s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    s->n_produced = (size_t)h.n_produced;
+    s->stopped = h.stopped != 0;
+    return CW_OK;
+}
+
 static int run_step(cw_session* s) {
     bool decode = !(s->host_pos + 1 < s->n_prompt);
     CW_CHECK(s->host_pos < s->max_seq, CW_ERR_INVALID_ARG,
@@ -956,6 +967,7 @@ int cw_model_free(cw_model* m) {
             m->ctx->bufs.erase(it);
         }
     }
+    for (void* p : m->split_mem) cudaFree(p);
     delete m;
     return CW_OK;
 }
@@ -1100,16 +1112,6 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     return CW_OK;
 }
 
-// Host counters from the device state (EOS may have ended the sequence
-// inside a run of steps).
-static int sync_counts(cw_session* s) {
-    DevState h;
-    CW_CUDA(cudaMemcpyAsync(&h, s->st, sizeof h, cudaMemcpyDeviceToHost, s->ctx->stream));
-    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
-    s->n_produced = (size_t)h.n_produced;
-    s->stopped = h.stopped != 0;
-    return CW_OK;
-}
 
 int cw_session_set_sampling(cw_session* s, float temperature, uint32_t top_k, float top_p,
                             uint64_t seed) {

@@ -32,6 +32,7 @@
 #include "cw_device.cuh"
 #include "cw_gemm.cuh"
 #include "cw_model.h"
+#include "cw_sample.cuh"
 
 namespace cw {
 
@@ -509,11 +510,21 @@ int pf_chunk(cw_session* s, int p0, int C) {
         sc.reset();
         if (ctx->profiling) sc.reset(new OpScope(ctx, name));
     };
+    const bool cached = !m->split.empty();  // f16 pairs built once (co-batched step)
+    int widx = 0;                             // layer-major index into m->split
     auto gemm = [&](const QW& w, int K, int N, float* y, const float* bias, int epi) {
-        stage("prefill.split_w");
-        CW_TRY(q4_split(ctx, w.payload, w.scales, N, K, wh, wl));
+        const void *ph = wh, *pl = wl;
+        if (cached) {
+            const SplitW& sw = m->split[widx];
+            ph = sw.h;
+            pl = sw.l;
+        } else {
+            stage("prefill.split_w");
+            CW_TRY(q4_split(ctx, w.payload, w.scales, N, K, wh, wl));
+        }
+        widx++;
         stage("prefill.gemm");
-        return gemm_x3(ctx, xh, xl, wh, wl, C, N, K, y, N, bias, epi);
+        return gemm_x3(ctx, xh, xl, ph, pl, C, N, K, y, N, bias, epi);
     };
     const int ew_grid = std::max(1, std::min(C * 8, ctx->sm_count * 8));
     auto tap = [&](int kind, uint32_t li, const float* src, int ld) {
@@ -532,6 +543,7 @@ int pf_chunk(cw_session* s, int p0, int C) {
     CW_TRY(check_launch("prefill embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
+        widx = 4 * (int)li;  // qkv, wo, gate_up, down
         float* kc = s->kc + (size_t)li * nkv * s->max_seq * hd;
         float* vc = s->vc + (size_t)li * nkv * s->max_seq * hd;
         const bool pre_t = post && li > 0;  // previous layer's FFN output, post-normed in
@@ -633,3 +645,473 @@ int session_prefill(cw_session* s, size_t* n_done) {
 }
 
 }  // namespace cw
+
+// ===========================================================================
+// co-batched decode: one step of B independent sessions together
+// ===========================================================================
+// Each row is one session at its own position with its own KV cache; the
+// projections of all rows share one pass over the weights as tensor-core
+// GEMMs (the f16 pairs of model->split), so the weight stream is paid once
+// per step instead of once per session.  Per session the step does exactly
+// what its single-session step does (embed, layers, final norm, LM head,
+// argmax / sampling / EOS, generate-loop bookkeeping, mod.rs:57-125).
+namespace cw {
+namespace {
+
+struct GrpRow {
+    DevState* st;
+    const unsigned* prompt;
+    unsigned* toks;
+    float* logits;  // the session's logits buffer (cw_session_logits)
+    const SampleParams* smp;
+    float *kc, *vc;  // layer-0 cache bases
+    int max_seq, pad;
+};
+
+__global__ void k_grp_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
+                            int dim, float scale, const GrpRow* __restrict__ rows,
+                            float* __restrict__ H) {
+    const int r = blockIdx.x, nb = dim / 32;
+    const unsigned tok = rows[r].st->token;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const int b = i >> 5, j = i & 31;
+        const size_t blk = (size_t)tok * nb + b;
+        const float d = __half2float(scales[blk]);
+        const uint8_t byte = payload[blk * 16 + (j & 15)];
+        const int q = (j < 16) ? (byte & 0xf) : (byte >> 4);
+        const float v = __fmul_rn(d, (float)(q - 8));
+        H[(size_t)r * dim + i] = scale > 0.f ? __fmul_rn(v, scale) : v;
+    }
+}
+
+// k_pf_qk for rows of different sessions (position and cache per row).
+__global__ void __launch_bounds__(256) k_grp_qk(float* __restrict__ QKV, int ld,
+                                                const float* __restrict__ q_norm,
+                                                const float* __restrict__ k_norm, float eps,
+                                                const float* __restrict__ inv_freq,
+                                                const GrpRow* __restrict__ rows, int li, int nh,
+                                                int nkv, int hd) {
+    extern __shared__ float rb[];
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nw = blockDim.x >> 5, half = hd / 2;
+    const GrpRow R = rows[r];
+    const int pos = R.st->pos;
+    const size_t lstride = (size_t)nkv * R.max_seq * hd;
+    float* kc = R.kc + li * lstride;
+    float* vc = R.vc + li * lstride;
+    const int qd = nh * hd, kvd = nkv * hd;
+    float* row = QKV + (size_t)r * ld;
+    float* sb = rb + (size_t)warp * hd;
+    for (int h = warp; h < nh + nkv; h += nw) {
+        const bool isq = h < nh;
+        float* src = isq ? row + (size_t)h * hd : row + qd + (size_t)(h - nh) * hd;
+        const float* nwt = isq ? q_norm : k_norm;
+        float ss = 0.f;
+        for (int d = lane; d < hd; d += 32) {
+            const float v = src[d];
+            sb[d] = v;
+            ss = fmaf(v, v, ss);
+        }
+        __syncwarp();
+        if (nwt) {
+            ss = warp_sum(ss);
+            const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+            for (int d = lane; d < hd; d += 32) sb[d] = __fmul_rn(__fmul_rn(sb[d], inv), nwt[d]);
+            __syncwarp();
+        }
+        float* dst = isq ? src : kc + ((size_t)(h - nh) * R.max_seq + pos) * hd;
+        for (int k = lane; k < half; k += 32) {
+            const float freq = __fmul_rn((float)pos, inv_freq[k]);
+            float sn, cs;
+            sincosf(freq, &sn, &cs);
+            const float lo = sb[k], hi = sb[k + half];
+            dst[k] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
+            dst[k + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+        }
+        __syncwarp();
+    }
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
+        const int g = i / hd, d = i - g * hd;
+        vc[((size_t)g * R.max_seq + pos) * hd + d] = row[qd + kvd + i];
+    }
+}
+
+// k_pf_attn for rows of different sessions.
+template <int EPL, int GMAX>
+__global__ void __launch_bounds__(128) k_grp_attn(const float* __restrict__ QKV, int ld,
+                                                  const GrpRow* __restrict__ rows, int li, int nh,
+                                                  int nkv, int hd, int window, float scale,
+                                                  float softcap, __half* __restrict__ xh,
+                                                  __half* __restrict__ xl) {
+    extern __shared__ float sm[];
+    const int r = blockIdx.x, g = blockIdx.y, G = nh / nkv, W = hd + 2;
+    const GrpRow R = rows[r];
+    const int seq = R.st->pos + 1;
+    const size_t lstride = (size_t)nkv * R.max_seq * hd;
+    float* qs = sm + attn_smem_floats(G, hd, 1);
+    const float* qsrc = QKV + (size_t)r * ld + (size_t)g * G * hd;
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = qsrc[i];
+    __syncthreads();
+    int jlo, jhi;
+    attn_range(seq, window, 0, 1, &jlo, &jhi);
+    float* res = sm + 4 * G * W;
+    attn_core<EPL, GMAX, KV_NC>(qs, G, hd, R.kc + li * lstride + (size_t)g * R.max_seq * hd,
+                                R.vc + li * lstride + (size_t)g * R.max_seq * hd, hd, jlo, jhi,
+                                scale, softcap, sm, res);
+    const size_t o0 = (size_t)r * nh * hd + (size_t)g * G * hd;
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int gi = i / hd, d = i - gi * hd;
+        const float o = res[gi * W + d] * (1.0f / res[gi * W + hd + 1]);
+        split_f16(o, xh + o0 + i, xl + o0 + i);
+    }
+}
+
+// Per session: soft-capped logits into its buffer, argmax (ties -> lowest,
+// argmax.wgsl), then the generate-loop bookkeeping of its own step
+// (mod.rs:114-122) with sampling and stop tokens as cw_sample.cu applies them.
+__global__ void __launch_bounds__(SMP_THREADS) k_grp_finalize(const GrpRow* __restrict__ rows,
+                                                              const float* __restrict__ logits,
+                                                              int V, float softcap) {
+    __shared__ SmpShared S;
+    __shared__ unsigned long long best[SMP_THREADS / 32];
+    const GrpRow R = rows[blockIdx.x];
+    const float* lr = logits + (size_t)blockIdx.x * V;
+    unsigned long long k = argmax_key_init();
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        float v = lr[i];
+        if (softcap > 0.f) v = softcap * tanhf(v / softcap);
+        R.logits[i] = v;
+        const unsigned long long c = argmax_key(v, (unsigned)i);
+        k = c > k ? c : k;
+    }
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long c = __shfl_xor_sync(0xffffffffu, k, o);
+        k = c > k ? c : k;
+    }
+    if ((threadIdx.x & 31) == 0) best[threadIdx.x >> 5] = k;
+    __syncthreads();
+    k = best[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) k = best[w] > k ? best[w] : k;
+    const unsigned amax = argmax_key_index(k);
+    DevState* st = R.st;
+    const int pos = st->pos;
+    __syncthreads();
+    if (pos + 1 < st->n_prompt) {  // a prompt position: the next input is the next prompt token
+        if (threadIdx.x == 0) {
+            st->token = R.prompt[pos + 1];
+            st->pos = pos + 1;
+        }
+        return;
+    }
+    const SampleParams p = *R.smp;
+    const int np = st->n_produced;
+    const unsigned t = sample_core(S, R.logits, V, p, (unsigned long long)np, amax);
+    if (threadIdx.x == 0) {
+        if (!st->stopped) {
+            bool eos = false;
+            for (unsigned j = 0; j < p.n_eos; j++) eos |= p.eos[j] == t;
+            if (eos) {
+                st->stopped = 1;
+            } else {
+                R.toks[np] = t;
+                st->n_produced = np + 1;
+            }
+        }
+        st->token = t;
+        st->pos = pos + 1;
+    }
+}
+
+struct GrpLayout {
+    size_t H, T, QKV, G, xh, xl, logits, total;
+};
+
+GrpLayout grp_layout(const cw_model* m, size_t B) {
+    const cw_model_info& I = m->info;
+    const size_t qd = (size_t)I.n_heads * I.head_dim, kvd = (size_t)I.n_kv * I.head_dim;
+    const size_t xk = std::max({(size_t)I.dim, qd, (size_t)I.hidden});
+    GrpLayout L{};
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        size_t at = o;
+        o += al256(bytes);
+        return at;
+    };
+    L.H = take(B * I.dim * 4);
+    L.T = take(B * I.dim * 4);
+    L.QKV = take(B * (qd + 2 * kvd) * 4);
+    L.G = take(B * 2 * (size_t)I.hidden * 4);
+    L.xh = take(B * xk * 2);
+    L.xl = take(B * xk * 2);
+    L.logits = take(B * (size_t)I.vocab * 4);
+    L.total = o;
+    return L;
+}
+
+}  // namespace
+
+int model_split_weights(cw_model* m) {
+    if (!m->split.empty()) return CW_OK;
+    cw_ctx* ctx = m->ctx;
+    std::vector<SplitW> out;
+    std::vector<void*> mem;
+    auto add = [&](const QW& w) -> int {
+        SplitW sw;
+        sw.rows = w.rows;
+        sw.K = w.in_f;
+        const size_t n = (size_t)w.rows * w.in_f * 2;
+        void* p = nullptr;
+        CW_CUDA(cudaMalloc(&p, 2 * n));
+        mem.push_back(p);
+        sw.h = p;
+        sw.l = (char*)p + n;
+        CW_TRY(q4_split(ctx, w.payload, w.scales, w.rows, w.in_f, sw.h, sw.l));
+        out.push_back(sw);
+        return CW_OK;
+    };
+    int rc = CW_OK;
+    for (const Layer& l : m->L) {
+        for (const QW* w : {&l.qkv, &l.wo, &l.gate_up, &l.down})
+            if (rc == CW_OK) rc = add(*w);
+    }
+    if (rc == CW_OK) rc = add(m->head);
+    if (rc == CW_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+        rc = set_error(CW_ERR_CUDA, "weight split failed");
+    if (rc != CW_OK) {
+        for (void* p : mem) cudaFree(p);
+        return rc;
+    }
+    m->split = out;
+    m->split_mem = mem;
+    return CW_OK;
+}
+
+}  // namespace cw
+
+struct cw_group {
+    cw_model* m = nullptr;
+    std::vector<cw_session*> ss;
+    cw::GrpRow* rows = nullptr;  // device
+    void* mem = nullptr;         // scratch (GrpLayout)
+    cudaGraphExec_t graph = nullptr;
+};
+
+namespace cw {
+
+static int grp_enqueue(cw_group* g) {
+    cw_model* m = g->m;
+    cw_ctx* ctx = m->ctx;
+    const cw_model_info& I = m->info;
+    const int B = (int)g->ss.size();
+    const int dim = (int)I.dim, nh = (int)I.n_heads, nkv = (int)I.n_kv, hd = (int)I.head_dim;
+    const int qd = nh * hd, kvd = nkv * hd, qkv_rows = qd + 2 * kvd, hid = (int)I.hidden;
+    const bool post = I.post_norms != 0;
+    const int unit = I.norm_kind == 1;
+    const GrpLayout L = grp_layout(m, (size_t)B);
+    uint8_t* b = (uint8_t*)g->mem;
+    float* H = (float*)(b + L.H);
+    float* T = (float*)(b + L.T);
+    float* QKV = (float*)(b + L.QKV);
+    float* Gm = (float*)(b + L.G);
+    float* logits = (float*)(b + L.logits);
+    void *xh = b + L.xh, *xl = b + L.xl;
+    auto gemm = [&](int widx, int K, int N, float* y, const float* bias, int epi) {
+        const SplitW& sw = m->split[widx];
+        return gemm_x3(ctx, xh, xl, sw.h, sw.l, B, N, K, y, N, bias, epi);
+    };
+    const int ew_grid = std::max(1, std::min(B * 8, ctx->sm_count * 8));
+    k_grp_embed<<<B, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, dim, I.embed_scale,
+                                            g->rows, H);
+    CW_TRY(check_launch("group embed"));
+    for (uint32_t li = 0; li < I.n_layers; li++) {
+        const Layer& l = m->L[li];
+        const bool pre_t = post && li > 0;
+        k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, pre_t ? T : nullptr,
+                                                    pre_t ? m->L[li - 1].post_ffw : nullptr,
+                                                    l.attn_norm, unit, I.eps, dim, (__half*)xh,
+                                                    (__half*)xl);
+        CW_TRY(check_launch("group norm"));
+        CW_TRY(gemm(4 * li + 0, dim, qkv_rows, QKV, l.qkv_bias, GE_STORE));
+        k_grp_qk<<<B, 256, 8 * hd * 4, ctx->stream>>>(QKV, qkv_rows, l.q_norm, l.k_norm, I.eps,
+                                                      m->inv_freq, g->rows, (int)li, nh, nkv, hd);
+        CW_TRY(check_launch("group qk"));
+        {
+            const int G = nh / nkv, epl = (hd + 31) / 32;
+            const size_t smem = (attn_smem_floats(G, hd, 1) + (size_t)G * hd) * sizeof(float);
+            const int window = (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
+            const float scale = powf((float)hd, -0.5f);  // attention.rs:18
+            dim3 grid(B, nkv);
+            auto go = [&](auto kern) -> int {
+                if (smem > 48 * 1024)
+                    CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem));
+                kern<<<grid, 128, smem, ctx->stream>>>(QKV, qkv_rows, g->rows, (int)li, nh, nkv,
+                                                        hd, window, scale, I.attn_softcap,
+                                                        (__half*)xh, (__half*)xl);
+                return check_launch("group attention");
+            };
+#define CW_GA(E, GM) CW_TRY(go(k_grp_attn<E, GM>))
+#define CW_GAE(E)                 \
+    if (G <= 1) CW_GA(E, 1);      \
+    else if (G <= 2) CW_GA(E, 2); \
+    else if (G <= 4) CW_GA(E, 4); \
+    else CW_GA(E, 8);
+            if (epl <= 1) { CW_GAE(1) }
+            else if (epl <= 2) { CW_GAE(2) }
+            else if (epl <= 4) { CW_GAE(4) }
+            else { CW_GAE(8) }
+#undef CW_GAE
+#undef CW_GA
+        }
+        CW_TRY(gemm(4 * li + 1, qd, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
+        k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
+                                                    post ? l.post_attn : nullptr, l.ffn_norm, unit,
+                                                    I.eps, dim, (__half*)xh, (__half*)xl);
+        CW_TRY(check_launch("group norm"));
+        CW_TRY(gemm(4 * li + 2, dim, 2 * hid, Gm, nullptr, GE_STORE));
+        k_pf_glu<<<ew_grid, 256, 0, ctx->stream>>>(Gm, hid, I.activation == 1, B, (__half*)xh,
+                                                    (__half*)xl);
+        CW_TRY(check_launch("group glu"));
+        CW_TRY(gemm(4 * li + 3, hid, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
+    }
+    // final norm (post-norm families: the last FFN output folded in first), head, finalize
+    k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
+                                                post ? m->L[I.n_layers - 1].post_ffw : nullptr,
+                                                m->final_norm, unit, I.eps, dim, (__half*)xh,
+                                                (__half*)xl);
+    CW_TRY(check_launch("group final norm"));
+    CW_TRY(gemm(4 * (int)I.n_layers, dim, (int)I.vocab, logits, nullptr, GE_STORE));
+    k_grp_finalize<<<B, SMP_THREADS, 0, ctx->stream>>>(g->rows, logits, (int)I.vocab,
+                                                      I.final_softcap);
+    return check_launch("group finalize");
+}
+
+static int grp_step(cw_group* g) {
+    for (cw_session* s : g->ss)
+        CW_CHECK(s->host_pos < s->max_seq, CW_ERR_INVALID_ARG,
+                 "group step: a session is full (position %zu, max_seq %zu)", s->host_pos,
+                 s->max_seq);
+    cw_ctx* ctx = g->m->ctx;
+    if (!g->graph) {
+        cudaGraph_t gr = nullptr;
+        CW_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = grp_enqueue(g);
+        cudaError_t e = cudaStreamEndCapture(ctx->stream, &gr);
+        if (rc != CW_OK) {
+            if (gr) cudaGraphDestroy(gr);
+            return rc;
+        }
+        if (e != cudaSuccess) return set_error(CW_ERR_CUDA, "group capture: %s", cudaGetErrorString(e));
+        e = cudaGraphInstantiate(&g->graph, gr, 0);
+        cudaGraphDestroy(gr);
+        if (e != cudaSuccess)
+            return set_error(CW_ERR_CUDA, "group instantiate: %s", cudaGetErrorString(e));
+    }
+    CW_CUDA(cudaGraphLaunch(g->graph, ctx->stream));
+    for (cw_session* s : g->ss) {
+        if (s->host_pos + 1 >= s->n_prompt) s->n_produced++;
+        s->host_pos++;
+    }
+    return CW_OK;
+}
+
+static int grp_sync(cw_group* g) {
+    for (cw_session* s : g->ss) CW_TRY(sync_counts(s));
+    return CW_OK;
+}
+
+}  // namespace cw
+
+using namespace cw;
+
+extern "C" {
+
+int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
+    clear_error();
+    CW_CHECK(sessions && out && n > 0 && n <= 1024, CW_ERR_INVALID_ARG,
+             "cw_group_create: 1..1024 sessions");
+    cw_model* m = sessions[0] ? sessions[0]->m : nullptr;
+    CW_CHECK(m, CW_ERR_INVALID_ARG, "cw_group_create: NULL session");
+    for (size_t i = 0; i < n; i++) {
+        CW_CHECK(sessions[i] && sessions[i]->m == m, CW_ERR_INVALID_ARG,
+                 "cw_group_create: sessions must share one model");
+        for (size_t j = 0; j < i; j++)
+            CW_CHECK(sessions[j] != sessions[i], CW_ERR_INVALID_ARG,
+                     "cw_group_create: a session appears twice");
+    }
+    cw_ctx* ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    CW_TRY(model_split_weights(m));
+    cw_group* g = new cw_group();
+    g->m = m;
+    g->ss.assign(sessions, sessions + n);
+    std::vector<GrpRow> h(n);
+    for (size_t i = 0; i < n; i++) {
+        cw_session* s = sessions[i];
+        h[i] = GrpRow{s->st, s->prompt, s->toks, s->logits, (const SampleParams*)s->smp_dev,
+                      s->kc, s->vc, (int)s->max_seq, 0};
+    }
+    int rc = CW_OK;
+    if (cudaMalloc(&g->rows, n * sizeof(GrpRow)) != cudaSuccess ||
+        cudaMalloc(&g->mem, grp_layout(m, n).total) != cudaSuccess)
+        rc = set_error(CW_ERR_OOM, "cw_group_create: device allocation failed");
+    if (rc == CW_OK &&
+        (cudaMemcpyAsync(g->rows, h.data(), n * sizeof(GrpRow), cudaMemcpyHostToDevice,
+                         ctx->stream) != cudaSuccess ||
+         cudaStreamSynchronize(ctx->stream) != cudaSuccess))
+        rc = set_error(CW_ERR_CUDA, "cw_group_create: upload failed");
+    if (rc != CW_OK) {
+        cw_group_free(g);
+        return rc;
+    }
+    *out = g;
+    return CW_OK;
+}
+
+int cw_group_free(cw_group* g) {
+    if (!g) return CW_OK;
+    cudaSetDevice(g->m->ctx->device);
+    cudaStreamSynchronize(g->m->ctx->stream);
+    if (g->graph) cudaGraphExecDestroy(g->graph);
+    if (g->rows) cudaFree(g->rows);
+    if (g->mem) cudaFree(g->mem);
+    delete g;
+    return CW_OK;
+}
+
+int cw_group_run(cw_group* g, size_t n_steps) {
+    clear_error();
+    CW_CHECK(g, CW_ERR_INVALID_ARG, "cw_group_run: group is NULL");
+    for (cw_session* s : g->ss)
+        CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_group_run: a session has not begun");
+    cudaSetDevice(g->m->ctx->device);
+    for (size_t i = 0; i < n_steps; i++) CW_TRY(grp_step(g));
+    CW_TRY(grp_sync(g));
+    return check_device_status(g->m->ctx);
+}
+
+int cw_group_run_timed(cw_group* g, size_t n_steps, double* ms) {
+    clear_error();
+    CW_CHECK(g && ms, CW_ERR_INVALID_ARG, "cw_group_run_timed: bad arguments");
+    cw_ctx* ctx = g->m->ctx;
+    cudaSetDevice(ctx->device);
+    cudaEvent_t e0, e1;
+    CW_CUDA(cudaEventCreate(&e0));
+    CW_CUDA(cudaEventCreate(&e1));
+    int rc = CW_OK;
+    if (!g->graph && n_steps) rc = grp_step(g), n_steps--;  // capture outside the timed region
+    cudaEventRecord(e0, ctx->stream);
+    for (size_t i = 0; i < n_steps && rc == CW_OK; i++) rc = grp_step(g);
+    cudaEventRecord(e1, ctx->stream);
+    cudaEventSynchronize(e1);
+    float f = 0.f;
+    cudaEventElapsedTime(&f, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    CW_TRY(rc);
+    *ms = f;
+    CW_TRY(grp_sync(g));
+    return check_device_status(ctx);
+}
+
+}  // extern "C"

@@ -220,6 +220,39 @@ class Session:
         return int(n.value)
 
 
+class SessionGroup:
+    """Co-batched decode of several sessions of one model (cw_group_*): each
+    step runs every session's next position with one pass over the weights
+    (tensor-core GEMMs over all rows)."""
+
+    def __init__(self, sessions):
+        self.sessions = list(sessions)
+        arr = (C.c_void_p * len(self.sessions))(*[s._h for s in self.sessions])
+        h = C.c_void_p()
+        _lib.call("cw_group_create", arr, len(self.sessions), C.byref(h))
+        self._h = h
+        self.sessions[0].model._sessions.add(self)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.load().cw_group_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def run(self, n_steps: int) -> None:
+        _lib.call("cw_group_run", self._h, int(n_steps))
+
+    def run_timed(self, n_steps: int) -> float:
+        ms = C.c_double()
+        _lib.call("cw_group_run_timed", self._h, int(n_steps), C.byref(ms))
+        return ms.value
+
+
 def generate(model: Model, prompt, max_new: int) -> np.ndarray:
     """model::generate (mod.rs:57-125) through cw_generate: greedy, one token
     read back per step; max_new == 0 still yields one token."""

@@ -260,6 +260,24 @@ int cw_session_prefill(cw_session* s, size_t* n_done);
 /* Copy the K and V cache rows [0, n_pos) of `layer` to the host, each laid
  * out [n_kv][n_pos][head_dim] f32 (cache.rs:7-31 holds the same values). */
 int cw_session_read_kv(cw_session* s, uint32_t layer, size_t n_pos, float* k, float* v);
+/* Co-batched decode (no reference counterpart: its sessions run one at a
+ * time).  A group steps n sessions of one model together: one batched step
+ * runs every session's next position (prompt or decode, each at its own
+ * position with its own KV cache, sampling settings and stop tokens) with
+ * the projections and LM head of all n rows as one tensor-core GEMM each,
+ * so the weights are read once per step for all sessions.  Per session the
+ * result equals its own cw_session_run step within 1e-3 relative.  Uses f16
+ * hi/lo copies of the model's weights (4 bytes per weight, built once per
+ * model by the first group).  Sessions must have begun (cw_session_begin)
+ * and stay owned by the caller; hook taps are not recorded by group steps.
+ * cw_group_run advances every session by n_steps positions. */
+typedef struct cw_group cw_group;
+int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out);
+int cw_group_free(cw_group* g);
+int cw_group_run(cw_group* g, size_t n_steps);
+/* cw_group_run timed with CUDA events on the context stream (the first step
+ * of a new group is captured as a graph and run before the timed region). */
+int cw_group_run_timed(cw_group* g, size_t n_steps, double* ms);
 /* Tokens produced so far (<= cap). */
 int cw_session_tokens(cw_session* s, uint32_t* out, size_t cap, size_t* n);
 /* Logits of the last produced token (vocab floats) and the position count. */
