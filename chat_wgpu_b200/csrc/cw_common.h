@@ -135,8 +135,11 @@ int ensure_counters(cw_ctx* ctx, size_t n);
 
 // cw_gemm.cu: the tcgen05 prefill GEMM, Y[M,N] (=|+=) X[M,K] W[N,K]^T (+bias)
 // over split f16 operands (xh/xl [M,K], wh/wl [N,K]; see cw_gemm.cuh).
+// ws (may be null): workspace for split-K partial tiles when M is small and N
+// has few tiles; the split is chosen to fit ws_bytes.
 int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const void* wl, int M,
-            int N, int K, float* y, int ldy, const float* bias, int epi);
+            int N, int K, float* y, int ldy, const float* bias, int epi, float* ws = nullptr,
+            size_t ws_bytes = 0);
 // Packed Q4_0 [rows, K] -> wh, wl; X f32 [M, K] (row stride ldx) -> xh, xl.
 int q4_split(cw_ctx* ctx, const void* payload, const void* scales, long rows, int K, void* wh,
              void* wl);

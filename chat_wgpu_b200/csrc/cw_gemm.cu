@@ -24,9 +24,18 @@ __global__ void __launch_bounds__(192, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tiles = (a.M + GM_BM - 1) / GM_BM, n_tiles = (a.N + GM_BN - 1) / GM_BN;
     int mt, nt;
-    gm_tile(blockIdx.x, m_tiles, n_tiles, a.group_m, &mt, &nt);
+    const int ks = blockIdx.x % a.ksplit;  // this CTA's K range
+    gm_tile(blockIdx.x / a.ksplit, m_tiles, n_tiles, a.group_m, &mt, &nt);
     const int m0 = mt * GM_BM, n0 = nt * GM_BN;
-    const int KB = (a.K + GM_BK - 1) / GM_BK;
+    const int KB_all = (a.K + GM_BK - 1) / GM_BK;
+    const int per = (KB_all + a.ksplit - 1) / a.ksplit;
+    const int kb0 = min(KB_all, ks * per);
+    const int KB = min(KB_all, kb0 + per) - kb0;  // K steps of this CTA (>= 1 by the host's choice)
+    const bool partial = a.ksplit > 1;
+    float* const ybase = partial ? a.ws + (size_t)ks * a.M * a.N : a.y;
+    const int ldy = partial ? a.N : a.ldy;
+    const float* const bias = partial ? nullptr : a.bias;
+    const int epi = partial ? GE_STORE : a.epi;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < GM_ST; s++) {
@@ -57,7 +66,7 @@ __global__ void __launch_bounds__(192, 1)
                 }
                 uint8_t* st = sm + (size_t)s * GM_STAGE;
                 mbar_expect_tx(&full[s], GM_STAGE);
-                const int kx = kb * GM_BK;
+                const int kx = (kb0 + kb) * GM_BK;
                 tma_load_2d(st, &tXh, kx, m0, &full[s]);
                 tma_load_2d(st + GM_TILE, &tXl, kx, m0, &full[s]);
                 tma_load_2d(st + 2 * GM_TILE, &tWh, kx, n0, &full[s]);
@@ -108,9 +117,9 @@ __global__ void __launch_bounds__(192, 1)
             tmem_ld16(lane_base + GM_BN + c, l);
             tmem_wait_ld();
             if (!ok || row >= a.M) continue;
-            float* yr = a.y + (size_t)row * a.ldy;
+            float* yr = ybase + (size_t)row * ldy;
             const int nb = n0 + c;
-            if (nb + 16 <= a.N && (a.ldy & 3) == 0) {
+            if (nb + 16 <= a.N && (ldy & 3) == 0) {
 #pragma unroll
                 for (int j = 0; j < 16; j += 4) {
                     float r[4];
@@ -118,10 +127,10 @@ __global__ void __launch_bounds__(192, 1)
                     for (int t = 0; t < 4; t++) {
                         r[t] = __uint_as_float(h[j + t]) +
                                __uint_as_float(l[j + t]) * (1.0f / GM_LO);
-                        if (a.bias) r[t] += a.bias[nb + j + t];
+                        if (bias) r[t] += bias[nb + j + t];
                     }
                     float4* dst = (float4*)(yr + nb + j);
-                    if (a.epi == GE_ADD) {
+                    if (epi == GE_ADD) {
                         const float4 o = *dst;
                         r[0] += o.x;
                         r[1] += o.y;
@@ -136,8 +145,8 @@ __global__ void __launch_bounds__(192, 1)
                     if (nb + j >= a.N) continue;
                     float acc =
                         __uint_as_float(h[j]) + __uint_as_float(l[j]) * (1.0f / GM_LO);
-                    if (a.bias) acc += a.bias[nb + j];
-                    if (a.epi == GE_ADD) acc += yr[nb + j];
+                    if (bias) acc += bias[nb + j];
+                    if (epi == GE_ADD) acc += yr[nb + j];
                     yr[nb + j] = acc;
                 }
             }
@@ -148,6 +157,23 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, GM_TMEM_COLS);
+    }
+}
+
+// Split-K: y (=|+=) bias + sum of the ksplit partial tiles, in split order
+// (deterministic).
+__global__ void k_gemm_reduce(const float* __restrict__ ws, int ksplit, int M, int N,
+                              float* __restrict__ y, int ldy, const float* __restrict__ bias,
+                              int epi) {
+    const long n = (long)M * N;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+         i += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / N), c = (int)(i - (long)r * N);
+        float acc = ws[i];
+        for (int k = 1; k < ksplit; k++) acc += ws[(size_t)k * n + i];
+        if (bias) acc += bias[c];
+        float* dst = y + (size_t)r * ldy + c;
+        *dst = epi == GE_ADD ? *dst + acc : acc;
     }
 }
 
@@ -236,7 +262,8 @@ static int tmap_f16(CUtensorMap* map, const void* base, long rows, int K) {
 }
 
 int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const void* wl, int M,
-            int N, int K, float* y, int ldy, const float* bias, int epi) {
+            int N, int K, float* y, int ldy, const float* bias, int epi, float* ws,
+            size_t ws_bytes) {
     CW_CHECK(M > 0 && N > 0 && K > 0 && K % 32 == 0 && ldy >= N, CW_ERR_INVALID_ARG,
              "gemm: bad shape M=%d N=%d K=%d ldy=%d", M, N, K, ldy);
     CUtensorMap m_xh, m_xl, m_wh, m_wl;
@@ -261,8 +288,23 @@ int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const v
     a.group_m = 8;
     a.status = ctx->d_status;
     const int m_tiles = (M + GM_BM - 1) / GM_BM, n_tiles = (N + GM_BN - 1) / GM_BN;
-    k_gemm_x3<<<m_tiles * n_tiles, 192, GM_SMEM, ctx->stream>>>(m_xh, m_xl, m_wh, m_wl, a);
-    return check_launch("gemm_x3");
+    // split K until about two CTAs per SM are busy (each split >= 2 K steps),
+    // as far as the workspace holds the partial tiles
+    const int KB = (K + GM_BK - 1) / GM_BK;
+    int ks = 1;
+    if (ws)
+        while (m_tiles * n_tiles * ks * 2 < 2 * ctx->sm_count && ks * 2 <= KB / 2 && ks < 32 &&
+               (size_t)(ks * 2) * M * N * 4 <= ws_bytes)
+            ks *= 2;
+    a.ksplit = ks;
+    a.ws = ws;
+    k_gemm_x3<<<m_tiles * n_tiles * ks, 192, GM_SMEM, ctx->stream>>>(m_xh, m_xl, m_wh, m_wl, a);
+    CW_TRY(check_launch("gemm_x3"));
+    if (ks == 1) return CW_OK;
+    const long n = (long)M * N;
+    const int grid = (int)std::min<long>((n + 255) / 256, (long)ctx->sm_count * 8);
+    k_gemm_reduce<<<grid, 256, 0, ctx->stream>>>(ws, ks, M, N, y, ldy, bias, epi);
+    return check_launch("gemm split-K reduce");
 }
 
 int q4_split(cw_ctx* ctx, const void* payload, const void* scales, long rows, int K, void* wh,
@@ -320,9 +362,11 @@ int cw_q4_0_gemm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t in_f, size
     ew = &ctx->bufs[w];
     const size_t xbytes = (rows * in_f * 2 + 255) / 256 * 256;
     const size_t wbytes = (out_f * in_f * 2 + 255) / 256 * 256;
+    const size_t wsbytes = 32ull << 20;  // split-K partials (short M)
     uint8_t* sc = nullptr;
-    CW_TRY(gemm_scratch(ctx, 2 * xbytes + 2 * wbytes, &sc));
+    CW_TRY(gemm_scratch(ctx, 2 * xbytes + 2 * wbytes + wsbytes, &sc));
     uint8_t *xh = sc, *xl = sc + xbytes, *wh = sc + 2 * xbytes, *wl = wh + wbytes;
+    float* ws = (float*)(wl + wbytes);
     OpScope scope(ctx, "q4_gemm");
     {
         OpScope s1(ctx, "q4_gemm.split_x");
@@ -335,7 +379,7 @@ int cw_q4_0_gemm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t in_f, size
     }
     OpScope s3(ctx, "q4_gemm.mma");
     return gemm_x3(ctx, xh, xl, wh, wl, (int)rows, (int)out_f, (int)in_f, (float*)ey->ptr,
-                   (int)out_f, nullptr, GE_STORE);
+                   (int)out_f, nullptr, GE_STORE, ws, wsbytes);
 }
 
 }  // extern "C"

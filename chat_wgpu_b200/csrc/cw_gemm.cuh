@@ -53,6 +53,8 @@ struct GemmArgs {
     int epi;              // GE_STORE: y = acc (+bias); GE_ADD: y += acc (+bias)
     int group_m;          // M tiles per raster group (L2 reuse of W tiles)
     int* status;          // device status word
+    int ksplit;           // K ranges per output tile (split-K for short M, few N tiles)
+    float* ws;            // ksplit > 1: partial tiles [ksplit][M][N], summed by k_gemm_reduce
 };
 
 // ---- tcgen05 / TMA primitives ---------------------------------------------------

@@ -401,8 +401,10 @@ __global__ void k_pf_done(DevState* st, const unsigned* __restrict__ prompt, int
 // ===========================================================================
 namespace {
 
+constexpr size_t GEMM_WS_BYTES = 64ull << 20;  // split-K partial tiles of the small-M GEMMs
+
 struct PfLayout {
-    size_t H, T, QKV, G, xh, xl, wh, wl, total;
+    size_t H, T, QKV, G, xh, xl, wh, wl, ws, total;
 };
 
 size_t al256(size_t v) { return (v + 255) / 256 * 256; }
@@ -430,6 +432,7 @@ PfLayout pf_layout(const cw_model* m, size_t C) {
     L.xl = take(C * xk * 2);
     L.wh = take(wmax * 2);
     L.wl = take(wmax * 2);
+    L.ws = take(C <= 256 ? GEMM_WS_BYTES : 0);
     L.total = o;
     return L;
 }
@@ -524,7 +527,8 @@ int pf_chunk(cw_session* s, int p0, int C) {
         }
         widx++;
         stage("prefill.gemm");
-        return gemm_x3(ctx, xh, xl, ph, pl, C, N, K, y, N, bias, epi);
+        return gemm_x3(ctx, xh, xl, ph, pl, C, N, K, y, N, bias, epi, (float*)(b + L.ws),
+                       C <= 256 ? GEMM_WS_BYTES : 0);
     };
     const int ew_grid = std::max(1, std::min(C * 8, ctx->sm_count * 8));
     auto tap = [&](int kind, uint32_t li, const float* src, int ld) {
@@ -823,7 +827,7 @@ __global__ void __launch_bounds__(SMP_THREADS) k_grp_finalize(const GrpRow* __re
 }
 
 struct GrpLayout {
-    size_t H, T, QKV, G, xh, xl, logits, total;
+    size_t H, T, QKV, G, xh, xl, logits, ws, total;
 };
 
 GrpLayout grp_layout(const cw_model* m, size_t B) {
@@ -844,6 +848,7 @@ GrpLayout grp_layout(const cw_model* m, size_t B) {
     L.xh = take(B * xk * 2);
     L.xl = take(B * xk * 2);
     L.logits = take(B * (size_t)I.vocab * 4);
+    L.ws = take(GEMM_WS_BYTES);
     L.total = o;
     return L;
 }
@@ -915,26 +920,37 @@ static int grp_enqueue(cw_group* g) {
     float* Gm = (float*)(b + L.G);
     float* logits = (float*)(b + L.logits);
     void *xh = b + L.xh, *xl = b + L.xl;
+    std::unique_ptr<OpScope> sc;
+    auto stage = [&](const char* name) {
+        sc.reset();
+        if (ctx->profiling) sc.reset(new OpScope(ctx, name));
+    };
     auto gemm = [&](int widx, int K, int N, float* y, const float* bias, int epi) {
         const SplitW& sw = m->split[widx];
-        return gemm_x3(ctx, xh, xl, sw.h, sw.l, B, N, K, y, N, bias, epi);
+        stage(widx == 4 * (int)I.n_layers ? "group.gemm_head" : "group.gemm");
+        return gemm_x3(ctx, xh, xl, sw.h, sw.l, B, N, K, y, N, bias, epi, (float*)(b + L.ws),
+                       GEMM_WS_BYTES);
     };
     const int ew_grid = std::max(1, std::min(B * 8, ctx->sm_count * 8));
+    stage("group.embed");
     k_grp_embed<<<B, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, dim, I.embed_scale,
                                             g->rows, H);
     CW_TRY(check_launch("group embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
         const bool pre_t = post && li > 0;
+        stage("group.norm");
         k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, pre_t ? T : nullptr,
                                                     pre_t ? m->L[li - 1].post_ffw : nullptr,
                                                     l.attn_norm, unit, I.eps, dim, (__half*)xh,
                                                     (__half*)xl);
         CW_TRY(check_launch("group norm"));
         CW_TRY(gemm(4 * li + 0, dim, qkv_rows, QKV, l.qkv_bias, GE_STORE));
+        stage("group.qk");
         k_grp_qk<<<B, 256, 8 * hd * 4, ctx->stream>>>(QKV, qkv_rows, l.q_norm, l.k_norm, I.eps,
                                                       m->inv_freq, g->rows, (int)li, nh, nkv, hd);
         CW_TRY(check_launch("group qk"));
+        stage("group.attn");
         {
             const int G = nh / nkv, epl = (hd + 31) / 32;
             const size_t smem = (attn_smem_floats(G, hd, 1) + (size_t)G * hd) * sizeof(float);
@@ -964,25 +980,30 @@ static int grp_enqueue(cw_group* g) {
 #undef CW_GA
         }
         CW_TRY(gemm(4 * li + 1, qd, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
+        stage("group.norm");
         k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
                                                     post ? l.post_attn : nullptr, l.ffn_norm, unit,
                                                     I.eps, dim, (__half*)xh, (__half*)xl);
         CW_TRY(check_launch("group norm"));
         CW_TRY(gemm(4 * li + 2, dim, 2 * hid, Gm, nullptr, GE_STORE));
+        stage("group.glu");
         k_pf_glu<<<ew_grid, 256, 0, ctx->stream>>>(Gm, hid, I.activation == 1, B, (__half*)xh,
                                                     (__half*)xl);
         CW_TRY(check_launch("group glu"));
         CW_TRY(gemm(4 * li + 3, hid, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
     }
     // final norm (post-norm families: the last FFN output folded in first), head, finalize
+    stage("group.norm");
     k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
                                                 post ? m->L[I.n_layers - 1].post_ffw : nullptr,
                                                 m->final_norm, unit, I.eps, dim, (__half*)xh,
                                                 (__half*)xl);
     CW_TRY(check_launch("group final norm"));
     CW_TRY(gemm(4 * (int)I.n_layers, dim, (int)I.vocab, logits, nullptr, GE_STORE));
+    stage("group.finalize");
     k_grp_finalize<<<B, SMP_THREADS, 0, ctx->stream>>>(g->rows, logits, (int)I.vocab,
                                                       I.final_softcap);
+    sc.reset();
     return check_launch("group finalize");
 }
 
@@ -992,7 +1013,9 @@ static int grp_step(cw_group* g) {
                  "group step: a session is full (position %zu, max_seq %zu)", s->host_pos,
                  s->max_seq);
     cw_ctx* ctx = g->m->ctx;
-    if (!g->graph) {
+    if (ctx->profiling) {  // direct launches, each stage bracketed by profiler events
+        CW_TRY(grp_enqueue(g));
+    } else if (!g->graph) {
         cudaGraph_t gr = nullptr;
         CW_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
         int rc = grp_enqueue(g);
@@ -1007,7 +1030,7 @@ static int grp_step(cw_group* g) {
         if (e != cudaSuccess)
             return set_error(CW_ERR_CUDA, "group instantiate: %s", cudaGetErrorString(e));
     }
-    CW_CUDA(cudaGraphLaunch(g->graph, ctx->stream));
+    if (!ctx->profiling) CW_CUDA(cudaGraphLaunch(g->graph, ctx->stream));
     for (cw_session* s : g->ss) {
         if (s->host_pos + 1 >= s->n_prompt) s->n_produced++;
         s->host_pos++;
