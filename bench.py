@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--model", default="qwen3-0.6b")
     ap.add_argument("--prompt-len", type=int, default=128)
+    ap.add_argument("--sessions", type=int, default=8,
+                    help="co-batched sessions per GPU for the sessions_per_gpu figure (1 = skip)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--per-stage", action="store_true",
@@ -401,6 +403,19 @@ def run_cuda(args, dist):
                    "note": "GEMMs issue three f16 MMAs per K step (hi/lo operand split); "
                            "pipe_frac is against measured burst bf16 TFLOP/s"}
 
+    # ---- co-batched: 8 independent sessions per GPU stepped together
+    # (BASELINE config 3's scaling setup), each after its own prompt
+    group = None
+    if args.sessions > 1:
+        from chat_wgpu_b200.groupbench import bench as group_bench
+        r = group_bench(model, args.sessions, P, K, warmup=W, seed=args.seed)
+        t_max = dist.max(r["ms_per_step"] * K / 1000.0)  # seconds, slowest rank
+        group = {"sessions_per_gpu": args.sessions,
+                 "tok_s": replica_rate(K * args.sessions, dist.world, t_max),
+                 "unit": "tok/s (all GPUs, all sessions)", "ms_per_step": t_max * 1e3 / K,
+                 "positions": r["positions"],
+                 "path": "SessionGroup: one tensor-core pass over the weights per step"}
+
     # ---- e2e: public per-token API with host round trips
     s2 = Session(model, max_seq)
     s2.begin(prompt)
@@ -461,6 +476,7 @@ def run_cuda(args, dist):
                           "roofline_tok_s": peaks["hbm_gbs"] * 1e9 / sb},
         "kernels": per_kernel,
         "prefill": prefill,
+        "sessions_per_gpu": group,
         "clocks": clocks,
     }
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
