@@ -140,6 +140,14 @@ int ensure_counters(cw_ctx* ctx, size_t n);
 int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const void* wl, int M,
             int N, int K, float* y, int ldy, const float* bias, int epi, float* ws = nullptr,
             size_t ws_bytes = 0);
+// The same product with W as packed Q4_0 tile records (q4_tile_pack), the
+// f16 pairs formed in shared memory (0.5625 bytes of W streamed per weight).
+size_t q4_tile_bytes(int rows, int K);
+int q4_tile_pack(cw_ctx* ctx, const void* payload, const void* scales, int rows, int K,
+                 void* out);
+int gemm_q4(cw_ctx* ctx, const void* xh, const void* xl, const void* wpack, int M, int N, int K,
+            float* y, int ldy, const float* bias, int epi, float* ws = nullptr,
+            size_t ws_bytes = 0);
 // Packed Q4_0 [rows, K] -> wh, wl; X f32 [M, K] (row stride ldx) -> xh, xl.
 int q4_split(cw_ctx* ctx, const void* payload, const void* scales, long rows, int K, void* wh,
              void* wl);

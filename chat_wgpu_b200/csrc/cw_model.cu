@@ -967,7 +967,7 @@ int cw_model_free(cw_model* m) {
             m->ctx->bufs.erase(it);
         }
     }
-    for (void* p : m->split_mem) cudaFree(p);
+    for (void* p : m->packed) cudaFree(p);
     delete m;
     return CW_OK;
 }

@@ -42,12 +42,7 @@ struct Layer {
     QW qkv, wo, gate_up, down;
 };
 
-// A Q4_0 weight dequantised once into the f16 hi/lo pair the tensor-core GEMM
-// consumes (cw_gemm.cuh): 4 bytes per weight, kept for the co-batched step.
-struct SplitW {
-    void *h = nullptr, *l = nullptr;
-    int rows = 0, K = 0;
-};
+
 
 struct StepPlan;  // cw_step.cu
 
@@ -75,10 +70,10 @@ struct cw_model {
     std::vector<cw::QW> wo_cm;    // O projections, column-block-major (persistent step)
     std::vector<cw_buf> owned;
     const float* inv_freq = nullptr;
-    // f16 hi/lo copies of every projection and the head (4 per layer, then the
-    // head), built on first use by the co-batched step (cw_prefill.cu)
-    std::vector<cw::SplitW> split;
-    std::vector<void*> split_mem;
+    // every projection and the head (4 per layer: qkv, wo, gate_up, down; then
+    // the head) in the tensor-core GEMM's packed Q4_0 tile records
+    // (cw_gemm.cu), built on first use by prefill or a session group
+    std::vector<void*> packed;
 };
 
 struct cw_session {
@@ -133,8 +128,8 @@ int step_profile(cw_session* s, size_t n_steps,
 // cw_prefill.cu: prompt positions [host_pos, n_prompt - 1) in batched chunks
 // on the tensor cores; advances host_pos and the device state.
 int session_prefill(cw_session* s, size_t* n_done);
-// cw_prefill.cu: the f16 hi/lo weight cache (model->split), idempotent.
-int model_split_weights(cw_model* m);
+// cw_prefill.cu: the packed GEMM copies of the weights (model->packed), idempotent.
+int model_pack_weights(cw_model* m);
 
 const Tap* find_tap(const cw_session* s, int kind, uint32_t layer);
 int sync_counts(cw_session* s);  // host n_produced / stopped from the device state (syncs)

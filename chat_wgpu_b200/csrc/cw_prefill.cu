@@ -414,9 +414,6 @@ PfLayout pf_layout(const cw_model* m, size_t C) {
     const size_t qd = (size_t)I.n_heads * I.head_dim, kvd = (size_t)I.n_kv * I.head_dim;
     const size_t qkv = qd + 2 * kvd;
     const size_t xk = std::max({(size_t)I.dim, qd, (size_t)I.hidden});
-    const size_t wmax =
-        std::max({qkv * I.dim, (size_t)I.dim * qd, 2 * (size_t)I.hidden * I.dim,
-                  (size_t)I.dim * I.hidden});
     PfLayout L{};
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -430,8 +427,10 @@ PfLayout pf_layout(const cw_model* m, size_t C) {
     L.G = take(C * 2 * (size_t)I.hidden * 4);
     L.xh = take(C * xk * 2);
     L.xl = take(C * xk * 2);
-    L.wh = take(wmax * 2);
-    L.wl = take(wmax * 2);
+    const size_t wmax = std::max({qkv * I.dim, (size_t)I.dim * qd, 2 * (size_t)I.hidden * I.dim,
+                                  (size_t)I.dim * I.hidden});
+    L.wh = take(C > 256 ? wmax * 2 : 0);  // f16 pair of one weight (long chunks)
+    L.wl = take(C > 256 ? wmax * 2 : 0);
     L.ws = take(C <= 256 ? GEMM_WS_BYTES : 0);
     L.total = o;
     return L;
@@ -513,22 +512,25 @@ int pf_chunk(cw_session* s, int p0, int C) {
         sc.reset();
         if (ctx->profiling) sc.reset(new OpScope(ctx, name));
     };
-    const bool cached = !m->split.empty();  // f16 pairs built once (co-batched step)
-    int widx = 0;                             // layer-major index into m->split
+    // Long chunks: each weight is split into its f16 pair once per chunk and the
+    // GEMM streams the pair (fastest at large M: the MMA pipe is the bound and
+    // shared memory carries only TMA traffic).  Short chunks (<= 256 rows):
+    // the weights' packed Q4_0 records, dequantised in shared memory.
+    const bool short_chunk = C <= 256;
+    if (short_chunk) CW_TRY(model_pack_weights(m));
+    int widx = 0;  // layer-major index into m->packed
     auto gemm = [&](const QW& w, int K, int N, float* y, const float* bias, int epi) {
-        const void *ph = wh, *pl = wl;
-        if (cached) {
-            const SplitW& sw = m->split[widx];
-            ph = sw.h;
-            pl = sw.l;
-        } else {
-            stage("prefill.split_w");
-            CW_TRY(q4_split(ctx, w.payload, w.scales, N, K, wh, wl));
+        float* ws = (float*)(b + L.ws);
+        if (short_chunk) {
+            stage("prefill.gemm");
+            return gemm_q4(ctx, xh, xl, m->packed[widx++], C, N, K, y, N, bias, epi, ws,
+                           GEMM_WS_BYTES);
         }
         widx++;
+        stage("prefill.split_w");
+        CW_TRY(q4_split(ctx, w.payload, w.scales, N, K, wh, wl));
         stage("prefill.gemm");
-        return gemm_x3(ctx, xh, xl, ph, pl, C, N, K, y, N, bias, epi, (float*)(b + L.ws),
-                       C <= 256 ? GEMM_WS_BYTES : 0);
+        return gemm_x3(ctx, xh, xl, wh, wl, C, N, K, y, N, bias, epi);
     };
     const int ew_grid = std::max(1, std::min(C * 8, ctx->sm_count * 8));
     auto tap = [&](int kind, uint32_t li, const float* src, int ld) {
@@ -855,24 +857,15 @@ GrpLayout grp_layout(const cw_model* m, size_t B) {
 
 }  // namespace
 
-int model_split_weights(cw_model* m) {
-    if (!m->split.empty()) return CW_OK;
+int model_pack_weights(cw_model* m) {
+    if (!m->packed.empty()) return CW_OK;
     cw_ctx* ctx = m->ctx;
-    std::vector<SplitW> out;
-    std::vector<void*> mem;
+    std::vector<void*> out;
     auto add = [&](const QW& w) -> int {
-        SplitW sw;
-        sw.rows = w.rows;
-        sw.K = w.in_f;
-        const size_t n = (size_t)w.rows * w.in_f * 2;
         void* p = nullptr;
-        CW_CUDA(cudaMalloc(&p, 2 * n));
-        mem.push_back(p);
-        sw.h = p;
-        sw.l = (char*)p + n;
-        CW_TRY(q4_split(ctx, w.payload, w.scales, w.rows, w.in_f, sw.h, sw.l));
-        out.push_back(sw);
-        return CW_OK;
+        CW_CUDA(cudaMalloc(&p, q4_tile_bytes(w.rows, w.in_f)));
+        out.push_back(p);
+        return q4_tile_pack(ctx, w.payload, w.scales, w.rows, w.in_f, p);
     };
     int rc = CW_OK;
     for (const Layer& l : m->L) {
@@ -881,13 +874,12 @@ int model_split_weights(cw_model* m) {
     }
     if (rc == CW_OK) rc = add(m->head);
     if (rc == CW_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess)
-        rc = set_error(CW_ERR_CUDA, "weight split failed");
+        rc = set_error(CW_ERR_CUDA, "weight packing failed");
     if (rc != CW_OK) {
-        for (void* p : mem) cudaFree(p);
+        for (void* p : out) cudaFree(p);
         return rc;
     }
-    m->split = out;
-    m->split_mem = mem;
+    m->packed = out;
     return CW_OK;
 }
 
@@ -926,10 +918,9 @@ static int grp_enqueue(cw_group* g) {
         if (ctx->profiling) sc.reset(new OpScope(ctx, name));
     };
     auto gemm = [&](int widx, int K, int N, float* y, const float* bias, int epi) {
-        const SplitW& sw = m->split[widx];
         stage(widx == 4 * (int)I.n_layers ? "group.gemm_head" : "group.gemm");
-        return gemm_x3(ctx, xh, xl, sw.h, sw.l, B, N, K, y, N, bias, epi, (float*)(b + L.ws),
-                       GEMM_WS_BYTES);
+        return gemm_q4(ctx, xh, xl, m->packed[widx], B, N, K, y, N, bias, epi,
+                       (float*)(b + L.ws), GEMM_WS_BYTES);
     };
     const int ew_grid = std::max(1, std::min(B * 8, ctx->sm_count * 8));
     stage("group.embed");
@@ -1064,7 +1055,7 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
     }
     cw_ctx* ctx = m->ctx;
     cudaSetDevice(ctx->device);
-    CW_TRY(model_split_weights(m));
+    CW_TRY(model_pack_weights(m));
     cw_group* g = new cw_group();
     g->m = m;
     g->ss.assign(sessions, sessions + n);

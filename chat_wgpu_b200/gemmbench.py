@@ -45,7 +45,7 @@ def bench(ctx: GpuContext, rows: int, in_f: int, out_f: int, iters: int = 10, se
     return {"rows": rows, "in_f": in_f, "out_f": out_f,
             "us_total": 1e3 * rep.get("q4_gemm", float("nan")),
             "us_split_x": 1e3 * rep.get("q4_gemm.split_x", float("nan")),
-            "us_split_w": 1e3 * rep.get("q4_gemm.split_w", float("nan")),
+            "us_prep_w": 1e3 * rep.get("q4_gemm.prep_w", float("nan")),
             "us_mma": 1e3 * mma_ms,
             "tflops_mma": flops / (mma_ms * 1e-3) / 1e12,
             "tflops_pipe": 3 * flops / (mma_ms * 1e-3) / 1e12,
@@ -69,7 +69,7 @@ def main():
             out.append(r)
             if not a.json:
                 print(f"M={rows:5d} K={in_f:6d} N={out_f:6d}  total {r['us_total']:9.1f} us  "
-                      f"split_x {r['us_split_x']:7.1f}  split_w {r['us_split_w']:7.1f}  "
+                      f"split_x {r['us_split_x']:7.1f}  prep_w {r['us_prep_w']:7.1f}  "
                       f"mma {r['us_mma']:9.1f} us  {r['tflops_mma']:7.1f} TFLOP/s "
                       f"(pipe {r['tflops_pipe']:7.1f})", flush=True)
     if a.json:

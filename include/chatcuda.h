@@ -202,9 +202,10 @@ int cw_q4_0_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_
  * through q4::gemv (q4.rs:9-30, mod.rs:78-83); each output row equals that
  * GEMV of the same x row within 1e-3 relative (f16 hi/lo operand split,
  * three MMAs per K step, f32 accumulation).  X f32 row-major; the result is
- * an arena buffer of rows*out_f f32.  Uses a context-owned scratch of
- * 4*(rows + out_f)*in_f bytes plus 32 MB of split-K partials (grown on
- * demand, which synchronises). */
+ * an arena buffer of rows*out_f f32.  rows <= 256 stream the Q4_0 blocks
+ * (dequantised in shared memory, split-K partials); larger rows stream W's
+ * f16 pair (split once per call).  Uses a context-owned scratch of at most
+ * 4*(rows + out_f)*in_f bytes + 32 MB (grown on demand, which synchronises). */
 int cw_q4_0_gemm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t in_f, size_t out_f,
                  cw_buf* out);
 /* Exact f32 dequantisation of a packed weight (dequant.rs:62-78). */

@@ -60,10 +60,11 @@ def test_prefill_vs_oracle(ctx, orc, models, name):  # noqa: F811
     om.close()
 
 
-@pytest.mark.parametrize("chunk", ["7", "128"])
+@pytest.mark.parametrize("chunk", ["7", "128", "4096"])
 def test_prefill_chunks_long_prompt(ctx, models, monkeypatch, chunk):  # noqa: F811
     """A 300-token prompt in several chunks (the later chunks attend over
-    cache rows the earlier ones wrote) equals the token-by-token steps."""
+    cache rows the earlier ones wrote) equals the token-by-token steps; one
+    299-row chunk takes the long-chunk GEMM path (split weights)."""
     from chat_wgpu_b200.model import Model
     monkeypatch.setenv("CW_PREFILL_CHUNK", chunk)
     m = Model(ctx, models["small-qwen3"])
