@@ -49,3 +49,18 @@ def q4_0_gemm(ctx, x: Buffer, w: Buffer, rows: int, in_f: int, out_f: int) -> Bu
 def q4_0_dequant(ctx, w: Buffer, rows: int, in_f: int) -> Buffer:
     """Exact f32 dequantisation of a packed weight (dequant.rs:62-78)."""
     return op(ctx, "cw_q4_0_dequant", w.handle, int(rows), int(in_f))
+
+
+# ---- GGUF k-quants (raw blocks in HBM) -------------------------------------------
+Q4_K, Q5_K, Q6_K = 12, 13, 14
+KQ_BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
+
+
+def kquant_gemv(ctx, x: Buffer, w: Buffer, qtype: int, in_f: int, out_f: int) -> Buffer:
+    """y[out_f] = W x over raw GGUF Q4_K / Q5_K / Q6_K blocks (cw_storage_bytes)."""
+    return op(ctx, "cw_kquant_gemv", x.handle, w.handle, int(qtype), int(in_f), int(out_f))
+
+
+def kquant_dequant(ctx, w: Buffer, qtype: int, rows: int, in_f: int) -> Buffer:
+    """Exact f32 dequantisation of a raw k-quant weight [rows, in_f]."""
+    return op(ctx, "cw_kquant_dequant", w.handle, int(qtype), int(rows), int(in_f))

@@ -218,6 +218,21 @@ int cw_q4_0_dequant(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out
 int cw_q4_0_gemv_bench(cw_ctx* ctx, cw_buf x, const cw_buf* ws, size_t n_w, size_t in_f,
                        size_t out_f, size_t iters, double* us_per_launch);
 
+/* ---- GGUF k-quants: Q4_K / Q5_K / Q6_K super-blocks of 256 weights --------
+ * The weight is the raw GGUF blocks ([rows][in_f/256] blocks of 144 / 176 /
+ * 210 bytes) uploaded with cw_storage_bytes.  Q6_K dequantises exactly like
+ * dequant_q6_k (dequant.rs:102-131); Q4_K / Q5_K (not implemented by the
+ * reference: dequant.rs:6, ROADMAP.md:52-53) follow ggml's published block
+ * layout.  in_f must be a multiple of 256 (at most 16384 for the GEMV). */
+#define CW_GGUF_Q4_K 12
+#define CW_GGUF_Q5_K 13
+#define CW_GGUF_Q6_K 14
+/* y[out_f] = W x (f32 accumulation). */
+int cw_kquant_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, int type, size_t in_f, size_t out_f,
+                   cw_buf* out);
+/* Exact f32 dequantisation of the [rows, in_f] weight. */
+int cw_kquant_dequant(cw_ctx* ctx, cw_buf w, int type, size_t rows, size_t in_f, cw_buf* out);
+
 /* ---- model: src/model/{mod,qwen3,layers,cache}.rs --------------------------------------------- */
 typedef struct {
     uint32_t dim, n_layers, n_heads, n_kv, head_dim, hidden, vocab;

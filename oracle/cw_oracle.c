@@ -136,6 +136,57 @@ void orc_dequant_q6_k(const uint8_t* b, size_t n, float* out) {
     }
 }
 
+/* GGUF Q4_K / Q5_K (ggml block_q4_K 144 B, block_q5_K 176 B per 256 weights).
+ * The reference does not implement them (dequant.rs:6, ROADMAP.md:52-53);
+ * this restates ggml's published layout: f16 d, f16 dmin, 12 bytes of eight
+ * 6-bit (scale, min) pairs, [Q5_K: 32 bytes of fifth bits,] 128 bytes of
+ * nibbles.  Chunk c (64 weights) uses pair 2c for its low nibbles (weights
+ * 64c .. 64c+31) and 2c+1 for its high nibbles; w = (d*sc)*q - (dmin*m) in
+ * f32, two roundings, no contraction. */
+static void kq_scale_min(int j, const uint8_t* q, int* sc, int* m) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+static void dequant_qk_45(const uint8_t* b, size_t n, float* out, int five) {
+    const size_t bs = five ? 176 : 144;
+    for (size_t blk = 0; blk < n / 256; blk++) {
+        const uint8_t* base = b + blk * bs;
+        const float d = orc_f16_to_f32(rd16(base));
+        const float dmin = orc_f16_to_f32(rd16(base + 2));
+        const uint8_t* scales = base + 4;
+        const uint8_t* qh = five ? base + 16 : NULL;
+        const uint8_t* qs = base + (five ? 48 : 16);
+        float* y = out + blk * 256;
+        for (int c = 0; c < 4; c++) {
+            int sc1, m1, sc2, m2;
+            kq_scale_min(2 * c, scales, &sc1, &m1);
+            kq_scale_min(2 * c + 1, scales, &sc2, &m2);
+            const float d1 = d * (float)sc1, mm1 = dmin * (float)m1;
+            const float d2 = d * (float)sc2, mm2 = dmin * (float)m2;
+            for (int l = 0; l < 32; l++) {
+                int lo = qs[32 * c + l] & 0x0f, hi = qs[32 * c + l] >> 4;
+                if (five) {
+                    lo += ((qh[l] >> (2 * c)) & 1) << 4;
+                    hi += ((qh[l] >> (2 * c + 1)) & 1) << 4;
+                }
+                float t = d1 * (float)lo;
+                y[64 * c + l] = t - mm1;
+                t = d2 * (float)hi;
+                y[64 * c + 32 + l] = t - mm2;
+            }
+        }
+    }
+}
+
+void orc_dequant_q4_k(const uint8_t* b, size_t n, float* out) { dequant_qk_45(b, n, out, 0); }
+void orc_dequant_q5_k(const uint8_t* b, size_t n, float* out) { dequant_qk_45(b, n, out, 1); }
+
 /* ======================================================================== */
 /* q4 re-quantiser and GEMVs                                                 */
 /* ======================================================================== */

@@ -30,6 +30,10 @@ void orc_dequant_q8_0(const uint8_t* b, size_t n, float* out);      /* :46-58  *
 void orc_dequant_q4_0(const uint8_t* b, size_t n, float* out);      /* :62-78  */
 void orc_dequant_q4_1(const uint8_t* b, size_t n, float* out);      /* :82-97  */
 void orc_dequant_q6_k(const uint8_t* b, size_t n, float* out);      /* :102-131 */
+/* Q4_K / Q5_K: not in the reference (dequant.rs:6, ROADMAP.md:52-53); ggml's
+ * published block_q4_K / block_q5_K layout restated (cw_oracle.c). */
+void orc_dequant_q4_k(const uint8_t* b, size_t n, float* out);
+void orc_dequant_q5_k(const uint8_t* b, size_t n, float* out);
 
 /* ---- q4 re-quantiser + GEMVs ------------------------------------------ */
 /* src/kernels/q4.rs:37-60 */

@@ -49,6 +49,8 @@ def lib():
                 "orc_dequant_q4_0": (None, [_u8p, _sz, _f32p]),
                 "orc_dequant_q4_1": (None, [_u8p, _sz, _f32p]),
                 "orc_dequant_q6_k": (None, [_u8p, _sz, _f32p]),
+                "orc_dequant_q4_k": (None, [_u8p, _sz, _f32p]),
+                "orc_dequant_q5_k": (None, [_u8p, _sz, _f32p]),
                 "orc_quantize_q4_0": (None, [_f32p, _sz, _sz, _f32p, _u32p]),
                 "orc_q4_gemv": (None, [_f32p, _f32p, _u32p, _sz, _sz, _f32p]),
                 "orc_q4_0_gemv": (None, [_f32p, _u8p, _sz, _sz, _f32p]),
@@ -130,6 +132,16 @@ def dequant_q4_1(raw, n: int) -> np.ndarray:
 def dequant_q6_k(raw, n: int) -> np.ndarray:
     """src/loader/dequant.rs:102-131"""
     return _deq("orc_dequant_q6_k", raw, n)
+
+
+def dequant_q4_k(raw, n: int) -> np.ndarray:
+    """ggml block_q4_K (not in the reference; ROADMAP.md:52-53)"""
+    return _deq("orc_dequant_q4_k", raw, n)
+
+
+def dequant_q5_k(raw, n: int) -> np.ndarray:
+    """ggml block_q5_K (not in the reference; ROADMAP.md:52-53)"""
+    return _deq("orc_dequant_q5_k", raw, n)
 
 
 def dequant_f16(raw, n: int) -> np.ndarray:

@@ -183,3 +183,23 @@ def test_gguf_minimal_kat(orc, tmp_path):
 
 import sys  # noqa: E402
 sys.path.insert(0, GOLDEN)
+
+
+def test_oracle_q4_k_q5_k_by_construction(orc):
+    """Q4_K / Q5_K (ggml block layout, not in the reference): a block with
+    d = 1, dmin = 0.5, 6-bit (scale, min) pairs (3, 2) for sub-blocks 0-3 and
+    (5, 4) for 4-7, nibbles lo = 1, hi = 2 (and for Q5_K every fifth bit set
+    on sub-block 0 only) dequantises to (d*sc)*q - dmin*m."""
+    b = np.zeros(176, np.uint8)
+    b[0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    b[2:4] = np.frombuffer(np.float16(0.5).tobytes(), np.uint8)
+    b[4:8], b[8:12], b[12:16] = 3, 2, 5 | (4 << 4)
+    q4 = b[:144].copy()
+    q4[16:] = 0x21
+    y = orc.dequant_q4_k(q4, 256)
+    assert (y[0], y[32], y[128], y[160]) == (2.0, 5.0, 3.0, 8.0)
+    q5 = b.copy()
+    q5[16:48] = 0x01            # fifth bit of sub-block 0 (chunk 0, low nibbles)
+    q5[48:] = 0x21
+    y5 = orc.dequant_q5_k(q5, 256)
+    assert y5[0] == 3 * 17 - 1 and y5[32] == 5.0 and y5[64] == 3 * 1 - 1
