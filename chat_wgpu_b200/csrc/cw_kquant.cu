@@ -105,6 +105,131 @@ __device__ __forceinline__ void kq_lane(const uint8_t* __restrict__ blk, int lan
     }
 }
 
+// Raw words one lane needs from a super-block, loaded ahead of the math so
+// several blocks' loads are in flight at once.
+template <int T>
+struct KqRaw {
+    uint32_t v[6];
+};
+
+template <int T>
+__device__ __forceinline__ KqRaw<T> kq_load(const uint8_t* __restrict__ blk, int lane) {
+    KqRaw<T> r;
+    if constexpr (T == CW_GGUF_Q6_K) {  // 210-byte blocks: 2-byte alignment
+        const int h = lane >> 4, l0 = 2 * (lane & 15);
+        const uint16_t* b16 = (const uint16_t*)blk;
+        r.v[0] = __ldg(b16 + (64 * h + l0) / 2);              // ql[l0], ql[l0+1]
+        r.v[1] = __ldg(b16 + (64 * h + 32 + l0) / 2);         // ql[l0+32], ql[l0+33]
+        r.v[2] = __ldg(b16 + (128 + 32 * h + l0) / 2);        // qh[l0], qh[l0+1]
+        r.v[3] = __ldg(b16 + (192 + 8 * h) / 2) | ((uint32_t)__ldg(b16 + (194 + 8 * h) / 2) << 16);
+        r.v[4] = __ldg(b16 + (196 + 8 * h) / 2) | ((uint32_t)__ldg(b16 + (198 + 8 * h) / 2) << 16);
+        r.v[5] = __ldg(b16 + 104);                            // d
+    } else {
+        constexpr bool five = T == CW_GGUF_Q5_K;
+        const uint32_t* b32 = (const uint32_t*)blk;
+        const int c = lane >> 3, j = lane & 7;
+        r.v[0] = __ldg(b32 + 0);  // d, dmin
+        r.v[1] = __ldg(b32 + 1);  // scales 0..3
+        r.v[2] = __ldg(b32 + 2);  // scales 4..7
+        r.v[3] = __ldg(b32 + 3);  // scales 8..11
+        r.v[4] = __ldg(b32 + (five ? 12 : 4) + 8 * c + j);  // 4 nibble bytes
+        r.v[5] = five ? __ldg(b32 + 4 + j) : 0u;            // 4 fifth-bit bytes
+    }
+    return r;
+}
+
+__device__ __forceinline__ float kq_h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu)));
+}
+
+// Partial dot of one lane's 8 weights of a block with x (xb = block's x).
+template <int T>
+__device__ __forceinline__ float kq_dot(const KqRaw<T>& r, const float* __restrict__ xb, int lane,
+                                        float acc) {
+    if constexpr (T == CW_GGUF_Q6_K) {
+        const int h = lane >> 4, l0 = 2 * (lane & 15), is = l0 >> 4;
+        const float d = kq_h2f(r.v[5]);
+        const uint32_t scw = is ? (r.v[3] >> 8) | (r.v[4] << 24) : r.v[3];  // sc[is..is+3]
+        const uint32_t scw2 = is ? (r.v[4] >> 8) : r.v[4];                 // sc[is+4..]
+        const float s0 = (float)(int8_t)(scw & 0xff), s2 = (float)(int8_t)((scw >> 16) & 0xff);
+        const float s4 = (float)(int8_t)(scw2 & 0xff), s6 = (float)(int8_t)((scw2 >> 16) & 0xff);
+        const float ds0 = __fmul_rn(d, s0), ds2 = __fmul_rn(d, s2);
+        const float ds4 = __fmul_rn(d, s4), ds6 = __fmul_rn(d, s6);
+        // per scale, the two weights' q*x first, then one multiply by d*sc
+        float t1 = 0.f, t2 = 0.f, t3 = 0.f, t4 = 0.f;
+        const float* xl = xb + 128 * h + l0;
+        const float2 x1 = *reinterpret_cast<const float2*>(xl);
+        const float2 x2 = *reinterpret_cast<const float2*>(xl + 32);
+        const float2 x3 = *reinterpret_cast<const float2*>(xl + 64);
+        const float2 x4 = *reinterpret_cast<const float2*>(xl + 96);
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int a = (r.v[0] >> (8 * u)) & 0xff, b = (r.v[1] >> (8 * u)) & 0xff;
+            const int hb = (r.v[2] >> (8 * u)) & 0xff;
+            const int q1 = ((a & 0x0f) | ((hb & 3) << 4)) - 32;
+            const int q2 = ((b & 0x0f) | (((hb >> 2) & 3) << 4)) - 32;
+            const int q3 = ((a >> 4) | (((hb >> 4) & 3) << 4)) - 32;
+            const int q4 = ((b >> 4) | (((hb >> 6) & 3) << 4)) - 32;
+            t1 = fmaf((float)q1, u ? x1.y : x1.x, t1);
+            t2 = fmaf((float)q2, u ? x2.y : x2.x, t2);
+            t3 = fmaf((float)q3, u ? x3.y : x3.x, t3);
+            t4 = fmaf((float)q4, u ? x4.y : x4.x, t4);
+        }
+        acc = fmaf(ds0, t1, acc);
+        acc = fmaf(ds2, t2, acc);
+        acc = fmaf(ds4, t3, acc);
+        acc = fmaf(ds6, t4, acc);
+        return acc;
+    } else {
+        // lane j (of each 8) decodes (scale, min) pair j; lane l then takes
+        // pairs 2c, 2c+1 (c = l/8) by shuffle.  The sub-block sum is
+        // d1 * sum(q x) - dmin*m * sum(x), sum(x) per 4 x values from xs4.
+        constexpr bool five = T == CW_GGUF_Q5_K;
+        const int c = lane >> 3, j0 = 4 * (lane & 7), jp = lane & 7;
+        const float d = kq_h2f(r.v[0]), dmin = kq_h2f(r.v[0] >> 16);
+        const uint32_t sw[3] = {r.v[1], r.v[2], r.v[3]};
+        auto byte = [&](int i) { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 0xff); };
+        int sc, m;
+        if (jp < 4) {
+            sc = byte(jp) & 63;
+            m = byte(jp + 4) & 63;
+        } else {
+            sc = (byte(jp + 4) & 0x0f) | ((byte(jp - 4) >> 6) << 4);
+            m = (byte(jp + 4) >> 4) | ((byte(jp) >> 6) << 4);
+        }
+        const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)m);
+        const float d1 = __shfl_sync(0xffffffffu, ds, 2 * c), mm1 = __shfl_sync(0xffffffffu, dm, 2 * c);
+        const float d2 = __shfl_sync(0xffffffffu, ds, 2 * c + 1),
+                    mm2 = __shfl_sync(0xffffffffu, dm, 2 * c + 1);
+        const float* x0 = xb + 64 * c + j0;
+        const float4 xl = *reinterpret_cast<const float4*>(x0);
+        const float4 xh = *reinterpret_cast<const float4*>(x0 + 32);
+        const uint32_t qw = r.v[4];
+        uint32_t lo4 = qw & 0x0f0f0f0fu, hi4 = (qw >> 4) & 0x0f0f0f0fu;
+        if constexpr (five) {
+            const uint32_t hb = r.v[5];
+            lo4 |= ((hb >> (2 * c)) & 0x01010101u) << 4;
+            hi4 |= ((hb >> (2 * c + 1)) & 0x01010101u) << 4;
+        }
+        float ql = (float)(lo4 & 0xff) * xl.x;
+        ql = fmaf((float)((lo4 >> 8) & 0xff), xl.y, ql);
+        ql = fmaf((float)((lo4 >> 16) & 0xff), xl.z, ql);
+        ql = fmaf((float)(lo4 >> 24), xl.w, ql);
+        float qhs = (float)(hi4 & 0xff) * xh.x;
+        qhs = fmaf((float)((hi4 >> 8) & 0xff), xh.y, qhs);
+        qhs = fmaf((float)((hi4 >> 16) & 0xff), xh.z, qhs);
+        qhs = fmaf((float)(hi4 >> 24), xh.w, qhs);
+        const float sxl = (xl.x + xl.y) + (xl.z + xl.w), sxh = (xh.x + xh.y) + (xh.z + xh.w);
+        acc = fmaf(d1, ql, acc);
+        acc = fmaf(-mm1, sxl, acc);
+        acc = fmaf(d2, qhs, acc);
+        acc = fmaf(-mm2, sxh, acc);
+        return acc;
+    }
+}
+
+constexpr int KQ_UNROLL = 4;  // super-blocks whose loads are in flight together
+
 template <int T>
 __global__ void __launch_bounds__(256) k_kq_gemv(const uint8_t* __restrict__ wraw, int K, int N,
                                                  const float* __restrict__ x,
@@ -117,14 +242,15 @@ __global__ void __launch_bounds__(256) k_kq_gemv(const uint8_t* __restrict__ wra
     for (int r = blockIdx.x * 8 + warp; r < N; r += gridDim.x * 8) {
         const uint8_t* row = wraw + (size_t)r * nbk * BYTES;
         float acc = 0.f;
-        for (int b = 0; b < nbk; b++) {
-            float w[8];
-            int idx[8];
-            kq_lane<T>(row + (size_t)b * BYTES, lane, w, idx);
-            const float* xb = xs + 256 * b;
+        int b = 0;
+        for (; b + KQ_UNROLL <= nbk; b += KQ_UNROLL) {
+            KqRaw<T> raw[KQ_UNROLL];
 #pragma unroll
-            for (int i = 0; i < 8; i++) acc = fmaf(w[i], xb[idx[i]], acc);
+            for (int u = 0; u < KQ_UNROLL; u++) raw[u] = kq_load<T>(row + (size_t)(b + u) * BYTES, lane);
+#pragma unroll
+            for (int u = 0; u < KQ_UNROLL; u++) acc = kq_dot<T>(raw[u], xs + 256 * (b + u), lane, acc);
         }
+        for (; b < nbk; b++) acc = kq_dot<T>(kq_load<T>(row + (size_t)b * BYTES, lane), xs + 256 * b, lane, acc);
         acc = warp_sum(acc);
         if (lane == 0) y[r] = acc;
     }

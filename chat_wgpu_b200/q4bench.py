@@ -52,18 +52,57 @@ def bench_shape(ctx: GpuContext, in_f: int, out_f: int, iters: int = 200, seed: 
             "gbs": nbytes / (us.value * 1e-6) / 1e9, "copies": n_w}
 
 
+KQ_TYPES = {"q4_k": (12, 144), "q5_k": (13, 176), "q6_k": (14, 210)}
+
+
+def bench_kquant(ctx: GpuContext, qname: str, in_f: int, out_f: int, iters: int = 50,
+                 seed: int = 0, l2_bytes: int = 126 << 20) -> dict:
+    """k-quant GEMV (cw_kquant_gemv): device time per launch from the context
+    profiler, cycling through copies that exceed 4x L2."""
+    qtype, bb = KQ_TYPES[qname]
+    rng = np.random.default_rng(seed)
+    nb = out_f * (in_f // 256)
+    wbytes = nb * bb
+    raw = rng.integers(0, 256, nb * bb, dtype=np.uint8).reshape(nb, bb)
+    off = 208 if qtype == 14 else 0
+    raw[:, off:off + 2] = rng.uniform(1e-3, 1e-2, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    n_w = max(2, min(64, -(-4 * l2_bytes // wbytes)))
+    ws = [ctx.storage_bytes(raw.ravel()) for _ in range(n_w)]
+    x = ctx.storage(rng.normal(0, 1, in_f).astype(np.float32))
+    for w in ws[:2]:
+        q4.kquant_gemv(ctx, x, w, qtype, in_f, out_f)
+        ctx.reset_frame()
+    ctx.sync()
+    ctx.begin_profile()
+    for i in range(max(iters, n_w)):
+        q4.kquant_gemv(ctx, x, ws[i % n_w], qtype, in_f, out_f)
+        ctx.reset_frame()
+    rep = {name: ms / c for name, c, ms in ctx.report_profile()}
+    for w in ws:
+        w.release()
+    us = 1e3 * rep["kquant_gemv"]
+    nbytes = wbytes + 4 * in_f + 4 * out_f
+    return {"type": qname, "in_f": in_f, "out_f": out_f, "us": us, "bytes": nbytes,
+            "gbs": nbytes / (us * 1e-6) / 1e9}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", action="store_true")
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--shape", default=None, help="one shape as IN_FxOUT_F, e.g. 1024x151936")
+    ap.add_argument("--kquant", choices=sorted(KQ_TYPES), default=None,
+                    help="time the k-quant GEMV of this type instead of Q4_0")
     args = ap.parse_args()
     shapes = SHAPES
     if args.shape:
         k, n = (int(v) for v in args.shape.lower().split("x"))
         shapes = [(k, n)]
     ctx = GpuContext(0)
-    rows = [bench_shape(ctx, k, n, args.iters) for k, n in shapes]
+    if args.kquant:
+        rows = [bench_kquant(ctx, args.kquant, k, n) for k, n in shapes if k % 256 == 0]
+    else:
+        rows = [bench_shape(ctx, k, n, args.iters) for k, n in shapes]
     if args.json:
         print(json.dumps(rows))
     else:
