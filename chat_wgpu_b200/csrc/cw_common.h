@@ -133,13 +133,33 @@ int rope_table(cw_ctx* ctx, uint32_t head_dim, float theta, const float** out);
 // zeroed counters for the attention combine; grows on demand (syncs).
 int ensure_counters(cw_ctx* ctx, size_t n);
 
+// Kernel launch on the context stream, with programmatic stream serialisation
+// when `pdl` (the kernel may start before its predecessor finishes, up to its
+// griddepcontrol.wait).
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(cw_ctx* ctx, bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block,
+                      size_t smem, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    CW_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+    return CW_OK;
+}
+
 // cw_gemm.cu: the tcgen05 prefill GEMM, Y[M,N] (=|+=) X[M,K] W[N,K]^T (+bias)
 // over split f16 operands (xh/xl [M,K], wh/wl [N,K]; see cw_gemm.cuh).
 // ws (may be null): workspace for split-K partial tiles when M is small and N
 // has few tiles; the split is chosen to fit ws_bytes.
 int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const void* wl, int M,
             int N, int K, float* y, int ldy, const float* bias, int epi, float* ws = nullptr,
-            size_t ws_bytes = 0);
+            size_t ws_bytes = 0, bool pdl = false);
 // The same product with W as packed Q4_0 tile records (q4_tile_pack), the
 // f16 pairs formed in shared memory (0.5625 bytes of W streamed per weight).
 size_t q4_tile_bytes(int rows, int K);
@@ -147,7 +167,7 @@ int q4_tile_pack(cw_ctx* ctx, const void* payload, const void* scales, int rows,
                  void* out);
 int gemm_q4(cw_ctx* ctx, const void* xh, const void* xl, const void* wpack, int M, int N, int K,
             float* y, int ldy, const float* bias, int epi, float* ws = nullptr,
-            size_t ws_bytes = 0);
+            size_t ws_bytes = 0, bool pdl = false);
 // Packed Q4_0 [rows, K] -> wh, wl; X f32 [M, K] (row stride ldx) -> xh, xl.
 int q4_split(cw_ctx* ctx, const void* payload, const void* scales, long rows, int K, void* wh,
              void* wl);

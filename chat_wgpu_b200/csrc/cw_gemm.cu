@@ -54,6 +54,9 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    // setup above overlaps the previous kernel (PDL); inputs are read below
+    pdl_trigger();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {  // ---- TMA producer
@@ -165,6 +168,8 @@ __global__ void __launch_bounds__(192, 1)
 __global__ void k_gemm_reduce(const float* __restrict__ ws, int ksplit, int M, int N,
                               float* __restrict__ y, int ldy, const float* __restrict__ bias,
                               int epi) {
+    pdl_trigger();
+    pdl_wait();
     const long n = (long)M * N;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
          i += (long)gridDim.x * blockDim.x) {
@@ -236,9 +241,41 @@ __global__ void k_x_split(const float* __restrict__ x, long M, int K, int ldx,
 // (4096..4607).  Rows past N and blocks past K/32 are zero (they dequantise
 // to 0).  One cp.async.bulk moves a record.
 constexpr int GQ_REC = GM_BN * 32 + GM_BN * 4;  // 4608 bytes
-// Xh, Xl, Wh, Wl, raw record; stages 1024-byte aligned (128-byte swizzle atoms)
-constexpr int GQ_STAGE = (4 * GM_TILE + GQ_REC + 1023) / 1024 * 1024;
-constexpr size_t GQ_SMEM = (size_t)GM_ST * GQ_STAGE + 256 + 1024;
+// Short-M product with the roles swapped: the 128 W rows of a tile are the
+// MMA's M (operand A, dequantised into shared memory) and the M <= 256
+// activation rows its N (operand B, NX = M rounded up to 16), so the tensor
+// work is 128 x NX per K step instead of 128 x 128 -- at a decode batch of 8
+// sessions 1/8 of it.  Two MMA stages (Wh, Wl 16 KB each, Xh, Xl NX*128 B
+// each, 1024-byte aligned) and a deeper ring of raw records, so the weight
+// stream from HBM runs ahead of the dequantisation.
+constexpr int GQ_ST_MAX = 6, GQ_RS_MAX = 16;
+// warp 0 X producer, warp 1 MMA issuer, warps 2-17 dequantise (4 threads per
+// W row, two 8-weight chunks each; warps 2-5 also drain TMEM), warp 18 W producer
+constexpr int GQ_CONV = 512;
+constexpr int GQ_THREADS = 64 + GQ_CONV + 32;
+constexpr int GQ_WPROD = (64 + GQ_CONV) / 32;
+constexpr size_t GQ_SMEM_CAP = 227 * 1024;
+constexpr size_t GQ_FIXED = 1024 + 512;  // alignment slack + barriers
+__host__ __device__ constexpr int gq_stage_bytes(int nx) { return 2 * GM_TILE + 2 * nx * 128; }
+// MMA stages: as many as fit next to an 8-deep raw ring (2..6) -- the MMA
+// completion latency is hidden by the stages in flight, not by MMA work
+__host__ __device__ constexpr int gq_stages(int nx) {
+    return (int)((GQ_SMEM_CAP - GQ_FIXED - 8 * (size_t)GQ_REC) / gq_stage_bytes(nx)) > GQ_ST_MAX
+               ? GQ_ST_MAX
+           : (int)((GQ_SMEM_CAP - GQ_FIXED - 8 * (size_t)GQ_REC) / gq_stage_bytes(nx)) < 2
+               ? 2
+               : (int)((GQ_SMEM_CAP - GQ_FIXED - 8 * (size_t)GQ_REC) / gq_stage_bytes(nx));
+}
+__host__ __device__ constexpr int gq_ring(int nx) {  // raw ring depth that fits
+    return (int)((GQ_SMEM_CAP - GQ_FIXED - (size_t)gq_stages(nx) * gq_stage_bytes(nx)) / GQ_REC) <
+                   GQ_RS_MAX
+               ? (int)((GQ_SMEM_CAP - GQ_FIXED - (size_t)gq_stages(nx) * gq_stage_bytes(nx)) /
+                       GQ_REC)
+               : GQ_RS_MAX;
+}
+__host__ __device__ constexpr size_t gq_smem(int nx) {
+    return (size_t)gq_stages(nx) * gq_stage_bytes(nx) + (size_t)gq_ring(nx) * GQ_REC + GQ_FIXED;
+}
 
 __global__ void k_q4_tile_pack(const uint8_t* __restrict__ payload,
                                const __half* __restrict__ scales, int rows, int K,
@@ -268,8 +305,14 @@ __global__ void k_q4_tile_pack(const uint8_t* __restrict__ payload,
 // 8 weights of one 16-byte chunk: GGUF block byte j holds weight j (low
 // nibble) and j + 16 (high nibble); chunk c of a 64-wide K step covers
 // weights 8c .. 8c+7, i.e. block c/4, sub-range (c%4)*8.
-__device__ __forceinline__ void gq_chunk(const uint2 bytes8, bool high, float d, uint4* hi,
-                                         uint4* lo) {
+// Half2 arithmetic, two weights per instruction: nibble n becomes the f16
+// 1024 + n (exponent bits 0x6400 | n), minus 1032 gives q - 8 exactly;
+// hi = f16(q*d) is one correctly rounded multiply of exact operands, and
+// lo = f16(q*(d*2^12) - hi*2^12) one fused multiply-add of exact operands,
+// i.e. the same pair as rounding (q-8)*d in f32 and its remainder.  Scales
+// with |d| > 1 (where d*2^12 or hi*2^12 could overflow f16) take the f32 path.
+__device__ __forceinline__ void gq_chunk_f32(const uint2 bytes8, bool high, float d, uint4* hi,
+                                             uint4* lo) {
     const uint32_t w2[2] = {bytes8.x, bytes8.y};
     __align__(16) __half hv[8], lv[8];
 #pragma unroll
@@ -285,27 +328,61 @@ __device__ __forceinline__ void gq_chunk(const uint2 bytes8, bool high, float d,
     *lo = *(const uint4*)lv;
 }
 
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+__device__ __forceinline__ void gq_chunk(const uint2 bytes8, bool high, float d, uint4* hi,
+                                         uint4* lo) {
+    if (!(fabsf(d) <= 1.0f)) {
+        gq_chunk_f32(bytes8, high, d, hi, lo);
+        return;
+    }
+    const __half2 d2 = __float2half2_rn(d);                 // exact: d came from an f16
+    const __half2 D2 = __float2half2_rn(d * GM_LO);         // exact: power-of-two scaling
+    const __half2 k12 = __float2half2_rn(GM_LO);
+    const __half2 bias = u32_as_h2(0x64086408u);            // 1032 in both halves
+    uint32_t ho[4], lo_[4];
+#pragma unroll
+    for (int w = 0; w < 2; w++) {
+        const uint32_t v = (w ? bytes8.y : bytes8.x) >> (high ? 4 : 0);
+        const __half2 q02 = __hsub2(u32_as_h2((v & 0x000f000fu) | 0x64006400u), bias);
+        const __half2 q13 = __hsub2(u32_as_h2(((v >> 8) & 0x000f000fu) | 0x64006400u), bias);
+        const __half2 h02 = __hmul2(q02, d2), h13 = __hmul2(q13, d2);
+        const __half2 l02 = __hfma2(q02, D2, __hneg2(__hmul2(h02, k12)));
+        const __half2 l13 = __hfma2(q13, D2, __hneg2(__hmul2(h13, k12)));
+        const uint32_t a = h2_as_u32(h02), b = h2_as_u32(h13);
+        const uint32_t c = h2_as_u32(l02), e = h2_as_u32(l13);
+        ho[2 * w] = __byte_perm(a, b, 0x5410);      // weights 4w, 4w+1
+        ho[2 * w + 1] = __byte_perm(a, b, 0x7632);  // weights 4w+2, 4w+3
+        lo_[2 * w] = __byte_perm(c, e, 0x5410);
+        lo_[2 * w + 1] = __byte_perm(c, e, 0x7632);
+    }
+    *hi = make_uint4(ho[0], ho[1], ho[2], ho[3]);
+    *lo = make_uint4(lo_[0], lo_[1], lo_[2], lo_[3]);
+}
+
 // k_gemm_x3 with W read as packed Q4_0 records: warps 2-5 (one thread per W
 // row) dequantise each stage's record into the swizzled f16 hi/lo tiles the
 // MMA reads (the same values k_q4_split produces), then drain TMEM as the
 // epilogue.  Streams 0.5625 bytes per weight instead of 4.
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GQ_THREADS, 1)
     k_gemm_q4(const __grid_constant__ CUtensorMap tXh, const __grid_constant__ CUtensorMap tXl,
-              const uint8_t* __restrict__ wpack, GemmArgs a) {
+              const uint8_t* __restrict__ wpack, GemmArgs a, int nx) {
     extern __shared__ uint8_t gm_raw[];
     uint8_t* sm = (uint8_t*)(((uintptr_t)gm_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = (uint64_t*)(sm + (size_t)GM_ST * GQ_STAGE);  // X tiles + raw record landed
-    uint64_t* bfull = full + GM_ST;                                // W tiles written
-    uint64_t* empty = bfull + GM_ST;                               // stage consumed by the MMAs
-    uint64_t* done = empty + GM_ST;
+    const int SB = gq_stage_bytes(nx), RS = gq_ring(nx), ST = gq_stages(nx);
+    uint8_t* rings = sm + (size_t)ST * SB;                         // raw records
+    uint64_t* full = (uint64_t*)(rings + (size_t)RS * GQ_REC);     // X tiles landed
+    uint64_t* bfull = full + GQ_ST_MAX;                            // W tiles written
+    uint64_t* empty = bfull + GQ_ST_MAX;                           // stage consumed by the MMAs
+    uint64_t* rfull = empty + GQ_ST_MAX;                           // raw record landed
+    uint64_t* rempty = rfull + GQ_RS_MAX;                          // raw record dequantised
+    uint64_t* done = rempty + GQ_RS_MAX;
     uint32_t* tslot = (uint32_t*)(done + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m_tiles = (a.M + GM_BM - 1) / GM_BM, n_tiles = (a.N + GM_BN - 1) / GM_BN;
-    int mt, nt;
-    const int ks = blockIdx.x % a.ksplit;
-    gm_tile(blockIdx.x / a.ksplit, m_tiles, n_tiles, a.group_m, &mt, &nt);
-    const int m0 = mt * GM_BM, n0 = nt * GM_BN;
+    const int nt = blockIdx.x / a.ksplit, ks = blockIdx.x % a.ksplit;
+    const int n0 = nt * GM_BN;  // W rows of this tile
     const int KB_all = (a.K + GM_BK - 1) / GM_BK;
     const int per = (KB_all + a.ksplit - 1) / a.ksplit;
     const int kb0 = min(KB_all, ks * per);
@@ -316,156 +393,169 @@ __global__ void __launch_bounds__(192, 1)
     const float* const bias = partial ? nullptr : a.bias;
     const int epi = partial ? GE_STORE : a.epi;
     const uint8_t* wtile = wpack + ((size_t)nt * KB_all + kb0) * GQ_REC;
+    // TMEM: two accumulators of nx columns, allocated as a power of two >= 32
+    uint32_t cols = 32;
+    while (cols < 2u * (uint32_t)nx) cols <<= 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < GM_ST; s++) {
+        for (int s = 0; s < ST; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&bfull[s], 128);
+            mbar_init(&bfull[s], GQ_CONV / 32);  // one arrival per converter warp
             mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < RS; r++) {
+            mbar_init(&rfull[r], 1);
+            mbar_init(&rempty[r], GQ_CONV / 32);
         }
         mbar_init(done, 1);
         fence_mbar_init();
         tma_prefetch_desc(&tXh);
         tma_prefetch_desc(&tXl);
     }
-    if (warp == 1) tmem_alloc(tslot, GM_TMEM_COLS);
+    if (warp == 1) tmem_alloc(tslot, cols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-
-    if (warp == 0) {
-        if (lane == 0) {  // ---- TMA / bulk producer
+    // weight records are constant: start streaming them before the
+    // dependency wait, which only the X tiles and the output need
+    if (warp == GQ_WPROD) {
+        if (lane == 0) {  // ---- W record producer
             int kb = 0;
             for (; kb < KB; kb++) {
-                const int s = kb % GM_ST;
-                if (kb >= GM_ST && !mbar_wait(&empty[s], ((kb / GM_ST) - 1) & 1, GM_WAIT_NS)) {
+                const int r = kb % RS;
+                if (kb >= RS && !mbar_wait(&rempty[r], ((kb / RS) - 1) & 1, GM_WAIT_NS)) {
                     gm_fail(a.status);
                     break;
                 }
-                uint8_t* st = sm + (size_t)s * GQ_STAGE;
-                mbar_expect_tx(&full[s], 2 * GM_TILE + GQ_REC);
-                const int kx = (kb0 + kb) * GM_BK;
-                tma_load_2d(st, &tXh, kx, m0, &full[s]);
-                tma_load_2d(st + GM_TILE, &tXl, kx, m0, &full[s]);
-                bulk_g2s(st + 4 * GM_TILE, wtile + (size_t)kb * GQ_REC, GQ_REC, &full[s]);
+                mbar_expect_tx(&rfull[r], GQ_REC);
+                bulk_g2s(rings + (size_t)r * GQ_REC, wtile + (size_t)kb * GQ_REC, GQ_REC, &rfull[r]);
             }
-            for (int j = max(0, kb - GM_ST); j < kb; j++)
-                if (!mbar_wait(&full[j % GM_ST], (j / GM_ST) & 1, GM_WAIT_NS)) gm_fail(a.status);
+            for (int j = max(0, kb - RS); j < kb; j++)
+                if (!mbar_wait(&rfull[j % RS], (j / RS) & 1, GM_WAIT_NS)) gm_fail(a.status);
+        }
+    }
+    pdl_trigger();
+    pdl_wait();
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- X tile producer (TMA), nx rows per tile
+            const unsigned xbytes = 2u * (unsigned)nx * GM_BK * 2u;
+            int kb = 0;
+            for (; kb < KB; kb++) {
+                const int s = kb % ST;
+                if (kb >= ST && !mbar_wait(&empty[s], ((kb / ST) - 1) & 1, GM_WAIT_NS)) {
+                    gm_fail(a.status);
+                    break;
+                }
+                uint8_t* st = sm + (size_t)s * SB + 2 * GM_TILE;
+                mbar_expect_tx(&full[s], xbytes);
+                const int kx = (kb0 + kb) * GM_BK;
+                tma_load_2d(st, &tXh, kx, 0, &full[s]);
+                tma_load_2d(st + nx * 128, &tXl, kx, 0, &full[s]);
+            }
+            for (int j = max(0, kb - ST); j < kb; j++)
+                if (!mbar_wait(&full[j % ST], (j / ST) & 1, GM_WAIT_NS)) gm_fail(a.status);
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // ---- MMA issuer
-            constexpr uint32_t idesc = umma_idesc_f16(GM_BM, GM_BN);
-            const uint32_t acc_hi = tmem, acc_lo = tmem + GM_BN;
+        if (lane == 0) {  // ---- MMA issuer: D[W rows][x rows] += W . X^T
+            const uint32_t idesc = umma_idesc_f16(GM_BN, nx);
+            const uint32_t acc_hi = tmem, acc_lo = tmem + (uint32_t)nx;
             for (int kb = 0; kb < KB; kb++) {
-                const int s = kb % GM_ST;
-                if (!mbar_wait(&full[s], (kb / GM_ST) & 1, GM_WAIT_NS) ||
-                    !mbar_wait(&bfull[s], (kb / GM_ST) & 1, GM_WAIT_NS)) {
+                const int s = kb % ST;
+                if (!mbar_wait(&full[s], (kb / ST) & 1, GM_WAIT_NS) ||
+                    !mbar_wait(&bfull[s], (kb / ST) & 1, GM_WAIT_NS)) {
                     gm_fail(a.status);
                     break;
                 }
                 tc_fence_after();
-                const uint32_t st = smem_addr(sm + (size_t)s * GQ_STAGE);
-                const uint64_t dxh = umma_desc_sw128(st), dxl = umma_desc_sw128(st + GM_TILE);
-                const uint64_t dwh = umma_desc_sw128(st + 2 * GM_TILE),
-                               dwl = umma_desc_sw128(st + 3 * GM_TILE);
+                const uint32_t st = smem_addr(sm + (size_t)s * SB);
+                const uint64_t dwh = umma_desc_sw128(st), dwl = umma_desc_sw128(st + GM_TILE);
+                const uint64_t dxh = umma_desc_sw128(st + 2 * GM_TILE),
+                               dxl = umma_desc_sw128(st + 2 * GM_TILE + nx * 128);
 #pragma unroll
                 for (int k = 0; k < GM_BK / 16; k++) {
                     const uint64_t adv = (uint64_t)(k * 32) >> 4;
                     const uint32_t first = (kb > 0 || k > 0) ? 1u : 0u;
-                    umma_f16(acc_hi, dxh + adv, dwh + adv, idesc, first);
-                    umma_f16(acc_lo, dxh + adv, dwl + adv, idesc, first);
-                    umma_f16(acc_lo, dxl + adv, dwh + adv, idesc, 1u);
+                    umma_f16(acc_hi, dwh + adv, dxh + adv, idesc, first);
+                    umma_f16(acc_lo, dwh + adv, dxl + adv, idesc, first);
+                    umma_f16(acc_lo, dwl + adv, dxh + adv, idesc, 1u);
                 }
                 tc_commit(&empty[s]);
             }
             tc_commit(done);
         }
-    } else {  // ---- warps 2..5: dequantise W records, then the epilogue
-        const int t = threadIdx.x - 64;  // W row within the tile
+    } else if (warp < GQ_WPROD) {  // ---- warps 2..17: dequantise W records; 2..5: epilogue
+        const int t = threadIdx.x - 64;
+        const int row = t & (GM_BN - 1), part = t >> 7;  // W row, chunk pair 2part, 2part+1
         bool ok = true;
         for (int kb = 0; kb < KB && ok; kb++) {
-            const int s = kb % GM_ST;
-            if (!mbar_wait(&full[s], (kb / GM_ST) & 1, GM_WAIT_NS)) {
+            const int s = kb % ST, r = kb % RS;
+            // the raw record has landed and the MMAs are done with this stage's W tiles
+            if (!mbar_wait(&rfull[r], (kb / RS) & 1, GM_WAIT_NS) ||
+                (kb >= ST && !mbar_wait(&empty[s], ((kb / ST) - 1) & 1, GM_WAIT_NS))) {
                 gm_fail(a.status);
                 ok = false;
                 break;
             }
-            uint8_t* st = sm + (size_t)s * GQ_STAGE;
-            const uint8_t* rec = st + 4 * GM_TILE;
-            const uint4 pay0 = *(const uint4*)(rec + t * 32);
-            const uint4 pay1 = *(const uint4*)(rec + t * 32 + 16);
-            const __half2 sc = *(const __half2*)(rec + GM_BN * 32 + t * 4);
-            const float d0 = __low2float(sc), d1 = __high2float(sc);
-            uint8_t* wh = st + 2 * GM_TILE + t * 128;
-            uint8_t* wl = st + 3 * GM_TILE + t * 128;
-            const int sw = t & 7;
+            uint8_t* st = sm + (size_t)s * SB;
+            const uint8_t* rec = rings + (size_t)r * GQ_REC;
+            const uint4 pay = *(const uint4*)(rec + row * 32 + (part >> 1) * 16);
+            const __half2 sc = *(const __half2*)(rec + GM_BN * 32 + row * 4);
+            __syncwarp();  // the warp's record reads are done: one arrival frees the slot
+            if (lane == 0) mbar_arrive(&rempty[r]);
+            const float d = (part >> 1) ? __high2float(sc) : __low2float(sc);
+            uint8_t* wh = st + row * 128;
+            uint8_t* wl = st + GM_TILE + row * 128;
+            const int sw = row & 7;
+            const bool high = part & 1;  // chunks 2, 3 of a block: high nibbles
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                const uint4 pay = c < 4 ? pay0 : pay1;
-                const int sub = c & 3;
-                const uint2 b8 = (sub & 1) ? make_uint2(pay.z, pay.w) : make_uint2(pay.x, pay.y);
+            for (int u = 0; u < 2; u++) {
+                const int c = 2 * part + u;
+                const uint2 b8 = u ? make_uint2(pay.z, pay.w) : make_uint2(pay.x, pay.y);
                 uint4 h, l;
-                gq_chunk(b8, sub >= 2, c < 4 ? d0 : d1, &h, &l);
+                gq_chunk(b8, high, d, &h, &l);
                 *(uint4*)(wh + ((c ^ sw) << 4)) = h;
                 *(uint4*)(wl + ((c ^ sw) << 4)) = l;
             }
             fence_proxy_async();  // generic-proxy stores -> visible to the MMA's async proxy
-            mbar_arrive(&bfull[s]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bfull[s]);  // per warp: 512 thread arrivals serialise
         }
+        if (warp > 5) goto gq_end;
         const bool ok_done = mbar_wait(done, 0, GM_WAIT_NS);
         if (!ok_done) gm_fail(a.status);
         ok = ok && ok_done;
         tc_fence_after();
+        // TMEM lane = W row n, column = activation row m
         const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
+        const int n = n0 + q * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        const float bn = (bias && n < a.N) ? bias[n] : 0.f;
 #pragma unroll 1
-        for (int c = 0; c < GM_BN; c += 16) {
+        for (int c = 0; c < nx; c += 16) {
             uint32_t h[16], l[16];
             tmem_ld16(lane_base + c, h);
-            tmem_ld16(lane_base + GM_BN + c, l);
+            tmem_ld16(lane_base + nx + c, l);
             tmem_wait_ld();
-            if (!ok || row >= a.M) continue;
-            float* yr = ybase + (size_t)row * ldy;
-            const int nb = n0 + c;
-            if (nb + 16 <= a.N && (ldy & 3) == 0) {
+            if (!ok || n >= a.N) continue;
 #pragma unroll
-                for (int j = 0; j < 16; j += 4) {
-                    float r[4];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        r[u] = __uint_as_float(h[j + u]) +
-                               __uint_as_float(l[j + u]) * (1.0f / GM_LO);
-                        if (bias) r[u] += bias[nb + j + u];
-                    }
-                    float4* dst = (float4*)(yr + nb + j);
-                    if (epi == GE_ADD) {
-                        const float4 o = *dst;
-                        r[0] += o.x;
-                        r[1] += o.y;
-                        r[2] += o.z;
-                        r[3] += o.w;
-                    }
-                    *dst = make_float4(r[0], r[1], r[2], r[3]);
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    if (nb + j >= a.N) continue;
-                    float acc = __uint_as_float(h[j]) + __uint_as_float(l[j]) * (1.0f / GM_LO);
-                    if (bias) acc += bias[nb + j];
-                    if (epi == GE_ADD) acc += yr[nb + j];
-                    yr[nb + j] = acc;
-                }
+            for (int j = 0; j < 16; j++) {
+                const int m = c + j;
+                if (m >= a.M) break;
+                float v = __uint_as_float(h[j]) + __uint_as_float(l[j]) * (1.0f / GM_LO) + bn;
+                float* dst = ybase + (size_t)m * ldy + n;
+                if (epi == GE_ADD) v += *dst;
+                *dst = v;
             }
         }
     }
+gq_end:
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, GM_TMEM_COLS);
+        tmem_dealloc(tmem, cols);
     }
 }
 
@@ -485,14 +575,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
 
 // f16 [rows, K] row-major, box 64 (K) x 128 (rows), 128-byte swizzle: the
 // canonical K-major operand layout the MMA descriptors expect.
-static int tmap_f16(CUtensorMap* map, const void* base, long rows, int K) {
+static int tmap_f16(CUtensorMap* map, const void* base, long rows, int K, int box_rows = GM_BM) {
     auto enc = tmap_encode_fn();
     CW_CHECK(enc, CW_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
     CW_CHECK(((uintptr_t)base & 15) == 0 && K % 8 == 0, CW_ERR_INVALID_ARG,
              "gemm operand must be 16-byte aligned with K %% 8 == 0");
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    cuuint32_t box[2] = {(cuuint32_t)GM_BK, (cuuint32_t)GM_BM};
+    cuuint32_t box[2] = {(cuuint32_t)GM_BK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -503,7 +593,7 @@ static int tmap_f16(CUtensorMap* map, const void* base, long rows, int K) {
 
 int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const void* wl, int M,
             int N, int K, float* y, int ldy, const float* bias, int epi, float* ws,
-            size_t ws_bytes) {
+            size_t ws_bytes, bool pdl) {
     CW_CHECK(M > 0 && N > 0 && K > 0 && K % 32 == 0 && ldy >= N, CW_ERR_INVALID_ARG,
              "gemm: bad shape M=%d N=%d K=%d ldy=%d", M, N, K, ldy);
     CUtensorMap m_xh, m_xl, m_wh, m_wl;
@@ -536,14 +626,20 @@ int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const v
         while (m_tiles * n_tiles * ks * 2 < 2 * ctx->sm_count && ks * 2 <= KB / 2 && ks < 32 &&
                (size_t)(ks * 2) * M * N * 4 <= ws_bytes)
             ks *= 2;
+    {  // every split gets at least one K step
+        const int per = (KB + ks - 1) / ks;
+        ks = (KB + per - 1) / per;
+    }
     a.ksplit = ks;
     a.ws = ws;
-    k_gemm_x3<<<m_tiles * n_tiles * ks, 192, GM_SMEM, ctx->stream>>>(m_xh, m_xl, m_wh, m_wl, a);
+    CW_TRY(launch_pdl(ctx, pdl, k_gemm_x3, dim3(m_tiles * n_tiles * ks), dim3(192), GM_SMEM,
+                      m_xh, m_xl, m_wh, m_wl, a));
     CW_TRY(check_launch("gemm_x3"));
     if (ks == 1) return CW_OK;
     const long n = (long)M * N;
     const int grid = (int)std::min<long>((n + 255) / 256, (long)ctx->sm_count * 8);
-    k_gemm_reduce<<<grid, 256, 0, ctx->stream>>>(ws, ks, M, N, y, ldy, bias, epi);
+    CW_TRY(launch_pdl(ctx, pdl, k_gemm_reduce, dim3(grid), dim3(256), 0, (const float*)ws, ks, M,
+                      N, y, ldy, bias, epi));
     return check_launch("gemm split-K reduce");
 }
 
@@ -562,17 +658,20 @@ int q4_tile_pack(cw_ctx* ctx, const void* payload, const void* scales, int rows,
 }
 
 int gemm_q4(cw_ctx* ctx, const void* xh, const void* xl, const void* wpack, int M, int N, int K,
-            float* y, int ldy, const float* bias, int epi, float* ws, size_t ws_bytes) {
+            float* y, int ldy, const float* bias, int epi, float* ws, size_t ws_bytes, bool pdl) {
     CW_CHECK(M > 0 && N > 0 && K > 0 && K % 32 == 0 && ldy >= N, CW_ERR_INVALID_ARG,
              "gemm: bad shape M=%d N=%d K=%d ldy=%d", M, N, K, ldy);
     CW_CHECK(((uintptr_t)wpack & 15) == 0, CW_ERR_INVALID_ARG, "gemm: packed W not 16-byte aligned");
+    CW_CHECK(M <= 256, CW_ERR_INVALID_ARG, "gemm_q4: M=%d above the 256 rows of one tile", M);
+    // the activation rows are the MMA's N: a multiple of 16 (M = 128 shape)
+    const int nx = (M + 15) / 16 * 16;
     CUtensorMap m_xh, m_xl;
-    CW_TRY(tmap_f16(&m_xh, xh, M, K));
-    CW_TRY(tmap_f16(&m_xl, xl, M, K));
+    CW_TRY(tmap_f16(&m_xh, xh, M, K, nx));
+    CW_TRY(tmap_f16(&m_xl, xl, M, K, nx));
     static bool attr_set[64] = {};
     if (!attr_set[ctx->device & 63]) {
         CW_CUDA(cudaFuncSetAttribute(k_gemm_q4, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)GQ_SMEM));
+                                     (int)GQ_SMEM_CAP));
         attr_set[ctx->device & 63] = true;
     }
     GemmArgs a{};
@@ -585,22 +684,27 @@ int gemm_q4(cw_ctx* ctx, const void* xh, const void* xl, const void* wpack, int 
     a.epi = epi;
     a.group_m = 8;
     a.status = ctx->d_status;
-    const int m_tiles = (M + GM_BM - 1) / GM_BM, n_tiles = (N + GM_BN - 1) / GM_BN;
+    const int n_tiles = (N + GM_BN - 1) / GM_BN;
     const int KB = (K + GM_BK - 1) / GM_BK;
     int ks = 1;
     if (ws)
-        while (m_tiles * n_tiles * ks * 2 < 2 * ctx->sm_count && ks * 2 <= KB / 2 && ks < 32 &&
+        while (n_tiles * ks * 2 < 2 * ctx->sm_count && ks * 2 <= KB / 2 && ks < 32 &&
                (size_t)(ks * 2) * M * N * 4 <= ws_bytes)
             ks *= 2;
+    {  // every split gets at least one K step
+        const int per = (KB + ks - 1) / ks;
+        ks = (KB + per - 1) / per;
+    }
     a.ksplit = ks;
     a.ws = ws;
-    k_gemm_q4<<<m_tiles * n_tiles * ks, 192, GQ_SMEM, ctx->stream>>>(
-        m_xh, m_xl, (const uint8_t*)wpack, a);
+    CW_TRY(launch_pdl(ctx, pdl, k_gemm_q4, dim3(n_tiles * ks), dim3(GQ_THREADS), gq_smem(nx),
+                      m_xh, m_xl, (const uint8_t*)wpack, a, nx));
     CW_TRY(check_launch("gemm_q4"));
     if (ks == 1) return CW_OK;
     const long n = (long)M * N;
     const int grid = (int)std::min<long>((n + 255) / 256, (long)ctx->sm_count * 8);
-    k_gemm_reduce<<<grid, 256, 0, ctx->stream>>>(ws, ks, M, N, y, ldy, bias, epi);
+    CW_TRY(launch_pdl(ctx, pdl, k_gemm_reduce, dim3(grid), dim3(256), 0, (const float*)ws, ks, M,
+                      N, y, ldy, bias, epi));
     return check_launch("gemm split-K reduce");
 }
 

@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(256) k_pf_norm(float* __restrict__ H, const fl
                                                  const float* __restrict__ norm_w, int unit,
                                                  float eps, int dim, __half* __restrict__ xh,
                                                  __half* __restrict__ xl) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float hb[];
     __shared__ float red[32];
     const size_t r0 = (size_t)blockIdx.x * dim;
@@ -369,6 +371,8 @@ __global__ void __launch_bounds__(256) k_pf_fattn(const float* __restrict__ QKV,
 // interleaved gate/up GEMM output (column 2i gate_i, 2i+1 up_i).
 __global__ void k_pf_glu(const float* __restrict__ Gm, int I, int geglu, long rows,
                          __half* __restrict__ xh, __half* __restrict__ xl) {
+    pdl_trigger();
+    pdl_wait();
     const long n = rows * (long)I;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
          i += (long)gridDim.x * blockDim.x) {
@@ -677,6 +681,8 @@ struct GrpRow {
 __global__ void k_grp_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
                             int dim, float scale, const GrpRow* __restrict__ rows,
                             float* __restrict__ H) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x, nb = dim / 32;
     const unsigned tok = rows[r].st->token;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
@@ -697,6 +703,8 @@ __global__ void __launch_bounds__(256) k_grp_qk(float* __restrict__ QKV, int ld,
                                                 const float* __restrict__ inv_freq,
                                                 const GrpRow* __restrict__ rows, int li, int nh,
                                                 int nkv, int hd) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float rb[];
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nw = blockDim.x >> 5, half = hd / 2;
@@ -749,6 +757,8 @@ __global__ void __launch_bounds__(128) k_grp_attn(const float* __restrict__ QKV,
                                                   int nkv, int hd, int window, float scale,
                                                   float softcap, __half* __restrict__ xh,
                                                   __half* __restrict__ xl) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float sm[];
     const int r = blockIdx.x, g = blockIdx.y, G = nh / nkv, W = hd + 2;
     const GrpRow R = rows[r];
@@ -778,6 +788,8 @@ __global__ void __launch_bounds__(128) k_grp_attn(const float* __restrict__ QKV,
 __global__ void __launch_bounds__(SMP_THREADS) k_grp_finalize(const GrpRow* __restrict__ rows,
                                                               const float* __restrict__ logits,
                                                               int V, float softcap) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ SmpShared S;
     __shared__ unsigned long long best[SMP_THREADS / 32];
     const GrpRow R = rows[blockIdx.x];
@@ -920,26 +932,27 @@ static int grp_enqueue(cw_group* g) {
     auto gemm = [&](int widx, int K, int N, float* y, const float* bias, int epi) {
         stage(widx == 4 * (int)I.n_layers ? "group.gemm_head" : "group.gemm");
         return gemm_q4(ctx, xh, xl, m->packed[widx], B, N, K, y, N, bias, epi,
-                       (float*)(b + L.ws), GEMM_WS_BYTES);
+                       (float*)(b + L.ws), GEMM_WS_BYTES, true);
     };
     const int ew_grid = std::max(1, std::min(B * 8, ctx->sm_count * 8));
     stage("group.embed");
-    k_grp_embed<<<B, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, dim, I.embed_scale,
-                                            g->rows, H);
+    CW_TRY(launch_pdl(ctx, true, k_grp_embed, dim3(B), dim3(256), 0, m->embed.payload,
+                      m->embed.scales, dim, I.embed_scale, (const GrpRow*)g->rows, H));
     CW_TRY(check_launch("group embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
         const bool pre_t = post && li > 0;
         stage("group.norm");
-        k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, pre_t ? T : nullptr,
+        CW_TRY(launch_pdl(ctx, true, k_pf_norm, dim3(B), dim3(256), (size_t)dim * 4, H, pre_t ? T : nullptr,
                                                     pre_t ? m->L[li - 1].post_ffw : nullptr,
                                                     l.attn_norm, unit, I.eps, dim, (__half*)xh,
-                                                    (__half*)xl);
+                                                    (__half*)xl));
         CW_TRY(check_launch("group norm"));
         CW_TRY(gemm(4 * li + 0, dim, qkv_rows, QKV, l.qkv_bias, GE_STORE));
         stage("group.qk");
-        k_grp_qk<<<B, 256, 8 * hd * 4, ctx->stream>>>(QKV, qkv_rows, l.q_norm, l.k_norm, I.eps,
-                                                      m->inv_freq, g->rows, (int)li, nh, nkv, hd);
+        CW_TRY(launch_pdl(ctx, true, k_grp_qk, dim3(B), dim3(256), (size_t)8 * hd * 4, QKV,
+                          qkv_rows, (const float*)l.q_norm, (const float*)l.k_norm, I.eps,
+                          m->inv_freq, (const GrpRow*)g->rows, (int)li, nh, nkv, hd));
         CW_TRY(check_launch("group qk"));
         stage("group.attn");
         {
@@ -952,9 +965,9 @@ static int grp_enqueue(cw_group* g) {
                 if (smem > 48 * 1024)
                     CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)smem));
-                kern<<<grid, 128, smem, ctx->stream>>>(QKV, qkv_rows, g->rows, (int)li, nh, nkv,
-                                                        hd, window, scale, I.attn_softcap,
-                                                        (__half*)xh, (__half*)xl);
+                CW_TRY(launch_pdl(ctx, true, kern, grid, dim3(128), smem, (const float*)QKV,
+                                  qkv_rows, (const GrpRow*)g->rows, (int)li, nh, nkv, hd, window,
+                                  scale, I.attn_softcap, (__half*)xh, (__half*)xl));
                 return check_launch("group attention");
             };
 #define CW_GA(E, GM) CW_TRY(go(k_grp_attn<E, GM>))
@@ -972,28 +985,29 @@ static int grp_enqueue(cw_group* g) {
         }
         CW_TRY(gemm(4 * li + 1, qd, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
         stage("group.norm");
-        k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
+        CW_TRY(launch_pdl(ctx, true, k_pf_norm, dim3(B), dim3(256), (size_t)dim * 4, H, post ? T : nullptr,
                                                     post ? l.post_attn : nullptr, l.ffn_norm, unit,
-                                                    I.eps, dim, (__half*)xh, (__half*)xl);
+                                                    I.eps, dim, (__half*)xh, (__half*)xl));
         CW_TRY(check_launch("group norm"));
         CW_TRY(gemm(4 * li + 2, dim, 2 * hid, Gm, nullptr, GE_STORE));
         stage("group.glu");
-        k_pf_glu<<<ew_grid, 256, 0, ctx->stream>>>(Gm, hid, I.activation == 1, B, (__half*)xh,
-                                                    (__half*)xl);
+        CW_TRY(launch_pdl(ctx, true, k_pf_glu, dim3(ew_grid), dim3(256), 0, (const float*)Gm, hid,
+                          (int)(I.activation == 1), (long)B, (__half*)xh, (__half*)xl));
         CW_TRY(check_launch("group glu"));
         CW_TRY(gemm(4 * li + 3, hid, dim, post ? T : H, nullptr, post ? GE_STORE : GE_ADD));
     }
     // final norm (post-norm families: the last FFN output folded in first), head, finalize
     stage("group.norm");
-    k_pf_norm<<<B, 256, dim * 4, ctx->stream>>>(H, post ? T : nullptr,
+    CW_TRY(launch_pdl(ctx, true, k_pf_norm, dim3(B), dim3(256), (size_t)dim * 4, H, post ? T : nullptr,
                                                 post ? m->L[I.n_layers - 1].post_ffw : nullptr,
                                                 m->final_norm, unit, I.eps, dim, (__half*)xh,
-                                                (__half*)xl);
+                                                (__half*)xl));
     CW_TRY(check_launch("group final norm"));
     CW_TRY(gemm(4 * (int)I.n_layers, dim, (int)I.vocab, logits, nullptr, GE_STORE));
     stage("group.finalize");
-    k_grp_finalize<<<B, SMP_THREADS, 0, ctx->stream>>>(g->rows, logits, (int)I.vocab,
-                                                      I.final_softcap);
+    CW_TRY(launch_pdl(ctx, true, k_grp_finalize, dim3(B), dim3(SMP_THREADS), 0,
+                      (const GrpRow*)g->rows, (const float*)logits, (int)I.vocab,
+                      I.final_softcap));
     sc.reset();
     return check_launch("group finalize");
 }
