@@ -254,7 +254,7 @@ constexpr int GQ_ST_MAX = 6, GQ_RS_MAX = 16;
 constexpr int GQ_CONV = 512;
 constexpr int GQ_THREADS = 64 + GQ_CONV + 32;
 constexpr int GQ_WPROD = (64 + GQ_CONV) / 32;
-constexpr size_t GQ_SMEM_CAP = 227 * 1024;
+constexpr size_t GQ_SMEM_CAP = 226 * 1024;  // dynamic; the kernel also has static shared memory
 constexpr size_t GQ_FIXED = 1024 + 512;  // alignment slack + barriers
 __host__ __device__ constexpr int gq_stage_bytes(int nx) { return 2 * GM_TILE + 2 * nx * 128; }
 // MMA stages: as many as fit next to an 8-deep raw ring (2..6) -- the MMA
@@ -624,22 +624,22 @@ int gemm_x3(cw_ctx* ctx, const void* xh, const void* xl, const void* wh, const v
     int ks = 1;
     if (ws)
         while (m_tiles * n_tiles * ks * 2 < 2 * ctx->sm_count && ks * 2 <= KB / 2 && ks < 32 &&
-               (size_t)(ks * 2) * M * N * 4 <= ws_bytes)
+               (size_t)(ks * 2) * M * N * 4 + GM_WS_CTR * 4 <= ws_bytes)
             ks *= 2;
     {  // every split gets at least one K step
         const int per = (KB + ks - 1) / ks;
         ks = (KB + per - 1) / per;
     }
     a.ksplit = ks;
-    a.ws = ws;
+    a.ws = ws ? ws + GM_WS_CTR : nullptr;  // workspace layout shared with k_gemm_q4
     CW_TRY(launch_pdl(ctx, pdl, k_gemm_x3, dim3(m_tiles * n_tiles * ks), dim3(192), GM_SMEM,
                       m_xh, m_xl, m_wh, m_wl, a));
     CW_TRY(check_launch("gemm_x3"));
     if (ks == 1) return CW_OK;
     const long n = (long)M * N;
     const int grid = (int)std::min<long>((n + 255) / 256, (long)ctx->sm_count * 8);
-    CW_TRY(launch_pdl(ctx, pdl, k_gemm_reduce, dim3(grid), dim3(256), 0, (const float*)ws, ks, M,
-                      N, y, ldy, bias, epi));
+    CW_TRY(launch_pdl(ctx, pdl, k_gemm_reduce, dim3(grid), dim3(256), 0, (const float*)a.ws, ks,
+                      M, N, y, ldy, bias, epi));
     return check_launch("gemm split-K reduce");
 }
 
@@ -688,23 +688,26 @@ int gemm_q4(cw_ctx* ctx, const void* xh, const void* xl, const void* wpack, int 
     const int KB = (K + GM_BK - 1) / GM_BK;
     int ks = 1;
     if (ws)
-        while (n_tiles * ks * 2 < 2 * ctx->sm_count && ks * 2 <= KB / 2 && ks < 32 &&
-               (size_t)(ks * 2) * M * N * 4 <= ws_bytes)
+        while (n_tiles <= GM_WS_CTR && n_tiles * ks * 2 < 2 * ctx->sm_count &&
+               ks * 2 <= KB / 2 && ks < 32 &&
+               (size_t)(ks * 2) * M * N * 4 + GM_WS_CTR * 4 <= ws_bytes)
             ks *= 2;
     {  // every split gets at least one K step
         const int per = (KB + ks - 1) / ks;
         ks = (KB + per - 1) / per;
     }
     a.ksplit = ks;
-    a.ws = ws;
+    a.ws = ws ? ws + GM_WS_CTR : nullptr;
     CW_TRY(launch_pdl(ctx, pdl, k_gemm_q4, dim3(n_tiles * ks), dim3(GQ_THREADS), gq_smem(nx),
                       m_xh, m_xl, (const uint8_t*)wpack, a, nx));
     CW_TRY(check_launch("gemm_q4"));
     if (ks == 1) return CW_OK;
+    // partial tiles summed in split order (deterministic) by a grid over all of
+    // Y: an in-kernel "last CTA reduces" pass serialises M x ksplit loads per thread
     const long n = (long)M * N;
     const int grid = (int)std::min<long>((n + 255) / 256, (long)ctx->sm_count * 8);
-    CW_TRY(launch_pdl(ctx, pdl, k_gemm_reduce, dim3(grid), dim3(256), 0, (const float*)ws, ks, M,
-                      N, y, ldy, bias, epi));
+    CW_TRY(launch_pdl(ctx, pdl, k_gemm_reduce, dim3(grid), dim3(256), 0, (const float*)a.ws, ks,
+                      M, N, y, ldy, bias, epi));
     return check_launch("gemm split-K reduce");
 }
 
@@ -732,6 +735,7 @@ static int gemm_scratch(cw_ctx* ctx, size_t bytes, uint8_t** p) {
         ctx->gemm_scratch = nullptr;
         ctx->gemm_scratch_bytes = 0;
         CW_CUDA(cudaMalloc(&ctx->gemm_scratch, bytes));
+        CW_CUDA(cudaMemsetAsync(ctx->gemm_scratch, 0, bytes, ctx->stream));  // split-K counters
         ctx->gemm_scratch_bytes = bytes;
     }
     *p = (uint8_t*)ctx->gemm_scratch;
@@ -768,11 +772,13 @@ int cw_q4_0_gemm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t in_f, size
     const size_t xbytes = (rows * in_f * 2 + 255) / 256 * 256;
     const size_t wbytes = big ? 2 * ((out_f * in_f * 2 + 255) / 256 * 256)
                               : (q4_tile_bytes((int)out_f, (int)in_f) + 255) / 256 * 256;
-    const size_t wsbytes = big ? 0 : 32ull << 20;
+    // the split-K workspace (with its self-resetting counters) sits at a fixed
+    // place, the start of the scratch
+    const size_t wsbytes = 32ull << 20;
     uint8_t* sc = nullptr;
-    CW_TRY(gemm_scratch(ctx, 2 * xbytes + wbytes + wsbytes, &sc));
-    uint8_t *xh = sc, *xl = sc + xbytes, *wp = sc + 2 * xbytes;
-    float* ws = (float*)(wp + wbytes);
+    CW_TRY(gemm_scratch(ctx, wsbytes + 2 * xbytes + wbytes, &sc));
+    float* ws = (float*)sc;
+    uint8_t *xh = sc + wsbytes, *xl = xh + xbytes, *wp = xl + xbytes;
     const char* scales = (const char*)ew->ptr + ew->scale_off;
     OpScope scope(ctx, "q4_gemm");
     {

@@ -57,6 +57,9 @@ struct GemmArgs {
     float* ws;            // ksplit > 1: partial tiles [ksplit][M][N], summed by k_gemm_reduce
 };
 
+// Split-K workspaces: GM_WS_CTR words reserved at the start, then the partials.
+constexpr int GM_WS_CTR = 2048;
+
 // ---- tcgen05 / TMA primitives ---------------------------------------------------
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

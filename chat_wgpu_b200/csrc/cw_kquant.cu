@@ -1,234 +1,15 @@
 // cw_kquant.cu -- GEMV and exact dequantisation over GGUF k-quant weights
-// (Q4_K, Q5_K, Q6_K super-blocks of 256 weights), kept in HBM as the raw
-// GGUF blocks.
-//
-// Q6_K follows the reference's dequant_q6_k (src/loader/dequant.rs:102-131):
-// w = (d * sc) * (q - 32), f32, left to right.  Q4_K / Q5_K are not in the
-// reference (dequant.rs:6, ROADMAP.md:52-53); they restate ggml's published
-// block_q4_K / block_q5_K layout: w = (d * sc) * q - (dmin * m).  Each
-// formula is evaluated in the stated order with one f32 rounding per
-// operation (no contraction), so dequantised values are exact to it.
+// kept in HBM as the raw GGUF blocks (formats and device code in
+// cw_kquant.cuh).
 //
 // GEMV: one warp per output row; the 32 lanes split each super-block 8
 // weights apiece (Q4_K/Q5_K lane l: 64-weight chunk l/8, 4 bytes of nibbles
 // at 4*(l%8) -> 4 low-nibble and 4 high-nibble weights; Q6_K lane t: half
 // t/16, weights l, l+1 (l = 2*(t%16)) at offsets 0/32/64/96 of the half),
 // x staged once per CTA in shared memory, f32 accumulation, warp reduction.
-#include <stdint.h>
-
-#include "cw_common.h"
-#include "cw_device.cuh"
+#include "cw_kquant.cuh"
 
 namespace cw {
-
-template <int T>
-struct KQ;
-template <>
-struct KQ<CW_GGUF_Q4_K> {
-    static constexpr int BYTES = 144;
-};
-template <>
-struct KQ<CW_GGUF_Q5_K> {
-    static constexpr int BYTES = 176;
-};
-template <>
-struct KQ<CW_GGUF_Q6_K> {
-    static constexpr int BYTES = 210;
-};
-
-__device__ __forceinline__ float kq_f16(const uint8_t* p) {
-    return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
-}
-
-__device__ __forceinline__ void kq_scale_min(int j, const uint8_t* q, int* sc, int* m) {
-    if (j < 4) {
-        *sc = q[j] & 63;
-        *m = q[j + 4] & 63;
-    } else {
-        *sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
-        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
-    }
-}
-
-// The 8 weights lane `lane` owns in super-block `blk`: values w[8] and their
-// indices within the block idx[8].
-template <int T>
-__device__ __forceinline__ void kq_lane(const uint8_t* __restrict__ blk, int lane, float (&w)[8],
-                                        int (&idx)[8]) {
-    if constexpr (T == CW_GGUF_Q6_K) {
-        const int h = lane >> 4, l0 = 2 * (lane & 15), is = l0 >> 4;
-        const uint8_t* ql = blk + 64 * h;
-        const uint8_t* qh = blk + 128 + 32 * h;
-        const int8_t* sc = (const int8_t*)(blk + 192 + 8 * h);
-        const float d = kq_f16(blk + 208);
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int l = l0 + u;
-            const int a = ql[l], b = ql[l + 32], hb = qh[l];
-            const int q1 = ((a & 0x0f) | (((hb >> 0) & 3) << 4)) - 32;
-            const int q2 = ((b & 0x0f) | (((hb >> 2) & 3) << 4)) - 32;
-            const int q3 = ((a >> 4) | (((hb >> 4) & 3) << 4)) - 32;
-            const int q4 = ((b >> 4) | (((hb >> 6) & 3) << 4)) - 32;
-            w[4 * u + 0] = __fmul_rn(__fmul_rn(d, (float)sc[is + 0]), (float)q1);
-            w[4 * u + 1] = __fmul_rn(__fmul_rn(d, (float)sc[is + 2]), (float)q2);
-            w[4 * u + 2] = __fmul_rn(__fmul_rn(d, (float)sc[is + 4]), (float)q3);
-            w[4 * u + 3] = __fmul_rn(__fmul_rn(d, (float)sc[is + 6]), (float)q4);
-            idx[4 * u + 0] = 128 * h + l;
-            idx[4 * u + 1] = 128 * h + l + 32;
-            idx[4 * u + 2] = 128 * h + l + 64;
-            idx[4 * u + 3] = 128 * h + l + 96;
-        }
-    } else {
-        constexpr bool five = T == CW_GGUF_Q5_K;
-        const int c = lane >> 3, j0 = 4 * (lane & 7);
-        const float d = kq_f16(blk), dmin = kq_f16(blk + 2);
-        const uint8_t* scales = blk + 4;
-        const uint8_t* qs = blk + (five ? 48 : 16) + 32 * c + j0;
-        int sc1, m1, sc2, m2;
-        kq_scale_min(2 * c, scales, &sc1, &m1);
-        kq_scale_min(2 * c + 1, scales, &sc2, &m2);
-        const float d1 = __fmul_rn(d, (float)sc1), mm1 = __fmul_rn(dmin, (float)m1);
-        const float d2 = __fmul_rn(d, (float)sc2), mm2 = __fmul_rn(dmin, (float)m2);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            int lo = qs[i] & 0x0f, hi = qs[i] >> 4;
-            if constexpr (five) {
-                const int hb = blk[16 + j0 + i];
-                lo += ((hb >> (2 * c)) & 1) << 4;
-                hi += ((hb >> (2 * c + 1)) & 1) << 4;
-            }
-            w[i] = __fsub_rn(__fmul_rn(d1, (float)lo), mm1);
-            w[4 + i] = __fsub_rn(__fmul_rn(d2, (float)hi), mm2);
-            idx[i] = 64 * c + j0 + i;
-            idx[4 + i] = 64 * c + 32 + j0 + i;
-        }
-    }
-}
-
-// Raw words one lane needs from a super-block, loaded ahead of the math so
-// several blocks' loads are in flight at once.
-template <int T>
-struct KqRaw {
-    uint32_t v[6];
-};
-
-template <int T>
-__device__ __forceinline__ KqRaw<T> kq_load(const uint8_t* __restrict__ blk, int lane) {
-    KqRaw<T> r;
-    if constexpr (T == CW_GGUF_Q6_K) {  // 210-byte blocks: 2-byte alignment
-        const int h = lane >> 4, l0 = 2 * (lane & 15);
-        const uint16_t* b16 = (const uint16_t*)blk;
-        r.v[0] = __ldg(b16 + (64 * h + l0) / 2);              // ql[l0], ql[l0+1]
-        r.v[1] = __ldg(b16 + (64 * h + 32 + l0) / 2);         // ql[l0+32], ql[l0+33]
-        r.v[2] = __ldg(b16 + (128 + 32 * h + l0) / 2);        // qh[l0], qh[l0+1]
-        r.v[3] = __ldg(b16 + (192 + 8 * h) / 2) | ((uint32_t)__ldg(b16 + (194 + 8 * h) / 2) << 16);
-        r.v[4] = __ldg(b16 + (196 + 8 * h) / 2) | ((uint32_t)__ldg(b16 + (198 + 8 * h) / 2) << 16);
-        r.v[5] = __ldg(b16 + 104);                            // d
-    } else {
-        constexpr bool five = T == CW_GGUF_Q5_K;
-        const uint32_t* b32 = (const uint32_t*)blk;
-        const int c = lane >> 3, j = lane & 7;
-        r.v[0] = __ldg(b32 + 0);  // d, dmin
-        r.v[1] = __ldg(b32 + 1);  // scales 0..3
-        r.v[2] = __ldg(b32 + 2);  // scales 4..7
-        r.v[3] = __ldg(b32 + 3);  // scales 8..11
-        r.v[4] = __ldg(b32 + (five ? 12 : 4) + 8 * c + j);  // 4 nibble bytes
-        r.v[5] = five ? __ldg(b32 + 4 + j) : 0u;            // 4 fifth-bit bytes
-    }
-    return r;
-}
-
-__device__ __forceinline__ float kq_h2f(uint32_t bits16) {
-    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu)));
-}
-
-// Partial dot of one lane's 8 weights of a block with x (xb = block's x).
-template <int T>
-__device__ __forceinline__ float kq_dot(const KqRaw<T>& r, const float* __restrict__ xb, int lane,
-                                        float acc) {
-    if constexpr (T == CW_GGUF_Q6_K) {
-        const int h = lane >> 4, l0 = 2 * (lane & 15), is = l0 >> 4;
-        const float d = kq_h2f(r.v[5]);
-        const uint32_t scw = is ? (r.v[3] >> 8) | (r.v[4] << 24) : r.v[3];  // sc[is..is+3]
-        const uint32_t scw2 = is ? (r.v[4] >> 8) : r.v[4];                 // sc[is+4..]
-        const float s0 = (float)(int8_t)(scw & 0xff), s2 = (float)(int8_t)((scw >> 16) & 0xff);
-        const float s4 = (float)(int8_t)(scw2 & 0xff), s6 = (float)(int8_t)((scw2 >> 16) & 0xff);
-        const float ds0 = __fmul_rn(d, s0), ds2 = __fmul_rn(d, s2);
-        const float ds4 = __fmul_rn(d, s4), ds6 = __fmul_rn(d, s6);
-        // per scale, the two weights' q*x first, then one multiply by d*sc
-        float t1 = 0.f, t2 = 0.f, t3 = 0.f, t4 = 0.f;
-        const float* xl = xb + 128 * h + l0;
-        const float2 x1 = *reinterpret_cast<const float2*>(xl);
-        const float2 x2 = *reinterpret_cast<const float2*>(xl + 32);
-        const float2 x3 = *reinterpret_cast<const float2*>(xl + 64);
-        const float2 x4 = *reinterpret_cast<const float2*>(xl + 96);
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int a = (r.v[0] >> (8 * u)) & 0xff, b = (r.v[1] >> (8 * u)) & 0xff;
-            const int hb = (r.v[2] >> (8 * u)) & 0xff;
-            const int q1 = ((a & 0x0f) | ((hb & 3) << 4)) - 32;
-            const int q2 = ((b & 0x0f) | (((hb >> 2) & 3) << 4)) - 32;
-            const int q3 = ((a >> 4) | (((hb >> 4) & 3) << 4)) - 32;
-            const int q4 = ((b >> 4) | (((hb >> 6) & 3) << 4)) - 32;
-            t1 = fmaf((float)q1, u ? x1.y : x1.x, t1);
-            t2 = fmaf((float)q2, u ? x2.y : x2.x, t2);
-            t3 = fmaf((float)q3, u ? x3.y : x3.x, t3);
-            t4 = fmaf((float)q4, u ? x4.y : x4.x, t4);
-        }
-        acc = fmaf(ds0, t1, acc);
-        acc = fmaf(ds2, t2, acc);
-        acc = fmaf(ds4, t3, acc);
-        acc = fmaf(ds6, t4, acc);
-        return acc;
-    } else {
-        // lane j (of each 8) decodes (scale, min) pair j; lane l then takes
-        // pairs 2c, 2c+1 (c = l/8) by shuffle.  The sub-block sum is
-        // d1 * sum(q x) - dmin*m * sum(x), sum(x) per 4 x values from xs4.
-        constexpr bool five = T == CW_GGUF_Q5_K;
-        const int c = lane >> 3, j0 = 4 * (lane & 7), jp = lane & 7;
-        const float d = kq_h2f(r.v[0]), dmin = kq_h2f(r.v[0] >> 16);
-        const uint32_t sw[3] = {r.v[1], r.v[2], r.v[3]};
-        auto byte = [&](int i) { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 0xff); };
-        int sc, m;
-        if (jp < 4) {
-            sc = byte(jp) & 63;
-            m = byte(jp + 4) & 63;
-        } else {
-            sc = (byte(jp + 4) & 0x0f) | ((byte(jp - 4) >> 6) << 4);
-            m = (byte(jp + 4) >> 4) | ((byte(jp) >> 6) << 4);
-        }
-        const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)m);
-        const float d1 = __shfl_sync(0xffffffffu, ds, 2 * c), mm1 = __shfl_sync(0xffffffffu, dm, 2 * c);
-        const float d2 = __shfl_sync(0xffffffffu, ds, 2 * c + 1),
-                    mm2 = __shfl_sync(0xffffffffu, dm, 2 * c + 1);
-        const float* x0 = xb + 64 * c + j0;
-        const float4 xl = *reinterpret_cast<const float4*>(x0);
-        const float4 xh = *reinterpret_cast<const float4*>(x0 + 32);
-        const uint32_t qw = r.v[4];
-        uint32_t lo4 = qw & 0x0f0f0f0fu, hi4 = (qw >> 4) & 0x0f0f0f0fu;
-        if constexpr (five) {
-            const uint32_t hb = r.v[5];
-            lo4 |= ((hb >> (2 * c)) & 0x01010101u) << 4;
-            hi4 |= ((hb >> (2 * c + 1)) & 0x01010101u) << 4;
-        }
-        float ql = (float)(lo4 & 0xff) * xl.x;
-        ql = fmaf((float)((lo4 >> 8) & 0xff), xl.y, ql);
-        ql = fmaf((float)((lo4 >> 16) & 0xff), xl.z, ql);
-        ql = fmaf((float)(lo4 >> 24), xl.w, ql);
-        float qhs = (float)(hi4 & 0xff) * xh.x;
-        qhs = fmaf((float)((hi4 >> 8) & 0xff), xh.y, qhs);
-        qhs = fmaf((float)((hi4 >> 16) & 0xff), xh.z, qhs);
-        qhs = fmaf((float)(hi4 >> 24), xh.w, qhs);
-        const float sxl = (xl.x + xl.y) + (xl.z + xl.w), sxh = (xh.x + xh.y) + (xh.z + xh.w);
-        acc = fmaf(d1, ql, acc);
-        acc = fmaf(-mm1, sxl, acc);
-        acc = fmaf(d2, qhs, acc);
-        acc = fmaf(-mm2, sxh, acc);
-        return acc;
-    }
-}
-
-constexpr int KQ_UNROLL = 4;  // super-blocks whose loads are in flight together
 
 template <int T>
 __global__ void __launch_bounds__(256) k_kq_gemv(const uint8_t* __restrict__ wraw, int K, int N,

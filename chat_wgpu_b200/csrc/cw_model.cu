@@ -32,6 +32,7 @@
 #include "cw_device.cuh"
 #include "cw_gemv.cuh"
 #include "cw_gguf.h"
+#include "cw_kquant.cuh"
 #include "cw_ops.h"
 #include "cw_model.h"
 #include "cw_q4.h"
@@ -299,20 +300,79 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
 // ---- embed / finalize ------------------------------------------------------
 // qwen3.rs:128-133: row `token` of token_embd, exact Q4_0 dequantisation.
 __global__ void k_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
-                        int dim, float scale, const DevState* __restrict__ st,
+                        int type, int dim, float scale, const DevState* __restrict__ st,
                         float* __restrict__ hidden) {
     pdl_trigger();
     pdl_wait();
-    const int nb = dim / 32;
     const unsigned tok = st->token;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-        int b = i >> 5, j = i & 31;
-        size_t blk = (size_t)tok * nb + b;
-        float d = __half2float(scales[blk]);
-        uint8_t byte = payload[blk * 16 + (j & 15)];
-        int q = (j < 16) ? (byte & 0xf) : (byte >> 4);
-        float v = __fmul_rn(d, (float)(q - 8));
+        const float v = embed_elem(payload, scales, type, tok, dim, i);
         hidden[i] = scale > 0.f ? __fmul_rn(v, scale) : v;
+    }
+}
+
+// LM head over a Q6_K table (real Q4_0 checkpoints often keep it Q6_K):
+// x = rmsnorm(h) (h = base, or base + post-normed delta) into shared memory
+// by every CTA (CTA 0 also writes xn_out), then one warp per row
+// (kq_dot<Q6_K>), soft-cap, logits, and the argmax key (atomicMax, ties ->
+// lowest index) -- the EPI_HEAD epilogue of the Q4_0 head.
+__global__ void __launch_bounds__(256) k_head_q6k(FArgs a) {
+    extern __shared__ float xs[];
+    __shared__ float red[32];
+    __shared__ unsigned long long red_key[8];
+    const int K = a.K, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
+    float inv_d = 0.f;
+    if (a.delta && a.post_w) {
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(a.delta[i], a.delta[i], ss);
+        ss = cta_sum(ss, red);
+        inv_d = 1.0f / sqrtf(ss / (float)K + a.eps);
+    }
+    float ssh = 0.f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        float h = a.base[i];
+        if (a.delta) {
+            float dv = a.delta[i];
+            if (a.post_w) {
+                const float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
+                dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
+            }
+            h = h + dv;
+        }
+        xs[i] = h;
+        ssh = fmaf(h, h, ssh);
+    }
+    ssh = cta_sum(ssh, red);
+    const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const float gw = a.unit ? 1.0f + a.norm_w[i] : a.norm_w[i];
+        const float v = __fmul_rn(__fmul_rn(xs[i], inv), gw);
+        xs[i] = v;
+        if (a.xn_out && blockIdx.x == 0) a.xn_out[i] = v;
+    }
+    __syncthreads();
+    const int nbk = K / 256;
+    unsigned long long best = argmax_key_init();
+    for (int r = blockIdx.x * 8 + warp; r < a.N; r += gridDim.x * 8) {
+        const uint8_t* row = a.payload + (size_t)r * nbk * 210;
+        float acc = 0.f;
+        for (int b = 0; b < nbk; b++)
+            acc = kq_dot<CW_GGUF_Q6_K>(kq_load<CW_GGUF_Q6_K>(row + (size_t)b * 210, lane),
+                                       xs + 256 * b, lane, acc);
+        acc = warp_sum(acc);
+        if (a.softcap > 0.f) acc = a.softcap * tanhf(acc / a.softcap);
+        if (lane == 0) a.y[r] = acc;
+        const unsigned long long k = argmax_key(acc, (unsigned)r);
+        best = k > best ? k : best;
+    }
+    if (lane == 0) red_key[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = red_key[w] > best ? red_key[w] : best;
+        best = red_key[0] > best ? red_key[0] : best;
+        atomicMax(a.key, best);
     }
 }
 
@@ -526,6 +586,34 @@ static int load_vec(cw_model* m, const GgufFile& f, const std::string& name, siz
 
 // Load one or more Q4_0 [rows_i, in_f] tensors as a single packed weight.
 // interleave: two parts with equal rows become rows p0[0], p1[0], p0[1], ...
+// A token embedding or LM head stored as GGUF Q6_K (real Q4_0 checkpoints often
+// keep these in Q6_K): the raw super-blocks go to HBM unchanged.
+static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out) {
+    CW_CHECK(in_f % 256 == 0, CW_ERR_UNSUPPORTED,
+             "tensor %s is Q6_K: its rows (%zu) must be a multiple of 256", t->name.c_str(), in_f);
+    CW_CHECK(!t->dims.empty() && t->dims[0] == in_f && t->n_elems % in_f == 0, CW_ERR_FORMAT,
+             "tensor %s: inner dimension %llu, expected %zu", t->name.c_str(),
+             (unsigned long long)(t->dims.empty() ? 0 : t->dims[0]), in_f);
+    const size_t rows = t->n_elems / in_f;
+    CW_CHECK(t->nbytes == rows * (in_f / 256) * 210, CW_ERR_FORMAT, "tensor %s: %zu bytes",
+             t->name.c_str(), t->nbytes);
+    void* p = nullptr;
+    CW_TRY(dev_alloc(m, t->nbytes, &p));
+    CW_CUDA(cudaMemcpyAsync(p, t->data, t->nbytes, cudaMemcpyHostToDevice, m->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    out->payload = (const uint8_t*)p;
+    out->scales = nullptr;
+    out->rows = (int)rows;
+    out->in_f = (int)in_f;
+    out->type = GGML_Q6_K;
+    out->buf = m->owned.back();
+    return CW_OK;
+}
+
+// Q4_0 (packed planes) or Q6_K (raw), by the tensor's type.
+static int load_q4_or_q6k(cw_model* m, const GgufFile& f, const std::string& name, size_t in_f,
+                          QW* out);
+
 static int load_q4(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
                    size_t in_f, bool interleave, QW* out) {
     std::vector<const GgufTensor*> parts;
@@ -589,6 +677,14 @@ static int load_q4(cw_model* m, const GgufFile& f, const std::vector<std::string
     out->buf = b;
     m->info.weight_bytes += rows * rb;
     return CW_OK;
+}
+
+static int load_q4_or_q6k(cw_model* m, const GgufFile& f, const std::string& name, size_t in_f,
+                          QW* out) {
+    const GgufTensor* t = f.tensor(name);
+    CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", name.c_str());
+    if (t->type == GGML_Q6_K) return load_q6k(m, t, in_f, out);
+    return load_q4(m, f, {name}, in_f, false, out);
 }
 
 static int model_load(cw_model* m, const std::string& path) {
@@ -679,11 +775,11 @@ static int model_load(cw_model* m, const std::string& path) {
         }
     }
     CW_TRY(load_vec(m, f, "output_norm.weight", I.dim, &m->final_norm));
-    CW_TRY(load_q4(m, f, {"token_embd.weight"}, I.dim, false, &m->embed));
+    CW_TRY(load_q4_or_q6k(m, f, "token_embd.weight", I.dim, &m->embed));
     CW_CHECK(m->embed.rows == (int)I.vocab, CW_ERR_FORMAT, "token_embd has %d rows, vocab %u",
              m->embed.rows, I.vocab);
     if (f.has("output.weight")) {  // untied head; tied otherwise (qwen3.rs:93-98)
-        CW_TRY(load_q4(m, f, {"output.weight"}, I.dim, false, &m->head));
+        CW_TRY(load_q4_or_q6k(m, f, "output.weight", I.dim, &m->head));
     } else {
         m->head = m->embed;
     }
@@ -750,7 +846,8 @@ static int enqueue_step_core(cw_session* s, bool decode) {
     };
     stage("embed");
     CW_TRY(launch_k(ctx, k_embed, dim3(1), dim3(256), 0, m->embed.payload, m->embed.scales,
-                    (int)I.dim, I.embed_scale, (const DevState*)s->st, s->hidden));
+                    m->embed.type, (int)I.dim, I.embed_scale, (const DevState*)s->st,
+                    s->hidden));
     CW_TRY(check_launch("embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         stage("attn_in");
@@ -872,7 +969,17 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         h.y = s->logits;
         h.softcap = I.final_softcap;
         h.key = &s->st->key;
-        CW_TRY((fgemv<PRO_NORM, EPI_HEAD>(ctx, h)));
+        if (m->head.type == GGML_Q6_K) {
+            const int grid = std::min<int>((h.N + 7) / 8, ctx->sm_count * 4);
+            const size_t smem = (size_t)h.K * 4;
+            if (smem > 48 * 1024)
+                CW_CUDA(cudaFuncSetAttribute(k_head_q6k,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            CW_TRY(launch_k(ctx, k_head_q6k, dim3(grid), dim3(256), smem, h));
+            CW_TRY(check_launch("lm_head q6_k"));
+        } else {
+            CW_TRY((fgemv<PRO_NORM, EPI_HEAD>(ctx, h)));
+        }
     }
     stage("finalize");
     CW_TRY(launch_k(ctx, k_finalize, dim3(1), dim3(1), 0, s->st, (const unsigned*)s->prompt,

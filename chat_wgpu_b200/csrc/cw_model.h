@@ -29,11 +29,12 @@ struct DevState {
     unsigned pad2;
 };
 
-struct QW {  // packed Q4_0 weight
-    const uint8_t* payload = nullptr;
-    const __half* scales = nullptr;
+struct QW {  // packed Q4_0 weight (type 2), or raw GGUF Q6_K blocks (type 14)
+    const uint8_t* payload = nullptr;  // Q4_0: nibble plane; Q6_K: the raw blocks
+    const __half* scales = nullptr;    // Q4_0 only
     int rows = 0, in_f = 0;
     cw_buf buf = 0;
+    int type = 2;
 };
 
 struct Layer {

@@ -31,6 +31,7 @@
 #include "cw_common.h"
 #include "cw_device.cuh"
 #include "cw_gemm.cuh"
+#include "cw_kquant.cuh"
 #include "cw_model.h"
 #include "cw_sample.cuh"
 
@@ -49,19 +50,14 @@ __device__ __forceinline__ float pf_block_sum(float v, float* red) {
     return t;
 }
 
-// Rows of token_embd for prompt[0 .. C), exact Q4_0 dequantisation.
+// Rows of token_embd for prompt[0 .. C), exact dequantisation (Q4_0 or Q6_K).
 __global__ void k_pf_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
-                           int dim, float scale, const unsigned* __restrict__ toks,
+                           int type, int dim, float scale, const unsigned* __restrict__ toks,
                            float* __restrict__ H) {
-    const int r = blockIdx.x, nb = dim / 32;
+    const int r = blockIdx.x;
     const unsigned tok = toks[r];
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-        const int b = i >> 5, j = i & 31;
-        const size_t blk = (size_t)tok * nb + b;
-        const float d = __half2float(scales[blk]);
-        const uint8_t byte = payload[blk * 16 + (j & 15)];
-        const int q = (j < 16) ? (byte & 0xf) : (byte >> 4);
-        const float v = __fmul_rn(d, (float)(q - 8));
+        const float v = embed_elem(payload, scales, type, tok, dim, i);
         H[(size_t)r * dim + i] = scale > 0.f ? __fmul_rn(v, scale) : v;
     }
 }
@@ -425,6 +421,9 @@ PfLayout pf_layout(const cw_model* m, size_t C) {
         o += al256(bytes);
         return at;
     };
+    // the split-K workspace first: its self-resetting counters must sit at
+    // the same address for every chunk size
+    L.ws = take(GEMM_WS_BYTES);
     L.H = take(C * I.dim * 4);
     L.T = take(I.post_norms ? C * I.dim * 4 : 0);
     L.QKV = take(C * qkv * 4);
@@ -435,7 +434,6 @@ PfLayout pf_layout(const cw_model* m, size_t C) {
                                   (size_t)I.dim * I.hidden});
     L.wh = take(C > 256 ? wmax * 2 : 0);  // f16 pair of one weight (long chunks)
     L.wl = take(C > 256 ? wmax * 2 : 0);
-    L.ws = take(C <= 256 ? GEMM_WS_BYTES : 0);
     L.total = o;
     return L;
 }
@@ -548,8 +546,8 @@ int pf_chunk(cw_session* s, int p0, int C) {
     const bool last_full = find_tap(s, TAP_POST_ATTN, last) || find_tap(s, TAP_LAYER_OUT, last);
 
     stage("prefill.embed");
-    k_pf_embed<<<C, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, dim, I.embed_scale,
-                                           s->prompt + p0, H);
+    k_pf_embed<<<C, 256, 0, ctx->stream>>>(m->embed.payload, m->embed.scales, m->embed.type,
+                                           dim, I.embed_scale, s->prompt + p0, H);
     CW_TRY(check_launch("prefill embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
@@ -641,6 +639,7 @@ int session_prefill(cw_session* s, size_t* n_done) {
             s->pf_mem = nullptr;
             s->pf_bytes = 0;
             CW_CUDA(cudaMalloc(&s->pf_mem, L.total));
+            CW_CUDA(cudaMemsetAsync(s->pf_mem, 0, L.total, s->ctx->stream));  // split-K counters
             s->pf_bytes = L.total;
         }
         while (s->host_pos < end) {
@@ -679,19 +678,14 @@ struct GrpRow {
 };
 
 __global__ void k_grp_embed(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
-                            int dim, float scale, const GrpRow* __restrict__ rows,
+                            int type, int dim, float scale, const GrpRow* __restrict__ rows,
                             float* __restrict__ H) {
     pdl_trigger();
     pdl_wait();
-    const int r = blockIdx.x, nb = dim / 32;
+    const int r = blockIdx.x;
     const unsigned tok = rows[r].st->token;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-        const int b = i >> 5, j = i & 31;
-        const size_t blk = (size_t)tok * nb + b;
-        const float d = __half2float(scales[blk]);
-        const uint8_t byte = payload[blk * 16 + (j & 15)];
-        const int q = (j < 16) ? (byte & 0xf) : (byte >> 4);
-        const float v = __fmul_rn(d, (float)(q - 8));
+        const float v = embed_elem(payload, scales, type, tok, dim, i);
         H[(size_t)r * dim + i] = scale > 0.f ? __fmul_rn(v, scale) : v;
     }
 }
@@ -855,6 +849,7 @@ GrpLayout grp_layout(const cw_model* m, size_t B) {
         o += al256(bytes);
         return at;
     };
+    L.ws = take(GEMM_WS_BYTES);  // first, as in the prefill layout
     L.H = take(B * I.dim * 4);
     L.T = take(B * I.dim * 4);
     L.QKV = take(B * (qd + 2 * kvd) * 4);
@@ -862,7 +857,6 @@ GrpLayout grp_layout(const cw_model* m, size_t B) {
     L.xh = take(B * xk * 2);
     L.xl = take(B * xk * 2);
     L.logits = take(B * (size_t)I.vocab * 4);
-    L.ws = take(GEMM_WS_BYTES);
     L.total = o;
     return L;
 }
@@ -884,7 +878,7 @@ int model_pack_weights(cw_model* m) {
         for (const QW* w : {&l.qkv, &l.wo, &l.gate_up, &l.down})
             if (rc == CW_OK) rc = add(*w);
     }
-    if (rc == CW_OK) rc = add(m->head);
+    if (rc == CW_OK && m->head.type == 2) rc = add(m->head);  // a Q6_K head has no record form
     if (rc == CW_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess)
         rc = set_error(CW_ERR_CUDA, "weight packing failed");
     if (rc != CW_OK) {
@@ -937,7 +931,8 @@ static int grp_enqueue(cw_group* g) {
     const int ew_grid = std::max(1, std::min(B * 8, ctx->sm_count * 8));
     stage("group.embed");
     CW_TRY(launch_pdl(ctx, true, k_grp_embed, dim3(B), dim3(256), 0, m->embed.payload,
-                      m->embed.scales, dim, I.embed_scale, (const GrpRow*)g->rows, H));
+                      m->embed.scales, m->embed.type, dim, I.embed_scale, (const GrpRow*)g->rows,
+                      H));
     CW_TRY(check_launch("group embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
@@ -1068,6 +1063,8 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
                      "cw_group_create: a session appears twice");
     }
     cw_ctx* ctx = m->ctx;
+    CW_CHECK(m->head.type == 2, CW_ERR_UNSUPPORTED,
+             "cw_group_create: the co-batched step takes a Q4_0 LM head (this model's is Q6_K)");
     cudaSetDevice(ctx->device);
     CW_TRY(model_pack_weights(m));
     cw_group* g = new cw_group();
@@ -1084,7 +1081,8 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
         cudaMalloc(&g->mem, grp_layout(m, n).total) != cudaSuccess)
         rc = set_error(CW_ERR_OOM, "cw_group_create: device allocation failed");
     if (rc == CW_OK &&
-        (cudaMemcpyAsync(g->rows, h.data(), n * sizeof(GrpRow), cudaMemcpyHostToDevice,
+        (cudaMemsetAsync(g->mem, 0, grp_layout(m, n).total, ctx->stream) != cudaSuccess ||
+         cudaMemcpyAsync(g->rows, h.data(), n * sizeof(GrpRow), cudaMemcpyHostToDevice,
                          ctx->stream) != cudaSuccess ||
          cudaStreamSynchronize(ctx->stream) != cudaSuccess))
         rc = set_error(CW_ERR_CUDA, "cw_group_create: upload failed");

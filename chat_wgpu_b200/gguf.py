@@ -19,7 +19,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-GGML_F32, GGML_F16, GGML_Q4_0 = 0, 1, 2
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q6_K = 0, 1, 2, 14
 
 # metadata value type ids (gguf.rs:125-151)
 _T_U8, _T_I8, _T_U16, _T_I16, _T_U32, _T_I32, _T_F32, _T_BOOL, _T_STR, _T_ARR, _T_U64, _T_I64, _T_F64 = range(13)
@@ -66,7 +66,8 @@ class GgufWriter:
     @staticmethod
     def nbytes(t: Tensor) -> int:
         n = int(np.prod(t.dims))
-        return {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18}[t.ggml_type]
+        return {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18,
+                GGML_Q6_K: n // 256 * 210}[t.ggml_type]
 
     def write(self, path: str) -> None:
         meta = dict(self.meta)
@@ -112,6 +113,17 @@ def random_q4_0_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.nda
     return blocks
 
 
+def random_q6_k_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.ndarray:
+    """[rows * in_f/256, 210] uint8 GGUF Q6_K super-blocks (dequant.rs:102-131
+    layout): random 6-bit codes, int8 sub-block scales in [-64, 64), f16 d ~
+    U(2e-4, 1e-3) (so values span about the Q4_0 blocks' range)."""
+    nb = rows * (in_f // 256)
+    b = rng.integers(0, 256, size=(nb, 210), dtype=np.uint8)
+    b[:, 192:208] = rng.integers(-64, 64, size=(nb, 16)).astype(np.int8).view(np.uint8)
+    b[:, 208:210] = rng.uniform(2e-4, 1e-3, size=nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    return b
+
+
 # Model shapes named by BASELINE.json's configs (random-init), plus the tiny
 # shape of the reference's RandomWeights verify model (src/main.rs:166-174).
 CONFIGS = {
@@ -132,6 +144,13 @@ CONFIGS = {
                         attn_softcap=2.0, final_softcap=3.0),
     "tiny-qwen2": dict(arch="qwen2", dim=256, n_layers=2, n_heads=8, n_kv=2, head_dim=32,
                        hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=False, bias=True),
+    # Q6_K token embedding (tied head) / Q6_K output, the layout of real Q4_0 files
+    "small-qwen3-q6k": dict(arch="qwen3", dim=512, n_layers=4, n_heads=8, n_kv=4, head_dim=64,
+                            hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True,
+                            embed_type="q6_k"),
+    "tiny-gemma2-q6k": dict(arch="gemma2", dim=256, n_layers=3, n_heads=4, n_kv=2, head_dim=64,
+                            hidden=512, vocab=512, eps=1e-6, theta=1e4, tied=False, window=6,
+                            attn_softcap=2.0, final_softcap=3.0, embed_type="q6_k"),
 }
 
 
@@ -167,16 +186,20 @@ def synth_model(path: str, cfg: dict, seed: int = 0) -> str:
         idx[0] += 1
         return np.random.default_rng(np.random.SeedSequence([seed, idx[0]]))
 
-    def mat(name, rows, in_f):
+    def mat(name, rows, in_f, q6k=False):
         r = rng()
-        w.add(name, GGML_Q4_0, (in_f, rows), lambda r=r: random_q4_0_blocks(r, rows, in_f))
+        if q6k:  # real Q4_0 checkpoints often keep token_embd / output in Q6_K
+            w.add(name, GGML_Q6_K, (in_f, rows), lambda r=r: random_q6_k_blocks(r, rows, in_f))
+        else:
+            w.add(name, GGML_Q4_0, (in_f, rows), lambda r=r: random_q4_0_blocks(r, rows, in_f))
 
     def vec(name, n, mean=None):
         r = rng()
         mean = (0.0 if unit else 1.0) if mean is None else mean
         w.add(name, GGML_F32, (n,), lambda r=r: r.normal(mean, 0.02, size=n).astype(np.float32))
 
-    mat("token_embd.weight", vocab, dim)
+    q6k = cfg.get("embed_type") == "q6_k"
+    mat("token_embd.weight", vocab, dim, q6k)
     for i in range(L):
         b = f"blk.{i}."
         vec(b + "attn_norm.weight", dim)
@@ -200,7 +223,7 @@ def synth_model(path: str, cfg: dict, seed: int = 0) -> str:
             vec(b + "post_ffw_norm.weight", dim)
     vec("output_norm.weight", dim)
     if not cfg.get("tied", True):
-        mat("output.weight", vocab, dim)
+        mat("output.weight", vocab, dim, q6k)
     w.write(path)
     return path
 
@@ -280,7 +303,8 @@ class GgufReader:
         """(ggml_type, dims, bytes) of a tensor."""
         tt, dims, off = self.infos[name]
         n = int(np.prod(dims))
-        nbytes = {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18}[tt]
+        nbytes = {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18,
+                  GGML_Q6_K: n // 256 * 210}[tt]
         s = self.data_start + off
         return tt, dims, self.buf[s:s + nbytes]
 
