@@ -690,90 +690,138 @@ __global__ void k_grp_embed(const uint8_t* __restrict__ payload, const __half* _
     }
 }
 
-// k_pf_qk for rows of different sessions (position and cache per row).
-__global__ void __launch_bounds__(256) k_grp_qk(float* __restrict__ QKV, int ld,
-                                                const float* __restrict__ q_norm,
-                                                const float* __restrict__ k_norm, float eps,
-                                                const float* __restrict__ inv_freq,
-                                                const GrpRow* __restrict__ rows, int li, int nh,
-                                                int nkv, int hd) {
-    pdl_trigger();
-    pdl_wait();
-    extern __shared__ float rb[];
-    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nw = blockDim.x >> 5, half = hd / 2;
-    const GrpRow R = rows[r];
-    const int pos = R.st->pos;
-    const size_t lstride = (size_t)nkv * R.max_seq * hd;
-    float* kc = R.kc + li * lstride;
-    float* vc = R.vc + li * lstride;
-    const int qd = nh * hd, kvd = nkv * hd;
-    float* row = QKV + (size_t)r * ld;
-    float* sb = rb + (size_t)warp * hd;
-    for (int h = warp; h < nh + nkv; h += nw) {
-        const bool isq = h < nh;
-        float* src = isq ? row + (size_t)h * hd : row + qd + (size_t)(h - nh) * hd;
-        const float* nwt = isq ? q_norm : k_norm;
-        float ss = 0.f;
-        for (int d = lane; d < hd; d += 32) {
-            const float v = src[d];
-            sb[d] = v;
-            ss = fmaf(v, v, ss);
-        }
-        __syncwarp();
-        if (nwt) {
-            ss = warp_sum(ss);
-            const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
-            for (int d = lane; d < hd; d += 32) sb[d] = __fmul_rn(__fmul_rn(sb[d], inv), nwt[d]);
-            __syncwarp();
-        }
-        float* dst = isq ? src : kc + ((size_t)(h - nh) * R.max_seq + pos) * hd;
-        for (int k = lane; k < half; k += 32) {
-            const float freq = __fmul_rn((float)pos, inv_freq[k]);
-            float sn, cs;
-            sincosf(freq, &sn, &cs);
-            const float lo = sb[k], hi = sb[k + half];
-            dst[k] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
-            dst[k + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
-        }
-        __syncwarp();
-    }
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) {
-        const int g = i / hd, d = i - g * hd;
-        vc[((size_t)g * R.max_seq + pos) * hd + d] = row[qd + kvd + i];
-    }
-}
-
-// k_pf_attn for rows of different sessions.
+// One group step's attention with QK-norm, RoPE and the K/V row write fused
+// in front (the single-session k_fattn of cw_model.cu over rows of different
+// sessions): CTA (split, kv head g, row r) takes key range `split` of row
+// r's live span; the CTA whose range holds the row's position writes its
+// K/V row, so no other CTA reads it.  With several splits the last CTA of a
+// (row, kv head) merges the partial states (fixed order) and writes the
+// output as the f16 hi/lo pair of the O projection.
 template <int EPL, int GMAX>
-__global__ void __launch_bounds__(128) k_grp_attn(const float* __restrict__ QKV, int ld,
-                                                  const GrpRow* __restrict__ rows, int li, int nh,
-                                                  int nkv, int hd, int window, float scale,
-                                                  float softcap, __half* __restrict__ xh,
-                                                  __half* __restrict__ xl) {
+__global__ void __launch_bounds__(128) k_grp_fattn(
+    const float* __restrict__ QKV, int ld, const GrpRow* __restrict__ rows, int li,
+    const float* __restrict__ q_norm, const float* __restrict__ k_norm, float eps,
+    const float* __restrict__ inv_freq, int nh, int nkv, int hd, int n_splits, int window,
+    float scale, float softcap, float* __restrict__ part, unsigned* __restrict__ counters,
+    __half* __restrict__ xh, __half* __restrict__ xl) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ float sm[];
-    const int r = blockIdx.x, g = blockIdx.y, G = nh / nkv, W = hd + 2;
+    const int split = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
+    const int G = nh / nkv, W = hd + 2, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const GrpRow R = rows[r];
-    const int seq = R.st->pos + 1;
-    const size_t lstride = (size_t)nkv * R.max_seq * hd;
-    float* qs = sm + attn_smem_floats(G, hd, 1);
-    const float* qsrc = QKV + (size_t)r * ld + (size_t)g * G * hd;
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = qsrc[i];
-    __syncthreads();
+    const int pos = R.st->pos, seq = pos + 1;
+    const int n_active = attn_active_splits(attn_span(seq, window), n_splits);
+    if (split >= n_active) return;
     int jlo, jhi;
-    attn_range(seq, window, 0, 1, &jlo, &jhi);
+    attn_range(seq, window, split, n_active, &jlo, &jhi);
+    const bool holds = pos >= jlo && pos < jhi;
+    const size_t lstride = (size_t)nkv * R.max_seq * hd;
+    float* kbase = R.kc + li * lstride + (size_t)g * R.max_seq * hd;
+    float* vbase = R.vc + li * lstride + (size_t)g * R.max_seq * hd;
+    float* qs = sm + attn_smem_floats(G, hd, n_splits);  // [G][hd]
+    float* ks = qs + (size_t)G * hd;                     // [hd]
+    const float* row = QKV + (size_t)r * ld;
+    const int qd = nh * hd, kvd = nkv * hd;
+    const int nrows = G + (holds ? 1 : 0);
+    for (int t = warp; t < nrows; t += 4) {  // QK-norm (qwen3.rs:154-155), one warp per row
+        const bool isq = t < G;
+        const float* src = isq ? row + (size_t)(g * G + t) * hd : row + qd + (size_t)g * hd;
+        const float* nw = isq ? q_norm : k_norm;
+        float* dst = isq ? qs + (size_t)t * hd : ks;
+        float v[EPL];
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; e++) {
+            const int d = lane + 32 * e;
+            v[e] = d < hd ? src[d] : 0.f;
+            ss = fmaf(v[e], v[e], ss);
+        }
+        if (nw) {
+            ss = warp_sum(ss);
+            const float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                const int d = lane + 32 * e;
+                if (d < hd) v[e] = __fmul_rn(__fmul_rn(v[e], inv), nw[d]);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < EPL; e++) {
+            const int d = lane + 32 * e;
+            if (d < hd) dst[d] = v[e];
+        }
+    }
+    __syncthreads();
+    const int half = hd / 2;  // RoPE (rope.wgsl:25-34) in place
+    for (int i = threadIdx.x; i < nrows * half; i += blockDim.x) {
+        const int t = i / half, k = i - t * half;
+        float* rw = t < G ? qs + (size_t)t * hd : ks;
+        const float freq = __fmul_rn((float)pos, inv_freq[k]);
+        float sn, cs;
+        sincosf(freq, &sn, &cs);
+        const float lo = rw[k], hi = rw[k + half];
+        rw[k] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
+        rw[k + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
+    }
+    __syncthreads();
+    if (holds) {  // cache.rs:21-24: this position's K (normed, roped) and V
+        const float* vsrc = row + qd + kvd + (size_t)g * hd;
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+            kbase[(size_t)pos * hd + d] = ks[d];
+            vbase[(size_t)pos * hd + d] = vsrc[d];
+        }
+    }
+    __syncthreads();
     float* res = sm + 4 * G * W;
-    attn_core<EPL, GMAX, KV_NC>(qs, G, hd, R.kc + li * lstride + (size_t)g * R.max_seq * hd,
-                                R.vc + li * lstride + (size_t)g * R.max_seq * hd, hd, jlo, jhi,
-                                scale, softcap, sm, res);
-    const size_t o0 = (size_t)r * nh * hd + (size_t)g * G * hd;
+    attn_core<EPL, GMAX, KV_PLAIN>(qs, G, hd, kbase, vbase, hd, jlo, jhi, scale, softcap, sm, res);
+    const size_t o0 = (size_t)r * qd + (size_t)g * G * hd;
+    if (n_active == 1) {
+        for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+            const int gi = i / hd, d = i - gi * hd;
+            split_f16(res[gi * W + d] * (1.0f / res[gi * W + hd + 1]), xh + o0 + i, xl + o0 + i);
+        }
+        return;
+    }
+    float* pr = part + ((size_t)r * nh + (size_t)g * G) * n_splits * W;  // [G][n_splits][W]
+    for (int i = threadIdx.x; i < G * W; i += blockDim.x) {
+        const int gi = i / W, d = i - gi * W;
+        pr[((size_t)gi * n_splits + split) * W + d] = res[i];
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    unsigned* ctr = counters + (size_t)r * nkv + g;
+    if (threadIdx.x == 0) s_last = atomicAdd(ctr, 1u) == (unsigned)n_active - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    float* cwt = sm;  // merge weights [G][n_active + 1]
+    for (int gi = warp; gi < G; gi += 4) {
+        const float* ph = pr + (size_t)gi * n_splits * W;
+        float M = REF_NEG_INF;
+        for (int t = lane; t < n_active; t += 32) M = fmaxf(M, __ldcg(ph + (size_t)t * W + hd));
+        M = warp_max(M);
+        float L = 0.f;
+        for (int t = lane; t < n_active; t += 32) {
+            const float c = expf(__ldcg(ph + (size_t)t * W + hd) - M);
+            cwt[gi * (n_active + 1) + t] = c;
+            L += __ldcg(ph + (size_t)t * W + hd + 1) * c;
+        }
+        L = warp_sum(L);
+        if (lane == 0) cwt[gi * (n_active + 1) + n_active] = 1.0f / L;
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
         const int gi = i / hd, d = i - gi * hd;
-        const float o = res[gi * W + d] * (1.0f / res[gi * W + hd + 1]);
-        split_f16(o, xh + o0 + i, xl + o0 + i);
+        const float* ph = pr + (size_t)gi * n_splits * W + d;
+        const float* c = cwt + gi * (n_active + 1);
+        float a = 0.f;
+        for (int t = 0; t < n_active; t++) a = fmaf(__ldcg(ph + (size_t)t * W), c[t], a);
+        split_f16(a * c[n_active], xh + o0 + i, xl + o0 + i);
     }
+    __syncthreads();
+    if (threadIdx.x == 0) *ctr = 0u;
 }
 
 // Per session: soft-capped logits into its buffer, argmax (ties -> lowest,
@@ -835,8 +883,15 @@ __global__ void __launch_bounds__(SMP_THREADS) k_grp_finalize(const GrpRow* __re
 }
 
 struct GrpLayout {
-    size_t H, T, QKV, G, xh, xl, logits, ws, total;
+    size_t H, T, QKV, G, xh, xl, logits, ws, part, ctr, total;
 };
+
+// Key splits of the group attention: about two CTAs per SM over all rows and
+// kv heads (at most 16).
+int grp_splits(const cw_model* m, size_t B, int sm_count) {
+    const int per = (int)(2 * sm_count / std::max<size_t>(1, B * m->info.n_kv));
+    return std::max(1, std::min(16, per));
+}
 
 GrpLayout grp_layout(const cw_model* m, size_t B) {
     const cw_model_info& I = m->info;
@@ -857,6 +912,8 @@ GrpLayout grp_layout(const cw_model* m, size_t B) {
     L.xh = take(B * xk * 2);
     L.xl = take(B * xk * 2);
     L.logits = take(B * (size_t)I.vocab * 4);
+    L.part = take(B * (size_t)I.n_heads * 16 * (I.head_dim + 2) * 4);  // up to 16 splits
+    L.ctr = take(B * (size_t)I.n_kv * 4);  // merge counters (zero, self-resetting)
     L.total = o;
     return L;
 }
@@ -893,6 +950,7 @@ int model_pack_weights(cw_model* m) {
 
 struct cw_group {
     cw_model* m = nullptr;
+    int n_splits = 1;  // key splits of the attention
     std::vector<cw_session*> ss;
     cw::GrpRow* rows = nullptr;  // device
     void* mem = nullptr;         // scratch (GrpLayout)
@@ -944,28 +1002,28 @@ static int grp_enqueue(cw_group* g) {
                                                     (__half*)xl));
         CW_TRY(check_launch("group norm"));
         CW_TRY(gemm(4 * li + 0, dim, qkv_rows, QKV, l.qkv_bias, GE_STORE));
-        stage("group.qk");
-        CW_TRY(launch_pdl(ctx, true, k_grp_qk, dim3(B), dim3(256), (size_t)8 * hd * 4, QKV,
-                          qkv_rows, (const float*)l.q_norm, (const float*)l.k_norm, I.eps,
-                          m->inv_freq, (const GrpRow*)g->rows, (int)li, nh, nkv, hd));
-        CW_TRY(check_launch("group qk"));
         stage("group.attn");
         {
-            const int G = nh / nkv, epl = (hd + 31) / 32;
-            const size_t smem = (attn_smem_floats(G, hd, 1) + (size_t)G * hd) * sizeof(float);
+            const int G = nh / nkv, epl = (hd + 31) / 32, ns = g->n_splits;
+            const size_t smem =
+                (attn_smem_floats(G, hd, ns) + (size_t)G * hd + hd) * sizeof(float);
             const int window = (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
             const float scale = powf((float)hd, -0.5f);  // attention.rs:18
-            dim3 grid(B, nkv);
+            dim3 grid(ns, nkv, B);
+            float* part = (float*)(b + L.part);
+            unsigned* ctr = (unsigned*)(b + L.ctr);
             auto go = [&](auto kern) -> int {
                 if (smem > 48 * 1024)
                     CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)smem));
                 CW_TRY(launch_pdl(ctx, true, kern, grid, dim3(128), smem, (const float*)QKV,
-                                  qkv_rows, (const GrpRow*)g->rows, (int)li, nh, nkv, hd, window,
-                                  scale, I.attn_softcap, (__half*)xh, (__half*)xl));
+                                  qkv_rows, (const GrpRow*)g->rows, (int)li,
+                                  (const float*)l.q_norm, (const float*)l.k_norm, I.eps,
+                                  m->inv_freq, nh, nkv, hd, ns, window, scale, I.attn_softcap,
+                                  part, ctr, (__half*)xh, (__half*)xl));
                 return check_launch("group attention");
             };
-#define CW_GA(E, GM) CW_TRY(go(k_grp_attn<E, GM>))
+#define CW_GA(E, GM) CW_TRY(go(k_grp_fattn<E, GM>))
 #define CW_GAE(E)                 \
     if (G <= 1) CW_GA(E, 1);      \
     else if (G <= 2) CW_GA(E, 2); \
@@ -1069,6 +1127,7 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
     CW_TRY(model_pack_weights(m));
     cw_group* g = new cw_group();
     g->m = m;
+    g->n_splits = grp_splits(m, n, ctx->sm_count);
     g->ss.assign(sessions, sessions + n);
     std::vector<GrpRow> h(n);
     for (size_t i = 0; i < n; i++) {
