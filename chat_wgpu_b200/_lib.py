@@ -102,6 +102,10 @@ SIGNATURES = {
     "cw_model_load_gguf": [_vp, C.c_char_p, C.POINTER(_vp)],
     "cw_model_free": [_vp],
     "cw_model_get_info": [_vp, C.POINTER(ModelInfo)],
+    "cw_tp_unique_id": [_vp, _sz],
+    "cw_model_load_gguf_tp": [_vp, C.c_char_p, C.c_int, C.c_int, _vp, C.POINTER(_vp)],
+    "cw_model_tp_info": [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_uint32),
+                         C.POINTER(C.c_uint32)],
     "cw_session_create": [_vp, _sz, C.POINTER(_vp)],
     "cw_session_free": [_vp],
     "cw_session_begin": [_vp, _vp, _sz],

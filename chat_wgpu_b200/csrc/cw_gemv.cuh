@@ -58,6 +58,7 @@ struct GemvArgs {
     const float* bias;              // EPI_STORE: optional per-row bias
     int geglu;                      // EPI_GLU: 0 SwiGLU, 1 GeGLU (rows 2i = gate_i, 2i+1 = up_i)
     float softcap;                  // EPI_HEAD: tanh soft-cap of the logits (0 = off)
+    unsigned key_offset;            // EPI_HEAD: index of row 0 in the full vocabulary (TP shard)
     unsigned long long* key;        // EPI_HEAD: argmax accumulator (atomicMax)
     int* status;                    // device status word
 };
@@ -451,7 +452,7 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
             } else if (EPI == EPI_HEAD) {
                 if (a.softcap > 0.f) v = a.softcap * tanhf(v / a.softcap);
                 a.y[row] = v;
-                const unsigned long long kk = argmax_key(v, (unsigned)row);
+                const unsigned long long kk = argmax_key(v, (unsigned)row + a.key_offset);
                 best = kk > best ? kk : best;
             } else {
                 a.y[row] = a.bias ? v + a.bias[row] : v;

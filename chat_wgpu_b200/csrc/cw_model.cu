@@ -35,6 +35,7 @@
 #include "cw_kquant.cuh"
 #include "cw_ops.h"
 #include "cw_model.h"
+#include "cw_nccl.h"
 #include "cw_q4.h"
 
 namespace cw {
@@ -159,7 +160,7 @@ __global__ void __launch_bounds__(256) k_fgemv(FArgs a) {
                     float v = acc[r];
                     if (a.softcap > 0.f) v = a.softcap * tanhf(v / a.softcap);
                     if (lane == r) a.y[row] = v;
-                    unsigned long long k = argmax_key(v, (unsigned)row);
+                    unsigned long long k = argmax_key(v, (unsigned)row + a.key_offset);
                     best = k > best ? k : best;
                 }
             }
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(256) k_head_q6k(FArgs a) {
         acc = warp_sum(acc);
         if (a.softcap > 0.f) acc = a.softcap * tanhf(acc / a.softcap);
         if (lane == 0) a.y[r] = acc;
-        const unsigned long long k = argmax_key(acc, (unsigned)r);
+        const unsigned long long k = argmax_key(acc, (unsigned)r + a.key_offset);
         best = k > best ? k : best;
     }
     if (lane == 0) red_key[warp] = best;
@@ -588,7 +589,8 @@ static int load_vec(cw_model* m, const GgufFile& f, const std::string& name, siz
 // interleave: two parts with equal rows become rows p0[0], p1[0], p0[1], ...
 // A token embedding or LM head stored as GGUF Q6_K (real Q4_0 checkpoints often
 // keep these in Q6_K): the raw super-blocks go to HBM unchanged.
-static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out) {
+static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out, int rdiv = 1,
+                    int ridx = 0) {
     CW_CHECK(in_f % 256 == 0, CW_ERR_UNSUPPORTED,
              "tensor %s is Q6_K: its rows (%zu) must be a multiple of 256", t->name.c_str(), in_f);
     CW_CHECK(!t->dims.empty() && t->dims[0] == in_f && t->n_elems % in_f == 0, CW_ERR_FORMAT,
@@ -597,13 +599,18 @@ static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out) {
     const size_t rows = t->n_elems / in_f;
     CW_CHECK(t->nbytes == rows * (in_f / 256) * 210, CW_ERR_FORMAT, "tensor %s: %zu bytes",
              t->name.c_str(), t->nbytes);
+    CW_CHECK(rows % rdiv == 0, CW_ERR_UNSUPPORTED, "tensor %s: %zu rows do not split %d ways",
+             t->name.c_str(), rows, rdiv);
+    // rows [ridx, ridx + 1) * rows / rdiv: a contiguous byte range of the raw blocks
+    const size_t n = rows / rdiv, nbytes = t->nbytes / rdiv;
     void* p = nullptr;
-    CW_TRY(dev_alloc(m, t->nbytes, &p));
-    CW_CUDA(cudaMemcpyAsync(p, t->data, t->nbytes, cudaMemcpyHostToDevice, m->ctx->stream));
+    CW_TRY(dev_alloc(m, nbytes, &p));
+    CW_CUDA(cudaMemcpyAsync(p, t->data + nbytes * ridx, nbytes, cudaMemcpyHostToDevice,
+                            m->ctx->stream));
     CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
     out->payload = (const uint8_t*)p;
     out->scales = nullptr;
-    out->rows = (int)rows;
+    out->rows = (int)n;
     out->in_f = (int)in_f;
     out->type = GGML_Q6_K;
     out->buf = m->owned.back();
@@ -613,6 +620,13 @@ static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out) {
 // Q4_0 (packed planes) or Q6_K (raw), by the tensor's type.
 static int load_q4_or_q6k(cw_model* m, const GgufFile& f, const std::string& name, size_t in_f,
                           QW* out);
+
+// Q4_0 tensors `names` stacked by rows (or interleaved row by row), optionally
+// sliced for tensor parallelism: rows [k/rdiv, (k+1)/rdiv) of each part with
+// k = ridx, and the column blocks [c/cdiv, (c+1)/cdiv) with c = cidx.
+static int load_q4_slice(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
+                         size_t in_f, bool interleave, int rdiv, int ridx, int cdiv, int cidx,
+                         QW* out);
 
 static int load_q4(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
                    size_t in_f, bool interleave, QW* out) {
@@ -679,6 +693,72 @@ static int load_q4(cw_model* m, const GgufFile& f, const std::vector<std::string
     return CW_OK;
 }
 
+static int load_q4_slice(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
+                         size_t in_f, bool interleave, int rdiv, int ridx, int cdiv, int cidx,
+                         QW* out) {
+    const size_t nb = in_f / 32, rb = nb * 18;
+    CW_CHECK(nb % cdiv == 0, CW_ERR_UNSUPPORTED, "%s: %zu blocks per row do not split %d ways",
+             names[0].c_str(), nb, cdiv);
+    const size_t cb0 = nb / cdiv * cidx, cbn = nb / cdiv, rbs = cbn * 18;
+    std::vector<const GgufTensor*> parts;
+    for (auto& n : names) {
+        const GgufTensor* t = f.tensor(n);
+        CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", n.c_str());
+        CW_CHECK(t->type == GGML_Q4_0, CW_ERR_UNSUPPORTED,
+                 "tensor %s is %s; the decode path takes Q4_0 matrices", n.c_str(),
+                 ggml_type_name(t->type));
+        CW_CHECK(!t->dims.empty() && t->dims[0] == in_f && t->n_elems % in_f == 0, CW_ERR_FORMAT,
+                 "tensor %s: inner dimension %llu, expected %zu", n.c_str(),
+                 (unsigned long long)(t->dims.empty() ? 0 : t->dims[0]), in_f);
+        CW_CHECK((t->n_elems / in_f) % rdiv == 0, CW_ERR_UNSUPPORTED,
+                 "tensor %s: %llu rows do not split %d ways", n.c_str(),
+                 (unsigned long long)(t->n_elems / in_f), rdiv);
+        parts.push_back(t);
+    }
+    CW_CHECK(!interleave || (parts.size() == 2 && parts[0]->n_elems == parts[1]->n_elems),
+             CW_ERR_FORMAT, "interleaved weights need two equal parts");
+    // the selected rows of every part, in output order
+    std::vector<const uint8_t*> src;
+    if (!interleave) {
+        for (auto* t : parts) {
+            const size_t n = t->n_elems / in_f / rdiv, r0 = n * ridx;
+            for (size_t r = 0; r < n; r++) src.push_back(t->data + (r0 + r) * rb);
+        }
+    } else {
+        const size_t n = parts[0]->n_elems / in_f / rdiv, r0 = n * ridx;
+        for (size_t r = 0; r < n; r++) {
+            src.push_back(parts[0]->data + (r0 + r) * rb);
+            src.push_back(parts[1]->data + (r0 + r) * rb);
+        }
+    }
+    const size_t rows = src.size();
+    std::vector<uint8_t> stage(rows * rbs);
+    for (size_t r = 0; r < rows; r++) memcpy(stage.data() + r * rbs, src[r] + cb0 * 18, rbs);
+    void* tmp = nullptr;
+    CW_CUDA(cudaMalloc(&tmp, stage.size()));
+    cudaError_t ce = cudaMemcpyAsync(tmp, stage.data(), stage.size(), cudaMemcpyHostToDevice,
+                                     m->ctx->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(m->ctx->stream);
+    if (ce != cudaSuccess) {
+        cudaFree(tmp);
+        return set_error(CW_ERR_CUDA, "weight upload: %s", cudaGetErrorString(ce));
+    }
+    cw_buf b;
+    int rc = pack_q4_0(m->ctx, tmp, rows, cbn * 32, &b);
+    cudaStreamSynchronize(m->ctx->stream);
+    cudaFree(tmp);
+    CW_TRY(rc);
+    m->owned.push_back(b);
+    BufEntry& e = m->ctx->bufs[b];
+    out->payload = (const uint8_t*)e.ptr;
+    out->scales = (const __half*)((const char*)e.ptr + e.scale_off);
+    out->rows = (int)rows;
+    out->in_f = (int)(cbn * 32);
+    out->buf = b;
+    m->info.weight_bytes += rows * rbs;
+    return CW_OK;
+}
+
 static int load_q4_or_q6k(cw_model* m, const GgufFile& f, const std::string& name, size_t in_f,
                           QW* out) {
     const GgufTensor* t = f.tensor(name);
@@ -735,40 +815,62 @@ static int model_load(cw_model* m, const std::string& path) {
     CW_CHECK(I.dim % 32 == 0 && I.hidden % 32 == 0 && (I.n_heads * I.head_dim) % 32 == 0,
              CW_ERR_UNSUPPORTED, "dimensions must be multiples of 32");
     const size_t qd = (size_t)I.n_heads * I.head_dim, kvd = (size_t)I.n_kv * I.head_dim;
+    // tensor parallelism over T ranks (Megatron-style): rank r holds heads
+    // [r, r+1) * n_heads/T (with their KV heads) and FFN columns
+    // [r, r+1) * hidden/T as row slices of q/k/v and gate/up and the matching
+    // column slices of the O and down projections, whose partial outputs are
+    // summed over the ranks; the LM head is split by vocabulary rows
+    const int T = m->tp_world, r = m->tp_rank;
+    if (T > 1)
+        CW_CHECK(I.n_kv % T == 0 && I.hidden % (32 * T) == 0 && I.vocab % T == 0 &&
+                     qd % (32 * T) == 0,
+                 CW_ERR_UNSUPPORTED,
+                 "tensor parallelism over %d ranks needs n_kv (%u), hidden/32 (%u), vocab (%u) "
+                 "and q width/32 (%zu) divisible by %d",
+                 T, I.n_kv, I.hidden / 32, I.vocab, qd / 32, T);
+    m->vocab_full = I.vocab;
     m->L.resize(I.n_layers);
     for (uint32_t i = 0; i < I.n_layers; i++) {
         Layer& l = m->L[i];
         std::string p = "blk." + std::to_string(i) + ".";
         CW_TRY(load_vec(m, f, p + "attn_norm.weight", I.dim, &l.attn_norm));
-        CW_TRY(load_q4(m, f, {p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"},
-                       I.dim, false, &l.qkv));
-        CW_CHECK((size_t)l.qkv.rows == qd + 2 * kvd, CW_ERR_FORMAT, "layer %u: q/k/v rows %d",
-                 i, l.qkv.rows);
+        const std::vector<std::string> qkv = {p + "attn_q.weight", p + "attn_k.weight",
+                                              p + "attn_v.weight"};
+        CW_TRY(T > 1 ? load_q4_slice(m, f, qkv, I.dim, false, T, r, 1, 0, &l.qkv)
+                     : load_q4(m, f, qkv, I.dim, false, &l.qkv));
+        CW_CHECK((size_t)l.qkv.rows == (qd + 2 * kvd) / T, CW_ERR_FORMAT,
+                 "layer %u: q/k/v rows %d", i, l.qkv.rows);
         if (f.has(p + "attn_q.bias")) {  // Linear bias (layers.rs:20-21,59-61)
             I.qkv_bias = 1;
             float *bq, *bk, *bv;
             CW_TRY(load_vec(m, f, p + "attn_q.bias", qd, &bq));
             CW_TRY(load_vec(m, f, p + "attn_k.bias", kvd, &bk));
             CW_TRY(load_vec(m, f, p + "attn_v.bias", kvd, &bv));
+            const size_t lq = qd / T, lkv = kvd / T;  // this rank's slice of each
             void* pb;
-            CW_TRY(dev_alloc(m, (qd + 2 * kvd) * 4, &pb));
+            CW_TRY(dev_alloc(m, (lq + 2 * lkv) * 4, &pb));
             cudaStream_t st = m->ctx->stream;
-            CW_CUDA(cudaMemcpyAsync(pb, bq, qd * 4, cudaMemcpyDeviceToDevice, st));
-            CW_CUDA(cudaMemcpyAsync((float*)pb + qd, bk, kvd * 4, cudaMemcpyDeviceToDevice, st));
-            CW_CUDA(cudaMemcpyAsync((float*)pb + qd + kvd, bv, kvd * 4, cudaMemcpyDeviceToDevice,
-                                    st));
+            CW_CUDA(cudaMemcpyAsync(pb, bq + lq * r, lq * 4, cudaMemcpyDeviceToDevice, st));
+            CW_CUDA(cudaMemcpyAsync((float*)pb + lq, bk + lkv * r, lkv * 4,
+                                    cudaMemcpyDeviceToDevice, st));
+            CW_CUDA(cudaMemcpyAsync((float*)pb + lq + lkv, bv + lkv * r, lkv * 4,
+                                    cudaMemcpyDeviceToDevice, st));
             CW_CUDA(cudaStreamSynchronize(st));
             l.qkv_bias = (float*)pb;
         }
-        CW_TRY(load_q4(m, f, {p + "attn_output.weight"}, qd, false, &l.wo));
+        CW_TRY(T > 1 ? load_q4_slice(m, f, {p + "attn_output.weight"}, qd, false, 1, 0, T, r, &l.wo)
+                     : load_q4(m, f, {p + "attn_output.weight"}, qd, false, &l.wo));
         if (I.qk_norm) {
             CW_TRY(load_vec(m, f, p + "attn_q_norm.weight", I.head_dim, &l.q_norm));
             CW_TRY(load_vec(m, f, p + "attn_k_norm.weight", I.head_dim, &l.k_norm));
         }
         CW_TRY(load_vec(m, f, p + "ffn_norm.weight", I.dim, &l.ffn_norm));
-        CW_TRY(load_q4(m, f, {p + "ffn_gate.weight", p + "ffn_up.weight"}, I.dim, true,
-                       &l.gate_up));
-        CW_TRY(load_q4(m, f, {p + "ffn_down.weight"}, I.hidden, false, &l.down));
+        const std::vector<std::string> gu = {p + "ffn_gate.weight", p + "ffn_up.weight"};
+        CW_TRY(T > 1 ? load_q4_slice(m, f, gu, I.dim, true, T, r, 1, 0, &l.gate_up)
+                     : load_q4(m, f, gu, I.dim, true, &l.gate_up));
+        CW_TRY(T > 1
+                   ? load_q4_slice(m, f, {p + "ffn_down.weight"}, I.hidden, false, 1, 0, T, r, &l.down)
+                   : load_q4(m, f, {p + "ffn_down.weight"}, I.hidden, false, &l.down));
         if (I.post_norms) {
             CW_TRY(load_vec(m, f, p + "post_attention_norm.weight", I.dim, &l.post_attn));
             CW_TRY(load_vec(m, f, p + "post_ffw_norm.weight", I.dim, &l.post_ffw));
@@ -778,12 +880,29 @@ static int model_load(cw_model* m, const std::string& path) {
     CW_TRY(load_q4_or_q6k(m, f, "token_embd.weight", I.dim, &m->embed));
     CW_CHECK(m->embed.rows == (int)I.vocab, CW_ERR_FORMAT, "token_embd has %d rows, vocab %u",
              m->embed.rows, I.vocab);
-    if (f.has("output.weight")) {  // untied head; tied otherwise (qwen3.rs:93-98)
+    if (T > 1) {  // this rank's vocabulary rows of the (untied or tied) head
+        const std::string hn = f.has("output.weight") ? "output.weight" : "token_embd.weight";
+        const GgufTensor* t = f.tensor(hn);
+        if (t->type == GGML_Q6_K)
+            CW_TRY(load_q6k(m, t, I.dim, &m->head, T, r));
+        else
+            CW_TRY(load_q4_slice(m, f, {hn}, I.dim, false, T, r, 1, 0, &m->head));
+    } else if (f.has("output.weight")) {  // untied head; tied otherwise (qwen3.rs:93-98)
         CW_TRY(load_q4_or_q6k(m, f, "output.weight", I.dim, &m->head));
     } else {
         m->head = m->embed;
     }
     CW_TRY(rope_table(m->ctx, I.head_dim, I.rope_theta, &m->inv_freq));
+    m->info_full = I;
+    if (T > 1) {  // the kernels see this rank's share
+        I.n_heads /= T;
+        I.n_kv /= T;
+        I.hidden /= T;
+        I.vocab /= T;
+        m->vocab_offset = I.vocab * r;
+        CW_CHECK(m->head.rows == (int)I.vocab, CW_ERR_FORMAT, "head shard has %d rows",
+                 m->head.rows);
+    }
     return CW_OK;
 }
 
@@ -836,6 +955,13 @@ static int enqueue_step_core(cw_session* s, bool decode) {
     const cw_model_info& I = m->info;
     const int qd = I.n_heads * I.head_dim;
     const bool post = I.post_norms != 0;
+    // Tensor parallelism: each rank's O and down projections produce a partial
+    // sum over its heads / FFN columns; it goes to tmp, is all-reduced over the
+    // ranks, and is added to the residual by the next prologue, as the
+    // post-norm families do with their normed branch outputs (no post norm
+    // then: post_w stays null).
+    const bool tp = m->tp_world > 1;
+    const bool defer = post || tp;
     const int unit = I.norm_kind == 1;
     // With the context profiler on (direct launches only), every kernel is
     // bracketed by CUDA events under its stage name.
@@ -859,10 +985,10 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         a.scales = l.qkv.scales;
         a.K = I.dim;
         a.N = l.qkv.rows;
-        if (post && li > 0) {
+        if (defer && li > 0) {
             a.base = s->hidden_b;
             a.delta = s->tmp;
-            a.post_w = m->L[li - 1].post_ffw;
+            a.post_w = post ? m->L[li - 1].post_ffw : nullptr;
             a.h_out = s->hidden;
         } else {
             a.base = s->hidden;
@@ -906,9 +1032,10 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         o.K = qd;
         o.N = I.dim;
         o.x = s->attn;
-        o.y = post ? s->tmp : s->hidden;
-        CW_TRY(post ? (fgemv<PRO_X, EPI_STORE>(ctx, o)) : (fgemv<PRO_X, EPI_RESID>(ctx, o)));
-        if (!post) CW_TRY(tap_copy(s, TAP_POST_ATTN, li, s->hidden));
+        o.y = defer ? s->tmp : s->hidden;
+        CW_TRY(defer ? (fgemv<PRO_X, EPI_STORE>(ctx, o)) : (fgemv<PRO_X, EPI_RESID>(ctx, o)));
+        if (tp) CW_TRY(tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
+        if (!defer) CW_TRY(tap_copy(s, TAP_POST_ATTN, li, s->hidden));
 
         stage("ffn_in");
         FArgs f{};
@@ -917,9 +1044,9 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         f.K = I.dim;
         f.N = l.gate_up.rows;
         f.base = s->hidden;
-        if (post) {
+        if (defer) {
             f.delta = s->tmp;
-            f.post_w = l.post_attn;
+            f.post_w = post ? l.post_attn : nullptr;
             f.h_out = s->hidden_b;
         }
         f.norm_w = l.ffn_norm;
@@ -937,9 +1064,10 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         d.K = I.hidden;
         d.N = I.dim;
         d.x = s->act;
-        d.y = post ? s->tmp : s->hidden;
-        CW_TRY(post ? (fgemv<PRO_X, EPI_STORE>(ctx, d)) : (fgemv<PRO_X, EPI_RESID>(ctx, d)));
-        if (!post) {
+        d.y = defer ? s->tmp : s->hidden;
+        CW_TRY(defer ? (fgemv<PRO_X, EPI_STORE>(ctx, d)) : (fgemv<PRO_X, EPI_RESID>(ctx, d)));
+        if (tp) CW_TRY(tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
+        if (!defer) {
             CW_TRY(tap_copy(s, TAP_LAYER_OUT, li, s->hidden));
         } else if (const Tap* tp = find_tap(s, TAP_LAYER_OUT, li)) {
             // the next prologue forms hidden_b + postnorm(tmp); form it here for the tap
@@ -955,10 +1083,11 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         h.scales = m->head.scales;
         h.K = I.dim;
         h.N = (int)I.vocab;
-        if (post) {
+        h.key_offset = m->vocab_offset;
+        if (defer) {
             h.base = s->hidden_b;
             h.delta = s->tmp;
-            h.post_w = m->L[I.n_layers - 1].post_ffw;
+            h.post_w = post ? m->L[I.n_layers - 1].post_ffw : nullptr;
         } else {
             h.base = s->hidden;
         }
@@ -980,6 +1109,8 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         } else {
             CW_TRY((fgemv<PRO_NORM, EPI_HEAD>(ctx, h)));
         }
+        // the best (logit, index) key over the vocabulary shards
+        if (tp) CW_TRY(tp_max_u64(m->nccl, &s->st->key, 1, ctx->stream));
     }
     stage("finalize");
     CW_TRY(launch_k(ctx, k_finalize, dim3(1), dim3(1), 0, s->st, (const unsigned*)s->prompt,
@@ -1063,10 +1194,55 @@ int cw_model_load_gguf(cw_ctx* ctx, const char* path, cw_model** out) {
     return CW_OK;
 }
 
+int cw_tp_unique_id(uint8_t* id, size_t n) {
+    clear_error();
+    CW_CHECK(id && n >= CW_TP_ID_BYTES, CW_ERR_INVALID_ARG,
+             "cw_tp_unique_id: need a buffer of %d bytes", CW_TP_ID_BYTES);
+    memset(id, 0, n);
+    return tp_unique_id(id, n);
+}
+
+int cw_model_load_gguf_tp(cw_ctx* ctx, const char* path, int rank, int world, const uint8_t* id,
+                          cw_model** out) {
+    clear_error();
+    CW_CHECK(ctx && path && out && id && world >= 1 && world <= 64 && rank >= 0 && rank < world,
+             CW_ERR_INVALID_ARG, "cw_model_load_gguf_tp: bad arguments");
+    if (world == 1) return cw_model_load_gguf(ctx, path, out);
+    cudaSetDevice(ctx->device);
+    cw_model* m = new cw_model();
+    m->ctx = ctx;
+    m->tp_rank = rank;
+    m->tp_world = world;
+    // the communicator first: the ranks read the same file, so a load error
+    // comes on every rank, after all of them have joined
+    int rc = tp_comm_init(id, rank, world, &m->nccl);
+    if (rc == CW_OK) rc = model_load(m, path);
+    if (rc != CW_OK) {
+        std::string msg = cw_last_error();
+        cw_model_free(m);
+        return set_error(rc, "%s", msg.c_str());
+    }
+    *out = m;
+    return CW_OK;
+}
+
+int cw_model_tp_info(cw_model* m, int* rank, int* world, uint32_t* vocab_offset,
+                     uint32_t* vocab_local) {
+    clear_error();
+    CW_CHECK(m, CW_ERR_INVALID_ARG, "cw_model_tp_info: model is NULL");
+    if (rank) *rank = m->tp_rank;
+    if (world) *world = m->tp_world;
+    if (vocab_offset) *vocab_offset = m->vocab_offset;
+    if (vocab_local) *vocab_local = m->info.vocab;
+    return CW_OK;
+}
+
 int cw_model_free(cw_model* m) {
     if (!m) return CW_OK;
     cudaSetDevice(m->ctx->device);
     cudaStreamSynchronize(m->ctx->stream);
+    tp_comm_destroy(m->nccl);
+    m->nccl = nullptr;
     for (cw_buf b : m->owned) {
         auto it = m->ctx->bufs.find(b);
         if (it != m->ctx->bufs.end()) {
@@ -1082,7 +1258,12 @@ int cw_model_free(cw_model* m) {
 int cw_model_get_info(cw_model* m, cw_model_info* info) {
     clear_error();
     CW_CHECK(m && info, CW_ERR_INVALID_ARG, "cw_model_get_info: bad arguments");
-    *info = m->info;
+    if (m->tp_world > 1) {  // the whole model's shapes; weight bytes held by this rank
+        *info = m->info_full;
+        info->weight_bytes = m->info.weight_bytes;
+    } else {
+        *info = m->info;
+    }
     return CW_OK;
 }
 
@@ -1204,9 +1385,9 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     CW_CHECK(n_prompt <= s->max_seq, CW_ERR_INVALID_ARG, "prompt of %zu tokens exceeds max_seq %zu",
              n_prompt, s->max_seq);
     for (size_t i = 0; i < n_prompt; i++)
-        CW_CHECK(prompt[i] < s->m->info.vocab, CW_ERR_INVALID_ARG,
+        CW_CHECK(prompt[i] < s->m->vocab_full, CW_ERR_INVALID_ARG,
                  "prompt token %u at %zu is outside the vocabulary (%u)", prompt[i], i,
-                 s->m->info.vocab);
+                 s->m->vocab_full);
     cudaSetDevice(s->ctx->device);
     CW_CUDA(cudaMemcpyAsync(s->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, s->ctx->stream));
     k_begin<<<1, 1, 0, s->ctx->stream>>>(s->st, s->prompt, (int)n_prompt, s->bar);
@@ -1226,6 +1407,9 @@ int cw_session_set_sampling(cw_session* s, float temperature, uint32_t top_k, fl
     CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_set_sampling: session is NULL");
     CW_CHECK(temperature == temperature && top_p >= 0.f && top_p <= 1.f, CW_ERR_INVALID_ARG,
              "cw_session_set_sampling: temperature must be a number and top_p in [0, 1]");
+    CW_CHECK(!(temperature > 0.f) || s->m->tp_world == 1, CW_ERR_UNSUPPORTED,
+             "cw_session_set_sampling: a tensor-parallel model decodes greedily (each rank "
+             "holds a slice of the logits)");
     cudaSetDevice(s->ctx->device);
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     destroy_graphs(s);  // the decode graph holds the sampling launch or not
@@ -1241,7 +1425,7 @@ int cw_session_set_eos(cw_session* s, const uint32_t* ids, size_t n) {
     CW_CHECK(s && (ids || n == 0) && n <= CW_MAX_EOS, CW_ERR_INVALID_ARG,
              "cw_session_set_eos: at most %d stop tokens", CW_MAX_EOS);
     for (size_t i = 0; i < n; i++)
-        CW_CHECK(ids[i] < s->m->info.vocab, CW_ERR_INVALID_ARG,
+        CW_CHECK(ids[i] < s->m->vocab_full, CW_ERR_INVALID_ARG,
                  "cw_session_set_eos: token %u outside the vocabulary", ids[i]);
     cudaSetDevice(s->ctx->device);
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
@@ -1264,6 +1448,8 @@ int cw_session_add_tap(cw_session* s, const char* name, uint32_t layer, size_t c
     const int kind = tap_kind(name);
     CW_CHECK(kind >= 0, CW_ERR_INVALID_ARG,
              "cw_session_add_tap: unknown tap '%s' (q, post_attn, layer_out)", name ? name : "");
+    CW_CHECK(s->m->tp_world == 1, CW_ERR_UNSUPPORTED,
+             "cw_session_add_tap: taps are not available on a tensor-parallel model");
     const cw_model_info& I = s->m->info;
     CW_CHECK(layer < I.n_layers && cap > 0 && cap <= s->max_seq, CW_ERR_INVALID_ARG,
              "cw_session_add_tap: layer %u of %u, cap %zu (1..max_seq)", layer, I.n_layers, cap);
@@ -1333,6 +1519,9 @@ int cw_session_prefill(cw_session* s, size_t* n_done) {
     clear_error();
     CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_prefill: session is NULL");
     CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_session_prefill: call cw_session_begin first");
+    CW_CHECK(s->m->tp_world == 1, CW_ERR_UNSUPPORTED,
+             "cw_session_prefill: not available on a tensor-parallel model (the prompt runs "
+             "through cw_session_run)");
     cudaSetDevice(s->ctx->device);
     CW_TRY(session_prefill(s, n_done));
     return check_launch("session prefill");
@@ -1411,7 +1600,7 @@ int cw_session_step(cw_session* s, uint32_t token_in, uint32_t* token_out) {
     clear_error();
     CW_CHECK(s && token_out, CW_ERR_INVALID_ARG, "cw_session_step: bad arguments");
     CW_CHECK(s->n_prompt > 0, CW_ERR_INVALID_ARG, "cw_session_step: call cw_session_begin first");
-    CW_CHECK(token_in == CW_TOKEN_DEVICE || token_in < s->m->info.vocab, CW_ERR_INVALID_ARG,
+    CW_CHECK(token_in == CW_TOKEN_DEVICE || token_in < s->m->vocab_full, CW_ERR_INVALID_ARG,
              "cw_session_step: token %u outside the vocabulary", token_in);
     cudaSetDevice(s->ctx->device);
     if (s->stopped) {  // an EOS token ended the sequence: nothing more to produce

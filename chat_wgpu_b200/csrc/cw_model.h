@@ -75,6 +75,13 @@ struct cw_model {
     // the head) in the tensor-core GEMM's packed Q4_0 tile records
     // (cw_gemm.cu), built on first use by prefill or a session group
     std::vector<void*> packed;
+    // tensor parallelism (cw_model_load_gguf_tp): this rank's share of heads,
+    // FFN columns and vocabulary; residual-branch sums all-reduced over NCCL
+    int tp_rank = 0, tp_world = 1;
+    void* nccl = nullptr;
+    cw_model_info info_full{};  // the whole model's shapes (info holds this rank's share)
+    uint32_t vocab_full = 0;    // token ids range over the full vocabulary
+    uint32_t vocab_offset = 0;  // first vocabulary row of this rank's LM-head shard
 };
 
 struct cw_session {

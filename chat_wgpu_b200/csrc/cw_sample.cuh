@@ -132,8 +132,9 @@ __device__ __forceinline__ unsigned long long smp_scan(SmpShared& S, unsigned lo
 __device__ inline unsigned sample_core(SmpShared& S, const float* __restrict__ logits, int n,
                                 const SampleParams& sp, unsigned long long draw, unsigned amax) {
     const int tid = threadIdx.x;
+    if (!(sp.temperature > 0.f)) return amax;  // greedy (logits may be a vocabulary shard)
     const float M = logits[amax];
-    if (!(sp.temperature > 0.f) || M != M) return amax;
+    if (M != M) return amax;
     const float invT = 1.0f / sp.temperature;
     // top-k threshold over the logits
     unsigned tk = 0u;

@@ -132,6 +132,7 @@ bool step_supported(const cw_model* m, const cw_session* s) {
         return false;
     if (I.head_dim % 32 || I.n_heads % I.n_kv || !find_kernel(I)) return false;
     if (m->embed.type != 2 || m->head.type != 2) return false;  // Q6_K embedding / head
+    if (m->tp_world > 1) return false;  // the all-reduces run between kernels
     const int ks[3] = {(int)I.dim, (int)(I.n_heads * I.head_dim), (int)I.hidden};
     for (int K : ks)
         if (K % 256 || mk_cfg_for(K) < 0) return false;

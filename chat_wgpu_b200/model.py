@@ -23,13 +23,31 @@ from .gguf import GgufReader
 from .kernels import activation, argmax, attention, norm, q4, rope
 
 
+TP_ID_BYTES = 128
+
+
+def tp_unique_id() -> bytes:
+    """A fresh NCCL communicator id for cw_model_load_gguf_tp (rank 0 makes it)."""
+    buf = C.create_string_buffer(TP_ID_BYTES)
+    _lib.call("cw_tp_unique_id", C.cast(buf, C.c_void_p), TP_ID_BYTES)
+    return buf.raw
+
+
 class Model:
     """Model::load (mod.rs:26) from a GGUF file; the native model handle."""
 
-    def __init__(self, ctx: GpuContext, path: str):
+    def __init__(self, ctx: GpuContext, path: str, tp: "tuple[int, int, bytes] | None" = None):
+        """`tp` = (rank, world, id): this process's shard of a tensor-parallel
+        model (cw_model_load_gguf_tp); `id` from `tp_unique_id()` on rank 0."""
         self.ctx = ctx
         h = C.c_void_p()
-        _lib.call("cw_model_load_gguf", ctx.handle, path.encode(), C.byref(h))
+        if tp is None:
+            _lib.call("cw_model_load_gguf", ctx.handle, path.encode(), C.byref(h))
+        else:
+            rank, world, uid = tp
+            ub = C.create_string_buffer(bytes(uid), TP_ID_BYTES)
+            _lib.call("cw_model_load_gguf_tp", ctx.handle, path.encode(), int(rank), int(world),
+                      C.cast(ub, C.c_void_p), C.byref(h))
         self._h = h
         self._sessions = weakref.WeakSet()  # released before the model
         ctx._adopt(self)
@@ -37,6 +55,10 @@ class Model:
         _lib.call("cw_model_get_info", self._h, C.byref(info))
         self.info = {k: (getattr(info, k).decode() if k == "arch" else getattr(info, k))
                      for k, _ in info._fields_}
+        r, w, off, nv = C.c_int(), C.c_int(), C.c_uint32(), C.c_uint32()
+        _lib.call("cw_model_tp_info", self._h, C.byref(r), C.byref(w), C.byref(off), C.byref(nv))
+        self.tp_rank, self.tp_world = r.value, w.value
+        self.vocab_offset, self.vocab_local = off.value, nv.value
 
     @property
     def handle(self):
@@ -172,7 +194,9 @@ class Session:
         return out[: n.value].copy()
 
     def logits(self) -> np.ndarray:
-        v = self.model.vocab_size
+        """The last decode step's logits (a tensor-parallel rank: its vocabulary
+        rows [model.vocab_offset, + model.vocab_local))."""
+        v = self.model.vocab_local
         out = np.zeros(v, dtype=np.float32)
         _lib.call("cw_session_logits", self._h, out.ctypes.data, v)
         return out

@@ -252,7 +252,26 @@ typedef struct {
  * norms and biases.  Weights stay Q4_0 in HBM (no re-quantisation). */
 int cw_model_load_gguf(cw_ctx* ctx, const char* path, cw_model** out);
 int cw_model_free(cw_model* model);
+/* The whole model's shapes (for a tensor-parallel rank too; weight_bytes is
+ * what this rank holds). */
 int cw_model_get_info(cw_model* model, cw_model_info* info);
+
+/* Tensor-parallel decode (no reference counterpart: the reference runs one
+ * model on one adapter).  `world` processes, one GPU each, load the same GGUF
+ * with cw_model_load_gguf_tp: rank r keeps heads [r, r+1) * n_heads/world
+ * with their KV heads, FFN columns [r, r+1) * hidden/world and LM-head rows
+ * [r, r+1) * vocab/world; the O and down partial sums and the argmax are
+ * all-reduced over NCCL (libnccl.so.2, opened at run time) inside each step.
+ * Every rank drives its session through the same calls in the same order.
+ * Greedy decode only: no sampling at temperature > 0, taps, cw_session_prefill
+ * or groups; cw_session_logits returns this rank's vocabulary slice.
+ * Rank 0 makes the id with cw_tp_unique_id and hands it to the others. */
+#define CW_TP_ID_BYTES 128
+int cw_tp_unique_id(uint8_t* id, size_t n);
+int cw_model_load_gguf_tp(cw_ctx* ctx, const char* path, int rank, int world, const uint8_t* id,
+                          cw_model** out);
+int cw_model_tp_info(cw_model* model, int* rank, int* world, uint32_t* vocab_offset,
+                     uint32_t* vocab_local);
 
 /* A decode session = Model::new_cache (qwen3.rs:115) + the per-token state of
  * generate (mod.rs:57-125).  max_seq bounds prompt + generated tokens. */

@@ -1,0 +1,53 @@
+"""One rank of a tensor-parallel decode, run as its own process by
+test_gpu_tp.py: loads its shard of the GGUF model on GPU `rank`, decodes
+greedily and saves its tokens and its slice of every step's logits.
+
+usage: tp_worker.py RANK WORLD MODEL ID_HEX PROMPT(comma-separated) N_NEW OUT.npz
+"""
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main(argv):
+    rank, world = int(argv[1]), int(argv[2])
+    path, uid = argv[3], bytes.fromhex(argv[4])
+    prompt = np.array([int(t) for t in argv[5].split(",")], np.uint32)
+    n_new, out = int(argv[6]), argv[7]
+    from chat_wgpu_b200.context import GpuContext
+    from chat_wgpu_b200.model import Model, Session
+    ctx = GpuContext(rank)
+    m = Model(ctx, path, tp=(rank, world, uid))
+    s = Session(m, len(prompt) + n_new)
+    assert not s.persistent
+    s.begin(prompt)
+    s.run(len(prompt) - 1)
+    logits = []
+    for _ in range(n_new):
+        s.run(1)
+        logits.append(s.logits())
+    toks = s.tokens()
+    # what a tensor-parallel model does not support fails cleanly (no collective runs)
+    from chat_wgpu_b200 import CwError
+    t = Session(m, 16)
+    t.begin(prompt[:4])
+    for call in (lambda: t.set_sampling(0.8), t.prefill, lambda: t.add_tap("q", 0, 4)):
+        try:
+            call()
+        except CwError:
+            continue
+        raise AssertionError("expected CwError")
+    t.set_sampling(0.0)  # greedy stays available
+    t.close()
+    np.savez(out, toks=toks, logits=np.stack(logits), vocab_offset=m.vocab_offset,
+             vocab=m.vocab_size, weight_bytes=m.info["weight_bytes"])
+    s.close()
+    m.close()
+    ctx.close()
+
+
+if __name__ == "__main__":
+    main(sys.argv)
