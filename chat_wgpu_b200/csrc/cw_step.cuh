@@ -701,7 +701,11 @@ __device__ __forceinline__ void mk_load_regs(const Q24& q, MRegs<CF>& R) {
 // One chunk of RC rows: wait for ring slot c.seq, dot each row with the
 // planes in R, reduce the per-warp partials into rb[row * WPR + sub], then
 // (after __syncthreads) issue the next copy into the freed slot.  Returns
-// rb, or null after a timed-out wait (the failure is recorded).
+// rb, or null after a timed-out wait (the failure is recorded).  Each thread
+// waits on the slot's mbarrier itself, so the only CTA barrier is the one at
+// the end: warps start on a chunk while the issuing lane is still queueing
+// the copies of the previous one, and a failed wait (whose thread reads
+// stale slot bytes, in bounds) is agreed on at that barrier.
 template <class CF>
 __device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int nb, int rows,
                                                  const MRegs<CF>& R, bool first) {
@@ -713,10 +717,6 @@ __device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int 
     for (int h = 0; h < NS; h++) {
         const int q = c.seq + h;
         ok = mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS) && ok;
-    }
-    if (__syncthreads_or(!ok)) {
-        mk_fail(p, c);
-        return nullptr;
     }
     if (first) mk_clk(c, CLK_WAITED);
     // this warp's rows lie in one slot (RS is a multiple of RPW)
@@ -749,7 +749,10 @@ __device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int 
     }
     const float v = warp_reduce_rows<RPW>(acc, lane);
     if ((lane & (32 / RPW - 1)) == 0) rb[(slot * RPW + lane / (32 / RPW)) * WPR + wsub] = v;
-    __syncthreads();  // slots consumed, row partials complete
+    if (__syncthreads_or(!ok)) {  // slots consumed, row partials complete
+        mk_fail(p, c);
+        return nullptr;
+    }
     if (first) mk_clk(c, CLK_SUMMED);
     if (threadIdx.x == MK_ISSUER)
         for (int k = 0; k < NS; k++) mk_issue_next(p, c);
@@ -914,11 +917,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
             const int r0 = k * MK_DOWN_ROWS, rows = min(MK_DOWN_ROWS, S.N2 - r0);
             const int rs = c.seq % MK_SLOTS;
             const unsigned par = (unsigned)((c.seq / MK_SLOTS) & 1);
-            const bool ok = mbar_wait(&sh->full[rs], par, MK_WAIT_NS);
-            if (__syncthreads_or(!ok)) {
-                mk_fail(p, c);
-                return false;
-            }
+            const bool ok = mbar_wait(&sh->full[rs], par, MK_WAIT_NS);  // agreed on below
             const unsigned char* pay = c.ring + (size_t)rs * MK_SLOT_BYTES;
             const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
             for (int r = tid; r < rows; r += MK_THREADS) {
@@ -926,10 +925,14 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
                 const float d = __half2float(scs[r]);
                 const float part = fmaf(d * asb, mk_block_dot(w4, xa, xb, acb), 0.f);
                 const long long fx = __float2ll_rn(part * MK_FIX);
-                atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.fold_a, r0 + r)),
-                          (unsigned long long)fx);
+                if (ok)
+                    atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.fold_a, r0 + r)),
+                              (unsigned long long)fx);
             }
-            __syncthreads();  // slot consumed
+            if (__syncthreads_or(!ok)) {  // slot consumed
+                mk_fail(p, c);
+                return false;
+            }
             if (tid == MK_ISSUER) mk_issue_next(p, c);
             c.seq++;
         }

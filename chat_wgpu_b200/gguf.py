@@ -131,6 +131,9 @@ CONFIGS = {
                        hidden=3072, vocab=151936, eps=1e-6, theta=1e6, tied=True),
     "qwen3-8b": dict(arch="qwen3", dim=4096, n_layers=36, n_heads=32, n_kv=8, head_dim=128,
                      hidden=12288, vocab=151936, eps=1e-6, theta=1e6, tied=False),
+    # Qwen3-8B layer and head shapes over two layers (profiling the step's stages)
+    "qwen3-8b-2l": dict(arch="qwen3", dim=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128,
+                        hidden=12288, vocab=151936, eps=1e-6, theta=1e6, tied=False),
     "gemma2-2b": dict(arch="gemma2", dim=2304, n_layers=26, n_heads=8, n_kv=4, head_dim=256,
                       hidden=9216, vocab=256000, eps=1e-6, theta=1e4, tied=True, window=4096,
                       attn_softcap=50.0, final_softcap=30.0),
@@ -144,6 +147,10 @@ CONFIGS = {
                         attn_softcap=2.0, final_softcap=3.0),
     "tiny-qwen2": dict(arch="qwen2", dim=256, n_layers=2, n_heads=8, n_kv=2, head_dim=32,
                        hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=False, bias=True),
+    # more FFN column blocks (hidden / 32 = 192) than a B200 has SMs: CTAs of the
+    # persistent step take several FFN units each
+    "wide-ffn-qwen3": dict(arch="qwen3", dim=512, n_layers=2, n_heads=8, n_kv=4, head_dim=64,
+                           hidden=6144, vocab=2048, eps=1e-6, theta=1e6, tied=True),
     # Q6_K token embedding (tied head) / Q6_K output, the layout of real Q4_0 files
     "small-qwen3-q6k": dict(arch="qwen3", dim=512, n_layers=4, n_heads=8, n_kv=4, head_dim=64,
                             hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True,

@@ -61,19 +61,22 @@ def models(tmp_path_factory):
     from chat_wgpu_b200 import gguf
     d = tmp_path_factory.mktemp("gpu_models")
     out = {}
-    for name, seed in [("tiny-qwen3", 7), ("small-qwen3", 2), ("tiny-gemma2", 3), ("tiny-qwen2", 5)]:
+    for name, seed in [("tiny-qwen3", 7), ("small-qwen3", 2), ("tiny-gemma2", 3), ("tiny-qwen2", 5),
+                       ("wide-ffn-qwen3", 9)]:
         out[name] = gguf.synth_model(str(d / f"{name}.gguf"), gguf.CONFIGS[name], seed=seed)
     return out
 
 
 # families the persistent one-launch step covers (the others always use the
 # per-stage kernels)
-PERSISTENT = {"tiny-qwen3": False, "small-qwen3": True, "tiny-gemma2": False, "tiny-qwen2": True}
+PERSISTENT = {"tiny-qwen3": False, "small-qwen3": True, "tiny-gemma2": False, "tiny-qwen2": True,
+              "wide-ffn-qwen3": True}
 
 
 @pytest.mark.parametrize("persistent", [False, True, "split", "fused"],
                          ids=["per-stage", "persistent", "persistent-split", "persistent-fused"])
-@pytest.mark.parametrize("name", ["tiny-qwen3", "small-qwen3", "tiny-gemma2", "tiny-qwen2"])
+@pytest.mark.parametrize("name", ["tiny-qwen3", "small-qwen3", "tiny-gemma2", "tiny-qwen2",
+                                  "wide-ffn-qwen3"])
 def test_fused_session_vs_oracle(ctx, orc, models, name, persistent):
     from chat_wgpu_b200.model import Model
     if persistent and not PERSISTENT[name]:
