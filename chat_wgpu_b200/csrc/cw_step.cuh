@@ -465,20 +465,10 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
         // the attention output of 2..MK_DEFER splits per head, merged here
         // (attention.wgsl:88-95 across splits): per head M = max_s m_s,
         // c_s = exp(m_s - M), 1/L with L = sum_s l_s c_s; then
-        // x = (sum_s acc_s c_s) / L per element
+        // x = (sum_s acc_s c_s) / L per element.  Each lane forms the weights
+        // of its own head from (m_s, l_s) loaded together with its partials,
+        // so the merge costs one round of L2 loads and no CTA barrier.
         const int hd = p.hd, W = hd + 2, na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
-        float* cw = hbuf;  // [n_heads][na + 1]
-        for (int h = warp; h < p.n_heads; h += MK_WARPS) {
-            const float* ph = p.part + (size_t)h * p.part_stride * W;
-            const float m = lane < na ? __ldcg(ph + (size_t)lane * W + hd) : REF_NEG_INF;
-            const float l = lane < na ? __ldcg(ph + (size_t)lane * W + hd + 1) : 0.f;
-            const float M = warp_max(m);
-            const float cc = lane < na ? expf(m - M) : 0.f;
-            const float L = warp_sum(l * cc);
-            if (lane < na) cw[h * (na + 1) + lane] = cc;
-            if (lane == 0) cw[h * (na + 1) + na] = 1.0f / L;
-        }
-        __syncthreads();
         for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
             float4 v[MK_QB];
 #pragma unroll
@@ -487,18 +477,33 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
                 v[k] = f4_zero();
                 if (b < nb) {
                     const int i0 = b * 32 + e0, h = i0 / hd, d0 = i0 - h * hd;
-                    const float* ph = p.part + (size_t)h * p.part_stride * W + d0;
-                    const float* cc = cw + h * (na + 1);
-                    // splits in groups of four (W even, d0 % 4 == 0: 8-byte
-                    // aligned float2 pairs); fixed summation tree
+                    const float* ph = p.part + (size_t)h * p.part_stride * W;
+                    // (m_s, l_s) of every split: 8-byte aligned pairs (W, hd even)
+                    float2 ml[MK_DEFER];
+#pragma unroll
+                    for (int s = 0; s < MK_DEFER; s++)
+                        ml[s] = s < na ? __ldcg(reinterpret_cast<const float2*>(ph + (size_t)s * W + hd))
+                                       : make_float2(REF_NEG_INF, 0.f);
+                    // splits in groups of four (d0 % 4 == 0: 8-byte aligned
+                    // float2 pairs); fixed summation tree
                     float r[4] = {0.f, 0.f, 0.f, 0.f};
+                    float M = ml[0].x;
+#pragma unroll
+                    for (int s = 1; s < MK_DEFER; s++) M = s < na ? fmaxf(M, ml[s].x) : M;
+                    float cc[MK_DEFER], L = 0.f;
+#pragma unroll
+                    for (int s = 0; s < MK_DEFER; s++) {
+                        cc[s] = s < na ? expf(ml[s].x - M) : 0.f;
+                        L = s < na ? fmaf(ml[s].y, cc[s], L) : L;
+                    }
 #pragma unroll
                     for (int s0 = 0; s0 < MK_DEFER; s0 += 4) {
                         if (s0 >= na) break;
                         float2 lo[4], hi[4];
 #pragma unroll
                         for (int j = 0; j < 4; j++) {
-                            const float2* q2 = reinterpret_cast<const float2*>(ph + (size_t)(s0 + j) * W);
+                            const float2* q2 =
+                                reinterpret_cast<const float2*>(ph + (size_t)(s0 + j) * W + d0);
                             lo[j] = s0 + j < na ? __ldcg(q2) : make_float2(0.f, 0.f);
                             hi[j] = s0 + j < na ? __ldcg(q2 + 1) : make_float2(0.f, 0.f);
                         }
@@ -508,13 +513,13 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
 #pragma unroll
                             for (int j = 0; j < 4; j++) {
                                 const float2 t2 = e < 2 ? lo[j] : hi[j];
-                                a[j] = (s0 + j < na ? ((e & 1) ? t2.y : t2.x) : 0.f) *
-                                       cc[s0 + j < na ? s0 + j : 0];
+                                a[j] = ((e & 1) ? t2.y : t2.x) * cc[s0 + j];
                             }
                             r[e] = r[e] + ((a[0] + a[1]) + (a[2] + a[3]));
                         }
                     }
-                    v[k] = make_float4(r[0] * cc[na], r[1] * cc[na], r[2] * cc[na], r[3] * cc[na]);
+                    const float inv = 1.0f / L;
+                    v[k] = make_float4(r[0] * inv, r[1] * inv, r[2] * inv, r[3] * inv);
                 }
             }
 #pragma unroll
