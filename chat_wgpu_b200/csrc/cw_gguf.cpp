@@ -18,6 +18,8 @@ const char* ggml_type_name(uint32_t t) {
         case GGML_Q4_0: return "Q4_0";
         case GGML_Q4_1: return "Q4_1";
         case GGML_Q8_0: return "Q8_0";
+        case GGML_Q4_K: return "Q4_K";
+        case GGML_Q5_K: return "Q5_K";
         case GGML_Q6_K: return "Q6_K";
         case GGML_BF16: return "BF16";
         default: return "unknown";
@@ -31,6 +33,8 @@ size_t ggml_row_bytes(uint32_t type, size_t n) {
         case GGML_Q4_0: return n % 32 ? 0 : n / 32 * 18;
         case GGML_Q4_1: return n % 32 ? 0 : n / 32 * 20;
         case GGML_Q8_0: return n % 32 ? 0 : n / 32 * 34;
+        case GGML_Q4_K: return n % 256 ? 0 : n / 256 * 144;
+        case GGML_Q5_K: return n % 256 ? 0 : n / 256 * 176;
         case GGML_Q6_K: return n % 256 ? 0 : n / 256 * 210;
         default: return 0;
     }

@@ -19,6 +19,8 @@ enum GgmlType : uint32_t {
     GGML_Q4_0 = 2,
     GGML_Q4_1 = 3,
     GGML_Q8_0 = 8,
+    GGML_Q4_K = 12,
+    GGML_Q5_K = 13,
     GGML_Q6_K = 14,
     GGML_BF16 = 30,
 };

@@ -312,68 +312,98 @@ __global__ void k_embed(const uint8_t* __restrict__ payload, const __half* __res
     }
 }
 
-// LM head over a Q6_K table (real Q4_0 checkpoints often keep it Q6_K):
-// x = rmsnorm(h) (h = base, or base + post-normed delta) into shared memory
-// by every CTA (CTA 0 also writes xn_out), then one warp per row
-// (kq_dot<Q6_K>), soft-cap, logits, and the argmax key (atomicMax, ties ->
-// lowest index) -- the EPI_HEAD epilogue of the Q4_0 head.
-__global__ void __launch_bounds__(256) k_head_q6k(FArgs a) {
+// Projections and LM heads kept as raw GGUF k-quant blocks (Q4_K / Q5_K /
+// Q6_K: real checkpoints keep the LM head, and Q4_K_M files some projections,
+// in these types).  Prologue: x = rmsnorm(h) (h = base, or base + delta,
+// post-normed when post_w is set; CTA 0 writes h_out and xn_out) or x from
+// global memory, staged once per CTA in shared memory.  Then one warp per
+// output row (kq_dot: exact per-weight dequantisation, f32 accumulation) and
+// the Q4_0 GEMV's epilogues: store (+bias), residual add, the gated unit over
+// interleaved gate/up rows, or the LM head's soft-cap, logits and argmax key
+// (atomicMax, ties -> lowest index).
+template <int T, int PRO, int EPI>
+__global__ void __launch_bounds__(256) k_kq_fgemv(FArgs a) {
     extern __shared__ float xs[];
     __shared__ float red[32];
     __shared__ unsigned long long red_key[8];
+    constexpr int BYTES = KQ<T>::BYTES;
     const int K = a.K, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_trigger();
     pdl_wait();
-    float inv_d = 0.f;
-    if (a.delta && a.post_w) {
-        float ss = 0.f;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(a.delta[i], a.delta[i], ss);
-        ss = cta_sum(ss, red);
-        inv_d = 1.0f / sqrtf(ss / (float)K + a.eps);
-    }
-    float ssh = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        float h = a.base[i];
-        if (a.delta) {
-            float dv = a.delta[i];
-            if (a.post_w) {
-                const float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
-                dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
-            }
-            h = h + dv;
+    if (PRO == PRO_NORM) {
+        float inv_d = 0.f;
+        if (a.delta && a.post_w) {
+            float ss = 0.f;
+            for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(a.delta[i], a.delta[i], ss);
+            ss = cta_sum(ss, red);
+            inv_d = 1.0f / sqrtf(ss / (float)K + a.eps);
         }
-        xs[i] = h;
-        ssh = fmaf(h, h, ssh);
-    }
-    ssh = cta_sum(ssh, red);
-    const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const float gw = a.unit ? 1.0f + a.norm_w[i] : a.norm_w[i];
-        const float v = __fmul_rn(__fmul_rn(xs[i], inv), gw);
-        xs[i] = v;
-        if (a.xn_out && blockIdx.x == 0) a.xn_out[i] = v;
+        float ssh = 0.f;
+        const bool wh = a.h_out && blockIdx.x == 0;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            float h = a.base[i];
+            if (a.delta) {
+                float dv = a.delta[i];
+                if (a.post_w) {
+                    const float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
+                    dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
+                }
+                h = h + dv;
+            }
+            xs[i] = h;
+            if (wh) a.h_out[i] = h;
+            ssh = fmaf(h, h, ssh);
+        }
+        ssh = cta_sum(ssh, red);
+        const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            const float gw = a.unit ? 1.0f + a.norm_w[i] : a.norm_w[i];
+            const float v = __fmul_rn(__fmul_rn(xs[i], inv), gw);
+            xs[i] = v;
+            if (a.xn_out && blockIdx.x == 0) a.xn_out[i] = v;
+        }
+    } else {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = a.x[i];
     }
     __syncthreads();
     const int nbk = K / 256;
-    unsigned long long best = argmax_key_init();
-    for (int r = blockIdx.x * 8 + warp; r < a.N; r += gridDim.x * 8) {
-        const uint8_t* row = a.payload + (size_t)r * nbk * 210;
+    auto dot = [&](int r) {
+        const uint8_t* row = a.payload + (size_t)r * nbk * BYTES;
         float acc = 0.f;
         for (int b = 0; b < nbk; b++)
-            acc = kq_dot<CW_GGUF_Q6_K>(kq_load<CW_GGUF_Q6_K>(row + (size_t)b * 210, lane),
-                                       xs + 256 * b, lane, acc);
-        acc = warp_sum(acc);
-        if (a.softcap > 0.f) acc = a.softcap * tanhf(acc / a.softcap);
-        if (lane == 0) a.y[r] = acc;
-        const unsigned long long k = argmax_key(acc, (unsigned)r + a.key_offset);
-        best = k > best ? k : best;
+            acc = kq_dot<T>(kq_load<T>(row + (size_t)b * BYTES, lane), xs + 256 * b, lane, acc);
+        return warp_sum(acc);
+    };
+    if (EPI == EPI_GLU) {  // rows 2i = gate_i, 2i+1 = up_i
+        for (int i = blockIdx.x * 8 + warp; i < a.N / 2; i += gridDim.x * 8) {
+            const float gv = dot(2 * i), uv = dot(2 * i + 1);
+            if (lane == 0) a.y[i] = (a.geglu ? gelu_ref_f(gv) : silu_ref_f(gv)) * uv;
+        }
+        return;
     }
-    if (lane == 0) red_key[warp] = best;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) best = red_key[w] > best ? red_key[w] : best;
-        best = red_key[0] > best ? red_key[0] : best;
-        atomicMax(a.key, best);
+    unsigned long long best = argmax_key_init();
+    for (int r = blockIdx.x * 8 + warp; r < a.N; r += gridDim.x * 8) {
+        float v = dot(r);
+        if (EPI == EPI_HEAD) {
+            if (a.softcap > 0.f) v = a.softcap * tanhf(v / a.softcap);
+            if (lane == 0) a.y[r] = v;
+            const unsigned long long k = argmax_key(v, (unsigned)r + a.key_offset);
+            best = k > best ? k : best;
+        } else if (EPI == EPI_RESID) {
+            if (lane == 0) a.y[r] = a.y[r] + v;
+        } else {
+            if (lane == 0) a.y[r] = a.bias ? v + a.bias[r] : v;
+        }
+    }
+    if (EPI == EPI_HEAD) {
+        if (lane == 0) red_key[warp] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+                best = red_key[w] > best ? red_key[w] : best;
+            best = red_key[0] > best ? red_key[0] : best;
+            atomicMax(a.key, best);
+        }
     }
 }
 
@@ -494,6 +524,38 @@ static int fgemv(cw_ctx* ctx, const FArgs& a) {
     } else {
         if (r == 2) return launch_fgemv<PRO, EPI, 2>(ctx, a);
         return launch_fgemv<PRO, EPI, 1>(ctx, a);
+    }
+}
+
+template <int T, int PRO, int EPI>
+static int kq_fgemv_t(cw_ctx* ctx, const FArgs& a) {
+    auto kern = k_kq_fgemv<T, PRO, EPI>;
+    const size_t smem = (size_t)a.K * 4;
+    if (smem > 48 * 1024) {
+        CW_CHECK((int)smem <= ctx->max_smem_optin, CW_ERR_UNSUPPORTED,
+                 "k-quant gemv: K=%d needs %zu bytes of shared memory", a.K, smem);
+        CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    }
+    const long rows = EPI == EPI_GLU ? a.N / 2 : a.N;
+    const int grid = (int)std::min<long>((rows + 7) / 8, (long)ctx->sm_count * 4);
+    CW_TRY(launch_k(ctx, kern, dim3(grid), dim3(256), smem, a));
+    return check_launch("k-quant gemv");
+}
+
+// One projection of the per-stage step over weight `w`: the streaming Q4_0
+// GEMV, or the k-quant GEMV for raw Q4_K / Q5_K / Q6_K blocks.
+template <int PRO, int EPI>
+static int proj(cw_ctx* ctx, const QW& w, FArgs a) {
+    a.payload = w.payload;
+    a.scales = w.scales;
+    a.K = w.in_f;
+    a.N = w.rows;
+    switch (w.type) {
+        case GGML_Q4_0: return fgemv<PRO, EPI>(ctx, a);
+        case GGML_Q4_K: return kq_fgemv_t<GGML_Q4_K, PRO, EPI>(ctx, a);
+        case GGML_Q5_K: return kq_fgemv_t<GGML_Q5_K, PRO, EPI>(ctx, a);
+        case GGML_Q6_K: return kq_fgemv_t<GGML_Q6_K, PRO, EPI>(ctx, a);
+        default: return set_error(CW_ERR_UNSUPPORTED, "projection of ggml type %d", w.type);
     }
 }
 
@@ -620,6 +682,68 @@ static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out, int 
 // Q4_0 (packed planes) or Q6_K (raw), by the tensor's type.
 static int load_q4_or_q6k(cw_model* m, const GgufFile& f, const std::string& name, size_t in_f,
                           QW* out);
+
+static bool is_kquant(uint32_t t) { return t == GGML_Q4_K || t == GGML_Q5_K || t == GGML_Q6_K; }
+
+// k-quant tensors `names` of one type kept as raw GGUF blocks, stacked by rows
+// (or interleaved row by row: gate/up).
+static int load_kq(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
+                   size_t in_f, bool interleave, QW* out) {
+    std::vector<const GgufTensor*> parts;
+    for (auto& n : names) {
+        const GgufTensor* t = f.tensor(n);
+        CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", n.c_str());
+        CW_CHECK(is_kquant(t->type) && t->type == f.tensor(names[0])->type, CW_ERR_UNSUPPORTED,
+                 "tensor %s is %s; expected %s", n.c_str(), ggml_type_name(t->type),
+                 ggml_type_name(f.tensor(names[0])->type));
+        CW_CHECK(in_f % 256 == 0 && !t->dims.empty() && t->dims[0] == in_f &&
+                     t->n_elems % in_f == 0,
+                 CW_ERR_FORMAT, "tensor %s: inner dimension must be %zu (a multiple of 256)",
+                 n.c_str(), in_f);
+        parts.push_back(t);
+    }
+    CW_CHECK(!interleave || (parts.size() == 2 && parts[0]->n_elems == parts[1]->n_elems),
+             CW_ERR_FORMAT, "interleaved weights need two equal parts");
+    const uint32_t type = parts[0]->type;
+    const size_t rb = ggml_row_bytes(type, in_f);
+    size_t rows = 0;
+    for (auto* t : parts) {
+        CW_CHECK(t->nbytes == t->n_elems / in_f * rb, CW_ERR_FORMAT, "tensor %s: %zu bytes",
+                 t->name.c_str(), t->nbytes);
+        rows += t->n_elems / in_f;
+    }
+    std::vector<uint8_t> stage(rows * rb);
+    if (!interleave) {
+        size_t off = 0;
+        for (auto* t : parts) {
+            memcpy(stage.data() + off, t->data, t->nbytes);
+            off += t->nbytes;
+        }
+    } else {
+        for (size_t r = 0; r < rows / 2; r++) {
+            memcpy(stage.data() + (2 * r) * rb, parts[0]->data + r * rb, rb);
+            memcpy(stage.data() + (2 * r + 1) * rb, parts[1]->data + r * rb, rb);
+        }
+    }
+    void* p = nullptr;
+    CW_TRY(dev_alloc(m, stage.size(), &p));
+    CW_CUDA(cudaMemcpyAsync(p, stage.data(), stage.size(), cudaMemcpyHostToDevice,
+                            m->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    out->payload = (const uint8_t*)p;
+    out->scales = nullptr;
+    out->rows = (int)rows;
+    out->in_f = (int)in_f;
+    out->type = (int)type;
+    out->buf = m->owned.back();
+    m->info.weight_bytes += stage.size();
+    return CW_OK;
+}
+
+// One projection (or a stack / interleave of several) by the tensors' type:
+// Q4_0 packed planes, or raw k-quant blocks.
+static int load_proj(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
+                     size_t in_f, bool interleave, QW* out);
 
 // Q4_0 tensors `names` stacked by rows (or interleaved row by row), optionally
 // sliced for tensor parallelism: rows [k/rdiv, (k+1)/rdiv) of each part with
@@ -759,6 +883,19 @@ static int load_q4_slice(cw_model* m, const GgufFile& f, const std::vector<std::
     return CW_OK;
 }
 
+static int load_proj(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
+                     size_t in_f, bool interleave, QW* out) {
+    const GgufTensor* t = f.tensor(names[0]);
+    CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", names[0].c_str());
+    if (is_kquant(t->type)) {
+        CW_CHECK(m->tp_world == 1, CW_ERR_UNSUPPORTED,
+                 "tensor %s is %s; tensor parallelism takes Q4_0 projections", names[0].c_str(),
+                 ggml_type_name(t->type));
+        return load_kq(m, f, names, in_f, interleave, out);
+    }
+    return load_q4(m, f, names, in_f, interleave, out);
+}
+
 static int load_q4_or_q6k(cw_model* m, const GgufFile& f, const std::string& name, size_t in_f,
                           QW* out) {
     const GgufTensor* t = f.tensor(name);
@@ -836,10 +973,28 @@ static int model_load(cw_model* m, const std::string& path) {
         CW_TRY(load_vec(m, f, p + "attn_norm.weight", I.dim, &l.attn_norm));
         const std::vector<std::string> qkv = {p + "attn_q.weight", p + "attn_k.weight",
                                               p + "attn_v.weight"};
-        CW_TRY(T > 1 ? load_q4_slice(m, f, qkv, I.dim, false, T, r, 1, 0, &l.qkv)
-                     : load_q4(m, f, qkv, I.dim, false, &l.qkv));
-        CW_CHECK((size_t)l.qkv.rows == (qd + 2 * kvd) / T, CW_ERR_FORMAT,
-                 "layer %u: q/k/v rows %d", i, l.qkv.rows);
+        uint32_t qt[3];
+        for (int j = 0; j < 3; j++) {
+            const GgufTensor* t = f.tensor(qkv[j]);
+            CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", qkv[j].c_str());
+            qt[j] = t->type;
+        }
+        if (qt[0] == qt[1] && qt[1] == qt[2]) {
+            CW_TRY(T > 1 ? load_q4_slice(m, f, qkv, I.dim, false, T, r, 1, 0, &l.qkv)
+                         : load_proj(m, f, qkv, I.dim, false, &l.qkv));
+            CW_CHECK((size_t)l.qkv.rows == (qd + 2 * kvd) / T, CW_ERR_FORMAT,
+                     "layer %u: q/k/v rows %d", i, l.qkv.rows);
+        } else {  // mixed types: three weights over one qkv vector
+            CW_CHECK(T == 1, CW_ERR_UNSUPPORTED,
+                     "layer %u: q/k/v of different types; tensor parallelism takes Q4_0", i);
+            l.qkv_split = true;
+            CW_TRY(load_proj(m, f, {qkv[0]}, I.dim, false, &l.q));
+            CW_TRY(load_proj(m, f, {qkv[1]}, I.dim, false, &l.k));
+            CW_TRY(load_proj(m, f, {qkv[2]}, I.dim, false, &l.v));
+            CW_CHECK((size_t)l.q.rows == qd && (size_t)l.k.rows == kvd && (size_t)l.v.rows == kvd,
+                     CW_ERR_FORMAT, "layer %u: q/k/v rows %d/%d/%d", i, l.q.rows, l.k.rows,
+                     l.v.rows);
+        }
         if (f.has(p + "attn_q.bias")) {  // Linear bias (layers.rs:20-21,59-61)
             I.qkv_bias = 1;
             float *bq, *bk, *bv;
@@ -859,7 +1014,7 @@ static int model_load(cw_model* m, const std::string& path) {
             l.qkv_bias = (float*)pb;
         }
         CW_TRY(T > 1 ? load_q4_slice(m, f, {p + "attn_output.weight"}, qd, false, 1, 0, T, r, &l.wo)
-                     : load_q4(m, f, {p + "attn_output.weight"}, qd, false, &l.wo));
+                     : load_proj(m, f, {p + "attn_output.weight"}, qd, false, &l.wo));
         if (I.qk_norm) {
             CW_TRY(load_vec(m, f, p + "attn_q_norm.weight", I.head_dim, &l.q_norm));
             CW_TRY(load_vec(m, f, p + "attn_k_norm.weight", I.head_dim, &l.k_norm));
@@ -867,10 +1022,10 @@ static int model_load(cw_model* m, const std::string& path) {
         CW_TRY(load_vec(m, f, p + "ffn_norm.weight", I.dim, &l.ffn_norm));
         const std::vector<std::string> gu = {p + "ffn_gate.weight", p + "ffn_up.weight"};
         CW_TRY(T > 1 ? load_q4_slice(m, f, gu, I.dim, true, T, r, 1, 0, &l.gate_up)
-                     : load_q4(m, f, gu, I.dim, true, &l.gate_up));
+                     : load_proj(m, f, gu, I.dim, true, &l.gate_up));
         CW_TRY(T > 1
                    ? load_q4_slice(m, f, {p + "ffn_down.weight"}, I.hidden, false, 1, 0, T, r, &l.down)
-                   : load_q4(m, f, {p + "ffn_down.weight"}, I.hidden, false, &l.down));
+                   : load_proj(m, f, {p + "ffn_down.weight"}, I.hidden, false, &l.down));
         if (I.post_norms) {
             CW_TRY(load_vec(m, f, p + "post_attention_norm.weight", I.dim, &l.post_attn));
             CW_TRY(load_vec(m, f, p + "post_ffw_norm.weight", I.dim, &l.post_ffw));
@@ -888,7 +1043,7 @@ static int model_load(cw_model* m, const std::string& path) {
         else
             CW_TRY(load_q4_slice(m, f, {hn}, I.dim, false, T, r, 1, 0, &m->head));
     } else if (f.has("output.weight")) {  // untied head; tied otherwise (qwen3.rs:93-98)
-        CW_TRY(load_q4_or_q6k(m, f, "output.weight", I.dim, &m->head));
+        CW_TRY(load_proj(m, f, {"output.weight"}, I.dim, false, &m->head));
     } else {
         m->head = m->embed;
     }
@@ -998,7 +1153,19 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         a.unit = unit;
         a.y = s->qkv;
         a.bias = l.qkv_bias;
-        CW_TRY((fgemv<PRO_NORM, EPI_STORE>(ctx, a)));
+        if (!l.qkv_split) {
+            CW_TRY((proj<PRO_NORM, EPI_STORE>(ctx, l.qkv, a)));
+        } else {  // the q, k and v slices of the qkv vector (one prologue each)
+            size_t off = 0;
+            for (const QW* w : {&l.q, &l.k, &l.v}) {
+                FArgs b = a;
+                b.y = s->qkv + off;
+                b.bias = l.qkv_bias ? l.qkv_bias + off : nullptr;
+                if (off) b.h_out = nullptr;  // written once
+                CW_TRY((proj<PRO_NORM, EPI_STORE>(ctx, *w, b)));
+                off += (size_t)w->rows;
+            }
+        }
 
         stage("attention");
         AArgs t{};
@@ -1033,7 +1200,7 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         o.N = I.dim;
         o.x = s->attn;
         o.y = defer ? s->tmp : s->hidden;
-        CW_TRY(defer ? (fgemv<PRO_X, EPI_STORE>(ctx, o)) : (fgemv<PRO_X, EPI_RESID>(ctx, o)));
+        CW_TRY(defer ? (proj<PRO_X, EPI_STORE>(ctx, l.wo, o)) : (proj<PRO_X, EPI_RESID>(ctx, l.wo, o)));
         if (tp) CW_TRY(tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
         if (!defer) CW_TRY(tap_copy(s, TAP_POST_ATTN, li, s->hidden));
 
@@ -1054,7 +1221,7 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         f.unit = unit;
         f.y = s->act;
         f.geglu = I.activation == 1;
-        CW_TRY((fgemv<PRO_NORM, EPI_GLU>(ctx, f)));
+        CW_TRY((proj<PRO_NORM, EPI_GLU>(ctx, l.gate_up, f)));
         if (post) CW_TRY(tap_copy(s, TAP_POST_ATTN, li, s->hidden_b));  // h_out of this prologue
 
         stage("ffn_out");
@@ -1065,7 +1232,7 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         d.N = I.dim;
         d.x = s->act;
         d.y = defer ? s->tmp : s->hidden;
-        CW_TRY(defer ? (fgemv<PRO_X, EPI_STORE>(ctx, d)) : (fgemv<PRO_X, EPI_RESID>(ctx, d)));
+        CW_TRY(defer ? (proj<PRO_X, EPI_STORE>(ctx, l.down, d)) : (proj<PRO_X, EPI_RESID>(ctx, l.down, d)));
         if (tp) CW_TRY(tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
         if (!defer) {
             CW_TRY(tap_copy(s, TAP_LAYER_OUT, li, s->hidden));
@@ -1098,17 +1265,7 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         h.y = s->logits;
         h.softcap = I.final_softcap;
         h.key = &s->st->key;
-        if (m->head.type == GGML_Q6_K) {
-            const int grid = std::min<int>((h.N + 7) / 8, ctx->sm_count * 4);
-            const size_t smem = (size_t)h.K * 4;
-            if (smem > 48 * 1024)
-                CW_CUDA(cudaFuncSetAttribute(k_head_q6k,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            CW_TRY(launch_k(ctx, k_head_q6k, dim3(grid), dim3(256), smem, h));
-            CW_TRY(check_launch("lm_head q6_k"));
-        } else {
-            CW_TRY((fgemv<PRO_NORM, EPI_HEAD>(ctx, h)));
-        }
+        CW_TRY((proj<PRO_NORM, EPI_HEAD>(ctx, m->head, h)));
         // the best (logit, index) key over the vocabulary shards
         if (tp) CW_TRY(tp_max_u64(m->nccl, &s->st->key, 1, ctx->stream));
     }
@@ -1143,6 +1300,15 @@ static void destroy_graphs(cw_session* s) {
                 cudaGraphExecDestroy(g);
                 g = nullptr;
             }
+}
+
+bool model_q4_only(const cw_model* m, bool head) {
+    if (head && m->head.type != GGML_Q4_0) return false;
+    for (const Layer& l : m->L)
+        if (l.qkv_split || l.qkv.type != GGML_Q4_0 || l.wo.type != GGML_Q4_0 ||
+            l.gate_up.type != GGML_Q4_0 || l.down.type != GGML_Q4_0)
+            return false;
+    return true;
 }
 
 // Host counters from the device state (EOS may have ended the sequence
@@ -1522,6 +1688,9 @@ int cw_session_prefill(cw_session* s, size_t* n_done) {
     CW_CHECK(s->m->tp_world == 1, CW_ERR_UNSUPPORTED,
              "cw_session_prefill: not available on a tensor-parallel model (the prompt runs "
              "through cw_session_run)");
+    CW_CHECK(model_q4_only(s->m, false), CW_ERR_UNSUPPORTED,
+             "cw_session_prefill: the tensor-core prefill takes Q4_0 projections (the prompt "
+             "runs through cw_session_run)");
     cudaSetDevice(s->ctx->device);
     CW_TRY(session_prefill(s, n_done));
     return check_launch("session prefill");

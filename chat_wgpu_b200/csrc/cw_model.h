@@ -41,6 +41,10 @@ struct Layer {
     float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *ffn_norm = nullptr;
     float *post_attn = nullptr, *post_ffw = nullptr, *qkv_bias = nullptr;
     QW qkv, wo, gate_up, down;
+    // q, k and v of different k-quant types (Q4_K_M files keep some v in Q6_K)
+    // stay three weights, each writing its slice of the qkv vector
+    bool qkv_split = false;
+    QW q, k, v;
 };
 
 
@@ -140,7 +144,10 @@ int session_prefill(cw_session* s, size_t* n_done);
 int model_pack_weights(cw_model* m);
 
 const Tap* find_tap(const cw_session* s, int kind, uint32_t layer);
-int sync_counts(cw_session* s);  // host n_produced / stopped from the device state (syncs)
+int sync_counts(cw_session* s);
+// Every projection (and, with `head`, the LM head) is Q4_0: the persistent
+// step, batched prefill and session groups take only those.
+bool model_q4_only(const cw_model* m, bool head);  // host n_produced / stopped from the device state (syncs)
 
 // cw_sample.cu: device-side sampling / EOS after a decode step's finalize.
 int sample_params_size();

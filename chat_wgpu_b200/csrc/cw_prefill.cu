@@ -1123,8 +1123,8 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
     cw_ctx* ctx = m->ctx;
     CW_CHECK(m->tp_world == 1, CW_ERR_UNSUPPORTED,
              "cw_group_create: not available on a tensor-parallel model");
-    CW_CHECK(m->head.type == 2, CW_ERR_UNSUPPORTED,
-             "cw_group_create: the co-batched step takes a Q4_0 LM head (this model's is Q6_K)");
+    CW_CHECK(model_q4_only(m, true), CW_ERR_UNSUPPORTED,
+             "cw_group_create: the co-batched step takes Q4_0 projections and LM head");
     cudaSetDevice(ctx->device);
     CW_TRY(model_pack_weights(m));
     cw_group* g = new cw_group();

@@ -131,7 +131,7 @@ bool step_supported(const cw_model* m, const cw_session* s) {
         I.activation != 0 || I.norm_kind != 0)
         return false;
     if (I.head_dim % 32 || I.n_heads % I.n_kv || !find_kernel(I)) return false;
-    if (m->embed.type != 2 || m->head.type != 2) return false;  // Q6_K embedding / head
+    if (m->embed.type != 2 || !model_q4_only(m, true)) return false;  // Q6_K / k-quant weights
     if (m->tp_world > 1) return false;  // the all-reduces run between kernels
     const int ks[3] = {(int)I.dim, (int)(I.n_heads * I.head_dim), (int)I.hidden};
     for (int K : ks)

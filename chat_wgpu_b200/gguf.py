@@ -19,7 +19,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q6_K = 0, 1, 2, 14
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K = 0, 1, 2, 12, 13, 14
 
 # metadata value type ids (gguf.rs:125-151)
 _T_U8, _T_I8, _T_U16, _T_I16, _T_U32, _T_I32, _T_F32, _T_BOOL, _T_STR, _T_ARR, _T_U64, _T_I64, _T_F64 = range(13)
@@ -67,6 +67,7 @@ class GgufWriter:
     def nbytes(t: Tensor) -> int:
         n = int(np.prod(t.dims))
         return {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18,
+                GGML_Q4_K: n // 256 * 144, GGML_Q5_K: n // 256 * 176,
                 GGML_Q6_K: n // 256 * 210}[t.ggml_type]
 
     def write(self, path: str) -> None:
@@ -124,6 +125,21 @@ def random_q6_k_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.nda
     return b
 
 
+def random_q45_k_blocks(rng: np.random.Generator, rows: int, in_f: int, five: bool) -> np.ndarray:
+    """[rows * in_f/256, 144 | 176] uint8 GGUF Q4_K / Q5_K super-blocks (ggml's
+    block_q4_K / block_q5_K): random codes and 6-bit (scale, min) pairs, f16 d
+    ~ U(1e-4, 3e-4) (Q5_K: half that) and dmin = d * (7.5 | 15.5) so the
+    weights centre near zero and span about the Q4_0 blocks' range."""
+    nb = rows * (in_f // 256)
+    size = 176 if five else 144
+    b = rng.integers(0, 256, size=(nb, size), dtype=np.uint8)
+    d = rng.uniform(1e-4, 3e-4, size=nb) * (0.5 if five else 1.0)
+    dmin = d * (15.5 if five else 7.5)
+    b[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(nb, 2)
+    b[:, 2:4] = dmin.astype(np.float16).view(np.uint8).reshape(nb, 2)
+    return b
+
+
 # Model shapes named by BASELINE.json's configs (random-init), plus the tiny
 # shape of the reference's RandomWeights verify model (src/main.rs:166-174).
 CONFIGS = {
@@ -151,6 +167,17 @@ CONFIGS = {
     # persistent step take several FFN units each
     "wide-ffn-qwen3": dict(arch="qwen3", dim=512, n_layers=2, n_heads=8, n_kv=4, head_dim=64,
                            hidden=6144, vocab=2048, eps=1e-6, theta=1e6, tied=True),
+    # k-quant projections in the mixes of Q4_K_M-style files (q/k/v of different
+    # types, Q6_K down projections, a Q4_K head; a Q5_K variant)
+    "small-qwen3-q4km": dict(arch="qwen3", dim=512, n_layers=3, n_heads=8, n_kv=4, head_dim=64,
+                             hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=False,
+                             embed_type="q6_k",
+                             proj_types=dict(q="q4_k", k="q4_k", v="q6_k", o="q4_k",
+                                             gate="q4_k", up="q4_k", down="q6_k", head="q4_k")),
+    "tiny-qwen2-q5k": dict(arch="qwen2", dim=256, n_layers=2, n_heads=8, n_kv=2, head_dim=32,
+                           hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=True, bias=True,
+                           proj_types=dict(q="q5_k", k="q5_k", v="q5_k", o="q5_k",
+                                           gate="q5_k", up="q5_k", down="q5_k")),
     # Q6_K token embedding (tied head) / Q6_K output, the layout of real Q4_0 files
     "small-qwen3-q6k": dict(arch="qwen3", dim=512, n_layers=4, n_heads=8, n_kv=4, head_dim=64,
                             hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True,
@@ -193,12 +220,21 @@ def synth_model(path: str, cfg: dict, seed: int = 0) -> str:
         idx[0] += 1
         return np.random.default_rng(np.random.SeedSequence([seed, idx[0]]))
 
-    def mat(name, rows, in_f, q6k=False):
+    def mat(name, rows, in_f, q6k=False, kind=None):
         r = rng()
-        if q6k:  # real Q4_0 checkpoints often keep token_embd / output in Q6_K
+        kind = kind or ("q6_k" if q6k else "q4_0")
+        if kind == "q6_k":  # real Q4_0 checkpoints often keep token_embd / output in Q6_K
             w.add(name, GGML_Q6_K, (in_f, rows), lambda r=r: random_q6_k_blocks(r, rows, in_f))
+        elif kind in ("q4_k", "q5_k"):
+            five = kind == "q5_k"
+            w.add(name, GGML_Q5_K if five else GGML_Q4_K, (in_f, rows),
+                  lambda r=r: random_q45_k_blocks(r, rows, in_f, five))
         else:
             w.add(name, GGML_Q4_0, (in_f, rows), lambda r=r: random_q4_0_blocks(r, rows, in_f))
+
+    # per-projection types ("q", "k", "v", "o", "gate", "up", "down", "head"):
+    # the mixes of Q4_K_M-style files; Q4_0 where not named
+    pt = cfg.get("proj_types", {})
 
     def vec(name, n, mean=None):
         r = rng()
@@ -210,27 +246,27 @@ def synth_model(path: str, cfg: dict, seed: int = 0) -> str:
     for i in range(L):
         b = f"blk.{i}."
         vec(b + "attn_norm.weight", dim)
-        mat(b + "attn_q.weight", qd, dim)
-        mat(b + "attn_k.weight", kvd, dim)
-        mat(b + "attn_v.weight", kvd, dim)
+        mat(b + "attn_q.weight", qd, dim, kind=pt.get("q"))
+        mat(b + "attn_k.weight", kvd, dim, kind=pt.get("k"))
+        mat(b + "attn_v.weight", kvd, dim, kind=pt.get("v"))
         if cfg.get("bias"):
             vec(b + "attn_q.bias", qd, mean=0.0)
             vec(b + "attn_k.bias", kvd, mean=0.0)
             vec(b + "attn_v.bias", kvd, mean=0.0)
-        mat(b + "attn_output.weight", dim, qd)
+        mat(b + "attn_output.weight", dim, qd, kind=pt.get("o"))
         if arch == "qwen3":
             vec(b + "attn_q_norm.weight", hd)
             vec(b + "attn_k_norm.weight", hd)
         vec(b + "ffn_norm.weight", dim)
-        mat(b + "ffn_gate.weight", hid, dim)
-        mat(b + "ffn_up.weight", hid, dim)
-        mat(b + "ffn_down.weight", dim, hid)
+        mat(b + "ffn_gate.weight", hid, dim, kind=pt.get("gate"))
+        mat(b + "ffn_up.weight", hid, dim, kind=pt.get("up"))
+        mat(b + "ffn_down.weight", dim, hid, kind=pt.get("down"))
         if arch == "gemma2":
             vec(b + "post_attention_norm.weight", dim)
             vec(b + "post_ffw_norm.weight", dim)
     vec("output_norm.weight", dim)
     if not cfg.get("tied", True):
-        mat("output.weight", vocab, dim, q6k)
+        mat("output.weight", vocab, dim, q6k, kind=pt.get("head"))
     w.write(path)
     return path
 
@@ -311,6 +347,7 @@ class GgufReader:
         tt, dims, off = self.infos[name]
         n = int(np.prod(dims))
         nbytes = {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18,
+                  GGML_Q4_K: n // 256 * 144, GGML_Q5_K: n // 256 * 176,
                   GGML_Q6_K: n // 256 * 210}[tt]
         s = self.data_start + off
         return tt, dims, self.buf[s:s + nbytes]

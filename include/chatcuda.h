@@ -249,7 +249,13 @@ typedef struct {
 
 /* Model::load (mod.rs:26, qwen3.rs:44-99) from a GGUF file: architectures
  * qwen3 / qwen2 / llama / gemma2; Q4_0 projections and embeddings, F32/F16
- * norms and biases.  Weights stay Q4_0 in HBM (no re-quantisation). */
+ * norms and biases.  Weights stay in their GGUF format in HBM (no
+ * re-quantisation).  Projections and untied LM heads may also be Q4_K /
+ * Q5_K / Q6_K (the mixes of Q4_K_M-style files, q/k/v of different types
+ * included; no reference counterpart, ROADMAP.md:52-53) and token embeddings
+ * Q6_K; such models decode through the per-stage kernels, and
+ * cw_session_prefill / cw_group_create / the persistent step take Q4_0
+ * projections only. */
 int cw_model_load_gguf(cw_ctx* ctx, const char* path, cw_model** out);
 int cw_model_free(cw_model* model);
 /* The whole model's shapes (for a tensor-parallel rank too; weight_bytes is

@@ -608,6 +608,8 @@ static size_t row_bytes_for(uint32_t dtype, size_t in_f) {
         case 2: return in_f / 32 * 18;
         case 3: return in_f / 32 * 20;
         case 8: return in_f / 32 * 34;
+        case 12: return in_f / 256 * 144;
+        case 13: return in_f / 256 * 176;
         case 14: return in_f / 256 * 210;
         default: return 0;
     }
@@ -622,6 +624,8 @@ static void dequant_row(const orc_mat* m, size_t row, float* out) {
         case 2: orc_dequant_q4_0(b, m->in_f, out); break;
         case 3: orc_dequant_q4_1(b, m->in_f, out); break;
         case 8: orc_dequant_q8_0(b, m->in_f, out); break;
+        case 12: orc_dequant_q4_k(b, m->in_f, out); break;
+        case 13: orc_dequant_q5_k(b, m->in_f, out); break;
         case 14: orc_dequant_q6_k(b, m->in_f, out); break;
     }
 }
