@@ -240,13 +240,32 @@ __device__ __forceinline__ float q6k_elem(const uint8_t* __restrict__ blk, int j
     return __fmul_rn(__fmul_rn(d, sc), (float)q);
 }
 
+// Weight j (0..255) of a Q4_K / Q5_K super-block: chunk c = j / 64, its low
+// nibbles (scale/min pair 2c) for j % 64 < 32, else its high nibbles (pair
+// 2c+1); w = (d*sc)*q - dmin*m, the rounding steps of kq_lane.
+template <bool FIVE>
+__device__ __forceinline__ float q45k_elem(const uint8_t* __restrict__ blk, int j) {
+    const int c = j >> 6, l = j & 31, hi = (j >> 5) & 1;
+    int sc, m;
+    kq_scale_min(2 * c + hi, blk + 4, &sc, &m);
+    const int qb = blk[(FIVE ? 48 : 16) + 32 * c + l];
+    int q = hi ? (qb >> 4) : (qb & 0x0f);
+    if (FIVE) q += ((blk[16 + l] >> (2 * c + hi)) & 1) << 4;
+    const float d1 = __fmul_rn(kq_f16(blk), (float)sc), mm = __fmul_rn(kq_f16(blk + 2), (float)m);
+    return __fsub_rn(__fmul_rn(d1, (float)q), mm);
+}
+
 // Element i of row `tok` of a token-embedding table: packed Q4_0 planes
-// (type 2, dequant.rs:62-78) or raw Q6_K blocks (type 14; dim % 256 == 0).
+// (type 2, dequant.rs:62-78) or raw Q4_K / Q5_K / Q6_K blocks (dim % 256 == 0).
 __device__ __forceinline__ float embed_elem(const uint8_t* __restrict__ payload,
                                             const __half* __restrict__ scales, int type,
                                             unsigned tok, int dim, int i) {
     if (type == CW_GGUF_Q6_K)
         return q6k_elem(payload + ((size_t)tok * (dim / 256) + (i >> 8)) * 210, i & 255);
+    if (type == CW_GGUF_Q4_K)
+        return q45k_elem<false>(payload + ((size_t)tok * (dim / 256) + (i >> 8)) * 144, i & 255);
+    if (type == CW_GGUF_Q5_K)
+        return q45k_elem<true>(payload + ((size_t)tok * (dim / 256) + (i >> 8)) * 176, i & 255);
     const int nb = dim / 32, b = i >> 5, j = i & 31;
     const size_t blk = (size_t)tok * nb + b;
     const float d = __half2float(scales[blk]);

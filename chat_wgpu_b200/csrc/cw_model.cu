@@ -1032,7 +1032,14 @@ static int model_load(cw_model* m, const std::string& path) {
         }
     }
     CW_TRY(load_vec(m, f, "output_norm.weight", I.dim, &m->final_norm));
-    CW_TRY(load_q4_or_q6k(m, f, "token_embd.weight", I.dim, &m->embed));
+    {  // Q4_0 planes, or raw k-quant rows (dequantised per element by the embed kernels)
+        const GgufTensor* te = f.tensor("token_embd.weight");
+        CW_CHECK(te, CW_ERR_NOT_FOUND, "missing tensor token_embd.weight");
+        if (te->type == GGML_Q4_K || te->type == GGML_Q5_K)
+            CW_TRY(load_kq(m, f, {"token_embd.weight"}, I.dim, false, &m->embed));
+        else
+            CW_TRY(load_q4_or_q6k(m, f, "token_embd.weight", I.dim, &m->embed));
+    }
     CW_CHECK(m->embed.rows == (int)I.vocab, CW_ERR_FORMAT, "token_embd has %d rows, vocab %u",
              m->embed.rows, I.vocab);
     if (T > 1) {  // this rank's vocabulary rows of the (untied or tied) head

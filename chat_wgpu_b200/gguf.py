@@ -171,13 +171,17 @@ CONFIGS = {
     # types, Q6_K down projections, a Q4_K head; a Q5_K variant)
     "small-qwen3-q4km": dict(arch="qwen3", dim=512, n_layers=3, n_heads=8, n_kv=4, head_dim=64,
                              hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=False,
-                             embed_type="q6_k",
+                             embed_type="q4_k",
                              proj_types=dict(q="q4_k", k="q4_k", v="q6_k", o="q4_k",
                                              gate="q4_k", up="q4_k", down="q6_k", head="q4_k")),
     "tiny-qwen2-q5k": dict(arch="qwen2", dim=256, n_layers=2, n_heads=8, n_kv=2, head_dim=32,
                            hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=True, bias=True,
                            proj_types=dict(q="q5_k", k="q5_k", v="q5_k", o="q5_k",
                                            gate="q5_k", up="q5_k", down="q5_k")),
+    # Q4_0 projections under a Q5_K token embedding shared with the LM head
+    "small-qwen3-q5k-embed": dict(arch="qwen3", dim=512, n_layers=2, n_heads=8, n_kv=4,
+                                  head_dim=64, hidden=1536, vocab=2048, eps=1e-6, theta=1e6,
+                                  tied=True, embed_type="q5_k"),
     # Q6_K token embedding (tied head) / Q6_K output, the layout of real Q4_0 files
     "small-qwen3-q6k": dict(arch="qwen3", dim=512, n_layers=4, n_heads=8, n_kv=4, head_dim=64,
                             hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True,
@@ -242,7 +246,7 @@ def synth_model(path: str, cfg: dict, seed: int = 0) -> str:
         w.add(name, GGML_F32, (n,), lambda r=r: r.normal(mean, 0.02, size=n).astype(np.float32))
 
     q6k = cfg.get("embed_type") == "q6_k"
-    mat("token_embd.weight", vocab, dim, q6k)
+    mat("token_embd.weight", vocab, dim, kind=cfg.get("embed_type"))
     for i in range(L):
         b = f"blk.{i}."
         vec(b + "attn_norm.weight", dim)

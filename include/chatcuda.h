@@ -253,7 +253,8 @@ typedef struct {
  * re-quantisation).  Projections and untied LM heads may also be Q4_K /
  * Q5_K / Q6_K (the mixes of Q4_K_M-style files, q/k/v of different types
  * included; no reference counterpart, ROADMAP.md:52-53) and token embeddings
- * Q6_K; such models decode through the per-stage kernels, and
+ * Q4_K / Q5_K / Q6_K; k-quant projections decode through the per-stage
+ * kernels, and
  * cw_session_prefill / cw_group_create / the persistent step take Q4_0
  * projections only. */
 int cw_model_load_gguf(cw_ctx* ctx, const char* path, cw_model** out);
