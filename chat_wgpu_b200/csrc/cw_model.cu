@@ -367,10 +367,18 @@ __global__ void __launch_bounds__(256) k_kq_fgemv(FArgs a) {
     }
     __syncthreads();
     const int nbk = K / 256;
-    auto dot = [&](int r) {
+    auto dot = [&](int r) {  // KQ_UNROLL super-blocks' loads in flight at once
         const uint8_t* row = a.payload + (size_t)r * nbk * BYTES;
         float acc = 0.f;
-        for (int b = 0; b < nbk; b++)
+        int b = 0;
+        for (; b + KQ_UNROLL <= nbk; b += KQ_UNROLL) {
+            KqRaw<T> raw[KQ_UNROLL];
+#pragma unroll
+            for (int u = 0; u < KQ_UNROLL; u++) raw[u] = kq_load<T>(row + (size_t)(b + u) * BYTES, lane);
+#pragma unroll
+            for (int u = 0; u < KQ_UNROLL; u++) acc = kq_dot<T>(raw[u], xs + 256 * (b + u), lane, acc);
+        }
+        for (; b < nbk; b++)
             acc = kq_dot<T>(kq_load<T>(row + (size_t)b * BYTES, lane), xs + 256 * b, lane, acc);
         return warp_sum(acc);
     };

@@ -178,6 +178,12 @@ CONFIGS = {
                            hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=True, bias=True,
                            proj_types=dict(q="q5_k", k="q5_k", v="q5_k", o="q5_k",
                                            gate="q5_k", up="q5_k", down="q5_k")),
+    # Qwen3-0.6B shapes in a Q4_K_M-style mix (decode through the k-quant GEMVs)
+    "qwen3-0.6b-q4km": dict(arch="qwen3", dim=1024, n_layers=28, n_heads=16, n_kv=8,
+                            head_dim=128, hidden=3072, vocab=151936, eps=1e-6, theta=1e6,
+                            tied=True, embed_type="q6_k",
+                            proj_types=dict(q="q4_k", k="q4_k", v="q6_k", o="q4_k",
+                                            gate="q4_k", up="q4_k", down="q6_k")),
     # Q4_0 projections under a Q5_K token embedding shared with the LM head
     "small-qwen3-q5k-embed": dict(arch="qwen3", dim=512, n_layers=2, n_heads=8, n_kv=4,
                                   head_dim=64, hidden=1536, vocab=2048, eps=1e-6, theta=1e6,
