@@ -219,6 +219,8 @@ __device__ __forceinline__ float gelu_ref_f(float x) {                          
     return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
 }
 
+constexpr int GEMV_PB = 8;  // residual elements per thread per load batch
+
 // x -> q24 planes in shared memory (PRO_X: x from global; PRO_NORM: the
 // rmsnorm prologue of the decode kernels, norm.wgsl:20-56).
 template <int LAYOUT, int PRO>
@@ -240,32 +242,56 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
     }
     // base/delta may have been written by other CTAs of a persistent kernel:
     // read them through L2 (ld.global.cg), never from a stale L1 line
+    // Each thread takes elements i = tid + u*blockDim.x in increasing order,
+    // GEMV_PB of them per batch with every load of the batch issued before
+    // the math (one L2 round trip per batch, not per element).
     const int K = a.K;
     float inv_d = 0.f;
     if (a.delta && a.post_w) {
         float ss = 0.f;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) {
-            const float dv = __ldcg(a.delta + i);
-            ss = fmaf(dv, dv, ss);
+        for (int i0 = threadIdx.x; i0 < K; i0 += GEMV_PB * blockDim.x) {
+            float dv[GEMV_PB];
+#pragma unroll
+            for (int u = 0; u < GEMV_PB; u++) {
+                const int i = i0 + u * blockDim.x;
+                dv[u] = i < K ? __ldcg(a.delta + i) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < GEMV_PB; u++)
+                if (i0 + u * (int)blockDim.x < K) ss = fmaf(dv[u], dv[u], ss);
         }
         ss = gemv_cta_sum(ss, red8);
         inv_d = 1.0f / sqrtf(ss / (float)K + a.eps);
     }
     float ssh = 0.f;
     const bool wr = a.h_out && blockIdx.x == 0;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        float h = a.base_smem ? a.base[i] : __ldcg(a.base + i);
-        if (a.delta) {
-            float dv = __ldcg(a.delta + i);
-            if (a.post_w) {
-                float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
-                dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
-            }
-            h = h + dv;
+    for (int i0 = threadIdx.x; i0 < K; i0 += GEMV_PB * blockDim.x) {
+        float hv[GEMV_PB], dv[GEMV_PB], gv[GEMV_PB];
+#pragma unroll
+        for (int u = 0; u < GEMV_PB; u++) {
+            const int i = i0 + u * blockDim.x;
+            const bool in = i < K;
+            hv[u] = !in ? 0.f : a.base_smem ? a.base[i] : __ldcg(a.base + i);
+            dv[u] = in && a.delta ? __ldcg(a.delta + i) : 0.f;
+            gv[u] = in && a.delta && a.post_w ? a.post_w[i] : 0.f;
         }
-        hbuf[i] = h;
-        if (wr) a.h_out[i] = h;
-        ssh = fmaf(h, h, ssh);
+#pragma unroll
+        for (int u = 0; u < GEMV_PB; u++) {
+            const int i = i0 + u * blockDim.x;
+            if (i >= K) continue;
+            float h = hv[u];
+            if (a.delta) {
+                float d = dv[u];
+                if (a.post_w) {
+                    const float gw = a.unit ? 1.0f + gv[u] : gv[u];
+                    d = __fmul_rn(__fmul_rn(d, inv_d), gw);
+                }
+                h = h + d;
+            }
+            hbuf[i] = h;
+            if (wr) a.h_out[i] = h;
+            ssh = fmaf(h, h, ssh);
+        }
     }
     ssh = gemv_cta_sum(ssh, red8);
     const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);

@@ -340,19 +340,34 @@ __global__ void __launch_bounds__(256) k_kq_fgemv(FArgs a) {
         }
         float ssh = 0.f;
         const bool wh = a.h_out && blockIdx.x == 0;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) {
-            float h = a.base[i];
-            if (a.delta) {
-                float dv = a.delta[i];
-                if (a.post_w) {
-                    const float gw = a.unit ? 1.0f + a.post_w[i] : a.post_w[i];
-                    dv = __fmul_rn(__fmul_rn(dv, inv_d), gw);
-                }
-                h = h + dv;
+        // loads of GEMV_PB elements issued before their math and stores
+        for (int i0 = threadIdx.x; i0 < K; i0 += GEMV_PB * blockDim.x) {
+            float hv[GEMV_PB], dv[GEMV_PB], gv[GEMV_PB];
+#pragma unroll
+            for (int u = 0; u < GEMV_PB; u++) {
+                const int i = i0 + u * blockDim.x;
+                const bool in = i < K;
+                hv[u] = in ? a.base[i] : 0.f;
+                dv[u] = in && a.delta ? a.delta[i] : 0.f;
+                gv[u] = in && a.delta && a.post_w ? a.post_w[i] : 0.f;
             }
-            xs[i] = h;
-            if (wh) a.h_out[i] = h;
-            ssh = fmaf(h, h, ssh);
+#pragma unroll
+            for (int u = 0; u < GEMV_PB; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i >= K) continue;
+                float h = hv[u];
+                if (a.delta) {
+                    float d = dv[u];
+                    if (a.post_w) {
+                        const float gw = a.unit ? 1.0f + gv[u] : gv[u];
+                        d = __fmul_rn(__fmul_rn(d, inv_d), gw);
+                    }
+                    h = h + d;
+                }
+                xs[i] = h;
+                if (wh) a.h_out[i] = h;
+                ssh = fmaf(h, h, ssh);
+            }
         }
         ssh = cta_sum(ssh, red);
         const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
