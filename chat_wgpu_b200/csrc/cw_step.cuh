@@ -948,8 +948,8 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
 }
 
 // ---- attention stage: QK-norm + RoPE + K/V write + split-KV attention -----------
-// Thread 0 of the CTA that will run attention unit blockIdx.x: pull the cached
-// K/V rows of that unit into L2 while the stage before it runs.
+// Thread 0 of a CTA: pull the cached K/V rows of the attention units it will
+// run into L2 while the stage before it runs.
 __device__ inline void mk_kv_prefetch(const MParams& p, const MStage& A, const MCtx& c) {
     const int seq = c.pos + 1;
     if (A.kind == SK_ATTNO) {  // unit = query head: all cached rows of its group
@@ -962,17 +962,17 @@ __device__ inline void mk_kv_prefetch(const MParams& p, const MStage& A, const M
         return;
     }
     const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
-    const int u = blockIdx.x;
-    if (u >= p.n_kv * n_active) return;
-    const int g = u % p.n_kv, split = u / p.n_kv;
-    int jlo, jhi;
-    attn_range(seq, 0, split, n_active, &jlo, &jhi);
-    const int j1 = min(jhi, c.pos);
-    if (j1 <= jlo) return;
-    const float* kb = A.kc + (size_t)g * p.max_seq * p.hd;
-    const float* vb = A.vc + (size_t)g * p.max_seq * p.hd;
-    prefetch_l2(kb + (size_t)jlo * p.hd, kb + (size_t)j1 * p.hd);
-    prefetch_l2(vb + (size_t)jlo * p.hd, vb + (size_t)j1 * p.hd);
+    for (int u = blockIdx.x; u < p.n_kv * n_active; u += gridDim.x) {  // every unit of this CTA
+        const int g = u % p.n_kv, split = u / p.n_kv;
+        int jlo, jhi;
+        attn_range(seq, 0, split, n_active, &jlo, &jhi);
+        const int j1 = min(jhi, c.pos);
+        if (j1 <= jlo) continue;
+        const float* kb = A.kc + (size_t)g * p.max_seq * p.hd;
+        const float* vb = A.vc + (size_t)g * p.max_seq * p.hd;
+        prefetch_l2(kb + (size_t)jlo * p.hd, kb + (size_t)j1 * p.hd);
+        prefetch_l2(vb + (size_t)jlo * p.hd, vb + (size_t)j1 * p.hd);
+    }
 }
 
 template <int EPL, int GMAX>
