@@ -72,7 +72,7 @@ struct GemvCfg {
 };
 using GemvC32 = GemvCfg<1, 1, 4>;   // K <= 1024:  32 rows per chunk
 using GemvC64 = GemvCfg<1, 2, 2>;   // K <= 2048:  16 rows
-using GemvC96 = GemvCfg<1, 3, 1>;   // K <= 3072:   8 rows
+using GemvC96 = GemvCfg<1, 3, 2>;   // K <= 3072:  16 rows
 using GemvC128 = GemvCfg<2, 2, 2>;  // K <= 4096:   8 rows (18 KB chunks at 4096, no idle lanes)
 using GemvC192 = GemvCfg<2, 3, 1>;  // K <= 6144:   4 rows
 using GemvC256 = GemvCfg<4, 2, 2>;  // K <= 8192:   4 rows
