@@ -74,9 +74,9 @@ using GemvC32 = GemvCfg<1, 1, 4>;   // K <= 1024:  32 rows per chunk
 using GemvC64 = GemvCfg<1, 2, 2>;   // K <= 2048:  16 rows
 using GemvC96 = GemvCfg<1, 3, 2>;   // K <= 3072:  16 rows
 using GemvC128 = GemvCfg<2, 2, 2>;  // K <= 4096:   8 rows (18 KB chunks at 4096, no idle lanes)
-using GemvC192 = GemvCfg<2, 3, 1>;  // K <= 6144:   4 rows
+using GemvC192 = GemvCfg<2, 3, 2>;  // K <= 6144:   8 rows
 using GemvC256 = GemvCfg<4, 2, 2>;  // K <= 8192:   4 rows
-using GemvC384 = GemvCfg<4, 3, 1>;  // K <= 12288:  2 rows
+using GemvC384 = GemvCfg<4, 3, 2>;  // K <= 12288:  4 rows
 using GemvC768 = GemvCfg<8, 3, 1>;  // K <= 24576:  1 row
 
 constexpr uint64_t GEMV_WAIT_NS = 2000000000ull;  // 2 s
