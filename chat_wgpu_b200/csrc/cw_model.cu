@@ -206,8 +206,10 @@ struct AArgs {
     float* q_out;  // optional: the normed, rotated q rows (hook tap "q")
 };
 
+constexpr int FA_NW = 8;  // warps of the per-stage attention CTA (FA_NW*4 keys per pass)
+
 template <int EPL, int GMAX>
-__global__ void __launch_bounds__(128) k_fattn(AArgs a) {
+__global__ void __launch_bounds__(FA_NW * 32) k_fattn(AArgs a) {
     extern __shared__ float sm[];
     const int G = a.n_heads / a.n_kv, hd = a.hd;
     const int g = blockIdx.y, split = blockIdx.x;
@@ -233,11 +235,11 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
             prefetch_l2(vb0 + (size_t)jlo * hd, vb0 + (size_t)j1 * hd);
         }
     }
-    float* qs = sm + attn_smem_floats(G, hd, a.n_splits);  // [G][hd]
+    float* qs = sm + attn_smem_floats(G, hd, a.n_splits, FA_NW);  // [G][hd]
     float* ks = qs + (size_t)G * hd;           // [hd]
     const int qd = a.n_heads * hd, kvd = a.n_kv * hd;
     const int nrows = G + (holds ? 1 : 0);
-    for (int r = warp; r < nrows; r += 4) {
+    for (int r = warp; r < nrows; r += FA_NW) {
         const bool isq = r < G;
         const float* src = isq ? a.qkv + (size_t)(g * G + r) * hd : a.qkv + qd + (size_t)g * hd;
         const float* nw = isq ? a.q_norm : a.k_norm;
@@ -291,9 +293,9 @@ __global__ void __launch_bounds__(128) k_fattn(AArgs a) {
         }
     }
     __syncthreads();
-    float* res = sm + 4 * G * (hd + 2);
-    float* cwt = sm + 5 * G * (hd + 2);
-    attn_core<EPL, GMAX, KV_PLAIN>(qs, G, hd, kbase, vbase, hd, jlo, jhi, a.scale, a.softcap, sm,
+    float* res = sm + FA_NW * G * (hd + 2);
+    float* cwt = sm + (FA_NW + 1) * G * (hd + 2);
+    attn_core<EPL, GMAX, KV_PLAIN, FA_NW>(qs, G, hd, kbase, vbase, hd, jlo, jhi, a.scale, a.softcap, sm,
                                    res);
     attn_finish(res, G, hd, g, split, n_active, a.n_splits, a.part, a.counters, a.out, cwt);
 }
@@ -587,7 +589,7 @@ static int fattn_go(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
     if (smem > 48 * 1024)
         CW_CUDA(cudaFuncSetAttribute(k_fattn<EPL, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem));
-    CW_TRY(launch_k(ctx, k_fattn<EPL, GM>, grid, dim3(128), smem, a));
+    CW_TRY(launch_k(ctx, k_fattn<EPL, GM>, grid, dim3(FA_NW * 32), smem, a));
     return CW_OK;
 }
 
@@ -604,7 +606,7 @@ static int launch_fattn_e(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
 }
 
 static size_t fattn_smem(int G, int hd, int n_splits) {
-    return (attn_smem_floats(G, hd, n_splits) + (size_t)G * hd + hd) * sizeof(float);
+    return (attn_smem_floats(G, hd, n_splits, FA_NW) + (size_t)G * hd + hd) * sizeof(float);
 }
 
 static int launch_fattn(cw_ctx* ctx, const AArgs& a) {
