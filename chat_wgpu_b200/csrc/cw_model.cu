@@ -206,10 +206,14 @@ struct AArgs {
     float* q_out;  // optional: the normed, rotated q rows (hook tap "q")
 };
 
-constexpr int FA_NW = 8;  // warps of the per-stage attention CTA (FA_NW*4 keys per pass)
+// Warps of the per-stage attention CTA (4 keys each per pass): 16, or 8 for
+// the variants whose per-lane state (EPL x GMAX) would not fit 128 registers.
+template <int EPL, int GMAX>
+constexpr int fa_nw() { return EPL * GMAX <= 16 ? 16 : 8; }
 
 template <int EPL, int GMAX>
-__global__ void __launch_bounds__(FA_NW * 32) k_fattn(AArgs a) {
+__global__ void __launch_bounds__(fa_nw<EPL, GMAX>() * 32) k_fattn(AArgs a) {
+    constexpr int FA_NW = fa_nw<EPL, GMAX>();
     extern __shared__ float sm[];
     const int G = a.n_heads / a.n_kv, hd = a.hd;
     const int g = blockIdx.y, split = blockIdx.x;
@@ -585,7 +589,11 @@ static int proj(cw_ctx* ctx, const QW& w, FArgs a) {
 }
 
 template <int EPL, int GM>
-static int fattn_go(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
+static int fattn_go(cw_ctx* ctx, const AArgs& a, dim3 grid) {
+    constexpr int FA_NW = fa_nw<EPL, GM>();
+    const size_t smem =
+        (attn_smem_floats(a.n_heads / a.n_kv, a.hd, a.n_splits, FA_NW) +
+         (size_t)(a.n_heads / a.n_kv) * a.hd + a.hd) * sizeof(float);
     if (smem > 48 * 1024)
         CW_CUDA(cudaFuncSetAttribute(k_fattn<EPL, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem));
@@ -594,9 +602,9 @@ static int fattn_go(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
 }
 
 template <int EPL>
-static int launch_fattn_e(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
+static int launch_fattn_e(cw_ctx* ctx, const AArgs& a, dim3 grid) {
     int G = a.n_heads / a.n_kv;
-#define CW_FATTN(GM) CW_TRY((fattn_go<EPL, GM>(ctx, a, grid, smem)))
+#define CW_FATTN(GM) CW_TRY((fattn_go<EPL, GM>(ctx, a, grid)))
     if (G <= 1) CW_FATTN(1);
     else if (G <= 2) CW_FATTN(2);
     else if (G <= 4) CW_FATTN(4);
@@ -605,19 +613,13 @@ static int launch_fattn_e(cw_ctx* ctx, const AArgs& a, dim3 grid, size_t smem) {
     return check_launch("fused attention");
 }
 
-static size_t fattn_smem(int G, int hd, int n_splits) {
-    return (attn_smem_floats(G, hd, n_splits, FA_NW) + (size_t)G * hd + hd) * sizeof(float);
-}
-
 static int launch_fattn(cw_ctx* ctx, const AArgs& a) {
     dim3 grid(a.n_splits, a.n_kv);
-    int G = a.n_heads / a.n_kv;
-    size_t smem = fattn_smem(G, a.hd, a.n_splits);
     int epl = (a.hd + 31) / 32;
-    if (epl <= 1) return launch_fattn_e<1>(ctx, a, grid, smem);
-    if (epl <= 2) return launch_fattn_e<2>(ctx, a, grid, smem);
-    if (epl <= 4) return launch_fattn_e<4>(ctx, a, grid, smem);
-    return launch_fattn_e<8>(ctx, a, grid, smem);
+    if (epl <= 1) return launch_fattn_e<1>(ctx, a, grid);
+    if (epl <= 2) return launch_fattn_e<2>(ctx, a, grid);
+    if (epl <= 4) return launch_fattn_e<4>(ctx, a, grid);
+    return launch_fattn_e<8>(ctx, a, grid);
 }
 
 // ---- loading ----------------------------------------------------------------
