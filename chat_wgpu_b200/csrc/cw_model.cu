@@ -565,8 +565,12 @@ static int kq_fgemv_t(cw_ctx* ctx, const FArgs& a) {
                  "k-quant gemv: K=%d needs %zu bytes of shared memory", a.K, smem);
         CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     }
+    // as many CTAs as fit on the SMs at once: each warp's rows are latency-bound
+    int per_sm = 0;
+    CW_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem));
     const long rows = EPI == EPI_GLU ? a.N / 2 : a.N;
-    const int grid = (int)std::min<long>((rows + 7) / 8, (long)ctx->sm_count * 4);
+    const int grid =
+        (int)std::min<long>((rows + 7) / 8, (long)ctx->sm_count * std::max(per_sm, 1));
     CW_TRY(launch_k(ctx, kern, dim3(grid), dim3(256), smem, a));
     return check_launch("k-quant gemv");
 }
