@@ -3,8 +3,9 @@ one per GPU, each holding half of the heads, FFN columns and LM-head rows,
 with the O / down partial sums and the argmax all-reduced over NCCL.  The
 greedy stream must match the single-GPU stream and the oracle (same gates as
 test_gpu_model: tokens until the first ambiguous step, logits within 1e-3
-relative), the ranks must agree on every token, and the calls a
-tensor-parallel model does not support must fail cleanly."""
+relative), the ranks must agree on every token, a stop token must end every rank's
+stream at the same place, and the calls a tensor-parallel model does not
+support must fail cleanly."""
 import os
 import subprocess
 import sys
@@ -66,6 +67,11 @@ def test_tp2_matches_single_gpu_and_oracle(ctx, orc, tp_models, name, tmp_path):
     ranks = run_ranks(path, prompt, n_new, 2, str(tmp_path))
     # every rank produced the same tokens; the logits slices tile the vocabulary
     assert np.array_equal(ranks[0]["toks"], ranks[1]["toks"])
+    # with the 4th token as a stop token, the stream ends before its first occurrence
+    first = int(np.argmax(ranks[0]["toks"] == ranks[0]["toks"][3]))
+    for r in ranks:
+        assert bool(r["eos_stopped"])
+        assert np.array_equal(r["eos_toks"], ranks[0]["toks"][:first])
     vocab = int(ranks[0]["vocab"])
     assert vocab == om.vocab
     logits = np.zeros((n_new, vocab), np.float32)

@@ -42,8 +42,16 @@ def main(argv):
         raise AssertionError("expected CwError")
     t.set_sampling(0.0)  # greedy stays available
     t.close()
+    # a stop token (greedy): the stream ends before it, on every rank
+    e = Session(m, len(prompt) + n_new)
+    e.set_eos([int(toks[3])])
+    e.begin(prompt)
+    e.run(len(prompt) - 1 + n_new)
+    eos_toks, eos_stopped = e.tokens(), e.stopped
+    e.close()
     np.savez(out, toks=toks, logits=np.stack(logits), vocab_offset=m.vocab_offset,
-             vocab=m.vocab_size, weight_bytes=m.info["weight_bytes"])
+             vocab=m.vocab_size, weight_bytes=m.info["weight_bytes"], eos_toks=eos_toks,
+             eos_stopped=eos_stopped)
     s.close()
     m.close()
     ctx.close()
