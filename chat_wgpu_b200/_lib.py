@@ -111,6 +111,8 @@ SIGNATURES = {
     "cw_session_begin": [_vp, _vp, _sz],
     "cw_session_run": [_vp, _sz, C.POINTER(_sz)],
     "cw_session_prefill": [_vp, C.POINTER(_sz)],
+    "cw_session_set_prefill_chunk": [_vp, _sz],
+    "cw_gguf_inspect": [C.c_char_p, C.POINTER(_sz), C.POINTER(C.c_uint64)],
     "cw_session_set_sampling": [_vp, C.c_float, C.c_uint32, C.c_float, C.c_uint64],
     "cw_session_set_eos": [_vp, _vp, _sz],
     "cw_session_stopped": [_vp, C.POINTER(C.c_int)],

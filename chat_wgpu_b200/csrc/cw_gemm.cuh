@@ -16,7 +16,7 @@
 //
 // Three MMAs per K step into two f32 TMEM accumulators; the scaled low terms
 // keep every f16 operand in the normal range.  Max relative error against
-// an f64 dot is ~1e-4 on the SURVEY synthetic distribution, versus ~0.7 for
+// an f64 dot is ~1e-4 on the synthetic benchmark distribution, versus ~0.7 for
 // a single f16 pass (measured with the 1e-3*rms floor of the parity rule).
 //
 // Tile: 128 (M, one TMEM lane per row) x 128 (N) x 64 (K, one 128-byte

@@ -8,6 +8,7 @@
 #include <unistd.h>
 
 #include "../../include/chatcuda.h"
+#include "cw_common.h"
 
 namespace cw {
 
@@ -163,11 +164,18 @@ int GgufFile::open(const std::string& path, std::string& err) {
             c.bad = true;
             break;
         }
+        // a zero or overflowing dimension would break the size arithmetic
+        // below (rows = n_elems / dims[0], nbytes = row * rows)
         t.n_elems = 1;
         for (uint32_t d = 0; d < nd; d++) {
             uint64_t v = c.get<uint64_t>();
             t.dims.push_back(v);
-            t.n_elems *= v;
+            if (v == 0 || __builtin_mul_overflow(t.n_elems, v, &t.n_elems)) {
+                if (!c.bad) {
+                    err = "tensor " + t.name + ": zero or overflowing dimension";
+                    return CW_ERR_FORMAT;
+                }
+            }
         }
         t.type = c.get<uint32_t>();
         t.offset = c.get<uint64_t>();
@@ -188,11 +196,15 @@ int GgufFile::open(const std::string& path, std::string& err) {
     }
     const uint8_t* data = (const uint8_t*)p + ds;
     size_t data_len = map_len_ - ds;
+    data_bytes = data_len;
     for (size_t i = 0; i < tensors.size(); i++) {
         GgufTensor& t = tensors[i];
         size_t row = t.dims.empty() ? 0 : ggml_row_bytes(t.type, (size_t)t.dims[0]);
         size_t rows = t.dims.empty() ? 0 : (size_t)(t.n_elems / t.dims[0]);
-        t.nbytes = row * rows;
+        if (__builtin_mul_overflow(row, rows, &t.nbytes)) {
+            err = "tensor " + t.name + ": byte size overflows";
+            return CW_ERR_FORMAT;
+        }
         if (t.nbytes && (t.offset > data_len || t.nbytes > data_len - t.offset)) {
             err = "tensor " + t.name + " extends past the end of the file";
             return CW_ERR_FORMAT;
@@ -233,3 +245,15 @@ const GgufTensor* GgufFile::tensor(const std::string& name) const {
 }
 
 }  // namespace cw
+
+extern "C" int cw_gguf_inspect(const char* path, size_t* n_tensors, uint64_t* data_bytes) {
+    cw::clear_error();
+    CW_CHECK(path, CW_ERR_INVALID_ARG, "cw_gguf_inspect: path is NULL");
+    cw::GgufFile f;
+    std::string err;
+    const int rc = f.open(path, err);
+    if (rc != CW_OK) return cw::set_error(rc, "%s", err.c_str());
+    if (n_tensors) *n_tensors = f.tensors.size();
+    if (data_bytes) *data_bytes = f.data_bytes;
+    return CW_OK;
+}

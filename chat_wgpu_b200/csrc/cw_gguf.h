@@ -61,6 +61,7 @@ public:
     bool has(const std::string& name) const { return tensor(name) != nullptr; }
 
     std::vector<GgufTensor> tensors;
+    size_t data_bytes = 0;  // size of the data section
 
 private:
     std::unordered_map<std::string, GgufMeta> meta_;

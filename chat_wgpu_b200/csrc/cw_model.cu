@@ -1734,6 +1734,15 @@ int cw_session_prefill(cw_session* s, size_t* n_done) {
     return check_launch("session prefill");
 }
 
+int cw_session_set_prefill_chunk(cw_session* s, size_t rows) {
+    clear_error();
+    CW_CHECK(s, CW_ERR_INVALID_ARG, "cw_session_set_prefill_chunk: session is NULL");
+    CW_CHECK(rows <= 4096, CW_ERR_INVALID_ARG,
+             "cw_session_set_prefill_chunk: %zu rows (1..4096, or 0 for the default)", rows);
+    s->pf_chunk = rows;
+    return CW_OK;
+}
+
 int cw_session_read_kv(cw_session* s, uint32_t layer, size_t n_pos, float* k, float* v) {
     clear_error();
     CW_CHECK(s && k && v && layer < s->m->info.n_layers && n_pos <= s->max_seq,

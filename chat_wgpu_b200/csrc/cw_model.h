@@ -114,6 +114,7 @@ struct cw_session {
     float* opart = nullptr;             // per-head O-projection row sums (persistent step)
     void* pf_mem = nullptr;             // batched-prefill scratch (cw_prefill.cu), grown on demand
     size_t pf_bytes = 0;
+    size_t pf_chunk = 0;                // rows per prefill chunk (0 = PF_CHUNK)
     // sampling and stop tokens (cw_sample.cu); temperature 0 = greedy
     float smp_temperature = 0.f, smp_top_p = 1.f;
     unsigned smp_top_k = 0;

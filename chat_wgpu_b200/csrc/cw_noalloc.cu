@@ -2,9 +2,8 @@
 // device memory.
 //
 // Some hosts must not call cudaMalloc on the decode path: a runtime that owns
-// every device allocation through its own pool, code running while a CUDA
-// graph is being captured or replayed, or a plugin inside a process whose
-// allocator must never see a new block.  cw_attention (the op of
+// every device allocation through its own pool, or a plugin inside a process
+// whose allocator must never see a new block.  cw_attention (the op of
 // attention.rs:7-38) needs scratch memory for its split-KV partial results
 // and the per-kv-head counters that elect the CTA merging the splits, and
 // takes both from the context's arena.  This entry point takes the same
@@ -16,7 +15,9 @@
 // the library until the process exits.  All calls on a device share it and it
 // keeps the last call's contents: the counters are cleared by every call
 // before its kernel, and two calls whose kernels overlap on the GPU (different
-// streams, no ordering between them) race on it.
+// streams, no ordering between them) race on it.  The array's device address
+// is looked up once per device and kept for the life of the process, so the
+// entry point must not be used on a device after cudaDeviceReset there.
 #include <mutex>
 
 #include "cw_common.h"
@@ -49,6 +50,24 @@ static int scratch_address(int device, void** out) {
     return CW_OK;
 }
 
+// Makes a device current for the length of one call and restores the
+// thread's previous current device on destruction.
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t enter(int device) {
+        cudaError_t e = cudaGetDevice(&prev);
+        if (e != cudaSuccess) {
+            prev = -1;
+            return e;
+        }
+        return prev == device ? cudaSuccess : cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
 }  // namespace cw
 
 using namespace cw;
@@ -68,7 +87,10 @@ extern "C" int cw_attention_noalloc(int device, void* stream, const float* q, co
     CW_CHECK(head_dim > 0 && head_dim <= 256, CW_ERR_INVALID_ARG,
              "cw_attention_noalloc: head_dim %zu (1..256)", head_dim);
     CW_CHECK(seq > 0 && seq < (1u << 30), CW_ERR_INVALID_ARG, "cw_attention_noalloc: seq must be >= 1");
-    CW_CUDA(cudaSetDevice(device));
+    // the lookups below need `device` current; the caller's current device
+    // is put back on every return path
+    DeviceGuard guard;
+    CW_CUDA(guard.enter(device));
     int sm = 0;
     CW_CUDA(cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, device));
     // the same split count as cw_attention, so both give the same result

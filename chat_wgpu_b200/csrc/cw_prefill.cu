@@ -628,9 +628,7 @@ int session_prefill(cw_session* s, size_t* n_done) {
     const size_t end = s->n_prompt - 1;  // the last prompt token runs through the decode step
     size_t done = 0;
     if (s->host_pos < end) {
-        size_t chunk = PF_CHUNK;
-        if (const char* e = getenv("CW_PREFILL_CHUNK"))  // smaller chunks (tests of the chunk seams)
-            chunk = std::max(1, std::min(atoi(e), PF_CHUNK));
+        const size_t chunk = s->pf_chunk ? std::min<size_t>(s->pf_chunk, PF_CHUNK) : PF_CHUNK;
         const size_t C = std::min<size_t>(end - s->host_pos, chunk);
         const PfLayout L = pf_layout(s->m, C);
         if (s->pf_bytes < L.total) {

@@ -320,10 +320,6 @@ static int build_variant(cw_session* s, bool fused, int grid, int n_splits, size
     pp.n_splits = n_splits;
     pp.part_stride = s->n_splits;
     pp.attn_min = MK_ATTN_MIN;
-    if (const char* ev = getenv("CW_ATTN_MIN_KEYS")) {  // tuning knob
-        const int v = atoi(ev);
-        if (v >= 1) pp.attn_min = v;
-    }
     pp.eps = I.eps;
     pp.inv_dim = 1.0f / (float)dim;
     pp.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
@@ -354,7 +350,6 @@ int step_plan_create(cw_session* s) {
     // the fused attention stage needs a CTA per query head and spare CTAs to fold
     P->has_fused = (int)I.n_heads < grid && I.n_layers > 0;
     P->fuse_max = MK_FUSE_MAX;
-    if (const char* ev = getenv("CW_FUSE_MAX_KEYS")) P->fuse_max = atoi(ev);  // tuning knob
     size_t need0 = 0, need1 = 0;
     CW_TRY(build_variant(s, false, grid, n_splits, work, &P->v[0], &need0));
     if (P->has_fused) CW_TRY(build_variant(s, true, grid, n_splits, work, &P->v[1], &need1));
@@ -389,8 +384,6 @@ void step_set_mode(cw_session* s, int mode) {
     StepPlan* P = s->plan;
     if (!P) return;
     P->fuse_max = mode == 2 ? 0 : mode == 3 ? (1 << 30) : MK_FUSE_MAX;
-    if (mode == 1)
-        if (const char* ev = getenv("CW_FUSE_MAX_KEYS")) P->fuse_max = atoi(ev);  // tuning knob
 }
 
 int step_variant(const cw_session* s) {

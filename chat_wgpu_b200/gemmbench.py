@@ -6,7 +6,7 @@ Algorithmic work is 2*M*N*K flops (the product the reference's token-by-
 token GEMVs would form); the kernel itself issues three f16 MMAs per K step
 (the hi/lo operand split), so its tensor-pipe work is 3x that.
 
-    python -m chat_wgpu_b200.gemmbench                # BASELINE prefill sweep, M = 128, 512
+    python -m chat_wgpu_b200.gemmbench                # prefill sweep, M = 128, 512
     python -m chat_wgpu_b200.gemmbench --rows 4096 --json
     python -m chat_wgpu_b200.gemmbench --rows 4096 --shape 4096 12288 --iters 2
 """

@@ -140,7 +140,7 @@ def random_q45_k_blocks(rng: np.random.Generator, rows: int, in_f: int, five: bo
     return b
 
 
-# Model shapes named by BASELINE.json's configs (random-init), plus the tiny
+# Benchmark model shapes (random-init: Qwen3-0.6B/8B, Gemma-2-2B), plus the tiny
 # shape of the reference's RandomWeights verify model (src/main.rs:166-174).
 CONFIGS = {
     "qwen3-0.6b": dict(arch="qwen3", dim=1024, n_layers=28, n_heads=16, n_kv=8, head_dim=128,

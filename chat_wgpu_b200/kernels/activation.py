@@ -1,4 +1,4 @@
-"""Gated activations (chat-wgpu src/kernels/activation.rs:92-110)."""
+"""Gated activations (chat-wgpu src/kernels/activation.rs:42-48)."""
 from ..context import Buffer
 from ._util import op
 

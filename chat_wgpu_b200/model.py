@@ -178,6 +178,10 @@ class Session:
         _lib.call("cw_session_prefill", self._h, C.byref(n))
         return n.value
 
+    def set_prefill_chunk(self, rows: int) -> None:
+        """Rows per prefill chunk (cw_session_set_prefill_chunk; 0 = default)."""
+        _lib.call("cw_session_set_prefill_chunk", self._h, int(rows))
+
     def read_kv(self, layer: int, n_pos: int) -> tuple[np.ndarray, np.ndarray]:
         """K and V cache rows [0, n_pos) of `layer`, each [n_kv, n_pos, head_dim]."""
         I = self.model.info

@@ -6,7 +6,7 @@ Each shape cycles through enough distinct weight copies (> 4x the L2 size)
 that every launch streams its weight from HBM; the launches are replayed as
 one CUDA graph and timed with CUDA events (cw_q4_0_gemv_bench).
 
-    python -m chat_wgpu_b200.q4bench            # BASELINE shape sweep
+    python -m chat_wgpu_b200.q4bench            # Qwen3 projection shape sweep
     python -m chat_wgpu_b200.q4bench --json
 """
 from __future__ import annotations
@@ -22,7 +22,7 @@ from .context import GpuContext
 from .gguf import random_q4_0_blocks
 from .kernels import q4
 
-# (in_f, out_f): Qwen3 0.6B/1.7B/4B/8B projections and LM heads (BASELINE.json config 2)
+# (in_f, out_f): Qwen3 0.6B/1.7B/4B/8B projections and LM heads
 SHAPES = [(1024, 2048), (1024, 3072), (3072, 1024), (2048, 6144), (6144, 2048), (2560, 9728),
           (9728, 2560), (4096, 12288), (12288, 4096), (1024, 151936), (2048, 151936),
           (2560, 151936), (4096, 151936)]
@@ -37,7 +37,7 @@ def bench_shape(ctx: GpuContext, in_f: int, out_f: int, iters: int = 200, seed: 
                 l2_bytes: int = 126 << 20) -> dict:
     rng = np.random.default_rng(seed)
     wbytes = out_f * (in_f // 32) * 18
-    n_w = max(2, min(64, -(-4 * l2_bytes // wbytes)))
+    n_w = max(2, min(512, -(-4 * l2_bytes // wbytes)))  # > 4x L2 (3.2x for K=1024, N=2048)
     blocks = random_q4_0_blocks(rng, out_f, in_f)
     ws = [q4.q4_0_upload(ctx, blocks, out_f, in_f) for _ in range(n_w)]
     x = ctx.storage(rng.normal(0, 1, in_f).astype(np.float32))

@@ -151,7 +151,7 @@ int cw_rmsnorm(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t dim, float e
 int cw_rmsnorm_unit(cw_ctx* ctx, cw_buf x, cw_buf w, size_t rows, size_t dim, float eps, cw_buf* out);
 /* rope::rope (rope.rs:8-27): rotate-half at position pos. */
 int cw_rope(cw_ctx* ctx, cw_buf x, size_t rows, size_t head_dim, size_t pos, float theta, cw_buf* out);
-/* activation::swiglu / activation::geglu (activation.rs:103-110). */
+/* activation::swiglu / activation::geglu (activation.rs:42-48). */
 int cw_swiglu(cw_ctx* ctx, cw_buf gate, cw_buf up, size_t n, cw_buf* out);
 int cw_geglu(cw_ctx* ctx, cw_buf gate, cw_buf up, size_t n, cw_buf* out);
 /* argmax::argmax (argmax.rs:11-18): 1-element u32 buffer, ties -> lowest. */
@@ -163,16 +163,19 @@ int cw_sample(cw_ctx* ctx, cw_buf logits, size_t n, float temperature, uint32_t 
 
 /* ---- attention without allocation ----------------------------------------
  * No counterpart in the reference.  For callers that cannot allocate device
- * memory -- a host whose own pool owns every device allocation, code running
- * while a CUDA graph is captured, a plugin whose process allocator must not
- * see new blocks: the single-query GQA attention of cw_attention, with q
+ * memory -- a host whose own pool owns every device allocation, or a plugin
+ * whose process allocator must not see new blocks: the single-query GQA
+ * attention of cw_attention, with q
  * [n_heads*head_dim], k/v [seq, n_kv*head_dim] and out [n_heads*head_dim]
  * passed as device pointers, and the split scratch (partial results and merge
  * counters) kept in one static device array of CW_NOALLOC_SCRATCH_BYTES per
  * GPU that loads the library (held until the process exits).  It calls no
  * cudaMalloc, cudaFree or other allocating routine.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture.  Every call
+ * device current; make that first call before any stream capture.  The
+ * address is kept for the life of the process: do not call this on a device
+ * after a cudaDeviceReset of it.  The calling thread's current device is the
+ * same after the call as before it.  Every call
  * shares the array and it keeps the last call's contents: each call clears
  * the counters it uses before its kernel, and calls whose kernels can overlap
  * on the GPU (e.g. on unordered streams) race.  Shapes whose partials exceed
@@ -258,6 +261,14 @@ typedef struct {
  * cw_session_prefill / cw_group_create / the persistent step take Q4_0
  * projections only. */
 int cw_model_load_gguf(cw_ctx* ctx, const char* path, cw_model** out);
+/* GgufFile::open (gguf.rs:65-106) without a device: parse the header, the
+ * metadata and the tensor table, and check that every tensor's dimensions are
+ * non-zero, its byte size does not overflow and it lies inside the file.
+ * *n_tensors and *data_bytes (the size of the data section; either may be
+ * NULL) describe the file.  CW_ERR_FORMAT for a malformed file (where the
+ * reference panics, gguf.rs:192,203,206), CW_ERR_NOT_FOUND when it cannot be
+ * opened.  cw_model_load_gguf runs the same checks first. */
+int cw_gguf_inspect(const char* path, size_t* n_tensors, uint64_t* data_bytes);
 int cw_model_free(cw_model* model);
 /* The whole model's shapes (for a tensor-parallel rank too; weight_bytes is
  * what this rank holds). */
@@ -300,6 +311,10 @@ int cw_session_run(cw_session* s, size_t n_steps, size_t* n_produced);
  * at a time, mod.rs:78-83).  Allocates a session scratch on first use.
  * *n_done (may be NULL) = positions processed. */
 int cw_session_prefill(cw_session* s, size_t* n_done);
+/* Rows per cw_session_prefill chunk: 1..4096 (0 = the default, 4096).  Smaller
+ * chunks bound the prefill scratch (about 40 KB per row for Qwen3-0.6B
+ * shapes) at the cost of more launches; results do not depend on it. */
+int cw_session_set_prefill_chunk(cw_session* s, size_t rows);
 /* Copy the K and V cache rows [0, n_pos) of `layer` to the host, each laid
  * out [n_kv][n_pos][head_dim] f32 (cache.rs:7-31 holds the same values). */
 int cw_session_read_kv(cw_session* s, uint32_t layer, size_t n_pos, float* k, float* v);

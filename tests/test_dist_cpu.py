@@ -66,14 +66,23 @@ def test_single_process_needs_no_group():
 
 def test_reference_arm_runs_on_rank0_only(monkeypatch):
     """Under torchrun only rank 0 times the CPU reference; other ranks return
-    at once without touching the model."""
+    at once without touching the model or opening a process group."""
     sys.path.insert(0, ROOT)
     import bench
 
-    class FakeDist:
-        rank, world = 1, 2
-
-    called = []
+    monkeypatch.setenv("RANK", "1")
+    monkeypatch.setenv("WORLD_SIZE", "2")
     monkeypatch.setattr(bench, "np", None)  # any model work on rank 1 would fail
-    assert bench.run_reference(object(), FakeDist()) is None
-    assert not called
+    monkeypatch.setattr(bench, "Dist", None)  # nor may it open a process group
+    assert bench.run_reference(object()) is None
+    monkeypatch.setattr(bench, "parse", lambda: type("A", (), {"impl": "reference"})())
+    assert bench.main() is None
+
+
+def test_reference_arm_uses_every_host_core(monkeypatch):
+    """torchrun exports OMP_NUM_THREADS=1; the reference arm must not inherit it."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    monkeypatch.setenv("OMP_NUM_THREADS", "1")
+    assert bench.host_threads() == len(os.sched_getaffinity(0))

@@ -3,7 +3,7 @@
 Every output row must equal the reference's GEMV of the same activation row
 (q4.wgsl:40-73 semantics, oracle orc_q4_0_gemv) within the north-star's 1e-3
 relative gate; the weights are dequantised bit-exactly by the oracle and the
-product is formed in f64 for the larger cases.  Shapes: BASELINE's prefill
+product is formed in f64 for the larger cases.  Shapes: the benchmark's prefill
 sweep (the projection shapes at 128 and 512 rows), ragged M/N/K edges (a
 partial 128-row tile, N not a multiple of the 128-wide tile, K with a
 trailing half 64-wide K step) and activation extremes."""

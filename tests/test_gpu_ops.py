@@ -131,7 +131,7 @@ SWEEP = [(1024, 2048), (1024, 3072), (3072, 1024), (2048, 6144), (6144, 2048), (
 
 @pytest.mark.parametrize("in_f,out_f", SWEEP + [(32, 1), (64, 3), (96, 17), (256, 513)])
 def test_q4_0_gemv_vs_oracle(ctx, orc, in_f, out_f):
-    """GGUF Q4_0 GEMV over the BASELINE shape sweep and ragged edge shapes."""
+    """GGUF Q4_0 GEMV over the benchmark shape sweep and ragged edge shapes."""
     from chat_wgpu_b200.kernels import q4
     rng = np.random.default_rng(in_f + 3 * out_f)
     blocks = q4_0_blocks(rng, out_f, in_f, zero_frac=0.01)

@@ -16,11 +16,12 @@ pytestmark = pytest.mark.gpu
 REL = 1e-3
 
 
-def _stream(model, prompt, max_new, prefill, persistent=None):
+def _stream(model, prompt, max_new, prefill, persistent=None, chunk=0):
     from chat_wgpu_b200.model import Session
     s = Session(model, len(prompt) + max_new)
     if persistent is not None:
         s.set_persistent(persistent)
+    s.set_prefill_chunk(chunk)
     s.begin(prompt)
     if prefill:
         assert s.prefill() == len(prompt) - 1
@@ -60,16 +61,15 @@ def test_prefill_vs_oracle(ctx, orc, models, name):  # noqa: F811
     om.close()
 
 
-@pytest.mark.parametrize("chunk", ["7", "128", "4096"])
-def test_prefill_chunks_long_prompt(ctx, models, monkeypatch, chunk):  # noqa: F811
+@pytest.mark.parametrize("chunk", [7, 128, 4096])
+def test_prefill_chunks_long_prompt(ctx, models, chunk):  # noqa: F811
     """A 300-token prompt in several chunks (the later chunks attend over
     cache rows the earlier ones wrote) equals the token-by-token steps; one
     299-row chunk takes the long-chunk GEMM path (split weights)."""
     from chat_wgpu_b200.model import Model
-    monkeypatch.setenv("CW_PREFILL_CHUNK", chunk)
     m = Model(ctx, models["small-qwen3"])
     prompt = np.random.default_rng(3).integers(0, m.info["vocab"], 300).astype(np.uint32)
-    t1, l1, kv1 = _stream(m, prompt, 8, prefill=True)
+    t1, l1, kv1 = _stream(m, prompt, 8, prefill=True, chunk=chunk)
     t2, l2, kv2 = _stream(m, prompt, 8, prefill=False)
     _kv_close(kv1, kv2)
     for i in range(len(l1)):

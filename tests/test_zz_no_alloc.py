@@ -1,7 +1,8 @@
 """cw_attention_noalloc: the attention entry point for callers that cannot
-allocate device memory (their own pool owns the device, or they run during
-CUDA-graph capture).  It must give the same result as cw_attention while
-keeping its split scratch in the library's static device array.
+allocate device memory (their own pool owns the device, or their process
+allocator must not see new blocks).  It must give the same result as
+cw_attention while keeping its split scratch in the library's static device
+array.
 
 This file sorts last so that a run stopping at the first failure has run
 every other test; it also passes on its own in a fresh process."""
