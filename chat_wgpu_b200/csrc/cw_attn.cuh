@@ -187,7 +187,7 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
 // otherwise publish this split's state to part[head][split][hd+2] and let the
 // last CTA of the kv head merge the n_active splits (the counter resets itself
 // to 0).  cwt is shared scratch of G*(n_active+1) floats for the merge weights.
-__device__ __forceinline__ void attn_finish(const float* res, int G, int hd, int g, int split,
+static __device__ __noinline__ void attn_finish(const float* res, int G, int hd, int g, int split,
                                             int n_active, int n_splits_alloc,
                                             float* __restrict__ part,
                                             unsigned* __restrict__ counters,

@@ -1,6 +1,6 @@
-// cw_kquant.cu -- GEMV and exact dequantisation over GGUF k-quant weights
-// kept in HBM as the raw GGUF blocks (formats and device code in
-// cw_kquant.cuh).
+// cw_kquant.cu -- GEMV and exact dequantisation over raw GGUF weights kept
+// in HBM as the file's blocks: the k-quants and F32 / F16 / BF16 / Q8_0 /
+// Q4_1 (formats and device code in cw_kquant.cuh).
 //
 // GEMV: one warp per output row; the 32 lanes split each super-block 8
 // weights apiece (Q4_K/Q5_K lane l: 64-weight chunk l/8, 4 bytes of nibbles
@@ -55,9 +55,14 @@ __global__ void k_kq_dequant(const uint8_t* __restrict__ wraw, long n_blocks,
 
 int kq_block_bytes(int type) {
     switch (type) {
-        case CW_GGUF_Q4_K: return 144;
-        case CW_GGUF_Q5_K: return 176;
-        case CW_GGUF_Q6_K: return 210;
+        case CW_GGUF_Q4_K: return KQ<CW_GGUF_Q4_K>::BYTES;
+        case CW_GGUF_Q5_K: return KQ<CW_GGUF_Q5_K>::BYTES;
+        case CW_GGUF_Q6_K: return KQ<CW_GGUF_Q6_K>::BYTES;
+        case CW_GGUF_F32: return KQ<CW_GGUF_F32>::BYTES;
+        case CW_GGUF_F16: return KQ<CW_GGUF_F16>::BYTES;
+        case CW_GGUF_BF16: return KQ<CW_GGUF_BF16>::BYTES;
+        case CW_GGUF_Q8_0: return KQ<CW_GGUF_Q8_0>::BYTES;
+        case CW_GGUF_Q4_1: return KQ<CW_GGUF_Q4_1>::BYTES;
         default: return 0;
     }
 }
@@ -95,9 +100,16 @@ int cw_kquant_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, int type, size_t in_f, size_
                                                (const float*)ex->ptr, (float*)ey->ptr);
         return check_launch("kquant gemv");
     };
-    if (type == CW_GGUF_Q4_K) return go(k_kq_gemv<CW_GGUF_Q4_K>);
-    if (type == CW_GGUF_Q5_K) return go(k_kq_gemv<CW_GGUF_Q5_K>);
-    return go(k_kq_gemv<CW_GGUF_Q6_K>);
+    switch (type) {
+        case CW_GGUF_Q4_K: return go(k_kq_gemv<CW_GGUF_Q4_K>);
+        case CW_GGUF_Q5_K: return go(k_kq_gemv<CW_GGUF_Q5_K>);
+        case CW_GGUF_F32: return go(k_kq_gemv<CW_GGUF_F32>);
+        case CW_GGUF_F16: return go(k_kq_gemv<CW_GGUF_F16>);
+        case CW_GGUF_BF16: return go(k_kq_gemv<CW_GGUF_BF16>);
+        case CW_GGUF_Q8_0: return go(k_kq_gemv<CW_GGUF_Q8_0>);
+        case CW_GGUF_Q4_1: return go(k_kq_gemv<CW_GGUF_Q4_1>);
+        default: return go(k_kq_gemv<CW_GGUF_Q6_K>);
+    }
 }
 
 int cw_kquant_dequant(cw_ctx* ctx, cw_buf w, int type, size_t rows, size_t in_f, cw_buf* out) {
@@ -115,12 +127,18 @@ int cw_kquant_dequant(cw_ctx* ctx, cw_buf w, int type, size_t rows, size_t in_f,
     OpScope scope(ctx, "kquant_dequant");
     const uint8_t* src = (const uint8_t*)ew->ptr;
     float* dst = (float*)eo->ptr;
-    if (type == CW_GGUF_Q4_K)
-        k_kq_dequant<CW_GGUF_Q4_K><<<grid, 256, 0, ctx->stream>>>(src, nb, dst);
-    else if (type == CW_GGUF_Q5_K)
-        k_kq_dequant<CW_GGUF_Q5_K><<<grid, 256, 0, ctx->stream>>>(src, nb, dst);
-    else
-        k_kq_dequant<CW_GGUF_Q6_K><<<grid, 256, 0, ctx->stream>>>(src, nb, dst);
+#define CW_KQ_DEQ(T) k_kq_dequant<T><<<grid, 256, 0, ctx->stream>>>(src, nb, dst)
+    switch (type) {
+        case CW_GGUF_Q4_K: CW_KQ_DEQ(CW_GGUF_Q4_K); break;
+        case CW_GGUF_Q5_K: CW_KQ_DEQ(CW_GGUF_Q5_K); break;
+        case CW_GGUF_F32: CW_KQ_DEQ(CW_GGUF_F32); break;
+        case CW_GGUF_F16: CW_KQ_DEQ(CW_GGUF_F16); break;
+        case CW_GGUF_BF16: CW_KQ_DEQ(CW_GGUF_BF16); break;
+        case CW_GGUF_Q8_0: CW_KQ_DEQ(CW_GGUF_Q8_0); break;
+        case CW_GGUF_Q4_1: CW_KQ_DEQ(CW_GGUF_Q4_1); break;
+        default: CW_KQ_DEQ(CW_GGUF_Q6_K); break;
+    }
+#undef CW_KQ_DEQ
     return check_launch("kquant dequant");
 }
 

@@ -1,14 +1,22 @@
-// cw_kquant.cuh -- device code of the GGUF k-quant formats (Q4_K, Q5_K,
-// Q6_K super-blocks of 256 weights): per-lane dequantisation and dot
-// products shared by the k-quant GEMV (cw_kquant.cu) and the model's Q6_K
-// embedding rows and LM head (cw_model.cu).
+// cw_kquant.cuh -- device code of the GGUF weight formats kept raw in HBM:
+// the k-quants (Q4_K, Q5_K, Q6_K super-blocks of 256 weights) and the other
+// types the reference's loader takes (F32, F16, Q4_1, Q8_0: tensor_f32,
+// src/loader/gguf.rs:109-121) plus BF16, each read 256 weights at a time
+// (a "group": one super-block, or 8 blocks of 32).  Per-lane dequantisation
+// and dot products shared by the raw-weight GEMV (cw_kquant.cu) and the
+// model's projections, embedding rows and LM heads (cw_model.cu).
 //
 // Q6_K follows the reference's dequant_q6_k (src/loader/dequant.rs:102-131):
-// w = (d * sc) * (q - 32), f32, left to right.  Q4_K / Q5_K are not in the
-// reference (dequant.rs:6, ROADMAP.md:52-53); they restate ggml's published
-// block_q4_K / block_q5_K layout: w = (d * sc) * q - (dmin * m).  Each
-// formula is evaluated in the stated order with one f32 rounding per
-// operation (no contraction), so dequantised values are exact to it.
+// w = (d * sc) * (q - 32), f32, left to right; Q8_0 dequant_q8_0 (:46-58)
+// w = d * q; Q4_1 dequant_q4_1 (:82-97) w = d * q + m; F16 f16_to_f32
+// (:9-21).  Q4_K / Q5_K are not in the reference (dequant.rs:6,
+// ROADMAP.md:52-53); they restate ggml's published block_q4_K / block_q5_K
+// layout: w = (d * sc) * q - (dmin * m).  BF16 is the top half of an f32
+// (dequant_bf16, dequant.rs:41-43, which the reference's tensor_f32 does not
+// dispatch).  Each formula is evaluated in the stated order with
+// one f32 rounding per operation (no contraction), so dequantised values are
+// exact to it.  The GEMV dot products group the same terms differently
+// (d * sum(q x) instead of sum((d q) x)): f32-accumulation grade.
 #pragma once
 
 #include <stdint.h>
@@ -19,20 +27,51 @@
 namespace cw {
 
 
+// Bytes of one 256-weight group and raw words one lane loads per group.
 template <int T>
 struct KQ;
 template <>
 struct KQ<CW_GGUF_Q4_K> {
-    static constexpr int BYTES = 144;
+    static constexpr int BYTES = 144, WORDS = 6;
 };
 template <>
 struct KQ<CW_GGUF_Q5_K> {
-    static constexpr int BYTES = 176;
+    static constexpr int BYTES = 176, WORDS = 6;
 };
 template <>
 struct KQ<CW_GGUF_Q6_K> {
-    static constexpr int BYTES = 210;
+    static constexpr int BYTES = 210, WORDS = 6;
 };
+template <>
+struct KQ<CW_GGUF_F32> {
+    static constexpr int BYTES = 1024, WORDS = 8;
+};
+template <>
+struct KQ<CW_GGUF_F16> {
+    static constexpr int BYTES = 512, WORDS = 4;
+};
+template <>
+struct KQ<CW_GGUF_BF16> {
+    static constexpr int BYTES = 512, WORDS = 4;
+};
+template <>
+struct KQ<CW_GGUF_Q8_0> {  // 8 blocks of 34 bytes: f16 d, 32 x int8
+    static constexpr int BYTES = 272, WORDS = 3;
+};
+template <>
+struct KQ<CW_GGUF_Q4_1> {  // 8 blocks of 20 bytes: f16 d, f16 m, 16 nibble bytes
+    static constexpr int BYTES = 160, WORDS = 2;
+};
+// The formats whose 8 weights per lane are 8 consecutive elements (lane l:
+// elements 8l .. 8l+7 of the group): the plain float types and Q8_0.
+template <int T>
+constexpr bool kq_consecutive() {
+    return T == CW_GGUF_F32 || T == CW_GGUF_F16 || T == CW_GGUF_BF16 || T == CW_GGUF_Q8_0;
+}
+
+__device__ __forceinline__ float kq_bf16(uint32_t bits16) {
+    return __uint_as_float((bits16 & 0xffffu) << 16);
+}
 
 __device__ __forceinline__ float kq_f16(const uint8_t* p) {
     return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
@@ -53,7 +92,41 @@ __device__ __forceinline__ void kq_scale_min(int j, const uint8_t* q, int* sc, i
 template <int T>
 __device__ __forceinline__ void kq_lane(const uint8_t* __restrict__ blk, int lane, float (&w)[8],
                                         int (&idx)[8]) {
-    if constexpr (T == CW_GGUF_Q6_K) {
+    if constexpr (T == CW_GGUF_F32) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            w[i] = reinterpret_cast<const float*>(blk)[8 * lane + i];
+            idx[i] = 8 * lane + i;
+        }
+    } else if constexpr (T == CW_GGUF_F16 || T == CW_GGUF_BF16) {
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(blk) + 8 * lane;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            w[i] = T == CW_GGUF_F16 ? kq_f16(blk + 2 * (8 * lane + i)) : kq_bf16(h[i]);
+            idx[i] = 8 * lane + i;
+        }
+    } else if constexpr (T == CW_GGUF_Q8_0) {
+        const int c = lane >> 2, j0 = 8 * (lane & 3);
+        const uint8_t* b = blk + 34 * c;
+        const float d = kq_f16(b);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            w[i] = __fmul_rn(d, (float)(int8_t)b[2 + j0 + i]);
+            idx[i] = 32 * c + j0 + i;
+        }
+    } else if constexpr (T == CW_GGUF_Q4_1) {
+        const int c = lane >> 2, j0 = 4 * (lane & 3);
+        const uint8_t* b = blk + 20 * c;
+        const float d = kq_f16(b), m = kq_f16(b + 2);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int q = b[4 + j0 + i];
+            w[i] = __fadd_rn(__fmul_rn(d, (float)(q & 0x0f)), m);
+            w[4 + i] = __fadd_rn(__fmul_rn(d, (float)(q >> 4)), m);
+            idx[i] = 32 * c + j0 + i;
+            idx[4 + i] = 32 * c + 16 + j0 + i;
+        }
+    } else if constexpr (T == CW_GGUF_Q6_K) {
         const int h = lane >> 4, l0 = 2 * (lane & 15), is = l0 >> 4;
         const uint8_t* ql = blk + 64 * h;
         const uint8_t* qh = blk + 128 + 32 * h;
@@ -107,13 +180,31 @@ __device__ __forceinline__ void kq_lane(const uint8_t* __restrict__ blk, int lan
 // several blocks' loads are in flight at once.
 template <int T>
 struct KqRaw {
-    uint32_t v[6];
+    uint32_t v[KQ<T>::WORDS];
 };
 
 template <int T>
 __device__ __forceinline__ KqRaw<T> kq_load(const uint8_t* __restrict__ blk, int lane) {
     KqRaw<T> r;
-    if constexpr (T == CW_GGUF_Q6_K) {  // 210-byte blocks: 2-byte alignment
+    if constexpr (T == CW_GGUF_F32) {  // 32 bytes at 32*lane (group starts are 16-byte aligned)
+        const uint4* b4 = reinterpret_cast<const uint4*>(blk) + 2 * lane;
+        const uint4 a = __ldg(b4), b = __ldg(b4 + 1);
+        r.v[0] = a.x; r.v[1] = a.y; r.v[2] = a.z; r.v[3] = a.w;
+        r.v[4] = b.x; r.v[5] = b.y; r.v[6] = b.z; r.v[7] = b.w;
+    } else if constexpr (T == CW_GGUF_F16 || T == CW_GGUF_BF16) {  // 16 bytes at 16*lane
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(blk) + lane);
+        r.v[0] = a.x; r.v[1] = a.y; r.v[2] = a.z; r.v[3] = a.w;
+    } else if constexpr (T == CW_GGUF_Q8_0) {  // block lane/4 (2-byte aligned): d, 8 codes
+        const uint16_t* b16 = reinterpret_cast<const uint16_t*>(blk + 34 * (lane >> 2));
+        const int o = 1 + 4 * (lane & 3);  // u16 index of the lane's first code pair
+        r.v[0] = __ldg(b16 + o) | ((uint32_t)__ldg(b16 + o + 1) << 16);
+        r.v[1] = __ldg(b16 + o + 2) | ((uint32_t)__ldg(b16 + o + 3) << 16);
+        r.v[2] = __ldg(b16);
+    } else if constexpr (T == CW_GGUF_Q4_1) {  // block lane/4 (4-byte aligned): d|m, 4 bytes
+        const uint32_t* b32 = reinterpret_cast<const uint32_t*>(blk + 20 * (lane >> 2));
+        r.v[0] = __ldg(b32);
+        r.v[1] = __ldg(b32 + 1 + (lane & 3));
+    } else if constexpr (T == CW_GGUF_Q6_K) {  // 210-byte blocks: 2-byte alignment
         const int h = lane >> 4, l0 = 2 * (lane & 15);
         const uint16_t* b16 = (const uint16_t*)blk;
         r.v[0] = __ldg(b16 + (64 * h + l0) / 2);              // ql[l0], ql[l0+1]
@@ -144,7 +235,44 @@ __device__ __forceinline__ float kq_h2f(uint32_t bits16) {
 template <int T>
 __device__ __forceinline__ float kq_dot(const KqRaw<T>& r, const float* __restrict__ xb, int lane,
                                         float acc) {
-    if constexpr (T == CW_GGUF_Q6_K) {
+    if constexpr (kq_consecutive<T>()) {
+        const float4 x0 = *reinterpret_cast<const float4*>(xb + 8 * lane);
+        const float4 x1 = *reinterpret_cast<const float4*>(xb + 8 * lane + 4);
+        const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        if constexpr (T == CW_GGUF_Q8_0) {  // d * sum(q x)
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                s = fmaf((float)(int8_t)((r.v[i >> 2] >> (8 * (i & 3))) & 0xff), x[i], s);
+            return fmaf(kq_h2f(r.v[2]), s, acc);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                float w;
+                if constexpr (T == CW_GGUF_F32) w = __uint_as_float(r.v[i]);
+                else if constexpr (T == CW_GGUF_F16) w = kq_h2f(r.v[i >> 1] >> (16 * (i & 1)));
+                else w = kq_bf16(r.v[i >> 1] >> (16 * (i & 1)));
+                acc = fmaf(w, x[i], acc);
+            }
+            return acc;
+        }
+    } else if constexpr (T == CW_GGUF_Q4_1) {  // d * sum(q x) + m * sum(x)
+        const int c = lane >> 2, j0 = 4 * (lane & 3);
+        const float4 xl = *reinterpret_cast<const float4*>(xb + 32 * c + j0);
+        const float4 xh = *reinterpret_cast<const float4*>(xb + 32 * c + 16 + j0);
+        const uint32_t q = r.v[1];
+        float s = (float)(q & 0x0f) * xl.x;
+        s = fmaf((float)((q >> 8) & 0x0f), xl.y, s);
+        s = fmaf((float)((q >> 16) & 0x0f), xl.z, s);
+        s = fmaf((float)((q >> 24) & 0x0f), xl.w, s);
+        s = fmaf((float)((q >> 4) & 0x0f), xh.x, s);
+        s = fmaf((float)((q >> 12) & 0x0f), xh.y, s);
+        s = fmaf((float)((q >> 20) & 0x0f), xh.z, s);
+        s = fmaf((float)(q >> 28), xh.w, s);
+        const float sx = ((xl.x + xl.y) + (xl.z + xl.w)) + ((xh.x + xh.y) + (xh.z + xh.w));
+        acc = fmaf(kq_h2f(r.v[0]), s, acc);
+        return fmaf(kq_h2f(r.v[0] >> 16), sx, acc);
+    } else if constexpr (T == CW_GGUF_Q6_K) {
         const int h = lane >> 4, l0 = 2 * (lane & 15), is = l0 >> 4;
         const float d = kq_h2f(r.v[5]);
         const uint32_t scw = is ? (r.v[3] >> 8) | (r.v[4] << 24) : r.v[3];  // sc[is..is+3]
@@ -256,10 +384,25 @@ __device__ __forceinline__ float q45k_elem(const uint8_t* __restrict__ blk, int 
 }
 
 // Element i of row `tok` of a token-embedding table: packed Q4_0 planes
-// (type 2, dequant.rs:62-78) or raw Q4_K / Q5_K / Q6_K blocks (dim % 256 == 0).
+// (type 2, dequant.rs:62-78) or the file's raw rows of any other type the
+// loader keeps raw (dim % 256 == 0).
 __device__ __forceinline__ float embed_elem(const uint8_t* __restrict__ payload,
                                             const __half* __restrict__ scales, int type,
                                             unsigned tok, int dim, int i) {
+    const size_t e = (size_t)tok * dim + i;
+    if (type == CW_GGUF_F32) return reinterpret_cast<const float*>(payload)[e];
+    if (type == CW_GGUF_F16) return kq_f16(payload + 2 * e);
+    if (type == CW_GGUF_BF16) return kq_bf16(reinterpret_cast<const uint16_t*>(payload)[e]);
+    if (type == CW_GGUF_Q8_0) {  // dequant.rs:46-58
+        const uint8_t* b = payload + (e >> 5) * 34;
+        return __fmul_rn(kq_f16(b), (float)(int8_t)b[2 + (i & 31)]);
+    }
+    if (type == CW_GGUF_Q4_1) {  // dequant.rs:82-97
+        const uint8_t* b = payload + (e >> 5) * 20;
+        const int j = i & 31, byte = b[4 + (j & 15)];
+        const int q = j < 16 ? (byte & 0x0f) : (byte >> 4);
+        return __fadd_rn(__fmul_rn(kq_f16(b), (float)q), kq_f16(b + 2));
+    }
     if (type == CW_GGUF_Q6_K)
         return q6k_elem(payload + ((size_t)tok * (dim / 256) + (i >> 8)) * 210, i & 255);
     if (type == CW_GGUF_Q4_K)

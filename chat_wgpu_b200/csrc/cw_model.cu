@@ -588,6 +588,11 @@ static int proj(cw_ctx* ctx, const QW& w, FArgs a) {
         case GGML_Q4_K: return kq_fgemv_t<GGML_Q4_K, PRO, EPI>(ctx, a);
         case GGML_Q5_K: return kq_fgemv_t<GGML_Q5_K, PRO, EPI>(ctx, a);
         case GGML_Q6_K: return kq_fgemv_t<GGML_Q6_K, PRO, EPI>(ctx, a);
+        case GGML_F32: return kq_fgemv_t<GGML_F32, PRO, EPI>(ctx, a);
+        case GGML_F16: return kq_fgemv_t<GGML_F16, PRO, EPI>(ctx, a);
+        case GGML_BF16: return kq_fgemv_t<GGML_BF16, PRO, EPI>(ctx, a);
+        case GGML_Q8_0: return kq_fgemv_t<GGML_Q8_0, PRO, EPI>(ctx, a);
+        case GGML_Q4_1: return kq_fgemv_t<GGML_Q4_1, PRO, EPI>(ctx, a);
         default: return set_error(CW_ERR_UNSUPPORTED, "projection of ggml type %d", w.type);
     }
 }
@@ -715,16 +720,24 @@ static int load_q4_or_q6k(cw_model* m, const GgufFile& f, const std::string& nam
                           QW* out);
 
 static bool is_kquant(uint32_t t) { return t == GGML_Q4_K || t == GGML_Q5_K || t == GGML_Q6_K; }
+// Types kept in HBM as the file's raw rows and read 256 weights at a time
+// (cw_kquant.cuh): the k-quants and the other types the reference's loader
+// dequantises (tensor_f32, gguf.rs:109-121: F32, F16, Q4_1, Q8_0), plus BF16
+// (dequant_bf16, dequant.rs:41-43).
+static bool is_raw(uint32_t t) {
+    return is_kquant(t) || t == GGML_F32 || t == GGML_F16 || t == GGML_BF16 || t == GGML_Q8_0 ||
+           t == GGML_Q4_1;
+}
 
-// k-quant tensors `names` of one type kept as raw GGUF blocks, stacked by rows
-// (or interleaved row by row: gate/up).
+// Raw-type tensors `names` of one type kept as the file's rows, stacked by
+// rows (or interleaved row by row: gate/up).
 static int load_kq(cw_model* m, const GgufFile& f, const std::vector<std::string>& names,
                    size_t in_f, bool interleave, QW* out) {
     std::vector<const GgufTensor*> parts;
     for (auto& n : names) {
         const GgufTensor* t = f.tensor(n);
         CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", n.c_str());
-        CW_CHECK(is_kquant(t->type) && t->type == f.tensor(names[0])->type, CW_ERR_UNSUPPORTED,
+        CW_CHECK(is_raw(t->type) && t->type == f.tensor(names[0])->type, CW_ERR_UNSUPPORTED,
                  "tensor %s is %s; expected %s", n.c_str(), ggml_type_name(t->type),
                  ggml_type_name(f.tensor(names[0])->type));
         CW_CHECK(in_f % 256 == 0 && !t->dims.empty() && t->dims[0] == in_f &&
@@ -918,7 +931,7 @@ static int load_proj(cw_model* m, const GgufFile& f, const std::vector<std::stri
                      size_t in_f, bool interleave, QW* out) {
     const GgufTensor* t = f.tensor(names[0]);
     CW_CHECK(t, CW_ERR_NOT_FOUND, "missing tensor %s", names[0].c_str());
-    if (is_kquant(t->type)) {
+    if (is_raw(t->type)) {
         CW_CHECK(m->tp_world == 1, CW_ERR_UNSUPPORTED,
                  "tensor %s is %s; tensor parallelism takes Q4_0 projections", names[0].c_str(),
                  ggml_type_name(t->type));
@@ -1066,7 +1079,7 @@ static int model_load(cw_model* m, const std::string& path) {
     {  // Q4_0 planes, or raw k-quant rows (dequantised per element by the embed kernels)
         const GgufTensor* te = f.tensor("token_embd.weight");
         CW_CHECK(te, CW_ERR_NOT_FOUND, "missing tensor token_embd.weight");
-        if (te->type == GGML_Q4_K || te->type == GGML_Q5_K)
+        if (te->type != GGML_Q6_K && is_raw(te->type))
             CW_TRY(load_kq(m, f, {"token_embd.weight"}, I.dim, false, &m->embed));
         else
             CW_TRY(load_q4_or_q6k(m, f, "token_embd.weight", I.dim, &m->embed));
@@ -1501,15 +1514,16 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     // split-KV: about two CTAs per SM, at most one split per 8 keys
     s->n_splits = std::max(1, std::min<int>((int)((max_seq + 7) / 8),
                                             2 * ctx->sm_count / (int)I.n_kv));
-    A((size_t)I.n_heads * s->n_splits * (I.head_dim + 2) * 4, (void**)&s->part);
+    // split rows of (head_dim + 4) floats: the persistent step's 16-byte-aligned layout
+    A((size_t)I.n_heads * s->n_splits * (I.head_dim + 4) * 4, (void**)&s->part);
     A(max_seq * 4, (void**)&s->prompt);
     A(max_seq * 4, (void**)&s->toks);
     A((size_t)I.n_kv * 4, (void**)&s->counters);
     A(sizeof(DevState), (void**)&s->st);
     A(2 * sizeof(unsigned long long), (void**)&s->bar);
-    // fixed-point residual accumulator (persistent step: FFN partial sums)
-    A((size_t)I.dim * sizeof(long long), (void**)&s->racc);
-    A((size_t)I.n_heads * I.dim * sizeof(float), (void**)&s->opart);
+    // fixed-point residual accumulators of the persistent step (O-projection
+    // and FFN partial sums by layer parity)
+    A((size_t)4 * I.dim * sizeof(long long), (void**)&s->racc);
     A((size_t)sample_params_size(), &s->smp_dev);
     A(qd * 4, (void**)&s->qtap);
     if (rc == CW_OK) rc = sample_params_write(s);
@@ -1561,7 +1575,7 @@ int cw_session_set_persistent(cw_session* s, int on) {
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     // captured graphs hold one path or the other
     destroy_graphs(s);
-    CW_CHECK(on >= 0 && on <= 3, CW_ERR_INVALID_ARG, "cw_session_set_persistent: mode %d", on);
+    CW_CHECK(on >= 0 && on <= 2, CW_ERR_INVALID_ARG, "cw_session_set_persistent: mode %d", on);
     s->use_persistent = on != 0;
     if (!on) {
         step_plan_free(s);
@@ -1572,7 +1586,6 @@ int cw_session_set_persistent(cw_session* s, int on) {
                  "the persistent step does not cover this model family");
         CW_TRY(step_plan_create(s));
     }
-    step_set_mode(s, on);
     return CW_OK;
 }
 
@@ -1596,6 +1609,10 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     CW_CUDA(cudaMemcpyAsync(s->prompt, prompt, n_prompt * 4, cudaMemcpyHostToDevice, s->ctx->stream));
     k_begin<<<1, 1, 0, s->ctx->stream>>>(s->st, s->prompt, (int)n_prompt, s->bar);
     CW_TRY(check_launch("session begin"));
+    // the persistent step's accumulators start from zero (a step that timed
+    // out may have left partial sums behind)
+    CW_CUDA(cudaMemsetAsync(s->racc, 0, (size_t)4 * s->m->info.dim * sizeof(long long),
+                            s->ctx->stream));
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     s->host_pos = 0;
     s->n_prompt = n_prompt;

@@ -97,12 +97,13 @@ struct cw_session {
     float *hidden = nullptr, *hidden_b = nullptr, *tmp = nullptr, *qkv = nullptr, *attn = nullptr;
     float *act = nullptr, *logits = nullptr, *xnorm = nullptr, *part = nullptr;
     unsigned *prompt = nullptr, *toks = nullptr, *counters = nullptr;
-    long long* racc = nullptr;  // fixed-point residual accumulator, dim words (persistent step)
+    // fixed-point residual accumulators of the persistent step, 4 x dim words:
+    // the O-projection and FFN partial sums by layer parity (Y0, Y1, Z0, Z1)
+    long long* racc = nullptr;
     cw::DevState* st = nullptr;
     int n_splits = 1;
     bool use_graph = true;
-    // captured steps, [step variant][decode]: variant 1 is the persistent
-    // step's fused short-context plan, 0 everything else
+    // captured steps, [step variant][decode] (one variant in use)
     cudaGraphExec_t graphs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
     size_t host_pos = 0, n_prompt = 0, n_produced = 0;
     unsigned* h_tok = nullptr;     // pinned, one token for per-step reads
@@ -111,7 +112,6 @@ struct cw_session {
     cw::StepPlan* plan = nullptr;
     bool use_persistent = true;
     unsigned long long* bar = nullptr;  // [0] grid-barrier counter, [1] head counter (monotonic)
-    float* opart = nullptr;             // per-head O-projection row sums (persistent step)
     void* pf_mem = nullptr;             // batched-prefill scratch (cw_prefill.cu), grown on demand
     size_t pf_bytes = 0;
     size_t pf_chunk = 0;                // rows per prefill chunk (0 = PF_CHUNK)
@@ -134,7 +134,6 @@ int step_plan_create(cw_session* s);
 void step_plan_free(cw_session* s);
 int step_enqueue(cw_session* s, bool decode);
 int step_variant(const cw_session* s);  // 0 or 1: which plan the next step uses
-void step_set_mode(cw_session* s, int mode);  // 1 auto, 2 split plan only, 3 fused plan only
 int step_profile(cw_session* s, size_t n_steps,
                  std::map<std::string, std::pair<uint32_t, double>>* agg);
 

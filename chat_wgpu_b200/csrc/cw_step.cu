@@ -48,7 +48,7 @@ static int colmajor_copy(cw_model* m, const QW& w, QW* out) {
     return CW_OK;
 }
 
-// Down projections (FFN stage) and O projections (fused attention stage) in
+// Down projections (FFN stage) and O projections (O-projection stage) in
 // column-block-major order, built once per model.
 static int build_colmajor(cw_model* m) {
     if (!m->down_cm.empty()) return CW_OK;
@@ -66,8 +66,7 @@ static int build_colmajor(cw_model* m) {
     return CW_OK;
 }
 
-// One stage list: 0 = split attention + O-projection stage (any context
-// length), 1 = fused attention + O projection (contexts up to fuse_max keys).
+// The stage list of the step.
 struct StepVariant {
     std::vector<const char*> names;  // stage names, for the profile
     MStage* d_stages = nullptr;      // stage table + issue table, one allocation
@@ -76,21 +75,17 @@ struct StepVariant {
 };
 
 struct StepPlan {
-    StepVariant v[2];
-    bool has_fused = false;
-    int fuse_max = 0;  // keys (position + 1) up to which variant 1 runs
+    StepVariant v[1];
     size_t smem = 0;
     int grid = 0;
     void (*kern)(MParams) = nullptr;
 };
 
-// Kernel variants (head_dim / 32, GQA group bound, config of K = dim,
-// config of K = q-dim): Qwen3-0.6B, Qwen3-1.7B, Qwen3-4B/8B, Llama-3.2-1B-like
-// shapes, and the two small test shapes.  Other shapes use the per-stage
-// kernels.
-#define CW_STEP_VARIANTS(X) \
-    X(4, 2, 0, 1) X(4, 2, 1, 1) X(4, 4, 2, 2) X(2, 4, 1, 1) X(2, 2, 0, 0) X(1, 4, 0, 0)
-#define CW_STEP_DECL(E, G, D, Q) StepKernel step_kernel_##E##_##G##_##D##_##Q();
+// Kernel variants (head_dim / 32, GQA group bound, GEMV config of K = dim):
+// Qwen3-0.6B, Qwen3-1.7B, Qwen3-4B/8B, Llama-3.2-1B-like shapes, and the
+// small test shapes.  Other shapes use the per-stage kernels.
+#define CW_STEP_VARIANTS(X) X(4, 2, 0) X(4, 2, 1) X(4, 4, 2) X(2, 4, 1) X(2, 2, 0) X(1, 4, 0)
+#define CW_STEP_DECL(E, G, D) StepKernel step_kernel_##E##_##G##_##D();
 CW_STEP_VARIANTS(CW_STEP_DECL)
 #undef CW_STEP_DECL
 
@@ -99,9 +94,9 @@ static int gmax_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 static StepKernel find_kernel(const cw_model_info& I) {
     const int G = I.n_heads / I.n_kv;
     const int epl = (I.head_dim + 31) / 32, gmax = gmax_of(G);
-    const int cd = mk_cfg_for(I.dim), cq = mk_cfg_for(I.n_heads * I.head_dim);
-#define CW_STEP_FIND(E, G_, D, Q) \
-    if (epl == E && gmax == G_ && cd == D && cq == Q) return step_kernel_##E##_##G_##_##D##_##Q();
+    const int cd = mk_cfg_for(I.dim);
+#define CW_STEP_FIND(E, G_, D) \
+    if (epl == E && gmax == G_ && cd == D) return step_kernel_##E##_##G_##_##D();
     CW_STEP_VARIANTS(CW_STEP_FIND)
 #undef CW_STEP_FIND
     return nullptr;
@@ -114,15 +109,12 @@ static size_t work_bytes_for(const cw_model_info& I, int n_splits) {
     const int kmax = std::max<int>(I.dim, std::max<int>(I.n_heads * I.head_dim, I.hidden));
     const int qd = I.n_heads * I.head_dim;
     // PRO_X: q24 planes of K <= kmax; PRO_NORM (K = dim): planes + hbuf + wbuf;
-    // PRO_ATTN: planes of K = qd + the merge weights
+    // O-projection stage: one head's q24 blocks
     const size_t gemv = std::max({al16(q24_bytes(kmax / 32)),
                                   al16(q24_bytes((int)I.dim / 32)) + (size_t)I.dim * 8,
-                                  al16(q24_bytes(qd / 32)) + (size_t)I.n_heads * (MK_DEFER + 1) * 4});
+                                  al16(q24_bytes(qd / 32))});
     const size_t attn = (attn_smem_floats(G, hd, n_splits, MK_WARPS) + (size_t)G * hd + hd) * 4;
-    // fused stage: attn_core scratch for one head, q, k, output, its q24 blocks
-    const size_t attno = al16(((size_t)(MK_WARPS + 1) * (hd + 2) + MK_WARPS) * 4) +
-                         (size_t)3 * hd * 4 + q24_bytes(hd / 32);
-    return al16(std::max({gemv, attn, attno}));
+    return al16(std::max(gemv, attn));
 }
 
 bool step_supported(const cw_model* m, const cw_session* s) {
@@ -140,30 +132,49 @@ bool step_supported(const cw_model* m, const cw_session* s) {
     return true;
 }
 
-// Stage list of one variant, uploaded to the device.
-static int build_variant(cw_session* s, bool fused, int grid, int n_splits, size_t work,
-                         StepVariant* V, size_t* smem_need) {
+// Rows per O-projection unit (query head x row chunk): the smallest of 128,
+// 256, 512, 1024 that gives at most one unit per CTA.
+static int ocol_rows(const cw_model_info& I, int grid) {
+    int rc = 128;
+    while (rc < MK_DOWN_ROWS && (long)I.n_heads * ((I.dim + rc - 1) / rc) > grid) rc *= 2;
+    return rc;
+}
+
+// The stage list, uploaded to the device.  Per layer l (p = l % 2):
+//   attn_in    residual = hidden + Y[1-p] + Z[1-p] (layer 0: the embedding row)
+//              -> rmsnorm -> QKV GEMV (+bias) -> qkv
+//   attention  QK-norm, RoPE, K/V row write, split-KV attention; every CTA
+//              also folds Y[1-p] and Z[1-p] into hidden and zeroes them
+//              (layer 0: zeroes the previous step's last-layer pair)
+//   o_proj     per (query head, row chunk): that head's split merge and its
+//              column blocks of W_o, partial sums added into Y[p]
+//   ffn        residual = hidden + Y[p] -> rmsnorm -> gate/up -> SwiGLU -> its
+//              column block of W_down, partial sums added into Z[p]
+// and the LM head on hidden + Y[p] + Z[p] of the last layer.  Y and Z are
+// fixed-point int64 accumulators (s->racc: Y[0], Y[1], Z[0], Z[1]).
+static int build_variant(cw_session* s, int grid, int n_splits, size_t work, StepVariant* V,
+                         size_t* smem_need) {
     cw_model* m = s->m;
     cw_ctx* ctx = s->ctx;
     const cw_model_info& I = m->info;
-    const int dim = (int)I.dim;
-    long long* A = s->racc;  // FFN down-projection partial sums (fixed point)
+    const int dim = (int)I.dim, L = (int)I.n_layers;
+    long long* Y[2] = {s->racc, s->racc + dim};
+    long long* Z[2] = {s->racc + 2 * dim, s->racc + 3 * dim};
     std::vector<MStage> st;
     std::vector<MIssue> is;
     auto gemv = [&](const char* name, const QW& w, int pro, int epi, const float* x,
                     const float* base, const float* norm_w, float* y, const float* bias,
-                    float* xn_out, int acc_in, long long* r1, long long* r2, int acc_zero) {
+                    float* xn_out, int acc_in, long long* r1, long long* r2) {
         V->names.push_back(name);
         MStage S = {};
         S.acc_in = acc_in;
-        S.acc_zero = acc_zero;
         S.racc = r1;
         S.racc2 = r2;
-        S.acc_clear = s->racc;
         S.kind = SK_GEMV;
         S.cfg = mk_cfg_for(w.in_f);
         // two slots per chunk where a CTA would otherwise take several chunks
-        if ((w.rows + mk_rc(S.cfg) - 1) / mk_rc(S.cfg) > grid) S.cfg += MK_NCFG;
+        // (always for the LM head: one head variant per kernel)
+        if ((w.rows + mk_rc(S.cfg) - 1) / mk_rc(S.cfg) > grid || epi == EPI_HEAD) S.cfg += MK_NCFG;
         S.pro = pro;
         S.epi = epi;
         S.K = w.in_f;
@@ -189,57 +200,60 @@ static int build_variant(cw_session* s, bool fused, int grid, int n_splits, size
         Is.nb = S.K / 32;
         Is.n = S.N;
         is.push_back(Is);
-        return (int)st.size() - 1;
     };
-    for (uint32_t li = 0; li < I.n_layers; li++) {
+    const int nbh = (int)I.head_dim / 32;          // column blocks per query head
+    const int orc = ocol_rows(I, grid);            // rows per O-projection unit
+    const int ocpb = std::min(nbh, MK_DOWN_ROWS / orc);  // column blocks per ring slot
+    for (int li = 0; li < L; li++) {
         const Layer& l = m->L[li];
+        const int p = li % 2, q = 1 - p;
         float* kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
         float* vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
-        // QKV: residual = hidden + A (the previous layer's FFN output)
-        const int qi = gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, nullptr,
-                            li == 0 ? nullptr : s->hidden, l.attn_norm, s->qkv, l.qkv_bias,
-                            nullptr, li == 0 ? 0 : 1, A, nullptr, 0);
-        if (li == 0 && fused) st[qi].zero_acc = 1;
-        if (fused) {
-            V->names.push_back("attention_o");
-            MStage T = {};
-            T.kind = SK_ATTNO;
-            T.q_norm = l.q_norm;
-            T.k_norm = l.k_norm;
-            T.kc = kc;
-            T.vc = vc;
-            T.per1 = (dim + MK_DOWN_ROWS - 1) / MK_DOWN_ROWS;
-            T.layer = (int)li;
-            T.y = s->hidden;  // hidden = (hidden + A) + O projection, A = 0
-            T.fold_a = A;
-            st.push_back(T);
-            const QW& ocm = m->wo_cm[li];
-            MIssue It = {};
-            It.kind = SK_ATTNO;
-            It.pay1 = ocm.payload;
-            It.sc1 = ocm.scales;
-            It.n0 = (int)I.n_heads;
-            It.per0 = (int)I.head_dim / 32;
-            It.per1 = T.per1;
-            It.dim = dim;
-            is.push_back(It);
-        } else {
-            V->names.push_back("attention");
-            MStage T = {};
-            T.kind = SK_ATTN;
-            T.q_norm = l.q_norm;
-            T.k_norm = l.k_norm;
-            T.kc = kc;
-            T.vc = vc;
-            st.push_back(T);
-            MIssue It = {};
-            It.kind = SK_ATTN;
-            is.push_back(It);
-            // the residual read here includes the previous layer's FFN output
-            // (accumulator A), which is folded in and cleared
-            gemv("attn_out", l.wo, PRO_ATTN, EPI_RESID, s->attn, nullptr, nullptr, s->hidden,
-                 nullptr, nullptr, li > 0 ? 1 : 0, A, nullptr, 1);
-        }
+        gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, nullptr, li == 0 ? nullptr : s->hidden,
+             l.attn_norm, s->qkv, l.qkv_bias, nullptr, li == 0 ? 0 : 2, Y[q], Z[q]);
+        V->names.push_back("attention");
+        MStage T = {};
+        T.kind = SK_ATTN;
+        T.layer = li;
+        T.q_norm = l.q_norm;
+        T.k_norm = l.k_norm;
+        T.kc = kc;
+        T.vc = vc;
+        T.y = s->hidden;
+        // layer 0: the accumulators the previous step's last layer left behind
+        const int zp = li == 0 ? (L - 1) % 2 : q;
+        T.acc_in = li == 0 ? 0 : 1;
+        T.racc = Y[zp];
+        T.racc2 = Z[zp];
+        st.push_back(T);
+        MIssue It = {};
+        It.kind = SK_ATTN;
+        is.push_back(It);
+        V->names.push_back("o_proj");
+        const QW& ocm = m->wo_cm[li];
+        MStage O = {};
+        O.kind = SK_OCOL;
+        O.K = (int)(I.n_heads * I.head_dim);
+        O.N = dim;
+        O.RC = orc;
+        O.nunits = (int)I.n_heads * ((dim + orc - 1) / orc);
+        O.per1 = ocpb;
+        O.per0 = nbh / ocpb;
+        O.payload2 = ocm.payload;
+        O.scales2 = ocm.scales;
+        O.acc_out = Y[p];
+        st.push_back(O);
+        MIssue Io = {};
+        Io.kind = SK_OCOL;
+        Io.pay1 = ocm.payload;
+        Io.sc1 = ocm.scales;
+        Io.n0 = O.nunits;
+        Io.rc = orc;
+        Io.nb = nbh;
+        Io.per0 = O.per0;
+        Io.per1 = ocpb;
+        Io.dim = dim;
+        is.push_back(Io);
         V->names.push_back("ffn");
         const QW& dcm = m->down_cm[li];
         MStage F = {};
@@ -253,15 +267,15 @@ static int build_variant(cw_session* s, bool fused, int grid, int n_splits, size
         F.per0 = 64 / F.RC;
         F.per1 = (dim + MK_DOWN_ROWS - 1) / MK_DOWN_ROWS;
         F.N2 = dim;
-        F.racc = A;
-        F.acc_in = 0;  // the residual is hidden alone here (A folded in before)
+        F.acc_in = 1;
+        F.racc = Y[p];
         F.payload = l.gate_up.payload;
         F.scales = l.gate_up.scales;
         F.payload2 = dcm.payload;
         F.scales2 = dcm.scales;
         F.base = s->hidden;
         F.norm_w = l.ffn_norm;
-        F.fold_a = A;  // the accumulator the down projection adds into
+        F.acc_out = Z[p];
         st.push_back(F);
         MIssue If = {};
         If.kind = SK_FFN;
@@ -278,8 +292,9 @@ static int build_variant(cw_session* s, bool fused, int grid, int n_splits, size
         If.dim = F.N2;
         is.push_back(If);
     }
+    const int lp = (L - 1) % 2;
     gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, s->hidden, m->final_norm, s->logits,
-         nullptr, s->xnorm, I.n_layers == 0 ? 0 : 1, A, nullptr, 0);
+         nullptr, s->xnorm, L == 0 ? 0 : 2, Y[lp], Z[lp]);
     V->n_stages = (int)st.size();
     *smem_need = (size_t)MK_SLOTS * MK_SLOT_BYTES + work + al16((size_t)dim * 4) +
                  is.size() * sizeof(MIssue);
@@ -318,15 +333,13 @@ static int build_variant(cw_session* s, bool fused, int grid, int n_splits, size
     pp.hd = (int)I.head_dim;
     pp.max_seq = (int)s->max_seq;
     pp.n_splits = n_splits;
+    pp.n_layers = L;
     pp.part_stride = s->n_splits;
     pp.attn_min = MK_ATTN_MIN;
     pp.eps = I.eps;
     pp.inv_dim = 1.0f / (float)dim;
     pp.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18
     pp.work_bytes = work;
-    pp.opart = s->opart;
-    pp.hctr = s->bar + 1;
-    pp.hctr_per_step = fused ? (int)(I.n_layers * I.n_heads) : 0;
     return CW_OK;
 }
 
@@ -347,13 +360,7 @@ int step_plan_create(cw_session* s) {
     const int n_splits = std::max(1, std::min(s->n_splits, grid / (int)I.n_kv));
     CW_TRY(build_colmajor(m));
     const size_t work = work_bytes_for(I, n_splits);
-    // the fused attention stage needs a CTA per query head and spare CTAs to fold
-    P->has_fused = (int)I.n_heads < grid && I.n_layers > 0;
-    P->fuse_max = MK_FUSE_MAX;
-    size_t need0 = 0, need1 = 0;
-    CW_TRY(build_variant(s, false, grid, n_splits, work, &P->v[0], &need0));
-    if (P->has_fused) CW_TRY(build_variant(s, true, grid, n_splits, work, &P->v[1], &need1));
-    P->smem = std::max(need0, need1);
+    CW_TRY(build_variant(s, grid, n_splits, work, &P->v[0], &P->smem));
     cudaFuncAttributes fa{};
     cudaError_t e = cudaFuncGetAttributes(&fa, P->kern);
     if (e == cudaSuccess && (long)(P->smem + fa.sharedSizeBytes) > (long)ctx->max_smem_optin)
@@ -380,16 +387,9 @@ void step_plan_free(cw_session* s) {
     s->plan = nullptr;
 }
 
-void step_set_mode(cw_session* s, int mode) {
-    StepPlan* P = s->plan;
-    if (!P) return;
-    P->fuse_max = mode == 2 ? 0 : mode == 3 ? (1 << 30) : MK_FUSE_MAX;
-}
-
 int step_variant(const cw_session* s) {
-    const StepPlan* P = s->plan;
-    if (!P || !P->has_fused) return 0;
-    return (int)(s->host_pos + 1) <= P->fuse_max ? 1 : 0;
+    (void)s;
+    return 0;
 }
 
 static int step_launch(cw_session* s, bool decode, unsigned long long* stamps) {

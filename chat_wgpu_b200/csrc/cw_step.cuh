@@ -98,11 +98,11 @@ inline int mk_rc(int cfg) {  // rows per chunk
 }
 inline int mk_ns(int cfg) { return cfg >= MK_NCFG ? 2 : 1; }  // ring slots per chunk
 
-enum { SK_GEMV = 0, SK_ATTN = 1, SK_FFN = 2, SK_ATTNO = 3 };
+enum { SK_GEMV = 0, SK_ATTN = 1, SK_FFN = 2, SK_OCOL = 3 };
 
-// Fixed-point residual accumulator: the FFN stage adds its down-projection
-// partial sums into int64 words scaled by 2^32 with integer atomics, so the
-// total does not depend on the order in which CTAs arrive.
+// Fixed-point residual accumulators: the O-projection and FFN stages add
+// their partial sums into int64 words scaled by 2^32 with integer atomics, so
+// the totals do not depend on the order in which CTAs arrive.
 constexpr float MK_FIX = 4294967296.0f;      // 2^32
 constexpr float MK_UNFIX = 2.3283064365386963e-10f;  // 2^-32
 constexpr int MK_DOWN_ROWS = MK_SLOT_PAY / 16;  // rows of one down-projection slot (1024)
@@ -111,29 +111,23 @@ __host__ __device__ __forceinline__ long long* acc_at(long long* a, int r) { ret
 struct MStage {
     int kind, cfg, pro, epi;
     int K, N, RC, nchunks;
-    // FFN stage: act blocks (units), gate/up chunks and down slots per unit
+    // FFN: act blocks (units), gate/up chunks and down slots per unit.
+    // OCOL: units (query head x RC-row chunk), ring slots per unit, column
+    // blocks per slot.
     int nunits, per0, per1, N2;
-    // residual accumulators (fixed point): acc_in = 0, 1 (racc) or 2 (racc,
-    // racc2) of them added, in that order, to the residual read here;
-    // acc_zero: zero racc at the rows this stage writes; zero_acc: clear the
-    // accumulator acc_clear (dim rows) at the start of a step
-    int acc_in, acc_zero, zero_acc;
-    int layer;                // ATTNO: layer index (head-counter target)
-    int pad1, pad2, pad3, pad4;
+    // PRO_NORM: the residual is base + racc (acc_in >= 1) + racc2 (acc_in ==
+    // 2), added in that order.  ATTN: acc_in 1 folds racc and racc2 into the
+    // residual base y (the same additions) and zeroes them; 0 only zeroes them.
+    int acc_in, layer, pad0, pad1;
     long long* racc;
     long long* racc2;
-    long long* acc_clear;     // the accumulator cleared by zero_acc
-    long long* fold_a;        // ATTNO: accumulator folded into y (the residual) by the
-                              // CTAs without a head; FFN: the accumulator it adds into
-    long long* fold_b;        // (unused)
-    const uint8_t* payload2;  // FFN: down projection, column-block-major [K/32 of down][dim][16]
-    const __half* scales2;    //      and its scales [K/32 of down][dim]
-    const void* pad_ptr0;
-    const void* pad_ptr1;
-    const void* pad_ptr2;
+    long long* acc_out;       // FFN / OCOL: the accumulator its partial sums are added into
+    long long* pad_acc;
+    const uint8_t* payload2;  // FFN: down projection, OCOL: O projection, column-block-major
+    const __half* scales2;    //      [K/32][rows][16] + scales [K/32][rows]
     const uint8_t* payload;
     const __half* scales;
-    const float* x;        // PRO_X input
+    const float* x;        // (unused)
     const float* base;     // PRO_NORM input (null: this CTA's embedding row)
     const float* norm_w;
     float* xn_out;         // CTA 0 stores the normalised input here
@@ -183,13 +177,8 @@ struct MParams {
     unsigned* counters;
     const float* inv_freq;
     int dim, n_heads, n_kv, hd, max_seq, n_splits, part_stride, decode;
+    int n_layers;
     int attn_min;  // keys per attention split before splitting further
-    // fused attention stage: per-head O-projection row sums [n_heads][dim],
-    // and the counter the head CTAs bump when theirs are stored (monotonic;
-    // DevState.ctr_base is its value at the start of the step)
-    float* opart;
-    unsigned long long* hctr;
-    int hctr_per_step;
     float eps, scale;
     float inv_dim;      // 1/dim: the mean of squares as a product (exact for power-of-two dims)
     size_t work_bytes;  // shared-memory work region (q24 + hbuf + wbuf, or attention scratch)
@@ -202,20 +191,15 @@ struct MParams {
 // keys per attention split in the persistent step: one iteration of all
 // 16 warps (4 keys each) before a split is worth its combine
 constexpr int MK_ATTN_MIN = MK_WARPS * ATTN_U;
-constexpr int MK_PRE = 2;  // epilogue addends preloaded per stage (chunks)
-// Contexts (position + 1) up to which a step uses the fused attention + O
-// projection stage (one CTA per query head over all keys); longer contexts
-// use split-KV attention and a separate O-projection stage.
-// The fused plan is measured slower than the split plan on Qwen3-0.6B at
-// every context length (its single-CTA attention and the cross-head fold sit
-// on the critical path), so by default no step uses it (mode 3 selects it).
-constexpr int MK_FUSE_MAX = 0;
 // With 2..MK_DEFER active key splits, the attention stage only publishes each
 // split's (accumulator, max, denominator) and the O-projection stage merges
-// the splits while it builds its input (no combine step, fence or counter
-// inside the attention stage); with more splits the attention stage combines.
+// the splits of its head while it builds its input (no combine step, fence or
+// counter inside the attention stage); with more splits the attention stage
+// combines.
 constexpr int MK_DEFER = 8;
-enum { PRO_ATTN = 2 };  // prologue: merged attention splits (see MK_DEFER)
+// Floats per published split row (accumulator[hd], max, denominator, 2 pad):
+// a multiple of four, so every row starts 16-byte aligned.
+__host__ __device__ constexpr int mk_part_w(int hd) { return hd + 4; }
 
 // per-CTA state shared by all threads
 struct MShared {
@@ -228,6 +212,9 @@ struct MShared {
     float asb;
     __align__(16) float red[2][MK_WARPS];  // CTA-sum partials, alternating per call
     unsigned long long keys[MK_WARPS];
+    // RoPE angle pos * inv_freq[k] of this step's position: sin and cos,
+    // computed once at the kernel start (every layer rotates at that position)
+    float rsin[64], rcos[64];
 };
 
 struct MCtx {
@@ -241,7 +228,6 @@ struct MCtx {
     int redsel;         // CTA-sum buffer of the next call
     int nch;            // chunks consumed (row-partial buffer parity)
     int pos;
-    unsigned long long hbase;   // head counter at the start of the step
     unsigned long long* stamp;  // this stage's stamps (profiling) or null
 };
 
@@ -286,11 +272,10 @@ __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned 
 
 // Thread 0: issue the copy of this CTA's next weight chunk (in the stage
 // order) into the next ring slot.  Returns false when the step has no more.
-__device__ __forceinline__ void mk_issue_copy(MCtx& c, const uint8_t* pay, const __half* sc,
-                                              unsigned pb, unsigned sb) {
-    MShared* sh = c.sh;
+__device__ __forceinline__ void mk_issue_copy(MShared* sh, unsigned char* ring, const uint8_t* pay,
+                                              const __half* sc, unsigned pb, unsigned sb) {
     const int slot = sh->issued % MK_SLOTS;
-    unsigned char* dst = c.ring + (size_t)slot * MK_SLOT_BYTES;
+    unsigned char* dst = ring + (size_t)slot * MK_SLOT_BYTES;
     // the slot's previous contents were read before the __syncthreads that
     // precedes this call (a generic-proxy read followed by an async-proxy
     // write: ordered by that barrier, no proxy fence)
@@ -302,28 +287,42 @@ __device__ __forceinline__ void mk_issue_copy(MCtx& c, const uint8_t* pay, const
     sh->issued++;
 }
 
-__device__ inline bool mk_issue_next(const MParams& p, MCtx& c) {
-    MShared* sh = c.sh;
-    while (sh->it_stage < p.n_stages) {
-        const MIssue& I = c.iss[sh->it_stage];
+// Out of line: one thread runs it once per weight chunk, and its single copy
+// keeps the stages' instruction streams short.
+static __device__ __noinline__ bool mk_issue_next_impl(MShared* sh, const MIssue* iss, unsigned char* ring,
+                                                int n_stages) {
+    while (sh->it_stage < n_stages) {
+        const MIssue& I = iss[sh->it_stage];
         const long u = blockIdx.x + (long)sh->it_t * gridDim.x;
         if (I.kind == SK_GEMV) {  // copy it_t: part it_t % per0 of this CTA's chunk it_t / per0
             const long ch = blockIdx.x + (long)(sh->it_t / I.per0) * gridDim.x;
             if (ch < I.n0) {
                 const long row0 = (ch * I.per0 + sh->it_t % I.per0) * I.rc;
                 const int rows = (int)max(0L, min((long)I.rc, (long)I.n - row0));
-                mk_issue_copy(c, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
+                mk_issue_copy(sh, ring, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
                               (unsigned)rows * I.nb * 16, (unsigned)rows * I.nb * 2);
                 sh->it_t++;
                 return true;
             }
         }
-        if (I.kind == SK_ATTNO && u < I.n0) {  // head u: row chunk j / per0, column block j % per0
-            const int j = sh->it_j, rc = j / I.per0, k = j % I.per0;
-            const int r0 = rc * MK_DOWN_ROWS, rows = min(MK_DOWN_ROWS, I.dim - r0);
-            const size_t off = ((size_t)u * I.per0 + k) * I.dim + r0;
-            mk_issue_copy(c, I.pay1 + off * 16, I.sc1 + off, (unsigned)rows * 16, (unsigned)rows * 2);
-            if (++sh->it_j == I.per0 * I.per1) {
+        if (I.kind == SK_OCOL && u < I.n0) {
+            // unit u = (query head h, rows [r0, r0 + rc)); ring slot it_j of
+            // the unit holds column blocks h*nb + it_j*per1 .. + per1 - 1 of
+            // the column-block-major O projection, per1 copies side by side
+            const int nch = (I.dim + I.rc - 1) / I.rc, h = (int)(u / nch);
+            const int r0 = (int)(u - (long)h * nch) * I.rc, rows = min(I.rc, I.dim - r0);
+            const int slot = sh->issued % MK_SLOTS;
+            unsigned char* dst = ring + (size_t)slot * MK_SLOT_BYTES;
+            mbar_expect_tx(&sh->full[slot], (unsigned)(I.per1 * rows * 18));
+            for (int i = 0; i < I.per1; i++) {
+                const size_t off = (size_t)(h * I.nb + sh->it_j * I.per1 + i) * I.dim + r0;
+                bulk_g2s_hint(dst + (size_t)i * I.rc * 16, I.pay1 + off * 16, (unsigned)rows * 16,
+                              &sh->full[slot], sh->pol);
+                bulk_g2s_hint(dst + MK_SLOT_PAY + (size_t)i * I.rc * 2, I.sc1 + off,
+                              (unsigned)rows * 2, &sh->full[slot], sh->pol);
+            }
+            sh->issued++;
+            if (++sh->it_j == I.per0) {
                 sh->it_j = 0;
                 sh->it_t++;
             }
@@ -333,13 +332,13 @@ __device__ inline bool mk_issue_next(const MParams& p, MCtx& c) {
             const int j = sh->it_j;
             if (j < I.per0) {  // gate/up rows [64u + j*rc, +rc)
                 const long row0 = u * 64 + (long)j * I.rc;
-                mk_issue_copy(c, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
+                mk_issue_copy(sh, ring, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
                               (unsigned)I.rc * I.nb * 16, (unsigned)I.rc * I.nb * 2);
             } else {  // down rows [k*1024, ...) of column block u
                 const int k = j - I.per0, r0 = k * MK_DOWN_ROWS;
                 const int rows = min(MK_DOWN_ROWS, I.dim - r0);
                 const size_t off = (size_t)u * I.dim + r0;
-                mk_issue_copy(c, I.pay1 + off * 16, I.sc1 + off, (unsigned)rows * 16,
+                mk_issue_copy(sh, ring, I.pay1 + off * 16, I.sc1 + off, (unsigned)rows * 16,
                               (unsigned)rows * 2);
             }
             if (++sh->it_j == I.per0 + I.per1) {
@@ -353,6 +352,9 @@ __device__ inline bool mk_issue_next(const MParams& p, MCtx& c) {
         sh->it_j = 0;
     }
     return false;
+}
+__device__ __forceinline__ bool mk_issue_next(const MParams& p, MCtx& c) {
+    return mk_issue_next_impl(c.sh, c.iss, c.ring, p.n_stages);
 }
 
 // Wait (bounded) for every copy issued and not yet consumed, so no bulk copy
@@ -378,7 +380,14 @@ __device__ inline void mk_fail(const MParams& p, MCtx& c) {
 // reaches `target`, and __syncthreads passes that on to the CTA.  The status
 // word and the time limit are checked every 64 polls.
 __device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long long target) {
-    __syncthreads();
+    // Warps 0..14 order their writes before thread 0's release arrive.  The
+    // last warp is left out: its global writes all precede an earlier full
+    // CTA barrier (chunk barriers, the attention unit's closing barrier), and
+    // its remaining work -- queueing the weight copies -- only touches this
+    // CTA's shared memory, so it overlaps the arrive and the poll and joins
+    // at the closing __syncthreads.
+    if ((threadIdx.x >> 5) != MK_WARPS - 1)
+        asm volatile("bar.sync 1, %0;" ::"n"(MK_THREADS - 32) : "memory");
     if (threadIdx.x == 0) {
         red_release_add(p.bar, 1ull);
         uint64_t t0 = 0;
@@ -452,104 +461,71 @@ __device__ __forceinline__ float4 f4_norm(const float4& h, float inv, const floa
                        __fmul_rn(__fmul_rn(h.z, inv), g.z), __fmul_rn(__fmul_rn(h.w, inv), g.w));
 }
 
-// The stage input as q24 planes.  PRO_X: x from global.  PRO_NORM: rmsnorm
-// of `base` with the gains (norm.wgsl:20-56).  PRO_ATTN: merged attention
-// splits.  Each batch issues all of its global loads before using any.
-template <int PRO>
+// Elements d0 .. d0+3 of query head h's attention output.  With 2..MK_DEFER
+// active splits: the merge of the splits' published states
+// (attention.wgsl:88-95 across splits: M = max_s m_s, c_s = exp(m_s - M),
+// L = sum_s l_s c_s, x = (sum_s acc_s c_s) / L), from split rows of
+// mk_part_w(hd) floats (16-byte aligned), so the four accumulator values and
+// the (m_s, l_s) pair of every split come in ONE round of L2 loads.  Else
+// the normalised output the attention stage wrote to p.attn.
+static __device__ __noinline__ float4 mk_head_out4(const float* attn, const float* part, int part_stride,
+                                            int hd, int h, int d0, int na) {
+    if (na < 2 || na > MK_DEFER)
+        return __ldcg(reinterpret_cast<const float4*>(attn + (size_t)h * hd + d0));
+    const int WP = mk_part_w(hd);
+    const float* ph = part + (size_t)h * part_stride * WP;
+    float4 pv[MK_DEFER];
+    float2 ml[MK_DEFER];
+#pragma unroll
+    for (int s = 0; s < MK_DEFER; s++) {
+        pv[s] = s < na ? __ldcg(reinterpret_cast<const float4*>(ph + (size_t)s * WP + d0))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        ml[s] = s < na ? __ldcg(reinterpret_cast<const float2*>(ph + (size_t)s * WP + hd))
+                       : make_float2(REF_NEG_INF, 0.f);
+    }
+    float M = ml[0].x;
+#pragma unroll
+    for (int s = 1; s < MK_DEFER; s++) M = s < na ? fmaxf(M, ml[s].x) : M;
+    float cc[MK_DEFER], L = 0.f;
+#pragma unroll
+    for (int s = 0; s < MK_DEFER; s++) {
+        cc[s] = s < na ? expf(ml[s].x - M) : 0.f;
+        L = s < na ? fmaf(ml[s].y, cc[s], L) : L;
+    }
+    // splits in groups of four, fixed summation tree
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s0 = 0; s0 < MK_DEFER; s0 += 4) {
+        float a[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            a[j][0] = pv[s0 + j].x * cc[s0 + j];
+            a[j][1] = pv[s0 + j].y * cc[s0 + j];
+            a[j][2] = pv[s0 + j].z * cc[s0 + j];
+            a[j][3] = pv[s0 + j].w * cc[s0 + j];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+            if (s0 < na) r[e] = r[e] + ((a[0][e] + a[1][e]) + (a[2][e] + a[3][e]));
+    }
+    const float inv = 1.0f / L;
+    return make_float4(r[0] * inv, r[1] * inv, r[2] * inv, r[3] * inv);
+}
+
+// The stage input as q24 planes: the rmsnorm of `base` (plus the fixed-point
+// accumulators acc_in names) with the gains (norm.wgsl:20-56).  Each batch
+// issues all of its global loads before using any.  Inputs of up to
+// 4 * MK_WARPS * MK_QB blocks (K <= 4096) are one batch held in registers;
+// BIG kernels (K up to 16384) also compile the staged multi-batch path.
+template <class LD>
+__device__ inline void mk_prologue_staged(const MParams& p, const MStage& S, const Q24& q,
+                                          float* hbuf, float* wbuf, MCtx& c, const LD& ld_src);
+template <bool BIG>
 __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24& q, float* hbuf,
                             float* wbuf, MCtx& c) {
     const int nb = S.K / 32, nq = nb / 4;  // quad groups (nb is a multiple of 8)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sub = lane >> 3, e0 = 4 * (lane & 7);
-    if (PRO == PRO_ATTN) {
-        // the attention output of 2..MK_DEFER splits per head, merged here
-        // (attention.wgsl:88-95 across splits): per head M = max_s m_s,
-        // c_s = exp(m_s - M), 1/L with L = sum_s l_s c_s; then
-        // x = (sum_s acc_s c_s) / L per element.  Each lane forms the weights
-        // of its own head from (m_s, l_s) loaded together with its partials,
-        // so the merge costs one round of L2 loads and no CTA barrier.
-        const int hd = p.hd, W = hd + 2, na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
-        for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
-            float4 v[MK_QB];
-#pragma unroll
-            for (int k = 0; k < MK_QB; k++) {
-                const int b = 4 * (t0 + k * MK_WARPS) + sub;
-                v[k] = f4_zero();
-                if (b < nb) {
-                    const int i0 = b * 32 + e0, h = i0 / hd, d0 = i0 - h * hd;
-                    const float* ph = p.part + (size_t)h * p.part_stride * W;
-                    // (m_s, l_s) of every split: 8-byte aligned pairs (W, hd even)
-                    float2 ml[MK_DEFER];
-#pragma unroll
-                    for (int s = 0; s < MK_DEFER; s++)
-                        ml[s] = s < na ? __ldcg(reinterpret_cast<const float2*>(ph + (size_t)s * W + hd))
-                                       : make_float2(REF_NEG_INF, 0.f);
-                    // splits in groups of four (d0 % 4 == 0: 8-byte aligned
-                    // float2 pairs); fixed summation tree
-                    float r[4] = {0.f, 0.f, 0.f, 0.f};
-                    float M = ml[0].x;
-#pragma unroll
-                    for (int s = 1; s < MK_DEFER; s++) M = s < na ? fmaxf(M, ml[s].x) : M;
-                    float cc[MK_DEFER], L = 0.f;
-#pragma unroll
-                    for (int s = 0; s < MK_DEFER; s++) {
-                        cc[s] = s < na ? expf(ml[s].x - M) : 0.f;
-                        L = s < na ? fmaf(ml[s].y, cc[s], L) : L;
-                    }
-#pragma unroll
-                    for (int s0 = 0; s0 < MK_DEFER; s0 += 4) {
-                        if (s0 >= na) break;
-                        float2 lo[4], hi[4];
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const float2* q2 =
-                                reinterpret_cast<const float2*>(ph + (size_t)(s0 + j) * W + d0);
-                            lo[j] = s0 + j < na ? __ldcg(q2) : make_float2(0.f, 0.f);
-                            hi[j] = s0 + j < na ? __ldcg(q2 + 1) : make_float2(0.f, 0.f);
-                        }
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            float a[4];
-#pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                const float2 t2 = e < 2 ? lo[j] : hi[j];
-                                a[j] = ((e & 1) ? t2.y : t2.x) * cc[s0 + j];
-                            }
-                            r[e] = r[e] + ((a[0] + a[1]) + (a[2] + a[3]));
-                        }
-                    }
-                    const float inv = 1.0f / L;
-                    v[k] = make_float4(r[0] * inv, r[1] * inv, r[2] * inv, r[3] * inv);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < MK_QB; k++) {
-                const int b = 4 * (t0 + k * MK_WARPS) + sub;
-                if (t0 + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
-            }
-        }
-        mk_clk(c, CLK_LOADED);
-        mk_clk(c, CLK_NORMED);
-        return;
-    }
-    if (PRO == PRO_X) {
-        for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
-            float4 v[MK_QB];
-#pragma unroll
-            for (int k = 0; k < MK_QB; k++) {
-                const int b = 4 * (t0 + k * MK_WARPS) + sub;
-                v[k] = b < nb ? __ldcg(reinterpret_cast<const float4*>(S.x + b * 32 + e0)) : f4_zero();
-            }
-#pragma unroll
-            for (int k = 0; k < MK_QB; k++) {
-                const int b = 4 * (t0 + k * MK_WARPS) + sub;
-                if (t0 + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
-            }
-        }
-        mk_clk(c, CLK_LOADED);
-        mk_clk(c, CLK_NORMED);
-        return;
-    }
     const float* src = S.base ? S.base : c.emb;
     const bool gsrc = S.base != nullptr;
     const bool wx = S.xn_out && blockIdx.x == 0;
@@ -562,7 +538,7 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
         return h;
     };
     float ss = 0.f;
-    if (nq <= MK_WARPS * MK_QB) {  // one batch: everything stays in registers
+    if (!BIG || nq <= MK_WARPS * MK_QB) {  // one batch: everything stays in registers
         float4 v[MK_QB], w[MK_QB];
 #pragma unroll
         for (int k = 0; k < MK_QB; k++) {
@@ -594,6 +570,18 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
         }
         return;
     }
+    if constexpr (BIG) mk_prologue_staged(p, S, q, hbuf, wbuf, c, ld_src);
+}
+
+// The multi-batch path of mk_prologue: inputs staged in shared memory.
+template <class LD>
+__device__ inline void mk_prologue_staged(const MParams& p, const MStage& S, const Q24& q,
+                                          float* hbuf, float* wbuf, MCtx& c, const LD& ld_src) {
+    const int nb = S.K / 32, nq = nb / 4;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane >> 3, e0 = 4 * (lane & 7);
+    const bool wx = S.xn_out && blockIdx.x == 0;
+    float ss = 0.f;
     for (int t0 = warp; t0 < nq; t0 += MK_WARPS * MK_QB) {
         float4 v[MK_QB], w[MK_QB];
 #pragma unroll
@@ -661,21 +649,13 @@ __device__ __forceinline__ float mk_block_dot(const uint4& w4, const uint4 (&xa)
 }
 
 // The input vector of a GEMV stage as q24 planes in the work region.
+constexpr int MK_ONE_BATCH_BLOCKS = 4 * MK_WARPS * MK_QB;
+template <class CF>
 __device__ __forceinline__ void mk_input(const MParams& p, const MStage& S, const Q24& q,
                                          MCtx& c) {
     float* hbuf = reinterpret_cast<float*>(c.work + al16(q24_bytes(q.nb)));
     float* wbuf = hbuf + S.K;
-    if (S.pro == PRO_NORM) {
-        mk_prologue<PRO_NORM>(p, S, q, hbuf, wbuf, c);
-    } else if (S.pro == PRO_ATTN) {
-        const int na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
-        if (na >= 2 && na <= MK_DEFER)
-            mk_prologue<PRO_ATTN>(p, S, q, hbuf, wbuf, c);
-        else
-            mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
-    } else {
-        mk_prologue<PRO_X>(p, S, q, hbuf, wbuf, c);
-    }
+    mk_prologue<(CF::NB_MAX > MK_ONE_BATCH_BLOCKS)>(p, S, q, hbuf, wbuf, c);
 }
 
 // This lane's blocks of the q24 planes, kept in registers for the chunk loop.
@@ -767,31 +747,25 @@ __device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int 
     return rb;
 }
 
-template <class CF>
+// GEMV stage over the rmsnorm of the residual: EPI_STORE (the QKV
+// projection, + bias) or EPI_HEAD (the LM head: logits and the argmax key).
+// Each variant compiles only its own epilogue: the step kernel's code is
+// streamed through the instruction caches once per layer, so what a stage
+// does not run should not sit in its instruction stream.
+template <class CF, int EPI>
 __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
+    static_assert(EPI == EPI_STORE || EPI == EPI_HEAD, "QKV or LM head");
     constexpr int WPR = CF::WPR, RC = CF::RC;
     const int nb = S.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (S.zero_acc)  // start of a step: the residual accumulators from zero
-        for (int r = blockIdx.x * MK_THREADS + tid; r < p.dim; r += gridDim.x * MK_THREADS)
-            *acc_at(S.acc_clear, r) = 0;
     if ((int)blockIdx.x >= S.nchunks) return true;  // no rows of this stage here
-    // epilogue addends (old residual or bias) of the first chunks, requested
-    // now so they arrive while the prologue runs
-    const bool has_pre = S.epi == EPI_RESID || (S.epi == EPI_STORE && S.bias);
-    float pre[MK_PRE];
-#pragma unroll
-    for (int t = 0; t < MK_PRE; t++) {
-        const long row = (blockIdx.x + (long)t * gridDim.x) * RC + tid;
-        pre[t] = 0.f;
-        if (has_pre && tid < RC && row < S.N) {
-            pre[t] = S.epi == EPI_RESID ? __ldcg(S.y + row) : __ldg(S.bias + row);
-            if (S.epi == EPI_RESID && S.acc_in)
-                pre[t] = pre[t] + __ll2float_rn(__ldcg(acc_at(S.racc, (int)row))) * MK_UNFIX;
-        }
-    }
+    // the bias of the first chunk's rows, requested now so it arrives while
+    // the prologue runs
+    float add = 0.f;
+    if (EPI == EPI_STORE && S.bias && tid < RC && (long)blockIdx.x * RC + tid < S.N)
+        add = __ldg(S.bias + (long)blockIdx.x * RC + tid);
     const Q24 q = q24_carve(c.work, nb);
-    mk_input(p, S, q, c);
+    mk_input<CF>(p, S, q, c);
     mk_clk(c, CLK_Q24);
     __syncthreads();
     MRegs<CF> R;
@@ -803,47 +777,28 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     for (long chunk = blockIdx.x; chunk < S.nchunks; chunk += gridDim.x, t++) {
         const long row0 = chunk * RC;
         const int rows = (int)min((long)RC, (long)S.N - row0);
-        float add = 0.f;
-#pragma unroll
-        for (int u = 0; u < MK_PRE; u++)
-            if (u == t) add = pre[u];
-        if (t >= MK_PRE && has_pre && tid < rows) {  // later chunks: requested before the wait
-            add = S.epi == EPI_RESID ? __ldcg(S.y + row0 + tid) : __ldg(S.bias + row0 + tid);
-            if (S.epi == EPI_RESID && S.acc_in)
-                add = add + __ll2float_rn(__ldcg(acc_at(S.racc, (int)row0 + tid))) * MK_UNFIX;
-        }
+        if (EPI == EPI_STORE && t > 0 && S.bias && tid < rows)  // requested before the wait
+            add = __ldg(S.bias + row0 + tid);
         const float* rb = mk_chunk<CF>(p, c, nb, rows, R, t == 0);
         if (!rb) return false;
         // epilogue: fixed-order sum of the WPR partials of each row
-        if (S.epi == EPI_GLU) {
-            if (tid < RC / 2 && 2 * tid + 1 < rows) {
-                const int r0 = 2 * tid;
-                float gv = 0.f, uv = 0.f;
-#pragma unroll
-                for (int w = 0; w < WPR; w++) {
-                    gv += rb[r0 * WPR + w];
-                    uv += rb[(r0 + 1) * WPR + w];
-                }
-                S.y[(row0 + r0) / 2] = silu_ref_f(gv) * uv;
-            }
-        } else if (tid < rows) {
+        if (tid < rows) {
             float vv = 0.f;
 #pragma unroll
             for (int w = 0; w < WPR; w++) vv += rb[tid * WPR + w];
             const long row = row0 + tid;
-            if (S.epi == EPI_HEAD) {
+            if (EPI == EPI_HEAD) {
                 S.y[row] = vv;
                 const unsigned long long kk = argmax_key(vv, (unsigned)row);
                 best = kk > best ? kk : best;
             } else {
-                S.y[row] = has_pre ? (S.epi == EPI_RESID ? add + vv : vv + add) : vv;
-                if (S.acc_zero) *acc_at(S.racc, (int)row) = 0;
+                S.y[row] = S.bias ? vv + add : vv;
             }
         }
     }
     if (c.stamp && tid == 0) c.stamp[2] = global_ns();
     mk_clk(c, CLK_MAIN);
-    if (S.epi == EPI_HEAD) {
+    if (EPI == EPI_HEAD) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const unsigned long long tt = __shfl_xor_sync(FULL, best, o);
@@ -865,7 +820,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
 // converted to one q24 block, and the down projection's column block u
 // (MK_DOWN_ROWS rows per ring slot, one Q4_0 block per row) turns them into a
 // partial sum for every output row, added into the fixed-point residual
-// accumulator S.fold_a (the next stage that reads the residual adds it).
+// accumulator S.acc_out (the next stage that reads the residual adds it).
 template <class CF>
 __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
     constexpr int WPR = CF::WPR, RC = CF::RC;
@@ -873,7 +828,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if ((int)blockIdx.x >= S.nunits) return true;
     const Q24 q = q24_carve(c.work, nb);
-    mk_input(p, S, q, c);
+    mk_input<CF>(p, S, q, c);
     mk_clk(c, CLK_Q24);
     __syncthreads();
     MRegs<CF> R;
@@ -931,7 +886,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
                 const float part = fmaf(d * asb, mk_block_dot(w4, xa, xb, acb), 0.f);
                 const long long fx = __float2ll_rn(part * MK_FIX);
                 if (ok)
-                    atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.fold_a, r0 + r)),
+                    atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.acc_out, r0 + r)),
                               (unsigned long long)fx);
             }
             if (__syncthreads_or(!ok)) {  // slot consumed
@@ -948,31 +903,31 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
 }
 
 // ---- attention stage: QK-norm + RoPE + K/V write + split-KV attention -----------
+// Pull the cached K/V rows [jlo, min(jhi, pos)) of attention unit u (kv head
+// u % n_kv, key split u / n_kv of n_active) of the layer at kc / vc into L2.
+__device__ __forceinline__ void mk_kv_prefetch_unit(const MParams& p, const float* kc,
+                                                    const float* vc, int u, int n_active,
+                                                    int pos) {
+    const int g = u % p.n_kv, split = u / p.n_kv;
+    int jlo, jhi;
+    attn_range(pos + 1, 0, split, n_active, &jlo, &jhi);
+    const int j1 = min(jhi, pos);
+    if (j1 <= jlo) return;
+    const float* kb = kc + (size_t)g * p.max_seq * p.hd;
+    const float* vb = vc + (size_t)g * p.max_seq * p.hd;
+    prefetch_l2(kb + (size_t)jlo * p.hd, kb + (size_t)j1 * p.hd);
+    prefetch_l2(vb + (size_t)jlo * p.hd, vb + (size_t)j1 * p.hd);
+}
+
 // Thread 0 of a CTA: pull the cached K/V rows of the attention units it will
-// run into L2 while the stage before it runs.
+// run into L2 while the stage before it runs (layer 0; later layers are
+// prefetched by the CTAs idle in the previous layer's attention stage, off
+// every critical path).
 __device__ inline void mk_kv_prefetch(const MParams& p, const MStage& A, const MCtx& c) {
     const int seq = c.pos + 1;
-    if (A.kind == SK_ATTNO) {  // unit = query head: all cached rows of its group
-        if ((int)blockIdx.x >= p.n_heads || c.pos == 0) return;
-        const int g = blockIdx.x / (p.n_heads / p.n_kv);
-        const float* kb = A.kc + (size_t)g * p.max_seq * p.hd;
-        const float* vb = A.vc + (size_t)g * p.max_seq * p.hd;
-        prefetch_l2(kb, kb + (size_t)c.pos * p.hd);
-        prefetch_l2(vb, vb + (size_t)c.pos * p.hd);
-        return;
-    }
     const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
-    for (int u = blockIdx.x; u < p.n_kv * n_active; u += gridDim.x) {  // every unit of this CTA
-        const int g = u % p.n_kv, split = u / p.n_kv;
-        int jlo, jhi;
-        attn_range(seq, 0, split, n_active, &jlo, &jhi);
-        const int j1 = min(jhi, c.pos);
-        if (j1 <= jlo) continue;
-        const float* kb = A.kc + (size_t)g * p.max_seq * p.hd;
-        const float* vb = A.vc + (size_t)g * p.max_seq * p.hd;
-        prefetch_l2(kb + (size_t)jlo * p.hd, kb + (size_t)j1 * p.hd);
-        prefetch_l2(vb + (size_t)jlo * p.hd, vb + (size_t)j1 * p.hd);
-    }
+    for (int u = blockIdx.x; u < p.n_kv * n_active; u += gridDim.x)  // every unit of this CTA
+        mk_kv_prefetch_unit(p, A.kc, A.vc, u, n_active, c.pos);
 }
 
 template <int EPL, int GMAX>
@@ -988,6 +943,32 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
     float* cwt = sm + (size_t)(MK_WARPS + 1) * G * (hd + 2);
     float* qs = cwt + (size_t)G * (p.n_splits + 1);
     float* ks = qs + (size_t)G * hd;
+    {
+        // Fold the previous layer's accumulators into the residual base:
+        // y[r] = (y[r] + racc[r]) + racc2[r] -- the additions every PRO_NORM
+        // prologue of that residual made -- then zero both (acc_in 0: zero
+        // only).  Nothing reads the residual during this stage; each CTA
+        // takes a slice of rows, independent of its attention unit.
+        const int rpc = (p.dim + gridDim.x - 1) / gridDim.x, r = blockIdx.x * rpc + tid;
+        if (S.racc && tid < rpc && r < p.dim) {
+            if (S.acc_in) {
+                float hv = __ldcg(S.y + r);
+                hv = hv + __ll2float_rn(__ldcg(acc_at(S.racc, r))) * MK_UNFIX;
+                hv = hv + __ll2float_rn(__ldcg(acc_at(S.racc2, r))) * MK_UNFIX;
+                S.y[r] = hv;
+            }
+            *acc_at(S.racc, r) = 0;
+            *acc_at(S.racc2, r) = 0;
+        }
+    }
+    if ((int)blockIdx.x >= units) {  // no unit here: prefetch the next layer's K/V rows
+        const int f = blockIdx.x - units;
+        if (tid == 0 && f < units && S.layer + 1 < p.n_layers) {
+            const size_t ls = (size_t)p.n_kv * p.max_seq * hd;  // one layer of the cache
+            mk_kv_prefetch_unit(p, S.kc + ls, S.vc + ls, f, n_active, pos);
+        }
+        return true;
+    }
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const int g = u % p.n_kv, split = u / p.n_kv;
         int jlo, jhi;
@@ -1012,8 +993,6 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
             }
         }
         const float vnew = (holds && tid < hd) ? __ldcg(p.qkv + qd + kvd + (size_t)g * hd + tid) : 0.f;
-        float sn0 = 0.f, cs0 = 1.f;
-        if (tid < nrows * half) sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid % half)), &sn0, &cs0);
         if (has_row) {  // QK-norm (qwen3.rs:154-155)
             float* dst = isq ? qs + (size_t)r * hd : ks;
             if (nw) {
@@ -1036,8 +1015,7 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
         for (int i = tid; i < nrows * half; i += blockDim.x) {  // RoPE (rope.wgsl:25-34)
             const int rr = i / half, kq = i - rr * half;
             float* row = rr < G ? qs + (size_t)rr * hd : ks;
-            float sn = sn0, cs = cs0;
-            if (i != tid) sincosf(__fmul_rn((float)pos, p.inv_freq[kq]), &sn, &cs);
+            const float sn = c.sh->rsin[kq], cs = c.sh->rcos[kq];
             const float lo = row[kq], hi = row[kq + half];
             row[kq] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
             row[kq + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
@@ -1058,10 +1036,10 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
         mk_clk(c, CLK_REGS);  // attention: this split's state merged
         if (c.stamp && tid == 0) c.stamp[2] = global_ns();
         if (n_active >= 2 && n_active <= MK_DEFER) {
-            const int W = hd + 2;
+            const int W = hd + 2, WP = mk_part_w(hd);
             for (int i = tid; i < G * W; i += blockDim.x) {
                 const int gi = i / W, d = i - gi * W;
-                p.part[((size_t)(g * G + gi) * p.part_stride + split) * W + d] = res[i];
+                p.part[((size_t)(g * G + gi) * p.part_stride + split) * WP + d] = res[i];
             }
         } else {
             attn_finish(res, G, hd, g, split, n_active, p.part_stride, p.part, p.counters, p.attn,
@@ -1073,188 +1051,76 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
     return true;
 }
 
-// ---- fused attention + O projection (short contexts) ---------------------------------
-// Unit = query head h (CTA h): QK-norm + RoPE of q_h and of its group's k,
-// the group's new K/V row written to the cache (the G CTAs of a group write
-// the same values), attention over all keys in one split, the normalised
-// output (hd values) as q24 blocks, then its slice of the O projection --
-// column blocks h*hd/32 .. of W_o, MK_DOWN_ROWS rows per ring slot -- whose
-// row sums are stored to p.opart[h].  The CTAs without a head then add the
-// heads' sums, in head order, to the residual (nothing else reads or writes
-// the residual during this stage), folding in the FFN accumulator too.
-template <int EPL>
-__device__ inline bool mk_attno(const MParams& p, const MStage& S, MCtx& c) {
-    const int G = p.n_heads / p.n_kv, hd = p.hd, half = hd / 2, nbh = hd / 32;
+// ---- O projection by columns: one query head x RC output rows per unit --------------
+// Unit (h, rows [r0, r0 + RC)): warp 0 forms head h's attention output
+// (mk_head_out4: the split merge) as NBH = head_dim/32 q24 blocks, then the
+// CTA dots them with the head's column blocks of W_o for its rows -- one
+// row's NBH blocks on NBH consecutive lanes, summed in a fixed order -- and
+// adds each row's partial sum into the fixed-point accumulator S.acc_out.
+// Every residual row so receives one addition per query head, and a unit
+// needs only its own head's attention state, not the whole attention output.
+template <int NBH>
+__device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
+    static_assert(NBH == 1 || NBH == 2 || NBH == 4, "head_dim 32, 64 or 128");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int pos = c.pos, seq = pos + 1;
-    const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
-    if ((int)blockIdx.x >= p.n_heads) {
-        // CTAs without a head: rows [f*rpc, ...) of the residual.  The old
-        // residual (y + A) is read while the heads compute; once every head
-        // has stored its O-projection row sums (the head counter reaches this
-        // layer's target), y = (y + A) + sum_h part[h] in head order, A = 0.
-        const int nf = gridDim.x - p.n_heads, f = blockIdx.x - p.n_heads;
-        const int rpc = (p.dim + nf - 1) / nf, r = f * rpc + tid;
-        const bool mine = tid < rpc && r < p.dim;
-        const float h0 = mine ? __ldcg(S.y + r) + __ll2float_rn(__ldcg(acc_at(S.fold_a, r))) * MK_UNFIX
-                              : 0.f;
-        if (tid == 0) {
-            const unsigned long long target = c.hbase + (unsigned long long)(S.layer + 1) * p.n_heads;
-            uint64_t t0 = 0;
-            int ok = 1;
-            for (unsigned it = 1; ld_acquire_u64(p.hctr) < target; it++) {
-                if ((it & 63) == 0) {
-                    const uint64_t now = global_ns();
-                    if (t0 == 0) t0 = now;
-                    if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
-                        ok = 0;
-                        break;
-                    }
-                }
-            }
-            if (!ok) {
-                atomicExch(p.status, (int)DEV_TIMEOUT);
-                c.sh->abort = 1;
-            }
+    const int nch = (S.N + S.RC - 1) / S.RC;
+    const int na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
+    bool first = true;
+    for (int u = blockIdx.x; u < S.nunits; u += gridDim.x) {
+        const int h = u / nch, r0 = (u - h * nch) * S.RC, rows = min(S.RC, S.N - r0);
+        const Q24 aq = q24_carve(c.work, NBH);
+        if (warp == 0) {  // lane: block lane/8, elements 4*(lane%8) .. +3
+            const int b = lane >> 3;
+            const float4 v = b < NBH ? mk_head_out4(p.attn, p.part, p.part_stride, p.hd, h,
+                                                    b * 32 + 4 * (lane & 7), na)
+                                     : f4_zero();
+            mk_q24_quad(aq, b, b < NBH, v, lane);
         }
+        if (first) mk_clk(c, CLK_LOADED);
         __syncthreads();
-        if (c.sh->abort) return false;
-        if (mine) {
-            float o = 0.f;
-            for (int hh = 0; hh < p.n_heads; hh++) o += __ldcg(p.opart + (size_t)hh * p.dim + r);
-            S.y[r] = h0 + o;
-            *acc_at(S.fold_a, r) = 0;
+        if (first) {
+            mk_clk(c, CLK_Q24);
+            if (c.stamp && tid == 0) c.stamp[1] = global_ns();
         }
-        return true;
-    }
-    const int h = blockIdx.x, g = h / G;
-    const int W = hd + 2;
-    float* sm = reinterpret_cast<float*>(c.work);                   // attn_core scratch (G = 1)
-    float* res = sm + (size_t)MK_WARPS * W;
-    float* qs = sm + al16(((size_t)(MK_WARPS + 1) * W + MK_WARPS) * 4) / 4;
-    float* ks = qs + hd;
-    float* os = ks + hd;
-    const Q24 aq = q24_carve(os + hd, nbh);
-    // prologue: every global input requested first (q row h by warp 0, k row g
-    // by warp 1, with their gains; the new V row; this thread's RoPE angle)
-    {
-        const bool isq = warp == 0, has_row = warp < 2;
-        const float* src = isq ? p.qkv + (size_t)h * hd : p.qkv + qd + (size_t)g * hd;
-        const float* nw = isq ? S.q_norm : S.k_norm;
-        float vv[EPL], wv[EPL];
-#pragma unroll
-        for (int e = 0; e < EPL; e++) {
-            const int d = lane + 32 * e;
-            const bool in = has_row && d < hd;
-            vv[e] = in ? __ldcg(src + d) : 0.f;
-            wv[e] = (in && nw) ? __ldg(nw + d) : 0.f;
-        }
-        const float vnew = tid < hd ? __ldcg(p.qkv + qd + kvd + (size_t)g * hd + tid) : 0.f;
-        float sn = 0.f, cs = 1.f;
-        if (tid < 2 * half) sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid % half)), &sn, &cs);
-        if (has_row) {  // QK-norm (qwen3.rs:154-155)
-            if (nw) {
-                float ss = 0.f;
-#pragma unroll
-                for (int e = 0; e < EPL; e++) ss = fmaf(vv[e], vv[e], ss);
-                ss = warp_sum(ss);
-                const float inv = 1.0f / sqrtf(ss / (float)hd + p.eps);
-#pragma unroll
-                for (int e = 0; e < EPL; e++) vv[e] = __fmul_rn(__fmul_rn(vv[e], inv), wv[e]);
-            }
-            float* dst = isq ? qs : ks;
-#pragma unroll
-            for (int e = 0; e < EPL; e++) {
-                const int d = lane + 32 * e;
-                if (d < hd) dst[d] = vv[e];
-            }
-        }
-        __syncthreads();
-        if (tid < 2 * half) {  // RoPE (rope.wgsl:25-34): one rotated pair per thread
-            float* row = tid < half ? qs : ks;
-            const int kq = tid % half;
-            const float lo = row[kq], hi = row[kq + half];
-            row[kq] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
-            row[kq + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
-        }
-        __syncthreads();
-        float* kbase = S.kc + (size_t)g * p.max_seq * hd;
-        float* vbase = S.vc + (size_t)g * p.max_seq * hd;
-        if (tid < hd) {  // cache.rs:21-24
-            kbase[(size_t)pos * hd + tid] = ks[tid];
-            vbase[(size_t)pos * hd + tid] = vnew;
-        }
-        __syncthreads();
-        mk_clk(c, CLK_LOADED);
-        if (c.stamp && tid == 0) c.stamp[1] = global_ns();
-        attn_core<EPL, 1, KV_CG, MK_WARPS>(qs, 1, hd, kbase, vbase, hd, 0, seq, p.scale, 0.f, sm,
-                                           res);
-    }
-    mk_clk(c, CLK_NORMED);
-    if (tid < hd) os[tid] = res[tid] * (1.0f / res[hd + 1]);  // attention.wgsl:96
-    __syncthreads();
-    if (warp == 0) {  // the head's output as nbh q24 blocks (lane: block lane/8)
-        const int b = lane >> 3;
-        const float4 v = b < nbh ? *reinterpret_cast<const float4*>(os + b * 32 + 4 * (lane & 7))
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-        mk_q24_quad(aq, b, b < nbh, v, lane);
-    }
-    __syncthreads();
-    mk_clk(c, CLK_Q24);
-    if (c.stamp && tid == 0) c.stamp[2] = global_ns();
-    // O projection slice: per row chunk, the nbh column blocks (consecutive
-    // ring slots) waited for together and consumed in one pass
-    for (int rc = 0; rc < S.per1; rc++) {
-        const int r0 = rc * MK_DOWN_ROWS, rows = min(MK_DOWN_ROWS, p.dim - r0);
         bool ok = true;
-        for (int k = 0; k < nbh; k++) {
+        for (int k = 0; k < S.per0; k++) {
             const int q = c.seq + k;
             ok = mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS) && ok;
         }
-        if (__syncthreads_or(!ok)) {
+        if (first) mk_clk(c, CLK_WAITED);
+        for (int i0 = 0; i0 < S.RC * NBH; i0 += MK_THREADS) {
+            const int i = i0 + tid, row = i / NBH, k = i % NBH;
+            float part = 0.f;
+            if (row < rows) {
+                const int sj = k / S.per1, ii = k - sj * S.per1;
+                const unsigned char* pay = c.ring + (size_t)((c.seq + sj) % MK_SLOTS) * MK_SLOT_BYTES;
+                const size_t e = (size_t)ii * S.RC + row;
+                const uint4 w4 = reinterpret_cast<const uint4*>(pay)[e];
+                const float d = __half2float(reinterpret_cast<const __half*>(pay + MK_SLOT_PAY)[e]);
+                uint4 xa[3], xb[3];
+#pragma unroll
+                for (int pl = 0; pl < 3; pl++) {
+                    xa[pl] = aq.pl[(pl * 2 + 0) * NBH + k];
+                    xb[pl] = aq.pl[(pl * 2 + 1) * NBH + k];
+                }
+                part = fmaf(d * aq.sb[k], mk_block_dot(w4, xa, xb, aq.cb[k]), 0.f);
+            }
+#pragma unroll
+            for (int o = 1; o < NBH; o <<= 1) part += __shfl_xor_sync(FULL, part, o);
+            if (k == 0 && row < rows && ok)
+                atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.acc_out, r0 + row)),
+                          (unsigned long long)__float2ll_rn(part * MK_FIX));
+        }
+        if (__syncthreads_or(!ok)) {  // slots consumed
             mk_fail(p, c);
             return false;
         }
-        float acc[MK_DOWN_ROWS / MK_THREADS];
-#pragma unroll
-        for (int i = 0; i < MK_DOWN_ROWS / MK_THREADS; i++) acc[i] = 0.f;
-        for (int k = 0; k < nbh; k++) {
-            uint4 xa[3], xb[3];
-#pragma unroll
-            for (int pl = 0; pl < 3; pl++) {
-                xa[pl] = aq.pl[(pl * 2 + 0) * nbh + k];
-                xb[pl] = aq.pl[(pl * 2 + 1) * nbh + k];
-            }
-            const int acb = aq.cb[k];
-            const float asb = aq.sb[k];
-            const unsigned char* pay = c.ring + (size_t)((c.seq + k) % MK_SLOTS) * MK_SLOT_BYTES;
-            const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
-#pragma unroll
-            for (int i = 0; i < MK_DOWN_ROWS / MK_THREADS; i++) {
-                const int r = tid + i * MK_THREADS;
-                if (r < rows) {
-                    const uint4 w4 = reinterpret_cast<const uint4*>(pay)[r];
-                    const float d = __half2float(scs[r]);
-                    acc[i] = fmaf(d * asb, mk_block_dot(w4, xa, xb, acb), acc[i]);
-                }
-            }
-        }
-        __syncthreads();  // slots consumed
         if (tid == MK_ISSUER)
-            for (int k = 0; k < nbh; k++) mk_issue_next(p, c);
-        c.seq += nbh;
-#pragma unroll
-        for (int i = 0; i < MK_DOWN_ROWS / MK_THREADS; i++) {
-            const int r = tid + i * MK_THREADS;
-            if (r < rows) p.opart[(size_t)h * p.dim + r0 + r] = acc[i];
-        }
+            for (int k = 0; k < S.per0; k++) mk_issue_next(p, c);
+        c.seq += S.per0;
+        if (first && c.stamp && tid == 0) c.stamp[2] = global_ns();
+        first = false;
     }
-    __syncthreads();
-    if (tid == 0) {  // this head's row sums are stored: release them to the fold CTAs
-        __threadfence();
-        atomicAdd(p.hctr, 1ull);
-    }
-    mk_clk(c, CLK_REGS);
     mk_clk(c, CLK_MAIN);
     return true;
 }
@@ -1274,11 +1140,11 @@ template <> struct CfgOfT<4, 2> { using T = MD4; };
 template <int I, int NS> using CfgOf = typename CfgOfT<I, NS>::T;
 
 // The step kernel, specialised for one model shape: EPL = head_dim / 32
-// registers per lane and GMAX >= n_heads / n_kv for the attention stage,
-// CD / CQ the GEMV configs of K = dim (QKV, FFN gate/up, LM head) and
-// K = n_heads * head_dim (O projection).  Only the code one model runs is
-// compiled into its kernel, which keeps the instruction footprint small.
-template <int EPL, int GMAX, int CD, int CQ>
+// registers per lane and GMAX >= n_heads / n_kv for the attention stage (EPL
+// column blocks per head in the O projection), CD the GEMV config of K = dim
+// (QKV, FFN gate/up, LM head).  Only the code one model runs is compiled into
+// its kernel, which keeps the instruction footprint small.
+template <int EPL, int GMAX, int CD>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ MShared sh;
@@ -1315,8 +1181,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     const int pos = p.st->pos;
     const unsigned tok = p.st->token;
     const unsigned long long base = p.st->bar_base;
-    c.hbase = p.st->ctr_base;
     c.pos = pos;
+    if (tid < p.hd / 2)  // rope.wgsl:25-34: angle pos * theta^(-2k/hd), f32
+        sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid)), &sh.rsin[tid], &sh.rcos[tid]);
     __syncthreads();
     if (tid == MK_ISSUER)  // the first ring-full of weights
         for (int s = 0; s < MK_SLOTS; s++)
@@ -1349,23 +1216,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
         mk_load_stage(p, si + 2, &sst[(si + 2) % 3]);  // waited for at the stage end
         const MStage& S = sst[si % 3];
         const MStage& S1 = sst[(si + 1) % 3];
-        if (tid == 0 && si + 1 < p.n_stages && (S1.kind == SK_ATTN || S1.kind == SK_ATTNO))
+        if (tid == 0 && si + 1 < p.n_stages &&
+            S1.kind == SK_ATTN && S1.layer == 0)
             mk_kv_prefetch(p, S1, c);
         mk_clk(c, CLK_AHEAD);
         if (S.kind == SK_ATTN) {
             ok = mk_attn<EPL, GMAX>(p, S, c);
-        } else if (S.kind == SK_ATTNO) {
-            ok = mk_attno<EPL>(p, S, c);
+        } else if (S.kind == SK_OCOL) {
+            ok = mk_ocol<EPL>(p, S, c);
         } else if (S.kind == SK_FFN) {
             ok = mk_ffn<CfgOf<CD, 2>>(p, S, c);
-        } else if (S.cfg == CD) {
-            ok = mk_gemv<CfgOf<CD, 1>>(p, S, c);
-        } else if (S.cfg == CD + MK_NCFG) {
-            ok = mk_gemv<CfgOf<CD, 2>>(p, S, c);
-        } else if (S.cfg == CQ) {
-            ok = mk_gemv<CfgOf<CQ, 1>>(p, S, c);
+        } else if (S.epi == EPI_HEAD) {  // always two slots per chunk
+            ok = mk_gemv<CfgOf<CD, 2>, EPI_HEAD>(p, S, c);
         } else {
-            ok = mk_gemv<CfgOf<CQ, 2>>(p, S, c);
+            ok = S.cfg >= MK_NCFG ? mk_gemv<CfgOf<CD, 2>, EPI_STORE>(p, S, c)
+                                  : mk_gemv<CfgOf<CD, 1>, EPI_STORE>(p, S, c);
         }
         mk_load_stage_wait();  // made visible by the barrier's __syncthreads
         if (stamp) {
@@ -1399,7 +1264,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
             st->pos = pos + 1;
             st->done = 0;
             st->bar_base = base + (unsigned long long)(p.n_stages - 1) * gridDim.x;
-            st->ctr_base = c.hbase + (unsigned long long)p.hctr_per_step;
             __threadfence();
         }
     }

@@ -20,6 +20,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_K, GGML_Q5_K, GGML_Q6_K = 0, 1, 2, 12, 13, 14
+GGML_Q4_1, GGML_Q8_0, GGML_BF16 = 3, 8, 30
 
 # metadata value type ids (gguf.rs:125-151)
 _T_U8, _T_I8, _T_U16, _T_I16, _T_U32, _T_I32, _T_F32, _T_BOOL, _T_STR, _T_ARR, _T_U64, _T_I64, _T_F64 = range(13)
@@ -66,7 +67,8 @@ class GgufWriter:
     @staticmethod
     def nbytes(t: Tensor) -> int:
         n = int(np.prod(t.dims))
-        return {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_Q4_0: n // 32 * 18,
+        return {GGML_F32: 4 * n, GGML_F16: 2 * n, GGML_BF16: 2 * n, GGML_Q4_0: n // 32 * 18,
+                GGML_Q4_1: n // 32 * 20, GGML_Q8_0: n // 32 * 34,
                 GGML_Q4_K: n // 256 * 144, GGML_Q5_K: n // 256 * 176,
                 GGML_Q6_K: n // 256 * 210}[t.ggml_type]
 
@@ -114,6 +116,43 @@ def random_q4_0_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.nda
     return blocks
 
 
+def random_q8_0_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.ndarray:
+    """[rows * in_f/32, 34] uint8 GGUF Q8_0 blocks (dequant.rs:46-58): f16 d ~
+    U(0.0002, 0.002), int8 codes uniform in -127..127 (the spread of the Q4_0
+    weights)."""
+    nb = rows * (in_f // 32)
+    out = np.empty((nb, 34), np.uint8)
+    out[:, 0:2] = rng.uniform(0.0002, 0.002, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    out[:, 2:] = rng.integers(-127, 128, (nb, 32)).astype(np.int8).view(np.uint8)
+    return out
+
+
+def random_q4_1_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.ndarray:
+    """[rows * in_f/32, 20] uint8 GGUF Q4_1 blocks (dequant.rs:82-97): f16 d ~
+    U(0.002, 0.02), f16 minimum m ~ U(-0.16, -0.016) (about -8 d, so the
+    weights centre near zero), codes uniform in 0..15."""
+    nb = rows * (in_f // 32)
+    out = np.empty((nb, 20), np.uint8)
+    d = rng.uniform(0.002, 0.02, nb)
+    out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(nb, 2)
+    out[:, 2:4] = (-8.0 * d * rng.uniform(0.9, 1.1, nb)).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    out[:, 4:] = rng.integers(0, 256, (nb, 16), dtype=np.uint8)
+    return out
+
+
+def random_dense(rng: np.random.Generator, rows: int, in_f: int, kind: str) -> np.ndarray:
+    """A [rows, in_f] F32 / F16 / BF16 weight ~ N(0, 0.05) (the spread of the
+    Q4_0 weights), as the file's bytes."""
+    w = rng.normal(0.0, 0.05, (rows, in_f)).astype(np.float32)
+    if kind == "f16":
+        return w.astype(np.float16)
+    if kind == "bf16":  # round to nearest even on the top 16 bits
+        u = w.view(np.uint32)
+        u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        return u
+    return w
+
+
 def random_q6_k_blocks(rng: np.random.Generator, rows: int, in_f: int) -> np.ndarray:
     """[rows * in_f/256, 210] uint8 GGUF Q6_K super-blocks (dequant.rs:102-131
     layout): random 6-bit codes, int8 sub-block scales in [-64, 64), f16 d ~
@@ -158,6 +197,10 @@ CONFIGS = {
     # small shapes that exercise the family switches in tests
     "small-qwen3": dict(arch="qwen3", dim=512, n_layers=4, n_heads=8, n_kv=4, head_dim=64,
                         hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True),
+    # an odd layer count: the persistent step's per-layer accumulator parity
+    # wraps differently from one step to the next
+    "odd-qwen3": dict(arch="qwen3", dim=512, n_layers=3, n_heads=16, n_kv=4, head_dim=32,
+                      hidden=1024, vocab=1024, eps=1e-6, theta=1e6, tied=True),
     "tiny-gemma2": dict(arch="gemma2", dim=256, n_layers=3, n_heads=4, n_kv=2, head_dim=64,
                         hidden=512, vocab=512, eps=1e-6, theta=1e4, tied=True, window=6,
                         attn_softcap=2.0, final_softcap=3.0),
@@ -188,6 +231,27 @@ CONFIGS = {
     "small-qwen3-q5k-embed": dict(arch="qwen3", dim=512, n_layers=2, n_heads=8, n_kv=4,
                                   head_dim=64, hidden=1536, vocab=2048, eps=1e-6, theta=1e6,
                                   tied=True, embed_type="q5_k"),
+    # the other types the reference's loader takes (tensor_f32: F32, F16, Q4_1,
+    # Q8_0) as projections, embeddings and heads, q/k/v of different types
+    "small-qwen3-mixed": dict(arch="qwen3", dim=512, n_layers=3, n_heads=8, n_kv=4, head_dim=64,
+                              hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=False,
+                              embed_type="q8_0",
+                              proj_types=dict(q="f16", k="q8_0", v="q4_1", o="f32",
+                                              gate="q8_0", up="q8_0", down="q4_1", head="f16")),
+    # dense projections (the reference's Proj::Dense over an f32 file) with
+    # q/k/v biases
+    "tiny-qwen2-f32": dict(arch="qwen2", dim=256, n_layers=2, n_heads=8, n_kv=2, head_dim=32,
+                           hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=True, bias=True,
+                           embed_type="f32",
+                           proj_types=dict(q="f32", k="f32", v="f32", o="f32",
+                                           gate="f32", up="f32", down="f32")),
+    # BF16 projections under an F16 tied embedding (the reference decodes BF16,
+    # dequant.rs:41-43, but its tensor_f32 does not dispatch it)
+    "small-qwen3-bf16": dict(arch="qwen3", dim=512, n_layers=2, n_heads=8, n_kv=4, head_dim=64,
+                             hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True,
+                             embed_type="f16",
+                             proj_types=dict(q="bf16", k="bf16", v="bf16", o="bf16",
+                                             gate="bf16", up="bf16", down="bf16")),
     # Q6_K token embedding (tied head) / Q6_K output, the layout of real Q4_0 files
     "small-qwen3-q6k": dict(arch="qwen3", dim=512, n_layers=4, n_heads=8, n_kv=4, head_dim=64,
                             hidden=1536, vocab=2048, eps=1e-6, theta=1e6, tied=True,
@@ -235,6 +299,13 @@ def synth_model(path: str, cfg: dict, seed: int = 0) -> str:
         kind = kind or ("q6_k" if q6k else "q4_0")
         if kind == "q6_k":  # real Q4_0 checkpoints often keep token_embd / output in Q6_K
             w.add(name, GGML_Q6_K, (in_f, rows), lambda r=r: random_q6_k_blocks(r, rows, in_f))
+        elif kind == "q8_0":
+            w.add(name, GGML_Q8_0, (in_f, rows), lambda r=r: random_q8_0_blocks(r, rows, in_f))
+        elif kind == "q4_1":
+            w.add(name, GGML_Q4_1, (in_f, rows), lambda r=r: random_q4_1_blocks(r, rows, in_f))
+        elif kind in ("f32", "f16", "bf16"):
+            t = {"f32": GGML_F32, "f16": GGML_F16, "bf16": GGML_BF16}[kind]
+            w.add(name, t, (in_f, rows), lambda r=r, k=kind: random_dense(r, rows, in_f, k))
         elif kind in ("q4_k", "q5_k"):
             five = kind == "q5_k"
             w.add(name, GGML_Q5_K if five else GGML_Q4_K, (in_f, rows),

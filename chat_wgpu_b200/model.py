@@ -110,11 +110,10 @@ class Session:
         _lib.call("cw_session_set_graph", self._h, 1 if use_graph else 0)
 
     def set_persistent(self, on) -> None:
-        """Select the step kernel: True/1 one persistent cooperative launch per
-        token (default where the family is covered), "split"/2 or "fused"/3
-        that launch with one of its two plans only, False/0 one kernel per
-        stage."""
-        mode = {"split": 2, "fused": 3}.get(on, None) if isinstance(on, str) else (1 if on else 0)
+        """Select the step kernel: True/1 (or "split"/2, the same plan) one
+        persistent cooperative launch per token (default where the family is
+        covered), False/0 one kernel per stage."""
+        mode = {"split": 2}.get(on, None) if isinstance(on, str) else (1 if on else 0)
         if mode is None:
             raise ValueError(f"unknown persistent mode {on!r}")
         _lib.call("cw_session_set_persistent", self._h, int(mode))

@@ -2,7 +2,7 @@
 WGPU_PROFILE report, src/model/mod.rs:74-88, src/profile.rs:86-117).
 
     python -m chat_wgpu_b200.stepprof [--model qwen3-0.6b] [--prompt-len 128]
-                                      [--steps 16] [--path auto|split|fused|per-stage]
+                                      [--steps 16] [--path auto|split|per-stage]
 
 Runs the prompt, a few warm-up decode steps, times `--steps` decode steps
 with CUDA events, then prints Session.profile(): for the persistent step,
@@ -21,7 +21,7 @@ def main(argv=None) -> None:
     ap.add_argument("--model", default="qwen3-0.6b")
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--steps", type=int, default=16)
-    ap.add_argument("--path", choices=["auto", "split", "fused", "per-stage"], default="auto")
+    ap.add_argument("--path", choices=["auto", "split", "per-stage"], default="auto")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
     from . import gguf
@@ -33,7 +33,7 @@ def main(argv=None) -> None:
     m = Model(ctx, path)
     s = Session(m, a.prompt_len + 3 * a.steps + 8)
     if a.path != "auto":
-        s.set_persistent({"split": "split", "fused": "fused", "per-stage": False}[a.path])
+        s.set_persistent({"split": "split", "per-stage": False}[a.path])
     rng = np.random.default_rng(a.seed + 1)
     s.begin(rng.integers(0, m.vocab_size, a.prompt_len).astype(np.uint32))
     s.run(a.prompt_len - 1 + 4)

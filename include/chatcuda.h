@@ -221,15 +221,26 @@ int cw_q4_0_dequant(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out
 int cw_q4_0_gemv_bench(cw_ctx* ctx, cw_buf x, const cw_buf* ws, size_t n_w, size_t in_f,
                        size_t out_f, size_t iters, double* us_per_launch);
 
-/* ---- GGUF k-quants: Q4_K / Q5_K / Q6_K super-blocks of 256 weights --------
- * The weight is the raw GGUF blocks ([rows][in_f/256] blocks of 144 / 176 /
- * 210 bytes) uploaded with cw_storage_bytes.  Q6_K dequantises exactly like
- * dequant_q6_k (dequant.rs:102-131); Q4_K / Q5_K (not implemented by the
- * reference: dequant.rs:6, ROADMAP.md:52-53) follow ggml's published block
- * layout.  in_f must be a multiple of 256 (at most 16384 for the GEMV). */
+/* ---- raw GGUF weights: k-quants and the other loader types ---------------
+ * The weight is the raw GGUF rows ([rows][in_f/256] groups of 256 weights:
+ * one Q4_K / Q5_K / Q6_K super-block of 144 / 176 / 210 bytes, 8 Q8_0 /
+ * Q4_1 blocks of 34 / 20 bytes, or 256 F32 / F16 / BF16 values) uploaded
+ * with cw_storage_bytes.  Dequantisation is exact to the reference's
+ * dequant_q6_k / dequant_q8_0 / dequant_q4_1 / f16_to_f32
+ * (dequant.rs:102-131, 46-58, 82-97, 9-21: the types its tensor_f32 takes,
+ * gguf.rs:109-121); Q4_K / Q5_K (not implemented by the reference:
+ * dequant.rs:6, ROADMAP.md:52-53) follow ggml's published block layout;
+ * BF16 is the top half of an f32 (dequant_bf16, dequant.rs:41-43, which the
+ * reference's tensor_f32 does not dispatch).  in_f must be a
+ * multiple of 256 (at most 16384 for the GEMV). */
+#define CW_GGUF_F32 0
+#define CW_GGUF_F16 1
+#define CW_GGUF_Q4_1 3
+#define CW_GGUF_Q8_0 8
 #define CW_GGUF_Q4_K 12
 #define CW_GGUF_Q5_K 13
 #define CW_GGUF_Q6_K 14
+#define CW_GGUF_BF16 30
 /* y[out_f] = W x (f32 accumulation). */
 int cw_kquant_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, int type, size_t in_f, size_t out_f,
                    cw_buf* out);
@@ -351,10 +362,8 @@ int cw_session_set_graph(cw_session* s, int use_graph);
  * dispatches one compute pass per op).  1 = the whole step as ONE persistent
  * cooperative launch (default for the shapes it covers: no post-norms, no
  * sliding window, no soft-caps, RMSNorm, SwiGLU, dim/q-dim/hidden multiples
- * of 256, a compiled kernel variant for the head shape), choosing per step
- * between its fused short-context plan and its split-attention plan;
- * 2 / 3 = persistent with the split / fused plan only (testing); 0 = one
- * kernel per stage.  Returns CW_ERR_UNSUPPORTED when a persistent mode is
+ * of 256, a compiled kernel variant for the head shape); 2 = the same (the
+ * split-attention plan, its only plan); 0 = one kernel per stage.  Returns CW_ERR_UNSUPPORTED when a persistent mode is
  * asked for a family it does not cover.  cw_session_persistent reports
  * whether the persistent step is in use. */
 int cw_session_set_persistent(cw_session* s, int on);

@@ -611,6 +611,7 @@ static size_t row_bytes_for(uint32_t dtype, size_t in_f) {
         case 12: return in_f / 256 * 144;
         case 13: return in_f / 256 * 176;
         case 14: return in_f / 256 * 210;
+        case 30: return in_f * 2; /* BF16: dequant_bf16 (dequant.rs:41-43); tensor_f32 has no arm for it (gguf.rs:113-121) */
         default: return 0;
     }
 }
@@ -627,6 +628,7 @@ static void dequant_row(const orc_mat* m, size_t row, float* out) {
         case 12: orc_dequant_q4_k(b, m->in_f, out); break;
         case 13: orc_dequant_q5_k(b, m->in_f, out); break;
         case 14: orc_dequant_q6_k(b, m->in_f, out); break;
+        case 30: for (size_t i = 0; i < m->in_f; i++) out[i] = orc_bf16_to_f32(rd16(b + 2 * i)); break;
     }
 }
 
