@@ -1524,6 +1524,8 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     // fixed-point residual accumulators of the persistent step (O-projection
     // and FFN partial sums by layer parity)
     A((size_t)4 * I.dim * sizeof(long long), (void**)&s->racc);
+    A((size_t)2 * I.dim * sizeof(float), (void**)&s->hid2);
+    A((size_t)2 * I.n_layers * I.n_kv * sizeof(unsigned), (void**)&s->rdy);
     A((size_t)sample_params_size(), &s->smp_dev);
     A(qd * 4, (void**)&s->qtap);
     if (rc == CW_OK) rc = sample_params_write(s);
@@ -1612,6 +1614,9 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     // the persistent step's accumulators start from zero (a step that timed
     // out may have left partial sums behind)
     CW_CUDA(cudaMemsetAsync(s->racc, 0, (size_t)4 * s->m->info.dim * sizeof(long long),
+                            s->ctx->stream));
+    CW_CUDA(cudaMemsetAsync(s->rdy, 0,
+                            (size_t)2 * s->m->info.n_layers * s->m->info.n_kv * sizeof(unsigned),
                             s->ctx->stream));
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     s->host_pos = 0;

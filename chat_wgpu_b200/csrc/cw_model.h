@@ -100,6 +100,8 @@ struct cw_session {
     // fixed-point residual accumulators of the persistent step, 4 x dim words:
     // the O-projection and FFN partial sums by layer parity (Y0, Y1, Z0, Z1)
     long long* racc = nullptr;
+    float* hid2 = nullptr;    // the persistent step's residual base, two buffers [2][dim]
+    unsigned* rdy = nullptr;  // its ready counters [2][n_layers][n_kv]
     cw::DevState* st = nullptr;
     int n_splits = 1;
     bool use_graph = true;

@@ -140,18 +140,24 @@ static int ocol_rows(const cw_model_info& I, int grid) {
     return rc;
 }
 
-// The stage list, uploaded to the device.  Per layer l (p = l % 2):
-//   attn_in    residual = hidden + Y[1-p] + Z[1-p] (layer 0: the embedding row)
-//              -> rmsnorm -> QKV GEMV (+bias) -> qkv
-//   attention  QK-norm, RoPE, K/V row write, split-KV attention; every CTA
-//              also folds Y[1-p] and Z[1-p] into hidden and zeroes them
-//              (layer 0: zeroes the previous step's last-layer pair)
-//   o_proj     per (query head, row chunk): that head's split merge and its
+// The stage list, uploaded to the device.  Per layer l (p = l % 2, q = 1 - p):
+//   attn_in    residual = H[p] + Y[q] + Z[q] (layer 0: the embedding row)
+//              -> rmsnorm -> QKV GEMV (+bias) -> qkv; each CTA also stores
+//              its slice of the residual to H[q], the next base; per kv
+//              group the rows stored are counted (qrdy)
+//   attention  (no grid barrier: each unit waits for its group's rows)
+//              QK-norm, RoPE, K/V row write, split-KV attention; the units of
+//              each kv head are counted (ardy)
+//   o_proj     (no grid barrier: each unit waits for its kv head's units)
+//              per (query head, row chunk): that head's split merge and its
 //              column blocks of W_o, partial sums added into Y[p]
-//   ffn        residual = hidden + Y[p] -> rmsnorm -> gate/up -> SwiGLU -> its
-//              column block of W_down, partial sums added into Z[p]
-// and the LM head on hidden + Y[p] + Z[p] of the last layer.  Y and Z are
-// fixed-point int64 accumulators (s->racc: Y[0], Y[1], Z[0], Z[1]).
+//   ffn        residual = H[q] + Y[p] -> rmsnorm -> gate/up -> SwiGLU -> its
+//              column block of W_down, partial sums added into Z[p]; zeroes
+//              Y[q] and Z[q] (its slice of rows)
+// and the LM head on H[L%2] + Y + Z of the last layer.  Y and Z are fixed-
+// point int64 accumulators (s->racc: Y[0], Y[1], Z[0], Z[1]), H two f32
+// buffers (s->hid2); the ready counters, and the last layer's Y and Z, are
+// zeroed by the last CTA of every step.
 static int build_variant(cw_session* s, int grid, int n_splits, size_t work, StepVariant* V,
                          size_t* smem_need) {
     cw_model* m = s->m;
@@ -160,9 +166,10 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     const int dim = (int)I.dim, L = (int)I.n_layers;
     long long* Y[2] = {s->racc, s->racc + dim};
     long long* Z[2] = {s->racc + 2 * dim, s->racc + 3 * dim};
+    float* H[2] = {s->hid2, s->hid2 + dim};
     std::vector<MStage> st;
     std::vector<MIssue> is;
-    auto gemv = [&](const char* name, const QW& w, int pro, int epi, const float* x,
+    auto gemv = [&](const char* name, const QW& w, int pro, int epi, float* fold_to, int layer,
                     const float* base, const float* norm_w, float* y, const float* bias,
                     float* xn_out, int acc_in, long long* r1, long long* r2) {
         V->names.push_back(name);
@@ -183,7 +190,8 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         S.nchunks = (S.N + S.RC - 1) / S.RC;
         S.payload = w.payload;
         S.scales = w.scales;
-        S.x = x;
+        S.fold_to = fold_to;
+        S.layer = layer;
         S.base = base;
         S.norm_w = norm_w;
         S.y = y;
@@ -209,22 +217,17 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         const int p = li % 2, q = 1 - p;
         float* kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
         float* vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
-        gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, nullptr, li == 0 ? nullptr : s->hidden,
+        gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, H[q], li, li == 0 ? nullptr : H[p],
              l.attn_norm, s->qkv, l.qkv_bias, nullptr, li == 0 ? 0 : 2, Y[q], Z[q]);
         V->names.push_back("attention");
         MStage T = {};
         T.kind = SK_ATTN;
+        T.nobar = 1;
         T.layer = li;
         T.q_norm = l.q_norm;
         T.k_norm = l.k_norm;
         T.kc = kc;
         T.vc = vc;
-        T.y = s->hidden;
-        // layer 0: the accumulators the previous step's last layer left behind
-        const int zp = li == 0 ? (L - 1) % 2 : q;
-        T.acc_in = li == 0 ? 0 : 1;
-        T.racc = Y[zp];
-        T.racc2 = Z[zp];
         st.push_back(T);
         MIssue It = {};
         It.kind = SK_ATTN;
@@ -233,6 +236,8 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         const QW& ocm = m->wo_cm[li];
         MStage O = {};
         O.kind = SK_OCOL;
+        O.nobar = 1;
+        O.layer = li;
         O.K = (int)(I.n_heads * I.head_dim);
         O.N = dim;
         O.RC = orc;
@@ -267,13 +272,16 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         F.per0 = 64 / F.RC;
         F.per1 = (dim + MK_DOWN_ROWS - 1) / MK_DOWN_ROWS;
         F.N2 = dim;
+        F.layer = li;
         F.acc_in = 1;
         F.racc = Y[p];
+        F.zero_a = li == 0 ? nullptr : Y[q];
+        F.zero_b = li == 0 ? nullptr : Z[q];
         F.payload = l.gate_up.payload;
         F.scales = l.gate_up.scales;
         F.payload2 = dcm.payload;
         F.scales2 = dcm.scales;
-        F.base = s->hidden;
+        F.base = H[q];
         F.norm_w = l.ffn_norm;
         F.acc_out = Z[p];
         st.push_back(F);
@@ -293,8 +301,8 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         is.push_back(If);
     }
     const int lp = (L - 1) % 2;
-    gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, s->hidden, m->final_norm, s->logits,
-         nullptr, s->xnorm, L == 0 ? 0 : 2, Y[lp], Z[lp]);
+    gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, L, H[L % 2], m->final_norm, s->logits,
+         nullptr, s->xnorm, 2, Y[lp], Z[lp]);
     V->n_stages = (int)st.size();
     *smem_need = (size_t)MK_SLOTS * MK_SLOT_BYTES + work + al16((size_t)dim * 4) +
                  is.size() * sizeof(MIssue);
@@ -334,6 +342,10 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     pp.max_seq = (int)s->max_seq;
     pp.n_splits = n_splits;
     pp.n_layers = L;
+    pp.qrdy = s->rdy;
+    pp.ardy = s->rdy + (size_t)L * I.n_kv;
+    pp.zero_a = Y[lp];
+    pp.zero_b = Z[lp];
     pp.part_stride = s->n_splits;
     pp.attn_min = MK_ATTN_MIN;
     pp.eps = I.eps;

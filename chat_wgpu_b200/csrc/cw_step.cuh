@@ -116,18 +116,20 @@ struct MStage {
     // blocks per slot.
     int nunits, per0, per1, N2;
     // PRO_NORM: the residual is base + racc (acc_in >= 1) + racc2 (acc_in ==
-    // 2), added in that order.  ATTN: acc_in 1 folds racc and racc2 into the
-    // residual base y (the same additions) and zeroes them; 0 only zeroes them.
-    int acc_in, layer, pad0, pad1;
+    // 2), added in that order.  nobar: the stage starts without a grid
+    // barrier (its inputs are guarded by ready counters).
+    int acc_in, layer, nobar, pad1;
     long long* racc;
     long long* racc2;
     long long* acc_out;       // FFN / OCOL: the accumulator its partial sums are added into
-    long long* pad_acc;
+    long long* zero_a;        // FFN: accumulators of the previous layer, zeroed here (this
+    long long* zero_b;        //      CTA's slice of rows)
+    const void* pad_ptr;
     const uint8_t* payload2;  // FFN: down projection, OCOL: O projection, column-block-major
     const __half* scales2;    //      [K/32][rows][16] + scales [K/32][rows]
     const uint8_t* payload;
     const __half* scales;
-    const float* x;        // (unused)
+    float* fold_to;        // QKV stage: this CTA's slice of the residual is stored here
     const float* base;     // PRO_NORM input (null: this CTA's embedding row)
     const float* norm_w;
     float* xn_out;         // CTA 0 stores the normalised input here
@@ -179,6 +181,15 @@ struct MParams {
     int dim, n_heads, n_kv, hd, max_seq, n_splits, part_stride, decode;
     int n_layers;
     int attn_min;  // keys per attention split before splitting further
+    // Ready counters [n_layers][n_kv], zeroed at the end of every step:
+    // qrdy counts the QKV rows of each kv group's heads stored this step
+    // (the attention units wait for (G + 2) * head_dim), ardy the attention
+    // units of each kv head finished (the O-projection units wait for the
+    // step's active split count).
+    unsigned* qrdy;
+    unsigned* ardy;
+    long long* zero_a;  // the last layer's accumulators, zeroed at the end of the step
+    long long* zero_b;
     float eps, scale;
     float inv_dim;      // 1/dim: the mean of squares as a product (exact for power-of-two dims)
     size_t work_bytes;  // shared-memory work region (q24 + hbuf + wbuf, or attention scratch)
@@ -205,7 +216,7 @@ __host__ __device__ constexpr int mk_part_w(int hd) { return hd + 4; }
 struct MShared {
     uint64_t full[MK_SLOTS];
     uint64_t pol;  // L2 evict-first policy of the weight stream
-    int it_stage, it_t, it_j, issued, abort;
+    int it_stage, it_t, it_j, issued, abort, last;
     __align__(16) float act[32];  // FFN: the act block of the current unit
     __align__(16) uint4 aq[6];    // FFN: its q24 planes
     int acb;
@@ -268,6 +279,14 @@ __device__ __forceinline__ int ld_volatile_i32(const int* p) {
 }
 __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
     asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_add_u32(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // Thread 0: issue the copy of this CTA's next weight chunk (in the stage
@@ -411,6 +430,33 @@ __device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long lon
     return c.sh->abort == 0;
 }
 
+// One thread: bounded wait until the ready counter reaches `target` (acquire:
+// the producers' stores before their release add are visible afterwards).
+// A timeout, or an error raised by another CTA, sets the status word and the
+// CTA's abort flag.
+__device__ inline bool mk_wait_count(const MParams& p, MCtx& c, const unsigned* ctr,
+                                     unsigned target) {
+    uint64_t t0 = 0;
+    for (unsigned it = 1; ld_acquire_u32(ctr) < target; it++) {
+        if ((it & 63) == 0) {
+            const uint64_t now = global_ns();
+            if (t0 == 0) t0 = now;
+            if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
+                atomicExch(p.status, (int)DEV_TIMEOUT);
+                c.sh->abort = 1;
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Rows per CTA of the residual slices the QKV stage stores (fold_to) and the
+// FFN stage zeroes: a multiple of four, so slices are float4 groups.
+__device__ __forceinline__ int mk_slice_rows(int dim) {
+    return (((dim + gridDim.x - 1) / gridDim.x) + 3) & ~3;
+}
+
 // Stage descriptors travel global -> shared by cp.async (16 bytes per thread
 // of the loader lanes, no register staging), requested two stages ahead and
 // waited for at the end of the current stage, so no thread ever stalls on
@@ -546,6 +592,15 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
             v[k] = b < nb ? ld_src(i) : f4_zero();
             w[k] = b < nb ? __ldg(reinterpret_cast<const float4*>(S.norm_w + i)) : f4_zero();
         }
+        if (S.fold_to) {  // this CTA's slice of the residual: the next stages' base
+            const int rs = mk_slice_rows(S.K), lo = blockIdx.x * rs;
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) {
+                const int b = 4 * (warp + k * MK_WARPS) + sub, i = b * 32 + e0;
+                if (b < nb && i >= lo && i < lo + rs)
+                    *reinterpret_cast<float4*>(S.fold_to + i) = v[k];
+            }
+        }
 #pragma unroll
         for (int k = 0; k < MK_QB; k++) {  // padding adds +0
             ss = fmaf(v[k].x, v[k].x, ss);
@@ -604,8 +659,13 @@ __device__ inline void mk_prologue_staged(const MParams& p, const MStage& S, con
         }
     }
     mk_clk(c, CLK_LOADED);
-    ss = mk_cta_sum(ss, c);
+    ss = mk_cta_sum(ss, c);  // its barrier also publishes hbuf
     mk_clk(c, CLK_NORMED);
+    if (S.fold_to) {  // this CTA's slice of the residual: the next stages' base
+        const int rs = mk_slice_rows(S.K), i = blockIdx.x * rs + 4 * threadIdx.x;
+        if (4 * (int)threadIdx.x < rs && i < S.K)
+            *reinterpret_cast<float4*>(S.fold_to + i) = *reinterpret_cast<const float4*>(hbuf + i);
+    }
     const float inv = 1.0f / sqrtf(ss * p.inv_dim + p.eps);
     for (int t = warp; t < nq; t += MK_WARPS) {
         const int b = 4 * t + sub, i = b * 32 + e0;
@@ -758,7 +818,19 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     constexpr int WPR = CF::WPR, RC = CF::RC;
     const int nb = S.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if ((int)blockIdx.x >= S.nchunks) return true;  // no rows of this stage here
+    if ((int)blockIdx.x >= S.nchunks) {  // no rows of this stage here
+        if (S.fold_to) {  // but still this CTA's slice of the next residual base
+            const int rs = mk_slice_rows(S.K), i = blockIdx.x * rs + 4 * tid;
+            if (4 * tid < rs && i < S.K) {
+                float4 h = S.base ? __ldcg(reinterpret_cast<const float4*>(S.base + i))
+                                  : *reinterpret_cast<const float4*>(c.emb + i);
+                if (S.acc_in >= 1) h = mk_add_fixed4(h, S.racc, i);
+                if (S.acc_in >= 2) h = mk_add_fixed4(h, S.racc2, i);
+                *reinterpret_cast<float4*>(S.fold_to + i) = h;
+            }
+        }
+        return true;
+    }
     // the bias of the first chunk's rows, requested now so it arrives while
     // the prologue runs
     float add = 0.f;
@@ -798,6 +870,36 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     }
     if (c.stamp && tid == 0) c.stamp[2] = global_ns();
     mk_clk(c, CLK_MAIN);
+    if (EPI == EPI_STORE && p.qrdy) {
+        // QKV rows stored: add, per kv group, the rows of its q heads, k and v
+        // this CTA wrote (the attention units wait for (G + 2) * head_dim)
+        __syncthreads();
+        if (tid == 0) {
+            const int hd = p.hd, ghd = (p.n_heads / p.n_kv) * hd;
+            const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
+            unsigned* ctr = p.qrdy + (size_t)S.layer * p.n_kv;
+            for (long chunk = blockIdx.x; chunk < S.nchunks; chunk += gridDim.x) {
+                int r = (int)(chunk * RC);
+                const int end = min(r + RC, S.N);
+                while (r < end) {
+                    int g, seg;
+                    if (r < qd) {
+                        g = r / ghd;
+                        seg = (g + 1) * ghd;
+                    } else if (r < qd + kvd) {
+                        g = (r - qd) / hd;
+                        seg = qd + (g + 1) * hd;
+                    } else {
+                        g = (r - qd - kvd) / hd;
+                        seg = qd + kvd + (g + 1) * hd;
+                    }
+                    seg = min(seg, end);
+                    red_release_add_u32(ctr + g, (unsigned)(seg - r));
+                    r = seg;
+                }
+            }
+        }
+    }
     if (EPI == EPI_HEAD) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -826,6 +928,15 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
     constexpr int WPR = CF::WPR, RC = CF::RC;
     const int nb = S.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (S.zero_a && warp == MK_WARPS - 1) {
+        // the previous layer's accumulators: every reader (the QKV stage's
+        // prologue) is behind this stage's barrier; zero this CTA's slice
+        const int rs = mk_slice_rows(p.dim);
+        for (int r = blockIdx.x * rs + lane; r < min((int)(blockIdx.x + 1) * rs, p.dim); r += 32) {
+            *acc_at(S.zero_a, r) = 0;
+            *acc_at(S.zero_b, r) = 0;
+        }
+    }
     if ((int)blockIdx.x >= S.nunits) return true;
     const Q24 q = q24_carve(c.work, nb);
     mk_input<CF>(p, S, q, c);
@@ -943,24 +1054,6 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
     float* cwt = sm + (size_t)(MK_WARPS + 1) * G * (hd + 2);
     float* qs = cwt + (size_t)G * (p.n_splits + 1);
     float* ks = qs + (size_t)G * hd;
-    {
-        // Fold the previous layer's accumulators into the residual base:
-        // y[r] = (y[r] + racc[r]) + racc2[r] -- the additions every PRO_NORM
-        // prologue of that residual made -- then zero both (acc_in 0: zero
-        // only).  Nothing reads the residual during this stage; each CTA
-        // takes a slice of rows, independent of its attention unit.
-        const int rpc = (p.dim + gridDim.x - 1) / gridDim.x, r = blockIdx.x * rpc + tid;
-        if (S.racc && tid < rpc && r < p.dim) {
-            if (S.acc_in) {
-                float hv = __ldcg(S.y + r);
-                hv = hv + __ll2float_rn(__ldcg(acc_at(S.racc, r))) * MK_UNFIX;
-                hv = hv + __ll2float_rn(__ldcg(acc_at(S.racc2, r))) * MK_UNFIX;
-                S.y[r] = hv;
-            }
-            *acc_at(S.racc, r) = 0;
-            *acc_at(S.racc2, r) = 0;
-        }
-    }
     if ((int)blockIdx.x >= units) {  // no unit here: prefetch the next layer's K/V rows
         const int f = blockIdx.x - units;
         if (tid == 0 && f < units && S.layer + 1 < p.n_layers) {
@@ -973,6 +1066,11 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
         const int g = u % p.n_kv, split = u / p.n_kv;
         int jlo, jhi;
         attn_range(seq, 0, split, n_active, &jlo, &jhi);
+        // this kv group's q/k/v rows of the QKV stage (no grid barrier between)
+        if (tid == 0)
+            mk_wait_count(p, c, p.qrdy + (size_t)S.layer * p.n_kv + g, (unsigned)((G + 2) * hd));
+        __syncthreads();
+        if (c.sh->abort) return false;
         const bool holds = pos >= jlo && pos < jhi;
         const int nrows = G + (holds ? 1 : 0);  // <= 5 rows, one per warp
         // every global input of the prologue is requested before any is used:
@@ -1046,6 +1144,9 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
                         cwt);
         }
         __syncthreads();
+        // this unit's state (or, from the merging unit, the head's output) is
+        // stored: release it to the O-projection units of the kv head
+        if (tid == 0) red_release_add_u32(p.ardy + (size_t)S.layer * p.n_kv + g, 1u);
         mk_clk(c, CLK_MAIN);  // attention: output (or partial) published
     }
     return true;
@@ -1070,6 +1171,11 @@ __device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
         const int h = u / nch, r0 = (u - h * nch) * S.RC, rows = min(S.RC, S.N - r0);
         const Q24 aq = q24_carve(c.work, NBH);
         if (warp == 0) {  // lane: block lane/8, elements 4*(lane%8) .. +3
+            // every attention unit of this head's kv group has published
+            if (lane == 0)
+                mk_wait_count(p, c, p.ardy + (size_t)S.layer * p.n_kv + h / (p.n_heads / p.n_kv),
+                              (unsigned)na);
+            __syncwarp();
             const int b = lane >> 3;
             const float4 v = b < NBH ? mk_head_out4(p.attn, p.part, p.part_stride, p.hd, h,
                                                     b * 32 + 4 * (lane & 7), na)
@@ -1078,6 +1184,7 @@ __device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
         }
         if (first) mk_clk(c, CLK_LOADED);
         __syncthreads();
+        if (c.sh->abort) return false;
         if (first) {
             mk_clk(c, CLK_Q24);
             if (c.stamp && tid == 0) c.stamp[1] = global_ns();
@@ -1200,13 +1307,23 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
             float v = __fmul_rn(d, (float)(qv - 8));
             if (p.embed_scale > 0.f) v = __fmul_rn(v, p.embed_scale);
             c.emb[i] = v;
-            if (blockIdx.x == 0) p.hidden[i] = v;
         }
         __syncthreads();
     }
     bool ok = true;
+    unsigned nbar = 0;  // grid barriers passed this step
     for (int si = 0; si < p.n_stages && ok; si++) {
-        if (si > 0) ok = mk_grid_sync(p, c, base + (unsigned long long)si * gridDim.x);
+        if (si > 0) {
+            // the attention and O-projection stages wait on ready counters
+            // instead; the __syncthreads publishes the stage descriptor
+            const int kind = iss[si].kind;
+            if (kind == SK_ATTN || kind == SK_OCOL) {
+                __syncthreads();
+            } else {
+                nbar++;
+                ok = mk_grid_sync(p, c, base + (unsigned long long)nbar * gridDim.x);
+            }
+        }
         if (!ok) break;
         unsigned long long* stamp =
             p.stamps ? p.stamps + ((size_t)si * gridDim.x + blockIdx.x) * MK_STAMPS : nullptr;
@@ -1242,11 +1359,29 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     mk_load_stage_wait();
     mk_drain(c);
     if (!ok || sh.abort) return;
-    // the last CTA to finish does the generate-loop bookkeeping (mod.rs:114-122)
+    // the last CTA to finish clears what the next step expects at zero (the
+    // ready counters, the last layer's accumulators) and does the
+    // generate-loop bookkeeping (mod.rs:114-122)
     if (tid == 0) {
         __threadfence();
-        const unsigned prev = atomicAdd(&p.st->done, 1u);
-        if (prev == gridDim.x - 1) {
+        sh.last = atomicAdd(&p.st->done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (sh.last) {
+        __threadfence();
+        const int nc = p.n_layers * p.n_kv;
+        for (int i = tid; i < nc; i += blockDim.x) {
+            p.qrdy[i] = 0;
+            p.ardy[i] = 0;
+        }
+        for (int i = tid; i < p.dim; i += blockDim.x) {
+            *acc_at(p.zero_a, i) = 0;
+            *acc_at(p.zero_b, i) = 0;
+        }
+        __syncthreads();
+    }
+    if (sh.last && tid == 0) {
+        {
             __threadfence();
             DevState* st = p.st;
             unsigned next;
@@ -1263,7 +1398,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
             st->token = next;
             st->pos = pos + 1;
             st->done = 0;
-            st->bar_base = base + (unsigned long long)(p.n_stages - 1) * gridDim.x;
+            st->bar_base = base + (unsigned long long)nbar * gridDim.x;
             __threadfence();
         }
     }
