@@ -58,11 +58,21 @@ __device__ __forceinline__ int attn_span(int seq, int window) {
 // the un-normalised attention state over keys [jlo, jhi) of one kv head
 // (rows kb + j*rs, vb + j*rs).  On return res[gi*(hd+2) + d] holds the
 // accumulator A, res[.. + hd] the max M, res[.. + hd + 1] the denominator L.
-// All threads of the 128-thread CTA call it; it ends with __syncthreads().
+// All NW warps call it; it ends with a barrier over them (attn_sync).
 // LD selects the K/V load path (KV_NC must not be used for rows the calling
 // kernel wrote).  NW warps (the CTA has NW*32 threads) take groups of four
 // keys in turn.
-template <int EPL, int GMAX, int LD = KV_NC, int NW = 4>
+// CTA barrier of attn_core: __syncthreads, or (NAMED) named barrier 1 over
+// the NW warps that run it, for kernels with other warps that do not.
+template <bool NAMED, int NW>
+__device__ __forceinline__ void attn_sync() {
+    if constexpr (NAMED)
+        asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
+    else
+        __syncthreads();
+}
+
+template <int EPL, int GMAX, int LD = KV_NC, int NW = 4, bool NAMED = false>
 __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
                                           const float* __restrict__ kb,
                                           const float* __restrict__ vb, long rs, int jlo, int jhi,
@@ -153,7 +163,7 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
             }
         }
     }
-    __syncthreads();
+    attn_sync<NAMED, NW>();
     // merge the NW warp states (the merge rule of attention.wgsl:88-95): per
     // head, warp gi finds M = max_w m_w, the weights c_w = exp(m_w - M) and
     // L = sum_w l_w c_w (lane w holds warp w's state), so each output element
@@ -172,15 +182,15 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
             res[gi * W + hd + 1] = L;
         }
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+    attn_sync<NAMED, NW>();
+    for (int i = threadIdx.x; i < G * hd; i += NW * 32) {
         int gi = i / hd, d = i - gi * hd;
         float A = 0.f;
 #pragma unroll
         for (int w = 0; w < NW; w++) A = fmaf(sm[(size_t)(w * G + gi) * W + d], cw[gi * NW + w], A);
         res[gi * W + d] = A;
     }
-    __syncthreads();
+    attn_sync<NAMED, NW>();
 }
 
 // After attn_core: with one active split, write the normalised output;
@@ -191,29 +201,39 @@ static __device__ __noinline__ void attn_finish(const float* res, int G, int hd,
                                             int n_active, int n_splits_alloc,
                                             float* __restrict__ part,
                                             unsigned* __restrict__ counters,
-                                            float* __restrict__ out, float* cwt) {
+                                            float* __restrict__ out, float* cwt,
+                                            int nthreads = 0, bool named = false) {
+    // nthreads: the threads that run it (0: the whole CTA, __syncthreads);
+    // named: they synchronise with named barrier 1 (other warps do not)
+    if (nthreads == 0) nthreads = blockDim.x;
+    auto sync = [&]() {
+        if (named)
+            asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+        else
+            __syncthreads();
+    };
     const int W = hd + 2;
     if (n_active == 1) {
-        for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        for (int i = threadIdx.x; i < G * hd; i += nthreads) {
             int gi = i / hd, d = i - gi * hd;
             out[(size_t)(g * G + gi) * hd + d] = res[gi * W + d] * (1.0f / res[gi * W + hd + 1]);
         }
         return;
     }
-    for (int i = threadIdx.x; i < G * W; i += blockDim.x) {
+    for (int i = threadIdx.x; i < G * W; i += nthreads) {
         int gi = i / W, d = i - gi * W;
         part[((size_t)(g * G + gi) * n_splits_alloc + split) * W + d] = res[i];
     }
     __threadfence();
-    __syncthreads();
+    sync();
     __shared__ int s_last;
     if (threadIdx.x == 0) s_last = (atomicAdd(&counters[g], 1u) == (unsigned)n_active - 1);
-    __syncthreads();
+    sync();
     if (!s_last) return;
     __threadfence();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // merge weights c_s = exp(M_s - M) and 1/L per head, one warp per head
-    for (int gi = warp; gi < G; gi += (blockDim.x >> 5)) {
+    for (int gi = warp; gi < G; gi += (nthreads >> 5)) {
         const float* ph = part + (size_t)(g * G + gi) * n_splits_alloc * W;
         float M = REF_NEG_INF;
         for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(ph + (size_t)s * W + hd));
@@ -227,8 +247,8 @@ static __device__ __noinline__ void attn_finish(const float* res, int G, int hd,
         L = warp_sum(L);
         if (lane == 0) cwt[gi * (n_active + 1) + n_active] = 1.0f / L;
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+    sync();
+    for (int i = threadIdx.x; i < G * hd; i += nthreads) {
         int gi = i / hd, d = i - gi * hd;
         const float* ph = part + (size_t)(g * G + gi) * n_splits_alloc * W + d;
         const float* c = cwt + gi * (n_active + 1);
@@ -243,7 +263,7 @@ static __device__ __noinline__ void attn_finish(const float* res, int G, int hd,
         for (; s < n_active; s++) a0 = fmaf(__ldcg(ph + (size_t)s * W), c[s], a0);
         out[(size_t)(g * G + gi) * hd + d] = ((a0 + a1) + (a2 + a3)) * c[n_active];
     }
-    __syncthreads();
+    sync();
     if (threadIdx.x == 0) counters[g] = 0;
 }
 

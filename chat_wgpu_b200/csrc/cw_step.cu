@@ -384,7 +384,7 @@ int step_plan_create(cw_session* s) {
                                  (int)P->smem);
     int per_sm = 0;
     if (e == cudaSuccess)
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, P->kern, MK_THREADS, P->smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, P->kern, MK_BLOCK, P->smem);
     if (e != cudaSuccess || per_sm < 1)
         return set_error(CW_ERR_UNSUPPORTED, "persistent step cannot be resident: %s",
                          cudaGetErrorString(e));
@@ -413,7 +413,7 @@ static int step_launch(cw_session* s, bool decode, unsigned long long* stamps) {
     pp.n_stages = decode ? V.n_stages : V.n_stages - 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)P->grid);
-    cfg.blockDim = dim3(MK_THREADS);
+    cfg.blockDim = dim3(MK_BLOCK);
     cfg.dynamicSmemBytes = P->smem;
     cfg.stream = s->ctx->stream;
     cudaLaunchAttribute attr[1];

@@ -29,8 +29,30 @@
 
 namespace cw {
 
-constexpr int MK_THREADS = 512;
+// 16 compute warps and one producer warp that only queues the weight copies
+// (MK_BLOCK threads per CTA).  The compute warps synchronise among themselves
+// with named barrier 1 (mk_sync): the producer never waits on them except
+// through the ring's "empty" mbarriers, so the copy issue -- a few hundred
+// cycles per bulk copy -- never sits on the compute warps' critical path.
+constexpr int MK_THREADS = 512;  // compute threads
 constexpr int MK_WARPS = MK_THREADS / 32;
+constexpr int MK_BLOCK = MK_THREADS + 32;
+__device__ __forceinline__ void mk_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(MK_THREADS) : "memory");
+}
+// mk_sync that also returns whether any compute thread passed v != 0
+__device__ __forceinline__ bool mk_sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(MK_THREADS)
+        : "memory");
+    return r != 0;
+}
 constexpr int MK_SLOTS = 8;
 constexpr int MK_SLOT_PAY = 16384;  // nibble payload of one chunk
 constexpr int MK_SLOT_SC = 2048;    // its f16 scales
@@ -46,13 +68,13 @@ enum {
     CLK_LOADED = 2,   // prologue: global inputs arrived (NORM) / converted (X)
     CLK_NORMED = 3,   // prologue: CTA-wide sum of squares done
     CLK_Q24 = 4,      // prologue: q24 planes written
-    CLK_REGS = 5,     // planes in registers (after __syncthreads)
+    CLK_REGS = 5,     // planes in registers (after the CTA barrier)
     CLK_MAIN = 6,     // chunk loop done
     CLK_END = 7,      // stage end
     CLK_N = 8,
     // first chunk of the main loop (extra points, reported separately)
     CLK_WAITED = 8,   // its weights are in shared memory
-    CLK_SUMMED = 9,   // row partials complete (after __syncthreads)
+    CLK_SUMMED = 9,   // row partials complete (after the CTA barrier)
     CLK_ISSUED = 10,  // next copy issued
 };
 
@@ -214,9 +236,10 @@ __host__ __device__ constexpr int mk_part_w(int hd) { return hd + 4; }
 
 // per-CTA state shared by all threads
 struct MShared {
-    uint64_t full[MK_SLOTS];
+    uint64_t full[MK_SLOTS];   // a slot's copy has landed
+    uint64_t empty[MK_SLOTS];  // the compute warps are done with a slot
     uint64_t pol;  // L2 evict-first policy of the weight stream
-    int it_stage, it_t, it_j, issued, abort, last;
+    int it_stage, it_t, it_j, issued, abort, last, prod_done;
     __align__(16) float act[32];  // FFN: the act block of the current unit
     __align__(16) uint4 aq[6];    // FFN: its q24 planes
     int acb;
@@ -242,7 +265,7 @@ struct MCtx {
     unsigned long long* stamp;  // this stage's stamps (profiling) or null
 };
 
-// CTA-wide sum with one __syncthreads: the warps' partials go to one of two
+// CTA-wide sum with one CTA barrier: the warps' partials go to one of two
 // alternating buffers, so a call never overwrites the buffer the previous
 // call is still reading (every thread passed that call's barrier first).
 // Fixed summation order.
@@ -252,16 +275,15 @@ __device__ __forceinline__ float mk_cta_sum(float v, MCtx& c) {
     float* r = c.sh->red[c.redsel];
     c.redsel ^= 1;
     if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = v;
-    __syncthreads();
+    mk_sync();
     const float4* r4 = reinterpret_cast<const float4*>(r);
     const float4 a = r4[0], b = r4[1], d = r4[2], e = r4[3];
     return (((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w))) +
            (((d.x + d.y) + (d.z + d.w)) + ((e.x + e.y) + (e.z + e.w)));
 }
 
-// One lane of the last warp issues the weight copies, so the copy issue
-// never delays warp 0 (epilogue rows, barrier arrival).
-constexpr int MK_ISSUER = MK_THREADS - 32;
+// Lane 0 of the producer warp issues the weight copies.
+constexpr int MK_ISSUER = MK_THREADS;
 
 __device__ __forceinline__ void mk_clk(const MCtx& c, int k) {
     if (c.stamp && threadIdx.x == 0) c.stamp[4 + k] = clock64();
@@ -295,9 +317,10 @@ __device__ __forceinline__ void mk_issue_copy(MShared* sh, unsigned char* ring, 
                                               const __half* sc, unsigned pb, unsigned sb) {
     const int slot = sh->issued % MK_SLOTS;
     unsigned char* dst = ring + (size_t)slot * MK_SLOT_BYTES;
-    // the slot's previous contents were read before the __syncthreads that
-    // precedes this call (a generic-proxy read followed by an async-proxy
-    // write: ordered by that barrier, no proxy fence)
+    // the slot's previous contents were read before the compute warps'
+    // release of it (its "empty" mbarrier, which the producer waited on): a
+    // generic-proxy read followed by an async-proxy write, ordered by that
+    // mbarrier, no proxy fence
     mbar_expect_tx(&sh->full[slot], pb + sb);  // pb == 0: a plain arrive (rows past the end)
     if (pb) {
         bulk_g2s_hint(dst, pay, pb, &sh->full[slot], sh->pol);
@@ -376,37 +399,77 @@ __device__ __forceinline__ bool mk_issue_next(const MParams& p, MCtx& c) {
     return mk_issue_next_impl(c.sh, c.iss, c.ring, p.n_stages);
 }
 
-// Wait (bounded) for every copy issued and not yet consumed, so no bulk copy
-// writes shared memory after the CTA has left.
+// Compute thread 0, after the CTA barrier that ends the use of ring slots
+// seq .. seq+n-1: hand them back to the producer.
+__device__ __forceinline__ void mk_release(MCtx& c, int n) {
+    if (threadIdx.x == 0)
+        for (int k = 0; k < n; k++)
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                             smem_addr(&c.sh->empty[(c.seq + k) % MK_SLOTS]))
+                         : "memory");
+}
+
+__device__ __forceinline__ int ld_volatile_shared_i32(const int* p) {
+    return *reinterpret_cast<const volatile int*>(p);
+}
+
+// The producer warp's lane 0: queue every weight copy of the step in order,
+// copy q into ring slot q % MK_SLOTS once the compute warps released that
+// slot's previous copy (q - MK_SLOTS).  Stops early when the CTA aborts.
+__device__ inline void mk_produce(const MParams& p, MCtx& c) {
+    MShared* sh = c.sh;
+    for (int q = 0;; q++) {
+        if (q >= MK_SLOTS) {
+            uint64_t* e = &sh->empty[q % MK_SLOTS];
+            const unsigned par = (unsigned)(((q / MK_SLOTS) - 1) & 1);
+            bool ok = mbar_try_wait(e, par);
+            const uint64_t t0 = ok ? 0 : global_ns();
+            while (!ok) {
+                if (ld_volatile_shared_i32(&sh->abort)) break;
+                if (global_ns() - t0 > MK_WAIT_NS) {
+                    atomicExch(p.status, (int)DEV_TIMEOUT);
+                    sh->abort = 1;
+                    break;
+                }
+                ok = mbar_try_wait(e, par);
+            }
+            if (!ok) break;
+        }
+        if (ld_volatile_shared_i32(&sh->abort) || !mk_issue_next(p, c)) break;
+    }
+    __threadfence_block();
+    *reinterpret_cast<volatile int*>(&sh->prod_done) = 1;
+}
+
+// Compute threads: wait (bounded) until the producer has stopped, then for
+// every copy issued and not yet consumed, so no bulk copy writes shared
+// memory after the CTA has left.
 __device__ inline void mk_drain(MCtx& c) {
-    if (threadIdx.x == MK_ISSUER) {
-        for (int q = c.seq; q < c.sh->issued; q++)
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = global_ns();
+        while (!ld_volatile_shared_i32(&c.sh->prod_done) && global_ns() - t0 < MK_WAIT_NS) {
+        }
+        const int issued = ld_volatile_shared_i32(&c.sh->issued);
+        for (int q = c.seq; q < issued; q++)
             mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS);
     }
-    __syncthreads();
+    mk_sync();
 }
 
 __device__ inline void mk_fail(const MParams& p, MCtx& c) {
     if (threadIdx.x == 0) {
         atomicExch(p.status, (int)DEV_TIMEOUT);
-        c.sh->abort = 1;
+        *reinterpret_cast<volatile int*>(&c.sh->abort) = 1;
     }
-    __syncthreads();
+    mk_sync();
 }
 
-// Grid-wide barrier: __syncthreads orders the CTA's writes before thread 0's
-// gpu-scope release arrive; thread 0 polls (acquire) until the counter
-// reaches `target`, and __syncthreads passes that on to the CTA.  The status
+// Grid-wide barrier: a CTA barrier orders the compute warps' writes before
+// thread 0's gpu-scope release arrive; thread 0 polls (acquire) until the
+// counter reaches `target`, and a CTA barrier passes that on.  The status
 // word and the time limit are checked every 64 polls.
 __device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long long target) {
-    // Warps 0..14 order their writes before thread 0's release arrive.  The
-    // last warp is left out: its global writes all precede an earlier full
-    // CTA barrier (chunk barriers, the attention unit's closing barrier), and
-    // its remaining work -- queueing the weight copies -- only touches this
-    // CTA's shared memory, so it overlaps the arrive and the poll and joins
-    // at the closing __syncthreads.
-    if ((threadIdx.x >> 5) != MK_WARPS - 1)
-        asm volatile("bar.sync 1, %0;" ::"n"(MK_THREADS - 32) : "memory");
+    mk_sync();  // the compute warps' writes before thread 0's release arrive
     if (threadIdx.x == 0) {
         red_release_add(p.bar, 1ull);
         uint64_t t0 = 0;
@@ -423,10 +486,10 @@ __device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long lon
         }
         if (!ok) {
             atomicExch(p.status, (int)DEV_TIMEOUT);
-            c.sh->abort = 1;
+            *reinterpret_cast<volatile int*>(&c.sh->abort) = 1;
         }
     }
-    __syncthreads();
+    mk_sync();
     return c.sh->abort == 0;
 }
 
@@ -443,7 +506,7 @@ __device__ inline bool mk_wait_count(const MParams& p, MCtx& c, const unsigned* 
             if (t0 == 0) t0 = now;
             if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
                 atomicExch(p.status, (int)DEV_TIMEOUT);
-                c.sh->abort = 1;
+                *reinterpret_cast<volatile int*>(&c.sh->abort) = 1;
                 return false;
             }
         }
@@ -745,7 +808,7 @@ __device__ __forceinline__ void mk_load_regs(const Q24& q, MRegs<CF>& R) {
 
 // One chunk of RC rows: wait for ring slot c.seq, dot each row with the
 // planes in R, reduce the per-warp partials into rb[row * WPR + sub], then
-// (after __syncthreads) issue the next copy into the freed slot.  Returns
+// (after the CTA barrier) hand the slots back to the producer.  Returns
 // rb, or null after a timed-out wait (the failure is recorded).  Each thread
 // waits on the slot's mbarrier itself, so the only CTA barrier is the one at
 // the end: warps start on a chunk while the issuing lane is still queueing
@@ -794,13 +857,12 @@ __device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int 
     }
     const float v = warp_reduce_rows<RPW>(acc, lane);
     if ((lane & (32 / RPW - 1)) == 0) rb[(slot * RPW + lane / (32 / RPW)) * WPR + wsub] = v;
-    if (__syncthreads_or(!ok)) {  // slots consumed, row partials complete
+    if (mk_sync_or(!ok)) {  // slots consumed, row partials complete
         mk_fail(p, c);
         return nullptr;
     }
     if (first) mk_clk(c, CLK_SUMMED);
-    if (threadIdx.x == MK_ISSUER)
-        for (int k = 0; k < NS; k++) mk_issue_next(p, c);
+    mk_release(c, NS);
     if (first) mk_clk(c, CLK_ISSUED);
     c.seq += NS;
     c.nch++;
@@ -839,7 +901,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     const Q24 q = q24_carve(c.work, nb);
     mk_input<CF>(p, S, q, c);
     mk_clk(c, CLK_Q24);
-    __syncthreads();
+    mk_sync();
     MRegs<CF> R;
     mk_load_regs<CF>(q, R);
     if (c.stamp && tid == 0) c.stamp[1] = global_ns();
@@ -873,7 +935,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     if (EPI == EPI_STORE && p.qrdy) {
         // QKV rows stored: add, per kv group, the rows of its q heads, k and v
         // this CTA wrote (the attention units wait for (G + 2) * head_dim)
-        __syncthreads();
+        mk_sync();
         if (tid == 0) {
             const int hd = p.hd, ghd = (p.n_heads / p.n_kv) * hd;
             const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
@@ -907,7 +969,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
             best = tt > best ? tt : best;
         }
         if (lane == 0) c.sh->keys[warp] = best;
-        __syncthreads();
+        mk_sync();
         if (tid == 0) {
             for (int w = 1; w < MK_WARPS; w++) best = c.sh->keys[w] > best ? c.sh->keys[w] : best;
             atomicMax(&p.st->key, best);
@@ -941,7 +1003,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
     const Q24 q = q24_carve(c.work, nb);
     mk_input<CF>(p, S, q, c);
     mk_clk(c, CLK_Q24);
-    __syncthreads();
+    mk_sync();
     MRegs<CF> R;
     mk_load_regs<CF>(q, R);
     if (c.stamp && tid == 0) c.stamp[1] = global_ns();
@@ -964,7 +1026,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
                 sh->act[(j * RC + r0) / 2] = silu_ref_f(gv) * uv;
             }
         }
-        __syncthreads();
+        mk_sync();
         if (warp == 0) {  // the act block as q24 (lanes 0-7: four elements each)
             Q24 aq;
             aq.pl = sh->aq;
@@ -975,7 +1037,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
             mk_q24_quad(aq, 0, lane < 8, v, lane);
         }
-        __syncthreads();
+        mk_sync();
         uint4 xa[3], xb[3];
 #pragma unroll
         for (int pl = 0; pl < 3; pl++) {
@@ -1000,11 +1062,11 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
                     atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.acc_out, r0 + r)),
                               (unsigned long long)fx);
             }
-            if (__syncthreads_or(!ok)) {  // slot consumed
+            if (mk_sync_or(!ok)) {  // slot consumed
                 mk_fail(p, c);
                 return false;
             }
-            if (tid == MK_ISSUER) mk_issue_next(p, c);
+            mk_release(c, 1);
             c.seq++;
         }
     }
@@ -1069,7 +1131,7 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
         // this kv group's q/k/v rows of the QKV stage (no grid barrier between)
         if (tid == 0)
             mk_wait_count(p, c, p.qrdy + (size_t)S.layer * p.n_kv + g, (unsigned)((G + 2) * hd));
-        __syncthreads();
+        mk_sync();
         if (c.sh->abort) return false;
         const bool holds = pos >= jlo && pos < jhi;
         const int nrows = G + (holds ? 1 : 0);  // <= 5 rows, one per warp
@@ -1109,8 +1171,8 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
             }
         }
         mk_clk(c, CLK_LOADED);  // attention: inputs arrived, QK-norm done
-        __syncthreads();
-        for (int i = tid; i < nrows * half; i += blockDim.x) {  // RoPE (rope.wgsl:25-34)
+        mk_sync();
+        for (int i = tid; i < nrows * half; i += MK_THREADS) {  // RoPE (rope.wgsl:25-34)
             const int rr = i / half, kq = i - rr * half;
             float* row = rr < G ? qs + (size_t)rr * hd : ks;
             const float sn = c.sh->rsin[kq], cs = c.sh->rcos[kq];
@@ -1118,7 +1180,7 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
             row[kq] = __fsub_rn(__fmul_rn(lo, cs), __fmul_rn(hi, sn));
             row[kq + half] = __fadd_rn(__fmul_rn(hi, cs), __fmul_rn(lo, sn));
         }
-        __syncthreads();
+        mk_sync();
         mk_clk(c, CLK_NORMED);  // attention: RoPE done
         float* kbase = S.kc + (size_t)g * p.max_seq * hd;
         float* vbase = S.vc + (size_t)g * p.max_seq * hd;
@@ -1126,24 +1188,24 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
             kbase[(size_t)pos * hd + tid] = ks[tid];
             vbase[(size_t)pos * hd + tid] = vnew;
         }
-        __syncthreads();
+        mk_sync();
         mk_clk(c, CLK_Q24);  // attention: new K/V row stored
         if (c.stamp && tid == 0) c.stamp[1] = global_ns();
-        attn_core<EPL, GMAX, KV_CG, MK_WARPS>(qs, G, hd, kbase, vbase, hd, jlo, jhi, p.scale, 0.f,
+        attn_core<EPL, GMAX, KV_CG, MK_WARPS, true>(qs, G, hd, kbase, vbase, hd, jlo, jhi, p.scale, 0.f,
                                               sm, res);
         mk_clk(c, CLK_REGS);  // attention: this split's state merged
         if (c.stamp && tid == 0) c.stamp[2] = global_ns();
         if (n_active >= 2 && n_active <= MK_DEFER) {
             const int W = hd + 2, WP = mk_part_w(hd);
-            for (int i = tid; i < G * W; i += blockDim.x) {
+            for (int i = tid; i < G * W; i += MK_THREADS) {
                 const int gi = i / W, d = i - gi * W;
                 p.part[((size_t)(g * G + gi) * p.part_stride + split) * WP + d] = res[i];
             }
         } else {
             attn_finish(res, G, hd, g, split, n_active, p.part_stride, p.part, p.counters, p.attn,
-                        cwt);
+                        cwt, MK_THREADS, true);
         }
-        __syncthreads();
+        mk_sync();
         // this unit's state (or, from the merging unit, the head's output) is
         // stored: release it to the O-projection units of the kv head
         if (tid == 0) red_release_add_u32(p.ardy + (size_t)S.layer * p.n_kv + g, 1u);
@@ -1183,7 +1245,7 @@ __device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
             mk_q24_quad(aq, b, b < NBH, v, lane);
         }
         if (first) mk_clk(c, CLK_LOADED);
-        __syncthreads();
+        mk_sync();
         if (c.sh->abort) return false;
         if (first) {
             mk_clk(c, CLK_Q24);
@@ -1218,12 +1280,11 @@ __device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
                 atomicAdd(reinterpret_cast<unsigned long long*>(acc_at(S.acc_out, r0 + row)),
                           (unsigned long long)__float2ll_rn(part * MK_FIX));
         }
-        if (__syncthreads_or(!ok)) {  // slots consumed
+        if (mk_sync_or(!ok)) {  // slots consumed
             mk_fail(p, c);
             return false;
         }
-        if (tid == MK_ISSUER)
-            for (int k = 0; k < S.per0; k++) mk_issue_next(p, c);
+        mk_release(c, S.per0);
         c.seq += S.per0;
         if (first && c.stamp && tid == 0) c.stamp[2] = global_ns();
         first = false;
@@ -1252,7 +1313,7 @@ template <int I, int NS> using CfgOf = typename CfgOfT<I, NS>::T;
 // (QKV, FFN gate/up, LM head).  Only the code one model runs is compiled into
 // its kernel, which keeps the instruction footprint small.
 template <int EPL, int GMAX, int CD>
-__global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
+__global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ MShared sh;
     __shared__ float rowred[128];
@@ -1271,17 +1332,26 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     c.stamp = nullptr;
     const int tid = threadIdx.x;
     if (tid == 0) {
-        for (int s = 0; s < MK_SLOTS; s++) mbar_init(&sh.full[s], 1);
+        for (int s = 0; s < MK_SLOTS; s++) {
+            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.empty[s], 1);
+        }
         fence_mbar_init();
         sh.it_stage = 0;
         sh.it_t = 0;
         sh.it_j = 0;
         sh.issued = 0;
         sh.abort = 0;
+        sh.prod_done = 0;
         sh.pol = l2_evict_first();
     }
-    for (int i = tid; i < p.n_stages * 4; i += blockDim.x)
+    for (int i = tid; i < p.n_stages * 4; i += MK_BLOCK)
         reinterpret_cast<int4*>(iss)[i] = reinterpret_cast<const int4*>(p.issues)[i];
+    __syncthreads();  // every thread, the producer warp included
+    if (tid >= MK_THREADS) {  // the producer warp: the step's weight copies, in order
+        if (tid == MK_ISSUER) mk_produce(p, c);
+        return;
+    }
     mk_load_stage(p, 0, &sst[0]);
     mk_load_stage(p, 1, &sst[1]);
     mk_load_stage_wait();
@@ -1291,14 +1361,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
     c.pos = pos;
     if (tid < p.hd / 2)  // rope.wgsl:25-34: angle pos * theta^(-2k/hd), f32
         sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid)), &sh.rsin[tid], &sh.rcos[tid]);
-    __syncthreads();
-    if (tid == MK_ISSUER)  // the first ring-full of weights
-        for (int s = 0; s < MK_SLOTS; s++)
-            if (!mk_issue_next(p, c)) break;
+    mk_sync();
     // embedding row (qwen3.rs:128-133), every CTA its own copy
     {
         const int nb = p.dim / 32;
-        for (int i = tid; i < p.dim; i += blockDim.x) {
+        for (int i = tid; i < p.dim; i += MK_THREADS) {
             const int b = i >> 5, j = i & 31;
             const size_t blk = (size_t)tok * nb + b;
             const float d = __half2float(p.emb_scales[blk]);
@@ -1308,17 +1375,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
             if (p.embed_scale > 0.f) v = __fmul_rn(v, p.embed_scale);
             c.emb[i] = v;
         }
-        __syncthreads();
+        mk_sync();
     }
     bool ok = true;
     unsigned nbar = 0;  // grid barriers passed this step
     for (int si = 0; si < p.n_stages && ok; si++) {
         if (si > 0) {
             // the attention and O-projection stages wait on ready counters
-            // instead; the __syncthreads publishes the stage descriptor
+            // instead; the CTA barrier publishes the stage descriptor
             const int kind = iss[si].kind;
             if (kind == SK_ATTN || kind == SK_OCOL) {
-                __syncthreads();
+                mk_sync();
             } else {
                 nbar++;
                 ok = mk_grid_sync(p, c, base + (unsigned long long)nbar * gridDim.x);
@@ -1349,9 +1416,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
             ok = S.cfg >= MK_NCFG ? mk_gemv<CfgOf<CD, 2>, EPI_STORE>(p, S, c)
                                   : mk_gemv<CfgOf<CD, 1>, EPI_STORE>(p, S, c);
         }
-        mk_load_stage_wait();  // made visible by the barrier's __syncthreads
+        mk_load_stage_wait();  // made visible by the next stage's CTA barrier
         if (stamp) {
-            __syncthreads();
+            mk_sync();
             if (tid == 0) stamp[3] = global_ns();
             mk_clk(c, CLK_END);
         }
@@ -1366,19 +1433,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_step(MParams p) {
         __threadfence();
         sh.last = atomicAdd(&p.st->done, 1u) == gridDim.x - 1;
     }
-    __syncthreads();
+    mk_sync();
     if (sh.last) {
         __threadfence();
         const int nc = p.n_layers * p.n_kv;
-        for (int i = tid; i < nc; i += blockDim.x) {
+        for (int i = tid; i < nc; i += MK_THREADS) {
             p.qrdy[i] = 0;
             p.ardy[i] = 0;
         }
-        for (int i = tid; i < p.dim; i += blockDim.x) {
+        for (int i = tid; i < p.dim; i += MK_THREADS) {
             *acc_at(p.zero_a, i) = 0;
             *acc_at(p.zero_b, i) = 0;
         }
-        __syncthreads();
+        mk_sync();
     }
     if (sh.last && tid == 0) {
         {
