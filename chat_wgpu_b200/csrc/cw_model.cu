@@ -468,6 +468,7 @@ __global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n
     st->ctr_base = bar[1];
     st->done = 0;
     st->stopped = 0;
+    st->stall_us = 0;
 }
 
 // ---- hook taps (src/model/mod.rs:155-165) -----------------------------------
@@ -1588,6 +1589,18 @@ int cw_session_set_persistent(cw_session* s, int on) {
                  "the persistent step does not cover this model family");
         CW_TRY(step_plan_create(s));
     }
+    return CW_OK;
+}
+
+int cw_session_inject_stall(cw_session* s, uint32_t wait_us) {
+    clear_error();
+    CW_CHECK(s && wait_us > 0, CW_ERR_INVALID_ARG, "cw_session_inject_stall: bad arguments");
+    CW_CHECK(s->use_persistent && s->plan, CW_ERR_UNSUPPORTED,
+             "cw_session_inject_stall: the session is not on the persistent step");
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaMemcpyAsync(&s->st->stall_us, &wait_us, sizeof(uint32_t), cudaMemcpyHostToDevice,
+                            s->ctx->stream));
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     return CW_OK;
 }
 

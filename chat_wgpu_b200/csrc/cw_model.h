@@ -23,7 +23,7 @@ struct DevState {
     unsigned long long key;  // argmax accumulator of the current step
     unsigned long long bar_base;  // grid-barrier count at the start of the step
     unsigned done;           // CTAs that finished the current step
-    unsigned pad;
+    unsigned stall_us;       // fault injection (cw_session_inject_stall): 0 = off
     unsigned long long ctr_base;  // persistent step's head counter at the start of the step
     unsigned stopped;             // an EOS token ended the sequence (cw_sample.cu)
     unsigned pad2;

@@ -468,7 +468,8 @@ __device__ inline void mk_fail(const MParams& p, MCtx& c) {
 // thread 0's gpu-scope release arrive; thread 0 polls (acquire) until the
 // counter reaches `target`, and a CTA barrier passes that on.  The status
 // word and the time limit are checked every 64 polls.
-__device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long long target) {
+__device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long long target,
+                                    uint64_t limit_ns = MK_WAIT_NS) {
     mk_sync();  // the compute warps' writes before thread 0's release arrive
     if (threadIdx.x == 0) {
         red_release_add(p.bar, 1ull);
@@ -478,7 +479,7 @@ __device__ inline bool mk_grid_sync(const MParams& p, MCtx& c, unsigned long lon
             if ((it & 63) == 0) {
                 const uint64_t now = global_ns();
                 if (t0 == 0) t0 = now;
-                if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
+                if (ld_volatile_i32(p.status) != 0 || now - t0 > limit_ns) {
                     ok = 0;
                     break;
                 }
@@ -1358,6 +1359,9 @@ __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
     const int pos = p.st->pos;
     const unsigned tok = p.st->token;
     const unsigned long long base = p.st->bar_base;
+    // fault injection (tests of the timeout path): the first grid barrier
+    // waits for a count no CTA reaches and gives up after stall_us
+    const unsigned stall_us = p.st->stall_us;
     c.pos = pos;
     if (tid < p.hd / 2)  // rope.wgsl:25-34: angle pos * theta^(-2k/hd), f32
         sincosf(__fmul_rn((float)pos, __ldg(p.inv_freq + tid)), &sh.rsin[tid], &sh.rcos[tid]);
@@ -1388,7 +1392,11 @@ __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
                 mk_sync();
             } else {
                 nbar++;
-                ok = mk_grid_sync(p, c, base + (unsigned long long)nbar * gridDim.x);
+                if (stall_us && nbar == 1)
+                    ok = mk_grid_sync(p, c, base + (unsigned long long)(nbar + 1) * gridDim.x,
+                                      (uint64_t)stall_us * 1000ull);
+                else
+                    ok = mk_grid_sync(p, c, base + (unsigned long long)nbar * gridDim.x);
             }
         }
         if (!ok) break;

@@ -118,6 +118,11 @@ class Session:
             raise ValueError(f"unknown persistent mode {on!r}")
         _lib.call("cw_session_set_persistent", self._h, int(mode))
 
+    def inject_stall(self, wait_us: int) -> None:
+        """Fault injection for tests (cw_session_inject_stall): the next
+        persistent step times out after wait_us microseconds."""
+        _lib.call("cw_session_inject_stall", self._h, int(wait_us))
+
     @property
     def persistent(self) -> bool:
         v = C.c_int()

@@ -367,6 +367,14 @@ int cw_session_set_graph(cw_session* s, int use_graph);
  * asked for a family it does not cover.  cw_session_persistent reports
  * whether the persistent step is in use. */
 int cw_session_set_persistent(cw_session* s, int on);
+/* Fault injection for tests of the timeout path (no reference counterpart:
+ * the reference has no device-side waits).  The next persistent step waits
+ * at its first grid barrier for a count no CTA reaches, gives up after
+ * wait_us microseconds, and every CTA leaves early; the next synchronising
+ * call (cw_sync, cw_session_tokens, ...) reports CW_ERR_TIMEOUT.  The GPU
+ * context stays usable; the session must be restarted with
+ * cw_session_begin.  Only for sessions on the persistent step. */
+int cw_session_inject_stall(cw_session* s, uint32_t wait_us);
 int cw_session_persistent(cw_session* s, int* on);
 /* One step with a host round trip, the shape of the reference's loop body
  * (mod.rs:93-103): the input token is copied from the host (token_in, or
