@@ -72,7 +72,9 @@ __device__ __forceinline__ void attn_sync() {
         __syncthreads();
 }
 
-template <int EPL, int GMAX, int LD = KV_NC, int NW = 4, bool NAMED = false>
+// U keys per warp iteration (ATTN_U; fewer where EPL is large, to bound the
+// registers the iteration's K/V rows take).
+template <int EPL, int GMAX, int LD = KV_NC, int NW = 4, bool NAMED = false, int U = ATTN_U>
 __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
                                           const float* __restrict__ kb,
                                           const float* __restrict__ vb, long rs, int jlo, int jhi,
@@ -91,10 +93,10 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
             acc[gi][e] = 0.f;
         }
     }
-    for (int base = jlo + warp * ATTN_U; base < jhi; base += NW * ATTN_U) {
-        float kk[ATTN_U][EPL], vv[ATTN_U][EPL];
+    for (int base = jlo + warp * U; base < jhi; base += NW * U) {
+        float kk[U][EPL], vv[U][EPL];
 #pragma unroll
-        for (int u = 0; u < ATTN_U; u++) {
+        for (int u = 0; u < U; u++) {
             const int j = base + u;
             const bool ok = j < jhi;
             const float* kr = kb + (size_t)(ok ? j : jlo) * rs;
@@ -118,10 +120,10 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
 #pragma unroll
         for (int gi = 0; gi < GMAX; gi++) {
             if (gi < G) {
-                float s[ATTN_U];
+                float s[U];
                 float mn = m[gi];
 #pragma unroll
-                for (int u = 0; u < ATTN_U; u++) {
+                for (int u = 0; u < U; u++) {
                     float p = 0.f;
 #pragma unroll
                     for (int e = 0; e < EPL; e++) p = fmaf(qr[gi][e], kk[u][e], p);
@@ -130,9 +132,9 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
                     if (base + u < jhi) mn = fmaxf(mn, s[u]);
                 }
                 const float corr = expf(m[gi] - mn);
-                float pe[ATTN_U], psum = 0.f;
+                float pe[U], psum = 0.f;
 #pragma unroll
-                for (int u = 0; u < ATTN_U; u++) {
+                for (int u = 0; u < U; u++) {
                     pe[u] = (base + u < jhi) ? expf(s[u] - mn) : 0.f;
                     psum += pe[u];
                 }
@@ -141,7 +143,7 @@ __device__ __forceinline__ void attn_core(const float* qg, int G, int hd,
                 for (int e = 0; e < EPL; e++) {
                     float a = acc[gi][e] * corr;
 #pragma unroll
-                    for (int u = 0; u < ATTN_U; u++) a = fmaf(vv[u][e], pe[u], a);
+                    for (int u = 0; u < U; u++) a = fmaf(vv[u][e], pe[u], a);
                     acc[gi][e] = a;
                 }
                 m[gi] = mn;

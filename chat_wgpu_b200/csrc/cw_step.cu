@@ -81,11 +81,14 @@ struct StepPlan {
     void (*kern)(MParams) = nullptr;
 };
 
-// Kernel variants (head_dim / 32, GQA group bound, GEMV config of K = dim):
-// Qwen3-0.6B, Qwen3-1.7B, Qwen3-4B/8B, Llama-3.2-1B-like shapes, and the
-// small test shapes.  Other shapes use the per-stage kernels.
-#define CW_STEP_VARIANTS(X) X(4, 2, 0) X(4, 2, 1) X(4, 4, 2) X(2, 4, 1) X(2, 2, 0) X(1, 4, 0)
-#define CW_STEP_DECL(E, G, D) StepKernel step_kernel_##E##_##G##_##D();
+// Kernel variants (head_dim / 32, GQA group bound, GEMV config of K = dim,
+// post-norm residual): Qwen3-0.6B, Qwen3-1.7B, Qwen3-4B/8B, Llama-3.2-1B-like
+// shapes, Gemma-2-2B/9B, and the small test shapes.  Other shapes use the
+// per-stage kernels.
+#define CW_STEP_VARIANTS(X)                                                             \
+    X(4, 2, 0, 0) X(4, 2, 1, 0) X(4, 4, 2, 0) X(2, 4, 1, 0) X(2, 2, 0, 0) X(1, 4, 0, 0) \
+    X(8, 2, 2, 1) X(2, 2, 0, 1)
+#define CW_STEP_DECL(E, G, D, P) StepKernel step_kernel_##E##_##G##_##D##_##P();
 CW_STEP_VARIANTS(CW_STEP_DECL)
 #undef CW_STEP_DECL
 
@@ -94,9 +97,9 @@ static int gmax_of(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 static StepKernel find_kernel(const cw_model_info& I) {
     const int G = I.n_heads / I.n_kv;
     const int epl = (I.head_dim + 31) / 32, gmax = gmax_of(G);
-    const int cd = mk_cfg_for(I.dim);
-#define CW_STEP_FIND(E, G_, D) \
-    if (epl == E && gmax == G_ && cd == D) return step_kernel_##E##_##G_##_##D();
+    const int cd = mk_cfg_for(I.dim), post = I.post_norms ? 1 : 0;
+#define CW_STEP_FIND(E, G_, D, P) \
+    if (epl == E && gmax == G_ && cd == D && post == P) return step_kernel_##E##_##G_##_##D##_##P();
     CW_STEP_VARIANTS(CW_STEP_FIND)
 #undef CW_STEP_FIND
     return nullptr;
@@ -119,10 +122,15 @@ static size_t work_bytes_for(const cw_model_info& I, int n_splits) {
 
 bool step_supported(const cw_model* m, const cw_session* s) {
     const cw_model_info& I = m->info;
-    if (I.post_norms || I.sliding_window || I.attn_softcap > 0.f || I.final_softcap > 0.f ||
-        I.activation != 0 || I.norm_kind != 0)
+    // the two families the step composes: pre-norm SwiGLU (Qwen/Llama), and
+    // Gemma-2's post-norm GeGLU with (1 + w) gains and alternating windows
+    const bool post = I.post_norms != 0;
+    if (post ? (I.norm_kind != 1 || I.activation != 1)
+             : (I.sliding_window || I.attn_softcap > 0.f || I.final_softcap > 0.f ||
+                I.activation != 0 || I.norm_kind != 0))
         return false;
-    if (I.head_dim % 32 || I.n_heads % I.n_kv || !find_kernel(I)) return false;
+    if (post && I.dim > 4096) return false;  // its residual is formed in one register batch
+    if (I.head_dim % 32 || I.head_dim > 256 || I.n_heads % I.n_kv || !find_kernel(I)) return false;
     if (m->embed.type != 2 || !model_q4_only(m, true)) return false;  // Q6_K / k-quant weights
     if (m->tp_world > 1) return false;  // the all-reduces run between kernels
     const int ks[3] = {(int)I.dim, (int)(I.n_heads * I.head_dim), (int)I.hidden};
@@ -171,12 +179,15 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     std::vector<MIssue> is;
     auto gemv = [&](const char* name, const QW& w, int pro, int epi, float* fold_to, int layer,
                     const float* base, const float* norm_w, float* y, const float* bias,
-                    float* xn_out, int acc_in, long long* r1, long long* r2) {
+                    float* xn_out, int acc_in, long long* r1, long long* r2, const float* pa,
+                    const float* pf) {
         V->names.push_back(name);
         MStage S = {};
         S.acc_in = acc_in;
         S.racc = r1;
         S.racc2 = r2;
+        S.post_a = pa;
+        S.post_f = pf;
         S.kind = SK_GEMV;
         S.cfg = mk_cfg_for(w.in_f);
         // two slots per chunk where a CTA would otherwise take several chunks
@@ -212,18 +223,26 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     const int nbh = (int)I.head_dim / 32;          // column blocks per query head
     const int orc = ocol_rows(I, grid);            // rows per O-projection unit
     const int ocpb = std::min(nbh, MK_DOWN_ROWS / orc);  // column blocks per ring slot
+    const bool post = I.post_norms != 0;
+    // window of layer li: Gemma-2 alternates sliding-window (even) and global layers
+    auto window_of = [&](int li) {
+        return (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
+    };
     for (int li = 0; li < L; li++) {
         const Layer& l = m->L[li];
+        const Layer* lprev = li > 0 ? &m->L[li - 1] : nullptr;
         const int p = li % 2, q = 1 - p;
         float* kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
         float* vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
         gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, H[q], li, li == 0 ? nullptr : H[p],
-             l.attn_norm, s->qkv, l.qkv_bias, nullptr, li == 0 ? 0 : 2, Y[q], Z[q]);
+             l.attn_norm, s->qkv, l.qkv_bias, nullptr, li == 0 ? 0 : 2, Y[q], Z[q],
+             post && lprev ? lprev->post_attn : nullptr, post && lprev ? lprev->post_ffw : nullptr);
         V->names.push_back("attention");
         MStage T = {};
         T.kind = SK_ATTN;
         T.nobar = 1;
         T.layer = li;
+        T.window = window_of(li);
         T.q_norm = l.q_norm;
         T.k_norm = l.k_norm;
         T.kc = kc;
@@ -238,6 +257,7 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         O.kind = SK_OCOL;
         O.nobar = 1;
         O.layer = li;
+        O.window = window_of(li);
         O.K = (int)(I.n_heads * I.head_dim);
         O.N = dim;
         O.RC = orc;
@@ -275,6 +295,7 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         F.layer = li;
         F.acc_in = 1;
         F.racc = Y[p];
+        F.post_a = post ? l.post_attn : nullptr;
         F.zero_a = li == 0 ? nullptr : Y[q];
         F.zero_b = li == 0 ? nullptr : Z[q];
         F.payload = l.gate_up.payload;
@@ -302,7 +323,8 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     }
     const int lp = (L - 1) % 2;
     gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, L, H[L % 2], m->final_norm, s->logits,
-         nullptr, s->xnorm, 2, Y[lp], Z[lp]);
+         nullptr, s->xnorm, 2, Y[lp], Z[lp], post ? m->L[L - 1].post_attn : nullptr,
+         post ? m->L[L - 1].post_ffw : nullptr);
     V->n_stages = (int)st.size();
     *smem_need = (size_t)MK_SLOTS * MK_SLOT_BYTES + work + al16((size_t)dim * 4) +
                  is.size() * sizeof(MIssue);
@@ -347,7 +369,12 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     pp.zero_a = Y[lp];
     pp.zero_b = Z[lp];
     pp.part_stride = s->n_splits;
-    pp.attn_min = MK_ATTN_MIN;
+    pp.attn_min = mk_attn_min(((int)I.head_dim + 31) / 32);
+    pp.window_next = (int)I.sliding_window;
+    pp.unit = I.norm_kind == 1;
+    pp.geglu = I.activation == 1;
+    pp.attn_softcap = I.attn_softcap;
+    pp.final_softcap = I.final_softcap;
     pp.eps = I.eps;
     pp.inv_dim = 1.0f / (float)dim;
     pp.scale = powf((float)I.head_dim, -0.5f);  // attention.rs:18

@@ -138,14 +138,18 @@ struct MStage {
     // blocks per slot.
     int nunits, per0, per1, N2;
     // PRO_NORM: the residual is base + racc (acc_in >= 1) + racc2 (acc_in ==
-    // 2), added in that order.  nobar: the stage starts without a grid
-    // barrier (its inputs are guarded by ready counters).
-    int acc_in, layer, nobar, pad1;
+    // 2), added in that order; with post_a / post_f (post-norm families)
+    // each accumulator is first rmsnorm'd with those unit gains.  nobar: the
+    // stage starts without a grid barrier (its inputs are guarded by ready
+    // counters).  window: ATTN / OCOL: sliding-window keys (0 = all).
+    int acc_in, layer, nobar, window;
     long long* racc;
     long long* racc2;
     long long* acc_out;       // FFN / OCOL: the accumulator its partial sums are added into
     long long* zero_a;        // FFN: accumulators of the previous layer, zeroed here (this
     long long* zero_b;        //      CTA's slice of rows)
+    const float* post_a;      // PRO_NORM: post-attention norm gains of racc (or null)
+    const float* post_f;      // PRO_NORM: post-FFN norm gains of racc2 (or null)
     const void* pad_ptr;
     const uint8_t* payload2;  // FFN: down projection, OCOL: O projection, column-block-major
     const __half* scales2;    //      [K/32][rows][16] + scales [K/32][rows]
@@ -203,6 +207,7 @@ struct MParams {
     int dim, n_heads, n_kv, hd, max_seq, n_splits, part_stride, decode;
     int n_layers;
     int attn_min;  // keys per attention split before splitting further
+    int window_next;  // window of the layer after a non-windowed one (alternating families)
     // Ready counters [n_layers][n_kv], zeroed at the end of every step:
     // qrdy counts the QKV rows of each kv group's heads stored this step
     // (the attention units wait for (G + 2) * head_dim), ardy the attention
@@ -213,6 +218,10 @@ struct MParams {
     long long* zero_a;  // the last layer's accumulators, zeroed at the end of the step
     long long* zero_b;
     float eps, scale;
+    int unit;             // norm gains 1 + w (UnitShift) instead of w
+    int geglu;            // FFN activation GeGLU (gelu_tanh) instead of SwiGLU
+    float attn_softcap;   // attention logits cap * tanh(s / cap) (0 = off)
+    float final_softcap;  // LM-head logits cap * tanh(l / cap) (0 = off)
     float inv_dim;      // 1/dim: the mean of squares as a product (exact for power-of-two dims)
     size_t work_bytes;  // shared-memory work region (q24 + hbuf + wbuf, or attention scratch)
     // profiling only: per stage and CTA, %globaltimer at the stage's start
@@ -221,9 +230,11 @@ struct MParams {
     unsigned long long* stamps;
 };
 
-// keys per attention split in the persistent step: one iteration of all
-// 16 warps (4 keys each) before a split is worth its combine
-constexpr int MK_ATTN_MIN = MK_WARPS * ATTN_U;
+// Keys per warp iteration of the step's attention: ATTN_U, two for head_dim
+// 256 (its K/V rows take twice the registers); a split is worth its combine
+// from one iteration of all 16 warps on.
+__host__ __device__ constexpr int mk_attn_u(int epl) { return epl >= 8 ? 2 : ATTN_U; }
+__host__ __device__ constexpr int mk_attn_min(int epl) { return MK_WARPS * mk_attn_u(epl); }
 // With 2..MK_DEFER active key splits, the attention stage only publishes each
 // split's (accumulator, max, denominator) and the O-projection stage merges
 // the splits of its head while it builds its input (no combine step, fence or
@@ -248,7 +259,7 @@ struct MShared {
     unsigned long long keys[MK_WARPS];
     // RoPE angle pos * inv_freq[k] of this step's position: sin and cos,
     // computed once at the kernel start (every layer rotates at that position)
-    float rsin[64], rcos[64];
+    float rsin[128], rcos[128];  // RoPE table of this position (head_dim <= 256)
 };
 
 struct MCtx {
@@ -630,7 +641,30 @@ static __device__ __noinline__ float4 mk_head_out4(const float* attn, const floa
 template <class LD>
 __device__ inline void mk_prologue_staged(const MParams& p, const MStage& S, const Q24& q,
                                           float* hbuf, float* wbuf, MCtx& c, const LD& ld_src);
-template <bool BIG>
+__device__ inline void mk_prologue_tail(const MParams& p, const MStage& S, const Q24& q, MCtx& c,
+                                        float4 (&v)[MK_QB]);
+// h * 2^-32 for the four accumulator rows i .. i+3
+__device__ __forceinline__ float4 mk_fixed4(const long long* acc, int i) {
+    return mk_add_fixed4(f4_zero(), acc, i);
+}
+__device__ __forceinline__ float4 f4_add(const float4& a, const float4& b) {
+    return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+__device__ __forceinline__ float4 f4_unit(const float4& w) {  // 1 + w (UnitShift gains)
+    return make_float4(1.0f + w.x, 1.0f + w.y, 1.0f + w.z, 1.0f + w.w);
+}
+__device__ __forceinline__ float f4_ss(const float4& v, float ss) {
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    return fmaf(v.w, v.w, ss);
+}
+
+// POST (post-norm families, Gemma-2): the residual is
+// base + rmsnorm_unit(racc; post_a) + rmsnorm_unit(racc2; post_f), the
+// additions of the reference composition's x = x + post_norm(o) and
+// x = x + post_norm(ffn) (one batch in registers: K <= 4096).
+template <bool BIG, bool POST>
 __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24& q, float* hbuf,
                             float* wbuf, MCtx& c) {
     const int nb = S.K / 32, nq = nb / 4;  // quad groups (nb is a multiple of 8)
@@ -638,7 +672,6 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
     const int sub = lane >> 3, e0 = 4 * (lane & 7);
     const float* src = S.base ? S.base : c.emb;
     const bool gsrc = S.base != nullptr;
-    const bool wx = S.xn_out && blockIdx.x == 0;
     // the residual: base (+ the fixed-point FFN accumulator when acc_in)
     auto ld_src = [&](int i) {
         float4 h = gsrc ? __ldcg(reinterpret_cast<const float4*>(src + i))
@@ -647,14 +680,66 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
         if (S.acc_in >= 2) h = mk_add_fixed4(h, S.racc2, i);
         return h;
     };
-    float ss = 0.f;
+    if constexpr (POST) {
+        static_assert(!BIG, "post-norm residuals are formed in one batch");
+        float4 v[MK_QB], ya[MK_QB], zf[MK_QB], ga[MK_QB], gf[MK_QB];
+        float ssa = 0.f, ssf = 0.f;
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub, i = b * 32 + e0;
+            const bool in = b < nb;
+            v[k] = !in ? f4_zero()
+                       : gsrc ? __ldcg(reinterpret_cast<const float4*>(src + i))
+                              : *reinterpret_cast<const float4*>(src + i);
+            ya[k] = in && S.acc_in >= 1 ? mk_fixed4(S.racc, i) : f4_zero();
+            zf[k] = in && S.acc_in >= 2 ? mk_fixed4(S.racc2, i) : f4_zero();
+            ga[k] = in && S.acc_in >= 1 ? __ldg(reinterpret_cast<const float4*>(S.post_a + i)) : f4_zero();
+            gf[k] = in && S.acc_in >= 2 ? __ldg(reinterpret_cast<const float4*>(S.post_f + i)) : f4_zero();
+            ssa = f4_ss(ya[k], ssa);
+            ssf = f4_ss(zf[k], ssf);
+        }
+        if (S.acc_in >= 1) {
+            const float inva = 1.0f / sqrtf(mk_cta_sum(ssa, c) * p.inv_dim + p.eps);
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) v[k] = f4_add(v[k], f4_norm(ya[k], inva, f4_unit(ga[k])));
+        }
+        if (S.acc_in >= 2) {
+            const float invf = 1.0f / sqrtf(mk_cta_sum(ssf, c) * p.inv_dim + p.eps);
+#pragma unroll
+            for (int k = 0; k < MK_QB; k++) v[k] = f4_add(v[k], f4_norm(zf[k], invf, f4_unit(gf[k])));
+        }
+        mk_prologue_tail(p, S, q, c, v);
+        return;
+    }
     if (!BIG || nq <= MK_WARPS * MK_QB) {  // one batch: everything stays in registers
-        float4 v[MK_QB], w[MK_QB];
+        float4 v[MK_QB];
 #pragma unroll
         for (int k = 0; k < MK_QB; k++) {
             const int b = 4 * (warp + k * MK_WARPS) + sub, i = b * 32 + e0;
             v[k] = b < nb ? ld_src(i) : f4_zero();
+        }
+        mk_prologue_tail(p, S, q, c, v);
+        return;
+    }
+    if constexpr (BIG) mk_prologue_staged(p, S, q, hbuf, wbuf, c, ld_src);
+}
+
+// One-batch prologue from the residual v (four elements per lane per
+// quad group): this CTA's fold slice, the CTA-wide rmsnorm, the q24 planes.
+__device__ inline void mk_prologue_tail(const MParams& p, const MStage& S, const Q24& q, MCtx& c,
+                                        float4 (&v)[MK_QB]) {
+    const int nb = S.K / 32, nq = nb / 4;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane >> 3, e0 = 4 * (lane & 7);
+    const bool wx = S.xn_out && blockIdx.x == 0;
+    float ss = 0.f;
+    {
+        float4 w[MK_QB];
+#pragma unroll
+        for (int k = 0; k < MK_QB; k++) {
+            const int b = 4 * (warp + k * MK_WARPS) + sub, i = b * 32 + e0;
             w[k] = b < nb ? __ldg(reinterpret_cast<const float4*>(S.norm_w + i)) : f4_zero();
+            if (p.unit) w[k] = f4_unit(w[k]);
         }
         if (S.fold_to) {  // this CTA's slice of the residual: the next stages' base
             const int rs = mk_slice_rows(S.K), lo = blockIdx.x * rs;
@@ -687,9 +772,7 @@ __device__ inline void mk_prologue(const MParams& p, const MStage& S, const Q24&
             const int b = 4 * (warp + k * MK_WARPS) + sub;
             if (warp + k * MK_WARPS < nq) mk_q24_quad(q, b, b < nb, v[k], lane);
         }
-        return;
     }
-    if constexpr (BIG) mk_prologue_staged(p, S, q, hbuf, wbuf, c, ld_src);
 }
 
 // The multi-batch path of mk_prologue: inputs staged in shared memory.
@@ -708,6 +791,7 @@ __device__ inline void mk_prologue_staged(const MParams& p, const MStage& S, con
             const int b = 4 * (t0 + k * MK_WARPS) + sub, i = b * 32 + e0;
             v[k] = b < nb ? ld_src(i) : f4_zero();
             w[k] = b < nb ? __ldg(reinterpret_cast<const float4*>(S.norm_w + i)) : f4_zero();
+            if (p.unit) w[k] = f4_unit(w[k]);
         }
 #pragma unroll
         for (int k = 0; k < MK_QB; k++) {
@@ -774,12 +858,12 @@ __device__ __forceinline__ float mk_block_dot(const uint4& w4, const uint4 (&xa)
 
 // The input vector of a GEMV stage as q24 planes in the work region.
 constexpr int MK_ONE_BATCH_BLOCKS = 4 * MK_WARPS * MK_QB;
-template <class CF>
+template <class CF, bool POST>
 __device__ __forceinline__ void mk_input(const MParams& p, const MStage& S, const Q24& q,
                                          MCtx& c) {
     float* hbuf = reinterpret_cast<float*>(c.work + al16(q24_bytes(q.nb)));
     float* wbuf = hbuf + S.K;
-    mk_prologue<(CF::NB_MAX > MK_ONE_BATCH_BLOCKS)>(p, S, q, hbuf, wbuf, c);
+    mk_prologue<(CF::NB_MAX > MK_ONE_BATCH_BLOCKS), POST>(p, S, q, hbuf, wbuf, c);
 }
 
 // This lane's blocks of the q24 planes, kept in registers for the chunk loop.
@@ -875,14 +959,19 @@ __device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int 
 // Each variant compiles only its own epilogue: the step kernel's code is
 // streamed through the instruction caches once per layer, so what a stage
 // does not run should not sit in its instruction stream.
-template <class CF, int EPI>
+template <class CF, int EPI, bool POST>
 __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     static_assert(EPI == EPI_STORE || EPI == EPI_HEAD, "QKV or LM head");
     constexpr int WPR = CF::WPR, RC = CF::RC;
     const int nb = S.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if ((int)blockIdx.x >= S.nchunks) {  // no rows of this stage here
-        if (S.fold_to) {  // but still this CTA's slice of the next residual base
+        if (POST && S.fold_to) {
+            // but still this CTA's slice of the next residual base, which
+            // takes the norms of the whole accumulators: the full prologue
+            if ((int)blockIdx.x * mk_slice_rows(S.K) < S.K)
+                mk_input<CF, POST>(p, S, q24_carve(c.work, nb), c);
+        } else if (S.fold_to) {  // but still this CTA's slice of the next residual base
             const int rs = mk_slice_rows(S.K), i = blockIdx.x * rs + 4 * tid;
             if (4 * tid < rs && i < S.K) {
                 float4 h = S.base ? __ldcg(reinterpret_cast<const float4*>(S.base + i))
@@ -900,7 +989,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
     if (EPI == EPI_STORE && S.bias && tid < RC && (long)blockIdx.x * RC + tid < S.N)
         add = __ldg(S.bias + (long)blockIdx.x * RC + tid);
     const Q24 q = q24_carve(c.work, nb);
-    mk_input<CF>(p, S, q, c);
+    mk_input<CF, POST>(p, S, q, c);
     mk_clk(c, CLK_Q24);
     mk_sync();
     MRegs<CF> R;
@@ -923,6 +1012,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
             for (int w = 0; w < WPR; w++) vv += rb[tid * WPR + w];
             const long row = row0 + tid;
             if (EPI == EPI_HEAD) {
+                if (p.final_softcap > 0.f) vv = p.final_softcap * tanhf(vv / p.final_softcap);
                 S.y[row] = vv;
                 const unsigned long long kk = argmax_key(vv, (unsigned)row);
                 best = kk > best ? kk : best;
@@ -986,7 +1076,7 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
 // (MK_DOWN_ROWS rows per ring slot, one Q4_0 block per row) turns them into a
 // partial sum for every output row, added into the fixed-point residual
 // accumulator S.acc_out (the next stage that reads the residual adds it).
-template <class CF>
+template <class CF, bool POST>
 __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
     constexpr int WPR = CF::WPR, RC = CF::RC;
     const int nb = S.K / 32;
@@ -1002,7 +1092,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
     }
     if ((int)blockIdx.x >= S.nunits) return true;
     const Q24 q = q24_carve(c.work, nb);
-    mk_input<CF>(p, S, q, c);
+    mk_input<CF, POST>(p, S, q, c);
     mk_clk(c, CLK_Q24);
     mk_sync();
     MRegs<CF> R;
@@ -1024,7 +1114,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
                     gv += rb[r0 * WPR + w];
                     uv += rb[(r0 + 1) * WPR + w];
                 }
-                sh->act[(j * RC + r0) / 2] = silu_ref_f(gv) * uv;
+                sh->act[(j * RC + r0) / 2] = (p.geglu ? gelu_ref_f(gv) : silu_ref_f(gv)) * uv;
             }
         }
         mk_sync();
@@ -1081,10 +1171,10 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
 // u % n_kv, key split u / n_kv of n_active) of the layer at kc / vc into L2.
 __device__ __forceinline__ void mk_kv_prefetch_unit(const MParams& p, const float* kc,
                                                     const float* vc, int u, int n_active,
-                                                    int pos) {
+                                                    int pos, int window) {
     const int g = u % p.n_kv, split = u / p.n_kv;
     int jlo, jhi;
-    attn_range(pos + 1, 0, split, n_active, &jlo, &jhi);
+    attn_range(pos + 1, window, split, n_active, &jlo, &jhi);
     const int j1 = min(jhi, pos);
     if (j1 <= jlo) return;
     const float* kb = kc + (size_t)g * p.max_seq * p.hd;
@@ -1099,9 +1189,9 @@ __device__ __forceinline__ void mk_kv_prefetch_unit(const MParams& p, const floa
 // every critical path).
 __device__ inline void mk_kv_prefetch(const MParams& p, const MStage& A, const MCtx& c) {
     const int seq = c.pos + 1;
-    const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
+    const int n_active = attn_active_splits(attn_span(seq, A.window), p.n_splits, p.attn_min);
     for (int u = blockIdx.x; u < p.n_kv * n_active; u += gridDim.x)  // every unit of this CTA
-        mk_kv_prefetch_unit(p, A.kc, A.vc, u, n_active, c.pos);
+        mk_kv_prefetch_unit(p, A.kc, A.vc, u, n_active, c.pos, A.window);
 }
 
 template <int EPL, int GMAX>
@@ -1109,7 +1199,7 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
     const int G = p.n_heads / p.n_kv, hd = p.hd, half = hd / 2;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int pos = c.pos, seq = pos + 1;
-    const int n_active = attn_active_splits(seq, p.n_splits, p.attn_min);
+    const int n_active = attn_active_splits(attn_span(seq, S.window), p.n_splits, p.attn_min);
     const int units = p.n_kv * n_active;
     const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
     float* sm = reinterpret_cast<float*>(c.work);
@@ -1119,16 +1209,19 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
     float* ks = qs + (size_t)G * hd;
     if ((int)blockIdx.x >= units) {  // no unit here: prefetch the next layer's K/V rows
         const int f = blockIdx.x - units;
-        if (tid == 0 && f < units && S.layer + 1 < p.n_layers) {
+        if (tid == 0 && S.layer + 1 < p.n_layers) {
+            // the next layer's window (layers alternate in windowed families)
+            const int nw = S.window ? 0 : p.window_next;
+            const int na = attn_active_splits(attn_span(seq, nw), p.n_splits, p.attn_min);
             const size_t ls = (size_t)p.n_kv * p.max_seq * hd;  // one layer of the cache
-            mk_kv_prefetch_unit(p, S.kc + ls, S.vc + ls, f, n_active, pos);
+            if (f < p.n_kv * na) mk_kv_prefetch_unit(p, S.kc + ls, S.vc + ls, f, na, pos, nw);
         }
         return true;
     }
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const int g = u % p.n_kv, split = u / p.n_kv;
         int jlo, jhi;
-        attn_range(seq, 0, split, n_active, &jlo, &jhi);
+        attn_range(seq, S.window, split, n_active, &jlo, &jhi);
         // this kv group's q/k/v rows of the QKV stage (no grid barrier between)
         if (tid == 0)
             mk_wait_count(p, c, p.qrdy + (size_t)S.layer * p.n_kv + g, (unsigned)((G + 2) * hd));
@@ -1192,8 +1285,8 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
         mk_sync();
         mk_clk(c, CLK_Q24);  // attention: new K/V row stored
         if (c.stamp && tid == 0) c.stamp[1] = global_ns();
-        attn_core<EPL, GMAX, KV_CG, MK_WARPS, true>(qs, G, hd, kbase, vbase, hd, jlo, jhi, p.scale, 0.f,
-                                              sm, res);
+        attn_core<EPL, GMAX, KV_CG, MK_WARPS, true, mk_attn_u(EPL)>(
+            qs, G, hd, kbase, vbase, hd, jlo, jhi, p.scale, p.attn_softcap, sm, res);
         mk_clk(c, CLK_REGS);  // attention: this split's state merged
         if (c.stamp && tid == 0) c.stamp[2] = global_ns();
         if (n_active >= 2 && n_active <= MK_DEFER) {
@@ -1225,10 +1318,10 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
 // needs only its own head's attention state, not the whole attention output.
 template <int NBH>
 __device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
-    static_assert(NBH == 1 || NBH == 2 || NBH == 4, "head_dim 32, 64 or 128");
+    static_assert(NBH == 1 || NBH == 2 || NBH == 4 || NBH == 8, "head_dim 32 .. 256");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nch = (S.N + S.RC - 1) / S.RC;
-    const int na = attn_active_splits(c.pos + 1, p.n_splits, p.attn_min);
+    const int na = attn_active_splits(attn_span(c.pos + 1, S.window), p.n_splits, p.attn_min);
     bool first = true;
     for (int u = blockIdx.x; u < S.nunits; u += gridDim.x) {
         const int h = u / nch, r0 = (u - h * nch) * S.RC, rows = min(S.RC, S.N - r0);
@@ -1239,11 +1332,14 @@ __device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
                 mk_wait_count(p, c, p.ardy + (size_t)S.layer * p.n_kv + h / (p.n_heads / p.n_kv),
                               (unsigned)na);
             __syncwarp();
-            const int b = lane >> 3;
-            const float4 v = b < NBH ? mk_head_out4(p.attn, p.part, p.part_stride, p.hd, h,
-                                                    b * 32 + 4 * (lane & 7), na)
-                                     : f4_zero();
-            mk_q24_quad(aq, b, b < NBH, v, lane);
+#pragma unroll
+            for (int b0 = 0; b0 < NBH; b0 += 4) {  // four blocks per pass
+                const int b = b0 + (lane >> 3);
+                const float4 v = b < NBH ? mk_head_out4(p.attn, p.part, p.part_stride, p.hd, h,
+                                                        b * 32 + 4 * (lane & 7), na)
+                                         : f4_zero();
+                mk_q24_quad(aq, b, b < NBH, v, lane);
+            }
         }
         if (first) mk_clk(c, CLK_LOADED);
         mk_sync();
@@ -1311,9 +1407,10 @@ template <int I, int NS> using CfgOf = typename CfgOfT<I, NS>::T;
 // The step kernel, specialised for one model shape: EPL = head_dim / 32
 // registers per lane and GMAX >= n_heads / n_kv for the attention stage (EPL
 // column blocks per head in the O projection), CD the GEMV config of K = dim
-// (QKV, FFN gate/up, LM head).  Only the code one model runs is compiled into
-// its kernel, which keeps the instruction footprint small.
-template <int EPL, int GMAX, int CD>
+// (QKV, FFN gate/up, LM head), POST the post-norm residual of Gemma-2-like
+// families.  Only the code one model runs is compiled into its kernel, which
+// keeps the instruction footprint small.
+template <int EPL, int GMAX, int CD, bool POST>
 __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ MShared sh;
@@ -1417,12 +1514,12 @@ __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
         } else if (S.kind == SK_OCOL) {
             ok = mk_ocol<EPL>(p, S, c);
         } else if (S.kind == SK_FFN) {
-            ok = mk_ffn<CfgOf<CD, 2>>(p, S, c);
+            ok = mk_ffn<CfgOf<CD, 2>, POST>(p, S, c);
         } else if (S.epi == EPI_HEAD) {  // always two slots per chunk
-            ok = mk_gemv<CfgOf<CD, 2>, EPI_HEAD>(p, S, c);
+            ok = mk_gemv<CfgOf<CD, 2>, EPI_HEAD, POST>(p, S, c);
         } else {
-            ok = S.cfg >= MK_NCFG ? mk_gemv<CfgOf<CD, 2>, EPI_STORE>(p, S, c)
-                                  : mk_gemv<CfgOf<CD, 1>, EPI_STORE>(p, S, c);
+            ok = S.cfg >= MK_NCFG ? mk_gemv<CfgOf<CD, 2>, EPI_STORE, POST>(p, S, c)
+                                  : mk_gemv<CfgOf<CD, 1>, EPI_STORE, POST>(p, S, c);
         }
         mk_load_stage_wait();  // made visible by the next stage's CTA barrier
         if (stamp) {

@@ -4,6 +4,6 @@
 
 namespace cw {
 
-StepKernel step_kernel_1_4_0() { return k_step<1, 4, 0>; }
+StepKernel step_kernel_1_4_0_0() { return k_step<1, 4, 0, false>; }
 
 }  // namespace cw

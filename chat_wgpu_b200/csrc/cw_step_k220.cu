@@ -4,6 +4,6 @@
 
 namespace cw {
 
-StepKernel step_kernel_2_2_0() { return k_step<2, 2, 0>; }
+StepKernel step_kernel_2_2_0_0() { return k_step<2, 2, 0, false>; }
 
 }  // namespace cw

@@ -4,6 +4,6 @@
 
 namespace cw {
 
-StepKernel step_kernel_2_4_1() { return k_step<2, 4, 1>; }
+StepKernel step_kernel_2_4_1_0() { return k_step<2, 4, 1, false>; }
 
 }  // namespace cw

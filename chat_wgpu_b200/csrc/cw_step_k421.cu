@@ -4,6 +4,6 @@
 
 namespace cw {
 
-StepKernel step_kernel_4_2_1() { return k_step<4, 2, 1>; }
+StepKernel step_kernel_4_2_1_0() { return k_step<4, 2, 1, false>; }
 
 }  // namespace cw

@@ -4,6 +4,6 @@
 
 namespace cw {
 
-StepKernel step_kernel_4_4_2() { return k_step<4, 4, 2>; }
+StepKernel step_kernel_4_4_2_0() { return k_step<4, 4, 2, false>; }
 
 }  // namespace cw

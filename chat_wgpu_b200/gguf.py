@@ -192,6 +192,11 @@ CONFIGS = {
     "gemma2-2b": dict(arch="gemma2", dim=2304, n_layers=26, n_heads=8, n_kv=4, head_dim=256,
                       hidden=9216, vocab=256000, eps=1e-6, theta=1e4, tied=True, window=4096,
                       attn_softcap=50.0, final_softcap=30.0),
+    # Gemma-2 head and residual shapes (head_dim 256, dim 2304) over three layers,
+    # a short window and tight soft-caps: the post-norm persistent step variant
+    "mid-gemma2": dict(arch="gemma2", dim=2304, n_layers=3, n_heads=4, n_kv=2, head_dim=256,
+                       hidden=1536, vocab=4096, eps=1e-6, theta=1e4, tied=True, window=80,
+                       attn_softcap=5.0, final_softcap=8.0),
     "tiny-qwen3": dict(arch="qwen3", dim=64, n_layers=2, n_heads=4, n_kv=2, head_dim=16,
                        hidden=128, vocab=256, eps=1e-6, theta=1e6, tied=True),
     # small shapes that exercise the family switches in tests

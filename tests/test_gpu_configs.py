@@ -14,7 +14,8 @@ compared up to their first near-tie.
             on the persistent step; and the prompt through batched prefill
   config 4  Gemma-2-2B shapes (UnitShift norms, GeGLU, soft-caps, sliding
             window, post-norms), 128-token prompt through batched prefill and
-            token by token, 32 greedy tokens
+            token by token, 32 greedy tokens on the persistent step; 16 on
+            the per-stage kernels
   config 5  Qwen3-8B, 32-token prompt, 8 greedy tokens; and its layer shapes
             (qwen3-8b-2l) over a 4096-token prompt through batched prefill
             against the token-by-token steps (every K/V cache row, then the
@@ -133,14 +134,19 @@ def test_config3_qwen3_0_6b_bench_run(ctx, orc):
 def test_config4_gemma2_2b(ctx, orc):
     """Gemma-2-2B shapes: head_dim 256, GQA 8/4, UnitShift norms, GeGLU,
     post-attention / post-FFN norms, attention soft-cap 50, final soft-cap
-    30, embedding scale, alternating 4096-key sliding window; per-stage
-    kernels (the family the persistent step does not cover)."""
+    30, embedding scale, alternating 4096-key sliding window.  The prompt
+    through batched prefill, then the persistent step; token by token on the
+    persistent step and on the per-stage kernels."""
     from chat_wgpu_b200 import gguf
     from chat_wgpu_b200.model import Model
     _threads(orc)
     path = gguf.cached_model("gemma2-2b", seed=0)
     m = Model(ctx, path)
     assert m.info["head_dim"] == 256 and m.info["vocab"] == 256000
+    from chat_wgpu_b200.model import Session
+    probe = Session(m, 8)
+    assert probe.persistent  # the post-norm step variant covers Gemma-2-2B
+    probe.close()
     prompt = bench_prompt(m.info["vocab"], 128)
     toks, logits = gpu_stream(m, prompt, 32, prefill=True)
     om = orc.Model(path)
@@ -153,6 +159,9 @@ def test_config4_gemma2_2b(ctx, orc):
             n = i
             break
     check_forced(t2[:n + 1], l2[:n + 1], ref[:n + 1], "gemma2 token by token")
+    t3, l3 = gpu_stream(m, prompt, 16, persistent=False)
+    ref3 = ref[:16] if np.array_equal(t3, toks[:16]) else forced_logits(om, prompt, t3)
+    check_forced(t3, l3, ref3, "gemma2 per-stage")
     om.close()
     m.close()
 

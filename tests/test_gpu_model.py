@@ -69,7 +69,7 @@ def models(tmp_path_factory):
 
 # families the persistent one-launch step covers (the others always use the
 # per-stage kernels)
-PERSISTENT = {"tiny-qwen3": False, "small-qwen3": True, "tiny-gemma2": False, "tiny-qwen2": True,
+PERSISTENT = {"tiny-qwen3": False, "small-qwen3": True, "tiny-gemma2": True, "tiny-qwen2": True,
               "wide-ffn-qwen3": True, "odd-qwen3": True}
 
 
@@ -149,6 +149,33 @@ def test_persistent_equals_per_stage_long(ctx, orc, models, n_prompt):
     assert compare_streams(tp, ref_toks, ref_logits, lp) >= 4
     assert compare_streams(ts, ref_toks, ref_logits, ls) >= 4
     td, ld = session_stream(m, prompt, 40, use_graph=False, persistent=mode)
+    assert np.array_equal(tp, td)
+    assert np.array_equal(lp.view(np.uint32), ld.view(np.uint32))
+    m.close()
+    om.close()
+
+
+@pytest.mark.parametrize("n_prompt", [12, 150])
+def test_persistent_gemma2_hd256(ctx, orc, tmp_path, n_prompt):
+    """The post-norm step variant at Gemma-2 head and residual shapes
+    (head_dim 256, dim 2304, GQA 4/2): UnitShift gains, GeGLU, soft-caps 5 and
+    8, an 80-key window on even layers (150-token prompt: windowed layers read
+    2-3 key splits, global layers 5), an odd layer count.  Persistent and
+    per-stage paths both within tolerance of the oracle; graph == direct,
+    bit-exact."""
+    from chat_wgpu_b200 import gguf
+    from chat_wgpu_b200.model import Model
+    path = gguf.synth_model(str(tmp_path / "mid-gemma2.gguf"), gguf.CONFIGS["mid-gemma2"], seed=6)
+    om = orc.Model(path)
+    rng = np.random.default_rng(n_prompt)
+    prompt = rng.integers(0, om.vocab, n_prompt).astype(np.uint32)
+    ref_toks, ref_logits = om.generate(prompt, 24, want_logits=True)
+    m = Model(ctx, path)
+    tp, lp = session_stream(m, prompt, 24, persistent=True)
+    ts, ls = session_stream(m, prompt, 24, persistent=False)
+    assert compare_streams(tp, ref_toks, ref_logits, lp) >= 4
+    assert compare_streams(ts, ref_toks, ref_logits, ls) >= 4
+    td, ld = session_stream(m, prompt, 24, use_graph=False, persistent=True)
     assert np.array_equal(tp, td)
     assert np.array_equal(lp.view(np.uint32), ld.view(np.uint32))
     m.close()
