@@ -307,6 +307,43 @@ def oracle_leg(path: str, prompt, gpu_tokens, budget_s: float = 10.0, single_s: 
     return multi, single, parity
 
 
+def cpu_gemv_sweep(threads: int, budget_s: float = 12.0) -> dict:
+    """The GEMV sweep on the host: the oracle's Q4_0 dequant-dot
+    (orc_q4_0_gemv, dequant.rs:62-78 + matmul.wgsl:43-50) per shape, on all
+    host threads (repeated for at least 0.1 s) and on one thread (once).  All
+    shapes view one buffer of random blocks sized for the largest."""
+    from oracle import oracle as orc
+    from chat_wgpu_b200 import gguf
+    from chat_wgpu_b200.q4bench import SHAPES, algorithmic_bytes
+    kmax, nmax = max(SHAPES, key=lambda s: s[0] * s[1])
+    blocks = gguf.random_q4_0_blocks(np.random.default_rng(5), nmax, kmax).ravel()
+    rows = []
+    t_all = time.perf_counter()
+    for k, n in SHAPES:
+        if time.perf_counter() - t_all > budget_s:
+            break
+        w = blocks[: n * (k // 32) * 18]
+        x = np.random.default_rng(k + n).normal(0, 1, k).astype(np.float32)
+        b = algorithmic_bytes(k, n)
+        orc.set_threads(threads)
+        orc.q4_0_gemv(x, w, k, n)  # warm
+        reps, t0 = 0, time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < 0.1:
+            orc.q4_0_gemv(x, w, k, n)
+            reps += 1
+        multi = (time.perf_counter() - t0) / reps
+        orc.set_threads(1)
+        t1 = time.perf_counter()
+        orc.q4_0_gemv(x, w, k, n)
+        one = time.perf_counter() - t1
+        rows.append({"in_f": k, "out_f": n, "us": round(multi * 1e6, 1),
+                     "gbs": round(b / multi / 1e9, 2), "us_1thread": round(one * 1e6, 1),
+                     "gbs_1thread": round(b / one / 1e9, 3)})
+    orc.set_threads(threads)
+    return {"kind": "port", "cores": threads, "unit": "us per call, GB/s (same algorithmic bytes)",
+            "shapes": rows}
+
+
 def gemv_sweep(ctx, peak_gbs: float) -> list:
     """The metric's second half: Q4_0 GEMV (cw_q4_0_gemv) per shape, config 1
     (1024 -> 3072) and the Qwen3 projection sweep with the four LM heads.
@@ -554,6 +591,8 @@ def run_cuda(args, dist):
                               "sample": f"{single['steps']} further decode steps on one thread "
                                         f"({single['seconds']:.1f} s)"},
             "nproc": os.cpu_count()}
+        if not args.no_gemv:
+            line["cpu_baseline"]["gemv"] = cpu_gemv_sweep(multi["cores"])
         line["parity"] = parity
     model.close()
     ctx.close()

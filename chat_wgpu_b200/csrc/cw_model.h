@@ -71,8 +71,12 @@ struct cw_model {
     std::vector<cw::Layer> L;
     float* final_norm = nullptr;
     cw::QW embed, head;
-    std::vector<cw::QW> down_cm;  // down projections, column-block-major (persistent step)
-    std::vector<cw::QW> wo_cm;    // O projections, column-block-major (persistent step)
+    // persistent step (cw_step.cu): slot-packed copies of the matrices it
+    // streams, one contiguous [payload | scales] range per weight-ring slot;
+    // built on the first plan, for that plan's slot geometry (pk_key)
+    std::vector<const uint8_t*> pk_qkv, pk_gu, pk_down, pk_wo;
+    const uint8_t* pk_head = nullptr;
+    long long pk_key = -1;
     std::vector<cw_buf> owned;
     const float* inv_freq = nullptr;
     // every projection and the head (4 per layer: qkv, wo, gate_up, down; then

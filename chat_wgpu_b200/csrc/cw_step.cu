@@ -4,6 +4,7 @@
 // its own cw_step_k*.cu so they compile in parallel.
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <memory>
 #include <string>
@@ -14,55 +15,86 @@
 namespace cw {
 
 // ---- host ---------------------------------------------------------------------------
-// Column-block-major copy of a packed Q4_0 matrix: block b of row r moves to
-// [b][r], so the column block an FFN unit needs is one contiguous range.
-__global__ void k_colmajor(const uint8_t* __restrict__ pay, const __half* __restrict__ sc, int rows,
-                           int nb, uint8_t* __restrict__ opay, __half* __restrict__ osc) {
-    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+// Slot-packed copies of the matrices the step streams (layouts in MIssue,
+// cw_step.cuh): one contiguous [payload | scales] range per weight-ring slot,
+// so the producer lane fills a slot with one bulk copy.  Source: the
+// GGUF-split Q4_0 planes (payload [rows][nb][16], scales [rows][nb]).
+// Row slabs of RS rows: slab s at byte s*RS*nb*18.
+__global__ void k_pack_rows(const uint8_t* __restrict__ pay, const __half* __restrict__ sc, int rows,
+                            int nb, int RS, uint8_t* __restrict__ out) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;  // (row, block)
     if (i >= (long)rows * nb) return;
     const int r = (int)(i / nb), b = (int)(i - (long)r * nb);
-    reinterpret_cast<uint4*>(opay)[(size_t)b * rows + r] = reinterpret_cast<const uint4*>(pay)[i];
-    osc[(size_t)b * rows + r] = sc[i];
+    const int s = r / RS, ri = r - s * RS, srows = min(RS, rows - s * RS);
+    uint8_t* base = out + (size_t)s * RS * nb * 18;
+    reinterpret_cast<uint4*>(base)[(size_t)ri * nb + b] = reinterpret_cast<const uint4*>(pay)[i];
+    reinterpret_cast<__half*>(base + (size_t)srows * nb * 16)[(size_t)ri * nb + b] = sc[i];
+}
+// Column groups of G blocks over CH-row slabs: group g, slab c at byte
+// (g*rows + c*CH)*G*18, payload [block][row] then scales [block][row].
+__global__ void k_pack_cols(const uint8_t* __restrict__ pay, const __half* __restrict__ sc, int rows,
+                            int nb, int G, int CH, uint8_t* __restrict__ out) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;  // (row, column block)
+    if (i >= (long)rows * nb) return;
+    const int r = (int)(i / nb), cb = (int)(i - (long)r * nb);
+    const int g = cb / G, k = cb - g * G;
+    const int c = r / CH, ri = r - c * CH, crows = min(CH, rows - c * CH);
+    uint8_t* base = out + ((size_t)g * rows + (size_t)c * CH) * G * 18;
+    reinterpret_cast<uint4*>(base)[(size_t)k * crows + ri] = reinterpret_cast<const uint4*>(pay)[i];
+    reinterpret_cast<__half*>(base + (size_t)G * crows * 16)[(size_t)k * crows + ri] = sc[i];
 }
 
-// Column-block-major copy of a packed Q4_0 matrix (k_colmajor), owned by the model.
-static int colmajor_copy(cw_model* m, const QW& w, QW* out) {
+// One packed copy of w (rows x in_f Q4_0), owned by the model.  cols: column
+// groups of G blocks over CH-row slabs, else row slabs of RS rows.
+static int pack_copy(cw_model* m, const QW& w, bool cols, int RS, int G, int CH,
+                     const uint8_t** out) {
     cw_ctx* ctx = m->ctx;
-    const int rows = w.rows, nb = w.in_f / 32;
-    const size_t pb = (size_t)rows * nb * 16, sb = (size_t)rows * nb * 2;
-    const size_t soff = (pb + 255) / 256 * 256;
+    const int nb = w.in_f / 32;
     cw_buf b;
     BufEntry* e;
-    CW_TRY(buf_new(ctx, soff + sb, BUF_PERSISTENT, &b, &e));
+    CW_TRY(buf_new(ctx, (size_t)w.rows * nb * 18, BUF_PERSISTENT, &b, &e));
     m->owned.push_back(b);
-    out->payload = reinterpret_cast<const uint8_t*>(e->ptr);
-    out->scales = reinterpret_cast<const __half*>(reinterpret_cast<char*>(e->ptr) + soff);
-    out->rows = rows;
-    out->in_f = w.in_f;
-    out->buf = b;
-    const long n = (long)rows * nb;
-    k_colmajor<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
-        w.payload, w.scales, rows, nb, const_cast<uint8_t*>(out->payload),
-        const_cast<__half*>(out->scales));
+    uint8_t* dst = reinterpret_cast<uint8_t*>(e->ptr);
+    const long n = (long)w.rows * nb;
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    if (cols)
+        k_pack_cols<<<blocks, 256, 0, ctx->stream>>>(w.payload, w.scales, w.rows, nb, G, CH, dst);
+    else
+        k_pack_rows<<<blocks, 256, 0, ctx->stream>>>(w.payload, w.scales, w.rows, nb, RS, dst);
     CW_CUDA(cudaGetLastError());
+    *out = dst;
     return CW_OK;
 }
 
-// Down projections (FFN stage) and O projections (O-projection stage) in
-// column-block-major order, built once per model.
-static int build_colmajor(cw_model* m) {
-    if (!m->down_cm.empty()) return CW_OK;
-    std::vector<QW> down, wo;
+// The step's packed matrices for one slot geometry: rows per copy of the QKV
+// stage (rs_qkv), the LM head (rs_head) and the FFN gate/up (rs_gu); the O
+// projection's column blocks per slot (ocpb) and rows per unit (orc).  Built
+// once per model; a plan with another geometry rebuilds them (the previous
+// copies stay owned by the model).
+static int build_packed(cw_model* m, int rs_qkv, int rs_head, int rs_gu, int ocpb, int orc) {
+    const long long key = (((((long long)rs_qkv * 4096 + rs_head) * 4096 + rs_gu) * 64 + ocpb) * 4096) + orc;
+    if (m->pk_key == key) return CW_OK;
+    std::vector<const uint8_t*> qkv, gu, down, wo;
     for (const Layer& l : m->L) {
-        QW d, o;
-        CW_TRY(colmajor_copy(m, l.down, &d));
-        CW_TRY(colmajor_copy(m, l.wo, &o));
-        down.push_back(d);
-        wo.push_back(o);
+        const uint8_t *a, *b, *c, *d;
+        CW_TRY(pack_copy(m, l.qkv, false, rs_qkv, 1, 1, &a));
+        CW_TRY(pack_copy(m, l.gate_up, false, rs_gu, 1, 1, &b));
+        CW_TRY(pack_copy(m, l.down, true, 1, 1, MK_DOWN_ROWS, &c));
+        CW_TRY(pack_copy(m, l.wo, true, 1, ocpb, orc, &d));
+        qkv.push_back(a);
+        gu.push_back(b);
+        down.push_back(c);
+        wo.push_back(d);
     }
+    const uint8_t* head = nullptr;
+    CW_TRY(pack_copy(m, m->head, false, rs_head, 1, 1, &head));
     CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
-    m->down_cm.swap(down);
-    m->wo_cm.swap(wo);
+    m->pk_qkv.swap(qkv);
+    m->pk_gu.swap(gu);
+    m->pk_down.swap(down);
+    m->pk_wo.swap(wo);
+    m->pk_head = head;
+    m->pk_key = key;
     return CW_OK;
 }
 
@@ -177,7 +209,23 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     float* H[2] = {s->hid2, s->hid2 + dim};
     std::vector<MStage> st;
     std::vector<MIssue> is;
-    auto gemv = [&](const char* name, const QW& w, int pro, int epi, float* fold_to, int layer,
+    // GEMV stage config: two slots per chunk where a CTA would otherwise take
+    // several chunks (always for the LM head: one head variant per kernel)
+    auto gemv_cfg = [&](const QW& w, int epi) {
+        int cfg = mk_cfg_for(w.in_f);
+        if ((w.rows + mk_rc(cfg) - 1) / mk_rc(cfg) > grid || epi == EPI_HEAD) cfg += MK_NCFG;
+        return cfg;
+    };
+    const int nbh = (int)I.head_dim / 32;          // column blocks per query head
+    const int orc = ocol_rows(I, grid);            // rows per O-projection unit
+    const int ocpb = std::min(nbh, MK_DOWN_ROWS / orc);  // column blocks per ring slot
+    {
+        const int cq = gemv_cfg(m->L[0].qkv, EPI_STORE), ch = gemv_cfg(m->head, EPI_HEAD);
+        const int cg = mk_cfg_for(m->L[0].gate_up.in_f) + MK_NCFG;
+        CW_TRY(build_packed(m, mk_rc(cq) / mk_ns(cq), mk_rc(ch) / 2, mk_rc(cg) / 2, ocpb, orc));
+    }
+    auto gemv = [&](const char* name, const QW& w, const uint8_t* pk, int pro, int epi,
+                    float* fold_to, int layer,
                     const float* base, const float* norm_w, float* y, const float* bias,
                     float* xn_out, int acc_in, long long* r1, long long* r2, const float* pa,
                     const float* pf) {
@@ -189,18 +237,13 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         S.post_a = pa;
         S.post_f = pf;
         S.kind = SK_GEMV;
-        S.cfg = mk_cfg_for(w.in_f);
-        // two slots per chunk where a CTA would otherwise take several chunks
-        // (always for the LM head: one head variant per kernel)
-        if ((w.rows + mk_rc(S.cfg) - 1) / mk_rc(S.cfg) > grid || epi == EPI_HEAD) S.cfg += MK_NCFG;
+        S.cfg = gemv_cfg(w, epi);
         S.pro = pro;
         S.epi = epi;
         S.K = w.in_f;
         S.N = w.rows;
         S.RC = mk_rc(S.cfg);
         S.nchunks = (S.N + S.RC - 1) / S.RC;
-        S.payload = w.payload;
-        S.scales = w.scales;
         S.fold_to = fold_to;
         S.layer = layer;
         S.base = base;
@@ -211,8 +254,7 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         st.push_back(S);
         MIssue Is = {};
         Is.kind = SK_GEMV;
-        Is.pay0 = S.payload;
-        Is.sc0 = S.scales;
+        Is.pk0 = pk;
         Is.n0 = S.nchunks;
         Is.rc = S.RC / mk_ns(S.cfg);
         Is.per0 = mk_ns(S.cfg);
@@ -220,9 +262,6 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         Is.n = S.N;
         is.push_back(Is);
     };
-    const int nbh = (int)I.head_dim / 32;          // column blocks per query head
-    const int orc = ocol_rows(I, grid);            // rows per O-projection unit
-    const int ocpb = std::min(nbh, MK_DOWN_ROWS / orc);  // column blocks per ring slot
     const bool post = I.post_norms != 0;
     // window of layer li: Gemma-2 alternates sliding-window (even) and global layers
     auto window_of = [&](int li) {
@@ -234,7 +273,7 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         const int p = li % 2, q = 1 - p;
         float* kc = s->kc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
         float* vc = s->vc + (size_t)li * I.n_kv * s->max_seq * I.head_dim;
-        gemv("attn_in", l.qkv, PRO_NORM, EPI_STORE, H[q], li, li == 0 ? nullptr : H[p],
+        gemv("attn_in", l.qkv, m->pk_qkv[li], PRO_NORM, EPI_STORE, H[q], li, li == 0 ? nullptr : H[p],
              l.attn_norm, s->qkv, l.qkv_bias, nullptr, li == 0 ? 0 : 2, Y[q], Z[q],
              post && lprev ? lprev->post_attn : nullptr, post && lprev ? lprev->post_ffw : nullptr);
         V->names.push_back("attention");
@@ -252,7 +291,6 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         It.kind = SK_ATTN;
         is.push_back(It);
         V->names.push_back("o_proj");
-        const QW& ocm = m->wo_cm[li];
         MStage O = {};
         O.kind = SK_OCOL;
         O.nobar = 1;
@@ -264,14 +302,11 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         O.nunits = (int)I.n_heads * ((dim + orc - 1) / orc);
         O.per1 = ocpb;
         O.per0 = nbh / ocpb;
-        O.payload2 = ocm.payload;
-        O.scales2 = ocm.scales;
         O.acc_out = Y[p];
         st.push_back(O);
         MIssue Io = {};
         Io.kind = SK_OCOL;
-        Io.pay1 = ocm.payload;
-        Io.sc1 = ocm.scales;
+        Io.pk1 = m->pk_wo[li];
         Io.n0 = O.nunits;
         Io.rc = orc;
         Io.nb = nbh;
@@ -280,7 +315,6 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         Io.dim = dim;
         is.push_back(Io);
         V->names.push_back("ffn");
-        const QW& dcm = m->down_cm[li];
         MStage F = {};
         F.kind = SK_FFN;
         F.cfg = mk_cfg_for(l.gate_up.in_f) + MK_NCFG;
@@ -298,20 +332,14 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         F.post_a = post ? l.post_attn : nullptr;
         F.zero_a = li == 0 ? nullptr : Y[q];
         F.zero_b = li == 0 ? nullptr : Z[q];
-        F.payload = l.gate_up.payload;
-        F.scales = l.gate_up.scales;
-        F.payload2 = dcm.payload;
-        F.scales2 = dcm.scales;
         F.base = H[q];
         F.norm_w = l.ffn_norm;
         F.acc_out = Z[p];
         st.push_back(F);
         MIssue If = {};
         If.kind = SK_FFN;
-        If.pay0 = F.payload;
-        If.sc0 = F.scales;
-        If.pay1 = F.payload2;
-        If.sc1 = F.scales2;
+        If.pk0 = m->pk_gu[li];
+        If.pk1 = m->pk_down[li];
         If.n0 = F.nunits;
         If.rc = F.RC / mk_ns(F.cfg);
         If.nb = F.K / 32;
@@ -322,7 +350,7 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
         is.push_back(If);
     }
     const int lp = (L - 1) % 2;
-    gemv("lm_head", m->head, PRO_NORM, EPI_HEAD, nullptr, L, H[L % 2], m->final_norm, s->logits,
+    gemv("lm_head", m->head, m->pk_head, PRO_NORM, EPI_HEAD, nullptr, L, H[L % 2], m->final_norm, s->logits,
          nullptr, s->xnorm, 2, Y[lp], Z[lp], post ? m->L[L - 1].post_attn : nullptr,
          post ? m->L[L - 1].post_ffw : nullptr);
     V->n_stages = (int)st.size();
@@ -397,7 +425,6 @@ int step_plan_create(cw_session* s) {
     P->kern = find_kernel(I);
     const int grid = ctx->sm_count;
     const int n_splits = std::max(1, std::min(s->n_splits, grid / (int)I.n_kv));
-    CW_TRY(build_colmajor(m));
     const size_t work = work_bytes_for(I, n_splits);
     CW_TRY(build_variant(s, grid, n_splits, work, &P->v[0], &P->smem));
     cudaFuncAttributes fa{};
@@ -500,7 +527,7 @@ int step_profile(cw_session* s, size_t n_steps,
         auto& a = (*agg)["decode_step"];
         a.first += 1;
         a.second += ms;
-        unsigned long long prev_end = 0;
+        unsigned long long prev_end = 0, layer_t0 = 0;
         const StepVariant& V = P->v[vsel];
         for (int si = 0; si < V.n_stages; si++) {
             unsigned long long t0 = ~0ull, t1 = 0;
@@ -567,13 +594,24 @@ int step_profile(cw_session* s, size_t n_steps,
                 r.first += 1;
                 r.second += c3[k] / n3 / (double)ctx->clock_khz;
             }
-            if (si > 0) {
+            // stages opened by a grid barrier: the gap since the previous
+            // stage's end (the attention and O-projection stages overlap the
+            // stage before them and have none)
+            if (si > 0 && t0 >= prev_end) {
                 auto& g = (*agg)["grid_barrier"];
                 g.first += 1;
                 g.second += (double)(t0 - prev_end) * 1e-6;
                 auto& gs = (*agg)[std::string("barrier>") + V.names[si]];  // by the stage it opens
                 gs.first += 1;
                 gs.second += (double)(t0 - prev_end) * 1e-6;
+            }
+            // the layer's timeline: each stage's first start and last end
+            // from the first start of the layer's QKV stage
+            if (!strcmp(V.names[si], "attn_in") || !strcmp(V.names[si], "lm_head")) layer_t0 = t0;
+            for (int k = 0; k < 2; k++) {
+                auto& r = (*agg)[std::string(V.names[si]) + (k ? "@end" : "@start")];
+                r.first += 1;
+                r.second += (double)((k ? t1 : t0) - layer_t0) * 1e-6;
             }
             prev_end = t1;
         }

@@ -151,10 +151,6 @@ struct MStage {
     const float* post_a;      // PRO_NORM: post-attention norm gains of racc (or null)
     const float* post_f;      // PRO_NORM: post-FFN norm gains of racc2 (or null)
     const void* pad_ptr;
-    const uint8_t* payload2;  // FFN: down projection, OCOL: O projection, column-block-major
-    const __half* scales2;    //      [K/32][rows][16] + scales [K/32][rows]
-    const uint8_t* payload;
-    const __half* scales;
     float* fold_to;        // QKV stage: this CTA's slice of the residual is stored here
     const float* base;     // PRO_NORM input (null: this CTA's embedding row)
     const float* norm_w;
@@ -172,17 +168,25 @@ static_assert(MK_DOWN_ROWS % MK_THREADS == 0, "whole rows per thread in one-bloc
 static_assert(MK_SLOTS >= 4, "a head's O-projection column blocks (head_dim <= 128) fit the ring");
 
 // The weight-copy schedule of one stage (nchunks 0: no weights), kept in
-// shared memory so the copy issuer never waits on a global read.
+// shared memory so the copy issuer never waits on a global read.  The
+// matrices are the slot-packed copies the host builds for the step
+// (cw_step.cu, k_pack_rows / k_pack_cols): every ring slot is filled by ONE
+// bulk copy of a contiguous [payload | scales] range.
+//   row slabs (pk0: GEMV weight, FFN gate/up): rows [s*rc, +rc) at byte
+//     s*rc*nb*18, their payload (row-major, nb blocks of 16 B) then scales
+//   column groups (pk1: FFN down with per1 == 1 column block per slot and
+//     1024-row slabs; O projection with per1 column blocks per slot and
+//     rc-row units): blocks [g*G, +G) over rows [r0, +rows) at byte
+//     (g*dim + r0)*G*18, payload [block][row] then scales [block][row]
 struct MIssue {
-    const uint8_t* pay0;  // GEMV weight, or the FFN gate/up matrix
-    const __half* sc0;
-    const uint8_t* pay1;  // FFN: down projection, column-block-major
-    const __half* sc1;
-    int n0;               // GEMV: chunks; FFN: units (act blocks)
-    int rc, nb, n;        // rows per copy (ring slot), blocks per row, rows of pay0
+    const uint8_t* pk0;   // GEMV weight, or the FFN gate/up matrix (row slabs)
+    const uint8_t* pk1;   // FFN down / O projection (column groups)
+    int n0;               // GEMV: chunks; FFN: units (act blocks); OCOL: units
+    int rc, nb, n;        // rows per copy (ring slot), blocks per row, rows of pk0
     int per0, per1;       // GEMV: slots per chunk; FFN: gate/up copies and down slots per unit
-    int dim;              // FFN: rows of the down projection
+    int dim;              // FFN / OCOL: rows of pk1
     int kind;
+    int pad[4];
 };
 static_assert(sizeof(MIssue) == 64, "issue entries are copied as four int4");
 
@@ -250,7 +254,7 @@ struct MShared {
     uint64_t full[MK_SLOTS];   // a slot's copy has landed
     uint64_t empty[MK_SLOTS];  // the compute warps are done with a slot
     uint64_t pol;  // L2 evict-first policy of the weight stream
-    int it_stage, it_t, it_j, issued, abort, last, prod_done;
+    int issued, abort, last, prod_done;
     __align__(16) float act[32];  // FFN: the act block of the current unit
     __align__(16) uint4 aq[6];    // FFN: its q24 planes
     int acb;
@@ -322,92 +326,83 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
     return v;
 }
 
-// Thread 0: issue the copy of this CTA's next weight chunk (in the stage
-// order) into the next ring slot.  Returns false when the step has no more.
-__device__ __forceinline__ void mk_issue_copy(MShared* sh, unsigned char* ring, const uint8_t* pay,
-                                              const __half* sc, unsigned pb, unsigned sb) {
+// The producer lane: fill the next ring slot with `bytes` (a multiple of 16)
+// from the contiguous packed range at src, in one bulk copy.
+__device__ __forceinline__ void mk_issue_copy(MShared* sh, unsigned char* ring, const uint8_t* src,
+                                              unsigned bytes) {
     const int slot = sh->issued % MK_SLOTS;
     unsigned char* dst = ring + (size_t)slot * MK_SLOT_BYTES;
     // the slot's previous contents were read before the compute warps'
     // release of it (its "empty" mbarrier, which the producer waited on): a
     // generic-proxy read followed by an async-proxy write, ordered by that
     // mbarrier, no proxy fence
-    mbar_expect_tx(&sh->full[slot], pb + sb);  // pb == 0: a plain arrive (rows past the end)
-    if (pb) {
-        bulk_g2s_hint(dst, pay, pb, &sh->full[slot], sh->pol);
-        bulk_g2s_hint(dst + MK_SLOT_PAY, sc, sb, &sh->full[slot], sh->pol);
-    }
+    mbar_expect_tx(&sh->full[slot], bytes);  // 0: a plain arrive (rows past the end)
+    if (bytes) bulk_g2s_hint(dst, src, bytes, &sh->full[slot], sh->pol);
     sh->issued++;
 }
 
-// Out of line: one thread runs it once per weight chunk, and its single copy
-// keeps the stages' instruction streams short.
-static __device__ __noinline__ bool mk_issue_next_impl(MShared* sh, const MIssue* iss, unsigned char* ring,
-                                                int n_stages) {
-    while (sh->it_stage < n_stages) {
-        const MIssue& I = iss[sh->it_stage];
-        const long u = blockIdx.x + (long)sh->it_t * gridDim.x;
-        if (I.kind == SK_GEMV) {  // copy it_t: part it_t % per0 of this CTA's chunk it_t / per0
-            const long ch = blockIdx.x + (long)(sh->it_t / I.per0) * gridDim.x;
+// A position in this CTA's sequence of weight copies (the stage order of
+// the issue table).
+struct MIter {
+    int stage, t, j;
+};
+
+// The copy after position it (its packed source range; bytes 0: rows past
+// the end of a matrix, an empty slot) and advance it.  False when the step
+// has no more copies.  Out of line: only the producer lane runs it.
+static __device__ __noinline__ bool mk_next_copy(const MIssue* iss, int n_stages, MIter& it,
+                                                 const uint8_t** src, unsigned* bytes) {
+    while (it.stage < n_stages) {
+        const MIssue& I = iss[it.stage];
+        const long u = blockIdx.x + (long)it.t * gridDim.x;
+        if (I.kind == SK_GEMV) {  // copy t: part t % per0 of this CTA's chunk t / per0
+            const long ch = blockIdx.x + (long)(it.t / I.per0) * gridDim.x;
             if (ch < I.n0) {
-                const long row0 = (ch * I.per0 + sh->it_t % I.per0) * I.rc;
+                const long row0 = (ch * I.per0 + it.t % I.per0) * I.rc;
                 const int rows = (int)max(0L, min((long)I.rc, (long)I.n - row0));
-                mk_issue_copy(sh, ring, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
-                              (unsigned)rows * I.nb * 16, (unsigned)rows * I.nb * 2);
-                sh->it_t++;
+                *src = I.pk0 + (size_t)row0 * I.nb * 18;
+                *bytes = (unsigned)rows * I.nb * 18;
+                it.t++;
                 return true;
             }
         }
         if (I.kind == SK_OCOL && u < I.n0) {
-            // unit u = (query head h, rows [r0, r0 + rc)); ring slot it_j of
-            // the unit holds column blocks h*nb + it_j*per1 .. + per1 - 1 of
-            // the column-block-major O projection, per1 copies side by side
+            // unit u = (query head h, rows [r0, r0 + rc)); ring slot j of the
+            // unit holds column group h*per0 + j (column blocks
+            // h*nb + j*per1 .. + per1 - 1) over those rows
             const int nch = (I.dim + I.rc - 1) / I.rc, h = (int)(u / nch);
             const int r0 = (int)(u - (long)h * nch) * I.rc, rows = min(I.rc, I.dim - r0);
-            const int slot = sh->issued % MK_SLOTS;
-            unsigned char* dst = ring + (size_t)slot * MK_SLOT_BYTES;
-            mbar_expect_tx(&sh->full[slot], (unsigned)(I.per1 * rows * 18));
-            for (int i = 0; i < I.per1; i++) {
-                const size_t off = (size_t)(h * I.nb + sh->it_j * I.per1 + i) * I.dim + r0;
-                bulk_g2s_hint(dst + (size_t)i * I.rc * 16, I.pay1 + off * 16, (unsigned)rows * 16,
-                              &sh->full[slot], sh->pol);
-                bulk_g2s_hint(dst + MK_SLOT_PAY + (size_t)i * I.rc * 2, I.sc1 + off,
-                              (unsigned)rows * 2, &sh->full[slot], sh->pol);
-            }
-            sh->issued++;
-            if (++sh->it_j == I.per0) {
-                sh->it_j = 0;
-                sh->it_t++;
+            const size_t g = (size_t)h * I.per0 + it.j;
+            *src = I.pk1 + (g * I.dim + r0) * I.per1 * 18;
+            *bytes = (unsigned)(I.per1 * rows * 18);
+            if (++it.j == I.per0) {
+                it.j = 0;
+                it.t++;
             }
             return true;
         }
         if (I.kind == SK_FFN && u < I.n0) {
-            const int j = sh->it_j;
-            if (j < I.per0) {  // gate/up rows [64u + j*rc, +rc)
-                const long row0 = u * 64 + (long)j * I.rc;
-                mk_issue_copy(sh, ring, I.pay0 + (size_t)row0 * I.nb * 16, I.sc0 + (size_t)row0 * I.nb,
-                              (unsigned)I.rc * I.nb * 16, (unsigned)I.rc * I.nb * 2);
+            if (it.j < I.per0) {  // gate/up rows [64u + j*rc, +rc)
+                const long row0 = u * 64 + (long)it.j * I.rc;
+                *src = I.pk0 + (size_t)row0 * I.nb * 18;
+                *bytes = (unsigned)I.rc * I.nb * 18;
             } else {  // down rows [k*1024, ...) of column block u
-                const int k = j - I.per0, r0 = k * MK_DOWN_ROWS;
+                const int k = it.j - I.per0, r0 = k * MK_DOWN_ROWS;
                 const int rows = min(MK_DOWN_ROWS, I.dim - r0);
-                const size_t off = (size_t)u * I.dim + r0;
-                mk_issue_copy(sh, ring, I.pay1 + off * 16, I.sc1 + off, (unsigned)rows * 16,
-                              (unsigned)rows * 2);
+                *src = I.pk1 + ((size_t)u * I.dim + r0) * 18;
+                *bytes = (unsigned)rows * 18;
             }
-            if (++sh->it_j == I.per0 + I.per1) {
-                sh->it_j = 0;
-                sh->it_t++;
+            if (++it.j == I.per0 + I.per1) {
+                it.j = 0;
+                it.t++;
             }
             return true;
         }
-        sh->it_stage++;
-        sh->it_t = 0;
-        sh->it_j = 0;
+        it.stage++;
+        it.t = 0;
+        it.j = 0;
     }
     return false;
-}
-__device__ __forceinline__ bool mk_issue_next(const MParams& p, MCtx& c) {
-    return mk_issue_next_impl(c.sh, c.iss, c.ring, p.n_stages);
 }
 
 // Compute thread 0, after the CTA barrier that ends the use of ring slots
@@ -427,8 +422,11 @@ __device__ __forceinline__ int ld_volatile_shared_i32(const int* p) {
 // The producer warp's lane 0: queue every weight copy of the step in order,
 // copy q into ring slot q % MK_SLOTS once the compute warps released that
 // slot's previous copy (q - MK_SLOTS).  Stops early when the CTA aborts.
+// (An L2 prefetch of the copies one ring ahead made the step slower: 0.64 ->
+// 0.67 ms/token at Qwen3-0.6B, 2.36 -> 2.76 at Qwen3-8B.)
 __device__ inline void mk_produce(const MParams& p, MCtx& c) {
     MShared* sh = c.sh;
+    MIter it = {0, 0, 0};
     for (int q = 0;; q++) {
         if (q >= MK_SLOTS) {
             uint64_t* e = &sh->empty[q % MK_SLOTS];
@@ -446,7 +444,11 @@ __device__ inline void mk_produce(const MParams& p, MCtx& c) {
             }
             if (!ok) break;
         }
-        if (ld_volatile_shared_i32(&sh->abort) || !mk_issue_next(p, c)) break;
+        const uint8_t* src;
+        unsigned bytes;
+        if (ld_volatile_shared_i32(&sh->abort) || !mk_next_copy(c.iss, p.n_stages, it, &src, &bytes))
+            break;
+        mk_issue_copy(sh, c.ring, src, bytes);
     }
     __threadfence_block();
     *reinterpret_cast<volatile int*>(&sh->prod_done) = 1;
@@ -912,10 +914,12 @@ __device__ __forceinline__ const float* mk_chunk(const MParams& p, MCtx& c, int 
         ok = mbar_wait(&c.sh->full[q % MK_SLOTS], (unsigned)((q / MK_SLOTS) & 1), MK_WAIT_NS) && ok;
     }
     if (first) mk_clk(c, CLK_WAITED);
-    // this warp's rows lie in one slot (RS is a multiple of RPW)
+    // this warp's rows lie in one slot (RS is a multiple of RPW); the slot
+    // holds min(RS, rows - h*RS) rows' payload, then their scales
     const int h = (slot * RPW) / RS;
     const unsigned char* pay = c.ring + (size_t)((c.seq + h) % MK_SLOTS) * MK_SLOT_BYTES;
-    const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+    const int srows = max(0, min(RS, rows - h * RS));
+    const __half* scs = reinterpret_cast<const __half*>(pay + (size_t)srows * nb * 16);
     float* rb = c.rowred + (size_t)(c.nch & 1) * 64;
     uint4 w4[RPW][BPL];
     float dd[RPW][BPL];
@@ -1143,7 +1147,7 @@ __device__ inline bool mk_ffn(const MParams& p, const MStage& S, MCtx& c) {
             const unsigned par = (unsigned)((c.seq / MK_SLOTS) & 1);
             const bool ok = mbar_wait(&sh->full[rs], par, MK_WAIT_NS);  // agreed on below
             const unsigned char* pay = c.ring + (size_t)rs * MK_SLOT_BYTES;
-            const __half* scs = reinterpret_cast<const __half*>(pay + MK_SLOT_PAY);
+            const __half* scs = reinterpret_cast<const __half*>(pay + (size_t)rows * 16);
             for (int r = tid; r < rows; r += MK_THREADS) {
                 const uint4 w4 = reinterpret_cast<const uint4*>(pay)[r];
                 const float d = __half2float(scs[r]);
@@ -1360,9 +1364,10 @@ __device__ inline bool mk_ocol(const MParams& p, const MStage& S, MCtx& c) {
             if (row < rows) {
                 const int sj = k / S.per1, ii = k - sj * S.per1;
                 const unsigned char* pay = c.ring + (size_t)((c.seq + sj) % MK_SLOTS) * MK_SLOT_BYTES;
-                const size_t e = (size_t)ii * S.RC + row;
+                const size_t e = (size_t)ii * rows + row;  // [block][row], then the scales
                 const uint4 w4 = reinterpret_cast<const uint4*>(pay)[e];
-                const float d = __half2float(reinterpret_cast<const __half*>(pay + MK_SLOT_PAY)[e]);
+                const float d = __half2float(
+                    reinterpret_cast<const __half*>(pay + (size_t)S.per1 * rows * 16)[e]);
                 uint4 xa[3], xb[3];
 #pragma unroll
                 for (int pl = 0; pl < 3; pl++) {
@@ -1435,9 +1440,6 @@ __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
             mbar_init(&sh.empty[s], 1);
         }
         fence_mbar_init();
-        sh.it_stage = 0;
-        sh.it_t = 0;
-        sh.it_j = 0;
         sh.issued = 0;
         sh.abort = 0;
         sh.prod_done = 0;

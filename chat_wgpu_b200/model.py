@@ -239,11 +239,12 @@ class Session:
     def profile(self, n_steps: int) -> list[tuple[str, int, float]]:
         """Per-kernel device time of n_steps decode steps (kernel, launches, ms),
         sorted by total descending (cw_session_profile)."""
-        rows = (_lib.ProfileRow * 64)()
+        cap = 128
+        rows = (_lib.ProfileRow * cap)()
         n = C.c_size_t()
-        _lib.call("cw_session_profile", self._h, int(n_steps), rows, 64, C.byref(n))
+        _lib.call("cw_session_profile", self._h, int(n_steps), rows, cap, C.byref(n))
         return [(rows[i].kernel.decode(), int(rows[i].passes), float(rows[i].total_ms))
-                for i in range(min(n.value, 64))]
+                for i in range(min(n.value, cap))]
 
     @property
     def pos(self) -> int:

@@ -6,9 +6,9 @@ WGPU_PROFILE report, src/model/mod.rs:74-88, src/profile.rs:86-117).
 
 Runs the prompt, a few warm-up decode steps, times `--steps` decode steps
 with CUDA events, then prints Session.profile(): for the persistent step,
-per stage the span from its first CTA's start to its last CTA's end and the
-grid-barrier gaps (in-kernel %globaltimer stamps); for the per-stage path,
-CUDA-event time per kernel."""
+per stage the span from its first CTA's start to its last CTA's end, the
+grid-barrier gaps and the layer timeline (in-kernel %globaltimer stamps);
+for the per-stage path, CUDA-event time per kernel."""
 from __future__ import annotations
 
 import argparse
@@ -41,9 +41,14 @@ def main(argv=None) -> None:
     print(f"{a.model}: {ms / a.steps:.4f} ms/step over {a.steps} steps "
           f"({'persistent' if s.persistent else 'per-stage kernels'})")
     rows = s.profile(a.steps)
+    timeline = [r for r in rows if "@" in r[0]]
     print(f"{'stage':28s} {'count':>6s} {'us each':>9s} {'us/step':>9s}")
-    for name, count, total in sorted(rows, key=lambda r: -r[2]):
+    for name, count, total in sorted((r for r in rows if "@" not in r[0]), key=lambda r: -r[2]):
         print(f"{name:28s} {count:6d} {1000 * total / count:9.3f} {1000 * total / a.steps:9.2f}")
+    if timeline:  # persistent step: mean offsets within a layer
+        print("layer timeline (us from the first start of the layer's QKV stage; mean)")
+        for name, count, total in sorted(timeline, key=lambda r: r[2] / r[1]):
+            print(f"  {name:26s} {1000 * total / count:9.3f}")
     s.close()
     m.close()
     ctx.close()
