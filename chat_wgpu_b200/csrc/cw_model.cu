@@ -1535,7 +1535,7 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
         rc = set_error(CW_ERR_OOM, "pinned host allocation failed");
     if (rc == CW_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess)
         rc = set_error(CW_ERR_CUDA, "session setup failed");
-    if (rc == CW_OK && s->use_persistent && step_supported(m, s)) rc = step_plan_create(s);
+    if (rc == CW_OK && s->use_persistent && step_default(m, s)) rc = step_plan_create(s);
     if (rc != CW_OK) {
         std::string msg = cw_last_error();
         cw_session_free(s);

@@ -152,6 +152,10 @@ static size_t work_bytes_for(const cw_model_info& I, int n_splits) {
     return al16(std::max(gemv, attn));
 }
 
+bool step_default(const cw_model* m, const cw_session* s) {
+    return step_supported(m, s) && !m->info.post_norms;
+}
+
 bool step_supported(const cw_model* m, const cw_session* s) {
     const cw_model_info& I = m->info;
     // the two families the step composes: pre-norm SwiGLU (Qwen/Llama), and

@@ -15,7 +15,7 @@ compared up to their first near-tie.
   config 4  Gemma-2-2B shapes (UnitShift norms, GeGLU, soft-caps, sliding
             window, post-norms), 128-token prompt through batched prefill and
             token by token, 32 greedy tokens on the persistent step; 16 on
-            the per-stage kernels
+            the per-stage kernels (its default path)
   config 5  Qwen3-8B, 32-token prompt, 8 greedy tokens; and its layer shapes
             (qwen3-8b-2l) over a 4096-token prompt through batched prefill
             against the token-by-token steps (every K/V cache row, then the
@@ -145,14 +145,15 @@ def test_config4_gemma2_2b(ctx, orc):
     assert m.info["head_dim"] == 256 and m.info["vocab"] == 256000
     from chat_wgpu_b200.model import Session
     probe = Session(m, 8)
-    assert probe.persistent  # the post-norm step variant covers Gemma-2-2B
+    assert not probe.persistent  # per-stage by default for the post-norm family
+    probe.set_persistent(True)   # the post-norm step variant covers Gemma-2-2B
     probe.close()
     prompt = bench_prompt(m.info["vocab"], 128)
-    toks, logits = gpu_stream(m, prompt, 32, prefill=True)
+    toks, logits = gpu_stream(m, prompt, 32, prefill=True, persistent=True)
     om = orc.Model(path)
     ref = forced_logits(om, prompt, toks)
     check_forced(toks, logits, ref, "gemma2 prefill")
-    t2, l2 = gpu_stream(m, prompt, 32, prefill=False)
+    t2, l2 = gpu_stream(m, prompt, 32, prefill=False, persistent=True)
     n = 32
     for i in range(32):
         if t2[i] != toks[i]:
