@@ -60,6 +60,9 @@ def parse():
                     help="decode steps of the per-kernel profile pass (at least 1)")
     ap.add_argument("--no-gemv", action="store_true",
                     help="skip the Q4_0 GEMV shape sweep (the metric's second half)")
+    ap.add_argument("--tp-model", default="qwen3-8b",
+                    help="model of the tensor-parallel record when N > 1 ('' = skip)")
+    ap.add_argument("--tp-steps", type=int, default=64)
     return ap.parse_args()
 
 
@@ -106,6 +109,24 @@ class Dist:
         t = torch.tensor([v], dtype=torch.float64, device=self.device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    def allgather_bytes(self, data: bytes) -> list:
+        """Every rank's bytes, in rank order."""
+        if not self.pg:
+            return [data]
+        import torch.distributed as dist
+        out = [None] * self.world
+        dist.all_gather_object(out, data)
+        return out
+
+    def bcast_bytes(self, data):
+        """Rank 0's bytes on every rank."""
+        if not self.pg:
+            return data
+        import torch.distributed as dist
+        box = [data]
+        dist.broadcast_object_list(box, src=0)
+        return box[0]
 
     def close(self):
         if self.pg:
@@ -359,6 +380,64 @@ def gemv_sweep(ctx, peak_gbs: float) -> list:
     return rows
 
 
+def tp_leg(args, dist, ctx) -> dict:
+    """N > 1: the tensor-parallel record.  The --tp-model GGUF split over the
+    job's N GPUs (cw_model_load_gguf_tp, one rank per GPU), greedy decode on
+    the per-stage step with the O / down all-reduces and the argmax over
+    NVLink peer memory (Session.tp_attach), then over NCCL; ms/token timed
+    with CUDA events on every rank, max over ranks.  Rank 0 then decodes the
+    same prompt with the whole model on its GPU (the persistent step) and
+    counts the leading tokens on which the streams agree."""
+    from chat_wgpu_b200 import gguf
+    from chat_wgpu_b200.model import Model, Session, tp_unique_id
+    name = args.tp_model
+    if dist.rank == 0:
+        gguf.cached_model(name, seed=args.seed)  # written once, before the others read it
+    dist.barrier()
+    path = gguf.cached_model(name, seed=args.seed)
+    uid = dist.bcast_bytes(tp_unique_id() if dist.rank == 0 else None)
+    m = Model(ctx, path, tp=(dist.rank, dist.world, uid))
+    vocab = gguf.CONFIGS[name]["vocab"]
+    P, W, K = 32, 4, args.tp_steps
+    prompt = np.random.default_rng(args.seed + 2).integers(0, vocab, P).astype(np.uint32)
+    out = {"model": name, "tp": dist.world, "steps": K, "warmup": W,
+           "positions": f"{P - 1 + W}..{P - 2 + W + K}"}
+    toks = None
+    for mode in ("p2p", "nccl"):
+        s = Session(m, P + W + K + 2)
+        if mode == "p2p":
+            s.tp_attach_p2p(dist.allgather_bytes)
+        s.begin(prompt)
+        s.run(P - 1 + W)
+        dist.barrier()
+        ms = dist.max(s.run_timed(K))
+        t = s.tokens()
+        dist.barrier()  # every rank done stepping before any frees its exchange area
+        s.close()
+        out[mode] = {"ms_per_token": ms / K, "tok_s": K / (ms / 1e3)}
+        if mode == "p2p":
+            toks = t
+    out["path"] = ("per-stage kernels in a CUDA graph; p2p: each all-reduce one kernel of "
+                   "8-byte value+epoch NVLink peer stores and a rank-order sum (cw_tp_p2p.cu); "
+                   "nccl: ncclAllReduce nodes")
+    m.close()
+    if dist.rank == 0:
+        full = Model(ctx, path)
+        r = Session(full, P + W + K + 2)
+        r.begin(prompt)
+        r.run(P - 1 + W)
+        ms1 = r.run_timed(K)
+        ref = r.tokens()
+        r.close()
+        full.close()
+        out["single_gpu"] = {"ms_per_token": ms1 / K, "path": "persistent step, whole model"}
+        same = np.append(ref == toks, False)
+        out["tokens_agreeing_with_1gpu"] = int(np.argmin(same))
+        out["of"] = int(len(toks))
+    dist.barrier()
+    return out
+
+
 def run_reference(args):
     """--impl reference: the oracle port on all host cores, same config; rank 0
     only (no process group, no device)."""
@@ -595,6 +674,8 @@ def run_cuda(args, dist):
             line["cpu_baseline"]["gemv"] = cpu_gemv_sweep(multi["cores"])
         line["parity"] = parity
     model.close()
+    if dist.world > 1 and args.tp_model:
+        line["tp"] = tp_leg(args, dist, ctx)
     ctx.close()
     if dist.rank == 0:
         print(json.dumps(line), flush=True)

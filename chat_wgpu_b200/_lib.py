@@ -132,6 +132,8 @@ SIGNATURES = {
     "cw_session_set_graph": [_vp, C.c_int],
     "cw_session_set_persistent": [_vp, C.c_int],
     "cw_session_inject_stall": [_vp, C.c_uint32],
+    "cw_session_tp_handle": [_vp, _vp, _sz],
+    "cw_session_tp_attach": [_vp, _vp, _sz],
     "cw_session_persistent": [_vp, C.POINTER(C.c_int)],
     "cw_session_step": [_vp, C.c_uint32, C.POINTER(C.c_uint32)],
     "cw_session_run_timed": [_vp, _sz, C.POINTER(C.c_double)],

@@ -37,6 +37,7 @@
 #include "cw_model.h"
 #include "cw_nccl.h"
 #include "cw_q4.h"
+#include "cw_tp_p2p.h"
 
 namespace cw {
 
@@ -438,8 +439,9 @@ __global__ void __launch_bounds__(256) k_kq_fgemv(FArgs a) {
 
 // mod.rs:114-122: the next input is the next prompt token while the prompt
 // lasts, else the argmax, which is also appended to the output.
+// n_ar: the tensor-parallel peer all-reduces this step ran (cw_tp_p2p.cu).
 __global__ void k_finalize(DevState* st, const unsigned* __restrict__ prompt,
-                           unsigned* __restrict__ toks, int decode) {
+                           unsigned* __restrict__ toks, int decode, unsigned n_ar) {
     pdl_trigger();
     pdl_wait();
     int pos = st->pos;
@@ -455,6 +457,7 @@ __global__ void k_finalize(DevState* st, const unsigned* __restrict__ prompt,
     st->key = argmax_key_init();
     st->token = next;
     st->pos = pos + 1;
+    st->ar_seq += n_ar;
 }
 
 __global__ void k_begin(DevState* st, const unsigned* __restrict__ prompt, int n_prompt,
@@ -1168,6 +1171,7 @@ static int enqueue_step_core(cw_session* s, bool decode) {
     // post-norm families do with their normed branch outputs (no post norm
     // then: post_w stays null).
     const bool tp = m->tp_world > 1;
+    const bool p2p = tp && p2p_on(s);  // NVLink peer all-reduces (cw_tp_p2p.cu), else NCCL
     const bool defer = post || tp;
     const int unit = I.norm_kind == 1;
     // With the context profiler on (direct launches only), every kernel is
@@ -1253,7 +1257,9 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         o.x = s->attn;
         o.y = defer ? s->tmp : s->hidden;
         CW_TRY(defer ? (proj<PRO_X, EPI_STORE>(ctx, l.wo, o)) : (proj<PRO_X, EPI_RESID>(ctx, l.wo, o)));
-        if (tp) CW_TRY(tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
+        if (tp)
+            CW_TRY(p2p ? p2p_allreduce(s, s->tmp, 2 * (int)li)
+                       : tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
         if (!defer) CW_TRY(tap_copy(s, TAP_POST_ATTN, li, s->hidden));
 
         stage("ffn_in");
@@ -1285,7 +1291,9 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         d.x = s->act;
         d.y = defer ? s->tmp : s->hidden;
         CW_TRY(defer ? (proj<PRO_X, EPI_STORE>(ctx, l.down, d)) : (proj<PRO_X, EPI_RESID>(ctx, l.down, d)));
-        if (tp) CW_TRY(tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
+        if (tp)
+            CW_TRY(p2p ? p2p_allreduce(s, s->tmp, 2 * (int)li + 1)
+                       : tp_sum_f32(m->nccl, s->tmp, I.dim, ctx->stream));
         if (!defer) {
             CW_TRY(tap_copy(s, TAP_LAYER_OUT, li, s->hidden));
         } else if (const Tap* tp = find_tap(s, TAP_LAYER_OUT, li)) {
@@ -1319,11 +1327,11 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         h.key = &s->st->key;
         CW_TRY((proj<PRO_NORM, EPI_HEAD>(ctx, m->head, h)));
         // the best (logit, index) key over the vocabulary shards
-        if (tp) CW_TRY(tp_max_u64(m->nccl, &s->st->key, 1, ctx->stream));
+        if (tp) CW_TRY(p2p ? p2p_key(s) : tp_max_u64(m->nccl, &s->st->key, 1, ctx->stream));
     }
     stage("finalize");
     CW_TRY(launch_k(ctx, k_finalize, dim3(1), dim3(1), 0, s->st, (const unsigned*)s->prompt,
-                    s->toks, decode ? 1 : 0));
+                    s->toks, decode ? 1 : 0, p2p ? 2u * I.n_layers : 0u));
     sc.reset();
     return check_launch("finalize");
 }
@@ -1551,6 +1559,7 @@ int cw_session_free(cw_session* s) {
     cudaStreamSynchronize(s->ctx->stream);
     destroy_graphs(s);
     step_plan_free(s);
+    p2p_free(s);
     for (cw_buf b : s->owned) {
         auto it = s->ctx->bufs.find(b);
         if (it != s->ctx->bufs.end()) {
@@ -1590,6 +1599,25 @@ int cw_session_set_persistent(cw_session* s, int on) {
         CW_TRY(step_plan_create(s));
     }
     return CW_OK;
+}
+
+int cw_session_tp_handle(cw_session* s, uint8_t* out, size_t n) {
+    clear_error();
+    CW_CHECK(s && out && n >= CW_TP_HANDLE_BYTES, CW_ERR_INVALID_ARG,
+             "cw_session_tp_handle: bad arguments");
+    cudaSetDevice(s->ctx->device);
+    return p2p_handle(s, out);
+}
+
+int cw_session_tp_attach(cw_session* s, const uint8_t* handles, size_t n) {
+    clear_error();
+    CW_CHECK(s && handles, CW_ERR_INVALID_ARG, "cw_session_tp_attach: bad arguments");
+    CW_CHECK(n >= (size_t)s->m->tp_world * CW_TP_HANDLE_BYTES, CW_ERR_INVALID_ARG,
+             "cw_session_tp_attach: %zu bytes for %d ranks", n, s->m->tp_world);
+    cudaSetDevice(s->ctx->device);
+    CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
+    destroy_graphs(s);  // captured steps hold the NCCL all-reduces
+    return p2p_attach(s, handles);
 }
 
 int cw_session_inject_stall(cw_session* s, uint32_t wait_us) {

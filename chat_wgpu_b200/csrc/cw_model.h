@@ -26,7 +26,9 @@ struct DevState {
     unsigned stall_us;       // fault injection (cw_session_inject_stall): 0 = off
     unsigned long long ctr_base;  // persistent step's head counter at the start of the step
     unsigned stopped;             // an EOS token ended the sequence (cw_sample.cu)
-    unsigned pad2;
+    unsigned ar_seq;   // tensor-parallel peer all-reduces completed (cw_tp_p2p.cu)
+    unsigned key_seq;  // tensor-parallel argmax-key exchanges completed
+    unsigned pad3;
 };
 
 struct QW {  // packed Q4_0 weight (type 2), or raw GGUF Q6_K blocks (type 14)
@@ -130,6 +132,10 @@ struct cw_session {
     bool stopped = false;     // host view of DevState::stopped
     std::vector<cw::Tap> taps;  // active hook taps (force the per-stage step kernels)
     float* qtap = nullptr;      // the step's normed, rotated q (source of "q" taps)
+    // tensor parallelism over NVLink peer memory (cw_tp_p2p.cu): the all-
+    // reduces of the per-stage step once cw_session_tp_attach mapped every
+    // rank's exchange area (cw::TpP2P; null: NCCL)
+    void* p2p = nullptr;
 };
 
 namespace cw {

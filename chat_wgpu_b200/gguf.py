@@ -209,6 +209,9 @@ CONFIGS = {
     "tiny-gemma2": dict(arch="gemma2", dim=256, n_layers=3, n_heads=4, n_kv=2, head_dim=64,
                         hidden=512, vocab=512, eps=1e-6, theta=1e4, tied=True, window=6,
                         attn_softcap=2.0, final_softcap=3.0),
+    # eight kv heads and 64 FFN column blocks: splits 2, 4 and 8 ways (TP tests)
+    "tp8-qwen3": dict(arch="qwen3", dim=512, n_layers=3, n_heads=16, n_kv=8, head_dim=64,
+                      hidden=2048, vocab=2048, eps=1e-6, theta=1e6, tied=True),
     "tiny-qwen2": dict(arch="qwen2", dim=256, n_layers=2, n_heads=8, n_kv=2, head_dim=32,
                        hidden=768, vocab=300, eps=1e-6, theta=1e6, tied=False, bias=True),
     # more FFN column blocks (hidden / 32 = 192) than a B200 has SMs: CTAs of the

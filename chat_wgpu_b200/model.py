@@ -24,6 +24,7 @@ from .kernels import activation, argmax, attention, norm, q4, rope
 
 
 TP_ID_BYTES = 128
+TP_HANDLE_BYTES = 128  # CW_TP_HANDLE_BYTES
 
 
 def tp_unique_id() -> bytes:
@@ -245,6 +246,27 @@ class Session:
         _lib.call("cw_session_profile", self._h, int(n_steps), rows, cap, C.byref(n))
         return [(rows[i].kernel.decode(), int(rows[i].passes), float(rows[i].total_ms))
                 for i in range(min(n.value, cap))]
+
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-area handle for the peer all-reduces
+        (cw_session_tp_handle); every rank's goes to every rank's tp_attach."""
+        buf = C.create_string_buffer(TP_HANDLE_BYTES)
+        _lib.call("cw_session_tp_handle", self._h, C.cast(buf, C.c_void_p), TP_HANDLE_BYTES)
+        return buf.raw
+
+    def tp_attach(self, handles: "list[bytes]") -> None:
+        """Map every rank's exchange area (handles in rank order): the step's
+        all-reduces then run over NVLink peer memory instead of NCCL
+        (cw_session_tp_attach)."""
+        blob = b"".join(handles)
+        buf = C.create_string_buffer(blob, len(blob))
+        _lib.call("cw_session_tp_attach", self._h, C.cast(buf, C.c_void_p), len(blob))
+
+    def tp_attach_p2p(self, allgather) -> None:
+        """tp_handle + tp_attach with a host exchange: allgather(bytes) returns
+        every rank's bytes in rank order (e.g. torch.distributed
+        all_gather_object); the ranks are synchronised by it."""
+        self.tp_attach(list(allgather(self.tp_handle())))
 
     @property
     def pos(self) -> int:

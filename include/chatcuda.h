@@ -301,6 +301,22 @@ int cw_model_load_gguf_tp(cw_ctx* ctx, const char* path, int rank, int world, co
                           cw_model** out);
 int cw_model_tp_info(cw_model* model, int* rank, int* world, uint32_t* vocab_offset,
                      uint32_t* vocab_local);
+/* The per-stage step's all-reduces over NVLink peer memory instead of NCCL
+ * (the O and down partial sums, the argmax key).  Every rank of a session
+ * calls cw_session_tp_handle (its exchange area's CUDA IPC handle and its GPU,
+ * CW_TP_HANDLE_BYTES), the host hands all of them, in rank order, to every
+ * rank's cw_session_tp_attach, which maps the peers' areas.  From then on each
+ * all-reduce is one kernel: every element of the partial goes to every peer
+ * as one 8-byte NVLink store carrying value and exchange epoch together, each
+ * rank waits (bounded: CW_ERR_TIMEOUT after 2 s) for the words of the current
+ * epoch and sums them in rank order, identically on every rank.  Ranks must be
+ * on distinct GPUs (CW_ERR_UNSUPPORTED otherwise); every rank attaches before
+ * its next step and frees its session only after every rank has finished
+ * its last step (the host synchronises the ranks). */
+#define CW_TP_MAX_WORLD 8
+#define CW_TP_HANDLE_BYTES 128
+int cw_session_tp_handle(cw_session* s, uint8_t* out, size_t n);
+int cw_session_tp_attach(cw_session* s, const uint8_t* handles, size_t n);
 
 /* A decode session = Model::new_cache (qwen3.rs:115) + the per-token state of
  * generate (mod.rs:57-125).  max_seq bounds prompt + generated tokens. */

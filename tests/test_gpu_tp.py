@@ -1,6 +1,7 @@
-"""Tensor-parallel decode over 2 GPUs (cw_model_load_gguf_tp): two processes,
-one per GPU, each holding half of the heads, FFN columns and LM-head rows,
-with the O / down partial sums and the argmax all-reduced over NCCL.  The
+"""Tensor-parallel decode over 2, 4 and 8 GPUs (cw_model_load_gguf_tp): one
+process per GPU, each holding 1/world of the heads, FFN columns and LM-head
+rows, with the O / down partial sums and the argmax all-reduced over NCCL or
+over NVLink peer memory (Session.tp_attach).  The
 greedy stream must match the single-GPU stream and the oracle (same gates as
 test_gpu_model: tokens until the first ambiguous step, logits within 1e-3
 relative), the ranks must agree on every token, a stop token must end every rank's
@@ -19,7 +20,7 @@ from test_gpu_model import REL, compare_streams, session_stream
 pytestmark = pytest.mark.gpu
 
 WORKER = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tp_worker.py")
-NAMES = ["small-qwen3", "tiny-qwen2", "tiny-gemma2", "small-qwen3-q6k"]
+NAMES = ["small-qwen3", "tiny-qwen2", "tiny-gemma2", "small-qwen3-q6k", "tp8-qwen3"]
 
 
 def n_gpus():
@@ -34,13 +35,18 @@ def tp_models(tmp_path_factory):
     return {n: gguf.synth_model(str(d / f"{n}.gguf"), gguf.CONFIGS[n], seed=13) for n in NAMES}
 
 
-def run_ranks(path, prompt, n_new, world, out_dir):
+def run_ranks(path, prompt, n_new, world, out_dir, p2p=False):
     from chat_wgpu_b200.model import tp_unique_id
     uid = tp_unique_id().hex()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     outs = [os.path.join(out_dir, f"rank{r}.npz") for r in range(world)]
+    extra = []
+    if p2p:
+        d = os.path.join(out_dir, "p2p")
+        os.makedirs(d, exist_ok=True)
+        extra = [d]
     procs = [subprocess.Popen([sys.executable, WORKER, str(r), str(world), path, uid,
-                               ",".join(str(int(t)) for t in prompt), str(n_new), outs[r]],
+                               ",".join(str(int(t)) for t in prompt), str(n_new), outs[r]] + extra,
                               env=env)
              for r in range(world)]
     try:
@@ -55,18 +61,27 @@ def run_ranks(path, prompt, n_new, world, out_dir):
     return [dict(np.load(o)) for o in outs]
 
 
+@pytest.mark.parametrize("mode", ["nccl", "p2p"])
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("name", NAMES)
-def test_tp2_matches_single_gpu_and_oracle(ctx, orc, tp_models, name, tmp_path):
-    if n_gpus() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_tp_matches_single_gpu_and_oracle(ctx, orc, tp_models, name, world, mode, tmp_path):
+    """TP = world over NCCL or over NVLink peer memory (Session.tp_attach)."""
+    if n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from chat_wgpu_b200 import gguf
+    cfg = gguf.CONFIGS[name]
+    if (cfg["n_kv"] % world or cfg["hidden"] % (32 * world) or cfg["vocab"] % world
+            or (cfg["n_heads"] * cfg["head_dim"]) % (32 * world)):
+        pytest.skip(f"{name} does not split {world} ways")
     from chat_wgpu_b200.model import Model
     path = tp_models[name]
     om = orc.Model(path)
     prompt = (np.array([3, 17, 5, 9, 250, 1, 77, 12, 40], np.uint32) % om.vocab).astype(np.uint32)
     n_new = 16
-    ranks = run_ranks(path, prompt, n_new, 2, str(tmp_path))
+    ranks = run_ranks(path, prompt, n_new, world, str(tmp_path), p2p=mode == "p2p")
     # every rank produced the same tokens; the logits slices tile the vocabulary
-    assert np.array_equal(ranks[0]["toks"], ranks[1]["toks"])
+    for r in ranks[1:]:
+        assert np.array_equal(ranks[0]["toks"], r["toks"])
     # with the 4th token as a stop token, the stream ends before its first occurrence
     first = int(np.argmax(ranks[0]["toks"] == ranks[0]["toks"][3]))
     for r in ranks:

@@ -2,14 +2,39 @@
 test_gpu_tp.py: loads its shard of the GGUF model on GPU `rank`, decodes
 greedily and saves its tokens and its slice of every step's logits.
 
-usage: tp_worker.py RANK WORLD MODEL ID_HEX PROMPT(comma-separated) N_NEW OUT.npz
+usage: tp_worker.py RANK WORLD MODEL ID_HEX PROMPT(comma-separated) N_NEW OUT.npz [P2P_DIR]
+
+With P2P_DIR, the sessions' all-reduces run over NVLink peer memory
+(Session.tp_attach); the ranks swap their handles as files in P2P_DIR.
 """
 import os
 import sys
+import time
 
 import numpy as np
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def file_allgather(d, tag, rank, world, timeout=120.0):
+    """allgather(bytes) over files in d: write this rank's, wait for all."""
+    def gather(data):
+        tmp = os.path.join(d, f"{tag}.{rank}.tmp")
+        with open(tmp, "wb") as f:
+            f.write(data)
+        os.replace(tmp, os.path.join(d, f"{tag}.{rank}.bin"))
+        names = [os.path.join(d, f"{tag}.{r}.bin") for r in range(world)]
+        t0 = time.monotonic()
+        while not all(os.path.exists(n) for n in names):
+            if time.monotonic() - t0 > timeout:
+                raise TimeoutError(f"rank {rank}: handles of {tag} missing")
+            time.sleep(0.01)
+        out = []
+        for n in names:
+            with open(n, "rb") as f:
+                out.append(f.read())
+        return out
+    return gather
 
 
 def main(argv):
@@ -21,8 +46,11 @@ def main(argv):
     from chat_wgpu_b200.model import Model, Session
     ctx = GpuContext(rank)
     m = Model(ctx, path, tp=(rank, world, uid))
+    p2p = argv[8] if len(argv) > 8 else None
     s = Session(m, len(prompt) + n_new)
     assert not s.persistent
+    if p2p:
+        s.tp_attach_p2p(file_allgather(p2p, "s", rank, world))
     s.begin(prompt)
     s.run(len(prompt) - 1)
     logits = []
@@ -44,6 +72,8 @@ def main(argv):
     t.close()
     # a stop token (greedy): the stream ends before it, on every rank
     e = Session(m, len(prompt) + n_new)
+    if p2p:
+        e.tp_attach_p2p(file_allgather(p2p, "e", rank, world))
     e.set_eos([int(toks[3])])
     e.begin(prompt)
     e.run(len(prompt) - 1 + n_new)
