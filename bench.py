@@ -588,7 +588,13 @@ def run_cuda(args, dist):
                  "tok_s": replica_rate(K * args.sessions, dist.world, t_max),
                  "unit": "tok/s (all GPUs, all sessions)", "ms_per_step": t_max * 1e3 / K,
                  "positions": r["positions"],
-                 "path": "SessionGroup: one tensor-core pass over the weights per step"}
+                 "path": f"SessionGroup: one pass over the weights per step ({r['path']})"}
+        if r["path"].startswith("streaming"):  # the other projection path, for the record
+            r2 = group_bench(model, args.sessions, P, K, warmup=W, seed=args.seed,
+                             streaming=False)
+            t2 = dist.max(r2["ms_per_step"] * K / 1000.0)
+            group["other_path"] = {"path": r2["path"], "ms_per_step": t2 * 1e3 / K,
+                                   "tok_s": replica_rate(K * args.sessions, dist.world, t2)}
 
     # ---- e2e: public per-token API with host round trips
     s2 = Session(model, max_seq)

@@ -121,6 +121,7 @@ SIGNATURES = {
     "cw_group_free": [_vp],
     "cw_group_run": [_vp, _sz],
     "cw_group_run_timed": [_vp, _sz, C.POINTER(C.c_double)],
+    "cw_group_set_streaming": [_vp, C.c_int, C.POINTER(C.c_int)],
     "cw_session_clear_taps": [_vp],
     "cw_session_read_tap": [_vp, C.c_char_p, C.c_uint32, _sz, _vp, _sz],
     "cw_sample": [_vp, _buf, _sz, C.c_float, C.c_uint32, C.c_float, C.c_uint64, C.c_uint64, _pbuf],

@@ -31,6 +31,8 @@
 #include "cw_common.h"
 #include "cw_device.cuh"
 #include "cw_gemm.cuh"
+#include "cw_gemv.cuh"
+#include "cw_mgemv.h"
 #include "cw_kquant.cuh"
 #include "cw_model.h"
 #include "cw_sample.cuh"
@@ -701,7 +703,7 @@ __global__ void __launch_bounds__(128) k_grp_fattn(
     const float* __restrict__ q_norm, const float* __restrict__ k_norm, float eps,
     const float* __restrict__ inv_freq, int nh, int nkv, int hd, int n_splits, int window,
     float scale, float softcap, float* __restrict__ part, unsigned* __restrict__ counters,
-    __half* __restrict__ xh, __half* __restrict__ xl) {
+    __half* __restrict__ xh, __half* __restrict__ xl, float* __restrict__ xo) {
     pdl_trigger();
     pdl_wait();
     extern __shared__ float sm[];
@@ -777,7 +779,11 @@ __global__ void __launch_bounds__(128) k_grp_fattn(
     if (n_active == 1) {
         for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
             const int gi = i / hd, d = i - gi * hd;
-            split_f16(res[gi * W + d] * (1.0f / res[gi * W + hd + 1]), xh + o0 + i, xl + o0 + i);
+            const float o = res[gi * W + d] * (1.0f / res[gi * W + hd + 1]);
+            if (xo)
+                xo[o0 + i] = o;
+            else
+                split_f16(o, xh + o0 + i, xl + o0 + i);
         }
         return;
     }
@@ -816,7 +822,10 @@ __global__ void __launch_bounds__(128) k_grp_fattn(
         const float* c = cwt + gi * (n_active + 1);
         float a = 0.f;
         for (int t = 0; t < n_active; t++) a = fmaf(__ldcg(ph + (size_t)t * W), c[t], a);
-        split_f16(a * c[n_active], xh + o0 + i, xl + o0 + i);
+        if (xo)
+            xo[o0 + i] = a * c[n_active];
+        else
+            split_f16(a * c[n_active], xh + o0 + i, xl + o0 + i);
     }
     __syncthreads();
     if (threadIdx.x == 0) *ctr = 0u;
@@ -881,7 +890,7 @@ __global__ void __launch_bounds__(SMP_THREADS) k_grp_finalize(const GrpRow* __re
 }
 
 struct GrpLayout {
-    size_t H, T, QKV, G, xh, xl, logits, ws, part, ctr, total;
+    size_t H, T, QKV, G, xh, xl, X, logits, ws, part, ctr, total;
 };
 
 // Key splits of the group attention: about two CTAs per SM over all rows and
@@ -909,6 +918,7 @@ GrpLayout grp_layout(const cw_model* m, size_t B) {
     L.G = take(B * 2 * (size_t)I.hidden * 4);
     L.xh = take(B * xk * 2);
     L.xl = take(B * xk * 2);
+    L.X = take(B * qd * 4);
     L.logits = take(B * (size_t)I.vocab * 4);
     L.part = take(B * (size_t)I.n_heads * 16 * (I.head_dim + 2) * 4);  // up to 16 splits
     L.ctr = take(B * (size_t)I.n_kv * 4);  // merge counters (zero, self-resetting)
@@ -953,11 +963,133 @@ struct cw_group {
     cw::GrpRow* rows = nullptr;  // device
     void* mem = nullptr;         // scratch (GrpLayout)
     cudaGraphExec_t graph = nullptr;
+    // projections as co-batched streaming GEMVs (cw_mgemv.cu) instead of
+    // tensor-core GEMMs over the packed tile records; their products on the
+    // integer MMA where K allows (else dp4a)
+    bool streaming = false;
+    bool mma = true;
 };
 
 namespace cw {
 
+// The co-batched step with every projection a streaming GEMV over all rows
+// (cw_mgemv.cu): 5 launches per layer -- norm + QKV, attention, O +
+// residual, norm + gate/up + GLU, down + residual -- each one pass over its
+// weight for all sessions.
+static int grp_enqueue_streaming(cw_group* g) {
+    cw_model* m = g->m;
+    cw_ctx* ctx = m->ctx;
+    const cw_model_info& I = m->info;
+    const int B = (int)g->ss.size();
+    const int dim = (int)I.dim, nh = (int)I.n_heads, nkv = (int)I.n_kv, hd = (int)I.head_dim;
+    const int qd = nh * hd, kvd = nkv * hd, qkv_rows = qd + 2 * kvd, hid = (int)I.hidden;
+    const int unit = I.norm_kind == 1;
+    const GrpLayout L = grp_layout(m, (size_t)B);
+    uint8_t* b = (uint8_t*)g->mem;
+    float* H = (float*)(b + L.H);
+    float* QKV = (float*)(b + L.QKV);
+    float* A = (float*)(b + L.G);  // FFN activations [B][hid]
+    float* X = (float*)(b + L.X);  // attention output [B][qd]
+    float* logits = (float*)(b + L.logits);
+    std::unique_ptr<OpScope> sc;
+    auto stage = [&](const char* name) {
+        sc.reset();
+        if (ctx->profiling) sc.reset(new OpScope(ctx, name));
+    };
+    auto mg = [&](const char* name, const QW& w, int pro, int epi, const float* x, int ldx,
+                  const float* norm_w, float* y, int ldy, const float* bias) {
+        stage(name);
+        MgArgs a{};
+        a.payload = w.payload;
+        a.scales = w.scales;
+        a.K = w.in_f;
+        a.N = w.rows;
+        a.B = B;
+        a.x = x;
+        a.ldx = ldx;
+        a.norm_w = norm_w;
+        a.eps = I.eps;
+        a.unit = unit;
+        a.y = y;
+        a.ldy = ldy;
+        a.bias = bias;
+        a.geglu = I.activation == 1;
+        a.status = ctx->d_status;
+        a.mma = g->mma ? 1 : 0;
+        CW_TRY(launch_mgemv(ctx, pro, epi, a, true));
+        return check_launch(name);
+    };
+    stage("group.embed");
+    CW_TRY(launch_pdl(ctx, true, k_grp_embed, dim3(B), dim3(256), 0, m->embed.payload,
+                      m->embed.scales, m->embed.type, dim, I.embed_scale, (const GrpRow*)g->rows,
+                      H));
+    CW_TRY(check_launch("group embed"));
+    for (uint32_t li = 0; li < I.n_layers; li++) {
+        const Layer& l = m->L[li];
+        CW_TRY(mg("group.qkv", l.qkv, PRO_NORM, EPI_STORE, H, dim, l.attn_norm, QKV, qkv_rows,
+                  l.qkv_bias));
+        stage("group.attn");
+        {
+            const int G = nh / nkv, epl = (hd + 31) / 32, ns = g->n_splits;
+            const size_t smem =
+                (attn_smem_floats(G, hd, ns) + (size_t)G * hd + hd) * sizeof(float);
+            const int window = (I.sliding_window && li % 2 == 0) ? (int)I.sliding_window : 0;
+            const float scale = powf((float)hd, -0.5f);  // attention.rs:18
+            dim3 grid(ns, nkv, B);
+            float* part = (float*)(b + L.part);
+            unsigned* ctr = (unsigned*)(b + L.ctr);
+            auto go = [&](auto kern) -> int {
+                if (smem > 48 * 1024)
+                    CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)smem));
+                CW_TRY(launch_pdl(ctx, true, kern, grid, dim3(128), smem, (const float*)QKV,
+                                  qkv_rows, (const GrpRow*)g->rows, (int)li,
+                                  (const float*)l.q_norm, (const float*)l.k_norm, I.eps,
+                                  m->inv_freq, nh, nkv, hd, ns, window, scale, I.attn_softcap,
+                                  part, ctr, (__half*)nullptr, (__half*)nullptr, X));
+                return check_launch("group attention");
+            };
+#define CW_GA(E, GM) CW_TRY(go(k_grp_fattn<E, GM>))
+#define CW_GAE(E)                 \
+    if (G <= 1) CW_GA(E, 1);      \
+    else if (G <= 2) CW_GA(E, 2); \
+    else if (G <= 4) CW_GA(E, 4); \
+    else CW_GA(E, 8);
+            if (epl <= 1) { CW_GAE(1) }
+            else if (epl <= 2) { CW_GAE(2) }
+            else if (epl <= 4) { CW_GAE(4) }
+            else { CW_GAE(8) }
+#undef CW_GAE
+#undef CW_GA
+        }
+        CW_TRY(mg("group.o", l.wo, PRO_X, EPI_RESID, X, qd, nullptr, H, dim, nullptr));
+        CW_TRY(mg("group.gate_up", l.gate_up, PRO_NORM, EPI_GLU, H, dim, l.ffn_norm, A, hid,
+                  nullptr));
+        CW_TRY(mg("group.down", l.down, PRO_X, EPI_RESID, A, hid, nullptr, H, dim, nullptr));
+    }
+    CW_TRY(mg("group.head", m->head, PRO_NORM, EPI_STORE, H, dim, m->final_norm, logits,
+              (int)I.vocab, nullptr));
+    stage("group.finalize");
+    CW_TRY(launch_pdl(ctx, true, k_grp_finalize, dim3(B), dim3(SMP_THREADS), 0,
+                      (const GrpRow*)g->rows, (const float*)logits, (int)I.vocab,
+                      I.final_softcap));
+    sc.reset();
+    return check_launch("group finalize");
+}
+
+// Whether a group of B sessions can take the streaming step: pre-norm
+// families (post-norm residuals would need a second residual buffer), at
+// most 8 sessions, every projection's K a multiple of 256 within the
+// kernel's range.
+static bool grp_streaming_ok(const cw_model* m, size_t B) {
+    const cw_model_info& I = m->info;
+    const int qd = (int)(I.n_heads * I.head_dim);
+    return I.post_norms == 0 && mgemv_supported((int)I.dim, (int)B) &&
+           mgemv_supported(qd, (int)B) && mgemv_supported((int)I.hidden, (int)B);
+}
+
 static int grp_enqueue(cw_group* g) {
+    if (g->streaming) return grp_enqueue_streaming(g);
     cw_model* m = g->m;
     cw_ctx* ctx = m->ctx;
     const cw_model_info& I = m->info;
@@ -1018,7 +1150,7 @@ static int grp_enqueue(cw_group* g) {
                                   qkv_rows, (const GrpRow*)g->rows, (int)li,
                                   (const float*)l.q_norm, (const float*)l.k_norm, I.eps,
                                   m->inv_freq, nh, nkv, hd, ns, window, scale, I.attn_softcap,
-                                  part, ctr, (__half*)xh, (__half*)xl));
+                                  part, ctr, (__half*)xh, (__half*)xl, (float*)nullptr));
                 return check_launch("group attention");
             };
 #define CW_GA(E, GM) CW_TRY(go(k_grp_fattn<E, GM>))
@@ -1124,9 +1256,11 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
     CW_CHECK(model_q4_only(m, true), CW_ERR_UNSUPPORTED,
              "cw_group_create: the co-batched step takes Q4_0 projections and LM head");
     cudaSetDevice(ctx->device);
-    CW_TRY(model_pack_weights(m));
+    const bool streaming = grp_streaming_ok(m, n);
+    if (!streaming) CW_TRY(model_pack_weights(m));
     cw_group* g = new cw_group();
     g->m = m;
+    g->streaming = streaming;
     g->n_splits = grp_splits(m, n, ctx->sm_count);
     g->ss.assign(sessions, sessions + n);
     std::vector<GrpRow> h(n);
@@ -1161,6 +1295,27 @@ int cw_group_free(cw_group* g) {
     if (g->rows) cudaFree(g->rows);
     if (g->mem) cudaFree(g->mem);
     delete g;
+    return CW_OK;
+}
+
+int cw_group_set_streaming(cw_group* g, int on, int* streaming) {
+    clear_error();
+    CW_CHECK(g, CW_ERR_INVALID_ARG, "cw_group_set_streaming: group is NULL");
+    CW_CHECK(on >= -1 && on <= 2, CW_ERR_INVALID_ARG, "cw_group_set_streaming: on must be -1..2");
+    const int cur = g->streaming ? (g->mma ? 1 : 2) : 0;
+    if (on >= 0 && on != cur) {
+        cw_ctx* ctx = g->m->ctx;
+        cudaSetDevice(ctx->device);
+        CW_CHECK(!on || grp_streaming_ok(g->m, g->ss.size()), CW_ERR_UNSUPPORTED,
+                 "cw_group_set_streaming: the group does not qualify for the streaming step");
+        if (!on) CW_TRY(model_pack_weights(g->m));
+        CW_CUDA(cudaStreamSynchronize(ctx->stream));
+        if (g->graph) cudaGraphExecDestroy(g->graph);
+        g->graph = nullptr;
+        g->streaming = on != 0;
+        g->mma = on != 2;
+    }
+    if (streaming) *streaming = g->streaming ? (g->mma ? 1 : 2) : 0;
     return CW_OK;
 }
 

@@ -15,7 +15,9 @@ import numpy as np
 
 
 def bench(model, B: int, prompt_len: int, steps: int, warmup: int = 3, seed: int = 0,
-          profile: int = 0) -> dict:
+          profile: int = 0, streaming=None) -> dict:
+    """streaming: None = the group's default projection path, True / False =
+    streaming GEMVs / tensor-core GEMMs."""
     from .model import Session, SessionGroup
     rng = np.random.default_rng(seed + B)
     ss = []
@@ -25,6 +27,10 @@ def bench(model, B: int, prompt_len: int, steps: int, warmup: int = 3, seed: int
         s.prefill()
         ss.append(s)
     g = SessionGroup(ss)
+    if streaming is not None:
+        g.set_streaming(streaming)
+    path = {1: "streaming GEMVs, integer-MMA products", 2: "streaming GEMVs, dp4a products",
+            0: "tensor-core GEMMs"}[g.path]
     g.run(1 + warmup)  # the last prompt token (first produced token) + warm-up steps
     ms = g.run_timed(steps)
     produced = [len(s.tokens()) for s in ss]
@@ -44,6 +50,7 @@ def bench(model, B: int, prompt_len: int, steps: int, warmup: int = 3, seed: int
         s.close()
     assert all(p == 1 + warmup + steps for p in produced), produced
     return {"sessions": B, "steps": steps, "ms_per_step": ms / steps, "stages": stages,
+            "path": path,
             "tok_s": B * steps / (ms / 1e3),
             "positions": f"{prompt_len + warmup}..{prompt_len + warmup + steps - 1}"}
 
@@ -57,7 +64,10 @@ def main(argv=None) -> None:
     ap.add_argument("--profile", type=int, default=0, metavar="STEPS",
                     help="also print a per-stage breakdown over STEPS direct-launch steps")
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--path", choices=["auto", "streaming", "dp4a", "gemm"], default="auto",
+                    help="projection path of the group step")
     a = ap.parse_args(argv)
+    streaming = {"auto": None, "streaming": 1, "dp4a": 2, "gemm": 0}[a.path]
     from . import gguf
     from .context import GpuContext
     from .model import Model
@@ -65,11 +75,12 @@ def main(argv=None) -> None:
     m = Model(ctx, gguf.cached_model(a.model))
     out = []
     for B in a.sessions:
-        r = bench(m, B, a.prompt_len, a.steps, profile=a.profile)
+        r = bench(m, B, a.prompt_len, a.steps, profile=a.profile, streaming=streaming)
         out.append(r)
         if not a.json:
             print(f"{a.model}: {B:4d} sessions  {r['ms_per_step']:.3f} ms/step  "
-                  f"{r['tok_s']:9.0f} tok/s  (positions {r['positions']})", flush=True)
+                  f"{r['tok_s']:9.0f} tok/s  (positions {r['positions']}, {r['path']})",
+                  flush=True)
             for name, (c, t) in sorted((r["stages"] or {}).items(), key=lambda kv: -kv[1][1]):
                 print(f"    {name:20s} {c:5d} launches/step  {t:8.3f} ms/step")
     if a.json:

@@ -278,7 +278,8 @@ class Session:
 class SessionGroup:
     """Co-batched decode of several sessions of one model (cw_group_*): each
     step runs every session's next position with one pass over the weights
-    (tensor-core GEMMs over all rows)."""
+    (streaming GEMVs over all rows for groups of up to 8 sessions of a
+    pre-norm family, else tensor-core GEMMs)."""
 
     def __init__(self, sessions):
         self.sessions = list(sessions)
@@ -298,6 +299,25 @@ class SessionGroup:
             self.close()
         except Exception:
             pass
+
+    @property
+    def path(self) -> int:
+        """Projection path: 1 streaming GEMVs (integer-MMA products where K <=
+        4096), 2 streaming GEMVs with dp4a products, 0 tensor-core GEMMs."""
+        v = C.c_int()
+        _lib.call("cw_group_set_streaming", self._h, -1, C.byref(v))
+        return int(v.value)
+
+    @property
+    def streaming(self) -> bool:
+        """Whether the projections run as streaming GEMVs (else tensor-core GEMMs)."""
+        return self.path != 0
+
+    def set_streaming(self, on) -> None:
+        """Choose the projection path: True / 1 streaming (integer MMA where
+        K <= 4096), 2 streaming with dp4a products, False / 0 tensor-core GEMMs.
+        Streaming raises when the group does not qualify."""
+        _lib.call("cw_group_set_streaming", self._h, int(on), None)
 
     def run(self, n_steps: int) -> None:
         _lib.call("cw_group_run", self._h, int(n_steps))

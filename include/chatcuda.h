@@ -349,16 +349,26 @@ int cw_session_read_kv(cw_session* s, uint32_t layer, size_t n_pos, float* k, fl
  * time).  A group steps n sessions of one model together: one batched step
  * runs every session's next position (prompt or decode, each at its own
  * position with its own KV cache, sampling settings and stop tokens) with
- * the projections and LM head of all n rows as one tensor-core GEMM each,
- * so the weights are read once per step for all sessions.  Per session the
- * result equals its own cw_session_run step within 1e-3 relative.  Uses f16
- * hi/lo copies of the model's weights (4 bytes per weight, built once per
- * model by the first group).  Sessions must have begun (cw_session_begin)
- * and stay owned by the caller; hook taps are not recorded by group steps.
- * cw_group_run advances every session by n_steps positions. */
+ * each projection and the LM head read once per step for all n rows.  Per
+ * session the result equals its own cw_session_run step within 1e-3
+ * relative.  Groups of up to 8 sessions of a pre-norm family whose
+ * projection widths are multiples of 256 run every projection as one
+ * streaming GEMV over all rows (the Q4_0 weights as loaded); other groups
+ * run them as tensor-core GEMMs over packed tile records (+0.5625 bytes per
+ * weight, built once per model by the first such group).  Sessions must
+ * have begun (cw_session_begin) and stay owned by the caller; hook taps are
+ * not recorded by group steps.  cw_group_run advances every session by
+ * n_steps positions. */
 typedef struct cw_group cw_group;
 int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out);
 int cw_group_free(cw_group* g);
+/* Choose the group's projection path: 1 = streaming GEMVs with their
+ * products on the integer tensor cores where K <= 4096 (the default of a
+ * qualifying group), 2 = streaming GEMVs with dp4a products only (same
+ * integer sums), 0 = tensor-core GEMMs over packed tiles, -1 = no change.
+ * CW_ERR_UNSUPPORTED when the group does not qualify for streaming.
+ * *streaming (may be NULL) receives the path now in use (0, 1 or 2). */
+int cw_group_set_streaming(cw_group* g, int on, int* streaming);
 int cw_group_run(cw_group* g, size_t n_steps);
 /* cw_group_run timed with CUDA events on the context stream (the first step
  * of a new group is captured as a graph and run before the timed region). */
