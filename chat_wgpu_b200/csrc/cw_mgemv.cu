@@ -59,6 +59,10 @@ using Mg4b = MgCfg<4, 4, 2, 4>;   // K <= 2048: 16 rows
 using Mg4c = MgCfg<4, 8, 2, 4>;   // K <= 4096:  8 rows
 using Mg4d = MgCfg<4, 16, 3, 2>;  // K <= 12288: 2 rows
 
+__device__ __forceinline__ int ld_volatile_shared(const int* p) {
+    return *reinterpret_cast<const volatile int*>(p);
+}
+
 __device__ __forceinline__ float mg_ss4(const float4& v, float ss) {
     ss = fmaf(v.x, v.x, ss);
     ss = fmaf(v.y, v.y, ss);
@@ -313,14 +317,25 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_mgemv(MgArgs a, int S) {
 // are combined per (row, session, block) as there: T = D0 + 256 D1 - 8 sum X
 // + 65536 D2, acc += d * 2^(e-22) * T.
 //
-// A chunk is one 16-row tile; warp w takes blocks w, w + 16, ... of every
-// tile, keeping the B fragments (its blocks' planes of the 8 sessions) and
-// the per-(session, block) sums and scales in registers.  Each weight row
-// lands 16 bytes further along than the last (one bulk copy per row, issued
-// by 16 lanes of warp 0), so the A fragment loads -- word c of the block in
-// rows g and g + 8 -- hit 32 different banks.  The 16 warps' partial sums
-// of each (row, session) are added in a fixed order through shared memory.
-constexpr int MI_RC = 16;  // rows per chunk: one MMA tile
+// Weights: a tile-interleaved copy of the matrix (mg_tile_pack): per 16-row
+// tile its payload [block][row][16 B] then its scales [block][row], one
+// contiguous range, so a tile is ONE bulk copy and a warp's A-fragment loads
+// (word c of a block in rows g and g + 8) and scale loads hit distinct
+// banks.  The session inputs are converted once per CTA into q24 planes
+// stored fragment-major (per block, session and thread-in-group the six
+// B-fragment words, then (8 sum X, 2^(e-22)) pairs), so a block's B operands
+// are three conflict-free 8-byte loads and one 16-byte load.
+//
+// Work: the 16 compute warps form 16 / WG groups of WG warps; a group takes
+// a tile, each of its warps a 1/WG share of the blocks, and the group's
+// partial sums meet in shared memory behind a named barrier of the group
+// (which also agrees on a timed-out wait).  Tile q of the CTA goes to group
+// q % NG and ring stage q % S (S a multiple of NG, so every stage belongs to
+// one group).  A 17th warp only streams the tiles, refilling a stage once
+// its group released it (the stage's "empty" mbarrier).
+constexpr int MI_RC = 16;                      // rows per tile
+constexpr int MI_BLOCK = MG_THREADS + 32;      // + the producer warp
+constexpr int MI_SMAX = 16;                    // ring stages at most
 
 __device__ __forceinline__ void mma_u8u8(int (&d)[4], const unsigned (&a)[4], unsigned b0,
                                          unsigned b1) {
@@ -338,67 +353,114 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], const unsigned (&a)[4], un
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
-
-// shared-memory row pitch of the payload (one extra 16-byte unit per row)
-__host__ __device__ constexpr size_t mi_pitch(int nb) { return (size_t)nb * 16 + 16; }
-__host__ __device__ constexpr size_t mi_pay_bytes(int nb) { return al128(MI_RC * mi_pitch(nb)); }
-__host__ __device__ constexpr size_t mi_stage_bytes(int nb) {
-    return mi_pay_bytes(nb) + al128((size_t)MI_RC * nb * 2);
+// named barrier 1 over the 16 compute warps
+__device__ __forceinline__ void mi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(MG_THREADS) : "memory"); }
+// named barrier `id` over `n` threads; returns whether any passed v != 0
+__device__ __forceinline__ bool mi_group_sync_or(int id, int n, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
 }
-constexpr size_t MI_RED_BYTES = 2 * MG_WARPS * MI_RC * 8 * 4;  // [2][warp][row][session]
 
-template <int BPW, int PRO, int EPI>
-__global__ void __launch_bounds__(MG_THREADS, 1) k_mgemm(MgArgs a, int S) {
+// one tile of the tile-interleaved copy: 16 rows x nb blocks x 18 bytes
+__host__ __device__ constexpr size_t mi_tile_bytes(int nb) { return (size_t)MI_RC * nb * 18; }
+// fragment-major planes: words [nb][8 sessions][4 c][6], then int2 [nb][8]
+__host__ __device__ constexpr size_t mi_frag_bytes(int nb) { return (size_t)nb * (768 + 64); }
+constexpr size_t MI_RED_BYTES = 2 * MG_WARPS * MI_RC * 8 * 4;  // [group][2][warp in group][row][session]
+
+struct MiShared {
+    uint64_t full[MI_SMAX], empty[MI_SMAX];
+    int abort, issued, prod_done;
+};
+
+// Tile t of a Q4_0 matrix (payload [N][nb][16], scales [N][nb]) into the
+// tile-interleaved layout; rows past N are zeros (scale 0).
+__global__ void k_mg_pack(const uint8_t* __restrict__ payload, const __half* __restrict__ scales,
+                          int N, int nb, uint8_t* __restrict__ dst) {
+    const long t = blockIdx.x;
+    uint8_t* tp = dst + (size_t)t * mi_tile_bytes(nb);
+    uint4* pay = reinterpret_cast<uint4*>(tp);
+    __half* sc = reinterpret_cast<__half*>(tp + (size_t)MI_RC * nb * 16);
+    for (int i = threadIdx.x; i < MI_RC * nb; i += blockDim.x) {
+        const int b = i / MI_RC, r = i % MI_RC;
+        const long row = t * MI_RC + r;
+        const bool in = row < N;
+        pay[i] = in ? reinterpret_cast<const uint4*>(payload)[(size_t)row * nb + b] : make_uint4(0, 0, 0, 0);
+        sc[i] = in ? scales[(size_t)row * nb + b] : __float2half(0.0f);
+    }
+}
+
+template <int WG, int PRO, int EPI>
+__global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
+    constexpr int NG = MG_WARPS / WG;  // warp groups (tiles in flight per CTA)
     extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ MiShared sh;
     __shared__ float red[MG_WARPS];
     __shared__ float inv_s[8];
     const int nb = a.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = lane >> 2, c = lane & 3;  // MMA group (row / session column) and thread in group
     const int ns = min(8, a.B);
-    const long nchunks = ((long)a.N + MI_RC - 1) / MI_RC;
-    const int mycount =
-        blockIdx.x < nchunks ? (int)((nchunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
-    const size_t pitch = mi_pitch(nb), pay_b = mi_pay_bytes(nb), stage_b = mi_stage_bytes(nb);
-    const size_t qreg = al16(q24_bytes(nb));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-    unsigned char* planes = smem + 128;
-    float* rbuf = reinterpret_cast<float*>(planes + (size_t)8 * qreg);
+    const long ntiles = ((long)a.N + MI_RC - 1) / MI_RC;
+    const int mycount = blockIdx.x < ntiles ? (int)((ntiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    const size_t tile_b = mi_tile_bytes(nb), stage_b = al128(tile_b);
+    uint32_t* frag = reinterpret_cast<uint32_t*>(smem);
+    int2* cbsb = reinterpret_cast<int2*>(smem + (size_t)nb * 768);
+    float* rbuf = reinterpret_cast<float*>(smem + al128(mi_frag_bytes(nb)));
     unsigned char* stages = reinterpret_cast<unsigned char*>(rbuf) + MI_RED_BYTES;
 
-    // chunk i of this CTA into stage i % S (warp 0: lane 0 arms the barrier,
-    // lanes 0..rows-1 copy one row each, lane 16 the scales)
-    auto issue = [&](int i) {
-        const long ch = blockIdx.x + (long)i * gridDim.x;
-        const int st = i % S;
-        const long row0 = ch * MI_RC;
-        const int rows = (int)min((long)MI_RC, (long)a.N - row0);
-        const unsigned rb = (unsigned)nb * 16, sb = (unsigned)rows * nb * 2;
-        const uint64_t pol = l2_evict_first();
-        if (lane == 0) {
-            fence_proxy_async();
-            mbar_expect_tx(&bars[st], (unsigned)rows * rb + sb);
-        }
-        __syncwarp();
-        unsigned char* dst = stages + (size_t)st * stage_b;
-        if (lane < rows)
-            bulk_g2s_hint(dst + (size_t)lane * pitch, a.payload + (size_t)(row0 + lane) * rb, rb,
-                          &bars[st], pol);
-        if (lane == 16)
-            bulk_g2s_hint(dst + pay_b, a.scales + (size_t)row0 * nb, sb, &bars[st], pol);
-    };
     if (tid == 0) {
-        for (int st = 0; st < S; st++) mbar_init(&bars[st], 1);
+        for (int st = 0; st < S; st++) {
+            mbar_init(&sh.full[st], 1);
+            mbar_init(&sh.empty[st], 1);
+        }
         fence_mbar_init();
+        sh.abort = 0;
+        sh.issued = 0;
+        sh.prod_done = 0;
     }
     __syncthreads();
-    if (warp == 0)  // the weight stream does not depend on the previous kernel
-        for (int i = 0; i < S && i < mycount; i++) issue(i);
-    pdl_trigger();
+    if (warp == MG_WARPS) {
+        // ---- the producer: tile q into stage q % S once that stage's
+        // previous tile (q - S) was released.  The weight stream does not
+        // depend on the previous kernel.
+        pdl_trigger();
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first();
+            int q = 0;
+            for (; q < mycount; q++) {
+                const int st = q % S;
+                if (q >= S) {
+                    const unsigned par = (unsigned)(((q / S) - 1) & 1);
+                    bool ok = mbar_try_wait(&sh.empty[st], par);
+                    const uint64_t t0 = ok ? 0 : global_ns();
+                    while (!ok) {
+                        if (ld_volatile_shared(&sh.abort) || global_ns() - t0 > GEMV_WAIT_NS) break;
+                        ok = mbar_try_wait(&sh.empty[st], par);
+                    }
+                    if (!ok) break;
+                }
+                const long tile = blockIdx.x + (long)q * gridDim.x;
+                mbar_expect_tx(&sh.full[st], (unsigned)tile_b);
+                bulk_g2s_hint(stages + (size_t)st * stage_b, a.tiles + (size_t)tile * tile_b,
+                              (unsigned)tile_b, &sh.full[st], pol);
+            }
+            sh.issued = q;
+            __threadfence_block();
+            *reinterpret_cast<volatile int*>(&sh.prod_done) = 1;
+        }
+        return;
+    }
     pdl_wait();
 
-    // ---- prologue: per-session rmsnorm scales, then q24 planes of every
-    // (session, block) in shared memory (sessions >= ns stay unused)
+    // ---- prologue: per-session rmsnorm scales, then every (session, block)
+    // of the inputs as q24 planes, fragment-major; sessions >= ns are zeros
     if constexpr (PRO == PRO_NORM) {
         constexpr int TPS = MG_THREADS / 8, WPS = TPS / 32;  // 64 threads per session
         const int ps = tid / TPS, pt = tid % TPS;
@@ -411,109 +473,124 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_mgemm(MgArgs a, int S) {
         }
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
-        __syncthreads();
+        mi_sync();
         if (tid < 8) {
             float t = 0.f;
 #pragma unroll
             for (int w = 0; w < WPS; w++) t += red[tid * WPS + w];
             inv_s[tid] = 1.0f / sqrtf(t / (float)a.K + a.eps);
         }
-        __syncthreads();
+        mi_sync();
     }
     {
-        const int nq = nb / 4, items = ns * nq;
-        const int sub = lane >> 3, e0 = 4 * (lane & 7);
+        // item = (session s, four blocks 4t..4t+3); lane: block 4t + lane/8,
+        // half h = (lane/4) & 1, word c = lane & 3 -> elements 16h + 4c .. +3
+        const int nq = nb / 4, items = 8 * nq;
+        const int sub = lane >> 3, hh = (lane >> 2) & 1, cc = lane & 3;
         for (int it = warp; it < items; it += MG_WARPS) {
-            const int s = it / nq, b = 4 * (it - s * nq) + sub, i = b * 32 + e0;
-            float4 v = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)s * a.ldx + i));
-            if constexpr (PRO == PRO_NORM) {
-                const float inv = inv_s[s];
-                float4 w = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
-                if (a.unit) w = make_float4(1.0f + w.x, 1.0f + w.y, 1.0f + w.z, 1.0f + w.w);
-                v = make_float4(__fmul_rn(__fmul_rn(v.x, inv), w.x), __fmul_rn(__fmul_rn(v.y, inv), w.y),
-                                __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
-            }
-            q24_quad(q24_carve(planes + (size_t)s * qreg, nb), b, true, v, lane);
-        }
-    }
-    __syncthreads();
-    // B fragments of this warp's blocks: session column g, plane p, word c of
-    // each half; and for the D columns 2c, 2c+1: 8 sum X and 2^(e-22)
-    unsigned bf[BPW][3][2];
-    int cbv[BPW][2];
-    float sbv[BPW][2];
-#pragma unroll
-    for (int k = 0; k < BPW; k++) {
-        const int b = warp + k * MG_WARPS;
-        const bool in = b < nb;
-        const bool gv = in && g < ns;
-        const uint32_t* pw = reinterpret_cast<const uint32_t*>(planes + (size_t)(gv ? g : 0) * qreg);
-#pragma unroll
-        for (int p = 0; p < 3; p++) {
-            bf[k][p][0] = gv ? pw[((size_t)(p * 2 + 0) * nb + b) * 4 + c] : 0u;
-            bf[k][p][1] = gv ? pw[((size_t)(p * 2 + 1) * nb + b) * 4 + c] : 0u;
-        }
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int n = 2 * c + h;
-            const Q24 q = q24_carve(planes + (size_t)(n < ns ? n : 0) * qreg, nb);
-            cbv[k][h] = in && n < ns ? q.cb[b] : 0;
-            sbv[k][h] = in && n < ns ? q.sb[b] : 0.f;
-        }
-    }
-
-    // ---- stream the tiles
-    int failed = 0;
-    for (int i = 0; i < mycount; i++) {
-        const int st = i % S;
-        const bool ok = mbar_wait(&bars[st], (unsigned)((i / S) & 1), GEMV_WAIT_NS);
-        const unsigned char* pay = stages + (size_t)st * stage_b;
-        const __half* scs = reinterpret_cast<const __half*>(pay + pay_b);
-        const long row0 = (blockIdx.x + (long)i * gridDim.x) * MI_RC;
-        const int rows = (int)min((long)MI_RC, (long)a.N - row0);
-        float* rb = rbuf + (size_t)(i & 1) * MG_WARPS * MI_RC * 8;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const bool r0in = g < rows, r1in = g + 8 < rows;
-#pragma unroll
-        for (int k = 0; k < BPW; k++) {
-            const int b = warp + k * MG_WARPS;
-            if (b < nb) {  // warp-uniform
-                const unsigned w0 = r0in ? *reinterpret_cast<const unsigned*>(pay + (size_t)g * pitch + b * 16 + 4 * c) : 0x88888888u;
-                const unsigned w1 = r1in ? *reinterpret_cast<const unsigned*>(pay + (size_t)(g + 8) * pitch + b * 16 + 4 * c) : 0x88888888u;
-                const float d0 = r0in ? __half2float(scs[(size_t)g * nb + b]) : 0.f;
-                const float d1 = r1in ? __half2float(scs[(size_t)(g + 8) * nb + b]) : 0.f;
-                const unsigned af[4] = {w0 & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu,
-                                        (w1 >> 4) & 0x0f0f0f0fu};
-                int D0[4], D1[4], D2[4];
-                mma_u8u8(D0, af, bf[k][0][0], bf[k][0][1]);
-                mma_u8u8(D1, af, bf[k][1][0], bf[k][1][1]);
-                mma_u8s8(D2, af, bf[k][2][0], bf[k][2][1]);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int h = e & 1;
-                    const int s01 = D0[e] + (D1[e] << 8) - cbv[k][h];
-                    const float T = fmaf((float)D2[e], 65536.0f, (float)s01);
-                    acc[e] = fmaf((e < 2 ? d0 : d1) * sbv[k][h], T, acc[e]);
+            const int s = it / nq, b = 4 * (it - s * nq) + sub, i = b * 32 + 16 * hh + 4 * cc;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (s < ns) {  // warp-uniform
+                v = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)s * a.ldx + i));
+                if constexpr (PRO == PRO_NORM) {
+                    const float inv = inv_s[s];
+                    float4 w = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
+                    if (a.unit) w = make_float4(1.0f + w.x, 1.0f + w.y, 1.0f + w.z, 1.0f + w.w);
+                    v = make_float4(__fmul_rn(__fmul_rn(v.x, inv), w.x), __fmul_rn(__fmul_rn(v.y, inv), w.y),
+                                    __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
                 }
+            }
+            // block max and integer sum over the block's 8 lanes (q24_quad's scheme)
+            unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                             max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+            m = max(m, __shfl_xor_sync(FULL, m, 1));
+            m = max(m, __shfl_xor_sync(FULL, m, 2));
+            m = max(m, __shfl_xor_sync(FULL, m, 4));
+            int X0, X1, X2, X3;
+            float sb;
+            q24_scale(m, v.x, X0, sb);
+            q24_scale(m, v.y, X1, sb);
+            q24_scale(m, v.z, X2, sb);
+            q24_scale(m, v.w, X3, sb);
+            uint32_t* fw = frag + ((size_t)(b * 8 + s) * 4 + cc) * 6 + hh;
+#pragma unroll
+            for (int pl = 0; pl < 3; pl++) {
+                const unsigned sel = (unsigned)pl | ((4u + pl) << 4);
+                const unsigned lo = __byte_perm((unsigned)X0, (unsigned)X1, sel);
+                const unsigned hi = __byte_perm((unsigned)X2, (unsigned)X3, sel);
+                fw[2 * pl] = __byte_perm(lo, hi, 0x5410);
+            }
+            int sx = (X0 + X1) + (X2 + X3);
+            sx += __shfl_xor_sync(FULL, sx, 1);
+            sx += __shfl_xor_sync(FULL, sx, 2);
+            sx += __shfl_xor_sync(FULL, sx, 4);
+            if ((lane & 7) == 0) cbsb[b * 8 + s] = make_int2(8 * sx, __float_as_int(sb));
+        }
+    }
+    mi_sync();
+
+    // ---- this group's tiles: j, j + NG, ... of the CTA's tiles
+    const int j = warp / WG, wg = warp % WG, gt = tid - j * WG * 32;  // group, warp and thread in it
+    const int spg = S / NG;                                            // ring stages per group
+    const int g = lane >> 2, c = lane & 3;  // MMA group (row / session column), thread in group
+    float* rgrp = rbuf + (size_t)j * 2 * WG * MI_RC * 8;
+    int k = 0;  // tiles consumed by the group
+    bool bad = false;
+    for (int q = j; q < mycount; q += NG, k++) {
+        const int st = j + (k % spg) * NG;
+        const bool ok = mbar_wait(&sh.full[st], (unsigned)((k / spg) & 1), GEMV_WAIT_NS);
+        const unsigned char* pay = stages + (size_t)st * stage_b;
+        const unsigned char* scs = pay + (size_t)MI_RC * nb * 16;
+        const long row0 = (blockIdx.x + (long)q * gridDim.x) * MI_RC;
+        const int rows = (int)min((long)MI_RC, (long)a.N - row0);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+        for (int b = wg; b < nb; b += WG) {
+            const unsigned w0 = *reinterpret_cast<const unsigned*>(pay + ((size_t)b * MI_RC + g) * 16 + 4 * c);
+            const unsigned w1 = *reinterpret_cast<const unsigned*>(pay + ((size_t)b * MI_RC + g + 8) * 16 + 4 * c);
+            const float d0 = __half2float(*reinterpret_cast<const __half*>(scs + ((size_t)b * MI_RC + g) * 2));
+            const float d1 = __half2float(*reinterpret_cast<const __half*>(scs + ((size_t)b * MI_RC + g + 8) * 2));
+            const uint32_t* fb = frag + ((size_t)(b * 8 + g) * 4 + c) * 6;
+            const uint2 x0 = *reinterpret_cast<const uint2*>(fb);
+            const uint2 x1 = *reinterpret_cast<const uint2*>(fb + 2);
+            const uint2 x2 = *reinterpret_cast<const uint2*>(fb + 4);
+            const int4 cs = *reinterpret_cast<const int4*>(cbsb + b * 8 + 2 * c);
+            const unsigned af[4] = {w0 & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu,
+                                    (w1 >> 4) & 0x0f0f0f0fu};
+            int D0[4], D1[4], D2[4];
+            mma_u8u8(D0, af, x0.x, x0.y);
+            mma_u8u8(D1, af, x1.x, x1.y);
+            mma_u8s8(D2, af, x2.x, x2.y);
+            const int cb[2] = {cs.x, cs.z};
+            const float sbv[2] = {__int_as_float(cs.y), __int_as_float(cs.w)};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int h = e & 1;
+                const int s01 = D0[e] + (D1[e] << 8) - cb[h];
+                const float T = fmaf((float)D2[e], 65536.0f, (float)s01);
+                acc[e] = fmaf((e < 2 ? d0 : d1) * sbv[h], T, acc[e]);
             }
         }
         // this warp's partial sums: rows g, g + 8 x sessions 2c, 2c + 1
-        float* rw = rb + (size_t)warp * MI_RC * 8;
+        float* rb = rgrp + (size_t)(k & 1) * WG * MI_RC * 8;
+        float* rw = rb + (size_t)wg * MI_RC * 8;
         *reinterpret_cast<float2*>(rw + g * 8 + 2 * c) = make_float2(acc[0], acc[1]);
         *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * c) = make_float2(acc[2], acc[3]);
-        if (__syncthreads_or(!ok)) {  // stage consumed, partial sums complete
-            failed = i + 1;
+        if (mi_group_sync_or(2 + j, WG * 32, !ok)) {  // stage read, partial sums complete
+            bad = true;
             break;
         }
-        if (warp == 0 && i + S < mycount) issue(i + S);
-        // epilogue: fixed-order sum of the 16 warps' partials of each (row, session)
+        if (gt == 0)  // hand the stage back to the producer
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&sh.empty[st]))
+                         : "memory");
+        // epilogue: fixed-order sum of the group's WG partials of each (row, session)
         if constexpr (EPI == EPI_GLU) {
-            if (tid < (MI_RC / 2) * 8) {
-                const int pr = tid >> 3, s = tid & 7, r0 = 2 * pr;
+            if (gt < (MI_RC / 2) * 8) {
+                const int pr = gt >> 3, s = gt & 7, r0 = 2 * pr;
                 if (s < ns && r0 + 1 < rows) {
                     float gv = 0.f, uv = 0.f;
 #pragma unroll
-                    for (int w = 0; w < MG_WARPS; w++) {
+                    for (int w = 0; w < WG; w++) {
                         gv += rb[((size_t)w * MI_RC + r0) * 8 + s];
                         uv += rb[((size_t)w * MI_RC + r0 + 1) * 8 + s];
                     }
@@ -522,12 +599,12 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_mgemm(MgArgs a, int S) {
                 }
             }
         } else {
-            if (tid < MI_RC * 8) {
-                const int r = tid >> 3, s = tid & 7;
+            if (gt < MI_RC * 8) {
+                const int r = gt >> 3, s = gt & 7;
                 if (s < ns && r < rows) {
                     float v = 0.f;
 #pragma unroll
-                    for (int w = 0; w < MG_WARPS; w++) v += rb[((size_t)w * MI_RC + r) * 8 + s];
+                    for (int w = 0; w < WG; w++) v += rb[((size_t)w * MI_RC + r) * 8 + s];
                     const long row = row0 + r;
                     float* yp = a.y + (size_t)s * a.ldy + row;
                     if (EPI == EPI_RESID)
@@ -538,11 +615,18 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_mgemm(MgArgs a, int S) {
             }
         }
     }
-    if (failed && tid == 0) {
+    if (bad && gt == 0) {
+        // record the timeout, stop the producer, and let every tile it issued
+        // into this group's stages land before the group exits (bounded waits)
         atomicExch(a.status, (int)DEV_TIMEOUT);
-        const int issued = min(mycount, failed - 1 + S);
-        for (int i = failed - 1; i < issued; i++)
-            mbar_wait(&bars[i % S], (unsigned)((i / S) & 1), GEMV_WAIT_NS);
+        *reinterpret_cast<volatile int*>(&sh.abort) = 1;
+        const uint64_t t0 = global_ns();
+        while (!ld_volatile_shared(&sh.prod_done) && global_ns() - t0 < GEMV_WAIT_NS) {
+        }
+        const int issued = ld_volatile_shared(&sh.issued);
+        const int mine = issued > j ? (issued - j + NG - 1) / NG : 0;
+        for (int kk = k; kk < mine; kk++)
+            mbar_wait(&sh.full[j + (kk % spg) * NG], (unsigned)((kk / spg) & 1), GEMV_WAIT_NS);
     }
 }
 
@@ -587,18 +671,22 @@ static int mg_go(cw_ctx* ctx, const MgArgs& a, int sets, bool pdl) {
     return CW_OK;
 }
 
-template <int BPW, int PRO, int EPI>
+template <int WG, int PRO, int EPI>
 static int mi_go(cw_ctx* ctx, const MgArgs& a, bool pdl) {
+    constexpr int NG = MG_WARPS / WG;
     const int nb = a.K / 32;
-    const long nchunks = ((long)a.N + MI_RC - 1) / MI_RC;
-    auto kern = k_mgemm<BPW, PRO, EPI>;
-    const size_t stage_b = mi_stage_bytes(nb);
-    const size_t fixed = 128 + (size_t)8 * al16(q24_bytes(nb)) + MI_RED_BYTES + 1024;
-    const long grid_x = std::max<long>(1, std::min<long>(nchunks, ctx->sm_count));
-    const long per_cta = (nchunks + grid_x - 1) / grid_x;
-    const int s_fit = (int)std::min<size_t>(12, ((size_t)ctx->max_smem_optin - fixed) / stage_b);
-    CW_CHECK(s_fit >= 1, CW_ERR_UNSUPPORTED, "mgemm: K=%d tile does not fit shared memory", a.K);
-    const int S = (int)std::max<long>(1, std::min<long>(per_cta, s_fit));
+    CW_CHECK(a.tiles, CW_ERR_INVALID_ARG, "mgemm: no tile-interleaved weight copy");
+    const long ntiles = ((long)a.N + MI_RC - 1) / MI_RC;
+    auto kern = k_mgemm<WG, PRO, EPI>;
+    const size_t stage_b = al128(mi_tile_bytes(nb));
+    // (1 KB kept for the kernel's static shared memory)
+    const size_t fixed = al128(mi_frag_bytes(nb)) + MI_RED_BYTES + 1024;
+    const long grid_x = std::max<long>(1, std::min<long>(ntiles, ctx->sm_count));
+    const long per_cta = (ntiles + grid_x - 1) / grid_x;
+    // ring stages: a multiple of the group count, enough for this CTA's tiles
+    const int s_fit = (int)std::min<size_t>(MI_SMAX, ((size_t)ctx->max_smem_optin - fixed) / stage_b);
+    CW_CHECK(s_fit >= NG, CW_ERR_UNSUPPORTED, "mgemm: K=%d tiles do not fit shared memory", a.K);
+    const int S = (int)std::min<long>(s_fit / NG, (per_cta + NG - 1) / NG) * NG;
     const size_t smem = fixed - 1024 + (size_t)S * stage_b;
     static thread_local std::map<std::pair<int, const void*>, size_t> attr_set;
     const auto key = std::make_pair(ctx->device, (const void*)kern);
@@ -609,7 +697,7 @@ static int mi_go(cw_ctx* ctx, const MgArgs& a, bool pdl) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid_x);
-    cfg.blockDim = dim3(MG_THREADS);
+    cfg.blockDim = dim3(MI_BLOCK);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = ctx->stream;
     cudaLaunchAttribute attr[1];
@@ -626,11 +714,10 @@ static int mi_go(cw_ctx* ctx, const MgArgs& a, bool pdl) {
 template <int PRO, int EPI>
 static int mg_cfg(cw_ctx* ctx, const MgArgs& a, bool pdl) {
     const int nb = a.K / 32;
-    if (a.mma && nb <= 128) {  // the integer tensor-core variant
-        if (nb <= 16) return mi_go<1, PRO, EPI>(ctx, a, pdl);
-        if (nb <= 32) return mi_go<2, PRO, EPI>(ctx, a, pdl);
-        if (nb <= 64) return mi_go<4, PRO, EPI>(ctx, a, pdl);
-        return mi_go<8, PRO, EPI>(ctx, a, pdl);
+    if (a.mma && nb <= 128) {  // integer tensor cores; about 8 blocks per warp and tile
+        if (nb <= 32) return mi_go<4, PRO, EPI>(ctx, a, pdl);
+        if (nb <= 64) return mi_go<8, PRO, EPI>(ctx, a, pdl);
+        return mi_go<16, PRO, EPI>(ctx, a, pdl);
     }
     if (a.B > 4 && nb <= Mg8c::NB_MAX) {
         if (nb <= Mg8a::NB_MAX) return mg_go<Mg8a, PRO, EPI>(ctx, a, 1, pdl);
@@ -658,6 +745,22 @@ int launch_mgemv(cw_ctx* ctx, int pro, int epi, const MgArgs& a, bool pdl) {
     if (pro == PRO_X && epi == EPI_STORE) return mg_cfg<PRO_X, EPI_STORE>(ctx, a, pdl);
     return set_error(CW_ERR_UNSUPPORTED, "mgemv: prologue %d / epilogue %d not instantiated", pro,
                      epi);
+}
+
+}  // namespace cw
+
+namespace cw {
+
+size_t mg_tile_bytes(int rows, int K) {
+    return (size_t)((rows + MI_RC - 1) / MI_RC) * mi_tile_bytes(K / 32);
+}
+
+int mg_tile_pack(cw_ctx* ctx, const uint8_t* payload, const __half* scales, int rows, int K,
+                 void* dst) {
+    CW_CHECK(K % 256 == 0 && rows > 0, CW_ERR_INVALID_ARG, "mg_tile_pack: K=%d rows=%d", K, rows);
+    const int nt = (rows + MI_RC - 1) / MI_RC;
+    k_mg_pack<<<nt, 256, 0, ctx->stream>>>(payload, scales, rows, K / 32, (uint8_t*)dst);
+    return check_launch("mg_tile_pack");
 }
 
 }  // namespace cw

@@ -31,9 +31,19 @@ struct MgArgs {
     int geglu;
     int* status;  // device status word (bounded waits report DEV_TIMEOUT)
     // K <= 4096: run the products on the integer tensor cores (mma.sync
-    // m16n8k32) instead of dp4a; the integer sums are the same
+    // m16n8k32) instead of dp4a; the integer sums are the same.  They read
+    // the weight's tile-interleaved copy (mg_tile_pack).
     int mma;
+    const uint8_t* tiles;
 };
+
+// The tile-interleaved copy of a Q4_0 matrix the integer-MMA products read:
+// per 16-row tile its payload [block][row][16 B], then its scales
+// [block][row] (rows past the end zero).  Bytes for `rows` x K, and the
+// packing kernel (enqueued on ctx->stream).
+size_t mg_tile_bytes(int rows, int K);
+int mg_tile_pack(cw_ctx* ctx, const uint8_t* payload, const __half* scales, int rows, int K,
+                 void* dst);
 
 // Whether the co-batched GEMV takes K for a group of B sessions (K/32 a
 // multiple of 8 and at most 384 blocks; 1 <= B <= 8).

@@ -1477,6 +1477,7 @@ int cw_model_free(cw_model* m) {
         }
     }
     for (void* p : m->packed) cudaFree(p);
+    for (void* p : m->grp_tiles) cudaFree(p);
     delete m;
     return CW_OK;
 }

@@ -85,6 +85,10 @@ struct cw_model {
     // the head) in the tensor-core GEMM's packed Q4_0 tile records
     // (cw_gemm.cu), built on first use by prefill or a session group
     std::vector<void*> packed;
+    // the same matrices in the streaming group step's tile-interleaved form
+    // (cw_mgemv.cu, mg_tile_pack; null where K is beyond its integer-MMA
+    // path), built by the first group that streams
+    std::vector<void*> grp_tiles;
     // tensor parallelism (cw_model_load_gguf_tp): this rank's share of heads,
     // FFN columns and vocabulary; residual-branch sums all-reduced over NCCL
     int tp_rank = 0, tp_world = 1;

@@ -996,10 +996,11 @@ static int grp_enqueue_streaming(cw_group* g) {
         sc.reset();
         if (ctx->profiling) sc.reset(new OpScope(ctx, name));
     };
-    auto mg = [&](const char* name, const QW& w, int pro, int epi, const float* x, int ldx,
-                  const float* norm_w, float* y, int ldy, const float* bias) {
+    auto mg = [&](const char* name, int widx, const QW& w, int pro, int epi, const float* x,
+                  int ldx, const float* norm_w, float* y, int ldy, const float* bias) {
         stage(name);
         MgArgs a{};
+        a.tiles = (const uint8_t*)m->grp_tiles[widx];
         a.payload = w.payload;
         a.scales = w.scales;
         a.K = w.in_f;
@@ -1026,7 +1027,7 @@ static int grp_enqueue_streaming(cw_group* g) {
     CW_TRY(check_launch("group embed"));
     for (uint32_t li = 0; li < I.n_layers; li++) {
         const Layer& l = m->L[li];
-        CW_TRY(mg("group.qkv", l.qkv, PRO_NORM, EPI_STORE, H, dim, l.attn_norm, QKV, qkv_rows,
+        CW_TRY(mg("group.qkv", 4 * li + 0, l.qkv, PRO_NORM, EPI_STORE, H, dim, l.attn_norm, QKV, qkv_rows,
                   l.qkv_bias));
         stage("group.attn");
         {
@@ -1062,12 +1063,12 @@ static int grp_enqueue_streaming(cw_group* g) {
 #undef CW_GAE
 #undef CW_GA
         }
-        CW_TRY(mg("group.o", l.wo, PRO_X, EPI_RESID, X, qd, nullptr, H, dim, nullptr));
-        CW_TRY(mg("group.gate_up", l.gate_up, PRO_NORM, EPI_GLU, H, dim, l.ffn_norm, A, hid,
+        CW_TRY(mg("group.o", 4 * li + 1, l.wo, PRO_X, EPI_RESID, X, qd, nullptr, H, dim, nullptr));
+        CW_TRY(mg("group.gate_up", 4 * li + 2, l.gate_up, PRO_NORM, EPI_GLU, H, dim, l.ffn_norm, A, hid,
                   nullptr));
-        CW_TRY(mg("group.down", l.down, PRO_X, EPI_RESID, A, hid, nullptr, H, dim, nullptr));
+        CW_TRY(mg("group.down", 4 * li + 3, l.down, PRO_X, EPI_RESID, A, hid, nullptr, H, dim, nullptr));
     }
-    CW_TRY(mg("group.head", m->head, PRO_NORM, EPI_STORE, H, dim, m->final_norm, logits,
+    CW_TRY(mg("group.head", 4 * I.n_layers, m->head, PRO_NORM, EPI_STORE, H, dim, m->final_norm, logits,
               (int)I.vocab, nullptr));
     stage("group.finalize");
     CW_TRY(launch_pdl(ctx, true, k_grp_finalize, dim3(B), dim3(SMP_THREADS), 0,
@@ -1086,6 +1087,38 @@ static bool grp_streaming_ok(const cw_model* m, size_t B) {
     const int qd = (int)(I.n_heads * I.head_dim);
     return I.post_norms == 0 && mgemv_supported((int)I.dim, (int)B) &&
            mgemv_supported(qd, (int)B) && mgemv_supported((int)I.hidden, (int)B);
+}
+
+// The tile-interleaved weight copies of the streaming step (model->grp_tiles:
+// 4 per layer, then the head), idempotent; matrices whose K is beyond the
+// integer-MMA path keep a null entry.
+static int model_tile_weights(cw_model* m) {
+    if (!m->grp_tiles.empty()) return CW_OK;
+    cw_ctx* ctx = m->ctx;
+    std::vector<void*> out;
+    auto add = [&](const QW& w) -> int {
+        void* p = nullptr;
+        if (w.in_f / 32 <= 128) {
+            CW_CUDA(cudaMalloc(&p, mg_tile_bytes(w.rows, w.in_f)));
+            out.push_back(p);
+            return mg_tile_pack(ctx, w.payload, w.scales, w.rows, w.in_f, p);
+        }
+        out.push_back(nullptr);
+        return CW_OK;
+    };
+    int rc = CW_OK;
+    for (const Layer& l : m->L)
+        for (const QW* w : {&l.qkv, &l.wo, &l.gate_up, &l.down})
+            if (rc == CW_OK) rc = add(*w);
+    if (rc == CW_OK) rc = add(m->head);
+    if (rc == CW_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess)
+        rc = set_error(CW_ERR_CUDA, "weight tiling failed");
+    if (rc != CW_OK) {
+        for (void* p : out) cudaFree(p);
+        return rc;
+    }
+    m->grp_tiles = out;
+    return CW_OK;
 }
 
 static int grp_enqueue(cw_group* g) {
@@ -1257,7 +1290,7 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
              "cw_group_create: the co-batched step takes Q4_0 projections and LM head");
     cudaSetDevice(ctx->device);
     const bool streaming = grp_streaming_ok(m, n);
-    if (!streaming) CW_TRY(model_pack_weights(m));
+    CW_TRY(streaming ? model_tile_weights(m) : model_pack_weights(m));
     cw_group* g = new cw_group();
     g->m = m;
     g->streaming = streaming;
@@ -1308,7 +1341,7 @@ int cw_group_set_streaming(cw_group* g, int on, int* streaming) {
         cudaSetDevice(ctx->device);
         CW_CHECK(!on || grp_streaming_ok(g->m, g->ss.size()), CW_ERR_UNSUPPORTED,
                  "cw_group_set_streaming: the group does not qualify for the streaming step");
-        if (!on) CW_TRY(model_pack_weights(g->m));
+        CW_TRY(on ? model_tile_weights(g->m) : model_pack_weights(g->m));
         CW_CUDA(cudaStreamSynchronize(ctx->stream));
         if (g->graph) cudaGraphExecDestroy(g->graph);
         g->graph = nullptr;
