@@ -373,7 +373,8 @@ __device__ __forceinline__ bool mi_group_sync_or(int id, int n, bool v) {
 __host__ __device__ constexpr size_t mi_tile_bytes(int nb) { return (size_t)MI_RC * nb * 18; }
 // fragment-major planes: words [nb][8 sessions][4 c][6], then int2 [nb][8]
 __host__ __device__ constexpr size_t mi_frag_bytes(int nb) { return (size_t)nb * (768 + 64); }
-constexpr size_t MI_RED_BYTES = 2 * MG_WARPS * MI_RC * 8 * 4;  // [group][2][warp in group][row][session]
+// row partials [group][2][warp in group][MT * 16 rows][session]
+__host__ __device__ constexpr size_t mi_red_bytes(int MT) { return (size_t)2 * MG_WARPS * MI_RC * MT * 8 * 4; }
 
 struct MiShared {
     uint64_t full[MI_SMAX], empty[MI_SMAX];
@@ -397,9 +398,10 @@ __global__ void k_mg_pack(const uint8_t* __restrict__ payload, const __half* __r
     }
 }
 
-template <int WG, int PRO, int EPI>
+template <int WG, int MT, int PRO, int EPI>
 __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
-    constexpr int NG = MG_WARPS / WG;  // warp groups (tiles in flight per CTA)
+    constexpr int NG = MG_WARPS / WG;  // warp groups (stages being consumed per CTA)
+    constexpr int RS = MI_RC * MT;     // rows per stage: MT MMA tiles
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ MiShared sh;
     __shared__ float red[MG_WARPS];
@@ -408,12 +410,13 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ns = min(8, a.B);
     const long ntiles = ((long)a.N + MI_RC - 1) / MI_RC;
-    const int mycount = blockIdx.x < ntiles ? (int)((ntiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
-    const size_t tile_b = mi_tile_bytes(nb), stage_b = al128(tile_b);
+    const long nstage = (ntiles + MT - 1) / MT;  // stage loads of MT tiles
+    const int mycount = blockIdx.x < nstage ? (int)((nstage - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    const size_t tile_b = mi_tile_bytes(nb), stage_b = al128(MT * tile_b);
     uint32_t* frag = reinterpret_cast<uint32_t*>(smem);
     int2* cbsb = reinterpret_cast<int2*>(smem + (size_t)nb * 768);
     float* rbuf = reinterpret_cast<float*>(smem + al128(mi_frag_bytes(nb)));
-    unsigned char* stages = reinterpret_cast<unsigned char*>(rbuf) + MI_RED_BYTES;
+    unsigned char* stages = reinterpret_cast<unsigned char*>(rbuf) + mi_red_bytes(MT);
 
     if (tid == 0) {
         for (int st = 0; st < S; st++) {
@@ -427,7 +430,7 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
     }
     __syncthreads();
     if (warp == MG_WARPS) {
-        // ---- the producer: tile q into stage q % S once that stage's
+        // ---- the producer: stage load q (MT tiles) into stage q % S once that stage's
         // previous tile (q - S) was released.  The weight stream does not
         // depend on the previous kernel.
         pdl_trigger();
@@ -446,10 +449,11 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
                     }
                     if (!ok) break;
                 }
-                const long tile = blockIdx.x + (long)q * gridDim.x;
-                mbar_expect_tx(&sh.full[st], (unsigned)tile_b);
-                bulk_g2s_hint(stages + (size_t)st * stage_b, a.tiles + (size_t)tile * tile_b,
-                              (unsigned)tile_b, &sh.full[st], pol);
+                const long t0 = (blockIdx.x + (long)q * gridDim.x) * MT;  // first tile
+                const unsigned bytes = (unsigned)(min((long)MT, ntiles - t0) * tile_b);
+                mbar_expect_tx(&sh.full[st], bytes);
+                bulk_g2s_hint(stages + (size_t)st * stage_b, a.tiles + (size_t)t0 * tile_b, bytes,
+                              &sh.full[st], pol);
             }
             sh.issued = q;
             __threadfence_block();
@@ -529,53 +533,65 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
     }
     mi_sync();
 
-    // ---- this group's tiles: j, j + NG, ... of the CTA's tiles
+    // ---- this group's stage loads: j, j + NG, ... of the CTA's
     const int j = warp / WG, wg = warp % WG, gt = tid - j * WG * 32;  // group, warp and thread in it
     const int spg = S / NG;                                            // ring stages per group
     const int g = lane >> 2, c = lane & 3;  // MMA group (row / session column), thread in group
-    float* rgrp = rbuf + (size_t)j * 2 * WG * MI_RC * 8;
+    float* rgrp = rbuf + (size_t)j * 2 * WG * RS * 8;
     int k = 0;  // tiles consumed by the group
     bool bad = false;
     for (int q = j; q < mycount; q += NG, k++) {
         const int st = j + (k % spg) * NG;
         const bool ok = mbar_wait(&sh.full[st], (unsigned)((k / spg) & 1), GEMV_WAIT_NS);
         const unsigned char* pay = stages + (size_t)st * stage_b;
-        const unsigned char* scs = pay + (size_t)MI_RC * nb * 16;
-        const long row0 = (blockIdx.x + (long)q * gridDim.x) * MI_RC;
-        const int rows = (int)min((long)MI_RC, (long)a.N - row0);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const long row0 = (blockIdx.x + (long)q * gridDim.x) * RS;
+        const int rows = (int)min((long)RS, (long)a.N - row0);
+        float acc[MT][4];
+#pragma unroll
+        for (int t = 0; t < MT; t++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[t][e] = 0.f;
 #pragma unroll 2
         for (int b = wg; b < nb; b += WG) {
-            const unsigned w0 = *reinterpret_cast<const unsigned*>(pay + ((size_t)b * MI_RC + g) * 16 + 4 * c);
-            const unsigned w1 = *reinterpret_cast<const unsigned*>(pay + ((size_t)b * MI_RC + g + 8) * 16 + 4 * c);
-            const float d0 = __half2float(*reinterpret_cast<const __half*>(scs + ((size_t)b * MI_RC + g) * 2));
-            const float d1 = __half2float(*reinterpret_cast<const __half*>(scs + ((size_t)b * MI_RC + g + 8) * 2));
+            // the block's B operands, shared by the MT tiles of the stage
             const uint32_t* fb = frag + ((size_t)(b * 8 + g) * 4 + c) * 6;
             const uint2 x0 = *reinterpret_cast<const uint2*>(fb);
             const uint2 x1 = *reinterpret_cast<const uint2*>(fb + 2);
             const uint2 x2 = *reinterpret_cast<const uint2*>(fb + 4);
             const int4 cs = *reinterpret_cast<const int4*>(cbsb + b * 8 + 2 * c);
-            const unsigned af[4] = {w0 & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu,
-                                    (w1 >> 4) & 0x0f0f0f0fu};
-            int D0[4], D1[4], D2[4];
-            mma_u8u8(D0, af, x0.x, x0.y);
-            mma_u8u8(D1, af, x1.x, x1.y);
-            mma_u8s8(D2, af, x2.x, x2.y);
             const int cb[2] = {cs.x, cs.z};
             const float sbv[2] = {__int_as_float(cs.y), __int_as_float(cs.w)};
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int h = e & 1;
-                const int s01 = D0[e] + (D1[e] << 8) - cb[h];
-                const float T = fmaf((float)D2[e], 65536.0f, (float)s01);
-                acc[e] = fmaf((e < 2 ? d0 : d1) * sbv[h], T, acc[e]);
+            for (int t = 0; t < MT; t++) {
+                const unsigned char* tp = pay + (size_t)t * tile_b;  // rows past N: zero tiles
+                const unsigned char* scs = tp + (size_t)MI_RC * nb * 16;
+                const unsigned w0 = *reinterpret_cast<const unsigned*>(tp + ((size_t)b * MI_RC + g) * 16 + 4 * c);
+                const unsigned w1 = *reinterpret_cast<const unsigned*>(tp + ((size_t)b * MI_RC + g + 8) * 16 + 4 * c);
+                const float d0 = __half2float(*reinterpret_cast<const __half*>(scs + ((size_t)b * MI_RC + g) * 2));
+                const float d1 = __half2float(*reinterpret_cast<const __half*>(scs + ((size_t)b * MI_RC + g + 8) * 2));
+                const unsigned af[4] = {w0 & 0x0f0f0f0fu, w1 & 0x0f0f0f0fu, (w0 >> 4) & 0x0f0f0f0fu,
+                                        (w1 >> 4) & 0x0f0f0f0fu};
+                int D0[4], D1[4], D2[4];
+                mma_u8u8(D0, af, x0.x, x0.y);
+                mma_u8u8(D1, af, x1.x, x1.y);
+                mma_u8s8(D2, af, x2.x, x2.y);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int h = e & 1;
+                    const int s01 = D0[e] + (D1[e] << 8) - cb[h];
+                    const float T = fmaf((float)D2[e], 65536.0f, (float)s01);
+                    acc[t][e] = fmaf((e < 2 ? d0 : d1) * sbv[h], T, acc[t][e]);
+                }
             }
         }
-        // this warp's partial sums: rows g, g + 8 x sessions 2c, 2c + 1
-        float* rb = rgrp + (size_t)(k & 1) * WG * MI_RC * 8;
-        float* rw = rb + (size_t)wg * MI_RC * 8;
-        *reinterpret_cast<float2*>(rw + g * 8 + 2 * c) = make_float2(acc[0], acc[1]);
-        *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * c) = make_float2(acc[2], acc[3]);
+        // this warp's partial sums: rows 16t + g, 16t + g + 8 x sessions 2c, 2c + 1
+        float* rb = rgrp + (size_t)(k & 1) * WG * RS * 8;
+        float* rw = rb + (size_t)wg * RS * 8;
+#pragma unroll
+        for (int t = 0; t < MT; t++) {
+            *reinterpret_cast<float2*>(rw + (16 * t + g) * 8 + 2 * c) = make_float2(acc[t][0], acc[t][1]);
+            *reinterpret_cast<float2*>(rw + (16 * t + g + 8) * 8 + 2 * c) = make_float2(acc[t][2], acc[t][3]);
+        }
         if (mi_group_sync_or(2 + j, WG * 32, !ok)) {  // stage read, partial sums complete
             bad = true;
             break;
@@ -585,26 +601,26 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
                          : "memory");
         // epilogue: fixed-order sum of the group's WG partials of each (row, session)
         if constexpr (EPI == EPI_GLU) {
-            if (gt < (MI_RC / 2) * 8) {
+            if (gt < (RS / 2) * 8) {
                 const int pr = gt >> 3, s = gt & 7, r0 = 2 * pr;
                 if (s < ns && r0 + 1 < rows) {
                     float gv = 0.f, uv = 0.f;
 #pragma unroll
                     for (int w = 0; w < WG; w++) {
-                        gv += rb[((size_t)w * MI_RC + r0) * 8 + s];
-                        uv += rb[((size_t)w * MI_RC + r0 + 1) * 8 + s];
+                        gv += rb[((size_t)w * RS + r0) * 8 + s];
+                        uv += rb[((size_t)w * RS + r0 + 1) * 8 + s];
                     }
                     const float act = a.geglu ? gelu_ref_f(gv) : silu_ref_f(gv);
                     a.y[(size_t)s * a.ldy + (row0 + r0) / 2] = act * uv;
                 }
             }
         } else {
-            if (gt < MI_RC * 8) {
-                const int r = gt >> 3, s = gt & 7;
+            for (int o = gt; o < RS * 8; o += WG * 32) {
+                const int r = o >> 3, s = o & 7;
                 if (s < ns && r < rows) {
                     float v = 0.f;
 #pragma unroll
-                    for (int w = 0; w < WG; w++) v += rb[((size_t)w * MI_RC + r) * 8 + s];
+                    for (int w = 0; w < WG; w++) v += rb[((size_t)w * RS + r) * 8 + s];
                     const long row = row0 + r;
                     float* yp = a.y + (size_t)s * a.ldy + row;
                     if (EPI == EPI_RESID)
@@ -671,18 +687,19 @@ static int mg_go(cw_ctx* ctx, const MgArgs& a, int sets, bool pdl) {
     return CW_OK;
 }
 
-template <int WG, int PRO, int EPI>
+template <int WG, int MT, int PRO, int EPI>
 static int mi_go(cw_ctx* ctx, const MgArgs& a, bool pdl) {
     constexpr int NG = MG_WARPS / WG;
     const int nb = a.K / 32;
     CW_CHECK(a.tiles, CW_ERR_INVALID_ARG, "mgemm: no tile-interleaved weight copy");
     const long ntiles = ((long)a.N + MI_RC - 1) / MI_RC;
-    auto kern = k_mgemm<WG, PRO, EPI>;
-    const size_t stage_b = al128(mi_tile_bytes(nb));
+    const long nstage = (ntiles + MT - 1) / MT;
+    auto kern = k_mgemm<WG, MT, PRO, EPI>;
+    const size_t stage_b = al128(MT * mi_tile_bytes(nb));
     // (1 KB kept for the kernel's static shared memory)
-    const size_t fixed = al128(mi_frag_bytes(nb)) + MI_RED_BYTES + 1024;
-    const long grid_x = std::max<long>(1, std::min<long>(ntiles, ctx->sm_count));
-    const long per_cta = (ntiles + grid_x - 1) / grid_x;
+    const size_t fixed = al128(mi_frag_bytes(nb)) + mi_red_bytes(MT) + 1024;
+    const long grid_x = std::max<long>(1, std::min<long>(nstage, ctx->sm_count));
+    const long per_cta = (nstage + grid_x - 1) / grid_x;
     // ring stages: a multiple of the group count, enough for this CTA's tiles
     const int s_fit = (int)std::min<size_t>(MI_SMAX, ((size_t)ctx->max_smem_optin - fixed) / stage_b);
     CW_CHECK(s_fit >= NG, CW_ERR_UNSUPPORTED, "mgemm: K=%d tiles do not fit shared memory", a.K);
@@ -714,10 +731,13 @@ static int mi_go(cw_ctx* ctx, const MgArgs& a, bool pdl) {
 template <int PRO, int EPI>
 static int mg_cfg(cw_ctx* ctx, const MgArgs& a, bool pdl) {
     const int nb = a.K / 32;
-    if (a.mma && nb <= 128) {  // integer tensor cores; about 8 blocks per warp and tile
-        if (nb <= 32) return mi_go<4, PRO, EPI>(ctx, a, pdl);
-        if (nb <= 64) return mi_go<8, PRO, EPI>(ctx, a, pdl);
-        return mi_go<16, PRO, EPI>(ctx, a, pdl);
+    if (a.mma && nb <= 128) {
+        // integer tensor cores: about 8 blocks per warp and tile, and stage
+        // loads of at least ~18 KB (two tiles at K <= 1024): every stage costs
+        // a wait and a group barrier, which small copies do not amortise
+        if (nb <= 32) return mi_go<4, 2, PRO, EPI>(ctx, a, pdl);
+        if (nb <= 64) return mi_go<8, 1, PRO, EPI>(ctx, a, pdl);
+        return mi_go<16, 1, PRO, EPI>(ctx, a, pdl);
     }
     if (a.B > 4 && nb <= Mg8c::NB_MAX) {
         if (nb <= Mg8a::NB_MAX) return mg_go<Mg8a, PRO, EPI>(ctx, a, 1, pdl);
@@ -754,6 +774,7 @@ namespace cw {
 size_t mg_tile_bytes(int rows, int K) {
     return (size_t)((rows + MI_RC - 1) / MI_RC) * mi_tile_bytes(K / 32);
 }
+// (a stage load of MT tiles copies only the tiles that exist)
 
 int mg_tile_pack(cw_ctx* ctx, const uint8_t* payload, const __half* scales, int rows, int K,
                  void* dst) {
