@@ -113,3 +113,28 @@ def test_streaming_8b_layer_shapes(ctx):
         first = len(p) - 1
         assert compare_streams(t_s[i], toks, np.stack(solo[first:]), l_s[i][first:]) >= 1, i
     m.close()
+
+
+def test_streaming_qwen3_0_6b_eight_sessions(ctx):
+    """Benchmark config 3's scaling setup: 8 sessions of the bench's
+    Qwen3-0.6B checkpoint stepped as one group (the streaming path, integer
+    MMA products), each session's logits within 1e-3 relative of its own
+    single-session persistent step and the same greedy tokens."""
+    from chat_wgpu_b200 import gguf
+    from chat_wgpu_b200.model import Model, Session
+    m = Model(ctx, gguf.cached_model("qwen3-0.6b", seed=0))
+    prompts = _prompts(m.info["vocab"], [24, 9, 31, 16, 5, 40, 12, 20], 41)
+    steps = 48
+    t_s, l_s = _run_group(m, prompts, steps, 1, max_seq=96)
+    for i, p in enumerate(prompts):
+        s = Session(m, 96)
+        s.begin(p)
+        solo = []
+        for _ in range(steps):
+            s.run(1)
+            solo.append(s.logits())
+        toks = s.tokens()
+        s.close()
+        first = len(p) - 1
+        assert compare_streams(t_s[i], toks, np.stack(solo[first:]), l_s[i][first:]) >= 3, i
+    m.close()
