@@ -336,6 +336,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_mgemv(MgArgs a, int S) {
 constexpr int MI_RC = 16;                      // rows per tile
 constexpr int MI_BLOCK = MG_THREADS + 32;      // + the producer warp
 constexpr int MI_SMAX = 16;                    // ring stages at most
+constexpr int MI_IB = 4;                       // prologue items per warp and load batch
 
 __device__ __forceinline__ void mma_u8u8(int (&d)[4], const unsigned (&a)[4], unsigned b0,
                                          unsigned b1) {
@@ -488,47 +489,63 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
     }
     {
         // item = (session s, four blocks 4t..4t+3); lane: block 4t + lane/8,
-        // half h = (lane/4) & 1, word c = lane & 3 -> elements 16h + 4c .. +3
+        // half h = (lane/4) & 1, word c = lane & 3 -> elements 16h + 4c .. +3.
+        // Items in batches of MI_IB per warp, every load of a batch issued
+        // before any is used (one L2 round trip per batch, not per item).
         const int nq = nb / 4, items = 8 * nq;
         const int sub = lane >> 3, hh = (lane >> 2) & 1, cc = lane & 3;
-        for (int it = warp; it < items; it += MG_WARPS) {
-            const int s = it / nq, b = 4 * (it - s * nq) + sub, i = b * 32 + 16 * hh + 4 * cc;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (s < ns) {  // warp-uniform
-                v = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)s * a.ldx + i));
+        for (int it0 = warp; it0 < items; it0 += MI_IB * MG_WARPS) {
+            float4 vv[MI_IB], ww[MI_IB];
+#pragma unroll
+            for (int u = 0; u < MI_IB; u++) {
+                const int it = it0 + u * MG_WARPS;
+                const int s = it / nq, b = 4 * (it - s * nq) + sub, i = b * 32 + 16 * hh + 4 * cc;
+                const bool in = it < items && s < ns;  // warp-uniform
+                vv[u] = in ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)s * a.ldx + i))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                if constexpr (PRO == PRO_NORM)
+                    ww[u] = in ? __ldg(reinterpret_cast<const float4*>(a.norm_w + i))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < MI_IB; u++) {
+                const int it = it0 + u * MG_WARPS;
+                if (it >= items) break;  // warp-uniform
+                const int s = it / nq, b = 4 * (it - s * nq) + sub;
+                float4 v = vv[u];
                 if constexpr (PRO == PRO_NORM) {
                     const float inv = inv_s[s];
-                    float4 w = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
+                    float4 w = ww[u];
                     if (a.unit) w = make_float4(1.0f + w.x, 1.0f + w.y, 1.0f + w.z, 1.0f + w.w);
                     v = make_float4(__fmul_rn(__fmul_rn(v.x, inv), w.x), __fmul_rn(__fmul_rn(v.y, inv), w.y),
                                     __fmul_rn(__fmul_rn(v.z, inv), w.z), __fmul_rn(__fmul_rn(v.w, inv), w.w));
                 }
-            }
-            // block max and integer sum over the block's 8 lanes (q24_quad's scheme)
-            unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
-                             max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
-            m = max(m, __shfl_xor_sync(FULL, m, 1));
-            m = max(m, __shfl_xor_sync(FULL, m, 2));
-            m = max(m, __shfl_xor_sync(FULL, m, 4));
-            int X0, X1, X2, X3;
-            float sb;
-            q24_scale(m, v.x, X0, sb);
-            q24_scale(m, v.y, X1, sb);
-            q24_scale(m, v.z, X2, sb);
-            q24_scale(m, v.w, X3, sb);
-            uint32_t* fw = frag + ((size_t)(b * 8 + s) * 4 + cc) * 6 + hh;
+                // block max and integer sum over the block's 8 lanes (q24_quad's scheme)
+                unsigned m = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                                 max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+                m = max(m, __shfl_xor_sync(FULL, m, 1));
+                m = max(m, __shfl_xor_sync(FULL, m, 2));
+                m = max(m, __shfl_xor_sync(FULL, m, 4));
+                int X0, X1, X2, X3;
+                float sb;
+                q24_scale(m, v.x, X0, sb);
+                q24_scale(m, v.y, X1, sb);
+                q24_scale(m, v.z, X2, sb);
+                q24_scale(m, v.w, X3, sb);
+                uint32_t* fw = frag + ((size_t)(b * 8 + s) * 4 + cc) * 6 + hh;
 #pragma unroll
-            for (int pl = 0; pl < 3; pl++) {
-                const unsigned sel = (unsigned)pl | ((4u + pl) << 4);
-                const unsigned lo = __byte_perm((unsigned)X0, (unsigned)X1, sel);
-                const unsigned hi = __byte_perm((unsigned)X2, (unsigned)X3, sel);
-                fw[2 * pl] = __byte_perm(lo, hi, 0x5410);
+                for (int pl = 0; pl < 3; pl++) {
+                    const unsigned sel = (unsigned)pl | ((4u + pl) << 4);
+                    const unsigned lo = __byte_perm((unsigned)X0, (unsigned)X1, sel);
+                    const unsigned hi = __byte_perm((unsigned)X2, (unsigned)X3, sel);
+                    fw[2 * pl] = __byte_perm(lo, hi, 0x5410);
+                }
+                int sx = (X0 + X1) + (X2 + X3);
+                sx += __shfl_xor_sync(FULL, sx, 1);
+                sx += __shfl_xor_sync(FULL, sx, 2);
+                sx += __shfl_xor_sync(FULL, sx, 4);
+                if ((lane & 7) == 0) cbsb[b * 8 + s] = make_int2(8 * sx, __float_as_int(sb));
             }
-            int sx = (X0 + X1) + (X2 + X3);
-            sx += __shfl_xor_sync(FULL, sx, 1);
-            sx += __shfl_xor_sync(FULL, sx, 2);
-            sx += __shfl_xor_sync(FULL, sx, 4);
-            if ((lane & 7) == 0) cbsb[b * 8 + s] = make_int2(8 * sx, __float_as_int(sb));
         }
     }
     mi_sync();
@@ -540,6 +557,7 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
     float* rgrp = rbuf + (size_t)j * 2 * WG * RS * 8;
     int k = 0;  // tiles consumed by the group
     bool bad = false;
+    unsigned long long best = argmax_key_init();  // EPI_HEAD: this thread's session's best key
     for (int q = j; q < mycount; q += NG, k++) {
         const int st = j + (k % spg) * NG;
         const bool ok = mbar_wait(&sh.full[st], (unsigned)((k / spg) & 1), GEMV_WAIT_NS);
@@ -622,13 +640,36 @@ __global__ void __launch_bounds__(MI_BLOCK, 1) k_mgemm(MgArgs a, int S) {
 #pragma unroll
                     for (int w = 0; w < WG; w++) v += rb[((size_t)w * RS + r) * 8 + s];
                     const long row = row0 + r;
-                    float* yp = a.y + (size_t)s * a.ldy + row;
-                    if (EPI == EPI_RESID)
-                        *yp = *yp + v;
-                    else
-                        *yp = a.bias ? v + a.bias[row] : v;
+                    if constexpr (EPI == EPI_HEAD) {
+                        if (a.softcap > 0.f) v = a.softcap * tanhf(v / a.softcap);
+                        a.yrow[s][row] = v;
+                        const unsigned long long kk = argmax_key(v, (unsigned)row);
+                        best = kk > best ? kk : best;
+                    } else {
+                        float* yp = a.y + (size_t)s * a.ldy + row;
+                        if (EPI == EPI_RESID)
+                            *yp = *yp + v;
+                        else
+                            *yp = a.bias ? v + a.bias[row] : v;
+                    }
                 }
             }
+        }
+    }
+    if constexpr (EPI == EPI_HEAD) {
+        // per session: the CTA's best argmax key (the threads of session s
+        // are those with tid % 8 == s), one atomicMax per session and CTA
+        __shared__ unsigned long long kbuf[MG_WARPS][8];
+        unsigned long long t8 = __shfl_xor_sync(FULL, best, 8);
+        best = t8 > best ? t8 : best;
+        t8 = __shfl_xor_sync(FULL, best, 16);
+        best = t8 > best ? t8 : best;
+        if (lane < 8) kbuf[warp][lane] = best;
+        mi_sync();
+        if (tid < ns && !bad) {
+            unsigned long long kk = kbuf[0][tid];
+            for (int w = 1; w < MG_WARPS; w++) kk = kbuf[w][tid] > kk ? kbuf[w][tid] : kk;
+            atomicMax(a.keys + tid, kk);
         }
     }
     if (bad && gt == 0) {
@@ -739,16 +780,20 @@ static int mg_cfg(cw_ctx* ctx, const MgArgs& a, bool pdl) {
         if (nb <= 64) return mi_go<8, 1, PRO, EPI>(ctx, a, pdl);
         return mi_go<16, 1, PRO, EPI>(ctx, a, pdl);
     }
-    if (a.B > 4 && nb <= Mg8c::NB_MAX) {
-        if (nb <= Mg8a::NB_MAX) return mg_go<Mg8a, PRO, EPI>(ctx, a, 1, pdl);
-        if (nb <= Mg8b::NB_MAX) return mg_go<Mg8b, PRO, EPI>(ctx, a, 1, pdl);
-        return mg_go<Mg8c, PRO, EPI>(ctx, a, 1, pdl);
+    if constexpr (EPI == EPI_HEAD) {
+        return set_error(CW_ERR_UNSUPPORTED, "mgemv: the head epilogue needs the integer-MMA path");
+    } else {
+        if (a.B > 4 && nb <= Mg8c::NB_MAX) {
+            if (nb <= Mg8a::NB_MAX) return mg_go<Mg8a, PRO, EPI>(ctx, a, 1, pdl);
+            if (nb <= Mg8b::NB_MAX) return mg_go<Mg8b, PRO, EPI>(ctx, a, 1, pdl);
+            return mg_go<Mg8c, PRO, EPI>(ctx, a, 1, pdl);
+        }
+        const int sets = (a.B + 3) / 4;
+        if (nb <= Mg4a::NB_MAX) return mg_go<Mg4a, PRO, EPI>(ctx, a, sets, pdl);
+        if (nb <= Mg4b::NB_MAX) return mg_go<Mg4b, PRO, EPI>(ctx, a, sets, pdl);
+        if (nb <= Mg4c::NB_MAX) return mg_go<Mg4c, PRO, EPI>(ctx, a, sets, pdl);
+        return mg_go<Mg4d, PRO, EPI>(ctx, a, sets, pdl);
     }
-    const int sets = (a.B + 3) / 4;
-    if (nb <= Mg4a::NB_MAX) return mg_go<Mg4a, PRO, EPI>(ctx, a, sets, pdl);
-    if (nb <= Mg4b::NB_MAX) return mg_go<Mg4b, PRO, EPI>(ctx, a, sets, pdl);
-    if (nb <= Mg4c::NB_MAX) return mg_go<Mg4c, PRO, EPI>(ctx, a, sets, pdl);
-    return mg_go<Mg4d, PRO, EPI>(ctx, a, sets, pdl);
 }
 
 bool mgemv_supported(int K, int B) {
@@ -763,6 +808,7 @@ int launch_mgemv(cw_ctx* ctx, int pro, int epi, const MgArgs& a, bool pdl) {
     if (pro == PRO_NORM && epi == EPI_GLU) return mg_cfg<PRO_NORM, EPI_GLU>(ctx, a, pdl);
     if (pro == PRO_X && epi == EPI_RESID) return mg_cfg<PRO_X, EPI_RESID>(ctx, a, pdl);
     if (pro == PRO_X && epi == EPI_STORE) return mg_cfg<PRO_X, EPI_STORE>(ctx, a, pdl);
+    if (pro == PRO_NORM && epi == EPI_HEAD) return mg_cfg<PRO_NORM, EPI_HEAD>(ctx, a, pdl);
     return set_error(CW_ERR_UNSUPPORTED, "mgemv: prologue %d / epilogue %d not instantiated", pro,
                      epi);
 }

@@ -35,6 +35,12 @@ struct MgArgs {
     // the weight's tile-interleaved copy (mg_tile_pack).
     int mma;
     const uint8_t* tiles;
+    // EPI_HEAD (integer-MMA path): logits cap * tanh(l / cap) (softcap > 0)
+    // stored to yrow[s][row], and each session's argmax key (ties to the
+    // lowest row, argmax.wgsl) atomicMax'ed into keys[s]
+    float* const* yrow;
+    unsigned long long* keys;
+    float softcap;
 };
 
 // The tile-interleaved copy of a Q4_0 matrix the integer-MMA products read:
@@ -49,7 +55,7 @@ int mg_tile_pack(cw_ctx* ctx, const uint8_t* payload, const __half* scales, int 
 // multiple of 8 and at most 384 blocks; 1 <= B <= 8).
 bool mgemv_supported(int K, int B);
 // Launch on ctx->stream (pro: PRO_X / PRO_NORM, epi: EPI_STORE / EPI_RESID /
-// EPI_GLU of cw_gemv.cuh).
+// EPI_GLU / EPI_HEAD of cw_gemv.cuh).
 int launch_mgemv(cw_ctx* ctx, int pro, int epi, const MgArgs& a, bool pdl);
 
 }  // namespace cw

@@ -22,6 +22,7 @@
 // (cw_gemm.cuh); each weight matrix is split into its f16 pair once per
 // chunk, into a session scratch reused across layers.
 #include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 #include <cmath>
@@ -889,8 +890,50 @@ __global__ void __launch_bounds__(SMP_THREADS) k_grp_finalize(const GrpRow* __re
     }
 }
 
+// The streaming path's finalize: the head GEMV already stored each session's
+// soft-capped logits and reduced its argmax key into keys[r]; here the
+// generate-loop bookkeeping of each session (mod.rs:114-122) with sampling
+// and stop tokens as cw_sample.cu applies them, and the key reset for the
+// next step.
+__global__ void __launch_bounds__(SMP_THREADS) k_grp_finalize_keys(const GrpRow* __restrict__ rows,
+                                                                   unsigned long long* keys, int V) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ SmpShared S;
+    const GrpRow R = rows[blockIdx.x];
+    const unsigned amax = argmax_key_index(keys[blockIdx.x]);
+    DevState* st = R.st;
+    const int pos = st->pos;
+    __syncthreads();
+    if (threadIdx.x == 0) keys[blockIdx.x] = argmax_key_init();
+    if (pos + 1 < st->n_prompt) {  // a prompt position: the next input is the next prompt token
+        if (threadIdx.x == 0) {
+            st->token = R.prompt[pos + 1];
+            st->pos = pos + 1;
+        }
+        return;
+    }
+    const SampleParams p = *R.smp;
+    const int np = st->n_produced;
+    const unsigned t = sample_core(S, R.logits, V, p, (unsigned long long)np, amax);
+    if (threadIdx.x == 0) {
+        if (!st->stopped) {
+            bool eos = false;
+            for (unsigned j = 0; j < p.n_eos; j++) eos |= p.eos[j] == t;
+            if (eos) {
+                st->stopped = 1;
+            } else {
+                R.toks[np] = t;
+                st->n_produced = np + 1;
+            }
+        }
+        st->token = t;
+        st->pos = pos + 1;
+    }
+}
+
 struct GrpLayout {
-    size_t H, T, QKV, G, xh, xl, X, logits, ws, part, ctr, total;
+    size_t H, T, QKV, G, xh, xl, X, logits, ws, part, ctr, yrow, keys, total;
 };
 
 // Key splits of the group attention: about two CTAs per SM over all rows and
@@ -922,6 +965,8 @@ GrpLayout grp_layout(const cw_model* m, size_t B) {
     L.logits = take(B * (size_t)I.vocab * 4);
     L.part = take(B * (size_t)I.n_heads * 16 * (I.head_dim + 2) * 4);  // up to 16 splits
     L.ctr = take(B * (size_t)I.n_kv * 4);  // merge counters (zero, self-resetting)
+    L.yrow = take(B * sizeof(float*));     // each session's logits buffer (streaming head)
+    L.keys = take(B * 8);                  // each session's argmax key (streaming head)
     L.total = o;
     return L;
 }
@@ -1067,6 +1112,36 @@ static int grp_enqueue_streaming(cw_group* g) {
         CW_TRY(mg("group.gate_up", 4 * li + 2, l.gate_up, PRO_NORM, EPI_GLU, H, dim, l.ffn_norm, A, hid,
                   nullptr));
         CW_TRY(mg("group.down", 4 * li + 3, l.down, PRO_X, EPI_RESID, A, hid, nullptr, H, dim, nullptr));
+    }
+    if (dim / 32 <= 128) {
+        // the head's epilogue soft-caps, stores each session's logits and
+        // reduces its argmax key; finalize only does the bookkeeping (and
+        // samples where a session asks for it)
+        stage("group.head");
+        MgArgs a{};
+        a.tiles = (const uint8_t*)m->grp_tiles[4 * I.n_layers];
+        a.payload = m->head.payload;
+        a.scales = m->head.scales;
+        a.K = m->head.in_f;
+        a.N = m->head.rows;
+        a.B = B;
+        a.x = H;
+        a.ldx = dim;
+        a.norm_w = m->final_norm;
+        a.eps = I.eps;
+        a.unit = unit;
+        a.status = ctx->d_status;
+        a.mma = 1;
+        a.yrow = (float* const*)(b + L.yrow);
+        a.keys = (unsigned long long*)(b + L.keys);
+        a.softcap = I.final_softcap;
+        CW_TRY(launch_mgemv(ctx, PRO_NORM, EPI_HEAD, a, true));
+        CW_TRY(check_launch("group head"));
+        stage("group.finalize");
+        CW_TRY(launch_pdl(ctx, true, k_grp_finalize_keys, dim3(B), dim3(SMP_THREADS), 0,
+                          (const GrpRow*)g->rows, (unsigned long long*)(b + L.keys), (int)I.vocab));
+        sc.reset();
+        return check_launch("group finalize");
     }
     CW_TRY(mg("group.head", 4 * I.n_layers, m->head, PRO_NORM, EPI_STORE, H, dim, m->final_norm, logits,
               (int)I.vocab, nullptr));
@@ -1297,18 +1372,32 @@ int cw_group_create(cw_session* const* sessions, size_t n, cw_group** out) {
     g->n_splits = grp_splits(m, n, ctx->sm_count);
     g->ss.assign(sessions, sessions + n);
     std::vector<GrpRow> h(n);
+    std::vector<float*> yrow(n);
+    // argmax_key_init(): the reference's start value -3.402823e38 at index 0
+    // (argmax.wgsl:23), as the order-preserving key of cw_device.cuh
+    float start = -3.402823e38f;
+    uint32_t sbits;
+    memcpy(&sbits, &start, 4);
+    const uint64_t kinit = ((uint64_t)(~sbits) << 32) | 0xffffffffull;
+    std::vector<uint64_t> keys(n, kinit);
     for (size_t i = 0; i < n; i++) {
         cw_session* s = sessions[i];
         h[i] = GrpRow{s->st, s->prompt, s->toks, s->logits, (const SampleParams*)s->smp_dev,
                       s->kc, s->vc, (int)s->max_seq, 0};
+        yrow[i] = s->logits;
     }
+    const GrpLayout L = grp_layout(m, n);
     int rc = CW_OK;
     if (cudaMalloc(&g->rows, n * sizeof(GrpRow)) != cudaSuccess ||
-        cudaMalloc(&g->mem, grp_layout(m, n).total) != cudaSuccess)
+        cudaMalloc(&g->mem, L.total) != cudaSuccess)
         rc = set_error(CW_ERR_OOM, "cw_group_create: device allocation failed");
     if (rc == CW_OK &&
-        (cudaMemsetAsync(g->mem, 0, grp_layout(m, n).total, ctx->stream) != cudaSuccess ||
+        (cudaMemsetAsync(g->mem, 0, L.total, ctx->stream) != cudaSuccess ||
          cudaMemcpyAsync(g->rows, h.data(), n * sizeof(GrpRow), cudaMemcpyHostToDevice,
+                         ctx->stream) != cudaSuccess ||
+         cudaMemcpyAsync((uint8_t*)g->mem + L.yrow, yrow.data(), n * sizeof(float*),
+                         cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess ||
+         cudaMemcpyAsync((uint8_t*)g->mem + L.keys, keys.data(), n * 8, cudaMemcpyHostToDevice,
                          ctx->stream) != cudaSuccess ||
          cudaStreamSynchronize(ctx->stream) != cudaSuccess))
         rc = set_error(CW_ERR_CUDA, "cw_group_create: upload failed");
