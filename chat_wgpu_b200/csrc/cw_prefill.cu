@@ -668,6 +668,11 @@ int session_prefill(cw_session* s, size_t* n_done) {
 namespace cw {
 namespace {
 
+// A plain (uncached) read of a word another kernel may be writing.
+__device__ __forceinline__ int ld_volatile_global(const int* p) {
+    return *reinterpret_cast<const volatile int*>(p);
+}
+
 struct GrpRow {
     DevState* st;
     const unsigned* prompt;
@@ -706,20 +711,37 @@ __global__ void __launch_bounds__(128) k_grp_fattn(
     float scale, float softcap, float* __restrict__ part, unsigned* __restrict__ counters,
     __half* __restrict__ xh, __half* __restrict__ xl, float* __restrict__ xo) {
     pdl_trigger();
-    pdl_wait();
     extern __shared__ float sm[];
     const int split = blockIdx.x, g = blockIdx.y, r = blockIdx.z;
     const int G = nh / nkv, W = hd + 2, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const GrpRow R = rows[r];
+    const GrpRow R = rows[r];  // the row table does not change while a group steps
+    const size_t lstride = (size_t)nkv * R.max_seq * hd;
+    float* kbase = R.kc + li * lstride + (size_t)g * R.max_seq * hd;
+    float* vbase = R.vc + li * lstride + (size_t)g * R.max_seq * hd;
+    if (threadIdx.x == 0) {
+        // while the QKV projection runs: pull this split's cached K/V rows
+        // into L2.  The position may still be the previous step's (a hint
+        // only; the range stays inside the cache), the real one is read
+        // after the wait.
+        const int hpos = min(max(ld_volatile_global(&R.st->pos), 0), R.max_seq - 1), hseq = hpos + 1;
+        const int hact = attn_active_splits(attn_span(hseq, window), n_splits);
+        if (split < hact) {
+            int a0, a1;
+            attn_range(hseq, window, split, hact, &a0, &a1);
+            a1 = min(a1, hpos);
+            if (a1 > a0) {
+                prefetch_l2(kbase + (size_t)a0 * hd, kbase + (size_t)a1 * hd);
+                prefetch_l2(vbase + (size_t)a0 * hd, vbase + (size_t)a1 * hd);
+            }
+        }
+    }
+    pdl_wait();
     const int pos = R.st->pos, seq = pos + 1;
     const int n_active = attn_active_splits(attn_span(seq, window), n_splits);
     if (split >= n_active) return;
     int jlo, jhi;
     attn_range(seq, window, split, n_active, &jlo, &jhi);
     const bool holds = pos >= jlo && pos < jhi;
-    const size_t lstride = (size_t)nkv * R.max_seq * hd;
-    float* kbase = R.kc + li * lstride + (size_t)g * R.max_seq * hd;
-    float* vbase = R.vc + li * lstride + (size_t)g * R.max_seq * hd;
     float* qs = sm + attn_smem_floats(G, hd, n_splits);  // [G][hd]
     float* ks = qs + (size_t)G * hd;                     // [hd]
     const float* row = QKV + (size_t)r * ld;
@@ -936,10 +958,10 @@ struct GrpLayout {
     size_t H, T, QKV, G, xh, xl, X, logits, ws, part, ctr, yrow, keys, total;
 };
 
-// Key splits of the group attention: about two CTAs per SM over all rows and
+// Key splits of the group attention: about four CTAs per SM over all rows and
 // kv heads (at most 16).
 int grp_splits(const cw_model* m, size_t B, int sm_count) {
-    const int per = (int)(2 * sm_count / std::max<size_t>(1, B * m->info.n_kv));
+    const int per = (int)(4 * sm_count / std::max<size_t>(1, B * m->info.n_kv));
     return std::max(1, std::min(16, per));
 }
 
