@@ -773,11 +773,28 @@ template <int PRO, int EPI>
 static int mg_cfg(cw_ctx* ctx, const MgArgs& a, bool pdl) {
     const int nb = a.K / 32;
     if (a.mma && nb <= 128) {
-        // integer tensor cores: about 8 blocks per warp and tile, and stage
-        // loads of at least ~18 KB (two tiles at K <= 1024): every stage costs
-        // a wait and a group barrier, which small copies do not amortise
-        if (nb <= 32) return mi_go<4, 2, PRO, EPI>(ctx, a, pdl);
-        if (nb <= 64) return mi_go<8, 1, PRO, EPI>(ctx, a, pdl);
+        // integer tensor cores.  Stage loads of at least ~18 KB (two tiles at
+        // K <= 1024): every stage costs a wait and a group barrier, which
+        // small copies do not amortise.  Warp groups sized by the stage loads
+        // a CTA gets: all 16 warps on one load (the per-layer projections,
+        // one or two loads per CTA), 8 on each of two, 4 on each of four
+        // (the LM head's long stream)
+        const int mt = nb <= 32 ? 2 : 1;
+        const long nstage = ((long)a.N + MI_RC * mt - 1) / (MI_RC * mt);
+        const long per_cta = (nstage + ctx->sm_count - 1) / ctx->sm_count;
+        int wg = per_cta >= 4 ? 4 : per_cta >= 2 ? 8 : 16;
+        // at least one ring stage per group must fit beside the planes
+        const size_t stage_b = al128(mt * mi_tile_bytes(nb));
+        const size_t fixed = al128(mi_frag_bytes(nb)) + mi_red_bytes(mt) + 1024;
+        const long s_fit = ((long)ctx->max_smem_optin - (long)fixed) / (long)stage_b;
+        while (wg < 16 && MG_WARPS / wg > s_fit) wg *= 2;
+        if (mt == 2) {
+            if (wg == 4) return mi_go<4, 2, PRO, EPI>(ctx, a, pdl);
+            if (wg == 8) return mi_go<8, 2, PRO, EPI>(ctx, a, pdl);
+            return mi_go<16, 2, PRO, EPI>(ctx, a, pdl);
+        }
+        if (wg == 4) return mi_go<4, 1, PRO, EPI>(ctx, a, pdl);
+        if (wg == 8) return mi_go<8, 1, PRO, EPI>(ctx, a, pdl);
         return mi_go<16, 1, PRO, EPI>(ctx, a, pdl);
     }
     if constexpr (EPI == EPI_HEAD) {
