@@ -366,6 +366,227 @@ __global__ void __launch_bounds__(256) k_pf_fattn(const float* __restrict__ QKV,
     }
 }
 
+// ---- causal prefill attention on the tensor cores (head_dim 128) ----------------
+// The same attention as k_pf_fattn (online softmax per query row, the
+// attention.wgsl merge rule) with both products on the warp-level f16 MMA
+// (mma.sync m16n8k16, f32 accumulation).  f16 alone misses the 1e-3 gate, so
+// every operand is split into an f16 pair x = xh + xl (xl = f16(x - xh),
+// ~22 bits together) and each product takes three MMAs, hh + hl + lh (the
+// dropped ll term is 2^-22 relative): S = QK^T from the Q and K pairs, then
+// O += P V from the probabilities P (split in registers straight from the S
+// accumulators: the m16n8 C layout of two key tiles is the m16n8k16 A layout)
+// and the V pair.  CTA: 64 query rows of one head, 4 warps of 16 rows; keys in
+// tiles of 64, converted from the f32 cache into f16 pairs in shared memory
+// (rows padded by 16 bytes: the ldmatrix row addresses of a fragment fall in
+// distinct banks).  No soft-cap or window (those layers keep k_pf_fattn).
+constexpr int PTC_BQ = 64, PTC_BK = 64, PTC_HD = 128, PTC_P = PTC_HD + 8;  // row pitch, halves
+constexpr size_t PTC_SMEM = (size_t)6 * 64 * PTC_P * sizeof(__half);     // Qh Ql Kh Kl Vh Vl
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const __half* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const __half* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+// f32 pair -> (hi, lo) f16 pairs
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    hi = h2_bits(h);
+    lo = h2_bits(__floats2half2_rn(a - hf.x, b - hf.y));
+}
+// four f32 -> hi / lo f16 stores (8-byte aligned)
+__device__ __forceinline__ void split_store4(const float4& v, __half* hi, __half* lo) {
+    uint32_t h0, l0, h1, l1;
+    split_h2(v.x, v.y, h0, l0);
+    split_h2(v.z, v.w, h1, l1);
+    *reinterpret_cast<uint2*>(hi) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(lo) = make_uint2(l0, l1);
+}
+
+__global__ void __launch_bounds__(128) k_pf_attn_tc(const float* __restrict__ QKV, int ld,
+                                                    const float* __restrict__ kc,
+                                                    const float* __restrict__ vc, int max_seq,
+                                                    int p0, int C, int nh, int nkv, float scale,
+                                                    __half* __restrict__ xh,
+                                                    __half* __restrict__ xl) {
+    extern __shared__ __align__(16) __half ptc[];
+    __half* Qh = ptc;
+    __half* Ql = Qh + 64 * PTC_P;
+    __half* Kh = Ql + 64 * PTC_P;
+    __half* Kl = Kh + 64 * PTC_P;
+    __half* Vh = Kl + 64 * PTC_P;
+    __half* Vl = Vh + 64 * PTC_P;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, c = lane & 3;
+    // longest rows (latest positions) first: the causal work grows with the row
+    const int r0 = (gridDim.x - 1 - blockIdx.x) * PTC_BQ;
+    const int h = blockIdx.y, kvh = h / (nh / nkv);
+    const int nrows = min(PTC_BQ, C - r0);
+    for (int i = tid; i < 64 * 32; i += 128) {  // Q rows (normed, roped) -> f16 pairs
+        const int r = i >> 5, c4 = i & 31;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < nrows)
+            v = *reinterpret_cast<const float4*>(QKV + (size_t)(r0 + r) * ld + (size_t)h * PTC_HD + 4 * c4);
+        split_store4(v, Qh + r * PTC_P + 4 * c4, Ql + r * PTC_P + 4 * c4);
+    }
+    const int pos_first = p0 + r0, j_end = p0 + r0 + nrows;  // keys [0, j_end)
+    const int rw = warp * 16;                                 // this warp's first row
+    const int pos_g = pos_first + rw + g, pos_g8 = pos_g + 8;
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = REF_NEG_INF, m1 = REF_NEG_INF, l0 = 0.f, l1 = 0.f;
+    const float* kb = kc + (size_t)kvh * max_seq * PTC_HD;
+    const float* vb = vc + (size_t)kvh * max_seq * PTC_HD;
+    // ldmatrix row addresses (thread t: matrix t / 8, row t % 8)
+    const int lrow = (lane & 7) + 8 * ((lane >> 3) & 1), lcol = 8 * (lane >> 4);
+    for (int kt = 0; kt < j_end; kt += PTC_BK) {
+        __syncthreads();  // the previous tile's K, V consumed (and Q stored, first time)
+#pragma unroll 4
+        for (int i = tid; i < 64 * 32; i += 128) {
+            const int r = i >> 5, c4 = i & 31;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (kt + r < j_end) {
+                kv = __ldg(reinterpret_cast<const float4*>(kb + (size_t)(kt + r) * PTC_HD) + c4);
+                vv = __ldg(reinterpret_cast<const float4*>(vb + (size_t)(kt + r) * PTC_HD) + c4);
+            }
+            split_store4(kv, Kh + r * PTC_P + 4 * c4, Kl + r * PTC_P + 4 * c4);
+            split_store4(vv, Vh + r * PTC_P + 4 * c4, Vl + r * PTC_P + 4 * c4);
+        }
+        __syncthreads();
+        // ---- S = Q K^T over the tile: 8 key tiles of 8, hd in 8 steps of 16
+        float sacc[8][4];
+#pragma unroll
+        for (int n = 0; n < 8; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 8; ks++) {
+            uint32_t qh[4], ql[4];
+            ldsm_x4(qh, Qh + (rw + lrow) * PTC_P + ks * 16 + lcol);
+            ldsm_x4(ql, Ql + (rw + lrow) * PTC_P + ks * 16 + lcol);
+#pragma unroll
+            for (int np = 0; np < 4; np++) {
+                // keys np*16 + (t%8) + 8*(t/16), hd ks*16 + 8*((t/8)%2): matrices
+                // (n-tile 2np: b0, b1), (n-tile 2np+1: b0, b1)
+                const int krow = np * 16 + (lane & 7) + 8 * (lane >> 4), kcol = ks * 16 + 8 * ((lane >> 3) & 1);
+                uint32_t khf[4], klf[4];
+                ldsm_x4(khf, Kh + krow * PTC_P + kcol);
+                ldsm_x4(klf, Kl + krow * PTC_P + kcol);
+                mma_f16(sacc[2 * np], qh, khf[0], khf[1]);
+                mma_f16(sacc[2 * np], qh, klf[0], klf[1]);
+                mma_f16(sacc[2 * np], ql, khf[0], khf[1]);
+                mma_f16(sacc[2 * np + 1], qh, khf[2], khf[3]);
+                mma_f16(sacc[2 * np + 1], qh, klf[2], klf[3]);
+                mma_f16(sacc[2 * np + 1], ql, khf[2], khf[3]);
+            }
+        }
+        // ---- online softmax: this thread's rows g and g + 8, keys 8n + 2c, +1
+        float mx0 = REF_NEG_INF, mx1 = REF_NEG_INF;
+#pragma unroll
+        for (int n = 0; n < 8; n++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int key = kt + 8 * n + 2 * c + e;
+                const float v0 = sacc[n][e] * scale, v1 = sacc[n][2 + e] * scale;
+                sacc[n][e] = key <= pos_g && key < j_end ? v0 : REF_NEG_INF;
+                sacc[n][2 + e] = key <= pos_g8 && key < j_end ? v1 : REF_NEG_INF;
+                mx0 = fmaxf(mx0, sacc[n][e]);
+                mx1 = fmaxf(mx1, sacc[n][2 + e]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        // a row with no key yet in this tile keeps its state (its keys start at 0)
+        const float c0 = mn0 == REF_NEG_INF ? 1.f : expf(m0 - mn0);
+        const float c1 = mn1 == REF_NEG_INF ? 1.f : expf(m1 - mn1);
+        float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+        for (int n = 0; n < 8; n++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const float p0v = sacc[n][e] == REF_NEG_INF ? 0.f : expf(sacc[n][e] - mn0);
+                const float p1v = sacc[n][2 + e] == REF_NEG_INF ? 0.f : expf(sacc[n][2 + e] - mn1);
+                sacc[n][e] = p0v;
+                sacc[n][2 + e] = p1v;
+                ps0 += p0v;
+                ps1 += p1v;
+            }
+        }
+        ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
+        ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
+        ps1 += __shfl_xor_sync(0xffffffffu, ps1, 1);
+        ps1 += __shfl_xor_sync(0xffffffffu, ps1, 2);
+        l0 = l0 * c0 + ps0;
+        l1 = l1 * c1 + ps1;
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int n = 0; n < 16; n++) {
+            o[n][0] *= c0;
+            o[n][1] *= c0;
+            o[n][2] *= c1;
+            o[n][3] *= c1;
+        }
+        // ---- O += P V: keys in 4 steps of 16, hd in 16 tiles of 8
+#pragma unroll
+        for (int k2 = 0; k2 < 4; k2++) {
+            uint32_t ph[4], pl[4];
+            split_h2(sacc[2 * k2][0], sacc[2 * k2][1], ph[0], pl[0]);
+            split_h2(sacc[2 * k2][2], sacc[2 * k2][3], ph[1], pl[1]);
+            split_h2(sacc[2 * k2 + 1][0], sacc[2 * k2 + 1][1], ph[2], pl[2]);
+            split_h2(sacc[2 * k2 + 1][2], sacc[2 * k2 + 1][3], ph[3], pl[3]);
+            // keys k2*16 + (t%8) + 8*((t/8)%2), hd nd*16 + 8*(t/16), transposed:
+            // (hd tile 2nd: b0, b1), (hd tile 2nd+1: b0, b1)
+            const int vrow = k2 * 16 + lrow;
+#pragma unroll
+            for (int nd = 0; nd < 8; nd++) {
+                uint32_t vhf[4], vlf[4];
+                ldsm_x4_t(vhf, Vh + vrow * PTC_P + nd * 16 + lcol);
+                ldsm_x4_t(vlf, Vl + vrow * PTC_P + nd * 16 + lcol);
+                mma_f16(o[2 * nd], ph, vhf[0], vhf[1]);
+                mma_f16(o[2 * nd], ph, vlf[0], vlf[1]);
+                mma_f16(o[2 * nd], pl, vhf[0], vhf[1]);
+                mma_f16(o[2 * nd + 1], ph, vhf[2], vhf[3]);
+                mma_f16(o[2 * nd + 1], ph, vlf[2], vlf[3]);
+                mma_f16(o[2 * nd + 1], pl, vhf[2], vhf[3]);
+            }
+        }
+    }
+    // ---- normalise and store as the O projection's f16 pair
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+    const int ra = rw + g, rb = rw + g + 8;
+#pragma unroll
+    for (int n = 0; n < 16; n++) {
+        const int d = 8 * n + 2 * c;
+        if (ra < nrows) {
+            const size_t oa = (size_t)(r0 + ra) * nh * PTC_HD + (size_t)h * PTC_HD + d;
+            split_f16(o[n][0] * i0, xh + oa, xl + oa);
+            split_f16(o[n][1] * i0, xh + oa + 1, xl + oa + 1);
+        }
+        if (rb < nrows) {
+            const size_t ob = (size_t)(r0 + rb) * nh * PTC_HD + (size_t)h * PTC_HD + d;
+            split_f16(o[n][2] * i1, xh + ob, xl + ob);
+            split_f16(o[n][3] * i1, xh + ob + 1, xl + ob + 1);
+        }
+    }
+}
+
 // act = silu(gate) * up or gelu(gate) * up (glu.wgsl:15-32) over the
 // interleaved gate/up GEMM output (column 2i gate_i, 2i+1 up_i).
 __global__ void k_pf_glu(const float* __restrict__ Gm, int I, int geglu, long rows,
@@ -486,6 +707,18 @@ int pf_fattn_go(cw_ctx* ctx, int C, const float* QKV, int ld, const float* kc, c
 int pf_fattn(cw_ctx* ctx, int hd, int C, const float* QKV, int ld, const float* kc,
              const float* vc, int max_seq, int p0, int nh, int nkv, int window, float scale,
              float softcap, void* xh, void* xl) {
+    if (hd == PTC_HD && window <= 0 && !(softcap > 0.f)) {  // the tensor-core kernel
+        static thread_local int attr_dev = -1;
+        if (attr_dev != ctx->device) {
+            CW_CUDA(cudaFuncSetAttribute(k_pf_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)PTC_SMEM));
+            attr_dev = ctx->device;
+        }
+        dim3 grid((C + PTC_BQ - 1) / PTC_BQ, nh);
+        k_pf_attn_tc<<<grid, 128, PTC_SMEM, ctx->stream>>>(QKV, ld, kc, vc, max_seq, p0, C, nh, nkv,
+                                                           scale, (__half*)xh, (__half*)xl);
+        return check_launch("prefill attention (tensor cores)");
+    }
     if (hd == 64)
         return pf_fattn_go<64>(ctx, C, QKV, ld, kc, vc, max_seq, p0, nh, nkv, window, scale,
                                softcap, xh, xl);
