@@ -375,12 +375,15 @@ __global__ void __launch_bounds__(256) k_pf_fattn(const float* __restrict__ QKV,
 // dropped ll term is 2^-22 relative): S = QK^T from the Q and K pairs, then
 // O += P V from the probabilities P (split in registers straight from the S
 // accumulators: the m16n8 C layout of two key tiles is the m16n8k16 A layout)
-// and the V pair.  CTA: 64 query rows of one head, 4 warps of 16 rows; keys in
-// tiles of 64, converted from the f32 cache into f16 pairs in shared memory
-// (rows padded by 16 bytes: the ldmatrix row addresses of a fragment fall in
-// distinct banks).  No soft-cap or window (those layers keep k_pf_fattn).
-constexpr int PTC_BQ = 64, PTC_BK = 64, PTC_HD = 128, PTC_P = PTC_HD + 8;  // row pitch, halves
-constexpr size_t PTC_SMEM = (size_t)6 * 64 * PTC_P * sizeof(__half);     // Qh Ql Kh Kl Vh Vl
+// and the V pair.  The layer's K and V rows are split into pairs once
+// (k_pf_kv_pairs); a CTA takes 64 query rows of one head (4 warps of 16 rows)
+// and streams its kv head's pairs 32 keys at a time with cp.async into two
+// shared-memory buffers, the next tile landing while the current one is
+// multiplied (rows padded by 16 bytes: the ldmatrix row addresses of a
+// fragment fall in distinct banks).  No soft-cap or window (those layers keep
+// k_pf_fattn).
+constexpr int PTC_BQ = 64, PTC_BK = 32, PTC_HD = 128, PTC_P = PTC_HD + 8;  // row pitch, halves
+constexpr size_t PTC_SMEM = ((size_t)2 * PTC_BQ + (size_t)2 * 4 * PTC_BK) * PTC_P * sizeof(__half);
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const __half* p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -416,71 +419,113 @@ __device__ __forceinline__ void split_store4(const float4& v, __half* hi, __half
     *reinterpret_cast<uint2*>(hi) = make_uint2(h0, h1);
     *reinterpret_cast<uint2*>(lo) = make_uint2(l0, l1);
 }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+
+// The K and V cache rows [0, n) of one layer (all kv heads, [kv][max_seq][128]
+// f32) as f16 pairs kp = [Kh | Kl | Vh | Vl], each [kv][stride][128]; rows
+// [n, n_pad) are zeros, so a key tile past the live keys multiplies finite
+// values (masked to zero weight).
+__global__ void k_pf_kv_pairs(const float* __restrict__ kc, const float* __restrict__ vc,
+                              int max_seq, int nkv, int n, int n_pad, int stride,
+                              __half* __restrict__ kp) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t plane = (size_t)nkv * stride * PTC_HD;
+    const long total = (long)nkv * n_pad * (PTC_HD / 4);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total;
+         i += (long)gridDim.x * blockDim.x) {
+        const int g = (int)(i / ((long)n_pad * (PTC_HD / 4)));
+        const long rem = i - (long)g * n_pad * (PTC_HD / 4);
+        const int r = (int)(rem / (PTC_HD / 4)), c4 = (int)(rem % (PTC_HD / 4));
+        float4 k = make_float4(0.f, 0.f, 0.f, 0.f), v = k;
+        if (r < n) {
+            k = *reinterpret_cast<const float4*>(kc + ((size_t)g * max_seq + r) * PTC_HD + 4 * c4);
+            v = *reinterpret_cast<const float4*>(vc + ((size_t)g * max_seq + r) * PTC_HD + 4 * c4);
+        }
+        const size_t o = ((size_t)g * stride + r) * PTC_HD + 4 * c4;
+        split_store4(k, kp + o, kp + plane + o);
+        split_store4(v, kp + 2 * plane + o, kp + 3 * plane + o);
+    }
+}
 
 __global__ void __launch_bounds__(128) k_pf_attn_tc(const float* __restrict__ QKV, int ld,
-                                                    const float* __restrict__ kc,
-                                                    const float* __restrict__ vc, int max_seq,
+                                                    const __half* __restrict__ kp, int stride,
                                                     int p0, int C, int nh, int nkv, float scale,
                                                     __half* __restrict__ xh,
                                                     __half* __restrict__ xl) {
+    pdl_trigger();
     extern __shared__ __align__(16) __half ptc[];
     __half* Qh = ptc;
-    __half* Ql = Qh + 64 * PTC_P;
-    __half* Kh = Ql + 64 * PTC_P;
-    __half* Kl = Kh + 64 * PTC_P;
-    __half* Vh = Kl + 64 * PTC_P;
-    __half* Vl = Vh + 64 * PTC_P;
+    __half* Ql = Qh + PTC_BQ * PTC_P;
+    __half* KV = Ql + PTC_BQ * PTC_P;  // [2 buffers][Kh, Kl, Vh, Vl][32][PTC_P]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, c = lane & 3;
     // longest rows (latest positions) first: the causal work grows with the row
     const int r0 = (gridDim.x - 1 - blockIdx.x) * PTC_BQ;
     const int h = blockIdx.y, kvh = h / (nh / nkv);
     const int nrows = min(PTC_BQ, C - r0);
-    for (int i = tid; i < 64 * 32; i += 128) {  // Q rows (normed, roped) -> f16 pairs
+    const size_t plane = (size_t)nkv * stride * PTC_HD;
+    const __half* src0 = kp + (size_t)kvh * stride * PTC_HD;
+    const int pos_first = p0 + r0, j_end = p0 + r0 + nrows;  // keys [0, j_end)
+    const int n_tiles = (j_end + PTC_BK - 1) / PTC_BK;
+    // tile t of the kv head's pairs into buffer t % 2 (16 cp.async per thread)
+    auto load_tile = [&](int t) {
+        __half* dst = KV + (size_t)(t & 1) * 4 * PTC_BK * PTC_P;
+        for (int i = tid; i < 4 * PTC_BK * 16; i += 128) {
+            const int mat = i >> 9, r = (i >> 4) & (PTC_BK - 1), ch = i & 15;
+            cp_async16(dst + ((size_t)mat * PTC_BK + r) * PTC_P + 8 * ch,
+                       src0 + mat * plane + (size_t)(t * PTC_BK + r) * PTC_HD + 8 * ch);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    pdl_wait();
+    load_tile(0);
+    for (int i = tid; i < PTC_BQ * 32; i += 128) {  // Q rows (normed, roped) -> f16 pairs
         const int r = i >> 5, c4 = i & 31;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (r < nrows)
             v = *reinterpret_cast<const float4*>(QKV + (size_t)(r0 + r) * ld + (size_t)h * PTC_HD + 4 * c4);
         split_store4(v, Qh + r * PTC_P + 4 * c4, Ql + r * PTC_P + 4 * c4);
     }
-    const int pos_first = p0 + r0, j_end = p0 + r0 + nrows;  // keys [0, j_end)
-    const int rw = warp * 16;                                 // this warp's first row
+    const int rw = warp * 16;  // this warp's first row
     const int pos_g = pos_first + rw + g, pos_g8 = pos_g + 8;
     float o[16][4];
 #pragma unroll
     for (int n = 0; n < 16; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m0 = REF_NEG_INF, m1 = REF_NEG_INF, l0 = 0.f, l1 = 0.f;
-    const float* kb = kc + (size_t)kvh * max_seq * PTC_HD;
-    const float* vb = vc + (size_t)kvh * max_seq * PTC_HD;
     // ldmatrix row addresses (thread t: matrix t / 8, row t % 8)
     const int lrow = (lane & 7) + 8 * ((lane >> 3) & 1), lcol = 8 * (lane >> 4);
-    for (int kt = 0; kt < j_end; kt += PTC_BK) {
-        __syncthreads();  // the previous tile's K, V consumed (and Q stored, first time)
-#pragma unroll 4
-        for (int i = tid; i < 64 * 32; i += 128) {
-            const int r = i >> 5, c4 = i & 31;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (kt + r < j_end) {
-                kv = __ldg(reinterpret_cast<const float4*>(kb + (size_t)(kt + r) * PTC_HD) + c4);
-                vv = __ldg(reinterpret_cast<const float4*>(vb + (size_t)(kt + r) * PTC_HD) + c4);
-            }
-            split_store4(kv, Kh + r * PTC_P + 4 * c4, Kl + r * PTC_P + 4 * c4);
-            split_store4(vv, Vh + r * PTC_P + 4 * c4, Vl + r * PTC_P + 4 * c4);
+    for (int t = 0; t < n_tiles; t++) {
+        if (t + 1 < n_tiles) {
+            load_tile(t + 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
-        __syncthreads();
-        // ---- S = Q K^T over the tile: 8 key tiles of 8, hd in 8 steps of 16
-        float sacc[8][4];
+        __syncthreads();  // tile t (and, the first time, Q) visible to every warp
+        const __half* Kh = KV + (size_t)(t & 1) * 4 * PTC_BK * PTC_P;
+        const __half* Kl = Kh + PTC_BK * PTC_P;
+        const __half* Vh = Kl + PTC_BK * PTC_P;
+        const __half* Vl = Vh + PTC_BK * PTC_P;
+        const int kt = t * PTC_BK;
+        // ---- S = Q K^T over the tile: 4 key tiles of 8, hd in 8 steps of 16
+        float sacc[4][4];
 #pragma unroll
-        for (int n = 0; n < 8; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
+        for (int n = 0; n < 4; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) {
             uint32_t qh[4], ql[4];
             ldsm_x4(qh, Qh + (rw + lrow) * PTC_P + ks * 16 + lcol);
             ldsm_x4(ql, Ql + (rw + lrow) * PTC_P + ks * 16 + lcol);
 #pragma unroll
-            for (int np = 0; np < 4; np++) {
+            for (int np = 0; np < 2; np++) {
                 // keys np*16 + (t%8) + 8*(t/16), hd ks*16 + 8*((t/8)%2): matrices
-                // (n-tile 2np: b0, b1), (n-tile 2np+1: b0, b1)
+                // (key tile 2np: b0, b1), (key tile 2np+1: b0, b1)
                 const int krow = np * 16 + (lane & 7) + 8 * (lane >> 4), kcol = ks * 16 + 8 * ((lane >> 3) & 1);
                 uint32_t khf[4], klf[4];
                 ldsm_x4(khf, Kh + krow * PTC_P + kcol);
@@ -496,7 +541,7 @@ __global__ void __launch_bounds__(128) k_pf_attn_tc(const float* __restrict__ QK
         // ---- online softmax: this thread's rows g and g + 8, keys 8n + 2c, +1
         float mx0 = REF_NEG_INF, mx1 = REF_NEG_INF;
 #pragma unroll
-        for (int n = 0; n < 8; n++) {
+        for (int n = 0; n < 4; n++) {
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 const int key = kt + 8 * n + 2 * c + e;
@@ -512,12 +557,12 @@ __global__ void __launch_bounds__(128) k_pf_attn_tc(const float* __restrict__ QK
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
         const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        // a row with no key yet in this tile keeps its state (its keys start at 0)
+        // a row with no key yet keeps its state (every row has key 0 in tile 0)
         const float c0 = mn0 == REF_NEG_INF ? 1.f : expf(m0 - mn0);
         const float c1 = mn1 == REF_NEG_INF ? 1.f : expf(m1 - mn1);
         float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
-        for (int n = 0; n < 8; n++) {
+        for (int n = 0; n < 4; n++) {
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 const float p0v = sacc[n][e] == REF_NEG_INF ? 0.f : expf(sacc[n][e] - mn0);
@@ -543,9 +588,9 @@ __global__ void __launch_bounds__(128) k_pf_attn_tc(const float* __restrict__ QK
             o[n][2] *= c1;
             o[n][3] *= c1;
         }
-        // ---- O += P V: keys in 4 steps of 16, hd in 16 tiles of 8
+        // ---- O += P V: keys in 2 steps of 16, hd in 16 tiles of 8
 #pragma unroll
-        for (int k2 = 0; k2 < 4; k2++) {
+        for (int k2 = 0; k2 < 2; k2++) {
             uint32_t ph[4], pl[4];
             split_h2(sacc[2 * k2][0], sacc[2 * k2][1], ph[0], pl[0]);
             split_h2(sacc[2 * k2][2], sacc[2 * k2][3], ph[1], pl[1]);
@@ -567,6 +612,7 @@ __global__ void __launch_bounds__(128) k_pf_attn_tc(const float* __restrict__ QK
                 mma_f16(o[2 * nd + 1], pl, vhf[2], vhf[3]);
             }
         }
+        __syncthreads();  // every warp is done with buffer t % 2 before it is refilled
     }
     // ---- normalise and store as the O projection's f16 pair
     const float i0 = 1.0f / l0, i1 = 1.0f / l1;
@@ -628,12 +674,19 @@ namespace {
 constexpr size_t GEMM_WS_BYTES = 64ull << 20;  // split-K partial tiles of the small-M GEMMs
 
 struct PfLayout {
-    size_t H, T, QKV, G, xh, xl, wh, wl, ws, total;
+    size_t H, T, QKV, G, xh, xl, wh, wl, ws, kvp, total;
 };
 
 size_t al256(size_t v) { return (v + 255) / 256 * 256; }
 
-PfLayout pf_layout(const cw_model* m, size_t C) {
+// Pair scratch of the tensor-core attention for keys up to max_keys: 4 planes
+// [nkv][stride][128] halves, stride = max_keys rounded up to a key tile.
+size_t pf_kv_pairs_bytes(int nkv, int max_keys) {
+    const size_t stride = (size_t)(max_keys + PTC_BK - 1) / PTC_BK * PTC_BK;
+    return 4 * (size_t)nkv * stride * PTC_HD * sizeof(__half);
+}
+
+PfLayout pf_layout(const cw_model* m, size_t C, size_t max_keys) {
     const cw_model_info& I = m->info;
     const size_t qd = (size_t)I.n_heads * I.head_dim, kvd = (size_t)I.n_kv * I.head_dim;
     const size_t qkv = qd + 2 * kvd;
@@ -658,6 +711,8 @@ PfLayout pf_layout(const cw_model* m, size_t C) {
                                   (size_t)I.dim * I.hidden});
     L.wh = take(C > 256 ? wmax * 2 : 0);  // f16 pair of one weight (long chunks)
     L.wl = take(C > 256 ? wmax * 2 : 0);
+    // the tensor-core attention's key/value pairs (head_dim 128 families)
+    L.kvp = take(I.head_dim == 128 ? pf_kv_pairs_bytes((int)I.n_kv, (int)max_keys) : 0);
     L.total = o;
     return L;
 }
@@ -704,19 +759,32 @@ int pf_fattn_go(cw_ctx* ctx, int C, const float* QKV, int ld, const float* kc, c
     return check_launch("prefill tiled attention");
 }
 
+// The tensor-core kernel's layers: head_dim 128, no window, no soft-cap.
+bool pf_attn_tc_ok(int hd, int window, float softcap) {
+    return hd == PTC_HD && window <= 0 && !(softcap > 0.f);
+}
+
 int pf_fattn(cw_ctx* ctx, int hd, int C, const float* QKV, int ld, const float* kc,
              const float* vc, int max_seq, int p0, int nh, int nkv, int window, float scale,
-             float softcap, void* xh, void* xl) {
-    if (hd == PTC_HD && window <= 0 && !(softcap > 0.f)) {  // the tensor-core kernel
+             float softcap, void* xh, void* xl, void* kvp) {
+    if (kvp && pf_attn_tc_ok(hd, window, softcap)) {  // the tensor-core kernel
         static thread_local int attr_dev = -1;
         if (attr_dev != ctx->device) {
             CW_CUDA(cudaFuncSetAttribute(k_pf_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)PTC_SMEM));
             attr_dev = ctx->device;
         }
+        const int stride = (max_seq + PTC_BK - 1) / PTC_BK * PTC_BK;
+        const int n = p0 + C, n_pad = (n + PTC_BK - 1) / PTC_BK * PTC_BK;
+        const long items = (long)nkv * n_pad * (PTC_HD / 4);
+        const int blocks = (int)std::min<long>((items + 255) / 256, (long)ctx->sm_count * 8);
+        k_pf_kv_pairs<<<blocks, 256, 0, ctx->stream>>>(kc, vc, max_seq, nkv, n, n_pad, stride,
+                                                        (__half*)kvp);
+        CW_TRY(check_launch("prefill key/value pairs"));
         dim3 grid((C + PTC_BQ - 1) / PTC_BQ, nh);
-        k_pf_attn_tc<<<grid, 128, PTC_SMEM, ctx->stream>>>(QKV, ld, kc, vc, max_seq, p0, C, nh, nkv,
-                                                           scale, (__half*)xh, (__half*)xl);
+        k_pf_attn_tc<<<grid, 128, PTC_SMEM, ctx->stream>>>(QKV, ld, (const __half*)kvp, stride, p0,
+                                                           C, nh, nkv, scale, (__half*)xh,
+                                                           (__half*)xl);
         return check_launch("prefill attention (tensor cores)");
     }
     if (hd == 64)
@@ -737,7 +805,7 @@ int pf_chunk(cw_session* s, int p0, int C) {
     const int qd = nh * hd, kvd = nkv * hd, qkv_rows = qd + 2 * kvd, hid = (int)I.hidden;
     const bool post = I.post_norms != 0;
     const int unit = I.norm_kind == 1;
-    const PfLayout L = pf_layout(m, (size_t)C);
+    const PfLayout L = pf_layout(m, (size_t)C, s->max_seq);
     uint8_t* b = (uint8_t*)s->pf_mem;
     float* H = (float*)(b + L.H);
     float* T = (float*)(b + L.T);
@@ -813,7 +881,7 @@ int pf_chunk(cw_session* s, int p0, int C) {
         const float scale = powf((float)hd, -0.5f);  // attention.rs:18
         if (hd == 64 || hd == 128 || hd == 256) {
             CW_TRY(pf_fattn(ctx, hd, C, QKV, qkv_rows, kc, vc, (int)s->max_seq, p0, nh, nkv,
-                            window, scale, I.attn_softcap, xh, xl));
+                            window, scale, I.attn_softcap, xh, xl, L.kvp ? b + L.kvp : nullptr));
         } else {  // other head sizes: one CTA per (row, kv head)
             const int G = nh / nkv, epl = (hd + 31) / 32;
             const size_t smem = (attn_smem_floats(G, hd, 1) + (size_t)G * hd) * sizeof(float);
@@ -866,7 +934,7 @@ int session_prefill(cw_session* s, size_t* n_done) {
     if (s->host_pos < end) {
         const size_t chunk = s->pf_chunk ? std::min<size_t>(s->pf_chunk, PF_CHUNK) : PF_CHUNK;
         const size_t C = std::min<size_t>(end - s->host_pos, chunk);
-        const PfLayout L = pf_layout(s->m, C);
+        const PfLayout L = pf_layout(s->m, C, s->max_seq);
         if (s->pf_bytes < L.total) {
             CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
             if (s->pf_mem) cudaFree(s->pf_mem);
