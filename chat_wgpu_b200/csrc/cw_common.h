@@ -59,6 +59,9 @@ struct BufEntry {
     // scale plane (the nibble plane starts at 0).
     size_t rows = 0, in_f = 0, scale_off = 0;
     bool q4_0 = false;
+    // Set for a Q6_K weight split for the streaming GEMV (cw_q6_k_split):
+    // [rows][in_f/256][208] payload, f16 d plane at scale_off.
+    bool q6k_split = false;
 };
 
 struct ProfRec {

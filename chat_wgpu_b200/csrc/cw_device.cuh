@@ -101,7 +101,44 @@ enum Q4Layout : int {
     // chat-wgpu's re-quantised layout (q4.rs:32-36): u32 quants, nibble n of
     // word w of block b = element b*32 + w*8 + n; f32 scales [rows][nb].
     LAYOUT_REF = 1,
+    // Raw GGUF Q4_K / Q5_K super-blocks [rows][K/256][144 | 176] (d, dmin,
+    // 12 bytes of 6-bit scales/mins, Q5_K's 32 fifth-bit bytes, 128 nibble
+    // bytes).  The GEMV takes each 16-byte run of nibbles as one "unit":
+    // run u of a super-block (chunk c = u/2, half h = u%2) holds elements
+    // 64c + 16h + i (low nibbles, sub-block 2c) and 64c + 32 + 16h + i (high
+    // nibbles, sub-block 2c+1), i < 16.
+    LAYOUT_Q4K = 2,
+    LAYOUT_Q5K = 3,
+    // GGUF Q6_K split into 16-byte-aligned planes (the file's 210-byte
+    // super-blocks are 2-byte aligned): [rows][K/256][208] = ql[128] qh[64]
+    // scales[16] as in the file, then the f16 d of every super-block
+    // [rows][K/256].  Unit u of a super-block (half h = u/4, s = (u/2)%2,
+    // t = u%2) is ql bytes 16u..16u+15: low nibbles elements 128h + 32s +
+    // 16t + i (scale 8h + 2s + t), high nibbles the same + 64 (scale + 4);
+    // their top two bits are bits 2s and 2s+4 of qh[32h + 16t + i].
+    LAYOUT_Q6K = 4,
 };
+
+template <int LAYOUT>
+__host__ __device__ constexpr bool layout_kq() {
+    return LAYOUT == LAYOUT_Q4K || LAYOUT == LAYOUT_Q5K || LAYOUT == LAYOUT_Q6K;
+}
+
+// Element of x that element e (0..31) of GEMV unit b pairs with: the unit's
+// 32-element block for Q4_0 planes; for the k-quant layouts, the unit's low
+// run (e < 16) and high run (e >= 16), 32 elements apart (Q6_K: 64).
+template <int LAYOUT>
+__device__ __forceinline__ int unit_elem(int b, int e) {
+    if constexpr (LAYOUT == LAYOUT_Q6K) {
+        const int u = b & 7;
+        return (b >> 3) * 256 + 128 * (u >> 2) + 32 * ((u >> 1) & 1) + 16 * (u & 1) + (e & 15) +
+               ((e & 16) << 2);
+    } else if constexpr (layout_kq<LAYOUT>()) {
+        return (b >> 1) * 64 + 16 * (b & 1) + (e & 15) + ((e & 16) << 1);
+    } else {
+        return b * 32 + e;
+    }
+}
 
 // Byte position, inside a block's 32-byte plane row, of block element j.
 // Words 0-3 pair with the low nibbles of payload words 0-3, words 4-7 with

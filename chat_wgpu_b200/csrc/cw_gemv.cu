@@ -10,7 +10,6 @@ namespace cw {
 
 template <int LAYOUT, int PRO, int EPI, class CF>
 static int sgemv_go(cw_ctx* ctx, const GemvArgs& a, bool pdl) {
-    constexpr int SW = LAYOUT == LAYOUT_GGUF ? 2 : 4;
     const int nb = a.K / 32;
     const long nchunks = ((long)a.N + CF::RC - 1) / CF::RC;
     // Small GEMVs (the per-layer decode projections): one chunk per CTA, all
@@ -21,7 +20,8 @@ static int sgemv_go(cw_ctx* ctx, const GemvArgs& a, bool pdl) {
     // (deeper rings measured slower: they cost CTAs per SM, and the large
     // GEMVs are bound by their consumers, not by bytes in flight)
     const int S = nchunks <= (long)ctx->sm_count * 2 ? 1 : 2;
-    const GemvSmem L(CF::RC, CF::WPR, nb, SW, S, a.K, PRO == PRO_NORM);
+    const GemvSmem L(CF::RC, CF::WPR, nb, gemv_pbb<LAYOUT>(), gemv_sc_bytes<LAYOUT>(CF::RC, nb), S,
+                     a.K, PRO == PRO_NORM);
     CW_CHECK((int)L.total <= ctx->max_smem_optin, CW_ERR_UNSUPPORTED,
              "gemv: K=%d needs %zu bytes of shared memory", a.K, L.total);
     static thread_local std::map<std::tuple<int, const void*, size_t>, int> occ;
@@ -71,6 +71,18 @@ static int sgemv_cfg(cw_ctx* ctx, const GemvArgs& a, bool pdl) {
     return set_error(CW_ERR_UNSUPPORTED, "gemv: K=%d too large for the streaming kernel", a.K);
 }
 
+template <int LAYOUT>
+static int sgemv_layout(cw_ctx* ctx, int pro, int epi, const GemvArgs& a, bool pdl) {
+    if (pro == PRO_X && epi == EPI_STORE) return sgemv_cfg<LAYOUT, PRO_X, EPI_STORE>(ctx, a, pdl);
+    if (pro == PRO_X && epi == EPI_RESID) return sgemv_cfg<LAYOUT, PRO_X, EPI_RESID>(ctx, a, pdl);
+    if (pro == PRO_NORM && epi == EPI_STORE)
+        return sgemv_cfg<LAYOUT, PRO_NORM, EPI_STORE>(ctx, a, pdl);
+    if (pro == PRO_NORM && epi == EPI_GLU) return sgemv_cfg<LAYOUT, PRO_NORM, EPI_GLU>(ctx, a, pdl);
+    if (pro == PRO_NORM && epi == EPI_HEAD)
+        return sgemv_cfg<LAYOUT, PRO_NORM, EPI_HEAD>(ctx, a, pdl);
+    return set_error(CW_ERR_UNSUPPORTED, "gemv: prologue %d / epilogue %d not instantiated", pro, epi);
+}
+
 int launch_sgemv(cw_ctx* ctx, int layout, int pro, int epi, const GemvArgs& a, bool pdl) {
     CW_CHECK(sgemv_supported(layout, a.K), CW_ERR_UNSUPPORTED,
              "gemv: K=%d not handled by the streaming kernel", a.K);
@@ -78,14 +90,10 @@ int launch_sgemv(cw_ctx* ctx, int layout, int pro, int epi, const GemvArgs& a, b
         CW_CHECK(pro == PRO_X && epi == EPI_STORE, CW_ERR_UNSUPPORTED, "gemv: crate layout is x->y only");
         return sgemv_cfg<LAYOUT_REF, PRO_X, EPI_STORE>(ctx, a, pdl);
     }
-    if (pro == PRO_X && epi == EPI_STORE) return sgemv_cfg<LAYOUT_GGUF, PRO_X, EPI_STORE>(ctx, a, pdl);
-    if (pro == PRO_X && epi == EPI_RESID) return sgemv_cfg<LAYOUT_GGUF, PRO_X, EPI_RESID>(ctx, a, pdl);
-    if (pro == PRO_NORM && epi == EPI_STORE)
-        return sgemv_cfg<LAYOUT_GGUF, PRO_NORM, EPI_STORE>(ctx, a, pdl);
-    if (pro == PRO_NORM && epi == EPI_GLU) return sgemv_cfg<LAYOUT_GGUF, PRO_NORM, EPI_GLU>(ctx, a, pdl);
-    if (pro == PRO_NORM && epi == EPI_HEAD)
-        return sgemv_cfg<LAYOUT_GGUF, PRO_NORM, EPI_HEAD>(ctx, a, pdl);
-    return set_error(CW_ERR_UNSUPPORTED, "gemv: prologue %d / epilogue %d not instantiated", pro, epi);
+    if (layout == LAYOUT_Q4K) return sgemv_layout<LAYOUT_Q4K>(ctx, pro, epi, a, pdl);
+    if (layout == LAYOUT_Q5K) return sgemv_layout<LAYOUT_Q5K>(ctx, pro, epi, a, pdl);
+    if (layout == LAYOUT_Q6K) return sgemv_layout<LAYOUT_Q6K>(ctx, pro, epi, a, pdl);
+    return sgemv_layout<LAYOUT_GGUF>(ctx, pro, epi, a, pdl);
 }
 
 }  // namespace cw

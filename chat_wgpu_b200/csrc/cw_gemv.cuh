@@ -1,5 +1,7 @@
 // cw_gemv.cuh -- the streaming Q4 GEMV: y[N] = W[N,K] x for Q4 weights,
 // shared by the stand-alone op entry points and the fused decode kernels.
+// The same kernel streams GGUF Q4_K / Q5_K super-blocks and the aligned
+// Q6_K split (layouts in cw_device.cuh; per-unit math in kq_chunk).
 //
 // Data movement (B200): weight rows are contiguous in both planes (16-byte
 // nibble payloads, then f16/f32 scales), so a CTA streams "chunks" of RC
@@ -154,12 +156,37 @@ __device__ __forceinline__ void fence_mbar_init() {
 __host__ __device__ constexpr size_t al128(size_t v) { return (v + 127) / 128 * 128; }
 __host__ __device__ constexpr size_t al16(size_t v) { return (v + 15) / 16 * 16; }
 
+// Bytes per 32-weight unit in the weight stream: the payload plane (Q4_0
+// nibbles; the k-quants' whole super-blocks, headers included) and the
+// separate scale plane (f16 / f32 for Q4_0, none for the k-quants).
+template <int LAYOUT>
+__host__ __device__ constexpr int gemv_pbb() {
+    return LAYOUT == LAYOUT_Q4K ? 18 : LAYOUT == LAYOUT_Q5K ? 22 : LAYOUT == LAYOUT_Q6K ? 26 : 16;
+}
+template <int LAYOUT>
+__host__ __device__ constexpr int gemv_sw() {
+    return LAYOUT == LAYOUT_GGUF ? 2 : LAYOUT == LAYOUT_REF ? 4 : 0;
+}
+// Scale-plane bytes of `rows` rows and their offset in the plane: Q6_K's f16
+// d per super-block, its copy rounded up to 16 bytes (the plane's buffer is
+// padded to 256 bytes, so the rounded copy stays inside it).
+template <int LAYOUT>
+__host__ __device__ constexpr size_t gemv_sc_bytes(long rows, int nb) {
+    return LAYOUT == LAYOUT_Q6K ? al16((size_t)rows * (nb / 8) * 2)
+                                : (size_t)rows * nb * gemv_sw<LAYOUT>();
+}
+template <int LAYOUT>
+__host__ __device__ constexpr size_t gemv_sc_off(long row0, int nb) {
+    return LAYOUT == LAYOUT_Q6K ? (size_t)row0 * (nb / 8) * 2 : (size_t)row0 * nb * gemv_sw<LAYOUT>();
+}
+
 // Shared-memory layout sizes (bytes).
 struct GemvSmem {
     size_t pay, sc, stage, q24, hbuf, red, total;
-    __host__ __device__ GemvSmem(int RC, int WPR, int nb, int sw, int S, int K, bool norm) {
-        pay = al128((size_t)RC * nb * 16);
-        sc = al128((size_t)RC * nb * sw);
+    __host__ __device__ GemvSmem(int RC, int WPR, int nb, int pbb, size_t scb, int S, int K,
+                                 bool norm) {
+        pay = al128((size_t)RC * nb * pbb);
+        sc = al128(scb);
         stage = pay + sc;
         q24 = al16(q24_bytes(nb));
         hbuf = norm ? al16((size_t)K * 4) : 0;
@@ -230,10 +257,12 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nw = blockDim.x >> 5, sub = lane >> 3, e0 = 4 * (lane & 7);
     if (PRO == PRO_X) {
-        if constexpr (LAYOUT == LAYOUT_GGUF) {  // four elements per lane (q24_quad); nb % 8 == 0
+        if constexpr (LAYOUT != LAYOUT_REF) {  // four elements per lane (q24_quad); nb % 8 == 0
             for (int t = warp; t < nb / 4; t += nw) {
                 const int b = 4 * t + sub;
-                q24_quad(q, b, true, __ldcg(reinterpret_cast<const float4*>(a.x + b * 32 + e0)), lane);
+                q24_quad(q, b, true,
+                         __ldcg(reinterpret_cast<const float4*>(a.x + unit_elem<LAYOUT>(b, e0))),
+                         lane);
             }
         } else {
             for (int b = warp; b < nb; b += nw) q24_block<LAYOUT>(q, b, __ldcg(a.x + b * 32 + lane), lane);
@@ -296,9 +325,9 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
     ssh = gemv_cta_sum(ssh, red8);
     const float inv = 1.0f / sqrtf(ssh / (float)K + a.eps);
     const bool wx = a.xn_out && blockIdx.x == 0;
-    if constexpr (LAYOUT == LAYOUT_GGUF) {  // four elements per lane (q24_quad); nb % 8 == 0
+    if constexpr (LAYOUT != LAYOUT_REF) {  // four elements per lane (q24_quad); nb % 8 == 0
         for (int t = warp; t < nb / 4; t += nw) {
-            const int b = 4 * t + sub, i = b * 32 + e0;
+            const int b = 4 * t + sub, i = unit_elem<LAYOUT>(b, e0);
             const float4 h = *reinterpret_cast<const float4*>(hbuf + i);
             float4 g = __ldg(reinterpret_cast<const float4*>(a.norm_w + i));
             if (a.unit) g = make_float4(1.0f + g.x, 1.0f + g.y, 1.0f + g.z, 1.0f + g.w);
@@ -320,18 +349,149 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
     }
 }
 
+// The (scale, min) pairs of sub-blocks 2c and 2c+1 of a Q4_K / Q5_K
+// super-block whose 16-byte header is h (.x = f16 d | f16 dmin << 16, .y .z .w
+// = the 12 packed 6-bit scale/min bytes q[0..11]): for j < 4 scale q[j] & 63,
+// min q[j+4] & 63; for j >= 4 scale (q[j+4] & 15) | (q[j-4] >> 6) << 4, min
+// (q[j+4] >> 4) | (q[j] >> 6) << 4.  Both sub-blocks at once, one per byte
+// of a 16-bit field.  Returns d*scale and dmin*min (exact in f32).
+__device__ __forceinline__ void kq_scales(const uint4& h, int c, float& alo, float& ahi,
+                                          float& blo, float& bhi) {
+    const int sh = 16 * (c & 1);
+    const unsigned y2 = h.y >> sh, z2 = h.z >> sh;
+    unsigned scp, mp;
+    if (c >= 2) {
+        const unsigned w2 = h.w >> sh;
+        scp = (w2 & 0x0f0fu) | ((y2 >> 2) & 0x3030u);
+        mp = ((w2 >> 4) & 0x0f0fu) | ((z2 >> 2) & 0x3030u);
+    } else {
+        scp = y2 & 0x3f3fu;
+        mp = z2 & 0x3f3fu;
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu)));
+    const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    alo = d * (float)(scp & 0xffu);
+    ahi = d * (float)((scp >> 8) & 0xffu);
+    blo = dm * (float)(mp & 0xffu);
+    bhi = dm * (float)((mp >> 8) & 0xffu);
+}
+
+// One stage of the k-quant GEMV: this warp's RPW rows x BPL units of the
+// raw super-blocks in shared memory (pay: the chunk's rows back to back).
+// Per unit, the low and high nibbles (+ Q5_K's fifth bits) are dotted with
+// the unit's q24 planes apart (their sub-blocks have their own scales):
+// sum = sb * (d*sc_lo * T_lo + d*sc_hi * T_hi) - (dmin*m_lo * sx_lo + dmin*m_hi * sx_hi)
+// with T = D0 + 256 D1 + 65536 D2 the integer dot products of the planes.
+//
+// Q6_K: q = the nibble | two bits of qh << 4 (0..63), w = d * sc * (q - 32):
+// sum = d * (sc_lo * (sb * T_lo - 32 sx_lo) + sc_hi * (sb * T_hi - 32 sx_hi)),
+// the int8 scales and the f16 d from their planes (scs: the chunk's d values).
+template <int LAYOUT, int RPW, int BPL, int WPR>
+__device__ __forceinline__ void kq_chunk(const unsigned char* pay, const unsigned char* scs, int nb,
+                                         int rows, int slot, int wsub, int lane, int c,
+                                         const uint4 (&xa)[BPL][3], const uint4 (&xb)[BPL][3],
+                                         const float (&sbr)[BPL], const float (&xsl)[BPL],
+                                         const float (&xsh)[BPL], float (&acc)[RPW]) {
+    constexpr bool FIVE = LAYOUT == LAYOUT_Q5K, SIX = LAYOUT == LAYOUT_Q6K;
+    constexpr int SBB = SIX ? 208 : FIVE ? 176 : 144, QOFF = SIX ? 0 : FIVE ? 48 : 16;
+    const int nbk = nb >> 3;
+    // Q6_K: this lane's unit u = lane % 8 of each super-block (half u/4,
+    // s = (u/2)%2, t = u%2): qh run 128 + 32h + 16t, scales 8h + 2s + t and + 4
+    const int u6 = lane & 7, qh6 = 128 + 32 * (u6 >> 2) + 16 * (u6 & 1), sc6 = 192 + 8 * (u6 >> 2);
+    const int sh6 = 2 * ((u6 >> 1) & 1), by6 = 8 * (u6 & 3);
+    uint4 w4[RPW][BPL], h4[RPW][BPL], q5[RPW][(FIVE || SIX) ? BPL : 1];
+    float d6[RPW][SIX ? BPL : 1];
+#pragma unroll
+    for (int j = 0; j < RPW; j++) {
+        const int r = slot * RPW + j;
+#pragma unroll
+        for (int k = 0; k < BPL; k++) {
+            const int b = wsub * 32 + lane + k * 32 * WPR;
+            const bool in = r < rows && b < nb;
+            const size_t sbi = (size_t)(in ? r : 0) * nbk + (in ? b >> 3 : 0);
+            const unsigned char* sb = pay + sbi * SBB;
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            w4[j][k] = in ? *reinterpret_cast<const uint4*>(sb + QOFF + (b & 7) * 16) : z;
+            if constexpr (SIX) {
+                q5[j][k] = in ? *reinterpret_cast<const uint4*>(sb + qh6) : z;
+                const uint2 sc2 = in ? *reinterpret_cast<const uint2*>(sb + sc6) : make_uint2(0, 0);
+                h4[j][k] = make_uint4(sc2.x, sc2.y, 0, 0);
+                d6[j][k] = in ? __half2float(reinterpret_cast<const __half*>(scs)[sbi]) : 0.f;
+            } else {
+                h4[j][k] = in ? *reinterpret_cast<const uint4*>(sb) : z;
+                if constexpr (FIVE)
+                    q5[j][k] = in ? *reinterpret_cast<const uint4*>(sb + 16 + (b & 1) * 16) : z;
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < RPW; j++) {
+        acc[j] = 0.f;
+#pragma unroll
+        for (int k = 0; k < BPL; k++) {
+            const unsigned w[4] = {w4[j][k].x, w4[j][k].y, w4[j][k].z, w4[j][k].w};
+            const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
+            const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
+            const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
+            const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
+            const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
+            const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
+            int s0l = 0, s0h = 0, s1l = 0, s1h = 0, s2l = 0, s2h = 0;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                unsigned lo = w[t] & 0x0f0f0f0fu;
+                unsigned hi = (w[t] >> 4) & 0x0f0f0f0fu;
+                if constexpr (FIVE) {  // qh byte i: bit 2c -> element i of sub-block 2c, 2c+1 -> 2c+1
+                    const unsigned qh = t == 0 ? q5[j][k].x : t == 1 ? q5[j][k].y
+                                      : t == 2 ? q5[j][k].z : q5[j][k].w;
+                    lo |= ((qh >> (2 * c)) & 0x01010101u) << 4;
+                    hi |= ((qh >> (2 * c + 1)) & 0x01010101u) << 4;
+                } else if constexpr (SIX) {  // bits 2s, 2s+1 (low run) and 2s+4, 2s+5 (high run)
+                    const unsigned qh = t == 0 ? q5[j][k].x : t == 1 ? q5[j][k].y
+                                      : t == 2 ? q5[j][k].z : q5[j][k].w;
+                    const unsigned q2 = qh >> sh6;
+                    lo |= (q2 & 0x03030303u) << 4;
+                    hi |= q2 & 0x30303030u;
+                }
+                s0l = dp4a_uu(lo, a0[t], s0l);
+                s0h = dp4a_uu(hi, b0[t], s0h);
+                s1l = dp4a_uu(lo, a1[t], s1l);
+                s1h = dp4a_uu(hi, b1[t], s1h);
+                s2l = dp4a_us(lo, a2[t], s2l);
+                s2h = dp4a_us(hi, b2[t], s2h);
+            }
+            const float tl = fmaf((float)s2l, 65536.0f, (float)(s0l + 256 * s1l));
+            const float th = fmaf((float)s2h, 65536.0f, (float)(s0h + 256 * s1h));
+            if constexpr (SIX) {
+                const float slo = (float)(int)(signed char)(h4[j][k].x >> by6);
+                const float shi = (float)(int)(signed char)(h4[j][k].y >> by6);
+                const float v = fmaf(slo, fmaf(sbr[k], tl, -32.0f * xsl[k]),
+                                     shi * fmaf(sbr[k], th, -32.0f * xsh[k]));
+                acc[j] = fmaf(d6[j][k], v, acc[j]);
+            } else {
+                float alo, ahi, blo, bhi;
+                kq_scales(h4[j][k], c, alo, ahi, blo, bhi);
+                float v = fmaf(sbr[k], fmaf(alo, tl, ahi * th), acc[j]);
+                v = fmaf(-blo, xsl[k], v);
+                acc[j] = fmaf(-bhi, xsh[k], v);
+            }
+        }
+    }
+}
+
 template <int LAYOUT, int PRO, int EPI, class CF>
 __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ float red8[32];
     constexpr int WPR = CF::WPR, BPL = CF::BPL, RPW = CF::RPW, RC = CF::RC;
-    constexpr int SW = LAYOUT == LAYOUT_GGUF ? 2 : 4;
+    constexpr int SW = gemv_sw<LAYOUT>(), PBB = gemv_pbb<LAYOUT>();
+    constexpr bool KQ = layout_kq<LAYOUT>();
     const int nb = a.K / 32;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const long nchunks = ((long)a.N + RC - 1) / RC;
     const int mycount =
         blockIdx.x < nchunks ? (int)((nchunks - 1 - blockIdx.x) / gridDim.x + 1) : 0;
-    const GemvSmem L(RC, WPR, nb, SW, S, a.K, PRO == PRO_NORM);
+    const GemvSmem L(RC, WPR, nb, PBB, gemv_sc_bytes<LAYOUT>(RC, nb), S, a.K, PRO == PRO_NORM);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
     unsigned char* stages = smem + 128;
     const Q24 q = q24_carve(stages + (size_t)S * L.stage, nb);
@@ -343,15 +503,16 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
         const int s = i % S;
         const long row0 = c * RC;
         const int rows = (int)min((long)RC, (long)a.N - row0);
-        const unsigned pb = (unsigned)rows * nb * 16, sb = (unsigned)rows * nb * SW;
+        const unsigned pb = (unsigned)rows * nb * PBB, sb = (unsigned)gemv_sc_bytes<LAYOUT>(rows, nb);
         const uint64_t pol = l2_evict_first();
         fence_proxy_async();
         mbar_expect_tx(&bars[s], pb + sb);
-        bulk_g2s_hint(stages + (size_t)s * L.stage, a.payload + (size_t)row0 * nb * 16, pb,
+        bulk_g2s_hint(stages + (size_t)s * L.stage, a.payload + (size_t)row0 * nb * PBB, pb,
                       &bars[s], pol);
-        bulk_g2s_hint(stages + (size_t)s * L.stage + L.pay,
-                      reinterpret_cast<const char*>(a.scales) + (size_t)row0 * nb * SW, sb,
-                      &bars[s], pol);
+        if constexpr (SW > 0 || LAYOUT == LAYOUT_Q6K)
+            bulk_g2s_hint(stages + (size_t)s * L.stage + L.pay,
+                          reinterpret_cast<const char*>(a.scales) + gemv_sc_off<LAYOUT>(row0, nb),
+                          sb, &bars[s], pol);
     };
     if (tid == 0) {
         for (int s = 0; s < S; s++) mbar_init(&bars[s], 1);
@@ -383,6 +544,35 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
         cbr[k] = in ? q.cb[b] : 0;
         sbr[k] = in ? q.sb[b] : 0.f;
     }
+    // k-quants: sb * (sum of the unit's low-run / high-run integers), for the
+    // sub-blocks' min terms; each unit sits at the same place in its
+    // super-block for all of this lane's units (b % 8 == lane % 8), so the
+    // scale/min pair it reads is fixed per lane: sub-blocks 2c and 2c+1
+    float xsl[BPL], xsh[BPL];
+    const int kc = (lane & 7) >> 1;
+    if constexpr (KQ) {
+#pragma unroll
+        for (int k = 0; k < BPL; k++) {
+            int sl = 0, sh = 0, tl = 0, th = 0, ul = 0, uh = 0;
+            const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
+            const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
+            const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
+            const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
+            const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
+            const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                sl = dp4a_uu(0x01010101u, a0[t], sl);
+                sh = dp4a_uu(0x01010101u, b0[t], sh);
+                tl = dp4a_uu(0x01010101u, a1[t], tl);
+                th = dp4a_uu(0x01010101u, b1[t], th);
+                ul = dp4a_us(0x01010101u, a2[t], ul);
+                uh = dp4a_us(0x01010101u, b2[t], uh);
+            }
+            xsl[k] = sbr[k] * (float)(sl + 256 * tl + 65536 * ul);
+            xsh[k] = sbr[k] * (float)(sh + 256 * th + 65536 * uh);
+        }
+    }
 
     unsigned long long best = argmax_key_init();
     int failed = 0;
@@ -399,6 +589,11 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
         const long row0 = (blockIdx.x + (long)i * gridDim.x) * RC;
         const int rows = (int)min((long)RC, (long)a.N - row0);
         float* rb = red + (size_t)(i & 1) * RC * WPR;
+        float acc[RPW];
+        if constexpr (KQ) {
+            kq_chunk<LAYOUT, RPW, BPL, WPR>(pay, scs, nb, rows, slot, wsub, lane, kc, xa, xb, sbr,
+                                            xsl, xsh, acc);
+        } else {
         // all of this warp's loads first (RPW rows x BPL blocks), then the math
         uint4 w4[RPW][BPL];
         float dd[RPW][BPL];
@@ -416,7 +611,6 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
                                           : reinterpret_cast<const float*>(scs)[blk]);
             }
         }
-        float acc[RPW];
 #pragma unroll
         for (int j = 0; j < RPW; j++) {
             acc[j] = 0.f;
@@ -446,6 +640,7 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
                 const float T = fmaf((float)(s2l + s2h), 65536.0f, (float)s01);
                 acc[j] = fmaf(dd[j][k] * sbr[k], T, acc[j]);
             }
+        }
         }
         // transposed butterfly: the RPW row sums in 5 shuffles; afterwards lane
         // (32/RPW)*j holds the warp's partial of row slot*RPW + j
@@ -506,13 +701,20 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
 }
 
 // ---- host side ----------------------------------------------------------------
-// The streaming kernel handles K with K/32 a multiple of 8 (GGUF f16 scales)
-// or 4 (crate f32 scales), so every chunk copy is a multiple of 16 bytes, and
-// K <= 24576.
+// The streaming kernel handles K with K/32 a multiple of 8 (GGUF f16 scales,
+// whole k-quant super-blocks) or 4 (crate f32 scales), so every chunk copy is
+// a multiple of 16 bytes, and K <= 24576.
 inline bool sgemv_supported(int layout, int K) {
     const int nb = K / 32;
     if (K % 32 || nb > GemvC768::NB_MAX) return false;
-    return layout == LAYOUT_GGUF ? nb % 8 == 0 : nb % 4 == 0;
+    if (layout == LAYOUT_REF) return nb % 4 == 0;
+    if (nb % 8) return false;
+    if (layout == LAYOUT_Q6K) {  // every chunk's d values start 16-byte aligned: RC * nb/8 % 8 == 0
+        const int rc = nb <= GemvC96::NB_MAX ? 16 : nb <= GemvC192::NB_MAX ? 8
+                     : nb <= GemvC384::NB_MAX ? 4 : 1;
+        return (rc * (nb / 8)) % 8 == 0;
+    }
+    return true;
 }
 
 int launch_sgemv(cw_ctx* ctx, int layout, int pro, int epi, const GemvArgs& a, bool pdl);

@@ -2,11 +2,16 @@
 // in HBM as the file's blocks: the k-quants and F32 / F16 / BF16 / Q8_0 /
 // Q4_1 (formats and device code in cw_kquant.cuh).
 //
-// GEMV: one warp per output row; the 32 lanes split each super-block 8
+// GEMV: Q4_K / Q5_K (raw super-blocks) and Q6_K (the aligned split of
+// cw_q6_k_split) run on the streaming GEMV of cw_gemv.cuh: weights streamed
+// through shared memory, integer dp4a products against q24 activation
+// planes.  The per-row kernel below serves the other types and Q6_K in its
+// raw form: one warp per output row; the 32 lanes split each super-block 8
 // weights apiece (Q4_K/Q5_K lane l: 64-weight chunk l/8, 4 bytes of nibbles
 // at 4*(l%8) -> 4 low-nibble and 4 high-nibble weights; Q6_K lane t: half
 // t/16, weights l, l+1 (l = 2*(t%16)) at offsets 0/32/64/96 of the half),
 // x staged once per CTA in shared memory, f32 accumulation, warp reduction.
+#include "cw_gemv.cuh"
 #include "cw_kquant.cuh"
 
 namespace cw {
@@ -53,6 +58,28 @@ __global__ void k_kq_dequant(const uint8_t* __restrict__ wraw, long n_blocks,
     }
 }
 
+// One warp per super-block: the 210-byte block is 2-byte aligned, so it is
+// moved as 105 half-words (104 to the payload plane, the last one is d).
+__global__ void k_q6k_split(const uint8_t* __restrict__ raw, long nsb, uint8_t* __restrict__ pay,
+                            __half* __restrict__ d) {
+    const int lane = threadIdx.x & 31;
+    const long w0 = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+    const long nw = ((long)gridDim.x * blockDim.x) >> 5;
+    for (long s = w0; s < nsb; s += nw) {
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(raw + s * 210);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(pay + s * 208);
+        for (int i = lane; i < 104; i += 32) dst[i] = src[i];
+        if (lane == 0) d[s] = __ushort_as_half(src[104]);
+    }
+}
+
+int q6k_split(cw_ctx* ctx, const uint8_t* raw, size_t nsb, uint8_t* pay, __half* d) {
+    if (!nsb) return CW_OK;
+    const int grid = (int)std::min<size_t>((nsb + 7) / 8, (size_t)ctx->sm_count * 16);
+    k_q6k_split<<<grid, 256, 0, ctx->stream>>>(raw, (long)nsb, pay, d);
+    return check_launch("q6_k split");
+}
+
 int kq_block_bytes(int type) {
     switch (type) {
         case CW_GGUF_Q4_K: return KQ<CW_GGUF_Q4_K>::BYTES;
@@ -89,9 +116,19 @@ int cw_kquant_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, int type, size_t in_f, size_
     CW_TRY(arena_get(ctx, out_f, out, &ey));
     ex = &ctx->bufs[x];
     ew = &ctx->bufs[w];
+    OpScope scope(ctx, "kquant_gemv");
+    if ((type == CW_GGUF_Q4_K || type == CW_GGUF_Q5_K) && sgemv_supported(LAYOUT_Q4K, (int)in_f)) {
+        GemvArgs a = {};
+        a.payload = (const uint8_t*)ew->ptr;
+        a.K = (int)in_f;
+        a.N = (int)out_f;
+        a.x = (const float*)ex->ptr;
+        a.y = (float*)ey->ptr;
+        return launch_sgemv(ctx, type == CW_GGUF_Q4_K ? LAYOUT_Q4K : LAYOUT_Q5K, PRO_X, EPI_STORE,
+                            a, false);
+    }
     const int grid = (int)std::min<size_t>((out_f + 7) / 8, (size_t)ctx->sm_count * 8);
     const size_t smem = in_f * 4;
-    OpScope scope(ctx, "kquant_gemv");
     auto go = [&](auto kern) -> int {
         if (smem > 48 * 1024)
             CW_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -110,6 +147,51 @@ int cw_kquant_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, int type, size_t in_f, size_
         case CW_GGUF_Q4_1: return go(k_kq_gemv<CW_GGUF_Q4_1>);
         default: return go(k_kq_gemv<CW_GGUF_Q6_K>);
     }
+}
+
+int cw_q6_k_split(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out) {
+    clear_error();
+    CW_CHECK(ctx && out && rows > 0 && in_f % 256 == 0 && in_f > 0, CW_ERR_INVALID_ARG,
+             "cw_q6_k_split: bad arguments");
+    const size_t nsb = rows * (in_f / 256);
+    BufEntry *ew, *eo;
+    CW_TRY(buf_get(ctx, w, &ew, nsb * 210, "cw_q6_k_split(w)"));
+    cudaSetDevice(ctx->device);
+    CW_TRY(buf_new(ctx, nsb * 210, BUF_PERSISTENT, out, &eo));
+    ew = &ctx->bufs[w];
+    eo->q6k_split = true;
+    eo->rows = rows;
+    eo->in_f = in_f;
+    eo->scale_off = nsb * 208;
+    uint8_t* base = (uint8_t*)eo->ptr;
+    return q6k_split(ctx, (const uint8_t*)ew->ptr, nsb, base, (__half*)(base + nsb * 208));
+}
+
+int cw_q6_k_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out) {
+    clear_error();
+    CW_CHECK(ctx && out && out_f > 0 && out_f < (1u << 31), CW_ERR_INVALID_ARG,
+             "cw_q6_k_gemv: bad arguments");
+    CW_CHECK(sgemv_supported(LAYOUT_Q6K, (int)in_f), CW_ERR_UNSUPPORTED,
+             "cw_q6_k_gemv: in_f=%zu not handled (a multiple of 256, at most 24576)", in_f);
+    BufEntry *ex, *ew, *ey;
+    CW_TRY(buf_get(ctx, x, &ex, in_f * 4, "cw_q6_k_gemv(x)"));
+    CW_TRY(buf_get(ctx, w, &ew, 0, "cw_q6_k_gemv(w)"));
+    CW_CHECK(ew->q6k_split && ew->rows == out_f && ew->in_f == in_f, CW_ERR_INVALID_ARG,
+             "cw_q6_k_gemv: buffer %llu is not a split Q6_K weight of [%zu, %zu]",
+             (unsigned long long)w, out_f, in_f);
+    cudaSetDevice(ctx->device);
+    CW_TRY(arena_get(ctx, out_f, out, &ey));
+    ex = &ctx->bufs[x];
+    ew = &ctx->bufs[w];
+    OpScope scope(ctx, "kquant_gemv");
+    GemvArgs a = {};
+    a.payload = (const uint8_t*)ew->ptr;
+    a.scales = (const char*)ew->ptr + ew->scale_off;
+    a.K = (int)in_f;
+    a.N = (int)out_f;
+    a.x = (const float*)ex->ptr;
+    a.y = (float*)ey->ptr;
+    return launch_sgemv(ctx, LAYOUT_Q6K, PRO_X, EPI_STORE, a, false);
 }
 
 int cw_kquant_dequant(cw_ctx* ctx, cw_buf w, int type, size_t rows, size_t in_f, cw_buf* out) {

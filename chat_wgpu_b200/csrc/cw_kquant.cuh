@@ -417,4 +417,8 @@ __device__ __forceinline__ float embed_elem(const uint8_t* __restrict__ payload,
     return __fmul_rn(d, (float)(q - 8));
 }
 
+// Split nsb raw Q6_K super-blocks (210 bytes each) into the streaming GEMV's
+// aligned planes: pay [nsb][208] (ql, qh, scales) and d [nsb] (f16).
+int q6k_split(cw_ctx* ctx, const uint8_t* raw, size_t nsb, uint8_t* pay, __half* d);
+
 }  // namespace cw

@@ -579,8 +579,16 @@ static int kq_fgemv_t(cw_ctx* ctx, const FArgs& a) {
     return check_launch("k-quant gemv");
 }
 
-// One projection of the per-stage step over weight `w`: the streaming Q4_0
-// GEMV, or the k-quant GEMV for raw Q4_K / Q5_K / Q6_K blocks.
+// Q4_K / Q5_K projections the streaming GEMV takes (the gated unit needs two
+// rows per chunk: K <= 12288).
+template <int EPI>
+static bool kq_stream_ok(int K) {
+    return sgemv_supported(LAYOUT_Q4K, K) && (EPI != EPI_GLU || K / 32 <= GemvC384::NB_MAX);
+}
+
+// One projection of the per-stage step over weight `w`: the streaming GEMV
+// (Q4_0 planes, raw Q4_K / Q5_K super-blocks, the Q6_K split), or the
+// per-row GEMV for the other raw types.
 template <int PRO, int EPI>
 static int proj(cw_ctx* ctx, const QW& w, FArgs a) {
     a.payload = w.payload;
@@ -589,9 +597,19 @@ static int proj(cw_ctx* ctx, const QW& w, FArgs a) {
     a.N = w.rows;
     switch (w.type) {
         case GGML_Q4_0: return fgemv<PRO, EPI>(ctx, a);
-        case GGML_Q4_K: return kq_fgemv_t<GGML_Q4_K, PRO, EPI>(ctx, a);
-        case GGML_Q5_K: return kq_fgemv_t<GGML_Q5_K, PRO, EPI>(ctx, a);
-        case GGML_Q6_K: return kq_fgemv_t<GGML_Q6_K, PRO, EPI>(ctx, a);
+        case GGML_Q4_K:
+            if (kq_stream_ok<EPI>(a.K)) return launch_sgemv(ctx, LAYOUT_Q4K, PRO, EPI, a, ctx->pdl);
+            return kq_fgemv_t<GGML_Q4_K, PRO, EPI>(ctx, a);
+        case GGML_Q5_K:
+            if (kq_stream_ok<EPI>(a.K)) return launch_sgemv(ctx, LAYOUT_Q5K, PRO, EPI, a, ctx->pdl);
+            return kq_fgemv_t<GGML_Q5_K, PRO, EPI>(ctx, a);
+        case GGML_Q6_K:
+            if (w.split && kq_stream_ok<EPI>(a.K)) {
+                a.payload = w.split;
+                a.scales = w.split_d;
+                return launch_sgemv(ctx, LAYOUT_Q6K, PRO, EPI, a, ctx->pdl);
+            }
+            return kq_fgemv_t<GGML_Q6_K, PRO, EPI>(ctx, a);
         case GGML_F32: return kq_fgemv_t<GGML_F32, PRO, EPI>(ctx, a);
         case GGML_F16: return kq_fgemv_t<GGML_F16, PRO, EPI>(ctx, a);
         case GGML_BF16: return kq_fgemv_t<GGML_BF16, PRO, EPI>(ctx, a);
@@ -687,6 +705,21 @@ static int load_vec(cw_model* m, const GgufFile& f, const std::string& name, siz
     return CW_OK;
 }
 
+// Q6_K weight: add the aligned split the streaming decode GEMV reads (same
+// bytes as the raw blocks: payload plane, then the f16 d plane).
+static int q6k_add_split(cw_model* m, QW* w) {
+    if (w->type != GGML_Q6_K || !sgemv_supported(LAYOUT_Q6K, w->in_f)) return CW_OK;
+    const size_t nsb = (size_t)w->rows * (w->in_f / 256);
+    void* p = nullptr;
+    CW_TRY(dev_alloc(m, nsb * 210, &p));
+    uint8_t* base = (uint8_t*)p;
+    CW_TRY(q6k_split(m->ctx, w->payload, nsb, base, (__half*)(base + nsb * 208)));
+    CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    w->split = base;
+    w->split_d = (const __half*)(base + nsb * 208);
+    return CW_OK;
+}
+
 // Load one or more Q4_0 [rows_i, in_f] tensors as a single packed weight.
 // interleave: two parts with equal rows become rows p0[0], p1[0], p0[1], ...
 // A token embedding or LM head stored as GGUF Q6_K (real Q4_0 checkpoints often
@@ -716,7 +749,7 @@ static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out, int 
     out->in_f = (int)in_f;
     out->type = GGML_Q6_K;
     out->buf = m->owned.back();
-    return CW_OK;
+    return q6k_add_split(m, out);
 }
 
 // Q4_0 (packed planes) or Q6_K (raw), by the tensor's type.
@@ -785,7 +818,7 @@ static int load_kq(cw_model* m, const GgufFile& f, const std::vector<std::string
     out->type = (int)type;
     out->buf = m->owned.back();
     m->info.weight_bytes += stage.size();
-    return CW_OK;
+    return q6k_add_split(m, out);
 }
 
 // One projection (or a stack / interleave of several) by the tensors' type:
@@ -1032,16 +1065,22 @@ static int model_load(cw_model* m, const std::string& path) {
                          : load_proj(m, f, qkv, I.dim, false, &l.qkv));
             CW_CHECK((size_t)l.qkv.rows == (qd + 2 * kvd) / T, CW_ERR_FORMAT,
                      "layer %u: q/k/v rows %d", i, l.qkv.rows);
-        } else {  // mixed types: three weights over one qkv vector
+        } else {  // mixed types: two or three weights over one qkv vector
             CW_CHECK(T == 1, CW_ERR_UNSUPPORTED,
                      "layer %u: q/k/v of different types; tensor parallelism takes Q4_0", i);
             l.qkv_split = true;
-            CW_TRY(load_proj(m, f, {qkv[0]}, I.dim, false, &l.q));
-            CW_TRY(load_proj(m, f, {qkv[1]}, I.dim, false, &l.k));
-            CW_TRY(load_proj(m, f, {qkv[2]}, I.dim, false, &l.v));
-            CW_CHECK((size_t)l.q.rows == qd && (size_t)l.k.rows == kvd && (size_t)l.v.rows == kvd,
-                     CW_ERR_FORMAT, "layer %u: q/k/v rows %d/%d/%d", i, l.q.rows, l.k.rows,
-                     l.v.rows);
+            // consecutive tensors of one type stack into one weight (one GEMV
+            // launch): q+k | v, or q | k+v; slots left over keep 0 rows
+            QW* dst[3] = {&l.q, &l.k, &l.v};
+            for (int j = 0, slot = 0; j < 3; slot++) {
+                int e = j + 1;
+                while (e < 3 && qt[e] == qt[j]) e++;
+                CW_TRY(load_proj(m, f, std::vector<std::string>(qkv.begin() + j, qkv.begin() + e),
+                                 I.dim, false, dst[slot]));
+                j = e;
+            }
+            CW_CHECK((size_t)(l.q.rows + l.k.rows + l.v.rows) == qd + 2 * kvd, CW_ERR_FORMAT,
+                     "layer %u: q/k/v rows %d/%d/%d", i, l.q.rows, l.k.rows, l.v.rows);
         }
         if (f.has(p + "attn_q.bias")) {  // Linear bias (layers.rs:20-21,59-61)
             I.qkv_bias = 1;
@@ -1211,9 +1250,10 @@ static int enqueue_step_core(cw_session* s, bool decode) {
         a.bias = l.qkv_bias;
         if (!l.qkv_split) {
             CW_TRY((proj<PRO_NORM, EPI_STORE>(ctx, l.qkv, a)));
-        } else {  // the q, k and v slices of the qkv vector (one prologue each)
+        } else {  // the slices of the qkv vector by weight type (one prologue each)
             size_t off = 0;
             for (const QW* w : {&l.q, &l.k, &l.v}) {
+                if (!w->rows) continue;
                 FArgs b = a;
                 b.y = s->qkv + off;
                 b.bias = l.qkv_bias ? l.qkv_bias + off : nullptr;

@@ -37,6 +37,12 @@ struct QW {  // packed Q4_0 weight (type 2), or raw GGUF Q6_K blocks (type 14)
     int rows = 0, in_f = 0;
     cw_buf buf = 0;
     int type = 2;
+    // Q6_K: the aligned split the streaming decode GEMV reads (payload plane
+    // [rows][in_f/256][208] and f16 d plane), beside the raw blocks that the
+    // embedding lookups and the other kernels read; null where the streaming
+    // GEMV does not take in_f
+    const uint8_t* split = nullptr;
+    const __half* split_d = nullptr;
 };
 
 struct Layer {
@@ -44,7 +50,8 @@ struct Layer {
     float *post_attn = nullptr, *post_ffw = nullptr, *qkv_bias = nullptr;
     QW qkv, wo, gate_up, down;
     // q, k and v of different k-quant types (Q4_K_M files keep some v in Q6_K)
-    // stay three weights, each writing its slice of the qkv vector
+    // stay two or three weights (consecutive ones of one type stacked), each
+    // writing its slice of the qkv vector; unused slots have 0 rows
     bool qkv_split = false;
     QW q, k, v;
 };

@@ -64,3 +64,13 @@ def kquant_gemv(ctx, x: Buffer, w: Buffer, qtype: int, in_f: int, out_f: int) ->
 def kquant_dequant(ctx, w: Buffer, qtype: int, rows: int, in_f: int) -> Buffer:
     """Exact f32 dequantisation of a raw k-quant weight [rows, in_f]."""
     return op(ctx, "cw_kquant_dequant", w.handle, int(qtype), int(rows), int(in_f))
+
+
+def q6_k_split(ctx, w: Buffer, rows: int, in_f: int) -> Buffer:
+    """Raw Q6_K blocks -> the streaming GEMV's aligned planes (a new buffer)."""
+    return op(ctx, "cw_q6_k_split", w.handle, int(rows), int(in_f))
+
+
+def q6_k_gemv(ctx, x: Buffer, w: Buffer, in_f: int, out_f: int) -> Buffer:
+    """y[out_f] = W x over a q6_k_split weight (the streaming GEMV)."""
+    return op(ctx, "cw_q6_k_gemv", x.handle, w.handle, int(in_f), int(out_f))

@@ -57,7 +57,8 @@ KQ_TYPES = {"q4_k": (12, 144), "q5_k": (13, 176), "q6_k": (14, 210)}
 
 def bench_kquant(ctx: GpuContext, qname: str, in_f: int, out_f: int, iters: int = 50,
                  seed: int = 0, l2_bytes: int = 126 << 20) -> dict:
-    """k-quant GEMV (cw_kquant_gemv): device time per launch from the context
+    """k-quant GEMV (cw_kquant_gemv; Q6_K: cw_q6_k_gemv over the aligned split
+    the model's decode step reads): device time per launch from the context
     profiler, cycling through copies that exceed 4x L2."""
     qtype, bb = KQ_TYPES[qname]
     rng = np.random.default_rng(seed)
@@ -68,14 +69,25 @@ def bench_kquant(ctx: GpuContext, qname: str, in_f: int, out_f: int, iters: int 
     raw[:, off:off + 2] = rng.uniform(1e-3, 1e-2, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
     n_w = max(2, min(64, -(-4 * l2_bytes // wbytes)))
     ws = [ctx.storage_bytes(raw.ravel()) for _ in range(n_w)]
+    if qtype == 14:
+        split = [q4.q6_k_split(ctx, w, out_f, in_f) for w in ws]
+        for w in ws:
+            w.release()
+        ws = split
+
+        def gemv(w):
+            return q4.q6_k_gemv(ctx, x, w, in_f, out_f)
+    else:
+        def gemv(w):
+            return q4.kquant_gemv(ctx, x, w, qtype, in_f, out_f)
     x = ctx.storage(rng.normal(0, 1, in_f).astype(np.float32))
     for w in ws[:2]:
-        q4.kquant_gemv(ctx, x, w, qtype, in_f, out_f)
+        gemv(w)
         ctx.reset_frame()
     ctx.sync()
     ctx.begin_profile()
     for i in range(max(iters, n_w)):
-        q4.kquant_gemv(ctx, x, ws[i % n_w], qtype, in_f, out_f)
+        gemv(ws[i % n_w])
         ctx.reset_frame()
     rep = {name: ms / c for name, c, ms in ctx.report_profile()}
     for w in ws:

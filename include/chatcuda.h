@@ -246,6 +246,17 @@ int cw_kquant_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, int type, size_t in_f, size_
                    cw_buf* out);
 /* Exact f32 dequantisation of the [rows, in_f] weight. */
 int cw_kquant_dequant(cw_ctx* ctx, cw_buf w, int type, size_t rows, size_t in_f, cw_buf* out);
+/* The Q6_K weight of dequant_q6_k (dequant.rs:102-131) as the streaming
+ * GEMV reads it: the file's 210-byte super-blocks are only 2-byte aligned,
+ * so they are split into a [rows][in_f/256][208] plane (ql, qh and the int8
+ * scales, as in the file) and a plane of the f16 d values; same bytes in
+ * total.  *out is a new persistent buffer (release it with cw_buf_release). */
+int cw_q6_k_split(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out);
+/* y[out_f] = W x over a cw_q6_k_split weight (in_f a multiple of 256, at most
+ * 24576): the sum of w x with w = d * scale * (q - 32) of dequant_q6_k, in
+ * integer dot products against the block-floating-point x of the Q4 GEMVs
+ * (within 1e-3 relative of the f32 dequantised product). */
+int cw_q6_k_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out);
 
 /* ---- model: src/model/{mod,qwen3,layers,cache}.rs --------------------------------------------- */
 typedef struct {

@@ -73,6 +73,45 @@ def test_kquant_gemv_vs_oracle(ctx, orc, qtype, in_f, out_f):
     w.release()
 
 
+@pytest.mark.parametrize("in_f,out_f", SHAPES)
+def test_q6_k_split_gemv_vs_oracle(ctx, orc, in_f, out_f):
+    """The streaming GEMV over the aligned Q6_K split (the decode step's form)
+    against the oracle's dequant_q6_k product and the per-row kernel."""
+    from chat_wgpu_b200 import CwError
+    from chat_wgpu_b200.kernels import q4
+    rng = np.random.default_rng(3 * in_f + out_f)
+    raw = kq_blocks(rng, Q6_K, out_f, in_f)
+    x = rng.normal(0, 1, in_f).astype(np.float32)
+    w = ctx.storage_bytes(raw.ravel())
+    ws = q4.q6_k_split(ctx, w, out_f, in_f)
+    xb = ctx.storage(x)
+    W = orc.dequant_q6_k(raw.ravel(), out_f * in_f).reshape(out_f, in_f).astype(np.float64)
+    y = ctx.read(q4.q6_k_gemv(ctx, xb, ws, in_f, out_f), out_f)
+    assert rel_err(y, W @ x.astype(np.float64)) < REL
+    # the per-row kernel over the raw blocks agrees too
+    y2 = ctx.read(q4.kquant_gemv(ctx, xb, w, Q6_K, in_f, out_f), out_f)
+    assert rel_err(y, y2.astype(np.float64)) < REL
+    with pytest.raises(CwError):  # a raw weight is not a split one
+        q4.q6_k_gemv(ctx, xb, w, in_f, out_f)
+    ws.release()
+    w.release()
+
+
+def test_q6_k_gemv_refuses_unaligned_chunks(ctx):
+    """in_f = 6400: 25 super-blocks per row, 4 rows per chunk -> a chunk's d
+    values would start 8 bytes off a 16-byte boundary; refused, not run."""
+    from chat_wgpu_b200 import CwError
+    from chat_wgpu_b200.kernels import q4
+    rng = np.random.default_rng(5)
+    raw = kq_blocks(rng, Q6_K, 8, 6400)
+    w = ctx.storage_bytes(raw.ravel())
+    ws = q4.q6_k_split(ctx, w, 8, 6400)
+    with pytest.raises(CwError):
+        q4.q6_k_gemv(ctx, ctx.storage(np.ones(6400, np.float32)), ws, 6400, 8)
+    ws.release()
+    w.release()
+
+
 def test_kquant_rejects_bad_shapes(ctx):
     from chat_wgpu_b200 import CwError
     from chat_wgpu_b200.kernels import q4
