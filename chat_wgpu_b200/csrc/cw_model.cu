@@ -1578,6 +1578,7 @@ int cw_session_create(cw_model* m, size_t max_seq, cw_session** out) {
     A((size_t)2 * I.n_layers * I.n_kv * sizeof(unsigned), (void**)&s->rdy);
     A((size_t)sample_params_size(), &s->smp_dev);
     A(qd * 4, (void**)&s->qtap);
+    A((qd + 2 * kvd) * 8, (void**)&s->qkv_words);
     if (rc == CW_OK) rc = sample_params_write(s);
     if (rc == CW_OK && (cudaMallocHost(&s->h_tok, sizeof(unsigned)) != cudaSuccess ||
                         cudaMallocHost(&s->h_tok_in, sizeof(unsigned)) != cudaSuccess))
@@ -1700,6 +1701,11 @@ int cw_session_begin(cw_session* s, const uint32_t* prompt, size_t n_prompt) {
     CW_CUDA(cudaMemsetAsync(s->rdy, 0,
                             (size_t)2 * s->m->info.n_layers * s->m->info.n_kv * sizeof(unsigned),
                             s->ctx->stream));
+    {  // tag 0, which no step uses
+        const cw_model_info& I = s->m->info;
+        CW_CUDA(cudaMemsetAsync(s->qkv_words, 0, (size_t)(I.n_heads + 2 * I.n_kv) * I.head_dim * 8,
+                                s->ctx->stream));
+    }
     CW_CUDA(cudaStreamSynchronize(s->ctx->stream));
     s->host_pos = 0;
     s->n_prompt = n_prompt;

@@ -143,6 +143,8 @@ struct cw_session {
     bool stopped = false;     // host view of DevState::stopped
     std::vector<cw::Tap> taps;  // active hook taps (force the per-stage step kernels)
     float* qtap = nullptr;      // the step's normed, rotated q (source of "q" taps)
+    // the persistent step's QKV rows as tagged 8-byte words (float | tag << 32)
+    unsigned long long* qkv_words = nullptr;
     // tensor parallelism over NVLink peer memory (cw_tp_p2p.cu): the all-
     // reduces of the per-stage step once cw_session_tp_attach mapped every
     // rank's exchange area (cw::TpP2P; null: NCCL)

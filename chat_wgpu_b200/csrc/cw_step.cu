@@ -186,10 +186,10 @@ static int ocol_rows(const cw_model_info& I, int grid) {
 
 // The stage list, uploaded to the device.  Per layer l (p = l % 2, q = 1 - p):
 //   attn_in    residual = H[p] + Y[q] + Z[q] (layer 0: the embedding row)
-//              -> rmsnorm -> QKV GEMV (+bias) -> qkv; each CTA also stores
-//              its slice of the residual to H[q], the next base; per kv
-//              group the rows stored are counted (qrdy)
-//   attention  (no grid barrier: each unit waits for its group's rows)
+//              -> rmsnorm -> QKV GEMV (+bias) -> qkv words tagged with the
+//              (step, layer); each CTA also stores its slice of the residual
+//              to H[q], the next base
+//   attention  (no grid barrier: each unit polls its group's tagged rows)
 //              QK-norm, RoPE, K/V row write, split-KV attention; the units of
 //              each kv head are counted (ardy)
 //   o_proj     (no grid barrier: each unit waits for its kv head's units)
@@ -382,7 +382,7 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     pp.emb_scales = m->embed.scales;
     pp.embed_scale = I.embed_scale;
     pp.hidden = s->hidden;
-    pp.qkv = s->qkv;
+    pp.qkv = s->qkv_words;
     pp.attn = s->attn;
     pp.prompt = s->prompt;
     pp.toks = s->toks;
@@ -396,7 +396,6 @@ static int build_variant(cw_session* s, int grid, int n_splits, size_t work, Ste
     pp.max_seq = (int)s->max_seq;
     pp.n_splits = n_splits;
     pp.n_layers = L;
-    pp.qrdy = s->rdy;
     pp.ardy = s->rdy + (size_t)L * I.n_kv;
     pp.zero_a = Y[lp];
     pp.zero_b = Z[lp];

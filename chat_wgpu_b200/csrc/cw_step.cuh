@@ -201,7 +201,11 @@ struct MParams {
     const __half* emb_scales;
     float embed_scale;
     float* hidden;
-    const float* qkv;
+    // the QKV rows as 8-byte words: float bits | tag << 32, the tag naming the
+    // (step, layer) that wrote them (mk_qkv_tag); the attention units poll the
+    // words of their kv group until the tag is theirs, so the hand-off needs
+    // no fence, counter or barrier
+    unsigned long long* qkv;
     float* attn;
     const unsigned* prompt;
     unsigned* toks;
@@ -212,12 +216,9 @@ struct MParams {
     int n_layers;
     int attn_min;  // keys per attention split before splitting further
     int window_next;  // window of the layer after a non-windowed one (alternating families)
-    // Ready counters [n_layers][n_kv], zeroed at the end of every step:
-    // qrdy counts the QKV rows of each kv group's heads stored this step
-    // (the attention units wait for (G + 2) * head_dim), ardy the attention
-    // units of each kv head finished (the O-projection units wait for the
-    // step's active split count).
-    unsigned* qrdy;
+    // Ready counters [n_layers][n_kv], zeroed at the end of every step: the
+    // attention units of each kv head finished (the O-projection units wait
+    // for the step's active split count).
     unsigned* ardy;
     long long* zero_a;  // the last layer's accumulators, zeroed at the end of the step
     long long* zero_b;
@@ -274,6 +275,7 @@ struct MCtx {
     float* rowred;      // 2 x 64 row partials
     MShared* sh;
     int seq;            // chunks consumed by this CTA so far (same in every thread)
+    unsigned tag0;      // QKV word tag of layer 0 this step (mk_qkv_tag)
     int redsel;         // CTA-sum buffer of the next call
     int nch;            // chunks consumed (row-partial buffer parity)
     int pos;
@@ -319,6 +321,14 @@ __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned 
 }
 __device__ __forceinline__ void red_release_add_u32(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
     unsigned v;
@@ -1020,43 +1030,15 @@ __device__ inline bool mk_gemv(const MParams& p, const MStage& S, MCtx& c) {
                 S.y[row] = vv;
                 const unsigned long long kk = argmax_key(vv, (unsigned)row);
                 best = kk > best ? kk : best;
-            } else {
-                S.y[row] = S.bias ? vv + add : vv;
+            } else {  // one tagged word per row (the attention units poll it)
+                const float v = S.bias ? vv + add : vv;
+                st_relaxed_u64(p.qkv + row, ((unsigned long long)(c.tag0 + S.layer) << 32) |
+                                                __float_as_uint(v));
             }
         }
     }
     if (c.stamp && tid == 0) c.stamp[2] = global_ns();
     mk_clk(c, CLK_MAIN);
-    if (EPI == EPI_STORE && p.qrdy) {
-        // QKV rows stored: add, per kv group, the rows of its q heads, k and v
-        // this CTA wrote (the attention units wait for (G + 2) * head_dim)
-        mk_sync();
-        if (tid == 0) {
-            const int hd = p.hd, ghd = (p.n_heads / p.n_kv) * hd;
-            const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
-            unsigned* ctr = p.qrdy + (size_t)S.layer * p.n_kv;
-            for (long chunk = blockIdx.x; chunk < S.nchunks; chunk += gridDim.x) {
-                int r = (int)(chunk * RC);
-                const int end = min(r + RC, S.N);
-                while (r < end) {
-                    int g, seg;
-                    if (r < qd) {
-                        g = r / ghd;
-                        seg = (g + 1) * ghd;
-                    } else if (r < qd + kvd) {
-                        g = (r - qd) / hd;
-                        seg = qd + (g + 1) * hd;
-                    } else {
-                        g = (r - qd - kvd) / hd;
-                        seg = qd + kvd + (g + 1) * hd;
-                    }
-                    seg = min(seg, end);
-                    red_release_add_u32(ctr + g, (unsigned)(seg - r));
-                    r = seg;
-                }
-            }
-        }
-    }
     if (EPI == EPI_HEAD) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -1226,31 +1208,58 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
         const int g = u % p.n_kv, split = u / p.n_kv;
         int jlo, jhi;
         attn_range(seq, S.window, split, n_active, &jlo, &jhi);
-        // this kv group's q/k/v rows of the QKV stage (no grid barrier between)
-        if (tid == 0)
-            mk_wait_count(p, c, p.qrdy + (size_t)S.layer * p.n_kv + g, (unsigned)((G + 2) * hd));
-        mk_sync();
-        if (c.sh->abort) return false;
         const bool holds = pos >= jlo && pos < jhi;
         const int nrows = G + (holds ? 1 : 0);  // <= 5 rows, one per warp
-        // every global input of the prologue is requested before any is used:
-        // this warp's q/k row and its norm gains, the new V row, the RoPE
-        // frequency of this thread's first rotated pair
+        // this warp's q/k row (the unit holding this step's position also the
+        // k and v rows it appends to the cache) from the QKV stage, with no
+        // barrier or counter between: each lane polls its tagged words until
+        // they carry this (step, layer)'s tag; the norm gains are requested first
         const int r = warp;
         const bool isq = r < G, has_row = r < nrows;
         const float* nw = isq ? S.q_norm : S.k_norm;
         float vv[EPL], wv[EPL];
-        {
-            const float* src = isq ? p.qkv + (size_t)(g * G + r) * hd : p.qkv + qd + (size_t)g * hd;
 #pragma unroll
-            for (int e = 0; e < EPL; e++) {
-                const int d = lane + 32 * e;
-                const bool in = has_row && d < hd;
-                vv[e] = in ? __ldcg(src + d) : 0.f;
-                wv[e] = (in && nw) ? __ldg(nw + d) : 0.f;
-            }
+        for (int e = 0; e < EPL; e++) {
+            const int d = lane + 32 * e;
+            wv[e] = (has_row && d < hd && nw) ? __ldg(nw + d) : 0.f;
         }
-        const float vnew = (holds && tid < hd) ? __ldcg(p.qkv + qd + kvd + (size_t)g * hd + tid) : 0.f;
+        float vnew = 0.f;
+        {
+            const unsigned tag = c.tag0 + S.layer;
+            const unsigned long long* src =
+                isq ? p.qkv + (size_t)(g * G + r) * hd : p.qkv + qd + (size_t)g * hd;
+            const unsigned long long* vsrc = p.qkv + qd + kvd + (size_t)g * hd + tid;
+            const bool wantv = holds && tid < hd;
+            unsigned long long w[EPL], wn = 0;
+            uint64_t t0 = 0;
+            for (unsigned it = 1;; it++) {
+                bool all = true;
+#pragma unroll
+                for (int e = 0; e < EPL; e++) {
+                    const int d = lane + 32 * e;
+                    const bool in = has_row && d < hd;
+                    w[e] = in ? ld_relaxed_u64(src + d) : 0ull;
+                    all = all && (!in || (unsigned)(w[e] >> 32) == tag);
+                }
+                if (wantv) {
+                    wn = ld_relaxed_u64(vsrc);
+                    all = all && (unsigned)(wn >> 32) == tag;
+                }
+                if (all) break;
+                if ((it & 15) == 0) {  // bounded as mk_wait_count
+                    const uint64_t now = global_ns();
+                    if (t0 == 0) t0 = now;
+                    if (ld_volatile_i32(p.status) != 0 || now - t0 > MK_WAIT_NS) {
+                        atomicExch(p.status, (int)DEV_TIMEOUT);
+                        *reinterpret_cast<volatile int*>(&c.sh->abort) = 1;
+                        break;
+                    }
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < EPL; e++) vv[e] = __uint_as_float((unsigned)w[e]);
+            vnew = __uint_as_float((unsigned)wn);
+        }
         if (has_row) {  // QK-norm (qwen3.rs:154-155)
             float* dst = isq ? qs + (size_t)r * hd : ks;
             if (nw) {
@@ -1270,6 +1279,7 @@ __device__ inline bool mk_attn(const MParams& p, const MStage& S, MCtx& c) {
         }
         mk_clk(c, CLK_LOADED);  // attention: inputs arrived, QK-norm done
         mk_sync();
+        if (c.sh->abort) return false;
         for (int i = tid; i < nrows * half; i += MK_THREADS) {  // RoPE (rope.wgsl:25-34)
             const int rr = i / half, kq = i - rr * half;
             float* row = rr < G ? qs + (size_t)rr * hd : ks;
@@ -1458,6 +1468,11 @@ __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
     const int pos = p.st->pos;
     const unsigned tok = p.st->token;
     const unsigned long long base = p.st->bar_base;
+    // QKV word tags: (step's first grid-barrier index) + 1 + layer.  The
+    // barrier count only grows and a step passes more barriers (two per
+    // layer) than it has layers, so no (step, layer) reuses a tag of a word
+    // still in the buffer; the session clears the buffer (tag 0) at its start.
+    c.tag0 = (unsigned)(base / gridDim.x) + 1u;
     // fault injection (tests of the timeout path): the first grid barrier
     // waits for a count no CTA reaches and gives up after stall_us
     const unsigned stall_us = p.st->stall_us;
@@ -1544,10 +1559,7 @@ __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
     if (sh.last) {
         __threadfence();
         const int nc = p.n_layers * p.n_kv;
-        for (int i = tid; i < nc; i += MK_THREADS) {
-            p.qrdy[i] = 0;
-            p.ardy[i] = 0;
-        }
+        for (int i = tid; i < nc; i += MK_THREADS) p.ardy[i] = 0;
         for (int i = tid; i < p.dim; i += MK_THREADS) {
             *acc_at(p.zero_a, i) = 0;
             *acc_at(p.zero_b, i) = 0;
