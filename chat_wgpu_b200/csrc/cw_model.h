@@ -118,7 +118,7 @@ struct cw_session {
     // the O-projection and FFN partial sums by layer parity (Y0, Y1, Z0, Z1)
     long long* racc = nullptr;
     float* hid2 = nullptr;    // the persistent step's residual base, two buffers [2][dim]
-    unsigned* rdy = nullptr;  // its ready counters [2][n_layers][n_kv]
+    unsigned* rdy = nullptr;  // its attention-done counters ([n_layers][n_kv], after a spare half)
     cw::DevState* st = nullptr;
     int n_splits = 1;
     bool use_graph = true;

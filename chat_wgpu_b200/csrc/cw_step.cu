@@ -200,8 +200,8 @@ static int ocol_rows(const cw_model_info& I, int grid) {
 //              Y[q] and Z[q] (its slice of rows)
 // and the LM head on H[L%2] + Y + Z of the last layer.  Y and Z are fixed-
 // point int64 accumulators (s->racc: Y[0], Y[1], Z[0], Z[1]), H two f32
-// buffers (s->hid2); the ready counters, and the last layer's Y and Z, are
-// zeroed by the last CTA of every step.
+// buffers (s->hid2); the attention-done counters, and the last layer's Y
+// and Z, are zeroed by the last CTA of every step.
 static int build_variant(cw_session* s, int grid, int n_splits, size_t work, StepVariant* V,
                          size_t* smem_need) {
     cw_model* m = s->m;

@@ -1499,7 +1499,8 @@ __global__ void __launch_bounds__(MK_BLOCK, 1) k_step(MParams p) {
     unsigned nbar = 0;  // grid barriers passed this step
     for (int si = 0; si < p.n_stages && ok; si++) {
         if (si > 0) {
-            // the attention and O-projection stages wait on ready counters
+            // the attention stage polls the tagged QKV words and the
+            // O-projection stage waits on the attention-done counters
             // instead; the CTA barrier publishes the stage descriptor
             const int kind = iss[si].kind;
             if (kind == SK_ATTN || kind == SK_OCOL) {

@@ -1,7 +1,8 @@
 """The timeout path of the persistent step, exercised without a GPU fault.
 
-Every device-side wait of the step (grid barriers, ready counters, the
-weight ring's mbarriers) is bounded by %globaltimer and reports through the
+Every device-side wait of the step (grid barriers, the attention-done
+counters, the polls of the tagged QKV words, the weight ring's mbarriers)
+is bounded by %globaltimer and reports through the
 context's status word.  cw_session_inject_stall makes the next step's first
 grid barrier wait for a count no CTA reaches; the step must give up after the
 injected limit, every CTA must leave (draining its bulk copies), the next
