@@ -207,7 +207,7 @@ class Clocks:
 # DRAM bytes (read + write) per launch of the dominant kernel from one ncu
 # capture of this bench's workload (profiles/decode_step_persistent_qwen3_0.6b.md:
 # dram throughput x duration of the decode launch at position 130).
-NCU_TRAFFIC = {("qwen3-0.6b", "decode_step"): 370.0e6}
+NCU_TRAFFIC = {("qwen3-0.6b", "decode_step"): 369.4e6}
 NCU_TRAFFIC_SRC = "ncu, one decode_step launch at position 130 (profiles/decode_step_persistent_qwen3_0.6b.md)"
 
 
