@@ -357,23 +357,24 @@ __device__ __forceinline__ void gemv_prologue(const GemvArgs& a, const Q24& q, f
 // of a 16-bit field.  Returns d*scale and dmin*min (exact in f32).
 __device__ __forceinline__ void kq_scales(const uint4& h, int c, float& alo, float& ahi,
                                           float& blo, float& bhi) {
+    // c is fixed per lane: the pair's masks are selects, not a branch
     const int sh = 16 * (c & 1);
+    const bool big = c >= 2;
+    const unsigned lowm = big ? 0x0f0fu : 0x3f3fu, hm = big ? 0x3030u : 0u;
     const unsigned y2 = h.y >> sh, z2 = h.z >> sh;
-    unsigned scp, mp;
-    if (c >= 2) {
-        const unsigned w2 = h.w >> sh;
-        scp = (w2 & 0x0f0fu) | ((y2 >> 2) & 0x3030u);
-        mp = ((w2 >> 4) & 0x0f0fu) | ((z2 >> 2) & 0x3030u);
-    } else {
-        scp = y2 & 0x3f3fu;
-        mp = z2 & 0x3f3fu;
-    }
+    const unsigned a2 = (big ? h.w : h.y) >> sh;
+    const unsigned scp = (a2 & lowm) | ((y2 >> 2) & hm);
+    const unsigned mp = ((big ? a2 >> 4 : z2) & lowm) | ((z2 >> 2) & hm);
     const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu)));
     const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-    alo = d * (float)(scp & 0xffu);
-    ahi = d * (float)((scp >> 8) & 0xffu);
-    blo = dm * (float)(mp & 0xffu);
-    bhi = dm * (float)((mp >> 8) & 0xffu);
+    // x (0..63) as the float 2^23 + x made from its bits, and d * x as
+    // fma(d, 2^23 + x, -d * 2^23): one rounding of the exact d * x, which
+    // has at most 17 significant bits, so the product is exact as before
+    const float nd = -8388608.0f * d, ndm = -8388608.0f * dm;
+    alo = fmaf(d, __uint_as_float(0x4B000000u | (scp & 0xffu)), nd);
+    ahi = fmaf(d, __uint_as_float(0x4B000000u | ((scp >> 8) & 0xffu)), nd);
+    blo = fmaf(dm, __uint_as_float(0x4B000000u | (mp & 0xffu)), ndm);
+    bhi = fmaf(dm, __uint_as_float(0x4B000000u | ((mp >> 8) & 0xffu)), ndm);
 }
 
 // One stage of the k-quant GEMV: this warp's RPW rows x BPL units of the
