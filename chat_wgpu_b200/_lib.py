@@ -99,6 +99,8 @@ SIGNATURES = {
     "cw_kquant_dequant": [_vp, _buf, C.c_int, _sz, _sz, _pbuf],
     "cw_q6_k_split": [_vp, _buf, _sz, _sz, _pbuf],
     "cw_q6_k_gemv": [_vp, _buf, _buf, _sz, _sz, _pbuf],
+    "cw_q8_0_split": [_vp, _buf, _sz, _sz, _pbuf],
+    "cw_q8_0_gemv": [_vp, _buf, _buf, _sz, _sz, _pbuf],
     "cw_q4_0_gemv_bench": [_vp, _buf, C.POINTER(C.c_uint64), _sz, _sz, _sz, _sz,
                            C.POINTER(C.c_double)],
     "cw_model_load_gguf": [_vp, C.c_char_p, C.POINTER(_vp)],

@@ -62,6 +62,9 @@ struct BufEntry {
     // Set for a Q6_K weight split for the streaming GEMV (cw_q6_k_split):
     // [rows][in_f/256][208] payload, f16 d plane at scale_off.
     bool q6k_split = false;
+    // Set for a Q8_0 weight split for the streaming GEMV (cw_q8_0_split):
+    // [rows][in_f/32][32] codes, f16 scale plane at scale_off.
+    bool q8_split = false;
 };
 
 struct ProfRec {

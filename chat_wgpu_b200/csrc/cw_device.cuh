@@ -53,6 +53,18 @@ __device__ __forceinline__ int dp4a_us(unsigned a, unsigned b, int c) {
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
+// d = c + sum_i a.s8[i] * b.u8[i]
+__device__ __forceinline__ int dp4a_su(unsigned a, unsigned b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// d = c + sum_i a.s8[i] * b.s8[i]
+__device__ __forceinline__ int dp4a_ss(unsigned a, unsigned b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
 
 // Streaming 16-byte load of read-once weight data: bypass L1.
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
@@ -117,6 +129,9 @@ enum Q4Layout : int {
     // 16t + i (scale 8h + 2s + t), high nibbles the same + 64 (scale + 4);
     // their top two bits are bits 2s and 2s+4 of qh[32h + 16t + i].
     LAYOUT_Q6K = 4,
+    // GGUF Q8_0 split like Q4_0: int8 codes [rows][nb][32] (byte j = element
+    // j of the block) and f16 scales [rows][nb].
+    LAYOUT_Q8 = 5,
 };
 
 template <int LAYOUT>

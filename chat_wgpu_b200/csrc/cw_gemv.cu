@@ -93,6 +93,7 @@ int launch_sgemv(cw_ctx* ctx, int layout, int pro, int epi, const GemvArgs& a, b
     if (layout == LAYOUT_Q4K) return sgemv_layout<LAYOUT_Q4K>(ctx, pro, epi, a, pdl);
     if (layout == LAYOUT_Q5K) return sgemv_layout<LAYOUT_Q5K>(ctx, pro, epi, a, pdl);
     if (layout == LAYOUT_Q6K) return sgemv_layout<LAYOUT_Q6K>(ctx, pro, epi, a, pdl);
+    if (layout == LAYOUT_Q8) return sgemv_layout<LAYOUT_Q8>(ctx, pro, epi, a, pdl);
     return sgemv_layout<LAYOUT_GGUF>(ctx, pro, epi, a, pdl);
 }
 

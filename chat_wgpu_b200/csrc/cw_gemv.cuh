@@ -161,11 +161,12 @@ __host__ __device__ constexpr size_t al16(size_t v) { return (v + 15) / 16 * 16;
 // separate scale plane (f16 / f32 for Q4_0, none for the k-quants).
 template <int LAYOUT>
 __host__ __device__ constexpr int gemv_pbb() {
-    return LAYOUT == LAYOUT_Q4K ? 18 : LAYOUT == LAYOUT_Q5K ? 22 : LAYOUT == LAYOUT_Q6K ? 26 : 16;
+    return LAYOUT == LAYOUT_Q4K ? 18 : LAYOUT == LAYOUT_Q5K ? 22 : LAYOUT == LAYOUT_Q6K ? 26
+         : LAYOUT == LAYOUT_Q8  ? 32 : 16;
 }
 template <int LAYOUT>
 __host__ __device__ constexpr int gemv_sw() {
-    return LAYOUT == LAYOUT_GGUF ? 2 : LAYOUT == LAYOUT_REF ? 4 : 0;
+    return (LAYOUT == LAYOUT_GGUF || LAYOUT == LAYOUT_Q8) ? 2 : LAYOUT == LAYOUT_REF ? 4 : 0;
 }
 // Scale-plane bytes of `rows` rows and their offset in the plane: Q6_K's f16
 // d per super-block, its copy rounded up to 16 bytes (the plane's buffer is
@@ -591,7 +592,55 @@ __global__ void __launch_bounds__(256) k_sgemv(GemvArgs a, int S) {
         const int rows = (int)min((long)RC, (long)a.N - row0);
         float* rb = red + (size_t)(i & 1) * RC * WPR;
         float acc[RPW];
-        if constexpr (KQ) {
+        if constexpr (LAYOUT == LAYOUT_Q8) {
+            // int8 codes (32 bytes per block: elements 0-15 pair with the
+            // low planes, 16-31 with the high ones) times the q24 planes:
+            // sum q X = D0 + 256 D1 + 65536 D2, q signed
+            uint4 wa[RPW][BPL], wb[RPW][BPL];
+            float dd[RPW][BPL];
+#pragma unroll
+            for (int j = 0; j < RPW; j++) {
+                const int r = slot * RPW + j;
+#pragma unroll
+                for (int k = 0; k < BPL; k++) {
+                    const int b = wsub * 32 + lane + k * 32 * WPR;
+                    const bool in = r < rows && b < nb;
+                    const size_t blk = in ? (size_t)r * nb + b : 0;
+                    const uint4 z = make_uint4(0, 0, 0, 0);
+                    wa[j][k] = in ? reinterpret_cast<const uint4*>(pay)[2 * blk] : z;
+                    wb[j][k] = in ? reinterpret_cast<const uint4*>(pay)[2 * blk + 1] : z;
+                    dd[j][k] = in ? __half2float(reinterpret_cast<const __half*>(scs)[blk]) : 0.f;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < RPW; j++) {
+                acc[j] = 0.f;
+#pragma unroll
+                for (int k = 0; k < BPL; k++) {
+                    const unsigned lo[4] = {wa[j][k].x, wa[j][k].y, wa[j][k].z, wa[j][k].w};
+                    const unsigned hi[4] = {wb[j][k].x, wb[j][k].y, wb[j][k].z, wb[j][k].w};
+                    const unsigned a0[4] = {xa[k][0].x, xa[k][0].y, xa[k][0].z, xa[k][0].w};
+                    const unsigned b0[4] = {xb[k][0].x, xb[k][0].y, xb[k][0].z, xb[k][0].w};
+                    const unsigned a1[4] = {xa[k][1].x, xa[k][1].y, xa[k][1].z, xa[k][1].w};
+                    const unsigned b1[4] = {xb[k][1].x, xb[k][1].y, xb[k][1].z, xb[k][1].w};
+                    const unsigned a2[4] = {xa[k][2].x, xa[k][2].y, xa[k][2].z, xa[k][2].w};
+                    const unsigned b2[4] = {xb[k][2].x, xb[k][2].y, xb[k][2].z, xb[k][2].w};
+                    int s0l = 0, s0h = 0, s1l = 0, s1h = 0, s2l = 0, s2h = 0;
+#pragma unroll
+                    for (int t = 0; t < 4; t++) {
+                        s0l = dp4a_su(lo[t], a0[t], s0l);
+                        s0h = dp4a_su(hi[t], b0[t], s0h);
+                        s1l = dp4a_su(lo[t], a1[t], s1l);
+                        s1h = dp4a_su(hi[t], b1[t], s1h);
+                        s2l = dp4a_ss(lo[t], a2[t], s2l);
+                        s2h = dp4a_ss(hi[t], b2[t], s2h);
+                    }
+                    const int s01 = (s0l + s0h) + (s1l + s1h) * 256;
+                    const float T = fmaf((float)(s2l + s2h), 65536.0f, (float)s01);
+                    acc[j] = fmaf(dd[j][k] * sbr[k], T, acc[j]);
+                }
+            }
+        } else if constexpr (KQ) {
             kq_chunk<LAYOUT, RPW, BPL, WPR>(pay, scs, nb, rows, slot, wsub, lane, kc, xa, xb, sbr,
                                             xsl, xsh, acc);
         } else {

@@ -2,8 +2,9 @@
 // in HBM as the file's blocks: the k-quants and F32 / F16 / BF16 / Q8_0 /
 // Q4_1 (formats and device code in cw_kquant.cuh).
 //
-// GEMV: Q4_K / Q5_K (raw super-blocks) and Q6_K (the aligned split of
-// cw_q6_k_split) run on the streaming GEMV of cw_gemv.cuh: weights streamed
+// GEMV: Q4_K / Q5_K (raw super-blocks), Q6_K and Q8_0 (the aligned splits of
+// cw_q6_k_split / cw_q8_0_split) run on the streaming GEMV of cw_gemv.cuh:
+// weights streamed
 // through shared memory, integer dp4a products against q24 activation
 // planes.  The per-row kernel below serves the other types and Q6_K in its
 // raw form: one warp per output row; the 32 lanes split each super-block 8
@@ -78,6 +79,28 @@ int q6k_split(cw_ctx* ctx, const uint8_t* raw, size_t nsb, uint8_t* pay, __half*
     const int grid = (int)std::min<size_t>((nsb + 7) / 8, (size_t)ctx->sm_count * 16);
     k_q6k_split<<<grid, 256, 0, ctx->stream>>>(raw, (long)nsb, pay, d);
     return check_launch("q6_k split");
+}
+
+// One thread per 34-byte block (2-byte aligned): d to the scale plane, the
+// 32 codes to one 32-byte payload row.
+__global__ void k_q8_split(const uint8_t* __restrict__ raw, long nb, uint8_t* __restrict__ pay,
+                           __half* __restrict__ d) {
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= nb) return;
+    const uint16_t* s = reinterpret_cast<const uint16_t*>(raw + i * 34);
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) w[k] = (uint32_t)s[1 + 2 * k] | ((uint32_t)s[2 + 2 * k] << 16);
+    d[i] = __ushort_as_half(s[0]);
+    uint4* p = reinterpret_cast<uint4*>(pay + i * 32);
+    p[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    p[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+int q8_split(cw_ctx* ctx, const uint8_t* raw, size_t nb, uint8_t* pay, __half* d) {
+    if (!nb) return CW_OK;
+    k_q8_split<<<(unsigned)((nb + 255) / 256), 256, 0, ctx->stream>>>(raw, (long)nb, pay, d);
+    return check_launch("q8_0 split");
 }
 
 int kq_block_bytes(int type) {
@@ -192,6 +215,51 @@ int cw_q6_k_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_
     a.x = (const float*)ex->ptr;
     a.y = (float*)ey->ptr;
     return launch_sgemv(ctx, LAYOUT_Q6K, PRO_X, EPI_STORE, a, false);
+}
+
+int cw_q8_0_split(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out) {
+    clear_error();
+    CW_CHECK(ctx && out && rows > 0 && in_f % 32 == 0 && in_f > 0, CW_ERR_INVALID_ARG,
+             "cw_q8_0_split: bad arguments");
+    const size_t nb = rows * (in_f / 32);
+    BufEntry *ew, *eo;
+    CW_TRY(buf_get(ctx, w, &ew, nb * 34, "cw_q8_0_split(w)"));
+    cudaSetDevice(ctx->device);
+    CW_TRY(buf_new(ctx, nb * 34, BUF_PERSISTENT, out, &eo));
+    ew = &ctx->bufs[w];
+    eo->q8_split = true;
+    eo->rows = rows;
+    eo->in_f = in_f;
+    eo->scale_off = nb * 32;
+    uint8_t* base = (uint8_t*)eo->ptr;
+    return q8_split(ctx, (const uint8_t*)ew->ptr, nb, base, (__half*)(base + nb * 32));
+}
+
+int cw_q8_0_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out) {
+    clear_error();
+    CW_CHECK(ctx && out && out_f > 0 && out_f < (1u << 31), CW_ERR_INVALID_ARG,
+             "cw_q8_0_gemv: bad arguments");
+    CW_CHECK(sgemv_supported(LAYOUT_Q8, (int)in_f), CW_ERR_UNSUPPORTED,
+             "cw_q8_0_gemv: in_f=%zu not handled (a multiple of 256, at most 24576)", in_f);
+    BufEntry *ex, *ew, *ey;
+    CW_TRY(buf_get(ctx, x, &ex, in_f * 4, "cw_q8_0_gemv(x)"));
+    CW_TRY(buf_get(ctx, w, &ew, 0, "cw_q8_0_gemv(w)"));
+    CW_CHECK(ew->q8_split && ew->rows == out_f && ew->in_f == in_f, CW_ERR_INVALID_ARG,
+             "cw_q8_0_gemv: buffer %llu is not a split Q8_0 weight of [%zu, %zu]",
+             (unsigned long long)w, out_f, in_f);
+    cudaSetDevice(ctx->device);
+    CW_TRY(arena_get(ctx, out_f, out, &ey));
+    ex = &ctx->bufs[x];
+    ew = &ctx->bufs[w];
+    OpScope scope(ctx, "kquant_gemv");
+    GemvArgs a = {};
+    a.payload = (const uint8_t*)ew->ptr;
+    a.scales = (const char*)ew->ptr + ew->scale_off;
+    a.K = (int)in_f;
+    a.N = (int)out_f;
+    a.x = (const float*)ex->ptr;
+    a.y = (float*)ey->ptr;
+    return launch_sgemv(ctx, LAYOUT_Q8, PRO_X, EPI_STORE, a, false);
 }
 
 int cw_kquant_dequant(cw_ctx* ctx, cw_buf w, int type, size_t rows, size_t in_f, cw_buf* out) {

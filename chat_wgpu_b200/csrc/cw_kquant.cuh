@@ -420,5 +420,8 @@ __device__ __forceinline__ float embed_elem(const uint8_t* __restrict__ payload,
 // Split nsb raw Q6_K super-blocks (210 bytes each) into the streaming GEMV's
 // aligned planes: pay [nsb][208] (ql, qh, scales) and d [nsb] (f16).
 int q6k_split(cw_ctx* ctx, const uint8_t* raw, size_t nsb, uint8_t* pay, __half* d);
+// Split nb raw Q8_0 blocks (34 bytes: f16 d, 32 int8 codes) into the codes
+// plane pay [nb][32] and the scales d [nb].
+int q8_split(cw_ctx* ctx, const uint8_t* raw, size_t nb, uint8_t* pay, __half* d);
 
 }  // namespace cw

@@ -613,7 +613,13 @@ static int proj(cw_ctx* ctx, const QW& w, FArgs a) {
         case GGML_F32: return kq_fgemv_t<GGML_F32, PRO, EPI>(ctx, a);
         case GGML_F16: return kq_fgemv_t<GGML_F16, PRO, EPI>(ctx, a);
         case GGML_BF16: return kq_fgemv_t<GGML_BF16, PRO, EPI>(ctx, a);
-        case GGML_Q8_0: return kq_fgemv_t<GGML_Q8_0, PRO, EPI>(ctx, a);
+        case GGML_Q8_0:
+            if (w.split && kq_stream_ok<EPI>(a.K)) {
+                a.payload = w.split;
+                a.scales = w.split_d;
+                return launch_sgemv(ctx, LAYOUT_Q8, PRO, EPI, a, ctx->pdl);
+            }
+            return kq_fgemv_t<GGML_Q8_0, PRO, EPI>(ctx, a);
         case GGML_Q4_1: return kq_fgemv_t<GGML_Q4_1, PRO, EPI>(ctx, a);
         default: return set_error(CW_ERR_UNSUPPORTED, "projection of ggml type %d", w.type);
     }
@@ -705,9 +711,20 @@ static int load_vec(cw_model* m, const GgufFile& f, const std::string& name, siz
     return CW_OK;
 }
 
-// Q6_K weight: add the aligned split the streaming decode GEMV reads (same
-// bytes as the raw blocks: payload plane, then the f16 d plane).
+// Q6_K / Q8_0 weight: add the aligned split the streaming decode GEMV reads
+// (same bytes as the raw blocks: payload plane, then the f16 d plane).
 static int q6k_add_split(cw_model* m, QW* w) {
+    if (w->type == GGML_Q8_0 && sgemv_supported(LAYOUT_Q8, w->in_f)) {
+        const size_t nb = (size_t)w->rows * (w->in_f / 32);
+        void* p = nullptr;
+        CW_TRY(dev_alloc(m, nb * 34, &p));
+        uint8_t* base = (uint8_t*)p;
+        CW_TRY(q8_split(m->ctx, w->payload, nb, base, (__half*)(base + nb * 32)));
+        CW_CUDA(cudaStreamSynchronize(m->ctx->stream));
+        w->split = base;
+        w->split_d = (const __half*)(base + nb * 32);
+        return CW_OK;
+    }
     if (w->type != GGML_Q6_K || !sgemv_supported(LAYOUT_Q6K, w->in_f)) return CW_OK;
     const size_t nsb = (size_t)w->rows * (w->in_f / 256);
     void* p = nullptr;

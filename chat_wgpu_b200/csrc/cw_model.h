@@ -37,8 +37,9 @@ struct QW {  // packed Q4_0 weight (type 2), or raw GGUF Q6_K blocks (type 14)
     int rows = 0, in_f = 0;
     cw_buf buf = 0;
     int type = 2;
-    // Q6_K: the aligned split the streaming decode GEMV reads (payload plane
-    // [rows][in_f/256][208] and f16 d plane), beside the raw blocks that the
+    // Q6_K / Q8_0: the aligned split the streaming decode GEMV reads (payload
+    // plane [rows][in_f/256][208] or [rows][in_f/32][32], and an f16 d
+    // plane), beside the raw blocks that the
     // embedding lookups and the other kernels read; null where the streaming
     // GEMV does not take in_f
     const uint8_t* split = nullptr;

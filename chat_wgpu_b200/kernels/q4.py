@@ -74,3 +74,13 @@ def q6_k_split(ctx, w: Buffer, rows: int, in_f: int) -> Buffer:
 def q6_k_gemv(ctx, x: Buffer, w: Buffer, in_f: int, out_f: int) -> Buffer:
     """y[out_f] = W x over a q6_k_split weight (the streaming GEMV)."""
     return op(ctx, "cw_q6_k_gemv", x.handle, w.handle, int(in_f), int(out_f))
+
+
+def q8_0_split(ctx, w: Buffer, rows: int, in_f: int) -> Buffer:
+    """Raw Q8_0 blocks -> the streaming GEMV's code and scale planes (a new buffer)."""
+    return op(ctx, "cw_q8_0_split", w.handle, int(rows), int(in_f))
+
+
+def q8_0_gemv(ctx, x: Buffer, w: Buffer, in_f: int, out_f: int) -> Buffer:
+    """y[out_f] = W x over a q8_0_split weight (the streaming GEMV)."""
+    return op(ctx, "cw_q8_0_gemv", x.handle, w.handle, int(in_f), int(out_f))

@@ -52,31 +52,39 @@ def bench_shape(ctx: GpuContext, in_f: int, out_f: int, iters: int = 200, seed: 
             "gbs": nbytes / (us.value * 1e-6) / 1e9, "copies": n_w}
 
 
-KQ_TYPES = {"q4_k": (12, 144), "q5_k": (13, 176), "q6_k": (14, 210)}
+KQ_TYPES = {"q4_k": (12, 144), "q5_k": (13, 176), "q6_k": (14, 210), "q8_0": (8, 272)}
 
 
 def bench_kquant(ctx: GpuContext, qname: str, in_f: int, out_f: int, iters: int = 50,
                  seed: int = 0, l2_bytes: int = 126 << 20) -> dict:
-    """k-quant GEMV (cw_kquant_gemv; Q6_K: cw_q6_k_gemv over the aligned split
-    the model's decode step reads): device time per launch from the context
+    """k-quant GEMV (cw_kquant_gemv; Q6_K / Q8_0: cw_q6_k_gemv / cw_q8_0_gemv
+    over the aligned split the model's decode step reads): device time per
+    launch from the context
     profiler, cycling through copies that exceed 4x L2."""
     qtype, bb = KQ_TYPES[qname]
     rng = np.random.default_rng(seed)
     nb = out_f * (in_f // 256)
     wbytes = nb * bb
     raw = rng.integers(0, 256, nb * bb, dtype=np.uint8).reshape(nb, bb)
-    off = 208 if qtype == 14 else 0
-    raw[:, off:off + 2] = rng.uniform(1e-3, 1e-2, nb).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    if qtype == 8:  # 8 Q8_0 blocks of 34 bytes per 256 weights: every block's d
+        for j in range(8):
+            raw[:, 34 * j:34 * j + 2] = (rng.uniform(1e-3, 1e-2, nb).astype(np.float16)
+                                         .view(np.uint8).reshape(nb, 2))
+    else:
+        off = 208 if qtype == 14 else 0
+        raw[:, off:off + 2] = (rng.uniform(1e-3, 1e-2, nb).astype(np.float16)
+                               .view(np.uint8).reshape(nb, 2))
     n_w = max(2, min(64, -(-4 * l2_bytes // wbytes)))
     ws = [ctx.storage_bytes(raw.ravel()) for _ in range(n_w)]
-    if qtype == 14:
-        split = [q4.q6_k_split(ctx, w, out_f, in_f) for w in ws]
+    if qtype in (8, 14):  # the split planes the decode projections stream
+        sp, gv = (q4.q6_k_split, q4.q6_k_gemv) if qtype == 14 else (q4.q8_0_split, q4.q8_0_gemv)
+        split = [sp(ctx, w, out_f, in_f) for w in ws]
         for w in ws:
             w.release()
         ws = split
 
         def gemv(w):
-            return q4.q6_k_gemv(ctx, x, w, in_f, out_f)
+            return gv(ctx, x, w, in_f, out_f)
     else:
         def gemv(w):
             return q4.kquant_gemv(ctx, x, w, qtype, in_f, out_f)

@@ -257,6 +257,13 @@ int cw_q6_k_split(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out);
  * integer dot products against the block-floating-point x of the Q4 GEMVs
  * (within 1e-3 relative of the f32 dequantised product). */
 int cw_q6_k_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out);
+/* The same for Q8_0 (dequant_q8_0, dequant.rs:46-58: w = d * q): its 34-byte
+ * blocks split into a [rows][in_f/32][32] plane of int8 codes and a plane of
+ * the f16 d values (cw_q8_0_split, a new persistent buffer), and the
+ * streaming GEMV over it (in_f a multiple of 256, at most 24576; within 1e-3
+ * relative of the f32 dequantised product). */
+int cw_q8_0_split(cw_ctx* ctx, cw_buf w, size_t rows, size_t in_f, cw_buf* out);
+int cw_q8_0_gemv(cw_ctx* ctx, cw_buf x, cw_buf w, size_t in_f, size_t out_f, cw_buf* out);
 
 /* ---- model: src/model/{mod,qwen3,layers,cache}.rs --------------------------------------------- */
 typedef struct {

@@ -8,7 +8,9 @@ GEMVs 256 weights at a time.
     restatement of dequant.rs for every type;
   * the GEMV (cw_kquant_gemv) within 1e-3 relative of the oracle's dense
     dot (the reference's Proj::Dense, src/model/layers.rs:103-117: f32
-    weights, sequential f32 dot, src/kernels/matmul.wgsl);
+    weights, sequential f32 dot, src/kernels/matmul.wgsl); Q8_0 also through
+    the streaming GEMV over its split planes (cw_q8_0_split / cw_q8_0_gemv),
+    the form the model's decode projections use;
   * whole models against the oracle's forward: a mix of F16 / Q8_0 / Q4_1 /
     F32 projections (q/k/v of different types), a Q8_0 embedding and an
     F16 untied head; an all-F32 qwen2 model with q/k/v biases (the
@@ -69,6 +71,30 @@ def test_gemv_vs_dense_oracle(ctx, orc, kind, in_f, out_f):
     w = _oracle_dequant(orc, kind, raw, out_f * in_f).reshape(out_f, in_f)
     ref = (w.astype(np.float64) @ x.astype(np.float64)).astype(np.float32)  # exact-grade dot
     assert rel_err(got, ref) < REL, (kind, rel_err(got, ref))
+
+
+@pytest.mark.parametrize("in_f,out_f", [(256, 64), (1024, 3072), (4096, 512), (3072, 77)])
+def test_q8_0_split_gemv_vs_dense_oracle(ctx, orc, in_f, out_f):
+    """The streaming GEMV over the Q8_0 code/scale planes (the decode step's
+    form) against the oracle's dense product and the per-row kernel."""
+    from chat_wgpu_b200 import CwError
+    from chat_wgpu_b200.kernels import q4
+    rng = np.random.default_rng(5 * in_f + out_f)
+    raw = _raw("q8_0", rng, out_f, in_f)
+    x = rng.normal(0, 1, in_f).astype(np.float32)
+    w = ctx.storage_bytes(raw)
+    ws = q4.q8_0_split(ctx, w, out_f, in_f)
+    xb = ctx.storage(x)
+    got = ctx.read(q4.q8_0_gemv(ctx, xb, ws, in_f, out_f), out_f)
+    wd = _oracle_dequant(orc, "q8_0", raw, out_f * in_f).reshape(out_f, in_f)
+    ref = (wd.astype(np.float64) @ x.astype(np.float64)).astype(np.float32)
+    assert rel_err(got, ref) < REL, rel_err(got, ref)
+    row = ctx.read(q4.kquant_gemv(ctx, xb, w, TYPES["q8_0"], in_f, out_f), out_f)
+    assert rel_err(got, row) < REL
+    with pytest.raises(CwError):  # a raw weight is not a split one
+        q4.q8_0_gemv(ctx, xb, w, in_f, out_f)
+    ws.release()
+    w.release()
 
 
 @pytest.fixture(scope="module")
