@@ -713,7 +713,7 @@ static int load_vec(cw_model* m, const GgufFile& f, const std::string& name, siz
 
 // Q6_K / Q8_0 weight: add the aligned split the streaming decode GEMV reads
 // (same bytes as the raw blocks: payload plane, then the f16 d plane).
-static int q6k_add_split(cw_model* m, QW* w) {
+static int add_stream_split(cw_model* m, QW* w) {
     if (w->type == GGML_Q8_0 && sgemv_supported(LAYOUT_Q8, w->in_f)) {
         const size_t nb = (size_t)w->rows * (w->in_f / 32);
         void* p = nullptr;
@@ -766,7 +766,7 @@ static int load_q6k(cw_model* m, const GgufTensor* t, size_t in_f, QW* out, int 
     out->in_f = (int)in_f;
     out->type = GGML_Q6_K;
     out->buf = m->owned.back();
-    return q6k_add_split(m, out);
+    return add_stream_split(m, out);
 }
 
 // Q4_0 (packed planes) or Q6_K (raw), by the tensor's type.
@@ -835,7 +835,7 @@ static int load_kq(cw_model* m, const GgufFile& f, const std::vector<std::string
     out->type = (int)type;
     out->buf = m->owned.back();
     m->info.weight_bytes += stage.size();
-    return q6k_add_split(m, out);
+    return add_stream_split(m, out);
 }
 
 // One projection (or a stack / interleave of several) by the tensors' type:
