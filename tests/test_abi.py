@@ -63,6 +63,14 @@ def test_null_arguments_rejected():
     assert lib.cw_ctx_create(0, None) == 1
     assert lib.cw_storage(None, None, 0, None) == 1
     assert b"bad arguments" in lib.cw_last_error()
+    # the split k-quant / Q8_0 GEMV entry points: a status, before any device work
+    for fn in ("cw_q6_k_split", "cw_q8_0_split"):
+        assert getattr(lib, fn)(None, 0, 256, 256, None) == 1, fn
+        assert b"bad arguments" in lib.cw_last_error()
+    for fn in ("cw_q6_k_gemv", "cw_q8_0_gemv"):
+        assert getattr(lib, fn)(None, 0, 0, 256, 16, None) == 1, fn
+        assert b"bad arguments" in lib.cw_last_error()
+    assert lib.cw_kquant_gemv(None, 0, 0, 12, 256, 16, None) == 1
 
 
 def test_product_does_not_link_the_oracle():
